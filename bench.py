@@ -1,0 +1,333 @@
+"""Benchmark of the B200 MoE FFN block (GPT-OSS-120B shapes).
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0).  A step is one forward of the MoE block over
+one batch of synthetic tokens (seeded Philox weights generated on the device,
+N(0,1) activations).  `value` times the device path with inputs resident in
+HBM; `e2e` times the C-ABI host call (pinned host x -> H2D -> block -> D2H).
+The L2 (126 MB) is flushed between timed steps by writing a 256 MB buffer.
+
+--impl reference times the CPU restatement of the reference's AVX2 path
+(oracle/, all host threads) on the same config; rank 0 only.
+
+Configs (BASELINE.json configs[i]): c0 T=1 decode, c1 T=32 prefill batch
+(default: the headline workload), c2 T=2048 Zipf-skewed routing.  Under
+torchrun every rank runs its own batch (token-sharded replicas, no collective
+on the data path): scaling is weak.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H = D = 2880
+E, K = 128, 4
+MATRIX_BYTES = 2880 * (2880 // 32) * 17          # one MXFP4 expert matrix, GGUF bytes
+ROUTER_BYTES = E * H * 4
+L2_BYTES = 126 << 20
+
+CONFIGS = {
+    "c0": dict(T=1, seed=0, zipf_s=0.0, zipf_beta=0.0, router_bias=True,
+               desc="decode, 1 token (BASELINE configs[0])"),
+    "c1": dict(T=32, seed=1, zipf_s=0.0, zipf_beta=0.0, router_bias=True,
+               desc="prefill batch T=32 (BASELINE configs[1])"),
+    "c2": dict(T=2048, seed=2, zipf_s=1.1, zipf_beta=1.0, router_bias=True,
+               desc="prefill T=2048, Zipf(1.1)-skewed router bias (BASELINE configs[2])"),
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback (6.65 TB/s)"
+
+
+def load_traffic(config):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    d = json.load(open(p))
+    return d.get(config, {}).get("gate_up_dram_bytes")
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (every 200 ms)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def dist_info():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def cpu_baseline(cfg_name, seconds=12.0, workers=None):
+    """The oracle (C restatement of the reference's AVX2 path) on the same
+    workload, all host threads.  Returns (tokens/s, cores, sample text)."""
+    from oracle import oracle
+    spt = importlib.import_module("stream-pt_b200")
+    c = CONFIGS[cfg_name]
+    cfg = spt.Config(H, D, E, K)
+    params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
+                             router_bias=c["router_bias"])
+    host = spt.synth_layer_host(cfg, params)
+    w = oracle.Weights(H, D, E, K, host["router"], host["router_bias"], host["gate"], host["up"],
+                       host["down"], host["gate_bias"], host["up_bias"], host["down_bias"])
+    workers = workers or os.cpu_count() or 1
+    T = c["T"]
+    # bounded sample: at most 64 tokens of the workload per repetition
+    Ts = min(T, 64)
+    x = spt.synth_normal_host(c["seed"], 1000, Ts * H)
+    oracle.forward_moe_batch(w, x, Ts, workers)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.forward_moe_batch(w, x, Ts, workers)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 1000:
+            break
+    tps = reps * Ts / el
+    return tps, workers, f"{reps} x {Ts} tokens of {cfg_name} ({el:.1f} s, memory-resident weights)"
+
+
+def run_reference(args):
+    rank, world, _ = dist_info()
+    if rank != 0:
+        return
+    tps, cores, sample = cpu_baseline(args.config, seconds=max(3.0, 2.0 * args.steps))
+    line = {"metric": "moe_block_tokens_per_s", "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * CONFIGS[args.config]["T"] / tps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (mxfp4 weights)",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"{args.config}: {CONFIGS[args.config]['desc']}",
+                       "tokens_per_step": CONFIGS[args.config]["T"], "hidden": H, "experts": E, "top_k": K},
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_info()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    spt = importlib.import_module("stream-pt_b200")
+    c = CONFIGS[args.config]
+    T = c["T"]
+    cfg = spt.Config(H, D, E, K)
+    params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
+                             router_bias=c["router_bias"])
+    ctx = spt.Context(local)
+    arena = ctx.synthetic_arena(cfg, params)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    x_host = spt.synth_normal_host(c["seed"] + 7919 * rank, 1000, T * H)
+    x_dev = torch.from_numpy(x_host).to(f"cuda:{local}")
+    out_dev = torch.empty_like(x_dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+
+    def step():
+        ctx.forward_moe_batch_device(arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
+
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    routing = ctx.last_routing(T, E, K)
+    n_active = int((routing["counts"] > 0).sum())
+
+    # ---- timed region: device-resident inputs ------------------------------
+    # No host synchronisation inside the loop; the 256 MB L2 flush before each
+    # step also lets the host enqueue the step's kernels ahead of the GPU.
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                flush.fill_(i & 0xFF)
+                starts[i].record(stream)
+                step()
+                ends[i].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if world > 1:
+        t = torch.tensor([total_ms], device=f"cuda:{local}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * T * args.steps / (total_ms / 1e3)
+
+    # ---- per-kernel durations (same workload, CUDA events around each stage
+    # on the launching stream) for the roofline -----------------------------
+    ctx.set_stage_timing(True)
+    stage_ms = []
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xFF)
+        step()
+        stage_ms.append(ctx.stage_times())
+    ctx.set_stage_timing(False)
+
+    # ---- e2e through the C ABI with pinned host buffers --------------------
+    x_pin = torch.from_numpy(x_host).pin_memory()
+    out_pin = torch.empty_like(x_pin).pin_memory()
+    xn, on = x_pin.numpy(), out_pin.numpy()
+    for _ in range(max(1, args.warmup)):
+        ctx.forward_moe_batch(arena, xn, T, out=on)
+    e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(i & 0xFF)
+        e_st[i].record(stream)
+        ctx.forward_moe_batch(arena, xn, T, out=on)
+        e_en[i].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_st, e_en))
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=f"cuda:{local}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+    ok = bool(np.array_equal(on.view(np.uint32), out_dev.cpu().numpy().view(np.uint32)) or
+              np.array_equal(np.nan_to_num(on), np.nan_to_num(out_dev.cpu().numpy())))
+
+    # ---- roofline of the dominant kernel (gate/up GEMV + SwiGLU) -----------
+    peak, peak_src = load_peaks()
+    gu = [s["gate_up_swiglu"] for s in stage_ms if s]
+    dn = [s["down"] for s in stage_ms if s]
+    gu_ms = sum(gu) / len(gu) if gu else float("nan")
+    dn_ms = sum(dn) / len(dn) if dn else float("nan")
+    gu_bytes = n_active * 2 * MATRIX_BYTES
+    dn_bytes = n_active * MATRIX_BYTES
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    stages_avg = {k: round(sum(s[k] for s in stage_ms) / len(stage_ms), 5) for k in stage_ms[0]} if stage_ms else {}
+    step_bytes = ROUTER_BYTES + 3 * n_active * MATRIX_BYTES
+    line = {
+        "metric": "moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (mxfp4 weights)", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H,
+                   "expert_dim": D, "experts": E, "top_k": K, "seed": c["seed"],
+                   "parallelism": f"token-sharded replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "256 MB buffer written between timed steps",
+                   "active_experts": n_active},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": load_traffic(args.config),
+                     "kernel": "k_gemv<gate_up> (fused gate+up MXFP4 GEMV + SwiGLU)",
+                     "algorithmic_bytes": gu_bytes, "avg_ms": gu_ms, "peak_source": peak_src,
+                     "down_kernel": {"achieved": dn_bytes / (dn_ms / 1e3) / 1e9, "avg_ms": dn_ms,
+                                     "algorithmic_bytes": dn_bytes},
+                     "step_hbm_fraction": step_bytes / (ms_per_step / 1e3) / 1e9 / peak},
+        "stages_ms": stages_avg,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4, "ms_per_step": e2e_ms / args.steps,
+                "matches_device_path": ok},
+        "gpu_launches": args.steps * ctx.kernels_per_forward(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, cores, sample = cpu_baseline(args.config)
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        line["clocks"] = clocks.summary()
+        print(json.dumps(line), flush=True)
+    arena.close()
+    ctx.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

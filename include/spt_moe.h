@@ -1,0 +1,251 @@
+/*
+ * spt_moe.h -- C ABI of the B200 (sm_100a) MoE FFN block for Stream-PT.
+ *
+ * The entry points replace the reference's Go functions in package
+ * `forward` (paths relative to the Stream-PT repository root):
+ *
+ *   spt_forward_moe_batch        forwardMoEBatch   forward/moe_batch.go:78-194
+ *   spt_forward_moe              forwardMoE        forward/moe.go:28-64
+ *   spt_route_moe_batch          routeMoEBatch     forward/moe_batch.go:221-303
+ *   spt_select_moe_batch         selectMoEBatch    forward/moe_batch.go:305-342
+ *   spt_dispatch_moe_batch       dispatch lists    forward/moe_batch.go:142-159
+ *   spt_mul_moe_batch_expert     mulMoEBatchExpert forward/mxfp4_batch.go:31-95
+ *   spt_swiglu                   gptOSSSwiGLU      forward/moe.go:66-70
+ *   spt_combine_moe_batch        combine loop      forward/moe_batch.go:163-192
+ *   spt_rmsnorm                  normBatch         forward/layer_batch.go:139-195
+ *   spt_mul_q80                  MulQ80Into/Argmax forward/q80.go:22-148
+ *   spt_arena_create             ggufmap.WithExpertRanges + readExpertBias
+ *                                (ggufmap/mmap_linux.go:391-555, forward/moe.go:72-92):
+ *                                the streamed mmap window becomes an HBM arena
+ *                                uploaded once.
+ *
+ * Conventions: plain pointers and sizes; every function returns an
+ * spt_status; the message of the last failure on a context is returned by
+ * spt_last_error().  Host-pointer entry points are synchronous (they return
+ * after the device work and the copies back have finished), like the Go
+ * functions they replace.  `*_device` entry points take device pointers and
+ * only enqueue work on the context's stream.  A non-NULL `cancel` flag is
+ * polled between stages; a nonzero value returns SPT_ERR_CANCELED
+ * (the reference returns ctx.Err()).
+ */
+#ifndef SPT_MOE_H
+#define SPT_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum spt_status {
+  SPT_OK = 0,
+  SPT_ERR_NULL_ARG = 1,      /* "nil MoE context, reader, configuration or weights" */
+  SPT_ERR_DIMENSIONS = 2,    /* "invalid MoE batch dimensions" / overflow / config */
+  SPT_ERR_OVERLAP = 3,       /* "MoE input and output overlap" */
+  SPT_ERR_ROUTER = 4,        /* "invalid F32 router shape or range" */
+  SPT_ERR_EXPERT = 5,        /* "expected MXFP4 expert tensor" / invalid expert range */
+  SPT_ERR_BIAS = 6,          /* unsupported bias type / invalid bias shape or range */
+  SPT_ERR_FILE_RANGE = 7,    /* tensor range outside the reader's file */
+  SPT_ERR_SCRATCH = 8,       /* "MoE batch scratch dimensions mismatch" */
+  SPT_ERR_CANCELED = 9,      /* context.Canceled */
+  SPT_ERR_CUDA = 10,         /* CUDA runtime failure (message in spt_last_error) */
+  SPT_ERR_NCCL = 11,         /* NCCL failure in the expert-parallel path */
+  SPT_ERR_TIMEOUT = 12,      /* a bounded device wait gave up */
+  SPT_ERR_UNSUPPORTED = 13,  /* shape or option this build does not implement */
+  SPT_ERR_NO_DEVICE = 14     /* no CUDA device / extension unusable */
+} spt_status;
+
+/* ggufindex.Tensor (ggufindex/index.go:15-26): name, GGML type, shape with
+ * ne0 fastest, byte range inside the model file.  name == NULL or "" marks an
+ * absent optional tensor (an unnamed bias, forward/moe_batch.go:196-201). */
+typedef struct spt_tensor {
+  const char *name;
+  uint32_t type;      /* 0 F32, 1 F16, 8 Q8_0, 30 BF16, 39 MXFP4 */
+  uint32_t n_dims;    /* entries of shape[] in use (0..4) */
+  uint64_t shape[4];
+  uint64_t start, end;
+} spt_tensor;
+
+/* ggufmap.Reader stand-in: one contiguous host view of the model file (an
+ * mmap of the GGUF shard, or any host buffer). */
+typedef struct spt_reader {
+  const uint8_t *base;
+  uint64_t size;
+} spt_reader;
+
+/* The forward.Config fields the MoE block reads (forward/config.go:57-75). */
+typedef struct spt_moe_config {
+  int64_t hidden_dim;        /* H, 2880 for GPT-OSS-120B */
+  int64_t expert_hidden_dim; /* D, 2880 */
+  int64_t num_experts;       /* E, 128 */
+  int64_t num_experts_used;  /* k, 4 */
+} spt_moe_config;
+
+/* The MoE tensors of forward.LayerWeights (forward/layer.go:66-81). */
+typedef struct spt_layer_weights {
+  spt_tensor ffn_gate_inp, ffn_gate_inp_bias;
+  spt_tensor ffn_gate_exps, ffn_gate_exps_bias;
+  spt_tensor ffn_up_exps, ffn_up_exps_bias;
+  spt_tensor ffn_down_exps, ffn_down_exps_bias;
+} spt_layer_weights;
+
+typedef struct spt_context spt_context;
+typedef struct spt_arena spt_arena;
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Create a context on CUDA device `device` with its own stream. */
+spt_status spt_context_create(int device, spt_context **out);
+void spt_context_destroy(spt_context *ctx);
+/* Message of the last failure on ctx (never NULL). */
+const char *spt_last_error(const spt_context *ctx);
+const char *spt_status_string(spt_status status);
+/* The cudaStream_t all of this context's work is enqueued on. */
+void *spt_context_stream(spt_context *ctx);
+/* Use an external cudaStream_t (NULL restores the context's own stream). */
+spt_status spt_context_set_stream(spt_context *ctx, void *stream);
+/* Synchronize the context's stream. */
+spt_status spt_context_sync(spt_context *ctx);
+
+/* ---- validation (no device work) ------------------------------------- */
+
+/* Exactly the tensor/config checks of forwardMoEBatch
+ * (forward/moe_batch.go:81-130, mxfp4_batch.go:17-27,
+ * moe_batch.go:196-219, mmap_linux.go:318-334). */
+spt_status spt_validate_moe_layer(spt_context *ctx, const spt_reader *reader,
+                                  const spt_moe_config *cfg, const spt_layer_weights *lw);
+
+/* ---- HBM expert arena -------------------------------------------------- */
+
+#define SPT_ARENA_GEMV 1u /* CUDA-core GEMV layout (decode, bit-exact order) */
+#define SPT_ARENA_MMA 2u  /* tcgen05 block-scaled GEMM layout (prefill) */
+
+/* Validate and upload n_layers layers (readers[i], layers[i]) once through
+ * pinned memory, repacking MXFP4 blocks on the device.  Replaces the
+ * ggufmap mmap window, hot-expert cache and lookahead. */
+spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers,
+                            const spt_moe_config *cfg, const spt_layer_weights *layers,
+                            int64_t n_layers, uint32_t flags, spt_arena **out);
+
+/* Seeded synthetic GPT-OSS-style weights generated on the device
+ * (counter-based Philox4x32-10; identical bytes from
+ * spt_synth_layer_host).  Not a reference interface: benchmark input. */
+typedef struct spt_synth_params {
+  uint64_t seed;
+  float router_std;   /* N(0, router_std) router weights (0.02) */
+  float bias_std;     /* N(0, bias_std) router and expert biases (0.01) */
+  uint8_t scale_lo;   /* E8M0 scale bytes uniform in [scale_lo, scale_hi] */
+  uint8_t scale_hi;
+  uint8_t expert_bias; /* 1: F32 expert biases present; 0: unnamed */
+  uint8_t router_bias; /* 1: router bias present */
+  float zipf_s;       /* >0: add a Zipf(zipf_s) skew to the router bias */
+  float zipf_beta;    /* logit scale of that skew */
+} spt_synth_params;
+
+spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cfg,
+                                      const spt_synth_params *params, int64_t n_layers,
+                                      uint32_t flags, spt_arena **out);
+void spt_arena_destroy(spt_arena *arena);
+/* Device bytes held by the arena. */
+uint64_t spt_arena_bytes(const spt_arena *arena);
+
+/* Host copy of one synthetic layer in GGUF tensor layout (for the CPU
+ * oracle and the baseline).  Sizes: router E*H*4, router_bias E*4,
+ * gate/up E*D*(H/32)*17, down E*H*(D/32)*17, gate/up bias E*D*4,
+ * down bias E*H*4.  Any pointer may be NULL to skip that tensor. */
+spt_status spt_synth_layer_host(const spt_moe_config *cfg, const spt_synth_params *params,
+                                int64_t layer, uint8_t *router, float *router_bias,
+                                uint8_t *gate, uint8_t *up, uint8_t *down, float *gate_bias,
+                                float *up_bias, float *down_bias);
+/* Seeded N(mean, std) fp32 activations (Box-Muller in double). */
+spt_status spt_synth_normal_host(uint64_t seed, uint64_t stream, float mean, float std,
+                                 float *out, int64_t n);
+
+/* ---- the block ----------------------------------------------------------- */
+
+/* forwardMoEBatch: x and out are host arrays of x_len / out_len floats,
+ * [batch, H] row-major; they must not overlap.  out is fully overwritten. */
+spt_status spt_forward_moe_batch(spt_context *ctx, spt_arena *arena, int64_t layer,
+                                 const float *x, int64_t x_len, float *out, int64_t out_len,
+                                 int64_t batch, const volatile int32_t *cancel);
+/* forwardMoE: the batch-1 decode wrapper. */
+spt_status spt_forward_moe(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
+                           int64_t x_len, float *out, int64_t out_len,
+                           const volatile int32_t *cancel);
+/* Same block on device pointers, enqueued on the context stream. */
+spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int64_t layer,
+                                        const float *x, float *out, int64_t batch);
+
+/* Drop-in one-shot form of forwardMoEBatch: validates every tensor against
+ * the reader, uploads the layer, runs it and frees it. */
+spt_status spt_forward_moe_batch_reader(spt_context *ctx, const spt_reader *reader,
+                                        const spt_moe_config *cfg,
+                                        const spt_layer_weights *lw, const float *x,
+                                        int64_t x_len, float *out, int64_t out_len,
+                                        int64_t batch, const volatile int32_t *cancel);
+
+/* Intermediates of the last spt_forward_moe_batch* call (host copies, for
+ * parity tests): logits [batch*E], selected index/weight [batch*k],
+ * dispatch permutation perm [dispatched] and per-expert counts [E].
+ * Any pointer may be NULL.  *dispatched receives the dispatched slot count. */
+spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index,
+                            float *sel_weight, int32_t *perm, int32_t *expert_count,
+                            int64_t *dispatched);
+
+/* Per-stage device timing of the block.  When enabled, every forward call
+ * records CUDA events on the context stream around its stages; spt_stage_times
+ * returns the durations (ms) of the last call:
+ * [0] router, [1] select, [2] dispatch, [3] gate/up+SwiGLU, [4] down, [5] combine.
+ * Returns the number of stages written (<= n). */
+#define SPT_NUM_STAGES 6
+spt_status spt_set_stage_timing(spt_context *ctx, int enable);
+int spt_stage_times(spt_context *ctx, float *ms, int n);
+/* Number of kernels one forward call launches. */
+int spt_kernels_per_forward(spt_context *ctx);
+
+/* ---- stage entry points (host pointers, synchronous) -------------------- */
+
+/* routeMoEBatch: data = E rows x hidden little-endian F32 (any byte
+ * alignment, data_len == E*hidden*4); logits[t*E+e]. */
+spt_status spt_route_moe_batch(spt_context *ctx, const uint8_t *data, uint64_t data_len,
+                               const float *x, int64_t x_len, const float *router_bias,
+                               int64_t batch, int64_t hidden, int64_t experts, float *logits,
+                               const volatile int32_t *cancel);
+/* selectMoEBatch for every token row of logits [batch, E]. */
+spt_status spt_select_moe_batch(spt_context *ctx, const float *logits, int64_t batch,
+                                int64_t experts, int64_t k, int32_t *index, float *weight);
+/* The reference's per-expert dispatch lists as a permutation: slots with
+ * weight > 0 or NaN, grouped by expert ascending, each group in
+ * descending slot order (the push-front list walk).  expert_offsets has
+ * E+1 entries; *dispatched = expert_offsets[E]. */
+spt_status spt_dispatch_moe_batch(spt_context *ctx, const int32_t *index, const float *weight,
+                                  int64_t batch, int64_t k, int64_t experts, int32_t *perm,
+                                  int32_t *expert_offsets, int64_t *dispatched);
+/* mulMoEBatchExpert: data = `output` rows of input/32 17-byte MXFP4 blocks;
+ * y[y_offsets[j]+r] = dot(row r, x[x_offsets[j] : +input]) + bias[r].
+ * bias may be NULL (zeros).  Offsets are bounds-checked against x_len/y_len. */
+spt_status spt_mul_moe_batch_expert(spt_context *ctx, const uint8_t *data, uint64_t data_len,
+                                    int64_t input, int64_t output, const float *x, int64_t x_len,
+                                    const int64_t *x_offsets, int64_t count, const float *bias,
+                                    float *y, int64_t y_len, const int64_t *y_offsets,
+                                    const volatile int32_t *cancel);
+/* act[i] = gptOSSSwiGLU(gate[i], up[i]). */
+spt_status spt_swiglu(spt_context *ctx, const float *gate, const float *up, float *act,
+                      int64_t n);
+/* out[t,:] = sum over ranks r (weight > 0 or NaN) of fma(results[t*k+r,:], w, out). */
+spt_status spt_combine_moe_batch(spt_context *ctx, const float *results, const float *weight,
+                                 int64_t batch, int64_t k, int64_t hidden, float *out);
+/* normBatch RMSNorm with an F32 weight vector, 8 accumulation lanes. */
+spt_status spt_rmsnorm(spt_context *ctx, const float *x, const float *weight, int64_t batch,
+                       int64_t dim, float eps, float *y);
+/* MulQ80Into + MulQ80Argmax: Q8_0 matrix [output rows x input/32 34-byte
+ * blocks]; y may be NULL; *argmax gets the lowest row of the maximum. */
+spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len, int64_t input,
+                       int64_t output, const float *x, float *y, int64_t *argmax,
+                       float *best_logit);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPT_MOE_H */

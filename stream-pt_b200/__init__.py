@@ -1,0 +1,491 @@
+"""Stream-PT MoE FFN block on B200: Python host mirror of the C ABI.
+
+The compute path is the sm_100a library ``libspt_moe.so`` built from
+``csrc/`` (``include/spt_moe.h`` is its interface).  This module mirrors the
+reference's Go interface of package ``forward`` for tests and benchmarks:
+``Tensor``/``Reader``/``Config``/``LayerWeights`` stand for ggufindex.Tensor,
+ggufmap.Reader, forward.Config and forward.LayerWeights, and each function
+raises ``SptError`` where the Go function returns an error.
+
+There is no CPU fallback: if the library is missing or no CUDA device is
+present, every compute call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libspt_moe.so")
+
+# spt_status codes (include/spt_moe.h)
+OK, ERR_NULL_ARG, ERR_DIMENSIONS, ERR_OVERLAP, ERR_ROUTER, ERR_EXPERT, ERR_BIAS = range(7)
+ERR_FILE_RANGE, ERR_SCRATCH, ERR_CANCELED, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT = range(7, 13)
+ERR_UNSUPPORTED, ERR_NO_DEVICE = 13, 14
+
+ARENA_GEMV, ARENA_MMA = 1, 2
+
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
+
+
+class SptError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[{status}] {message}")
+        self.status = status
+        self.message = message
+
+
+class CanceledError(SptError):
+    """context.Canceled equivalent."""
+
+
+# ---- C structs ------------------------------------------------------------
+class _Tensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_uint32), ("n_dims", ctypes.c_uint32),
+                ("shape", ctypes.c_uint64 * 4), ("start", ctypes.c_uint64), ("end", ctypes.c_uint64)]
+
+
+class _Reader(ctypes.Structure):
+    _fields_ = [("base", ctypes.c_void_p), ("size", ctypes.c_uint64)]
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [("hidden_dim", ctypes.c_int64), ("expert_hidden_dim", ctypes.c_int64),
+                ("num_experts", ctypes.c_int64), ("num_experts_used", ctypes.c_int64)]
+
+
+class _LayerWeights(ctypes.Structure):
+    _fields_ = [(n, _Tensor) for n in (
+        "ffn_gate_inp", "ffn_gate_inp_bias", "ffn_gate_exps", "ffn_gate_exps_bias",
+        "ffn_up_exps", "ffn_up_exps_bias", "ffn_down_exps", "ffn_down_exps_bias")]
+
+
+class _SynthParams(ctypes.Structure):
+    _fields_ = [("seed", ctypes.c_uint64), ("router_std", ctypes.c_float),
+                ("bias_std", ctypes.c_float), ("scale_lo", ctypes.c_uint8),
+                ("scale_hi", ctypes.c_uint8), ("expert_bias", ctypes.c_uint8),
+                ("router_bias", ctypes.c_uint8), ("zipf_s", ctypes.c_float),
+                ("zipf_beta", ctypes.c_float)]
+
+
+# ---- Go-side value types ---------------------------------------------------
+@dataclass
+class Tensor:
+    """ggufindex.Tensor: name ('' = absent), GGML type, shape (ne0 first), byte range."""
+    name: str = ""
+    type: int = 0
+    shape: Sequence[int] = ()
+    start: int = 0
+    end: int = 0
+
+    def _c(self) -> _Tensor:
+        t = _Tensor()
+        t.name = self.name.encode() if self.name else None
+        t.type = self.type
+        shape = list(self.shape)
+        t.n_dims = len(shape)
+        for i, v in enumerate(shape[:4]):
+            t.shape[i] = int(v) & ((1 << 64) - 1)
+        if len(shape) > 4:
+            t.n_dims = 5  # never valid for the MoE tensors
+        t.start = int(self.start) & ((1 << 64) - 1)
+        t.end = int(self.end) & ((1 << 64) - 1)
+        return t
+
+
+@dataclass
+class Config:
+    """The forward.Config fields the MoE block reads."""
+    hidden_dim: int
+    expert_hidden_dim: int
+    num_experts: int
+    num_experts_used: int
+
+    def _c(self) -> _Config:
+        m = (1 << 63) - 1
+        def clamp(v):
+            return max(-(1 << 63), min(m, int(v)))
+        return _Config(clamp(self.hidden_dim), clamp(self.expert_hidden_dim),
+                       clamp(self.num_experts), clamp(self.num_experts_used))
+
+
+@dataclass
+class LayerWeights:
+    ffn_gate_inp: Tensor = field(default_factory=Tensor)
+    ffn_gate_inp_bias: Tensor = field(default_factory=Tensor)
+    ffn_gate_exps: Tensor = field(default_factory=Tensor)
+    ffn_gate_exps_bias: Tensor = field(default_factory=Tensor)
+    ffn_up_exps: Tensor = field(default_factory=Tensor)
+    ffn_up_exps_bias: Tensor = field(default_factory=Tensor)
+    ffn_down_exps: Tensor = field(default_factory=Tensor)
+    ffn_down_exps_bias: Tensor = field(default_factory=Tensor)
+
+    def _c(self) -> _LayerWeights:
+        lw = _LayerWeights()
+        for name, _ in _LayerWeights._fields_:
+            setattr(lw, name, getattr(self, name)._c())
+        return lw
+
+
+class Reader:
+    """ggufmap.Reader stand-in: a host byte buffer holding the model file."""
+
+    def __init__(self, data: bytes | bytearray | np.ndarray):
+        self.buf = np.frombuffer(bytes(data), dtype=np.uint8) if not isinstance(data, np.ndarray) \
+            else np.ascontiguousarray(data, dtype=np.uint8)
+
+    def _c(self) -> _Reader:
+        return _Reader(self.buf.ctypes.data if self.buf.size else None, self.buf.size)
+
+
+@dataclass
+class SynthParams:
+    seed: int = 0
+    router_std: float = 0.02
+    bias_std: float = 0.01
+    scale_lo: int = 119
+    scale_hi: int = 123
+    expert_bias: bool = True
+    router_bias: bool = True
+    zipf_s: float = 0.0
+    zipf_beta: float = 0.0
+
+    def _c(self) -> _SynthParams:
+        return _SynthParams(self.seed, self.router_std, self.bias_std, self.scale_lo,
+                            self.scale_hi, int(self.expert_bias), int(self.router_bias),
+                            self.zipf_s, self.zipf_beta)
+
+
+# ---- library loading --------------------------------------------------------
+_lib = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def lib():
+    """Load libspt_moe.so; raises if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise SptError(ERR_NO_DEVICE, f"{LIB_PATH} not built (run stream-pt_b200/build.py)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i64, i32, f32, st = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float, ctypes.c_int
+    P = ctypes.POINTER
+    sigs = {
+        "spt_context_create": ([ctypes.c_int, P(vp)], st),
+        "spt_context_destroy": ([vp], None),
+        "spt_last_error": ([vp], ctypes.c_char_p),
+        "spt_status_string": ([st], ctypes.c_char_p),
+        "spt_context_stream": ([vp], vp),
+        "spt_context_set_stream": ([vp, vp], st),
+        "spt_context_sync": ([vp], st),
+        "spt_validate_moe_layer": ([vp, P(_Reader), P(_Config), P(_LayerWeights)], st),
+        "spt_arena_create": ([vp, P(_Reader), P(_Config), P(_LayerWeights), i64, ctypes.c_uint32, P(vp)], st),
+        "spt_arena_create_synthetic": ([vp, P(_Config), P(_SynthParams), i64, ctypes.c_uint32, P(vp)], st),
+        "spt_arena_destroy": ([vp], None),
+        "spt_arena_bytes": ([vp], ctypes.c_uint64),
+        "spt_synth_layer_host": ([P(_Config), P(_SynthParams), i64, vp, vp, vp, vp, vp, vp, vp, vp], st),
+        "spt_synth_normal_host": ([ctypes.c_uint64, ctypes.c_uint64, f32, f32, vp, i64], st),
+        "spt_forward_moe_batch": ([vp, vp, i64, vp, i64, vp, i64, i64, vp], st),
+        "spt_forward_moe": ([vp, vp, i64, vp, i64, vp, i64, vp], st),
+        "spt_forward_moe_batch_device": ([vp, vp, i64, vp, vp, i64], st),
+        "spt_forward_moe_batch_reader": ([vp, P(_Reader), P(_Config), P(_LayerWeights), vp, i64, vp, i64, i64, vp], st),
+        "spt_last_routing": ([vp, vp, vp, vp, vp, vp, P(i64)], st),
+        "spt_route_moe_batch": ([vp, vp, ctypes.c_uint64, vp, i64, vp, i64, i64, i64, vp, vp], st),
+        "spt_select_moe_batch": ([vp, vp, i64, i64, i64, vp, vp], st),
+        "spt_dispatch_moe_batch": ([vp, vp, vp, i64, i64, i64, vp, vp, P(i64)], st),
+        "spt_mul_moe_batch_expert": ([vp, vp, ctypes.c_uint64, i64, i64, vp, i64, vp, i64, vp, vp, i64, vp, vp], st),
+        "spt_swiglu": ([vp, vp, vp, vp, i64], st),
+        "spt_combine_moe_batch": ([vp, vp, vp, i64, i64, i64, vp], st),
+        "spt_rmsnorm": ([vp, vp, vp, i64, i64, f32, vp], st),
+        "spt_mul_q80": ([vp, vp, ctypes.c_uint64, i64, i64, vp, vp, P(i64), P(f32)], st),
+        "spt_set_stage_timing": ([vp, ctypes.c_int], st),
+        "spt_stage_times": ([vp, vp, ctypes.c_int], ctypes.c_int),
+        "spt_kernels_per_forward": ([vp], ctypes.c_int),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def exported_symbols() -> list[str]:
+    """Names this binding expects the library to export (include/spt_moe.h)."""
+    lib()
+    return sorted(n for n in dir(_lib) if n.startswith("spt_"))
+
+
+def _p(a: Optional[np.ndarray]):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Context:
+    """spt_context: one CUDA device + stream (device=-1: host-only validation)."""
+
+    def __init__(self, device: int = 0):
+        self._h = ctypes.c_void_p()
+        st = lib().spt_context_create(device, ctypes.byref(self._h))
+        if st != OK:
+            raise SptError(st, lib().spt_last_error(None).decode())
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if self._h:
+            lib().spt_context_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, st: int):
+        if st != OK:
+            msg = lib().spt_last_error(self._h).decode()
+            if st == ERR_CANCELED:
+                raise CanceledError(st, msg)
+            raise SptError(st, msg)
+
+    @property
+    def stream(self) -> int:
+        return lib().spt_context_stream(self._h) or 0
+
+    def set_stream(self, stream_ptr: int):
+        self.check(lib().spt_context_set_stream(self._h, ctypes.c_void_p(stream_ptr) if stream_ptr else None))
+
+    def sync(self):
+        self.check(lib().spt_context_sync(self._h))
+
+    STAGES = ("router", "select", "dispatch", "gate_up_swiglu", "down", "combine")
+
+    def set_stage_timing(self, enable: bool = True):
+        self.check(lib().spt_set_stage_timing(self._h, int(enable)))
+
+    def stage_times(self) -> dict:
+        ms = np.zeros(len(self.STAGES), np.float32)
+        n = lib().spt_stage_times(self._h, _p(ms), ms.size)
+        return {k: float(v) for k, v in zip(self.STAGES[:n], ms[:n])}
+
+    def kernels_per_forward(self) -> int:
+        return int(lib().spt_kernels_per_forward(self._h))
+
+    # ---- validation -----------------------------------------------------
+    def validate(self, reader: Reader, cfg: Config, lw: LayerWeights):
+        r, c, w = reader._c(), cfg._c(), lw._c()
+        self.check(lib().spt_validate_moe_layer(self._h, ctypes.byref(r), ctypes.byref(c), ctypes.byref(w)))
+
+    # ---- arenas -----------------------------------------------------------
+    def arena(self, readers: Sequence[Reader], cfg: Config, layers: Sequence[LayerWeights],
+              flags: int = ARENA_GEMV) -> "Arena":
+        n = len(layers)
+        rs = (_Reader * n)(*[r._c() for r in readers])
+        ls = (_LayerWeights * n)(*[l._c() for l in layers])
+        c = cfg._c()
+        h = ctypes.c_void_p()
+        self.check(lib().spt_arena_create(self._h, rs, ctypes.byref(c), ls, n, flags, ctypes.byref(h)))
+        return Arena(self, h, cfg, n, keep=(readers,))
+
+    def synthetic_arena(self, cfg: Config, params: SynthParams, n_layers: int = 1,
+                        flags: int = ARENA_GEMV) -> "Arena":
+        c, p = cfg._c(), params._c()
+        h = ctypes.c_void_p()
+        self.check(lib().spt_arena_create_synthetic(self._h, ctypes.byref(c), ctypes.byref(p), n_layers,
+                                                    flags, ctypes.byref(h)))
+        return Arena(self, h, cfg, n_layers)
+
+    # ---- the block ----------------------------------------------------------
+    def forward_moe_batch(self, arena: "Arena", x: np.ndarray, batch: int, layer: int = 0,
+                          out: Optional[np.ndarray] = None, cancel: Optional[np.ndarray] = None,
+                          x_len: Optional[int] = None, out_len: Optional[int] = None) -> np.ndarray:
+        x = _f32(x)
+        if out is None:
+            out = np.empty_like(x)
+        xl = x.size if x_len is None else x_len
+        ol = out.size if out_len is None else out_len
+        self.check(lib().spt_forward_moe_batch(self._h, arena.handle, layer, _p(x), xl, _p(out), ol, batch,
+                                               _p(cancel)))
+        return out
+
+    def forward_moe(self, arena: "Arena", x: np.ndarray, layer: int = 0) -> np.ndarray:
+        x = _f32(x)
+        out = np.empty_like(x)
+        self.check(lib().spt_forward_moe(self._h, arena.handle, layer, _p(x), x.size, _p(out), out.size, None))
+        return out
+
+    def forward_moe_batch_device(self, arena: "Arena", x_ptr: int, out_ptr: int, batch: int, layer: int = 0):
+        self.check(lib().spt_forward_moe_batch_device(self._h, arena.handle, layer, ctypes.c_void_p(x_ptr),
+                                                      ctypes.c_void_p(out_ptr), batch))
+
+    def forward_moe_batch_reader(self, reader: Reader, cfg: Config, lw: LayerWeights, x: np.ndarray,
+                                 out: np.ndarray, batch: int, cancel: Optional[np.ndarray] = None):
+        """Drop-in one-shot forwardMoEBatch (validate + upload + run)."""
+        r, c, w = reader._c(), cfg._c(), lw._c()
+        self.check(lib().spt_forward_moe_batch_reader(self._h, ctypes.byref(r), ctypes.byref(c), ctypes.byref(w),
+                                                      _p(x), x.size, _p(out), out.size, batch, _p(cancel)))
+        return out
+
+    def last_routing(self, batch: int, experts: int, k: int) -> dict:
+        logits = np.empty(batch * experts, np.float32)
+        idx = np.empty(batch * k, np.int32)
+        w = np.empty(batch * k, np.float32)
+        perm = np.empty(max(batch * k, 1), np.int32)
+        counts = np.empty(experts, np.int32)
+        n = ctypes.c_int64()
+        self.check(lib().spt_last_routing(self._h, _p(logits), _p(idx), _p(w), _p(perm), _p(counts),
+                                          ctypes.byref(n)))
+        return dict(logits=logits.reshape(batch, experts), sel_idx=idx.reshape(batch, k),
+                    sel_w=w.reshape(batch, k), perm=perm[: n.value], counts=counts,
+                    dispatched=n.value)
+
+    # ---- stage entry points ------------------------------------------------
+    def route_moe_batch(self, data: np.ndarray, x: np.ndarray, router_bias: Optional[np.ndarray],
+                        batch: int, hidden: int, experts: int, cancel=None) -> np.ndarray:
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        x = _f32(x)
+        rb = None if router_bias is None else _f32(router_bias)
+        logits = np.empty(batch * experts, np.float32)
+        self.check(lib().spt_route_moe_batch(self._h, _p(data), data.size, _p(x), x.size, _p(rb), batch, hidden,
+                                             experts, _p(logits), _p(cancel)))
+        return logits.reshape(batch, experts)
+
+    def select_moe_batch(self, logits: np.ndarray, k: int):
+        logits = _f32(logits)
+        batch, experts = logits.shape
+        idx = np.empty(batch * k, np.int32)
+        w = np.empty(batch * k, np.float32)
+        self.check(lib().spt_select_moe_batch(self._h, _p(logits), batch, experts, k, _p(idx), _p(w)))
+        return idx.reshape(batch, k), w.reshape(batch, k)
+
+    def dispatch_moe_batch(self, index: np.ndarray, weight: np.ndarray, experts: int):
+        index = np.ascontiguousarray(index, dtype=np.int32)
+        weight = _f32(weight)
+        batch, k = index.shape
+        perm = np.empty(batch * k, np.int32)
+        offs = np.empty(experts + 1, np.int32)
+        n = ctypes.c_int64()
+        self.check(lib().spt_dispatch_moe_batch(self._h, _p(index), _p(weight), batch, k, experts, _p(perm),
+                                                _p(offs), ctypes.byref(n)))
+        return perm[: n.value], offs
+
+    def mul_moe_batch_expert(self, data: np.ndarray, input_: int, output: int, x: np.ndarray,
+                             x_offsets: Sequence[int], bias: Optional[np.ndarray], y: np.ndarray,
+                             y_offsets: Sequence[int], cancel=None) -> np.ndarray:
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        x = _f32(x)
+        xo = np.ascontiguousarray(x_offsets, dtype=np.int64)
+        yo = np.ascontiguousarray(y_offsets, dtype=np.int64)
+        b = None if bias is None else _f32(bias)
+        assert y.dtype == np.float32 and y.flags.c_contiguous
+        self.check(lib().spt_mul_moe_batch_expert(self._h, _p(data), data.size, input_, output, _p(x), x.size,
+                                                  _p(xo), xo.size, _p(b), _p(y), y.size, _p(yo), _p(cancel)))
+        return y
+
+    def swiglu(self, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+        g, u = _f32(gate), _f32(up)
+        act = np.empty_like(g)
+        self.check(lib().spt_swiglu(self._h, _p(g), _p(u), _p(act), g.size))
+        return act
+
+    def combine_moe_batch(self, results: np.ndarray, weight: np.ndarray, batch: int, k: int, hidden: int):
+        r, w = _f32(results), _f32(weight)
+        out = np.empty(batch * hidden, np.float32)
+        self.check(lib().spt_combine_moe_batch(self._h, _p(r), _p(w), batch, k, hidden, _p(out)))
+        return out.reshape(batch, hidden)
+
+    def rmsnorm(self, x: np.ndarray, weight: np.ndarray, batch: int, dim: int, eps: float):
+        x, w = _f32(x), _f32(weight)
+        y = np.empty(batch * dim, np.float32)
+        self.check(lib().spt_rmsnorm(self._h, _p(x), _p(w), batch, dim, eps, _p(y)))
+        return y.reshape(batch, dim)
+
+    def mul_q80(self, data: np.ndarray, input_: int, output: int, x: np.ndarray):
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        x = _f32(x)
+        y = np.empty(output, np.float32)
+        am = ctypes.c_int64()
+        best = ctypes.c_float()
+        self.check(lib().spt_mul_q80(self._h, _p(data), data.size, input_, output, _p(x), _p(y),
+                                     ctypes.byref(am), ctypes.byref(best)))
+        return y, am.value, np.float32(best.value)
+
+
+class Arena:
+    """HBM-resident expert arena (spt_arena)."""
+
+    def __init__(self, ctx: Context, handle, cfg: Config, n_layers: int, keep=()):
+        self.ctx, self._h, self.cfg, self.n_layers = ctx, handle, cfg, n_layers
+        self._keep = keep
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def nbytes(self) -> int:
+        return int(lib().spt_arena_bytes(self._h))
+
+    def close(self):
+        if self._h:
+            lib().spt_arena_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def synth_layer_host(cfg: Config, params: SynthParams, layer: int = 0) -> dict:
+    """Host copy of a synthetic layer in GGUF tensor layout (same bytes as the arena)."""
+    H, D, E = cfg.hidden_dim, cfg.expert_hidden_dim, cfg.num_experts
+    router = np.empty(E * H * 4, np.uint8)
+    rb = np.empty(E, np.float32)
+    gate = np.empty(E * D * (H // 32) * 17, np.uint8)
+    up = np.empty_like(gate)
+    down = np.empty(E * H * (D // 32) * 17, np.uint8)
+    gb = np.empty(E * D, np.float32)
+    ub = np.empty(E * D, np.float32)
+    db = np.empty(E * H, np.float32)
+    c, p = cfg._c(), params._c()
+    st = lib().spt_synth_layer_host(ctypes.byref(c), ctypes.byref(p), layer, _p(router), _p(rb), _p(gate),
+                                    _p(up), _p(down), _p(gb), _p(ub), _p(db))
+    if st != OK:
+        raise SptError(st, lib().spt_last_error(None).decode())
+    return dict(router=router, router_bias=rb, gate=gate, up=up, down=down, gate_bias=gb,
+                up_bias=ub, down_bias=db)
+
+
+def synth_normal_host(seed: int, stream: int, n: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    st = lib().spt_synth_normal_host(seed, stream, mean, std, _p(out), n)
+    if st != OK:
+        raise SptError(st, lib().spt_last_error(None).decode())
+    return out
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    """Compile csrc/ for sm_100a (see build.py)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_spt_build", os.path.join(_HERE, "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build(verbose=verbose, force=force)

@@ -1,0 +1,1093 @@
+// spt_api.cu -- C ABI (include/spt_moe.h): validation, HBM expert arena,
+// orchestration of the MoE block on one CUDA stream, stage entry points.
+//
+// Validation follows forwardMoEBatch's checks in order
+// (forward/moe_batch.go:81-136, forward/mxfp4_batch.go:17-27,
+// forward/moe_batch.go:196-219, forward/layer.go:279-289,
+// ggufmap/mmap_linux.go:318-334); each failure maps to one spt_status.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "../../include/spt_moe.h"
+#include "spt_internal.cuh"
+#include "spt_philox.h"
+
+using namespace spt;
+
+namespace {
+
+thread_local std::string g_tls_error;
+
+struct DevBuf {
+  void *p = nullptr;
+  size_t bytes = 0;
+  cudaError_t ensure(size_t want) {
+    if (want <= bytes) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    size_t cap = std::max<size_t>(want, 256);
+    cudaError_t st = cudaMalloc(&p, cap);
+    if (st == cudaSuccess) bytes = cap;
+    return st;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  template <class T>
+  T *as() const { return reinterpret_cast<T *>(p); }
+};
+
+}  // namespace
+
+struct spt_context {
+  int device = -1;
+  bool has_device = false;
+  int sm_count = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  // per-call scratch
+  DevBuf logits, sel_idx, sel_w, offsets, perm, slot_pos, act_list, meta, act, res, xdev, outdev;
+  int64_t last_T = 0, last_E = 0, last_K = 0;
+  bool have_routing = false;
+  // optional per-stage timing (events on the launching stream)
+  bool timing = false;
+  cudaEvent_t ev[SPT_NUM_STAGES + 1] = {};
+};
+
+struct spt_arena {
+  int device = -1;
+  spt_moe_config cfg{};
+  std::vector<LayerDev> layers;
+  std::vector<void *> allocs;
+  uint64_t bytes = 0;
+  uint32_t flags = 0;
+};
+
+namespace {
+
+spt_status fail(spt_context *ctx, spt_status st, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (ctx) ctx->err = buf;
+  else g_tls_error = buf;
+  return st;
+}
+
+spt_status cuda_fail(spt_context *ctx, cudaError_t e, const char *what) {
+  return fail(ctx, SPT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define SPT_CUDA(ctx, call)                                  \
+  do {                                                       \
+    cudaError_t _e = (call);                                 \
+    if (_e != cudaSuccess) return cuda_fail((ctx), _e, #call); \
+  } while (0)
+
+bool canceled(const volatile int32_t *cancel) { return cancel && *cancel != 0; }
+
+// moeBatchProduct (forward/moe_batch.go:29-38): every factor > 0, no
+// overflow of Go's int (int64).
+bool product(std::initializer_list<int64_t> vals, int64_t *out) {
+  int64_t n = 1;
+  for (int64_t v : vals) {
+    if (v <= 0 || n > std::numeric_limits<int64_t>::max() / v) return false;
+    n *= v;
+  }
+  if (out) *out = n;
+  return true;
+}
+
+bool named(const spt_tensor &t) { return t.name && t.name[0] != '\0'; }
+const char *tname(const spt_tensor &t) { return t.name ? t.name : ""; }
+
+// validateMoEBatchExpert (forward/mxfp4_batch.go:17-27)
+spt_status validate_expert(spt_context *ctx, const spt_tensor &t, int64_t input, int64_t output,
+                           int64_t experts) {
+  if (t.type != 39 || t.n_dims != 3 || t.shape[0] != (uint64_t)input ||
+      t.shape[1] != (uint64_t)output || t.shape[2] != (uint64_t)experts || input % 32 != 0)
+    return fail(ctx, SPT_ERR_EXPERT, "\"%s\": expected MXFP4 expert tensor [%lld %lld %lld]",
+                tname(t), (long long)input, (long long)output, (long long)experts);
+  int64_t n = 0;
+  if (!product({input / 32, 17, output, experts}, &n) || t.end < t.start ||
+      t.end - t.start != (uint64_t)n)
+    return fail(ctx, SPT_ERR_EXPERT, "\"%s\": invalid expert range or overflow", tname(t));
+  return SPT_OK;
+}
+
+// validateMoEBatchBias (forward/moe_batch.go:196-219)
+spt_status validate_bias(spt_context *ctx, const spt_tensor &t, int64_t dim, int64_t count) {
+  if (!named(t)) {
+    if (t.end != t.start) return fail(ctx, SPT_ERR_BIAS, "unnamed MoE bias has nonempty range");
+    return SPT_OK;
+  }
+  int64_t width = 4;
+  if (t.type == 1 || t.type == 30) width = 2;
+  else if (t.type != 0) return fail(ctx, SPT_ERR_BIAS, "\"%s\": unsupported bias type", tname(t));
+  int64_t n = 0;
+  const bool ok = product({dim, count, width}, &n);
+  uint32_t want_dims = 2;
+  if (count == 1 && t.n_dims == 1) want_dims = 1;
+  if (!ok || t.n_dims != want_dims || t.shape[0] != (uint64_t)dim ||
+      (want_dims == 2 && t.shape[1] != (uint64_t)count) || t.end < t.start ||
+      t.end - t.start != (uint64_t)n)
+    return fail(ctx, SPT_ERR_BIAS, "\"%s\": invalid bias shape or range", tname(t));
+  return SPT_OK;
+}
+
+// validateRangeLocked (ggufmap/mmap_linux.go:318-334) for a tensor that the
+// reference would map.
+spt_status validate_file_range(spt_context *ctx, const spt_reader *r, const spt_tensor &t) {
+  if (t.end <= t.start) return fail(ctx, SPT_ERR_FILE_RANGE, "tensor \"%s\": empty or invalid range", tname(t));
+  if (t.end > r->size) return fail(ctx, SPT_ERR_FILE_RANGE, "tensor \"%s\": range exceeds file size", tname(t));
+  return SPT_OK;
+}
+
+spt_status validate_config(spt_context *ctx, const spt_moe_config *cfg) {
+  const int64_t h = cfg->hidden_dim, d = cfg->expert_hidden_dim, e = cfg->num_experts,
+                k = cfg->num_experts_used;
+  if (!product({h, 4}, nullptr) || k <= 0 || k > e || d <= 0)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  return SPT_OK;
+}
+
+spt_status validate_layer(spt_context *ctx, const spt_reader *reader, const spt_moe_config *cfg,
+                          const spt_layer_weights *lw) {
+  if (!reader || !cfg || !lw)
+    return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
+  spt_status st = validate_config(ctx, cfg);
+  if (st) return st;
+  const int64_t h = cfg->hidden_dim, d = cfg->expert_hidden_dim, e = cfg->num_experts;
+  const spt_tensor &router = lw->ffn_gate_inp;
+  int64_t router_bytes = 0;
+  const bool ok = product({h, e, 4}, &router_bytes);
+  if (!ok || router.type != 0 || router.n_dims != 2 || router.shape[0] != (uint64_t)h ||
+      router.shape[1] != (uint64_t)e || router.end < router.start ||
+      router.end - router.start != (uint64_t)router_bytes)
+    return fail(ctx, SPT_ERR_ROUTER, "\"%s\": invalid F32 router shape or range", tname(router));
+  if ((st = validate_expert(ctx, lw->ffn_gate_exps, h, d, e))) return st;
+  if ((st = validate_expert(ctx, lw->ffn_up_exps, h, d, e))) return st;
+  if ((st = validate_expert(ctx, lw->ffn_down_exps, d, h, e))) return st;
+  if ((st = validate_bias(ctx, lw->ffn_gate_inp_bias, e, 1))) return st;
+  if ((st = validate_bias(ctx, lw->ffn_gate_exps_bias, d, e))) return st;
+  if ((st = validate_bias(ctx, lw->ffn_up_exps_bias, d, e))) return st;
+  if ((st = validate_bias(ctx, lw->ffn_down_exps_bias, h, e))) return st;
+  // readFloatVector on the router bias needs a 1-D [E] tensor (layer.go:285-289)
+  if (named(lw->ffn_gate_inp_bias) && lw->ffn_gate_inp_bias.n_dims != 1)
+    return fail(ctx, SPT_ERR_BIAS, "\"%s\": invalid float vector shape or range",
+                tname(lw->ffn_gate_inp_bias));
+  const spt_tensor *mapped[] = {&lw->ffn_gate_inp_bias, &router, &lw->ffn_gate_exps,
+                                &lw->ffn_up_exps, &lw->ffn_down_exps, &lw->ffn_gate_exps_bias,
+                                &lw->ffn_up_exps_bias, &lw->ffn_down_exps_bias};
+  for (const spt_tensor *t : mapped) {
+    if (t != &router && t != &lw->ffn_gate_exps && t != &lw->ffn_up_exps &&
+        t != &lw->ffn_down_exps && !named(*t))
+      continue;
+    if ((st = validate_file_range(ctx, reader, *t))) return st;
+  }
+  if (!reader->base && reader->size > 0)
+    return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
+  return SPT_OK;
+}
+
+// readFloatVector element decode (forward/layer.go:291-301, q40.go:149-180).
+float f16_to_f32(uint16_t bits) {
+  uint32_t sign = (uint32_t)(bits & 0x8000u) << 16;
+  uint32_t exponent = (bits >> 10) & 0x1fu;
+  uint32_t mantissa = bits & 0x3ffu;
+  uint32_t out;
+  if (exponent == 0) {
+    if (mantissa == 0) {
+      out = sign;
+    } else {
+      uint32_t ex = 113;
+      while ((mantissa & 0x400u) == 0) {
+        mantissa <<= 1;
+        ex--;
+      }
+      out = sign | ex << 23 | (mantissa & 0x3ffu) << 13;
+    }
+  } else if (exponent == 31) {
+    out = sign | 0x7f800000u | mantissa << 13;
+  } else {
+    out = sign | (exponent + 112) << 23 | mantissa << 13;
+  }
+  float f;
+  memcpy(&f, &out, 4);
+  return f;
+}
+
+void decode_floats(const uint8_t *src, uint32_t type, int64_t n, float *dst) {
+  for (int64_t i = 0; i < n; ++i) {
+    if (type == 0) {
+      memcpy(&dst[i], src + 4 * i, 4);
+    } else {
+      uint16_t hbits;
+      memcpy(&hbits, src + 2 * i, 2);
+      if (type == 1) {
+        dst[i] = f16_to_f32(hbits);
+      } else {
+        uint32_t u = (uint32_t)hbits << 16;
+        memcpy(&dst[i], &u, 4);
+      }
+    }
+  }
+}
+
+// ---- host synthetic generation (shared by the arena and the host copy) --
+void synth_normal(uint64_t seed, uint32_t tag, float mean, float sd, float *out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    uint32_t a, b;
+    synth_uniform_pair(seed, tag, (uint64_t)i, &a, &b);
+    const double u1 = ((double)a + 1.0) / 4294967296.0;
+    const double u2 = (double)b / 4294967296.0;
+    const double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+    out[i] = (float)((double)mean + (double)sd * z);
+  }
+}
+
+void synth_router_bias(const spt_moe_config *cfg, const spt_synth_params *p, int64_t layer,
+                       float *bias) {
+  const int64_t E = cfg->num_experts;
+  if (p->router_bias) synth_normal(p->seed, synth_tag(layer, kSynthRouterBias), 0.0f, p->bias_std, bias, E);
+  else std::fill(bias, bias + E, 0.0f);
+  if (p->zipf_s > 0.0f) {
+    // seeded permutation of ranks 1..E (Fisher-Yates), bias += beta*(-s*ln(rank))
+    std::vector<int64_t> rank(E);
+    for (int64_t i = 0; i < E; ++i) rank[i] = i + 1;
+    for (int64_t i = E - 1; i > 0; --i) {
+      uint32_t a, b;
+      synth_uniform_pair(p->seed, synth_tag(layer, kSynthZipfPerm), (uint64_t)i, &a, &b);
+      const int64_t j = (int64_t)(((uint64_t)a * (uint64_t)(i + 1)) >> 32);
+      std::swap(rank[i], rank[j]);
+    }
+    for (int64_t e = 0; e < E; ++e)
+      bias[e] = (float)((double)bias[e] +
+                        (double)p->zipf_beta * (-(double)p->zipf_s * log((double)rank[e])));
+  }
+}
+
+// ---- arena ----------------------------------------------------------------
+template <class T>
+spt_status arena_alloc(spt_context *ctx, spt_arena *a, size_t count, T **out) {
+  void *p = nullptr;
+  const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaMalloc(arena)");
+  a->allocs.push_back(p);
+  a->bytes += bytes;
+  *out = reinterpret_cast<T *>(p);
+  return SPT_OK;
+}
+
+spt_status upload(spt_context *ctx, void *dst, const void *src, size_t bytes) {
+  // host -> device through a pinned staging buffer (the arena is uploaded once)
+  static const size_t kChunk = 32u << 20;
+  void *pinned = nullptr;
+  SPT_CUDA(ctx, cudaMallocHost(&pinned, std::min(bytes, kChunk) + 16));
+  for (size_t off = 0; off < bytes; off += kChunk) {
+    const size_t n = std::min(kChunk, bytes - off);
+    memcpy(pinned, (const uint8_t *)src + off, n);
+    cudaError_t e = cudaMemcpyAsync((uint8_t *)dst + off, pinned, n, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+      cudaFreeHost(pinned);
+      return cuda_fail(ctx, e, "upload");
+    }
+  }
+  cudaFreeHost(pinned);
+  return SPT_OK;
+}
+
+spt_status alloc_g8(spt_context *ctx, spt_arena *a, int64_t experts, int rows, int blocks,
+                    MatrixG8 *m, uint4 **nib, uint32_t **scl) {
+  spt_status st = arena_alloc(ctx, a, g8_nib_count(experts, rows, blocks), nib);
+  if (st) return st;
+  if ((st = arena_alloc(ctx, a, g8_scl_count(experts, rows, blocks), scl))) return st;
+  SPT_CUDA(ctx, cudaMemsetAsync(*nib, 0, g8_nib_count(experts, rows, blocks) * sizeof(uint4), ctx->stream));
+  SPT_CUDA(ctx, cudaMemsetAsync(*scl, 0, g8_scl_count(experts, rows, blocks) * sizeof(uint32_t), ctx->stream));
+  m->nib = *nib;
+  m->scl = *scl;
+  m->rows = rows;
+  m->blocks = blocks;
+  m->groups = (rows + 7) / 8;
+  m->quads = (blocks + 3) / 4;
+  return SPT_OK;
+}
+
+spt_status upload_mxfp4(spt_context *ctx, spt_arena *a, const uint8_t *src, int64_t experts,
+                        int rows, int blocks, MatrixG8 *m) {
+  uint4 *nib = nullptr;
+  uint32_t *scl = nullptr;
+  spt_status st = alloc_g8(ctx, a, experts, rows, blocks, m, &nib, &scl);
+  if (st) return st;
+  const size_t raw = (size_t)experts * rows * blocks * 17;
+  DevBuf staging;
+  SPT_CUDA(ctx, staging.ensure(raw));
+  if ((st = upload(ctx, staging.p, src, raw))) {
+    staging.release();
+    return st;
+  }
+  cudaError_t e = launch_repack_g8(staging.as<uint8_t>(), experts, rows, blocks, nib, scl, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  staging.release();
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "repack");
+  return SPT_OK;
+}
+
+spt_status upload_floats(spt_context *ctx, spt_arena *a, const float *host, size_t n,
+                         const float **out) {
+  float *d = nullptr;
+  spt_status st = arena_alloc(ctx, a, n, &d);
+  if (st) return st;
+  if ((st = upload(ctx, d, host, n * sizeof(float)))) return st;
+  *out = d;
+  return SPT_OK;
+}
+
+spt_status require_device(spt_context *ctx) {
+  if (!ctx) return fail(nullptr, SPT_ERR_NULL_ARG, "nil context");
+  if (!ctx->has_device) return fail(ctx, SPT_ERR_NO_DEVICE, "context has no CUDA device");
+  cudaError_t e = cudaSetDevice(ctx->device);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaSetDevice");
+  return SPT_OK;
+}
+
+spt_status ensure_scratch(spt_context *ctx, int64_t T, const spt_moe_config &c) {
+  const int64_t H = c.hidden_dim, D = c.expert_hidden_dim, E = c.num_experts, K = c.num_experts_used;
+  const int64_t S = std::max<int64_t>(T * K, 1);
+  SPT_CUDA(ctx, ctx->logits.ensure(sizeof(float) * std::max<int64_t>(T * E, 1)));
+  SPT_CUDA(ctx, ctx->sel_idx.ensure(sizeof(int32_t) * S));
+  SPT_CUDA(ctx, ctx->sel_w.ensure(sizeof(float) * S));
+  SPT_CUDA(ctx, ctx->offsets.ensure(sizeof(int32_t) * (E + 1)));
+  SPT_CUDA(ctx, ctx->perm.ensure(sizeof(int32_t) * S));
+  SPT_CUDA(ctx, ctx->slot_pos.ensure(sizeof(int32_t) * S));
+  SPT_CUDA(ctx, ctx->act_list.ensure(sizeof(int32_t) * E));
+  SPT_CUDA(ctx, ctx->meta.ensure(sizeof(int32_t) * 4));
+  SPT_CUDA(ctx, ctx->act.ensure(sizeof(float) * S * D));
+  SPT_CUDA(ctx, ctx->res.ensure(sizeof(float) * S * H));
+  return SPT_OK;
+}
+
+int pick_mt(int64_t T, int64_t K, int64_t E) {
+  const double avg = (double)(T * K) / (double)E;
+  if (T <= 1 || avg <= 0.5) return 1;
+  if (avg <= 1.5) return 2;
+  if (avg <= 3.0) return 4;
+  return 8;
+}
+
+// The whole block on device pointers (enqueue only).
+spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
+                          float *out, int64_t T) {
+  const spt_moe_config &c = arena->cfg;
+  const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
+            K = (int)c.num_experts_used;
+  if (E > kDispatchMaxExperts || K > kSelectMaxK)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "experts %d > %d or top-k %d > %d unsupported", E,
+                kDispatchMaxExperts, K, kSelectMaxK);
+  spt_status st = ensure_scratch(ctx, T, c);
+  if (st) return st;
+  const LayerDev &L = arena->layers[(size_t)layer];
+  cudaStream_t s = ctx->stream;
+#define SPT_MARK(i) \
+  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[i], s))
+  SPT_MARK(0);
+  SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s));
+  SPT_MARK(1);
+  SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, ctx->sel_idx.as<int32_t>(),
+                              ctx->sel_w.as<float>(), s));
+  SPT_MARK(2);
+  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)(T * K), E,
+                                ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
+                                ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
+                                ctx->meta.as<int32_t>(), s));
+  const int max_active = (int)std::min<int64_t>(E, T * K);
+  const int mt = pick_mt(T, K, E);
+  GemvLaunch gu;
+  gu.m0 = L.gate;
+  gu.m1 = L.up;
+  gu.bias0 = L.gate_bias;
+  gu.bias1 = L.up_bias;
+  gu.x = x;
+  gu.x_stride = H;
+  gu.y = ctx->act.as<float>();
+  gu.y_stride = D;
+  gu.perm = ctx->perm.as<int32_t>();
+  gu.offsets = ctx->offsets.as<int32_t>();
+  gu.act_list = ctx->act_list.as<int32_t>();
+  gu.meta = ctx->meta.as<int32_t>();
+  gu.top_k = K;
+  gu.mode = kRowsMoEGateUp;
+  gu.gate_up = true;
+  gu.max_active = max_active;
+  gu.mt = mt;
+  SPT_MARK(3);
+  SPT_CUDA(ctx, launch_gemv(gu, ctx->sm_count, s));
+  SPT_MARK(4);
+  GemvLaunch dn = gu;
+  dn.m0 = L.down;
+  dn.m1 = MatrixG8{};
+  dn.bias0 = L.down_bias;
+  dn.bias1 = nullptr;
+  dn.x = ctx->act.as<float>();
+  dn.x_stride = D;
+  dn.y = ctx->res.as<float>();
+  dn.y_stride = H;
+  dn.mode = kRowsMoEDown;
+  dn.gate_up = false;
+  SPT_CUDA(ctx, launch_gemv(dn, ctx->sm_count, s));
+  SPT_MARK(5);
+  SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), ctx->sel_w.as<float>(),
+                               ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
+  SPT_MARK(6);
+#undef SPT_MARK
+  ctx->last_T = T;
+  ctx->last_E = E;
+  ctx->last_K = K;
+  ctx->have_routing = true;
+  return SPT_OK;
+}
+
+spt_status check_batch(spt_context *ctx, const spt_moe_config &c, const float *x, int64_t x_len,
+                       const float *out, int64_t out_len, int64_t batch) {
+  int64_t n = 0;
+  const bool ok = product({batch, c.hidden_dim, 4}, &n);
+  if (!ok || x_len != n / 4 || out_len != n / 4 || c.num_experts_used <= 0 ||
+      c.num_experts_used > c.num_experts || c.expert_hidden_dim <= 0)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  if (!x || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE input or output");
+  const uintptr_t xs = (uintptr_t)x, ys = (uintptr_t)out;
+  if ((xs <= ys && ys - xs < (uintptr_t)n) || (ys < xs && xs - ys < (uintptr_t)n))
+    return fail(ctx, SPT_ERR_OVERLAP, "MoE input and output overlap");
+  return SPT_OK;
+}
+
+spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
+                        int64_t x_len, float *out, int64_t out_len, int64_t batch,
+                        const volatile int32_t *cancel) {
+  if (!ctx || !arena) return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  spt_status st = check_batch(ctx, arena->cfg, x, x_len, out, out_len, batch);
+  if (st) return st;
+  if (layer < 0 || layer >= (int64_t)arena->layers.size())
+    return fail(ctx, SPT_ERR_DIMENSIONS, "layer %lld out of range", (long long)layer);
+  if ((st = require_device(ctx))) return st;
+  const size_t bytes = sizeof(float) * (size_t)x_len;
+  SPT_CUDA(ctx, ctx->xdev.ensure(bytes));
+  SPT_CUDA(ctx, ctx->outdev.ensure(bytes));
+  SPT_CUDA(ctx, cudaMemcpyAsync(ctx->xdev.p, x, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  if ((st = forward_device(ctx, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch)))
+    return st;
+  SPT_CUDA(ctx, cudaMemcpyAsync(out, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  return SPT_OK;
+}
+
+// Temporary device buffer for stage entry points.
+struct Tmp {
+  void *p = nullptr;
+  ~Tmp() {
+    if (p) cudaFree(p);
+  }
+  cudaError_t alloc(size_t n) { return cudaMalloc(&p, std::max<size_t>(n, 16)); }
+  template <class T>
+  T *as() const { return reinterpret_cast<T *>(p); }
+};
+
+}  // namespace
+
+// =========================================================================
+extern "C" {
+
+const char *spt_status_string(spt_status s) {
+  switch (s) {
+    case SPT_OK: return "ok";
+    case SPT_ERR_NULL_ARG: return "nil argument";
+    case SPT_ERR_DIMENSIONS: return "invalid MoE batch dimensions";
+    case SPT_ERR_OVERLAP: return "MoE input and output overlap";
+    case SPT_ERR_ROUTER: return "invalid F32 router shape or range";
+    case SPT_ERR_EXPERT: return "invalid MXFP4 expert tensor";
+    case SPT_ERR_BIAS: return "invalid MoE bias";
+    case SPT_ERR_FILE_RANGE: return "tensor range outside the file";
+    case SPT_ERR_SCRATCH: return "MoE batch scratch dimensions mismatch";
+    case SPT_ERR_CANCELED: return "context canceled";
+    case SPT_ERR_CUDA: return "CUDA error";
+    case SPT_ERR_NCCL: return "NCCL error";
+    case SPT_ERR_TIMEOUT: return "device wait timed out";
+    case SPT_ERR_UNSUPPORTED: return "unsupported";
+    case SPT_ERR_NO_DEVICE: return "no CUDA device";
+  }
+  return "unknown status";
+}
+
+spt_status spt_context_create(int device, spt_context **out) {
+  if (!out) return fail(nullptr, SPT_ERR_NULL_ARG, "nil output pointer");
+  *out = nullptr;
+  spt_context *ctx = new spt_context();
+  if (device >= 0) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device >= n) {
+      cudaGetLastError();
+      spt_status st = fail(nullptr, SPT_ERR_NO_DEVICE, "CUDA device %d unavailable", device);
+      delete ctx;
+      return st;
+    }
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      spt_status st = fail(nullptr, SPT_ERR_NO_DEVICE, "CUDA device %d: %s", device, cudaGetErrorString(e));
+      delete ctx;
+      return st;
+    }
+    cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    ctx->device = device;
+    ctx->has_device = true;
+    ctx->stream = ctx->own_stream;
+  }
+  *out = ctx;
+  return SPT_OK;
+}
+
+void spt_context_destroy(spt_context *ctx) {
+  if (!ctx) return;
+  if (ctx->has_device) {
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (DevBuf *b : {&ctx->logits, &ctx->sel_idx, &ctx->sel_w, &ctx->offsets, &ctx->perm,
+                      &ctx->slot_pos, &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res,
+                      &ctx->xdev, &ctx->outdev})
+      b->release();
+    for (cudaEvent_t &e : ctx->ev)
+      if (e) cudaEventDestroy(e);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  }
+  delete ctx;
+}
+
+spt_status spt_set_stage_timing(spt_context *ctx, int enable) {
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  if (enable)
+    for (cudaEvent_t &e : ctx->ev)
+      if (!e) SPT_CUDA(ctx, cudaEventCreate(&e));
+  ctx->timing = enable != 0;
+  return SPT_OK;
+}
+
+int spt_stage_times(spt_context *ctx, float *ms, int n) {
+  if (!ctx || !ctx->timing || !ms) return 0;
+  if (cudaEventSynchronize(ctx->ev[SPT_NUM_STAGES]) != cudaSuccess) return 0;
+  int w = 0;
+  for (int i = 0; i < SPT_NUM_STAGES && i < n; ++i, ++w)
+    if (cudaEventElapsedTime(&ms[i], ctx->ev[i], ctx->ev[i + 1]) != cudaSuccess) ms[i] = -1.0f;
+  return w;
+}
+
+int spt_kernels_per_forward(spt_context *ctx) {
+  (void)ctx;
+  return 6;
+}
+
+const char *spt_last_error(const spt_context *ctx) {
+  return ctx ? ctx->err.c_str() : g_tls_error.c_str();
+}
+
+void *spt_context_stream(spt_context *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+spt_status spt_context_set_stream(spt_context *ctx, void *stream) {
+  if (!ctx) return fail(nullptr, SPT_ERR_NULL_ARG, "nil context");
+  ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+  return SPT_OK;
+}
+
+spt_status spt_context_sync(spt_context *ctx) {
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return SPT_OK;
+}
+
+spt_status spt_validate_moe_layer(spt_context *ctx, const spt_reader *reader,
+                                  const spt_moe_config *cfg, const spt_layer_weights *lw) {
+  return validate_layer(ctx, reader, cfg, lw);
+}
+
+spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,
+                            const spt_layer_weights *layers, int64_t n_layers, uint32_t flags,
+                            spt_arena **out) {
+  if (!out || !readers || !cfg || !layers || n_layers <= 0)
+    return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
+  *out = nullptr;
+  for (int64_t l = 0; l < n_layers; ++l) {
+    spt_status st = validate_layer(ctx, &readers[l], cfg, &layers[l]);
+    if (st) return st;
+  }
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  if (flags == 0) flags = SPT_ARENA_GEMV;
+  const int64_t H = cfg->hidden_dim, D = cfg->expert_hidden_dim, E = cfg->num_experts;
+  if (H > (1 << 30) || D > (1 << 30)) return fail(ctx, SPT_ERR_UNSUPPORTED, "dimensions too large");
+  spt_arena *a = new spt_arena();
+  a->device = ctx->device;
+  a->cfg = *cfg;
+  a->flags = flags;
+  a->layers.resize((size_t)n_layers);
+  std::vector<float> tmp;
+  for (int64_t l = 0; l < n_layers && st == SPT_OK; ++l) {
+    const spt_reader &r = readers[l];
+    const spt_layer_weights &w = layers[l];
+    LayerDev &L = a->layers[(size_t)l];
+    float *router = nullptr;
+    if ((st = arena_alloc(ctx, a, (size_t)(E * H), &router))) break;
+    if ((st = upload(ctx, router, r.base + w.ffn_gate_inp.start, (size_t)(E * H * 4)))) break;
+    L.router = router;
+    tmp.assign((size_t)E, 0.0f);
+    if (named(w.ffn_gate_inp_bias))
+      decode_floats(r.base + w.ffn_gate_inp_bias.start, w.ffn_gate_inp_bias.type, E, tmp.data());
+    if ((st = upload_floats(ctx, a, tmp.data(), (size_t)E, &L.router_bias))) break;
+    struct {
+      const spt_tensor *t;
+      int64_t dim;
+      const float **dst;
+    } biases[] = {{&w.ffn_gate_exps_bias, D, &L.gate_bias},
+                  {&w.ffn_up_exps_bias, D, &L.up_bias},
+                  {&w.ffn_down_exps_bias, H, &L.down_bias}};
+    for (auto &b : biases) {
+      tmp.assign((size_t)(E * b.dim), 0.0f);
+      if (named(*b.t)) decode_floats(r.base + b.t->start, b.t->type, E * b.dim, tmp.data());
+      if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), b.dst))) break;
+    }
+    if (st) break;
+    if ((st = upload_mxfp4(ctx, a, r.base + w.ffn_gate_exps.start, E, (int)D, (int)(H / 32), &L.gate))) break;
+    if ((st = upload_mxfp4(ctx, a, r.base + w.ffn_up_exps.start, E, (int)D, (int)(H / 32), &L.up))) break;
+    if ((st = upload_mxfp4(ctx, a, r.base + w.ffn_down_exps.start, E, (int)H, (int)(D / 32), &L.down))) break;
+  }
+  if (st) {
+    spt_arena_destroy(a);
+    return st;
+  }
+  *out = a;
+  return SPT_OK;
+}
+
+spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cfg,
+                                      const spt_synth_params *p, int64_t n_layers, uint32_t flags,
+                                      spt_arena **out) {
+  if (!out || !cfg || !p || n_layers <= 0)
+    return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  *out = nullptr;
+  spt_status st = validate_config(ctx, cfg);
+  if (st) return st;
+  const int64_t H = cfg->hidden_dim, D = cfg->expert_hidden_dim, E = cfg->num_experts;
+  if (H % 32 != 0 || D % 32 != 0)
+    return fail(ctx, SPT_ERR_EXPERT, "expected MXFP4 expert tensor dimensions divisible by 32");
+  if ((st = require_device(ctx))) return st;
+  if (flags == 0) flags = SPT_ARENA_GEMV;
+  spt_arena *a = new spt_arena();
+  a->device = ctx->device;
+  a->cfg = *cfg;
+  a->flags = flags;
+  a->layers.resize((size_t)n_layers);
+  std::vector<float> tmp;
+  for (int64_t l = 0; l < n_layers && st == SPT_OK; ++l) {
+    LayerDev &L = a->layers[(size_t)l];
+    tmp.resize((size_t)(E * H));
+    synth_normal(p->seed, synth_tag(l, kSynthRouter), 0.0f, p->router_std, tmp.data(), E * H);
+    if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), &L.router))) break;
+    tmp.resize((size_t)E);
+    synth_router_bias(cfg, p, l, tmp.data());
+    if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), &L.router_bias))) break;
+    struct {
+      uint32_t kind;
+      int64_t dim;
+      const float **dst;
+    } biases[] = {{kSynthGateBias, D, &L.gate_bias}, {kSynthUpBias, D, &L.up_bias},
+                  {kSynthDownBias, H, &L.down_bias}};
+    for (auto &b : biases) {
+      tmp.assign((size_t)(E * b.dim), 0.0f);
+      if (p->expert_bias) synth_normal(p->seed, synth_tag(l, b.kind), 0.0f, p->bias_std, tmp.data(), E * b.dim);
+      if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), b.dst))) break;
+    }
+    if (st) break;
+    struct {
+      uint32_t kind;
+      int rows, blocks;
+      MatrixG8 *m;
+    } mats[] = {{kSynthGate, (int)D, (int)(H / 32), &L.gate},
+                {kSynthUp, (int)D, (int)(H / 32), &L.up},
+                {kSynthDown, (int)H, (int)(D / 32), &L.down}};
+    for (auto &m : mats) {
+      uint4 *nib = nullptr;
+      uint32_t *scl = nullptr;
+      if ((st = alloc_g8(ctx, a, E, m.rows, m.blocks, m.m, &nib, &scl))) break;
+      cudaError_t e = launch_synth_g8(p->seed, synth_tag(l, m.kind), E, m.rows, m.blocks,
+                                      p->scale_lo, p->scale_hi, nib, scl, ctx->stream);
+      if (e != cudaSuccess) {
+        st = cuda_fail(ctx, e, "synth");
+        break;
+      }
+    }
+  }
+  if (st == SPT_OK) {
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) st = cuda_fail(ctx, e, "synth sync");
+  }
+  if (st) {
+    spt_arena_destroy(a);
+    return st;
+  }
+  *out = a;
+  return SPT_OK;
+}
+
+void spt_arena_destroy(spt_arena *a) {
+  if (!a) return;
+  if (a->device >= 0) cudaSetDevice(a->device);
+  for (void *p : a->allocs) cudaFree(p);
+  delete a;
+}
+
+uint64_t spt_arena_bytes(const spt_arena *a) { return a ? a->bytes : 0; }
+
+spt_status spt_synth_layer_host(const spt_moe_config *cfg, const spt_synth_params *p, int64_t layer,
+                                uint8_t *router, float *router_bias, uint8_t *gate, uint8_t *up,
+                                uint8_t *down, float *gate_bias, float *up_bias, float *down_bias) {
+  if (!cfg || !p) return fail(nullptr, SPT_ERR_NULL_ARG, "nil argument");
+  spt_status st = validate_config(nullptr, cfg);
+  if (st) return st;
+  const int64_t H = cfg->hidden_dim, D = cfg->expert_hidden_dim, E = cfg->num_experts;
+  if (H % 32 != 0 || D % 32 != 0) return fail(nullptr, SPT_ERR_EXPERT, "dimensions not divisible by 32");
+  if (router) {
+    std::vector<float> tmp((size_t)(E * H));
+    synth_normal(p->seed, synth_tag(layer, kSynthRouter), 0.0f, p->router_std, tmp.data(), E * H);
+    memcpy(router, tmp.data(), tmp.size() * 4);
+  }
+  if (router_bias) synth_router_bias(cfg, p, layer, router_bias);
+  struct {
+    uint32_t kind;
+    int64_t dim;
+    float *dst;
+  } biases[] = {{kSynthGateBias, D, gate_bias}, {kSynthUpBias, D, up_bias}, {kSynthDownBias, H, down_bias}};
+  for (auto &b : biases) {
+    if (!b.dst) continue;
+    if (p->expert_bias) synth_normal(p->seed, synth_tag(layer, b.kind), 0.0f, p->bias_std, b.dst, E * b.dim);
+    else std::fill(b.dst, b.dst + E * b.dim, 0.0f);
+  }
+  struct {
+    uint32_t kind;
+    int64_t rows, blocks;
+    uint8_t *dst;
+  } mats[] = {{kSynthGate, D, H / 32, gate}, {kSynthUp, D, H / 32, up}, {kSynthDown, H, D / 32, down}};
+  for (auto &m : mats) {
+    if (!m.dst) continue;
+    const int64_t n = E * m.rows * m.blocks;
+    for (int64_t i = 0; i < n; ++i)
+      synth_mxfp4_block(p->seed, synth_tag(layer, m.kind), (uint64_t)i, p->scale_lo, p->scale_hi, m.dst + 17 * i);
+  }
+  return SPT_OK;
+}
+
+spt_status spt_synth_normal_host(uint64_t seed, uint64_t stream, float mean, float sd, float *out,
+                                 int64_t n) {
+  if (!out && n > 0) return fail(nullptr, SPT_ERR_NULL_ARG, "nil output");
+  synth_normal(seed, (uint32_t)stream, mean, sd, out, n);
+  return SPT_OK;
+}
+
+spt_status spt_forward_moe_batch(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
+                                 int64_t x_len, float *out, int64_t out_len, int64_t batch,
+                                 const volatile int32_t *cancel) {
+  return forward_host(ctx, arena, layer, x, x_len, out, out_len, batch, cancel);
+}
+
+spt_status spt_forward_moe(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
+                           int64_t x_len, float *out, int64_t out_len,
+                           const volatile int32_t *cancel) {
+  return forward_host(ctx, arena, layer, x, x_len, out, out_len, 1, cancel);
+}
+
+spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int64_t layer,
+                                        const float *x, float *out, int64_t batch) {
+  if (!ctx || !arena || !x || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (batch <= 0 || layer < 0 || layer >= (int64_t)arena->layers.size())
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  return forward_device(ctx, arena, layer, x, out, batch);
+}
+
+spt_status spt_forward_moe_batch_reader(spt_context *ctx, const spt_reader *reader,
+                                        const spt_moe_config *cfg, const spt_layer_weights *lw,
+                                        const float *x, int64_t x_len, float *out, int64_t out_len,
+                                        int64_t batch, const volatile int32_t *cancel) {
+  if (!ctx || !reader || !cfg || !lw)
+    return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  spt_status st = validate_config(ctx, cfg);
+  if (st) return st;
+  if ((st = check_batch(ctx, *cfg, x, x_len, out, out_len, batch))) return st;
+  if ((st = validate_layer(ctx, reader, cfg, lw))) return st;
+  spt_arena *arena = nullptr;
+  if ((st = spt_arena_create(ctx, reader, cfg, lw, 1, SPT_ARENA_GEMV, &arena))) return st;
+  st = forward_host(ctx, arena, 0, x, x_len, out, out_len, batch, cancel);
+  spt_arena_destroy(arena);
+  return st;
+}
+
+spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index, float *sel_weight,
+                            int32_t *perm, int32_t *expert_count, int64_t *dispatched) {
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  if (!ctx->have_routing) return fail(ctx, SPT_ERR_DIMENSIONS, "no forward call yet");
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  const int64_t T = ctx->last_T, E = ctx->last_E, K = ctx->last_K;
+  int32_t meta[2];
+  SPT_CUDA(ctx, cudaMemcpy(meta, ctx->meta.p, sizeof meta, cudaMemcpyDeviceToHost));
+  if (logits) SPT_CUDA(ctx, cudaMemcpy(logits, ctx->logits.p, sizeof(float) * T * E, cudaMemcpyDeviceToHost));
+  if (sel_index) SPT_CUDA(ctx, cudaMemcpy(sel_index, ctx->sel_idx.p, sizeof(int32_t) * T * K, cudaMemcpyDeviceToHost));
+  if (sel_weight) SPT_CUDA(ctx, cudaMemcpy(sel_weight, ctx->sel_w.p, sizeof(float) * T * K, cudaMemcpyDeviceToHost));
+  if (perm && meta[1] > 0) SPT_CUDA(ctx, cudaMemcpy(perm, ctx->perm.p, sizeof(int32_t) * meta[1], cudaMemcpyDeviceToHost));
+  if (expert_count) {
+    std::vector<int32_t> off((size_t)E + 1);
+    SPT_CUDA(ctx, cudaMemcpy(off.data(), ctx->offsets.p, sizeof(int32_t) * (E + 1), cudaMemcpyDeviceToHost));
+    for (int64_t e = 0; e < E; ++e) expert_count[e] = off[e + 1] - off[e];
+  }
+  if (dispatched) *dispatched = meta[1];
+  return SPT_OK;
+}
+
+spt_status spt_route_moe_batch(spt_context *ctx, const uint8_t *data, uint64_t data_len,
+                               const float *x, int64_t x_len, const float *router_bias,
+                               int64_t batch, int64_t hidden, int64_t experts, float *logits,
+                               const volatile int32_t *cancel) {
+  if (!data || !x || !logits) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  int64_t nw = 0, nx = 0, nl = 0;
+  if (!product({experts, hidden, 4}, &nw) || !product({batch, hidden}, &nx) ||
+      !product({batch, experts}, &nl) || data_len != (uint64_t)nw || x_len != nx)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid router dimensions");
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  Tmp dw, dx, db, dl;
+  SPT_CUDA(ctx, dw.alloc((size_t)nw));
+  SPT_CUDA(ctx, dx.alloc(sizeof(float) * (size_t)nx));
+  SPT_CUDA(ctx, dl.alloc(sizeof(float) * (size_t)nl));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dw.p, data, (size_t)nw, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dx.p, x, sizeof(float) * (size_t)nx, cudaMemcpyHostToDevice, ctx->stream));
+  if (router_bias) {
+    SPT_CUDA(ctx, db.alloc(sizeof(float) * (size_t)experts));
+    SPT_CUDA(ctx, cudaMemcpyAsync(db.p, router_bias, sizeof(float) * (size_t)experts, cudaMemcpyHostToDevice, ctx->stream));
+  }
+  SPT_CUDA(ctx, launch_router(dw.as<float>(), dx.as<float>(), db.as<float>(), (int)batch, (int)hidden,
+                              (int)experts, dl.as<float>(), 8, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(logits, dl.p, sizeof(float) * (size_t)nl, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  return SPT_OK;
+}
+
+spt_status spt_select_moe_batch(spt_context *ctx, const float *logits, int64_t batch, int64_t experts,
+                                int64_t k, int32_t *index, float *weight) {
+  if (!logits || !index || !weight) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (batch <= 0 || experts <= 0 || k <= 0) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid dimensions");
+  if (k > kSelectMaxK) return fail(ctx, SPT_ERR_UNSUPPORTED, "top-k > %d", kSelectMaxK);
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  Tmp dl, di, dw;
+  SPT_CUDA(ctx, dl.alloc(sizeof(float) * batch * experts));
+  SPT_CUDA(ctx, di.alloc(sizeof(int32_t) * batch * k));
+  SPT_CUDA(ctx, dw.alloc(sizeof(float) * batch * k));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dl.p, logits, sizeof(float) * batch * experts, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, launch_select(dl.as<float>(), (int)batch, (int)experts, (int)k, di.as<int32_t>(), dw.as<float>(), ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(index, di.p, sizeof(int32_t) * batch * k, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(weight, dw.p, sizeof(float) * batch * k, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return SPT_OK;
+}
+
+spt_status spt_dispatch_moe_batch(spt_context *ctx, const int32_t *index, const float *weight,
+                                  int64_t batch, int64_t k, int64_t experts, int32_t *perm,
+                                  int32_t *expert_offsets, int64_t *dispatched) {
+  if (!index || !weight || !perm || !expert_offsets) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (batch <= 0 || k <= 0 || experts <= 0) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid dimensions");
+  if (experts > kDispatchMaxExperts) return fail(ctx, SPT_ERR_UNSUPPORTED, "experts > %d", kDispatchMaxExperts);
+  const int64_t S = batch * k;
+  for (int64_t s = 0; s < S; ++s)
+    if (index[s] < 0 || index[s] >= experts) return fail(ctx, SPT_ERR_DIMENSIONS, "expert index out of range");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  Tmp di, dw, doff, dperm, dpos, dact, dmeta;
+  SPT_CUDA(ctx, di.alloc(sizeof(int32_t) * S));
+  SPT_CUDA(ctx, dw.alloc(sizeof(float) * S));
+  SPT_CUDA(ctx, doff.alloc(sizeof(int32_t) * (experts + 1)));
+  SPT_CUDA(ctx, dperm.alloc(sizeof(int32_t) * S));
+  SPT_CUDA(ctx, dpos.alloc(sizeof(int32_t) * S));
+  SPT_CUDA(ctx, dact.alloc(sizeof(int32_t) * experts));
+  SPT_CUDA(ctx, dmeta.alloc(sizeof(int32_t) * 4));
+  SPT_CUDA(ctx, cudaMemcpyAsync(di.p, index, sizeof(int32_t) * S, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dw.p, weight, sizeof(float) * S, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, launch_dispatch(di.as<int32_t>(), dw.as<float>(), (int)S, (int)experts, doff.as<int32_t>(),
+                                dperm.as<int32_t>(), dpos.as<int32_t>(), dact.as<int32_t>(),
+                                dmeta.as<int32_t>(), ctx->stream));
+  int32_t meta[2];
+  SPT_CUDA(ctx, cudaMemcpyAsync(meta, dmeta.p, sizeof meta, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(expert_offsets, doff.p, sizeof(int32_t) * (experts + 1), cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (meta[1] > 0) SPT_CUDA(ctx, cudaMemcpy(perm, dperm.p, sizeof(int32_t) * meta[1], cudaMemcpyDeviceToHost));
+  if (dispatched) *dispatched = meta[1];
+  return SPT_OK;
+}
+
+spt_status spt_mul_moe_batch_expert(spt_context *ctx, const uint8_t *data, uint64_t data_len,
+                                    int64_t input, int64_t output, const float *x, int64_t x_len,
+                                    const int64_t *x_offsets, int64_t count, const float *bias,
+                                    float *y, int64_t y_len, const int64_t *y_offsets,
+                                    const volatile int32_t *cancel) {
+  if (!data || !x || !y || !x_offsets || !y_offsets) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  int64_t nbytes = 0;
+  if (input <= 0 || input % 32 != 0 || output <= 0 || count <= 0 ||
+      !product({input / 32, 17, output}, &nbytes) || data_len != (uint64_t)nbytes)
+    return fail(ctx, SPT_ERR_EXPERT, "expected MXFP4 expert matrix [%lld %lld]", (long long)input, (long long)output);
+  for (int64_t j = 0; j < count; ++j) {
+    if (x_offsets[j] < 0 || x_offsets[j] > x_len - input || y_offsets[j] < 0 ||
+        y_offsets[j] > y_len - output)
+      return fail(ctx, SPT_ERR_DIMENSIONS, "offset %lld out of range", (long long)j);
+  }
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  if (output > (1 << 30) || input > (1 << 30)) return fail(ctx, SPT_ERR_UNSUPPORTED, "matrix too large");
+  const int rows = (int)output, blocks = (int)(input / 32);
+  // one-expert G8 arena for this matrix
+  spt_arena tmp_arena;
+  tmp_arena.device = ctx->device;
+  MatrixG8 m;
+  if ((st = upload_mxfp4(ctx, &tmp_arena, data, 1, rows, blocks, &m))) {
+    for (void *p : tmp_arena.allocs) cudaFree(p);
+    return st;
+  }
+  std::vector<float> xg((size_t)(count * input));
+  for (int64_t j = 0; j < count; ++j)
+    memcpy(&xg[(size_t)(j * input)], x + x_offsets[j], sizeof(float) * (size_t)input);
+  Tmp dx, dy, db, doff, dact, dmeta;
+  cudaError_t e = dx.alloc(sizeof(float) * xg.size());
+  if (e == cudaSuccess) e = dy.alloc(sizeof(float) * (size_t)(count * output));
+  if (e == cudaSuccess) e = doff.alloc(sizeof(int32_t) * 2);
+  if (e == cudaSuccess) e = dact.alloc(sizeof(int32_t));
+  if (e == cudaSuccess) e = dmeta.alloc(sizeof(int32_t) * 4);
+  if (e == cudaSuccess && bias) e = db.alloc(sizeof(float) * (size_t)output);
+  const int32_t off_h[2] = {0, (int32_t)count}, act_h[1] = {0}, meta_h[4] = {1, (int32_t)count, 0, 0};
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dx.p, xg.data(), sizeof(float) * xg.size(), cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(doff.p, off_h, sizeof off_h, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dact.p, act_h, sizeof act_h, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dmeta.p, meta_h, sizeof meta_h, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess && bias) e = cudaMemcpyAsync(db.p, bias, sizeof(float) * (size_t)output, cudaMemcpyHostToDevice, ctx->stream);
+  std::vector<float> yg((size_t)(count * output));
+  if (e == cudaSuccess) {
+    GemvLaunch g;
+    g.m0 = m;
+    g.bias0 = db.as<float>();
+    g.x = dx.as<float>();
+    g.x_stride = input;
+    g.y = dy.as<float>();
+    g.y_stride = output;
+    g.offsets = doff.as<int32_t>();
+    g.act_list = dact.as<int32_t>();
+    g.meta = dmeta.as<int32_t>();
+    g.mode = kRowsMoEDown;
+    g.gate_up = false;
+    g.max_active = 1;
+    g.mt = count >= 8 ? 8 : (count >= 4 ? 4 : (count >= 2 ? 2 : 1));
+    e = launch_gemv(g, ctx->sm_count, ctx->stream);
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(yg.data(), dy.p, sizeof(float) * yg.size(), cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  for (void *p : tmp_arena.allocs) cudaFree(p);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "mul_moe_batch_expert");
+  for (int64_t j = 0; j < count; ++j)
+    memcpy(y + y_offsets[j], &yg[(size_t)(j * output)], sizeof(float) * (size_t)output);
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  return SPT_OK;
+}
+
+spt_status spt_swiglu(spt_context *ctx, const float *gate, const float *up, float *act, int64_t n) {
+  if (!gate || !up || !act) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (n <= 0) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid length");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  Tmp dg, du, da;
+  SPT_CUDA(ctx, dg.alloc(sizeof(float) * n));
+  SPT_CUDA(ctx, du.alloc(sizeof(float) * n));
+  SPT_CUDA(ctx, da.alloc(sizeof(float) * n));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dg.p, gate, sizeof(float) * n, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(du.p, up, sizeof(float) * n, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, launch_swiglu(dg.as<float>(), du.as<float>(), da.as<float>(), n, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(act, da.p, sizeof(float) * n, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return SPT_OK;
+}
+
+spt_status spt_combine_moe_batch(spt_context *ctx, const float *results, const float *weight,
+                                 int64_t batch, int64_t k, int64_t hidden, float *out) {
+  if (!results || !weight || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (batch <= 0 || k <= 0 || hidden <= 0 || hidden % 4 != 0)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid dimensions");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  Tmp dr, dw, dout;
+  SPT_CUDA(ctx, dr.alloc(sizeof(float) * batch * k * hidden));
+  SPT_CUDA(ctx, dw.alloc(sizeof(float) * batch * k));
+  SPT_CUDA(ctx, dout.alloc(sizeof(float) * batch * hidden));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dr.p, results, sizeof(float) * batch * k * hidden, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dw.p, weight, sizeof(float) * batch * k, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, launch_combine(dr.as<float>(), dw.as<float>(), nullptr, (int)batch, (int)k, (int)hidden,
+                               dout.as<float>(), ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(out, dout.p, sizeof(float) * batch * hidden, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return SPT_OK;
+}
+
+spt_status spt_rmsnorm(spt_context *ctx, const float *x, const float *weight, int64_t batch,
+                       int64_t dim, float eps, float *y) {
+  if (!x || !weight || !y) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (batch <= 0 || dim <= 0) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid dimensions");
+  if (eps < 0 || isnan(eps) || isinf(eps)) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid epsilon: %g", (double)eps);
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  Tmp dx, dw, dy;
+  SPT_CUDA(ctx, dx.alloc(sizeof(float) * batch * dim));
+  SPT_CUDA(ctx, dw.alloc(sizeof(float) * dim));
+  SPT_CUDA(ctx, dy.alloc(sizeof(float) * batch * dim));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dx.p, x, sizeof(float) * batch * dim, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(dw.p, weight, sizeof(float) * dim, cudaMemcpyHostToDevice, ctx->stream));
+  SPT_CUDA(ctx, launch_rmsnorm(dx.as<float>(), dw.as<float>(), (int)batch, (int)dim, eps, dy.as<float>(), 8, ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpyAsync(y, dy.p, sizeof(float) * batch * dim, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return SPT_OK;
+}
+
+spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len, int64_t input,
+                       int64_t output, const float *x, float *y, int64_t *argmax, float *best_logit) {
+  (void)data; (void)data_len; (void)input; (void)output; (void)x; (void)y; (void)argmax; (void)best_logit;
+  return fail(ctx, SPT_ERR_UNSUPPORTED, "Q8_0 LM-head kernel not built in this version");
+}
+
+}  // extern "C"

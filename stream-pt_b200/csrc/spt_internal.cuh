@@ -1,0 +1,132 @@
+// spt_internal.cuh -- device data layout and kernel launchers shared by the
+// C ABI (spt_api.cu) and the kernels (spt_kernels.cu).
+//
+// HBM layout of one expert matrix in the GEMV arena ("G8" layout)
+// --------------------------------------------------------------
+// A GGUF MXFP4 expert tensor is E experts x R rows x nb 17-byte blocks
+// (ggufindex/index.go:550, forward/mxfp4.go:56-59: byte 0 = E8M0 scale,
+// byte 1+i holds element i in its low nibble and element i+16 in its high
+// nibble).  17-byte blocks are not 16-byte aligned, so the arena repacks them
+// once into two planes:
+//
+//   nibbles: uint4 nib[E][G][NQ][32]  G = ceil(R/8) row groups, NQ = ceil(nb/4)
+//            lane l = 4*i + q of a warp owns row 8g+i and "chain quarter" q;
+//            the 16 bytes are four 32-bit words, word t = block 4*Q+t, and
+//            nibble j of a word is element 8q+j of that block.
+//   scales:  uint32 scl[E][G][NQ][8]  byte t of word i = E8M0 byte of block
+//            4*Q+t of row 8g+i.
+//
+// One warp-wide 16-byte load reads 512 contiguous bytes = 4 blocks of 8 rows.
+// Thread (i,q) then holds exactly the 8 FMA chains 8q..8q+7 of the
+// reference's AVX2 dot (forward/mxfp4_amd64.go:11-26): accumulator register
+// a_q of that kernel, lane by lane.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spt {
+
+constexpr int kDispatchMaxExperts = 256;  // shared-memory tables of the dispatch kernel
+constexpr int kSelectMaxK = 32;
+
+struct MatrixG8 {
+  const uint4 *nib = nullptr;     // [E][G][NQ][32]
+  const uint32_t *scl = nullptr;  // [E][G][NQ][8]
+  int rows = 0;                   // R
+  int blocks = 0;                 // nb = K/32
+  int groups = 0;                 // G
+  int quads = 0;                  // NQ
+};
+
+inline size_t g8_nib_count(int64_t experts, int rows, int blocks) {
+  return (size_t)experts * (size_t)((rows + 7) / 8) * (size_t)((blocks + 3) / 4) * 32;
+}
+inline size_t g8_scl_count(int64_t experts, int rows, int blocks) {
+  return (size_t)experts * (size_t)((rows + 7) / 8) * (size_t)((blocks + 3) / 4) * 8;
+}
+
+// Device pointers of one layer in the arena.
+struct LayerDev {
+  const float *router = nullptr;       // [E][H] fp32
+  const float *router_bias = nullptr;  // [E]
+  MatrixG8 gate, up, down;             // gate/up: R = D, K = H; down: R = H, K = D
+  const float *gate_bias = nullptr;    // [E][D]
+  const float *up_bias = nullptr;      // [E][D]
+  const float *down_bias = nullptr;    // [E][H]
+};
+
+// Per-call device scratch (owned by the context, grown on demand).
+struct ScratchDev {
+  float *logits = nullptr;      // [T][E]
+  int32_t *sel_idx = nullptr;   // [T*K]
+  float *sel_w = nullptr;       // [T*K]
+  int32_t *offsets = nullptr;   // [E+1] expert segment starts in dispatch order
+  int32_t *perm = nullptr;      // [T*K] dispatch position -> slot
+  int32_t *slot_pos = nullptr;  // [T*K] slot -> dispatch position, -1 if not dispatched
+  int32_t *act_list = nullptr;  // [E] active experts ascending
+  int32_t *meta = nullptr;      // [0] active experts, [1] dispatched slots
+  float *act = nullptr;         // [T*K][D] SwiGLU activations in dispatch order
+  float *res = nullptr;         // [T*K][H] down + bias in dispatch order
+};
+
+struct Dims {
+  int H, D, E, K;
+};
+
+// ---- launchers (spt_kernels.cu); all enqueue on `stream` ----------------
+
+cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
+                          float *logits, int portable_lanes, cudaStream_t stream);
+cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
+                          float *sel_w, cudaStream_t stream);
+cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
+                            int32_t *offsets, int32_t *perm, int32_t *slot_pos,
+                            int32_t *act_list, int32_t *meta, cudaStream_t stream);
+
+// Addressing of the token rows a GEMV launch reads and writes, per
+// dispatch position p of an expert segment:
+//   kRowsMoEGateUp: x row = perm[p] / K (token), y row = p
+//   kRowsMoEDown:   x row = p,                    y row = p
+//   kRowsOffsets:   x at xoff[p], y at yoff[p] (element offsets)
+enum RowMode : int { kRowsMoEGateUp = 0, kRowsMoEDown = 1, kRowsOffsets = 2 };
+
+struct GemvLaunch {
+  MatrixG8 m0, m1;             // m1 used only when gate_up
+  const float *bias0 = nullptr;  // [E][R] or null
+  const float *bias1 = nullptr;
+  const float *x = nullptr;
+  float *y = nullptr;
+  int64_t x_stride = 0;         // elements per x row (modes 0, 1)
+  int64_t y_stride = 0;         // elements per y row (modes 0, 1)
+  const int32_t *perm = nullptr;
+  const int64_t *xoff = nullptr;  // mode 2
+  const int64_t *yoff = nullptr;
+  const int32_t *offsets = nullptr;   // [E+1]
+  const int32_t *act_list = nullptr;  // [E]
+  const int32_t *meta = nullptr;      // meta[0] = active experts
+  int top_k = 1;
+  int mode = kRowsMoEGateUp;
+  bool gate_up = false;         // fused gate+up+SwiGLU (writes SwiGLU(act))
+  int max_active = 1;           // host upper bound of active experts (grid sizing)
+  int mt = 1;                   // tokens per pass (1, 2, 4, 8)
+};
+cudaError_t launch_gemv(const GemvLaunch &a, int sm_count, cudaStream_t stream);
+
+cudaError_t launch_combine(const float *res, const float *sel_w, const int32_t *slot_pos, int T,
+                           int K, int H, float *out, cudaStream_t stream);
+cudaError_t launch_swiglu(const float *g, const float *u, float *act, int64_t n,
+                          cudaStream_t stream);
+cudaError_t launch_rmsnorm(const float *x, const float *w, int T, int dim, float eps, float *y,
+                           int lanes, cudaStream_t stream);
+cudaError_t launch_add(float *dst, const float *src, int64_t n, cudaStream_t stream);
+
+// Repack `experts` x `rows` x `blocks` GGUF MXFP4 blocks (device bytes) into
+// the G8 planes (which must be zeroed beforehand).
+cudaError_t launch_repack_g8(const uint8_t *gguf, int64_t experts, int rows, int blocks,
+                             uint4 *nib, uint32_t *scl, cudaStream_t stream);
+// Generate synthetic MXFP4 blocks straight into the G8 planes.
+cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int rows, int blocks,
+                            uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
+                            cudaStream_t stream);
+
+}  // namespace spt

@@ -1,0 +1,676 @@
+// spt_kernels.cu -- sm_100a kernels of the MoE FFN block (CUDA cores).
+//
+// Every kernel reproduces the reference's arithmetic order so the GPU result
+// is bit-identical to the Go AVX2 path (paths relative to the Stream-PT
+// repository root):
+//   * router:   64 FMA chains + fixed tree, forward/vector_amd64.go:28-56
+//   * select:   k strict-> argmax passes + f64-exp softmax, forward/moe_batch.go:305-342
+//   * dispatch: per-expert push-front lists, forward/moe_batch.go:142-159
+//   * GEMV:     32 FMA chains over MXFP4 blocks + fixed tree,
+//               forward/mxfp4_amd64.go:11-26 and forward/quant_amd64.go:112-116
+//   * SwiGLU:   forward/moe.go:66-70
+//   * combine:  fma(result, weight, out) in rank order, forward/moe_batch.go:163-192
+// The file is compiled with -fmad=false: every fused multiply-add is an
+// explicit fmaf / fma.rn.f32x2, all other operations round separately.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "spt_internal.cuh"
+#include "spt_philox.h"
+
+namespace spt {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// Packed fp32 pair arithmetic (sm_100a f32x2): two independent IEEE
+// round-to-nearest operations per instruction.
+__device__ __forceinline__ void fma2(float &c0, float &c1, float a0, float a1, float b0,
+                                     float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ void mul2(float &a0, float &a1, float f) {
+  asm("{\n\t.reg .b64 ra, rb;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %2};\n\t"
+      "mul.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(f));
+}
+
+// quantSumAVX2 of an 8-lane vector (forward/quant_amd64.go:112-116).
+__device__ __forceinline__ float qsum8(const float s[8]) {
+  float p0 = s[0] + s[4], p1 = s[1] + s[5], p2 = s[2] + s[6], p3 = s[3] + s[7];
+  return (p0 + p1) + (p2 + p3);
+}
+
+// Go's builtin min/max on floats propagate NaN (forward/moe.go:67-68).
+__device__ __forceinline__ float go_min(float a, float b) {
+  return (isnan(a) || isnan(b)) ? __int_as_float(0x7fffffff) : (a < b ? a : b);
+}
+__device__ __forceinline__ float go_max(float a, float b) {
+  return (isnan(a) || isnan(b)) ? __int_as_float(0x7fffffff) : (a > b ? a : b);
+}
+
+// gptOSSSwiGLU (forward/moe.go:66-70): f32 clamp, f32 -1.702*g, f64 exp
+// rounded to f32, then g / (1+e) * (u+1) left to right.
+__device__ __forceinline__ float swiglu_ref(float g, float u) {
+  g = go_min(g, 7.0f);
+  u = go_max(-7.0f, go_min(u, 7.0f));
+  const float t = __fmul_rn(-1.702f, g);
+  const float e = (float)exp((double)t);
+  const float d = __fadd_rn(1.0f, e);
+  return __fmul_rn(__fdiv_rn(g, d), __fadd_rn(u, 1.0f));
+}
+
+// Decode 8 MXFP4 elements (nibble j of `w` = element 8q+j) with E8M0 byte s
+// into exactly fl(level * 2^(s-127)), the value of scaledFP4Table
+// (forward/mxfp4.go:24).  Bits (m<<22)|(sign<<31) form the float
+// +-level * 2^-126 (e2m1's exponent lands in the fp32 exponent, its mantissa
+// bit in the top mantissa bit, subnormals included), so one exact multiply
+// by 2^(s-1) gives the scaled level for s <= 128.  Larger s take a second
+// exact multiply (overflow rounds to Inf as in the reference) and s = 255
+// multiplies by +Inf (0 * Inf = NaN, as the reference table holds).
+__device__ __forceinline__ void decode8(uint32_t w, uint32_t s, float out[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t c = (((w >> (4 * j)) & 7u) << 22) | (((w >> (4 * j + 3)) & 1u) << 31);
+    out[j] = __uint_as_float(c);
+  }
+  float f = __uint_as_float((s + 126u) << 23);
+  if (s > 128u) f = (s == 255u) ? __uint_as_float(0x7f800000u) : 0x1p127f;
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) mul2(out[j], out[j + 1], f);
+  if (s > 128u && s < 255u) {
+    const float f2 = __uint_as_float((s - 1u) << 23);  // 2^(s-128)
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) mul2(out[j], out[j + 1], f2);
+  }
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int t) {
+  return t == 0 ? v.x : (t == 1 ? v.y : (t == 2 ? v.z : v.w));
+}
+
+// Cross-thread part of the AVX2 reduction: thread q of a row holds the 8
+// lanes of accumulator a_q; s[l] = ((a0[l]+a1[l])+a2[l])+a3[l], then
+// quantSum.  Valid in the q == 0 lane.
+__device__ __forceinline__ float reduce_row(const float acc[8], int lane) {
+  const int base = lane & ~3;
+  float s[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+    const float v1 = __shfl_sync(kFull, acc[l], base + 1);
+    const float v2 = __shfl_sync(kFull, acc[l], base + 2);
+    const float v3 = __shfl_sync(kFull, acc[l], base + 3);
+    s[l] = ((acc[l] + v1) + v2) + v3;
+  }
+  return qsum8(s);
+}
+
+// ---------------------------------------------------------------------------
+// Router: logits[t,e] = dotF32AVX2(W[e], x[t]) + bias[e].
+// One warp per (expert, MTR tokens).  Lane l runs chains l and l+32 of the
+// 64 chains (a_j[l'] with chain = 8j+l'); a 32-element tail (hidden%64 == 32)
+// feeds chains 0..31 (vector_amd64.go:45-52).
+template <int MTR>
+__global__ void __launch_bounds__(32) k_router(const float *__restrict__ W,
+                                               const float *__restrict__ x,
+                                               const float *__restrict__ bias, int T, int H,
+                                               int E, float *__restrict__ logits) {
+  const int e = blockIdx.x, t0 = blockIdx.y * MTR, lane = threadIdx.x;
+  const int nt = min(MTR, T - t0);
+  const float *w = W + (size_t)e * H;
+  float a[MTR], b[MTR];
+#pragma unroll
+  for (int j = 0; j < MTR; ++j) a[j] = b[j] = 0.0f;
+  int o = 0;
+  for (; o + 64 <= H; o += 64) {
+    const float w0 = __ldg(w + o + lane), w1 = __ldg(w + o + 32 + lane);
+#pragma unroll
+    for (int j = 0; j < MTR; ++j) {
+      if (j < nt) {
+        const float *xr = x + (size_t)(t0 + j) * H + o;
+        a[j] = fmaf(w0, __ldg(xr + lane), a[j]);
+        b[j] = fmaf(w1, __ldg(xr + 32 + lane), b[j]);
+      }
+    }
+  }
+  if (o < H) {
+    const float w0 = __ldg(w + o + lane);
+#pragma unroll
+    for (int j = 0; j < MTR; ++j)
+      if (j < nt) a[j] = fmaf(w0, __ldg(x + (size_t)(t0 + j) * H + o + lane), a[j]);
+  }
+  const float be = bias ? bias[e] : 0.0f;
+#pragma unroll
+  for (int j = 0; j < MTR; ++j) {
+    if (j < nt) {
+      const float a8 = __shfl_sync(kFull, a[j], (lane + 8) & 31);
+      const float a16 = __shfl_sync(kFull, a[j], (lane + 16) & 31);
+      const float a24 = __shfl_sync(kFull, a[j], (lane + 24) & 31);
+      const float b8 = __shfl_sync(kFull, b[j], (lane + 8) & 31);
+      const float b16 = __shfl_sync(kFull, b[j], (lane + 16) & 31);
+      const float b24 = __shfl_sync(kFull, b[j], (lane + 24) & 31);
+      const float s0 = ((a[j] + a8) + a16) + a24;
+      const float s1 = ((b[j] + b8) + b16) + b24;
+      const float s = s0 + s1;
+      const float p = s + __shfl_sync(kFull, s, (lane + 4) & 31);
+      const float qv = p + __shfl_sync(kFull, p, (lane + 1) & 31);
+      const float r = qv + __shfl_sync(kFull, qv, (lane + 2) & 31);
+      if (lane == 0) logits[(size_t)(t0 + j) * E + e] = r + be;
+    }
+  }
+}
+
+// Router for hidden % 32 != 0: the portable simd.Float32s order with `lanes`
+// lanes (forward/moe_batch.go:228-302): lane l accumulates elements l,
+// l+lanes, ... (zero-padded tail), then the lanes are summed in order.
+__global__ void k_router_portable(const float *__restrict__ W, const float *__restrict__ x,
+                                  const float *__restrict__ bias, int T, int H, int E,
+                                  int lanes, float *__restrict__ logits) {
+  const int e = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
+  float acc = 0.0f;
+  if (lane < lanes) {
+    for (int o = 0; o < H; o += lanes) {
+      const float wv = (o + lane < H) ? W[(size_t)e * H + o + lane] : 0.0f;
+      const float xv = (o + lane < H) ? x[(size_t)t * H + o + lane] : 0.0f;
+      acc = fmaf(wv, xv, acc);
+    }
+  }
+  float sum = 0.0f;
+  for (int l = 0; l < lanes; ++l) sum += __shfl_sync(kFull, acc, l);
+  if (lane == 0) logits[(size_t)t * E + e] = sum + (bias ? bias[e] : 0.0f);
+}
+
+// ---------------------------------------------------------------------------
+// selectMoEBatch: one warp per token.  Each pass takes the first strictly
+// greater logit among experts not yet chosen (lowest index wins ties, NaN
+// and -Inf never win); no candidate gives (index = pass, value 0).
+__global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits, int T, int E,
+                                                int K, int32_t *__restrict__ sel_idx,
+                                                float *__restrict__ sel_w) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const float *lg = logits + (size_t)t * E;
+  int chosen[kSelectMaxK];
+  float val[kSelectMaxK];
+  for (int r = 0; r < K; ++r) {
+    int best = -1;
+    float v = -INFINITY;
+    for (int e = lane; e < E; e += 32) {
+      bool already = false;
+      for (int p = 0; p < r; ++p) already |= (chosen[p] == e);
+      const float l = lg[e];
+      if (!already && l > v) {
+        v = l;
+        best = e;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, v, off);
+      const int ob = __shfl_xor_sync(kFull, best, off);
+      if (ob >= 0 && (best < 0 || ov > v || (ov == v && ob < best))) {
+        v = ov;
+        best = ob;
+      }
+    }
+    if (best < 0) {
+      best = r;
+      v = 0.0f;
+    }
+    chosen[r] = best;
+    val[r] = v;
+  }
+  if (lane == 0) {
+    float m = -INFINITY;
+    for (int r = 0; r < K; ++r)
+      if (val[r] > m) m = val[r];
+    float sum = 0.0f;
+    for (int r = 0; r < K; ++r) {
+      const float d = __fsub_rn(val[r], m);
+      val[r] = (float)exp((double)d);
+      sum = __fadd_rn(sum, val[r]);
+    }
+    if (sum > 0.0f) {
+      const float inv = __fdiv_rn(1.0f, sum);
+      for (int r = 0; r < K; ++r) val[r] = __fmul_rn(val[r], inv);
+    }
+    for (int r = 0; r < K; ++r) {
+      sel_idx[(size_t)t * K + r] = chosen[r];
+      sel_w[(size_t)t * K + r] = val[r];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch: the reference pushes slot t*k+r (weight > 0 or NaN) onto the
+// front of its expert's list (moe_batch.go:142-159), so walking a list visits
+// that expert's slots in descending slot order.  One CTA turns that into a
+// stable counting sort: histogram, exclusive scan over experts, then chunks
+// of 1024 slots taken in descending order, ranked within a warp by
+// __match_any_sync and across warps by a per-warp count table.
+__global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ sel_idx,
+                                                   const float *__restrict__ sel_w, int S, int E,
+                                                   int32_t *__restrict__ offsets,
+                                                   int32_t *__restrict__ perm,
+                                                   int32_t *__restrict__ slot_pos,
+                                                   int32_t *__restrict__ act_list,
+                                                   int32_t *__restrict__ meta) {
+  __shared__ int s_cnt[kDispatchMaxExperts];
+  __shared__ int s_off[kDispatchMaxExperts + 1];
+  __shared__ int s_run[kDispatchMaxExperts];
+  __shared__ int s_w[32 * kDispatchMaxExperts];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += blockDim.x) {
+    s_cnt[e] = 0;
+    s_run[e] = 0;
+  }
+  __syncthreads();
+  for (int s = tid; s < S; s += blockDim.x)
+    if (!(sel_w[s] <= 0.0f)) atomicAdd(&s_cnt[sel_idx[s]], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0, na = 0;
+    for (int e = 0; e < E; ++e) {
+      s_off[e] = acc;
+      acc += s_cnt[e];
+      if (s_cnt[e] > 0) act_list[na++] = e;
+    }
+    s_off[E] = acc;
+    meta[0] = na;
+    meta[1] = acc;
+  }
+  __syncthreads();
+  for (int e = tid; e <= E; e += blockDim.x) offsets[e] = s_off[e];
+  for (int base = 0; base < S; base += blockDim.x) {
+    const int s = S - 1 - (base + tid);
+    const bool valid = s >= 0;
+    int e = -1;
+    bool disp = false;
+    if (valid) {
+      disp = !(sel_w[s] <= 0.0f);
+      e = sel_idx[s];
+    }
+    const int key = disp ? e : -1;
+    const unsigned m = __match_any_sync(kFull, key);
+    const int rank = __popc(m & ((1u << lane) - 1u));
+    for (int k = tid; k < 32 * E; k += blockDim.x) s_w[k] = 0;
+    __syncthreads();
+    if (disp && rank == 0) s_w[warp * E + e] = __popc(m);
+    __syncthreads();
+    if (disp) {
+      int before = 0;
+      for (int w = 0; w < warp; ++w) before += s_w[w * E + e];
+      const int pos = s_off[e] + s_run[e] + before + rank;
+      perm[pos] = s;
+      slot_pos[s] = pos;
+    } else if (valid) {
+      slot_pos[s] = -1;
+    }
+    __syncthreads();
+    for (int k = tid; k < E; k += blockDim.x) {
+      int tot = 0;
+      for (int w = 0; w < 32; ++w) tot += s_w[w * E + k];
+      s_run[k] += tot;
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Grouped MXFP4 GEMV on CUDA cores, bit-exact with dotMXFP4Fast.
+// A warp owns (active expert, group of 8 rows); lane 4i+q runs FMA chains
+// 8q..8q+7 of row 8g+i for up to MT tokens of the expert at once, so each
+// decoded weight is reused across the tokens.  GU fuses gate and up and
+// writes SwiGLU(gate+bias, up+bias).
+template <int MT, bool GU>
+__global__ void __launch_bounds__(128) k_gemv(const GemvLaunch a) {
+  const int lane = threadIdx.x & 31, i = lane >> 2, q = lane & 3;
+  const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+  const int G = a.m0.groups, NQ = a.m0.quads, NB = a.m0.blocks, R = a.m0.rows;
+  const long long n_items = (long long)a.meta[0] * G;
+  for (long long item = gw; item < n_items; item += nw) {
+    const int ai = (int)(item / G), g = (int)(item - (long long)ai * G);
+    const int e = a.act_list[ai];
+    const int p0 = a.offsets[e], n = a.offsets[e + 1] - p0;
+    const int row = g * 8 + i;
+    const size_t base = ((size_t)e * G + g) * NQ;
+    const uint4 *nb0 = a.m0.nib + base * 32 + lane;
+    const uint32_t *sb0 = a.m0.scl + base * 8 + i;
+    const uint4 *nb1 = GU ? a.m1.nib + base * 32 + lane : nullptr;
+    const uint32_t *sb1 = GU ? a.m1.scl + base * 8 + i : nullptr;
+    for (int t0 = 0; t0 < n; t0 += MT) {
+      const int nt = min(MT, n - t0);
+      const float *xr[MT];
+#pragma unroll
+      for (int j = 0; j < MT; ++j) {
+        const int p = p0 + t0 + min(j, nt - 1);
+        const int src = (a.mode == kRowsMoEGateUp) ? a.perm[p] / a.top_k : p;
+        xr[j] = a.x + (size_t)src * a.x_stride + 8 * q;
+      }
+      float acc0[MT][8];
+      float acc1[GU ? MT : 1][8];
+#pragma unroll
+      for (int j = 0; j < MT; ++j)
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc0[j][l] = 0.0f;
+      if (GU) {
+#pragma unroll
+        for (int j = 0; j < (GU ? MT : 1); ++j)
+#pragma unroll
+          for (int l = 0; l < 8; ++l) acc1[j][l] = 0.0f;
+      }
+      uint4 w0 = __ldg(nb0);
+      uint32_t s0 = __ldg(sb0);
+      uint4 w1 = make_uint4(0, 0, 0, 0);
+      uint32_t s1 = 0;
+      if (GU) {
+        w1 = __ldg(nb1);
+        s1 = __ldg(sb1);
+      }
+      for (int Q = 0; Q < NQ; ++Q) {
+        // software pipeline: fetch the next quad before decoding this one
+        uint4 nw0 = w0, nw1 = w1;
+        uint32_t ns0 = s0, ns1 = s1;
+        if (Q + 1 < NQ) {
+          nw0 = __ldg(nb0 + (size_t)(Q + 1) * 32);
+          ns0 = __ldg(sb0 + (size_t)(Q + 1) * 8);
+          if (GU) {
+            nw1 = __ldg(nb1 + (size_t)(Q + 1) * 32);
+            ns1 = __ldg(sb1 + (size_t)(Q + 1) * 8);
+          }
+        }
+        const int nbq = min(4, NB - 4 * Q);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          if (t < nbq) {
+            float d0[8], d1[8];
+            decode8(word_of(w0, t), (s0 >> (8 * t)) & 0xffu, d0);
+            if (GU) decode8(word_of(w1, t), (s1 >> (8 * t)) & 0xffu, d1);
+            const int b = 4 * Q + t;
+#pragma unroll
+            for (int j = 0; j < MT; ++j) {
+              if (j < nt) {
+                const float4 xa = __ldg(reinterpret_cast<const float4 *>(xr[j] + 32 * b));
+                const float4 xb = __ldg(reinterpret_cast<const float4 *>(xr[j] + 32 * b + 4));
+                fma2(acc0[j][0], acc0[j][1], d0[0], d0[1], xa.x, xa.y);
+                fma2(acc0[j][2], acc0[j][3], d0[2], d0[3], xa.z, xa.w);
+                fma2(acc0[j][4], acc0[j][5], d0[4], d0[5], xb.x, xb.y);
+                fma2(acc0[j][6], acc0[j][7], d0[6], d0[7], xb.z, xb.w);
+                if (GU) {
+                  fma2(acc1[j][0], acc1[j][1], d1[0], d1[1], xa.x, xa.y);
+                  fma2(acc1[j][2], acc1[j][3], d1[2], d1[3], xa.z, xa.w);
+                  fma2(acc1[j][4], acc1[j][5], d1[4], d1[5], xb.x, xb.y);
+                  fma2(acc1[j][6], acc1[j][7], d1[6], d1[7], xb.z, xb.w);
+                }
+              }
+            }
+          }
+        }
+        w0 = nw0;
+        s0 = ns0;
+        w1 = nw1;
+        s1 = ns1;
+      }
+#pragma unroll
+      for (int j = 0; j < MT; ++j) {
+        if (j < nt) {
+          const float r0 = reduce_row(acc0[j], lane);
+          float r1 = 0.0f;
+          if (GU) r1 = reduce_row(acc1[GU ? j : 0], lane);
+          if (q == 0 && row < R) {
+            const float v0 = r0 + (a.bias0 ? a.bias0[(size_t)e * R + row] : 0.0f);
+            float outv = v0;
+            if (GU) {
+              const float v1 = r1 + (a.bias1 ? a.bias1[(size_t)e * R + row] : 0.0f);
+              outv = swiglu_ref(v0, v1);
+            }
+            a.y[(size_t)(p0 + t0 + j) * a.y_stride + row] = outv;
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Combine: out[t,h] = 0, then for r = 0..K-1 with weight > 0 or NaN,
+// out = fma(res[slot], w, out) (forward/moe_batch.go:163-192).
+__global__ void k_combine(const float *__restrict__ res, const float *__restrict__ sel_w,
+                          const int32_t *__restrict__ slot_pos, int T, int K, int H,
+                          float *__restrict__ out) {
+  const int t = blockIdx.y;
+  const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (t >= T || h >= H) return;
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int r = 0; r < K; ++r) {
+    const int s = t * K + r;
+    const float w = sel_w[s];
+    if (w <= 0.0f) continue;
+    const int pos = slot_pos ? slot_pos[s] : s;
+    const float4 v = *reinterpret_cast<const float4 *>(res + (size_t)pos * H + h);
+    o.x = fmaf(v.x, w, o.x);
+    o.y = fmaf(v.y, w, o.y);
+    o.z = fmaf(v.z, w, o.z);
+    o.w = fmaf(v.w, w, o.w);
+  }
+  *reinterpret_cast<float4 *>(out + (size_t)t * H + h) = o;
+}
+
+__global__ void k_swiglu(const float *__restrict__ g, const float *__restrict__ u,
+                         float *__restrict__ act, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    act[i] = swiglu_ref(g[i], u[i]);
+}
+
+// normBatch RMSNorm (forward/layer_batch.go:160-193) with `lanes`
+// accumulation lanes: squares[l] = fma(v, v, squares[l]) over offsets step
+// lanes (zero-padded), sequential lane sum, f = 1/float32(sqrt(float64(
+// sum/float32(dim)+eps))), y = (x*w)*f.
+__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, int T,
+                          int dim, float eps, int lanes, float *__restrict__ y) {
+  const int t = blockIdx.x, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float *in = x + (size_t)t * dim;
+  __shared__ float s_f;
+  if (threadIdx.x < 32) {
+    float acc = 0.0f;
+    if (lane < lanes)
+      for (int o = 0; o < dim; o += lanes) {
+        const float v = (o + lane < dim) ? in[o + lane] : 0.0f;
+        acc = fmaf(v, v, acc);
+      }
+    float sum = 0.0f;
+    for (int l = 0; l < lanes; ++l) sum = __fadd_rn(sum, __shfl_sync(kFull, acc, l));
+    if (lane == 0) {
+      const float qv = __fadd_rn(__fdiv_rn(sum, (float)dim), eps);
+      s_f = __fdiv_rn(1.0f, (float)sqrt((double)qv));
+    }
+  }
+  __syncthreads();
+  const float f = s_f;
+  for (int i2 = threadIdx.x; i2 < dim; i2 += blockDim.x)
+    y[(size_t)t * dim + i2] = __fmul_rn(__fmul_rn(in[i2], w[i2]), f);
+}
+
+__global__ void k_add(float *__restrict__ dst, const float *__restrict__ src, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = __fadd_rn(dst[i], src[i]);
+}
+
+// ---------------------------------------------------------------------------
+// GGUF 17-byte blocks -> G8 planes.  One thread per block.
+__device__ __forceinline__ void block_to_g8(const uint8_t blk[17], int64_t e, int r, int b,
+                                            int R, int NB, uint4 *nib, uint32_t *scl) {
+  uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int el = 8 * qq + j;
+      const uint32_t nbl = el < 16 ? (blk[1 + el] & 15u) : (uint32_t)(blk[1 + el - 16] >> 4);
+      words[qq] |= nbl << (4 * j);
+    }
+  const int G = (R + 7) / 8, NQ = (NB + 3) / 4;
+  const int g = r / 8, ii = r % 8, Q = b / 4, t = b % 4;
+  const size_t slot = (((size_t)e * G + g) * NQ + Q);
+  uint32_t *nw = reinterpret_cast<uint32_t *>(nib);
+#pragma unroll
+  for (int qq = 0; qq < 4; ++qq) nw[((slot * 32) + ii * 4 + qq) * 4 + t] = words[qq];
+  reinterpret_cast<uint8_t *>(scl)[((slot * 8) + ii) * 4 + t] = blk[0];
+}
+
+__global__ void k_repack_g8(const uint8_t *__restrict__ gguf, int64_t experts, int R, int NB,
+                            uint4 *nib, uint32_t *scl) {
+  const int64_t total = experts * R * NB;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx % NB);
+    const int64_t er = idx / NB;
+    const int r = (int)(er % R);
+    const int64_t e = er / R;
+    uint8_t blk[17];
+    const uint8_t *src = gguf + idx * 17;
+#pragma unroll
+    for (int k = 0; k < 17; ++k) blk[k] = src[k];
+    block_to_g8(blk, e, r, b, R, NB, nib, scl);
+  }
+}
+
+__global__ void k_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int R, int NB,
+                           uint8_t lo, uint8_t hi, uint4 *nib, uint32_t *scl) {
+  const int64_t total = experts * R * NB;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx % NB);
+    const int64_t er = idx / NB;
+    const int r = (int)(er % R);
+    const int64_t e = er / R;
+    uint8_t blk[17];
+    synth_mxfp4_block(seed, tag, (uint64_t)idx, lo, hi, blk);
+    block_to_g8(blk, e, r, b, R, NB, nib, scl);
+  }
+}
+
+inline unsigned grid_for(int64_t n, int threads, int64_t cap = 148 * 32) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (unsigned)g;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// launchers
+
+cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
+                          float *logits, int portable_lanes, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  if (H % 32 != 0) {
+    k_router_portable<<<dim3(E, T), 32, 0, stream>>>(W, x, bias, T, H, E, portable_lanes,
+                                                     logits);
+    return cudaGetLastError();
+  }
+  constexpr int MTR = 8;
+  k_router<MTR><<<dim3(E, (T + MTR - 1) / MTR), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
+                          float *sel_w, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  k_select<<<(T + 3) / 4, 128, 0, stream>>>(logits, T, E, K, sel_idx, sel_w);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
+                            int32_t *offsets, int32_t *perm, int32_t *slot_pos,
+                            int32_t *act_list, int32_t *meta, cudaStream_t stream) {
+  k_dispatch<<<1, 1024, 0, stream>>>(sel_idx, sel_w, S, E, offsets, perm, slot_pos, act_list,
+                                     meta);
+  return cudaGetLastError();
+}
+
+template <int MT, bool GU>
+static cudaError_t gemv_inst(const GemvLaunch &a, unsigned grid, cudaStream_t stream) {
+  k_gemv<MT, GU><<<grid, 128, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(const GemvLaunch &a, int sm_count, cudaStream_t stream) {
+  const int64_t items = (int64_t)a.max_active * a.m0.groups;
+  int64_t ctas = (items + 3) / 4;
+  const int64_t cap = (int64_t)(sm_count > 0 ? sm_count : 148) * 8;
+  if (ctas > cap) ctas = cap;
+  if (ctas < 1) ctas = 1;
+  const unsigned grid = (unsigned)ctas;
+  switch (a.mt) {
+    case 1: return a.gate_up ? gemv_inst<1, true>(a, grid, stream) : gemv_inst<1, false>(a, grid, stream);
+    case 2: return a.gate_up ? gemv_inst<2, true>(a, grid, stream) : gemv_inst<2, false>(a, grid, stream);
+    case 4: return a.gate_up ? gemv_inst<4, true>(a, grid, stream) : gemv_inst<4, false>(a, grid, stream);
+    default: return a.gate_up ? gemv_inst<8, true>(a, grid, stream) : gemv_inst<8, false>(a, grid, stream);
+  }
+}
+
+cudaError_t launch_combine(const float *res, const float *sel_w, const int32_t *slot_pos, int T,
+                           int K, int H, float *out, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  const int threads = 128;
+  dim3 grid((H / 4 + threads - 1) / threads, T);
+  k_combine<<<grid, threads, 0, stream>>>(res, sel_w, slot_pos, T, K, H, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const float *g, const float *u, float *act, int64_t n,
+                          cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  k_swiglu<<<grid_for(n, 256), 256, 0, stream>>>(g, u, act, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const float *x, const float *w, int T, int dim, float eps, float *y,
+                           int lanes, cudaStream_t stream) {
+  if (T <= 0) return cudaSuccess;
+  k_rmsnorm<<<T, 256, 0, stream>>>(x, w, T, dim, eps, lanes, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(float *dst, const float *src, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  k_add<<<grid_for(n, 256), 256, 0, stream>>>(dst, src, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack_g8(const uint8_t *gguf, int64_t experts, int rows, int blocks,
+                             uint4 *nib, uint32_t *scl, cudaStream_t stream) {
+  const int64_t n = experts * rows * blocks;
+  if (n <= 0) return cudaSuccess;
+  k_repack_g8<<<grid_for(n, 256), 256, 0, stream>>>(gguf, experts, rows, blocks, nib, scl);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int rows, int blocks,
+                            uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
+                            cudaStream_t stream) {
+  const int64_t n = experts * rows * blocks;
+  if (n <= 0) return cudaSuccess;
+  k_synth_g8<<<grid_for(n, 256), 256, 0, stream>>>(seed, tag, experts, rows, blocks, scale_lo,
+                                                   scale_hi, nib, scl);
+  return cudaGetLastError();
+}
+
+}  // namespace spt
