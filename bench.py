@@ -185,7 +185,9 @@ def run_ours(args):
     params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
                              router_bias=c["router_bias"])
     ctx = spt.Context(local)
-    arena = ctx.synthetic_arena(cfg, params)
+    flags = spt.ARENA_MMA if args.path == "mma" else spt.ARENA_GEMV
+    arena = ctx.synthetic_arena(cfg, params, flags=flags)
+    ctx.set_path(spt.PATH_MMA if args.path == "mma" else spt.PATH_EXACT)
     stream = torch.cuda.ExternalStream(ctx.stream)
     x_host = spt.synth_normal_host(c["seed"] + 7919 * rank, 1000, T * H)
     x_dev = torch.from_numpy(x_host).to(f"cuda:{local}")
@@ -280,15 +282,18 @@ def run_ours(args):
         "metric": "moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32 (mxfp4 weights)", "data": "synthetic",
+        "dtype": ("mxfp4 x 3-term mxfp8 -> f32 (tcgen05)" if args.path == "mma" else "f32 (mxfp4 weights)"),
+        "data": "synthetic",
         "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H,
+                   "expert_path": args.path,
                    "expert_dim": D, "experts": E, "top_k": K, "seed": c["seed"],
                    "parallelism": f"token-sharded replicas x{world}" if world > 1 else "single GPU",
                    "l2": "256 MB buffer written between timed steps",
                    "active_experts": n_active},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": load_traffic(args.config),
-                     "kernel": "k_gemv<gate_up> (fused gate+up MXFP4 GEMV + SwiGLU)",
+                     "kernel": ("k_mma_gemm gate/up (tcgen05 mxf8f6f4, fused SwiGLU)" if args.path == "mma"
+                                else "k_gemv<gate_up> (fused gate+up MXFP4 GEMV + SwiGLU)"),
                      "algorithmic_bytes": gu_bytes, "avg_ms": gu_ms, "peak_source": peak_src,
                      "down_kernel": {"achieved": dn_bytes / (dn_ms / 1e3) / 1e9, "avg_ms": dn_ms,
                                      "algorithmic_bytes": dn_bytes},
@@ -321,6 +326,8 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", default="mma", choices=["mma", "exact"],
+                    help="expert GEMMs on tcgen05 (mma) or the bit-exact CUDA-core GEMV (exact)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

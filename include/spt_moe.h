@@ -162,6 +162,19 @@ spt_status spt_synth_layer_host(const spt_moe_config *cfg, const spt_synth_param
 spt_status spt_synth_normal_host(uint64_t seed, uint64_t stream, float mean, float std,
                                  float *out, int64_t n);
 
+/* ---- expert-GEMM path ---------------------------------------------------- */
+
+/* SPT_PATH_EXACT: CUDA-core MXFP4 GEMV reproducing the reference's AVX2
+ * arithmetic bit for bit (needs an SPT_ARENA_GEMV arena).
+ * SPT_PATH_MMA: tcgen05 block-scaled GEMM, FP4 weights x 3-term MXFP8
+ * activations, fp32 accumulation; routing stays bit-exact, block outputs
+ * agree with the reference to ~1e-5 relative (needs SPT_ARENA_MMA).
+ * SPT_PATH_AUTO (default): MMA when the arena has it, else EXACT. */
+#define SPT_PATH_AUTO 0
+#define SPT_PATH_EXACT 1
+#define SPT_PATH_MMA 2
+spt_status spt_context_set_path(spt_context *ctx, int path);
+
 /* ---- the block ----------------------------------------------------------- */
 
 /* forwardMoEBatch: x and out are host arrays of x_len / out_len floats,
@@ -201,7 +214,7 @@ spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index,
 #define SPT_NUM_STAGES 6
 spt_status spt_set_stage_timing(spt_context *ctx, int enable);
 int spt_stage_times(spt_context *ctx, float *ms, int n);
-/* Number of kernels one forward call launches. */
+/* Number of kernels the last forward call launched. */
 int spt_kernels_per_forward(spt_context *ctx);
 
 /* ---- stage entry points (host pointers, synchronous) -------------------- */

@@ -28,6 +28,7 @@ ERR_FILE_RANGE, ERR_SCRATCH, ERR_CANCELED, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT = ran
 ERR_UNSUPPORTED, ERR_NO_DEVICE = 13, 14
 
 ARENA_GEMV, ARENA_MMA = 1, 2
+PATH_AUTO, PATH_EXACT, PATH_MMA = 0, 1, 2
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
 
@@ -209,6 +210,7 @@ def lib():
         "spt_set_stage_timing": ([vp, ctypes.c_int], st),
         "spt_stage_times": ([vp, vp, ctypes.c_int], ctypes.c_int),
         "spt_kernels_per_forward": ([vp], ctypes.c_int),
+        "spt_context_set_path": ([vp, ctypes.c_int], st),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -286,6 +288,10 @@ class Context:
 
     def kernels_per_forward(self) -> int:
         return int(lib().spt_kernels_per_forward(self._h))
+
+    def set_path(self, path: int):
+        """PATH_EXACT (CUDA-core, bit-exact), PATH_MMA (tcgen05) or PATH_AUTO."""
+        self.check(lib().spt_context_set_path(self._h, path))
 
     # ---- validation -----------------------------------------------------
     def validate(self, reader: Reader, cfg: Config, lw: LayerWeights):

@@ -65,6 +65,10 @@ struct spt_context {
   // optional per-stage timing (events on the launching stream)
   bool timing = false;
   cudaEvent_t ev[SPT_NUM_STAGES + 1] = {};
+  // tensor-core path
+  int path = SPT_PATH_AUTO;
+  int kernels_last = 0;
+  DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
 };
 
 struct spt_arena {
@@ -330,23 +334,46 @@ spt_status alloc_g8(spt_context *ctx, spt_arena *a, int64_t experts, int rows, i
   return SPT_OK;
 }
 
-spt_status upload_mxfp4(spt_context *ctx, spt_arena *a, const uint8_t *src, int64_t experts,
-                        int rows, int blocks, MatrixG8 *m) {
+spt_status stage_raw(spt_context *ctx, DevBuf *staging, const uint8_t *src, size_t raw) {
+  SPT_CUDA(ctx, staging->ensure(raw));
+  return upload(ctx, staging->p, src, raw);
+}
+
+spt_status repack_g8_from(spt_context *ctx, spt_arena *a, const uint8_t *dev_raw, int64_t experts,
+                          int rows, int blocks, MatrixG8 *m) {
   uint4 *nib = nullptr;
   uint32_t *scl = nullptr;
   spt_status st = alloc_g8(ctx, a, experts, rows, blocks, m, &nib, &scl);
   if (st) return st;
-  const size_t raw = (size_t)experts * rows * blocks * 17;
-  DevBuf staging;
-  SPT_CUDA(ctx, staging.ensure(raw));
-  if ((st = upload(ctx, staging.p, src, raw))) {
-    staging.release();
-    return st;
-  }
-  cudaError_t e = launch_repack_g8(staging.as<uint8_t>(), experts, rows, blocks, nib, scl, ctx->stream);
+  cudaError_t e = launch_repack_g8(dev_raw, experts, rows, blocks, nib, scl, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-  staging.release();
   if (e != cudaSuccess) return cuda_fail(ctx, e, "repack");
+  return SPT_OK;
+}
+
+spt_status upload_mxfp4(spt_context *ctx, spt_arena *a, const uint8_t *src, int64_t experts,
+                        int rows, int blocks, MatrixG8 *m) {
+  DevBuf staging;
+  spt_status st = stage_raw(ctx, &staging, src, (size_t)experts * rows * blocks * 17);
+  if (st == SPT_OK) st = repack_g8_from(ctx, a, staging.as<uint8_t>(), experts, rows, blocks, m);
+  staging.release();
+  return st;
+}
+
+// Allocate (zeroed) MMA planes for `experts` x `rows` x K and encode the TMA map.
+spt_status alloc_mma(spt_context *ctx, spt_arena *a, int64_t experts, int rows, int k, MmaMatrix *m) {
+  m->experts = experts;
+  m->rows = rows;
+  m->k = k;
+  m->kp = (k + kMmaKT - 1) / kMmaKT * kMmaKT;
+  m->mtiles = (rows + kMmaM - 1) / kMmaM;
+  const size_t wb = mma_w_bytes(experts, rows, k), sb = mma_sf_bytes(experts, rows, k);
+  spt_status st = arena_alloc(ctx, a, wb, &m->w);
+  if (st) return st;
+  if ((st = arena_alloc(ctx, a, sb, &m->sf))) return st;
+  SPT_CUDA(ctx, cudaMemsetAsync(m->w, 0, wb, ctx->stream));
+  SPT_CUDA(ctx, cudaMemsetAsync(m->sf, 0, sb, ctx->stream));
+  if (!mma_encode_weights(m)) return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed");
   return SPT_OK;
 }
 
@@ -392,6 +419,104 @@ int pick_mt(int64_t T, int64_t K, int64_t E) {
   return 8;
 }
 
+int pick_bn(int64_t T, int64_t K, int64_t E) { return (T * K) <= 8 * E ? 16 : 128; }
+
+// Expert GEMMs on the tensor cores (after router/select/dispatch):
+// plan -> quantize x -> gate/up GEMM (+SwiGLU) -> quantize act -> down GEMM.
+spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
+                       int64_t T, cudaStream_t s) {
+  const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
+            K = (int)c.num_experts_used;
+  const int64_t S = T * K;
+  const int bn = pick_bn(T, K, E);
+  const int64_t na_max = std::min<int64_t>(E, S);
+  const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
+  const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
+  if (!ctx->dev_err.p) {
+    SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
+    SPT_CUDA(ctx, cudaMemset(ctx->dev_err.p, 0, sizeof(int32_t)));
+  }
+  SPT_CUDA(ctx, ctx->pad_off.ensure(sizeof(int32_t) * E));
+  SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
+  SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
+  SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
+  SPT_CUDA(ctx, ctx->qx.ensure((size_t)kActTerms * rb * kph));
+  SPT_CUDA(ctx, ctx->sfx.ensure((size_t)kActTerms * (rb / kMmaM) * (kph / kMmaKT) * 512));
+  SPT_CUDA(ctx, ctx->qa.ensure((size_t)kActTerms * rb * kpd));
+  SPT_CUDA(ctx, ctx->sfa.ensure((size_t)kActTerms * (rb / kMmaM) * (kpd / kMmaKT) * 512));
+  const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
+  SPT_CUDA(ctx, launch_mma_plan(ctx->offsets.as<int32_t>(), ctx->act_list.as<int32_t>(), ctx->meta.as<int32_t>(),
+                                E, bn, mt_gu, mt_dn, ctx->pad_off.as<int32_t>(), ctx->tile_gu.as<int32_t>(),
+                                ctx->tile_dn.as<int32_t>(), ctx->pos_expert.as<int32_t>(), s));
+  SPT_CUDA(ctx, launch_quantize_act(x, H, ctx->perm.as<int32_t>(), K, true, ctx->offsets.as<int32_t>(),
+                                    ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
+                                    ctx->meta.as<int32_t>(), (int)S, H, kph, rb, bn, ctx->qx.as<uint8_t>(),
+                                    ctx->sfx.as<uint8_t>(), s));
+  MmaLaunch g;
+  g.tmap_a = L.gu_mma.tmap;
+  if (!mma_encode_acts(&g.tmap_b, ctx->qx.as<uint8_t>(), kph, rb, bn))
+    return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
+  g.sfa = L.gu_mma.sf;
+  g.sfb = ctx->sfx.as<uint8_t>();
+  g.rows = L.gu_mma.rows;
+  g.kp = kph;
+  g.mtiles = mt_gu;
+  g.ktiles = kph / kMmaKT;
+  g.rb = rb;
+  g.offsets = ctx->offsets.as<int32_t>();
+  g.pad_off = ctx->pad_off.as<int32_t>();
+  g.act_list = ctx->act_list.as<int32_t>();
+  g.tile_off = ctx->tile_gu.as<int32_t>();
+  g.meta = ctx->meta.as<int32_t>();
+  g.max_tiles = (int)std::min<int64_t>((int64_t)mt_gu * (na_max + S / bn + 1), 1 << 30);
+  g.mode = 0;
+  g.bias0 = L.gate_bias;
+  g.bias1 = L.up_bias;
+  g.y = ctx->act.as<float>();
+  g.y_stride = D;
+  g.out_rows = D;
+  g.err = ctx->dev_err.as<int32_t>();
+  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[3], s));
+  SPT_CUDA(ctx, launch_mma_gemm(g, bn, ctx->sm_count, s));
+  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[4], s));
+  SPT_CUDA(ctx, launch_quantize_act(ctx->act.as<float>(), D, nullptr, K, false, ctx->offsets.as<int32_t>(),
+                                    ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
+                                    ctx->meta.as<int32_t>(), (int)S, D, kpd, rb, bn, ctx->qa.as<uint8_t>(),
+                                    ctx->sfa.as<uint8_t>(), s));
+  MmaLaunch dn = g;
+  dn.tmap_a = L.dn_mma.tmap;
+  if (!mma_encode_acts(&dn.tmap_b, ctx->qa.as<uint8_t>(), kpd, rb, bn))
+    return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
+  dn.sfa = L.dn_mma.sf;
+  dn.sfb = ctx->sfa.as<uint8_t>();
+  dn.rows = L.dn_mma.rows;
+  dn.kp = kpd;
+  dn.mtiles = mt_dn;
+  dn.ktiles = kpd / kMmaKT;
+  dn.tile_off = ctx->tile_dn.as<int32_t>();
+  dn.max_tiles = (int)std::min<int64_t>((int64_t)mt_dn * (na_max + S / bn + 1), 1 << 30);
+  dn.mode = 1;
+  dn.bias0 = L.down_bias;
+  dn.bias1 = nullptr;
+  dn.y = ctx->res.as<float>();
+  dn.y_stride = H;
+  dn.out_rows = H;
+  SPT_CUDA(ctx, launch_mma_gemm(dn, bn, ctx->sm_count, s));
+  ctx->kernels_last = 9;
+  return SPT_OK;
+}
+
+spt_status check_device_error(spt_context *ctx) {
+  if (!ctx->dev_err.p) return SPT_OK;
+  int32_t e = 0;
+  SPT_CUDA(ctx, cudaMemcpy(&e, ctx->dev_err.p, sizeof e, cudaMemcpyDeviceToHost));
+  if (e != 0) {
+    cudaMemset(ctx->dev_err.p, 0, sizeof e);
+    return fail(ctx, SPT_ERR_TIMEOUT, "tensor-core GEMM: bounded wait %d gave up", e);
+  }
+  return SPT_OK;
+}
+
 // The whole block on device pointers (enqueue only).
 spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
                           float *out, int64_t T) {
@@ -418,40 +543,52 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
                                 ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
                                 ctx->meta.as<int32_t>(), s));
   const int max_active = (int)std::min<int64_t>(E, T * K);
-  const int mt = pick_mt(T, K, E);
-  GemvLaunch gu;
-  gu.m0 = L.gate;
-  gu.m1 = L.up;
-  gu.bias0 = L.gate_bias;
-  gu.bias1 = L.up_bias;
-  gu.x = x;
-  gu.x_stride = H;
-  gu.y = ctx->act.as<float>();
-  gu.y_stride = D;
-  gu.perm = ctx->perm.as<int32_t>();
-  gu.offsets = ctx->offsets.as<int32_t>();
-  gu.act_list = ctx->act_list.as<int32_t>();
-  gu.meta = ctx->meta.as<int32_t>();
-  gu.top_k = K;
-  gu.mode = kRowsMoEGateUp;
-  gu.gate_up = true;
-  gu.max_active = max_active;
-  gu.mt = mt;
-  SPT_MARK(3);
-  SPT_CUDA(ctx, launch_gemv(gu, ctx->sm_count, s));
-  SPT_MARK(4);
-  GemvLaunch dn = gu;
-  dn.m0 = L.down;
-  dn.m1 = MatrixG8{};
-  dn.bias0 = L.down_bias;
-  dn.bias1 = nullptr;
-  dn.x = ctx->act.as<float>();
-  dn.x_stride = D;
-  dn.y = ctx->res.as<float>();
-  dn.y_stride = H;
-  dn.mode = kRowsMoEDown;
-  dn.gate_up = false;
-  SPT_CUDA(ctx, launch_gemv(dn, ctx->sm_count, s));
+  const bool use_mma = L.has_mma && (ctx->path == SPT_PATH_MMA || (ctx->path == SPT_PATH_AUTO)) &&
+                       !(ctx->path == SPT_PATH_EXACT);
+  if (ctx->path == SPT_PATH_MMA && !L.has_mma)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_MMA");
+  if (!use_mma && !L.has_g8)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_GEMV");
+  if (use_mma) {
+    if ((st = forward_mma(ctx, L, c, x, T, s))) return st;
+  } else {
+    const int mt = pick_mt(T, K, E);
+    GemvLaunch gu;
+    gu.m0 = L.gate;
+    gu.m1 = L.up;
+    gu.bias0 = L.gate_bias;
+    gu.bias1 = L.up_bias;
+    gu.x = x;
+    gu.x_stride = H;
+    gu.y = ctx->act.as<float>();
+    gu.y_stride = D;
+    gu.perm = ctx->perm.as<int32_t>();
+    gu.offsets = ctx->offsets.as<int32_t>();
+    gu.act_list = ctx->act_list.as<int32_t>();
+    gu.meta = ctx->meta.as<int32_t>();
+    gu.top_k = K;
+    gu.mode = kRowsMoEGateUp;
+    gu.gate_up = true;
+    gu.max_active = max_active;
+    gu.mt = mt > 4 ? 4 : mt;
+    SPT_MARK(3);
+    SPT_CUDA(ctx, launch_gemv(gu, ctx->sm_count, s));
+    SPT_MARK(4);
+    GemvLaunch dn = gu;
+    dn.m0 = L.down;
+    dn.m1 = MatrixG8{};
+    dn.bias0 = L.down_bias;
+    dn.bias1 = nullptr;
+    dn.x = ctx->act.as<float>();
+    dn.x_stride = D;
+    dn.y = ctx->res.as<float>();
+    dn.y_stride = H;
+    dn.mode = kRowsMoEDown;
+    dn.gate_up = false;
+    dn.mt = mt;
+    SPT_CUDA(ctx, launch_gemv(dn, ctx->sm_count, s));
+    ctx->kernels_last = 6;
+  }
   SPT_MARK(5);
   SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), ctx->sel_w.as<float>(),
                                ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
@@ -497,6 +634,7 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
     return st;
   SPT_CUDA(ctx, cudaMemcpyAsync(out, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
   SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if ((st = check_device_error(ctx))) return st;
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
   return SPT_OK;
 }
@@ -573,7 +711,8 @@ void spt_context_destroy(spt_context *ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     for (DevBuf *b : {&ctx->logits, &ctx->sel_idx, &ctx->sel_w, &ctx->offsets, &ctx->perm,
                       &ctx->slot_pos, &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res,
-                      &ctx->xdev, &ctx->outdev})
+                      &ctx->xdev, &ctx->outdev, &ctx->dev_err, &ctx->pad_off, &ctx->tile_gu,
+                      &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa})
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
@@ -601,10 +740,7 @@ int spt_stage_times(spt_context *ctx, float *ms, int n) {
   return w;
 }
 
-int spt_kernels_per_forward(spt_context *ctx) {
-  (void)ctx;
-  return 6;
-}
+int spt_kernels_per_forward(spt_context *ctx) { return ctx ? ctx->kernels_last : 0; }
 
 const char *spt_last_error(const spt_context *ctx) {
   return ctx ? ctx->err.c_str() : g_tls_error.c_str();
@@ -622,6 +758,13 @@ spt_status spt_context_sync(spt_context *ctx) {
   spt_status st = require_device(ctx);
   if (st) return st;
   SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return check_device_error(ctx);
+}
+
+spt_status spt_context_set_path(spt_context *ctx, int path) {
+  if (!ctx) return fail(nullptr, SPT_ERR_NULL_ARG, "nil context");
+  if (path < SPT_PATH_AUTO || path > SPT_PATH_MMA) return fail(ctx, SPT_ERR_UNSUPPORTED, "unknown path %d", path);
+  ctx->path = path;
   return SPT_OK;
 }
 
@@ -676,9 +819,44 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const s
       if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), b.dst))) break;
     }
     if (st) break;
-    if ((st = upload_mxfp4(ctx, a, r.base + w.ffn_gate_exps.start, E, (int)D, (int)(H / 32), &L.gate))) break;
-    if ((st = upload_mxfp4(ctx, a, r.base + w.ffn_up_exps.start, E, (int)D, (int)(H / 32), &L.up))) break;
-    if ((st = upload_mxfp4(ctx, a, r.base + w.ffn_down_exps.start, E, (int)H, (int)(D / 32), &L.down))) break;
+    {
+      DevBuf sg, su;
+      const size_t gu_raw = (size_t)E * D * (H / 32) * 17;
+      if ((st = stage_raw(ctx, &sg, r.base + w.ffn_gate_exps.start, gu_raw)) == SPT_OK &&
+          (st = stage_raw(ctx, &su, r.base + w.ffn_up_exps.start, gu_raw)) == SPT_OK) {
+        if (flags & SPT_ARENA_GEMV) {
+          if (st == SPT_OK) st = repack_g8_from(ctx, a, sg.as<uint8_t>(), E, (int)D, (int)(H / 32), &L.gate);
+          if (st == SPT_OK) st = repack_g8_from(ctx, a, su.as<uint8_t>(), E, (int)D, (int)(H / 32), &L.up);
+        }
+        if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
+          st = alloc_mma(ctx, a, E, (int)(2 * D), (int)H, &L.gu_mma);
+          if (st == SPT_OK) {
+            cudaError_t e = launch_repack_mma_gu(sg.as<uint8_t>(), su.as<uint8_t>(), E, (int)D, (int)H, &L.gu_mma, ctx->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+            if (e != cudaSuccess) st = cuda_fail(ctx, e, "repack mma gate/up");
+          }
+        }
+      }
+      sg.release();
+      su.release();
+      if (st) break;
+      DevBuf sd;
+      if ((st = stage_raw(ctx, &sd, r.base + w.ffn_down_exps.start, (size_t)E * H * (D / 32) * 17)) == SPT_OK) {
+        if (flags & SPT_ARENA_GEMV) st = repack_g8_from(ctx, a, sd.as<uint8_t>(), E, (int)H, (int)(D / 32), &L.down);
+        if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
+          st = alloc_mma(ctx, a, E, (int)H, (int)D, &L.dn_mma);
+          if (st == SPT_OK) {
+            cudaError_t e = launch_repack_mma(sd.as<uint8_t>(), E, (int)H, (int)D, &L.dn_mma, ctx->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+            if (e != cudaSuccess) st = cuda_fail(ctx, e, "repack mma down");
+          }
+        }
+      }
+      sd.release();
+      if (st) break;
+      L.has_g8 = (flags & SPT_ARENA_GEMV) != 0;
+      L.has_mma = (flags & SPT_ARENA_MMA) != 0;
+    }
   }
   if (st) {
     spt_arena_destroy(a);
@@ -735,6 +913,7 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
                 {kSynthUp, (int)D, (int)(H / 32), &L.up},
                 {kSynthDown, (int)H, (int)(D / 32), &L.down}};
     for (auto &m : mats) {
+      if (!(flags & SPT_ARENA_GEMV)) break;
       uint4 *nib = nullptr;
       uint32_t *scl = nullptr;
       if ((st = alloc_g8(ctx, a, E, m.rows, m.blocks, m.m, &nib, &scl))) break;
@@ -745,6 +924,25 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
         break;
       }
     }
+    if (st) break;
+    if (flags & SPT_ARENA_MMA) {
+      if ((st = alloc_mma(ctx, a, E, (int)(2 * D), (int)H, &L.gu_mma))) break;
+      cudaError_t e = launch_synth_mma_gu(p->seed, synth_tag(l, kSynthGate), synth_tag(l, kSynthUp), E, (int)D,
+                                          (int)H, p->scale_lo, p->scale_hi, &L.gu_mma, ctx->stream);
+      if (e != cudaSuccess) {
+        st = cuda_fail(ctx, e, "synth mma");
+        break;
+      }
+      if ((st = alloc_mma(ctx, a, E, (int)H, (int)D, &L.dn_mma))) break;
+      e = launch_synth_mma(p->seed, synth_tag(l, kSynthDown), E, (int)H, (int)D, p->scale_lo, p->scale_hi,
+                           &L.dn_mma, ctx->stream);
+      if (e != cudaSuccess) {
+        st = cuda_fail(ctx, e, "synth mma");
+        break;
+      }
+    }
+    L.has_g8 = (flags & SPT_ARENA_GEMV) != 0;
+    L.has_mma = (flags & SPT_ARENA_MMA) != 0;
   }
   if (st == SPT_OK) {
     cudaError_t e = cudaStreamSynchronize(ctx->stream);

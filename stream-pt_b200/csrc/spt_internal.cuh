@@ -24,6 +24,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "spt_mma.cuh"
+
 namespace spt {
 
 constexpr int kDispatchMaxExperts = 256;  // shared-memory tables of the dispatch kernel
@@ -53,6 +55,9 @@ struct LayerDev {
   const float *gate_bias = nullptr;    // [E][D]
   const float *up_bias = nullptr;      // [E][D]
   const float *down_bias = nullptr;    // [E][H]
+  bool has_g8 = false;                 // CUDA-core GEMV planes present
+  bool has_mma = false;                // tcgen05 planes present
+  MmaMatrix gu_mma, dn_mma;            // gate/up interleaved [E][2D][KP/2]; down [E][H][KPd/2]
 };
 
 // Per-call device scratch (owned by the context, grown on demand).

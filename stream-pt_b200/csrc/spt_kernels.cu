@@ -16,6 +16,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "spt_device.cuh"
 #include "spt_internal.cuh"
 #include "spt_philox.h"
 
@@ -49,25 +50,6 @@ __device__ __forceinline__ void mul2(float &a0, float &a1, float f) {
 __device__ __forceinline__ float qsum8(const float s[8]) {
   float p0 = s[0] + s[4], p1 = s[1] + s[5], p2 = s[2] + s[6], p3 = s[3] + s[7];
   return (p0 + p1) + (p2 + p3);
-}
-
-// Go's builtin min/max on floats propagate NaN (forward/moe.go:67-68).
-__device__ __forceinline__ float go_min(float a, float b) {
-  return (isnan(a) || isnan(b)) ? __int_as_float(0x7fffffff) : (a < b ? a : b);
-}
-__device__ __forceinline__ float go_max(float a, float b) {
-  return (isnan(a) || isnan(b)) ? __int_as_float(0x7fffffff) : (a > b ? a : b);
-}
-
-// gptOSSSwiGLU (forward/moe.go:66-70): f32 clamp, f32 -1.702*g, f64 exp
-// rounded to f32, then g / (1+e) * (u+1) left to right.
-__device__ __forceinline__ float swiglu_ref(float g, float u) {
-  g = go_min(g, 7.0f);
-  u = go_max(-7.0f, go_min(u, 7.0f));
-  const float t = __fmul_rn(-1.702f, g);
-  const float e = (float)exp((double)t);
-  const float d = __fadd_rn(1.0f, e);
-  return __fmul_rn(__fdiv_rn(g, d), __fadd_rn(u, 1.0f));
 }
 
 // Decode 8 MXFP4 elements (nibble j of `w` = element 8q+j) with E8M0 byte s

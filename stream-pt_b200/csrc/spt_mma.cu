@@ -1,0 +1,674 @@
+// spt_mma.cu -- tcgen05 block-scaled grouped GEMM for the MoE experts
+// (layouts and numerics: spt_mma.cuh).
+//
+// One persistent CTA per SM, 6 warps:
+//   warp 0  TMA producer: weight tile (e2m1, unpacked to 16-byte groups by the
+//           TMA) + three activation tiles (e4m3) + their E8M0 scale atoms,
+//           into an NS-stage shared-memory ring guarded by mbarriers;
+//   warp 1  TMEM owner and single-thread MMA issuer: per stage it copies the
+//           scale atoms to TMEM (tcgen05.cp) and issues 4 K-steps x 3
+//           activation terms of tcgen05.mma.kind::mxf8f6f4.block_scale into a
+//           double-buffered fp32 accumulator;
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator (lane = output row),
+//           bias, fused SwiGLU (gate/up rows are interleaved, so a row pair
+//           sits in neighbouring lanes) or the down projection, fp32 stores.
+// Every mbarrier wait is bounded; on timeout the CTA records an error code
+// in `err`, drains its tensor-core work and exits.
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include "spt_device.cuh"
+#include "spt_mma.cuh"
+#include "spt_philox.h"
+
+namespace spt {
+
+size_t mma_w_bytes(int64_t experts, int rows, int k) {
+  const int kp = (k + kMmaKT - 1) / kMmaKT * kMmaKT;
+  return (size_t)experts * rows * (kp / 2);
+}
+
+size_t mma_sf_bytes(int64_t experts, int rows, int k) {
+  const int kp = (k + kMmaKT - 1) / kMmaKT * kMmaKT;
+  return (size_t)experts * ((rows + kMmaM - 1) / kMmaM) * (kp / kMmaKT) * 512;
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+bool mma_encode_weights(MmaMatrix *m) {
+  auto fn = encode_fn();
+  if (!fn || !m->w) return false;
+  if (m->kp % 128 != 0 || (reinterpret_cast<uintptr_t>(m->w) & 31) != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)m->kp, (cuuint64_t)(m->experts * m->rows)};
+  cuuint64_t strides[1] = {(cuuint64_t)(m->kp / 2)};
+  cuuint32_t box[2] = {128, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m->tmap, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, m->w, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn) {
+  auto fn = encode_fn();
+  if (!fn || !q) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)(kActTerms * (int64_t)rb)};
+  cuuint64_t strides[1] = {(cuuint64_t)kp};
+  cuuint32_t box[2] = {128, (cuuint32_t)bn};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// MMA arena repack: GGUF 17-byte blocks -> packed e2m1 rows + scale atoms.
+
+// Write block b (32 elements, GGUF order: byte 1+i = element i | element
+// i+16 << 4) of MMA row `row` of expert e.
+__device__ __forceinline__ void put_mma_block(const uint8_t blk[17], int64_t e, int row, int b,
+                                              int rows, int kp, uint8_t *w, uint8_t *sf) {
+  uint8_t *dst = w + ((size_t)e * rows + row) * (kp / 2) + (size_t)b * 16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int e0 = 2 * i, e1 = 2 * i + 1;  // natural order: element 2i low nibble
+    const uint32_t n0 = e0 < 16 ? (blk[1 + e0] & 15u) : (uint32_t)(blk[1 + e0 - 16] >> 4);
+    const uint32_t n1 = e1 < 16 ? (blk[1 + e1] & 15u) : (uint32_t)(blk[1 + e1 - 16] >> 4);
+    dst[i] = (uint8_t)(n0 | (n1 << 4));
+  }
+  const int mtiles = (rows + kMmaM - 1) / kMmaM, ktiles = kp / kMmaKT;
+  const int mt = row / kMmaM, m = row % kMmaM, kt = b / 4, kb = b % 4;
+  sf[(((size_t)e * mtiles + mt) * ktiles + kt) * 512 + (m % 32) * 16 + (m / 32) * 4 + kb] = blk[0];
+}
+
+// gate/up: MMA row 2d = gate row d, 2d+1 = up row d.
+__global__ void k_repack_mma_gu(const uint8_t *__restrict__ gate, const uint8_t *__restrict__ up,
+                                int64_t E, int D, int NB, int kp, uint8_t *w, uint8_t *sf) {
+  const int64_t total = E * D * NB;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx % NB);
+    const int64_t ed = idx / NB;
+    const int d = (int)(ed % D);
+    const int64_t e = ed / D;
+    uint8_t blk[17];
+#pragma unroll
+    for (int k = 0; k < 17; ++k) blk[k] = gate[idx * 17 + k];
+    put_mma_block(blk, e, 2 * d, b, 2 * D, kp, w, sf);
+#pragma unroll
+    for (int k = 0; k < 17; ++k) blk[k] = up[idx * 17 + k];
+    put_mma_block(blk, e, 2 * d + 1, b, 2 * D, kp, w, sf);
+  }
+}
+
+__global__ void k_repack_mma(const uint8_t *__restrict__ src, int64_t E, int R, int NB, int kp,
+                             uint8_t *w, uint8_t *sf) {
+  const int64_t total = E * R * NB;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx % NB);
+    const int64_t er = idx / NB;
+    const int r = (int)(er % R);
+    const int64_t e = er / R;
+    uint8_t blk[17];
+#pragma unroll
+    for (int k = 0; k < 17; ++k) blk[k] = src[idx * 17 + k];
+    put_mma_block(blk, e, r, b, R, kp, w, sf);
+  }
+}
+
+__global__ void k_synth_mma_gu(uint64_t seed, uint32_t tg, uint32_t tu, int64_t E, int D, int NB,
+                               uint8_t lo, uint8_t hi, int kp, uint8_t *w, uint8_t *sf) {
+  const int64_t total = E * D * NB;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx % NB);
+    const int64_t ed = idx / NB;
+    const int d = (int)(ed % D);
+    const int64_t e = ed / D;
+    uint8_t blk[17];
+    synth_mxfp4_block(seed, tg, (uint64_t)idx, lo, hi, blk);
+    put_mma_block(blk, e, 2 * d, b, 2 * D, kp, w, sf);
+    synth_mxfp4_block(seed, tu, (uint64_t)idx, lo, hi, blk);
+    put_mma_block(blk, e, 2 * d + 1, b, 2 * D, kp, w, sf);
+  }
+}
+
+__global__ void k_synth_mma(uint64_t seed, uint32_t tag, int64_t E, int R, int NB, uint8_t lo,
+                            uint8_t hi, int kp, uint8_t *w, uint8_t *sf) {
+  const int64_t total = E * R * NB;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx % NB);
+    const int64_t er = idx / NB;
+    const int r = (int)(er % R);
+    const int64_t e = er / R;
+    uint8_t blk[17];
+    synth_mxfp4_block(seed, tag, (uint64_t)idx, lo, hi, blk);
+    put_mma_block(blk, e, r, b, R, kp, w, sf);
+  }
+}
+
+unsigned grid_of(int64_t n) {
+  int64_t g = (n + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  return (unsigned)(g < 1 ? 1 : g);
+}
+
+// ---------------------------------------------------------------------------
+// Tile plan after dispatch (one CTA).
+__global__ void k_mma_plan(const int32_t *__restrict__ offsets, const int32_t *__restrict__ act_list,
+                           const int32_t *__restrict__ meta, int E, int bn, int mt_gu, int mt_dn,
+                           int32_t *pad_off, int32_t *tile_gu, int32_t *tile_dn,
+                           int32_t *pos_expert) {
+  const int na = meta[0], total = meta[1];
+  if (threadIdx.x == 0) {
+    int pad = 0, tg = 0, td = 0;
+    for (int a = 0; a < na; ++a) {
+      const int e = act_list[a];
+      const int n = offsets[e + 1] - offsets[e];
+      const int nt = (n + bn - 1) / bn;
+      pad_off[e] = pad;  // every token tile owns a 128-row slot of the activation buffer
+      pad += nt * kMmaM;
+      tile_gu[a] = tg;
+      tile_dn[a] = td;
+      tg += mt_gu * nt;
+      td += mt_dn * nt;
+    }
+    tile_gu[na] = tg;
+    tile_dn[na] = td;
+  }
+  for (int p = threadIdx.x; p < total; p += blockDim.x) {
+    int lo = 0, hi = E - 1;  // largest e with offsets[e] <= p
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (offsets[mid] <= p) lo = mid;
+      else hi = mid - 1;
+    }
+    pos_expert[p] = lo;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Activations -> three MXFP8 terms.  One warp per dispatch position; lane l
+// handles element l of every 32-element block.  Term scale: the smallest
+// power of two 2^e with max|block| / 2^e <= 448 (e4m3's largest finite), so
+// no element saturates; each residual is exact in fp32.
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
+
+__global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
+                               const int32_t *__restrict__ perm, int top_k, int gather,
+                               const int32_t *__restrict__ offsets, const int32_t *__restrict__ pad_off,
+                               const int32_t *__restrict__ pos_expert, const int32_t *__restrict__ meta,
+                               int S_max, int K, int kp, int rb, int bn, uint8_t *__restrict__ q,
+                               uint8_t *__restrict__ sf) {
+  const int lane = threadIdx.x & 31;
+  const int pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (pos >= S_max || pos >= meta[1]) return;
+  const int e = pos_expert[pos];
+  const int j = pos - offsets[e];
+  const int row = pad_off[e] + (j / bn) * kMmaM + (j % bn);
+  const int64_t srow = gather ? (int64_t)(perm[pos] / top_k) : (int64_t)pos;
+  const float *x = src + srow * stride;
+  const int nblk = kp / 32, kt_n = kp / kMmaKT, g = row / kMmaM, m = row % kMmaM;
+  for (int b = 0; b < nblk; ++b) {
+    float v = (b * 32 < K) ? x[b * 32 + lane] : 0.0f;
+#pragma unroll
+    for (int t = 0; t < kActTerms; ++t) {
+      float amax = fabsf(v);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      int ex = -126;
+      if (amax > 0.0f) {
+        int e2;
+        const float mant = frexpf(amax * (1.0f / 448.0f), &e2);  // amax/448 = mant * 2^e2
+        ex = (mant == 0.5f) ? e2 - 1 : e2;
+        if (__fmul_rn(amax, exp2i(-ex)) > 448.0f) ex += 1;
+        ex = max(-126, min(ex, 120));
+      }
+      const float scaled = __fmul_rn(v, exp2i(-ex));
+      const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(scaled, __NV_SATFINITE, __NV_E4M3);
+      const __half_raw hr = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
+      const float back = __fmul_rn(__half2float(__half(hr)), exp2i(ex));
+      q[((int64_t)t * rb + row) * kp + b * 32 + lane] = (uint8_t)code;
+      if (lane == 0)
+        sf[(((int64_t)t * (rb / kMmaM) + g) * kt_n + b / 4) * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] =
+            (uint8_t)(ex + 127);
+      v = __fsub_rn(v, back);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// PTX helpers (sm_100a).
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ~2^31 clock cycles (about a second at the
+// B200's clock) and records `code` in err.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
+      if (*(volatile int32_t *)err != 0) return false;  // another role already gave up
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, void *dst, uint64_t *bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// K-major shared-memory matrix descriptor (tcgen05): start address, leading
+// byte offset (unused with swizzling), stride byte offset between 8-row
+// groups, descriptor version 1, layout type (2 = 128-byte swizzle, 0 = none).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t sbo_bytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;                                 // LBO (16 B)
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;       // SBO
+  d |= (uint64_t)1u << 46;                                 // version
+  d |= (uint64_t)(layout & 7u) << 61;                      // layout type
+  return d;
+}
+
+// Block-scaled instruction descriptor: A = E2M1, B = E4M3, scales E8M0,
+// K-major A and B, M = 128, N = n, scale-factor byte ids.
+__device__ __forceinline__ uint32_t idesc_mxf8f6f4(int n, uint32_t sfa_id, uint32_t sfb_id) {
+  uint32_t d = 0;
+  d |= (sfb_id & 3u) << 4;
+  d |= 5u << 7;                      // a_format E2M1
+  d |= 0u << 10;                     // b_format E4M3
+  d |= (uint32_t)(n >> 3) << 17;     // N
+  d |= 1u << 23;                     // scale format E8M0
+  d |= (uint32_t)(kMmaM >> 4) << 24; // M
+  d |= (sfa_id & 3u) << 29;
+  return d;
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct TileInfo {
+  int e, mt, p0, nvalid, rowb;
+};
+
+template <int BN>
+__device__ __forceinline__ TileInfo tile_info(const MmaLaunch &a, const int32_t *tile_off, int tile,
+                                              int n_active) {
+  int lo = 0, hi = n_active - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (tile_off[mid] <= tile) lo = mid;
+    else hi = mid - 1;
+  }
+  TileInfo t;
+  t.e = a.act_list[lo];
+  const int local = tile - tile_off[lo];
+  const int n_e = a.offsets[t.e + 1] - a.offsets[t.e];
+  const int ntn = (n_e + BN - 1) / BN;
+  t.mt = local / ntn;
+  const int nt = local - t.mt * ntn;
+  t.p0 = a.offsets[t.e] + nt * BN;
+  t.nvalid = min(BN, n_e - nt * BN);
+  t.rowb = a.pad_off[t.e] + nt * kMmaM;
+  return t;
+}
+
+template <int BN>
+struct MmaShape {
+  static constexpr int kA = kMmaM * 128;            // 128 rows x 128 unpacked bytes
+  static constexpr int kB = BN * 128;               // e4m3 tile of one term
+  static constexpr int kStage = ((kA + kActTerms * kB + 512 + kActTerms * 512) + 1023) / 1024 * 1024;
+  static constexpr int kStages = (BN >= 128) ? 3 : ((BN >= 64) ? 4 : 8);
+  static constexpr int kAccCols = 2 * BN;           // double-buffered accumulator
+  static constexpr int kSfCols = 4 + 4 * kActTerms; // SFA + 3 SFB atoms
+  static constexpr int kCols = (kAccCols + kSfCols <= 32) ? 32
+                               : (kAccCols + kSfCols <= 64) ? 64
+                               : (kAccCols + kSfCols <= 128) ? 128
+                               : (kAccCols + kSfCols <= 256) ? 256 : 512;
+  // Transaction bytes count the packed 4-bit source (8 KB per 128x128 box),
+  // not the 16 KB the TMA writes to shared memory.
+  static constexpr int kTx = kA / 2 + kActTerms * kB + 512 + kActTerms * 512;
+  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ MmaLaunch a) {
+  using S = MmaShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kStages * S::kStage);
+  uint64_t *empty = full + S::kStages;
+  uint64_t *accf = empty + S::kStages;
+  uint64_t *acce = accf + 2;
+  uint64_t *drain = acce + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 128);
+    }
+    mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)S::kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_active = a.meta[0];
+  const int32_t *tile_off = a.tile_off;
+  const int n_tiles = n_active > 0 ? tile_off[n_active] : 0;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int s = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      const TileInfo t = tile_info<BN>(a, tile_off, tile, n_active);
+      const int rowa = t.e * a.rows + t.mt * kMmaM;
+      const uint8_t *sfa = a.sfa + (((size_t)t.e * a.mtiles + t.mt) * a.ktiles) * 512;
+      bool ok = true;
+      for (int kt = 0; kt < a.ktiles; ++kt) {
+        if (!mbar_wait(&empty[s], phase ^ 1u, a.err, 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t *st = smem + s * S::kStage;
+        mbar_expect_tx(&full[s], S::kTx);
+        tma_load_2d(&a.tmap_a, st, &full[s], kt * kMmaKT, rowa);
+        for (int term = 0; term < kActTerms; ++term)
+          tma_load_2d(&a.tmap_b, st + S::kA + term * S::kB, &full[s], kt * kMmaKT, term * a.rb + t.rowb);
+        bulk_load(st + S::kA + kActTerms * S::kB, sfa + (size_t)kt * 512, 512, &full[s]);
+        for (int term = 0; term < kActTerms; ++term)
+          bulk_load(st + S::kA + kActTerms * S::kB + 512 + term * 512,
+                    a.sfb + (((size_t)term * (a.rb / kMmaM) + t.rowb / kMmaM) * a.ktiles + kt) * 512, 512,
+                    &full[s]);
+        if (++s == S::kStages) {
+          s = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int s = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    const uint32_t sfa_t = tmem + 2 * BN;
+    const uint32_t sfb_t = sfa_t + 4;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t accph = (uint32_t)(local >> 1) & 1u;
+      if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + buf * BN;
+      for (int kt = 0; kt < a.ktiles; ++kt) {
+        if (!mbar_wait(&full[s], phase, a.err, 3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t *st = smem + s * S::kStage;
+        const uint32_t a_addr = smem_u32(st);
+        const uint32_t sf_addr = smem_u32(st + S::kA + kActTerms * S::kB);
+        tc_cp_sf(sfa_t, smem_desc(sf_addr, 128, 0));
+        for (int term = 0; term < kActTerms; ++term)
+          tc_cp_sf(sfb_t + 4 * term, smem_desc(sf_addr + 512 + 512 * term, 128, 0));
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = smem_desc(a_addr + 32 * ks, 1024, 2);
+#pragma unroll
+          for (int term = 0; term < kActTerms; ++term) {
+            const uint64_t bd = smem_desc(a_addr + S::kA + term * S::kB + 32 * ks, 1024, 2);
+            const uint32_t id = idesc_mxf8f6f4(BN, ks, ks);
+            tc_mma(d_tmem, ad, bd, id, sfa_t | ((uint32_t)ks << 30), (sfb_t + 4 * term) | ((uint32_t)ks << 30),
+                   (kt | ks | term) != 0);
+          }
+        }
+        tc_commit(&empty[s]);
+        if (++s == S::kStages) {
+          s = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) tc_commit(&accf[buf]);
+    }
+    // drain: wait until every tensor-core operation issued here has finished
+    tc_commit(drain);
+    mbar_wait(drain, 0, a.err, 4);
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_local = quad * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      const TileInfo t = tile_info<BN>(a, tile_off, tile, n_active);
+      const int buf = local & 1;
+      const uint32_t accph = (uint32_t)(local >> 1) & 1u;
+      if (!mbar_wait(&accf[buf], accph, a.err, 5)) break;
+      tc_fence_after();
+      const int r = t.mt * kMmaM + row_local;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tc_ld16(tmem + (uint32_t)(buf * BN + c0) + ((uint32_t)(quad * 32) << 16), v);
+        if (a.mode == 0) {
+          const int d = r >> 1;
+          const bool is_up = (r & 1) != 0;
+          const float bias = is_up ? (a.bias1 ? a.bias1[(size_t)t.e * a.out_rows + d] : 0.0f)
+                                   : (a.bias0 ? a.bias0[(size_t)t.e * a.out_rows + d] : 0.0f);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float val = v[j] + bias;
+            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+            if (!is_up && c0 + j < t.nvalid && d < a.out_rows)
+              a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + d] = swiglu_ref(val, other);
+          }
+        } else if (r < a.out_rows) {
+          const float bias = a.bias0 ? a.bias0[(size_t)t.e * a.out_rows + r] : 0.0f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < t.nvalid) a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + r] = v[j] + bias;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)S::kCols)
+                 : "memory");
+}
+
+template <int BN>
+cudaError_t launch_gemm_bn(const MmaLaunch &a, int sm_count, cudaStream_t s) {
+  using Sh = MmaShape<BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k_mma_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  int grid = a.max_tiles < sm_count ? a.max_tiles : sm_count;
+  if (grid < 1) grid = 1;
+  k_mma_gemm<BN><<<grid, 192, Sh::kSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_repack_mma_gu(const uint8_t *gate, const uint8_t *up, int64_t E, int D, int K,
+                                 MmaMatrix *m, cudaStream_t s) {
+  const int NB = K / 32;
+  k_repack_mma_gu<<<grid_of(E * D * NB), 256, 0, s>>>(gate, up, E, D, NB, m->kp, m->w, m->sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack_mma(const uint8_t *src, int64_t E, int R, int K, MmaMatrix *m, cudaStream_t s) {
+  const int NB = K / 32;
+  k_repack_mma<<<grid_of(E * R * NB), 256, 0, s>>>(src, E, R, NB, m->kp, m->w, m->sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tg, uint32_t tu, int64_t E, int D, int K,
+                                uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s) {
+  const int NB = K / 32;
+  k_synth_mma_gu<<<grid_of(E * D * NB), 256, 0, s>>>(seed, tg, tu, E, D, NB, lo, hi, m->kp, m->w, m->sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t E, int R, int K, uint8_t lo,
+                             uint8_t hi, MmaMatrix *m, cudaStream_t s) {
+  const int NB = K / 32;
+  k_synth_mma<<<grid_of(E * R * NB), 256, 0, s>>>(seed, tag, E, R, NB, lo, hi, m->kp, m->w, m->sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mma_plan(const int32_t *offsets, const int32_t *act_list, const int32_t *meta, int E,
+                            int bn, int mt_gu, int mt_dn, int32_t *pad_off, int32_t *tile_gu,
+                            int32_t *tile_dn, int32_t *pos_expert, cudaStream_t s) {
+  k_mma_plan<<<1, 1024, 0, s>>>(offsets, act_list, meta, E, bn, mt_gu, mt_dn, pad_off, tile_gu, tile_dn,
+                                pos_expert);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t *perm, int top_k,
+                                bool gather, const int32_t *offsets, const int32_t *pad_off,
+                                const int32_t *pos_expert, const int32_t *meta, int S_max, int K, int kp,
+                                int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s) {
+  if (S_max <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int blocks = (S_max * 32 + threads - 1) / threads;
+  k_quantize_act<<<blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off,
+                                            pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {
+  if (bn <= 16) return launch_gemm_bn<16>(a, sm_count, s);
+  return launch_gemm_bn<128>(a, sm_count, s);
+}
+
+}  // namespace spt

@@ -1,0 +1,102 @@
+// spt_mma.cuh -- tcgen05 block-scaled grouped GEMM for the MoE experts.
+//
+// D[rows, tokens] = W[rows, K] x X[tokens, K]^T per (expert, 128-row tile,
+// token tile) with kind::mxf8f6f4: A = the GGUF MXFP4 weights (e2m1 with the
+// GGUF E8M0 block scales, fed to the tensor core unchanged), B = activations
+// as three MXFP8 terms x = q1*s1 + q2*s2 + q3*s3 (e4m3 with per-32 E8M0
+// scales), accumulated in fp32 in TMEM.  Three terms keep the activation
+// error near 2^-12 of each 32-block's maximum, so block outputs stay well
+// inside the 1e-3 relative tolerance; one FP4 x FP8 product term would not.
+//
+// HBM layout of the MMA arena (one layer):
+//   gu_w   uint8 [E][2D][KP/2]   gate/up rows interleaved (row 2d = gate d,
+//                                row 2d+1 = up d), element k of a row at byte
+//                                k/2 (low nibble for even k); KP = K rounded
+//                                up to 128 (TMA 4-bit boxes are 128 wide),
+//                                pad elements are zero
+//   gu_sf  uint8 [E][2D/128][KP/128][512]  E8M0 scales in the tensor core's
+//                                scale-factor atom: row m of the tile, block
+//                                kb of the K tile at (m%32)*16 + (m/32)*4 + kb
+//   dn_w   uint8 [E][H][KPd/2], dn_sf [E][ceil(H/128)][KPd/128][512]
+// Activations (per call): q [3][RB][KP] e4m3 and sf [3][RB/128][KP/128][512].
+// Token j of expert e sits in row pad_off[e] + (j/BN)*128 + j%BN: every
+// BN-token tile owns one 128-row slot, so its scale atom starts at slot row 0.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spt {
+
+constexpr int kMmaM = 128;       // rows per tile (tcgen05 M for cta_group::1)
+constexpr int kMmaKT = 128;      // K elements per pipeline stage (one TMA box)
+constexpr int kActTerms = 3;     // MXFP8 terms of the activations
+
+struct MmaMatrix {
+  uint8_t *w = nullptr;      // packed e2m1 rows
+  uint8_t *sf = nullptr;     // scale-factor atoms
+  int rows = 0;              // rows per expert (2D for gate/up, H for down)
+  int k = 0;                 // logical K
+  int kp = 0;                // K padded to 128
+  int mtiles = 0;            // ceil(rows/128)
+  int64_t experts = 0;
+  alignas(64) CUtensorMap tmap;  // 2D [kp elements, experts*rows] 16U4_ALIGN16B, box 128x128, SW128
+};
+
+// Per-call operands of one grouped GEMM launch.
+struct MmaLaunch {
+  alignas(64) CUtensorMap tmap_a;  // weights
+  alignas(64) CUtensorMap tmap_b;  // activations: 2D [kp bytes, 3*rb rows], box [128, BN], SW128
+  const uint8_t *sfa = nullptr;
+  const uint8_t *sfb = nullptr;
+  int rows = 0, kp = 0, mtiles = 0, ktiles = 0;
+  int rb = 0;                        // activation rows per term (multiple of 128)
+  const int32_t *offsets = nullptr;  // [E+1] dispatch segment starts
+  const int32_t *pad_off = nullptr;  // [E] padded activation row of each segment
+  const int32_t *act_list = nullptr; // [E] active experts
+  const int32_t *tile_off = nullptr; // [E+1] tile prefix over active experts
+  const int32_t *meta = nullptr;     // [0] active experts
+  int max_tiles = 0;                 // host upper bound of tiles (grid sizing)
+  // epilogue
+  int mode = 0;                      // 0: gate/up + SwiGLU -> act[pos][D]; 1: down -> y[pos][H]
+  const float *bias0 = nullptr;      // gate bias [E][D] or down bias [E][H]
+  const float *bias1 = nullptr;      // up bias [E][D]
+  float *y = nullptr;
+  int y_stride = 0;                  // D (mode 0) or H (mode 1)
+  int out_rows = 0;                  // D (mode 0) or H (mode 1)
+  int32_t *err = nullptr;            // set nonzero when a bounded wait gives up
+};
+
+size_t mma_w_bytes(int64_t experts, int rows, int k);
+size_t mma_sf_bytes(int64_t experts, int rows, int k);
+
+// Encode the TMA map of a packed e2m1 matrix (returns false on failure).
+bool mma_encode_weights(MmaMatrix *m);
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn);
+
+cudaError_t launch_repack_mma_gu(const uint8_t *gate_gguf, const uint8_t *up_gguf, int64_t experts,
+                                 int D, int K, MmaMatrix *m, cudaStream_t s);
+cudaError_t launch_repack_mma(const uint8_t *gguf, int64_t experts, int rows, int K, MmaMatrix *m,
+                              cudaStream_t s);
+cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tag_gate, uint32_t tag_up, int64_t experts,
+                                int D, int K, uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
+cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t experts, int rows, int K,
+                             uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
+
+// Tile bookkeeping after dispatch: pad_off, tile_off (for BN tokens per tile
+// and `mtiles` row tiles per expert) and pos -> expert.
+cudaError_t launch_mma_plan(const int32_t *offsets, const int32_t *act_list, const int32_t *meta,
+                            int E, int bn, int mtiles_gu, int mtiles_dn, int32_t *pad_off,
+                            int32_t *tile_off_gu, int32_t *tile_off_dn, int32_t *pos_expert,
+                            cudaStream_t s);
+
+// Quantize rows to the three MXFP8 terms.  Source row of dispatch position
+// p: src[(gather ? perm[p]/top_k : p) * src_stride + k].
+cudaError_t launch_quantize_act(const float *src, int64_t src_stride, const int32_t *perm, int top_k,
+                                bool gather, const int32_t *offsets, const int32_t *pad_off,
+                                const int32_t *pos_expert, const int32_t *meta, int S_max, int K,
+                                int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s);
+
+cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s);
+
+}  // namespace spt

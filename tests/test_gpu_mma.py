@@ -1,0 +1,100 @@
+"""GPU parity of the tcgen05 path (FP4 weights x three MXFP8 activation
+terms on the tensor cores).
+
+Routing and dispatch are computed by the same bit-exact kernels as the exact
+path and must match the oracle bit for bit.  Block outputs are checked at
+the tolerance the block must meet: max |error| / max |reference| <= 1e-3 and
+cosine >= 0.99999 against the oracle's fp32 output.
+"""
+import numpy as np
+import pytest
+
+import refdata
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+spt = refdata.spt
+
+MAX_REL = 1e-3
+MIN_COS = 0.99999
+
+
+def _check_close(got, want, tag):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    assert np.isfinite(got).all(), tag
+    err = np.abs(got - want).max() / max(np.abs(want).max(), 1e-30)
+    cos = float(np.dot(got, want) / (np.linalg.norm(got) * np.linalg.norm(want) + 1e-300))
+    assert err <= MAX_REL and cos >= MIN_COS, (tag, err, cos)
+    return err, cos
+
+
+@pytest.fixture(scope="module")
+def mma_layer(ctx):
+    cfg = spt.Config(2880, 2880, 128, 4)
+    params = spt.SynthParams(seed=0)
+    host = spt.synth_layer_host(cfg, params)
+    dense = oracle.Weights(2880, 2880, 128, 4, host["router"], host["router_bias"], host["gate"],
+                           host["up"], host["down"], host["gate_bias"], host["up_bias"], host["down_bias"])
+    arena = ctx.synthetic_arena(cfg, params, flags=spt.ARENA_GEMV | spt.ARENA_MMA)
+    yield cfg, dense, arena
+    arena.close()
+    ctx.set_path(spt.PATH_AUTO)
+
+
+@pytest.mark.parametrize("T", [1, 4, 32, 300])
+def test_mma_block_matches_oracle(ctx, mma_layer, T):
+    cfg, dense, arena = mma_layer
+    x = spt.synth_normal_host(T, 2000, T * 2880)
+    ctx.set_path(spt.PATH_MMA)
+    got = ctx.forward_moe_batch(arena, x, T)
+    assert ctx.kernels_per_forward() == 9
+    r = ctx.last_routing(T, 128, 4)
+    sample = list(range(min(T, 8)))
+    want = oracle.forward_moe_batch(dense, x[: len(sample) * 2880], len(sample), workers=8,
+                                    want_internals=True)
+    full = oracle.forward_moe_batch(dense, x, T, workers=8, want_internals=True) if T <= 32 else None
+    if full is not None:
+        assert np.array_equal(r["sel_idx"], full["sel_idx"])
+        assert np.array_equal(r["perm"], full["perm"])
+        _check_close(got, full["out"], T)
+    _check_close(got[: len(sample) * 2880], want["out"], (T, "sample"))
+    # the exact path on the same arena stays bit-exact
+    ctx.set_path(spt.PATH_EXACT)
+    exact = ctx.forward_moe_batch(arena, x[: len(sample) * 2880], len(sample))
+    assert refdata.bits_equal(exact, want["out"].ravel()).all()
+
+
+@pytest.mark.parametrize("mode", ["normal", "ties", "underflow", "clamp"])
+@pytest.mark.parametrize("experts,k", [(4, 2), (7, 7), (8, 1)])
+def test_mma_reference_fixtures(ctx, mode, experts, k):
+    fx = refdata.moe_batch_fixture(96, 64, experts, k, 0, mode)
+    batch = 37
+    x = refdata.moe_batch_x(batch, 96, mode)
+    arena = ctx.arena([fx.reader], fx.cfg, [fx.lw], flags=spt.ARENA_MMA)
+    try:
+        ctx.set_path(spt.PATH_MMA)
+        got = ctx.forward_moe_batch(arena, x, batch)
+    finally:
+        ctx.set_path(spt.PATH_AUTO)
+        arena.close()
+    want = oracle.forward_moe_batch(fx.dense, x, batch)
+    _check_close(got, want, (mode, experts, k))
+
+
+def test_mma_large_batch_properties(ctx, mma_layer):
+    """T=2048 (128-token tiles): sampled tokens against the oracle and
+    permutation invariance of the batch (each token's result does not depend
+    on its neighbours)."""
+    cfg, dense, arena = mma_layer
+    T = 2048
+    x = spt.synth_normal_host(5, 2000, T * 2880)
+    ctx.set_path(spt.PATH_MMA)
+    got = ctx.forward_moe_batch(arena, x, T).reshape(T, 2880)
+    for t in (0, 5, 1023, 2047):
+        want = oracle.forward_moe_batch(dense, x[t * 2880:(t + 1) * 2880], 1, workers=8)
+        _check_close(got[t], want, t)
+    perm = np.random.default_rng(1).permutation(T)
+    gp = ctx.forward_moe_batch(arena, x.reshape(T, 2880)[perm].ravel(), T).reshape(T, 2880)
+    _check_close(gp, got[perm], "perm")
+    ctx.set_path(spt.PATH_AUTO)
