@@ -79,7 +79,7 @@ func sptTensor(t ggufindex.Tensor, names *[]*C.char) C.spt_tensor {
 
 // arenaFor uploads the layer once.  The reader's mapped file view is passed
 // as the spt_reader (ggufmap exposes it through WithTensor for the whole
-// file range; see INTEGRATION.md).
+// file range).
 func arenaFor(ctx *C.spt_context, reader *ggufmmap.Reader, cfg *Config, lw *LayerWeights) (*C.spt_arena, error) {
 	sptMu.Lock()
 	defer sptMu.Unlock()
