@@ -190,6 +190,20 @@ spt_status spt_forward_moe(spt_context *ctx, spt_arena *arena, int64_t layer, co
 spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int64_t layer,
                                         const float *x, float *out, int64_t batch);
 
+/* Allocation-free variant of spt_forward_moe_batch_device (no counterpart in
+ * the reference).  For callers that cannot let the library allocate device
+ * memory while they run: an engine that reserved all of HBM at load time, or
+ * a latency-critical decode loop that must not pay cudaMalloc/cudaFree's
+ * device-wide synchronisation.  Runs the exact (bit-identical) path with all
+ * intermediates in one static device array of about 2.2 MB, held by every GPU
+ * that loads the library.  Limits: batch x top-k <= 64, hidden and expert
+ * dimensions <= 4096, experts <= 256 (SPT_ERR_UNSUPPORTED otherwise); needs an
+ * SPT_ARENA_GEMV arena.  The first call on a device looks up the array's
+ * device address (make it before any stream capture).  All calls share the
+ * array: calls that overlap on the GPU race and must be serialised. */
+spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_arena *arena, int64_t layer,
+                                               const float *x, float *out, int64_t batch);
+
 /* Drop-in one-shot form of forwardMoEBatch: validates every tensor against
  * the reader, uploads the layer, runs it and frees it. */
 spt_status spt_forward_moe_batch_reader(spt_context *ctx, const spt_reader *reader,

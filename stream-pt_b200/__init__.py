@@ -197,6 +197,7 @@ def lib():
         "spt_forward_moe_batch": ([vp, vp, i64, vp, i64, vp, i64, i64, vp], st),
         "spt_forward_moe": ([vp, vp, i64, vp, i64, vp, i64, vp], st),
         "spt_forward_moe_batch_device": ([vp, vp, i64, vp, vp, i64], st),
+        "spt_forward_moe_batch_device_static": ([vp, vp, i64, vp, vp, i64], st),
         "spt_forward_moe_batch_reader": ([vp, P(_Reader), P(_Config), P(_LayerWeights), vp, i64, vp, i64, i64, vp], st),
         "spt_last_routing": ([vp, vp, vp, vp, vp, vp, P(i64)], st),
         "spt_route_moe_batch": ([vp, vp, ctypes.c_uint64, vp, i64, vp, i64, i64, i64, vp, vp], st),
@@ -339,6 +340,12 @@ class Context:
     def forward_moe_batch_device(self, arena: "Arena", x_ptr: int, out_ptr: int, batch: int, layer: int = 0):
         self.check(lib().spt_forward_moe_batch_device(self._h, arena.handle, layer, ctypes.c_void_p(x_ptr),
                                                       ctypes.c_void_p(out_ptr), batch))
+
+    def forward_moe_batch_device_static(self, arena: "Arena", x_ptr: int, out_ptr: int, batch: int,
+                                        layer: int = 0):
+        """Allocation-free forward on device pointers (static device scratch)."""
+        self.check(lib().spt_forward_moe_batch_device_static(self._h, arena.handle, layer, ctypes.c_void_p(x_ptr),
+                                                             ctypes.c_void_p(out_ptr), batch))
 
     def forward_moe_batch_reader(self, reader: Reader, cfg: Config, lw: LayerWeights, x: np.ndarray,
                                  out: np.ndarray, batch: int, cancel: Optional[np.ndarray] = None):

@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <limits>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1289,3 +1290,136 @@ spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len,
 }
 
 }  // extern "C"
+
+// =========================================================================
+// Allocation-free forward.  Some callers cannot let this library call
+// cudaMalloc once they are running: an engine that reserved all of HBM for
+// the expert arena and its own caching allocator at load time (a late
+// cudaMalloc would fail or evict), and latency-critical decode loops, where
+// cudaMalloc/cudaFree synchronise the whole device.  This entry point runs the
+// exact path with every intermediate in one file-scope device array instead
+// of the context's grow-on-demand buffers.
+namespace {
+
+constexpr int64_t kStaticMaxSlots = 64;     // tokens x top-k per call
+constexpr int64_t kStaticMaxDim = 4096;     // hidden and expert dimension
+constexpr int64_t kStaticMaxExperts = 256;  // experts (the dispatch kernel's limit too)
+
+constexpr size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+constexpr size_t kOffLogits = 0;
+constexpr size_t kOffSelIdx = kOffLogits + align256(sizeof(float) * kStaticMaxSlots * kStaticMaxExperts);
+constexpr size_t kOffSelW = kOffSelIdx + align256(sizeof(int32_t) * kStaticMaxSlots);
+constexpr size_t kOffOffsets = kOffSelW + align256(sizeof(float) * kStaticMaxSlots);
+constexpr size_t kOffPerm = kOffOffsets + align256(sizeof(int32_t) * (kStaticMaxExperts + 1));
+constexpr size_t kOffSlotPos = kOffPerm + align256(sizeof(int32_t) * kStaticMaxSlots);
+constexpr size_t kOffActList = kOffSlotPos + align256(sizeof(int32_t) * kStaticMaxSlots);
+constexpr size_t kOffMeta = kOffActList + align256(sizeof(int32_t) * kStaticMaxExperts);
+constexpr size_t kOffAct = kOffMeta + 256;
+constexpr size_t kOffRes = kOffAct + align256(sizeof(float) * kStaticMaxSlots * kStaticMaxDim);
+constexpr size_t kStaticBytes = kOffRes + align256(sizeof(float) * kStaticMaxSlots * kStaticMaxDim);
+
+}  // namespace
+
+// About 2.2 MB; every GPU that loads the library holds it until the process exits.
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
+
+namespace {
+
+std::mutex g_static_mu;
+void *g_static_addr[64] = {};
+
+// Device address of g_static_scratch on ctx's device.  The host-side name
+// is only a stand-in, so the address is looked up once per device (with that
+// device current) and cached.
+spt_status static_scratch(spt_context *ctx, unsigned char **out) {
+  if (ctx->device < 0 || ctx->device >= 64) return fail(ctx, SPT_ERR_UNSUPPORTED, "device index %d", ctx->device);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_addr[ctx->device]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGetSymbolAddress(static scratch)");
+    g_static_addr[ctx->device] = p;
+  }
+  *out = static_cast<unsigned char *>(g_static_addr[ctx->device]);
+  return SPT_OK;
+}
+
+}  // namespace
+
+extern "C" spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_arena *arena,
+                                                          int64_t layer, const float *x, float *out,
+                                                          int64_t batch) {
+  if (!ctx || !arena || !x || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (batch <= 0 || layer < 0 || layer >= (int64_t)arena->layers.size())
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  const spt_moe_config &c = arena->cfg;
+  const int64_t H = c.hidden_dim, D = c.expert_hidden_dim, E = c.num_experts, K = c.num_experts_used;
+  if (batch * K > kStaticMaxSlots || H > kStaticMaxDim || D > kStaticMaxDim || E > kStaticMaxExperts ||
+      K > kSelectMaxK)
+    return fail(ctx, SPT_ERR_UNSUPPORTED,
+                "batch %lld x top-k %lld, hidden %lld, expert dim %lld or %lld experts exceed the static "
+                "scratch (tokens x top-k <= %lld, dimensions <= %lld, experts <= %lld)",
+                (long long)batch, (long long)K, (long long)H, (long long)D, (long long)E,
+                (long long)kStaticMaxSlots, (long long)kStaticMaxDim, (long long)kStaticMaxExperts);
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  const LayerDev &L = arena->layers[(size_t)layer];
+  if (!L.has_g8) return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_GEMV");
+  unsigned char *base = nullptr;
+  if ((st = static_scratch(ctx, &base))) return st;
+  // Nothing here needs zeroing: every word is written before it is read within
+  // one call (the dispatch kernel counts in shared memory), so the previous
+  // call's contents are harmless.  Calls that overlap on the GPU (two streams,
+  // or two host threads on different contexts of one device) share this array
+  // and race: serialise them.
+  float *logits = reinterpret_cast<float *>(base + kOffLogits);
+  int32_t *sel_idx = reinterpret_cast<int32_t *>(base + kOffSelIdx);
+  float *sel_w = reinterpret_cast<float *>(base + kOffSelW);
+  int32_t *offsets = reinterpret_cast<int32_t *>(base + kOffOffsets);
+  int32_t *perm = reinterpret_cast<int32_t *>(base + kOffPerm);
+  int32_t *slot_pos = reinterpret_cast<int32_t *>(base + kOffSlotPos);
+  int32_t *act_list = reinterpret_cast<int32_t *>(base + kOffActList);
+  int32_t *meta = reinterpret_cast<int32_t *>(base + kOffMeta);
+  float *act = reinterpret_cast<float *>(base + kOffAct);
+  float *res = reinterpret_cast<float *>(base + kOffRes);
+  const int T = (int)batch;
+  cudaStream_t s = ctx->stream;
+  SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, T, (int)H, (int)E, logits, 8, s));
+  SPT_CUDA(ctx, launch_select(logits, T, (int)E, (int)K, sel_idx, sel_w, s));
+  SPT_CUDA(ctx, launch_dispatch(sel_idx, sel_w, (int)(T * K), (int)E, offsets, perm, slot_pos, act_list, meta, s));
+  const int mt = pick_mt(T, K, E);
+  GemvLaunch gu;
+  gu.m0 = L.gate;
+  gu.m1 = L.up;
+  gu.bias0 = L.gate_bias;
+  gu.bias1 = L.up_bias;
+  gu.x = x;
+  gu.x_stride = H;
+  gu.y = act;
+  gu.y_stride = D;
+  gu.perm = perm;
+  gu.offsets = offsets;
+  gu.act_list = act_list;
+  gu.meta = meta;
+  gu.top_k = (int)K;
+  gu.mode = kRowsMoEGateUp;
+  gu.gate_up = true;
+  gu.max_active = (int)std::min<int64_t>(E, T * K);
+  gu.mt = mt > 4 ? 4 : mt;
+  SPT_CUDA(ctx, launch_gemv(gu, ctx->sm_count, s));
+  GemvLaunch dn = gu;
+  dn.m0 = L.down;
+  dn.m1 = MatrixG8{};
+  dn.bias0 = L.down_bias;
+  dn.bias1 = nullptr;
+  dn.x = act;
+  dn.x_stride = D;
+  dn.y = res;
+  dn.y_stride = H;
+  dn.mode = kRowsMoEDown;
+  dn.gate_up = false;
+  dn.mt = mt;
+  SPT_CUDA(ctx, launch_gemv(dn, ctx->sm_count, s));
+  SPT_CUDA(ctx, launch_combine(res, sel_w, slot_pos, T, (int)K, (int)H, out, s));
+  return SPT_OK;
+}
