@@ -44,7 +44,7 @@ CONFIGS = {
                desc="decode, 1 token (BASELINE configs[0])"),
     "c1": dict(T=32, seed=1, zipf_s=0.0, zipf_beta=0.0, router_bias=True,
                desc="prefill batch T=32 (BASELINE configs[1])"),
-    "c2": dict(T=2048, seed=2, zipf_s=1.1, zipf_beta=1.0, router_bias=True,
+    "c2": dict(T=2048, seed=2, zipf_s=1.1, zipf_beta=0.9, router_bias=True,
                desc="prefill T=2048, Zipf(1.1)-skewed router bias (BASELINE configs[2])"),
 }
 
@@ -269,7 +269,7 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel (gate/up GEMV + SwiGLU) -----------
     peak, peak_src = load_peaks()
-    gu = [s["gate_up_swiglu"] for s in stage_ms if s]
+    gu = [s["gate_up"] for s in stage_ms if s]
     dn = [s["down"] for s in stage_ms if s]
     gu_ms = sum(gu) / len(gu) if gu else float("nan")
     dn_ms = sum(dn) / len(dn) if dn else float("nan")

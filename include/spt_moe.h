@@ -186,7 +186,8 @@ spt_status spt_forward_moe_batch(spt_context *ctx, spt_arena *arena, int64_t lay
 spt_status spt_forward_moe(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
                            int64_t x_len, float *out, int64_t out_len,
                            const volatile int32_t *cancel);
-/* Same block on device pointers, enqueued on the context stream. */
+/* Same block on device pointers (16-byte aligned), enqueued on the context
+ * stream. */
 spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int64_t layer,
                                         const float *x, float *out, int64_t batch);
 
@@ -223,9 +224,11 @@ spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index,
 /* Per-stage device timing of the block.  When enabled, every forward call
  * records CUDA events on the context stream around its stages; spt_stage_times
  * returns the durations (ms) of the last call:
- * [0] router, [1] select, [2] dispatch, [3] gate/up+SwiGLU, [4] down, [5] combine.
+ * [0] router, [1] select, [2] dispatch, [3] tile plan + activation quantisation,
+ * [4] gate/up + SwiGLU, [5] quantisation of the SwiGLU output, [6] down,
+ * [7] combine (stages 3 and 5 are empty on the exact path).
  * Returns the number of stages written (<= n). */
-#define SPT_NUM_STAGES 6
+#define SPT_NUM_STAGES 8
 spt_status spt_set_stage_timing(spt_context *ctx, int enable);
 int spt_stage_times(spt_context *ctx, float *ms, int n);
 /* Number of kernels the last forward call launched. */

@@ -277,7 +277,7 @@ class Context:
     def sync(self):
         self.check(lib().spt_context_sync(self._h))
 
-    STAGES = ("router", "select", "dispatch", "gate_up_swiglu", "down", "combine")
+    STAGES = ("router", "select", "dispatch", "quant_x", "gate_up", "quant_act", "down", "combine")
 
     def set_stage_timing(self, enable: bool = True):
         self.check(lib().spt_set_stage_timing(self._h, int(enable)))

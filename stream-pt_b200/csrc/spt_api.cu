@@ -10,6 +10,7 @@
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -445,6 +446,8 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   SPT_CUDA(ctx, ctx->sfx.ensure((size_t)kActTerms * (rb / kMmaM) * (kph / kMmaKT) * 512));
   SPT_CUDA(ctx, ctx->qa.ensure((size_t)kActTerms * rb * kpd));
   SPT_CUDA(ctx, ctx->sfa.ensure((size_t)kActTerms * (rb / kMmaM) * (kpd / kMmaKT) * 512));
+  const int terms = mma_stacked(bn) ? 1 : kActTerms;  // term planes in the activation layout
+  const int ks = mma_stage_tiles(bn);
   const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
   SPT_CUDA(ctx, launch_mma_plan(ctx->offsets.as<int32_t>(), ctx->act_list.as<int32_t>(), ctx->meta.as<int32_t>(),
                                 E, bn, mt_gu, mt_dn, ctx->pad_off.as<int32_t>(), ctx->tile_gu.as<int32_t>(),
@@ -454,8 +457,11 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
                                     ctx->meta.as<int32_t>(), (int)S, H, kph, rb, bn, ctx->qx.as<uint8_t>(),
                                     ctx->sfx.as<uint8_t>(), s));
   MmaLaunch g;
-  g.tmap_a = L.gu_mma.tmap;
-  if (!mma_encode_acts(&g.tmap_b, ctx->qx.as<uint8_t>(), kph, rb, bn))
+  g.ks = ks;
+  g.tmap_a = ks > 1 ? L.gu_mma.tmap2 : L.gu_mma.tmap;
+  g.tmap_a1 = L.gu_mma.tmap;
+  if (!mma_encode_acts(&g.tmap_b, ctx->qx.as<uint8_t>(), kph, rb, terms, mma_box_rows(bn), ks) ||
+      !mma_encode_acts(&g.tmap_b1, ctx->qx.as<uint8_t>(), kph, rb, terms, mma_box_rows(bn), 1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
   g.sfa = L.gu_mma.sf;
   g.sfb = ctx->sfx.as<uint8_t>();
@@ -477,16 +483,19 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.y_stride = D;
   g.out_rows = D;
   g.err = ctx->dev_err.as<int32_t>();
-  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[3], s));
-  SPT_CUDA(ctx, launch_mma_gemm(g, bn, ctx->sm_count, s));
+  if (const char *pf = getenv("SPT_MMA_PREFETCH")) g.prefetch = atoi(pf);
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[4], s));
+  SPT_CUDA(ctx, launch_mma_gemm(g, bn, ctx->sm_count, s));
+  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[5], s));
   SPT_CUDA(ctx, launch_quantize_act(ctx->act.as<float>(), D, nullptr, K, false, ctx->offsets.as<int32_t>(),
                                     ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
                                     ctx->meta.as<int32_t>(), (int)S, D, kpd, rb, bn, ctx->qa.as<uint8_t>(),
                                     ctx->sfa.as<uint8_t>(), s));
   MmaLaunch dn = g;
-  dn.tmap_a = L.dn_mma.tmap;
-  if (!mma_encode_acts(&dn.tmap_b, ctx->qa.as<uint8_t>(), kpd, rb, bn))
+  dn.tmap_a = ks > 1 ? L.dn_mma.tmap2 : L.dn_mma.tmap;
+  dn.tmap_a1 = L.dn_mma.tmap;
+  if (!mma_encode_acts(&dn.tmap_b, ctx->qa.as<uint8_t>(), kpd, rb, terms, mma_box_rows(bn), ks) ||
+      !mma_encode_acts(&dn.tmap_b1, ctx->qa.as<uint8_t>(), kpd, rb, terms, mma_box_rows(bn), 1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
   dn.sfa = L.dn_mma.sf;
   dn.sfb = ctx->sfa.as<uint8_t>();
@@ -502,6 +511,7 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   dn.y = ctx->res.as<float>();
   dn.y_stride = H;
   dn.out_rows = H;
+  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[6], s));
   SPT_CUDA(ctx, launch_mma_gemm(dn, bn, ctx->sm_count, s));
   ctx->kernels_last = 9;
   return SPT_OK;
@@ -543,6 +553,7 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
                                 ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
                                 ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
                                 ctx->meta.as<int32_t>(), s));
+  SPT_MARK(3);
   const int max_active = (int)std::min<int64_t>(E, T * K);
   const bool use_mma = L.has_mma && (ctx->path == SPT_PATH_MMA || (ctx->path == SPT_PATH_AUTO)) &&
                        !(ctx->path == SPT_PATH_EXACT);
@@ -572,9 +583,10 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     gu.gate_up = true;
     gu.max_active = max_active;
     gu.mt = mt > 4 ? 4 : mt;
-    SPT_MARK(3);
-    SPT_CUDA(ctx, launch_gemv(gu, ctx->sm_count, s));
     SPT_MARK(4);
+    SPT_CUDA(ctx, launch_gemv(gu, ctx->sm_count, s));
+    SPT_MARK(5);
+    SPT_MARK(6);
     GemvLaunch dn = gu;
     dn.m0 = L.down;
     dn.m1 = MatrixG8{};
@@ -590,10 +602,10 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     SPT_CUDA(ctx, launch_gemv(dn, ctx->sm_count, s));
     ctx->kernels_last = 6;
   }
-  SPT_MARK(5);
+  SPT_MARK(7);
   SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), ctx->sel_w.as<float>(),
                                ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
-  SPT_MARK(6);
+  SPT_MARK(8);
 #undef SPT_MARK
   ctx->last_T = T;
   ctx->last_E = E;
@@ -1028,6 +1040,8 @@ spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int6
   if (!ctx || !arena || !x || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
   if (batch <= 0 || layer < 0 || layer >= (int64_t)arena->layers.size())
     return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "device x and out must be 16-byte aligned");
   spt_status st = require_device(ctx);
   if (st) return st;
   return forward_device(ctx, arena, layer, x, out, batch);
@@ -1352,6 +1366,8 @@ extern "C" spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_
   if (!ctx || !arena || !x || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
   if (batch <= 0 || layer < 0 || layer >= (int64_t)arena->layers.size())
     return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "device x and out must be 16-byte aligned");
   const spt_moe_config &c = arena->cfg;
   const int64_t H = c.hidden_dim, D = c.expert_hidden_dim, E = c.num_experts, K = c.num_experts_used;
   if (batch * K > kStaticMaxSlots || H > kStaticMaxDim || D > kStaticMaxDim || E > kStaticMaxExperts ||

@@ -99,55 +99,79 @@ __device__ __forceinline__ float reduce_row(const float acc[8], int lane) {
 
 // ---------------------------------------------------------------------------
 // Router: logits[t,e] = dotF32AVX2(W[e], x[t]) + bias[e].
-// One warp per (expert, MTR tokens).  Lane l runs chains l and l+32 of the
-// 64 chains (a_j[l'] with chain = 8j+l'); a 32-element tail (hidden%64 == 32)
-// feeds chains 0..31 (vector_amd64.go:45-52).
-template <int MTR>
+// One warp per (ME experts, MTR tokens).  Lane l runs chains l and l+32 of
+// the 64 chains (a_j[l'] with chain = 8j+l'); a 32-element tail
+// (hidden%64 == 32) feeds chains 0..31 (vector_amd64.go:45-52).  The chunk
+// loop is unrolled UNR times so the loads of UNR chunks are in flight
+// together; x values are reused across the ME experts of the warp.
+template <int MTR, int ME, int UNR>
 __global__ void __launch_bounds__(32) k_router(const float *__restrict__ W,
                                                const float *__restrict__ x,
                                                const float *__restrict__ bias, int T, int H,
                                                int E, float *__restrict__ logits) {
-  const int e = blockIdx.x, t0 = blockIdx.y * MTR, lane = threadIdx.x;
+  const int e0 = blockIdx.x * ME, t0 = blockIdx.y * MTR, lane = threadIdx.x;
   const int nt = min(MTR, T - t0);
-  const float *w = W + (size_t)e * H;
-  float a[MTR], b[MTR];
+  const int ne = min(ME, E - e0);
+  float a[ME][MTR], b[ME][MTR];
 #pragma unroll
-  for (int j = 0; j < MTR; ++j) a[j] = b[j] = 0.0f;
+  for (int m = 0; m < ME; ++m)
+#pragma unroll
+    for (int j = 0; j < MTR; ++j) a[m][j] = b[m][j] = 0.0f;
+  const float *xr[MTR];
+#pragma unroll
+  for (int j = 0; j < MTR; ++j) xr[j] = x + (size_t)(t0 + min(j, nt - 1)) * H;
+  const float *wr[ME];
+#pragma unroll
+  for (int m = 0; m < ME; ++m) wr[m] = W + (size_t)(e0 + min(m, ne - 1)) * H;
+  const int full = H / 64;
   int o = 0;
-  for (; o + 64 <= H; o += 64) {
-    const float w0 = __ldg(w + o + lane), w1 = __ldg(w + o + 32 + lane);
+#pragma unroll UNR
+  for (int c = 0; c < full; ++c, o += 64) {
+    float w0[ME], w1[ME], x0[MTR], x1[MTR];
+#pragma unroll
+    for (int m = 0; m < ME; ++m) {
+      w0[m] = __ldg(wr[m] + o + lane);
+      w1[m] = __ldg(wr[m] + o + 32 + lane);
+    }
 #pragma unroll
     for (int j = 0; j < MTR; ++j) {
-      if (j < nt) {
-        const float *xr = x + (size_t)(t0 + j) * H + o;
-        a[j] = fmaf(w0, __ldg(xr + lane), a[j]);
-        b[j] = fmaf(w1, __ldg(xr + 32 + lane), b[j]);
-      }
+      x0[j] = __ldg(xr[j] + o + lane);
+      x1[j] = __ldg(xr[j] + o + 32 + lane);
     }
+#pragma unroll
+    for (int m = 0; m < ME; ++m)
+#pragma unroll
+      for (int j = 0; j < MTR; ++j) {
+        a[m][j] = fmaf(w0[m], x0[j], a[m][j]);
+        b[m][j] = fmaf(w1[m], x1[j], b[m][j]);
+      }
   }
   if (o < H) {
-    const float w0 = __ldg(w + o + lane);
 #pragma unroll
-    for (int j = 0; j < MTR; ++j)
-      if (j < nt) a[j] = fmaf(w0, __ldg(x + (size_t)(t0 + j) * H + o + lane), a[j]);
+    for (int m = 0; m < ME; ++m) {
+      const float w0 = __ldg(wr[m] + o + lane);
+#pragma unroll
+      for (int j = 0; j < MTR; ++j) a[m][j] = fmaf(w0, __ldg(xr[j] + o + lane), a[m][j]);
+    }
   }
-  const float be = bias ? bias[e] : 0.0f;
 #pragma unroll
-  for (int j = 0; j < MTR; ++j) {
-    if (j < nt) {
-      const float a8 = __shfl_sync(kFull, a[j], (lane + 8) & 31);
-      const float a16 = __shfl_sync(kFull, a[j], (lane + 16) & 31);
-      const float a24 = __shfl_sync(kFull, a[j], (lane + 24) & 31);
-      const float b8 = __shfl_sync(kFull, b[j], (lane + 8) & 31);
-      const float b16 = __shfl_sync(kFull, b[j], (lane + 16) & 31);
-      const float b24 = __shfl_sync(kFull, b[j], (lane + 24) & 31);
-      const float s0 = ((a[j] + a8) + a16) + a24;
-      const float s1 = ((b[j] + b8) + b16) + b24;
-      const float s = s0 + s1;
-      const float p = s + __shfl_sync(kFull, s, (lane + 4) & 31);
+  for (int m = 0; m < ME; ++m) {
+    const float be = (bias && m < ne) ? bias[e0 + m] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < MTR; ++j) {
+      const float a8 = __shfl_sync(kFull, a[m][j], (lane + 8) & 31);
+      const float a16 = __shfl_sync(kFull, a[m][j], (lane + 16) & 31);
+      const float a24 = __shfl_sync(kFull, a[m][j], (lane + 24) & 31);
+      const float b8 = __shfl_sync(kFull, b[m][j], (lane + 8) & 31);
+      const float b16 = __shfl_sync(kFull, b[m][j], (lane + 16) & 31);
+      const float b24 = __shfl_sync(kFull, b[m][j], (lane + 24) & 31);
+      const float s0 = ((a[m][j] + a8) + a16) + a24;
+      const float s1 = ((b[m][j] + b8) + b16) + b24;
+      const float sv = s0 + s1;
+      const float p = sv + __shfl_sync(kFull, sv, (lane + 4) & 31);
       const float qv = p + __shfl_sync(kFull, p, (lane + 1) & 31);
       const float r = qv + __shfl_sync(kFull, qv, (lane + 2) & 31);
-      if (lane == 0) logits[(size_t)(t0 + j) * E + e] = r + be;
+      if (lane == 0 && j < nt && m < ne) logits[(size_t)(t0 + j) * E + e0 + m] = r + be;
     }
   }
 }
@@ -567,8 +591,13 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
                                                      logits);
     return cudaGetLastError();
   }
-  constexpr int MTR = 8;
-  k_router<MTR><<<dim3(E, (T + MTR - 1) / MTR), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+  if (T <= 2) {
+    k_router<2, 1, 9><<<dim3(E, (T + 1) / 2), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+  } else if (T <= 64) {
+    k_router<4, 2, 3><<<dim3((E + 1) / 2, (T + 3) / 4), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+  } else {
+    k_router<8, 4, 1><<<dim3((E + 3) / 4, (T + 7) / 8), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+  }
   return cudaGetLastError();
 }
 

@@ -28,7 +28,8 @@ namespace spt {
 
 size_t mma_w_bytes(int64_t experts, int rows, int k) {
   const int kp = (k + kMmaKT - 1) / kMmaKT * kMmaKT;
-  return (size_t)experts * rows * (kp / 2);
+  const int mtiles = (rows + kMmaM - 1) / kMmaM;
+  return (size_t)experts * mtiles * (kp / kMmaKT) * kMmaM * (kMmaKT / 2);
 }
 
 size_t mma_sf_bytes(int64_t experts, int rows, int k) {
@@ -56,26 +57,47 @@ bool mma_encode_weights(MmaMatrix *m) {
   auto fn = encode_fn();
   if (!fn || !m->w) return false;
   if (m->kp % 128 != 0 || (reinterpret_cast<uintptr_t>(m->w) & 31) != 0) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)m->kp, (cuuint64_t)(m->experts * m->rows)};
-  cuuint64_t strides[1] = {(cuuint64_t)(m->kp / 2)};
+  // Tile-major: every 128-row x 128-element box is one contiguous 8 KB block,
+  // so the map is [rows = boxes * 128][128 elements] with a 64-byte pitch.
+  const uint64_t boxes = (uint64_t)m->experts * m->mtiles * (m->kp / kMmaKT);
+  cuuint64_t dims[2] = {(cuuint64_t)kMmaKT, (cuuint64_t)(boxes * kMmaM)};
+  cuuint64_t strides[1] = {(cuuint64_t)(kMmaKT / 2)};
   cuuint32_t box[2] = {128, 128};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(&m->tmap, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, m->w, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  cuuint64_t dims3[3] = {(cuuint64_t)kMmaKT, (cuuint64_t)kMmaM, (cuuint64_t)boxes};
+  cuuint64_t strides3[2] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)(kMmaKT / 2) * kMmaM};
+  cuuint32_t box3[3] = {128, 128, 2};
+  cuuint32_t estr3[3] = {1, 1, 1};
+  r = fn(&m->tmap2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, m->w, dims3, strides3, box3, estr3,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn) {
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int terms, int box_rows, int ktiles) {
   auto fn = encode_fn();
-  if (!fn || !q) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)(kActTerms * (int64_t)rb)};
-  cuuint64_t strides[1] = {(cuuint64_t)kp};
-  cuuint32_t box[2] = {128, (cuuint32_t)bn};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (!fn || !q || box_rows < 1 || box_rows > 256 || (terms != 1 && terms != kActTerms)) return false;
+  const cuuint64_t kt_n = (cuuint64_t)(kp / kMmaKT);
+  CUresult r;
+  if (terms == 1) {
+    cuuint64_t dims[3] = {128, (cuuint64_t)rb, kt_n};
+    cuuint64_t strides[2] = {128, (cuuint64_t)rb * 128};
+    cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)ktiles};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[4] = {128, (cuuint64_t)rb, (cuuint64_t)terms, kt_n};
+    cuuint64_t strides[3] = {128, (cuuint64_t)rb * 128, (cuuint64_t)rb * 128 * terms};
+    cuuint32_t box[4] = {128, (cuuint32_t)box_rows, (cuuint32_t)terms, (cuuint32_t)ktiles};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   return r == CUDA_SUCCESS;
 }
 
@@ -88,7 +110,9 @@ namespace {
 // i+16 << 4) of MMA row `row` of expert e.
 __device__ __forceinline__ void put_mma_block(const uint8_t blk[17], int64_t e, int row, int b,
                                               int rows, int kp, uint8_t *w, uint8_t *sf) {
-  uint8_t *dst = w + ((size_t)e * rows + row) * (kp / 2) + (size_t)b * 16;
+  const int mtiles_ = (rows + kMmaM - 1) / kMmaM, ktiles_ = kp / kMmaKT;
+  const size_t box = ((size_t)e * mtiles_ + row / kMmaM) * ktiles_ + (size_t)(b / 4);
+  uint8_t *dst = w + (box * kMmaM + (size_t)(row % kMmaM)) * (kMmaKT / 2) + (size_t)(b % 4) * 16;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int e0 = 2 * i, e1 = 2 * i + 1;  // natural order: element 2i low nibble
@@ -177,29 +201,48 @@ unsigned grid_of(int64_t n) {
 
 // ---------------------------------------------------------------------------
 // Tile plan after dispatch (one CTA).
-__global__ void k_mma_plan(const int32_t *__restrict__ offsets, const int32_t *__restrict__ act_list,
-                           const int32_t *__restrict__ meta, int E, int bn, int mt_gu, int mt_dn,
-                           int32_t *pad_off, int32_t *tile_gu, int32_t *tile_dn,
-                           int32_t *pos_expert) {
-  const int na = meta[0], total = meta[1];
-  if (threadIdx.x == 0) {
-    int pad = 0, tg = 0, td = 0;
-    for (int a = 0; a < na; ++a) {
-      const int e = act_list[a];
-      const int n = offsets[e + 1] - offsets[e];
-      const int nt = (n + bn - 1) / bn;
-      pad_off[e] = pad;  // every token tile owns a 128-row slot of the activation buffer
-      pad += nt * kMmaM;
-      tile_gu[a] = tg;
-      tile_dn[a] = td;
-      tg += mt_gu * nt;
-      td += mt_dn * nt;
-    }
-    tile_gu[na] = tg;
-    tile_dn[na] = td;
+__global__ void __launch_bounds__(1024) k_mma_plan(const int32_t *__restrict__ offsets,
+                                                   const int32_t *__restrict__ act_list,
+                                                   const int32_t *__restrict__ meta, int E, int bn, int mt_gu,
+                                                   int mt_dn, int32_t *pad_off, int32_t *tile_gu,
+                                                   int32_t *tile_dn, int32_t *pos_expert) {
+  // Exclusive scans over the active experts (at most 1024) of: 128-row slots
+  // per token tile, gate/up tiles and down tiles.
+  __shared__ int sc[3][1024];
+  const int na = meta[0], total = meta[1], tid = threadIdx.x;
+  int e = -1, nt = 0;
+  if (tid < na) {
+    e = act_list[tid];
+    nt = (offsets[e + 1] - offsets[e] + bn - 1) / bn;
   }
-  for (int p = threadIdx.x; p < total; p += blockDim.x) {
-    int lo = 0, hi = E - 1;  // largest e with offsets[e] <= p
+  sc[0][tid] = tid < na ? nt * kMmaM : 0;
+  sc[1][tid] = tid < na ? nt * mt_gu : 0;
+  sc[2][tid] = tid < na ? nt * mt_dn : 0;
+  __syncthreads();
+  for (int d = 1; d < 1024; d <<= 1) {  // inclusive Hillis-Steele scan
+    int v0 = 0, v1 = 0, v2 = 0;
+    if (tid >= d) {
+      v0 = sc[0][tid - d];
+      v1 = sc[1][tid - d];
+      v2 = sc[2][tid - d];
+    }
+    __syncthreads();
+    sc[0][tid] += v0;
+    sc[1][tid] += v1;
+    sc[2][tid] += v2;
+    __syncthreads();
+  }
+  if (tid < na) {
+    pad_off[e] = sc[0][tid] - nt * kMmaM;
+    tile_gu[tid] = sc[1][tid] - nt * mt_gu;
+    tile_dn[tid] = sc[2][tid] - nt * mt_dn;
+  }
+  if (tid == 0) {
+    tile_gu[na] = na > 0 ? sc[1][na - 1] : 0;
+    tile_dn[na] = na > 0 ? sc[2][na - 1] : 0;
+  }
+  for (int p = tid; p < total; p += blockDim.x) {
+    int lo = 0, hi = E - 1;  // largest expert with offsets[e] <= p
     while (lo < hi) {
       const int mid = (lo + hi + 1) / 2;
       if (offsets[mid] <= p) lo = mid;
@@ -220,41 +263,60 @@ __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
                                const int32_t *__restrict__ perm, int top_k, int gather,
                                const int32_t *__restrict__ offsets, const int32_t *__restrict__ pad_off,
                                const int32_t *__restrict__ pos_expert, const int32_t *__restrict__ meta,
-                               int S_max, int K, int kp, int rb, int bn, uint8_t *__restrict__ q,
-                               uint8_t *__restrict__ sf) {
-  const int lane = threadIdx.x & 31;
-  const int pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                               int S_max, int K, int kp, int rb, int bn, int stacked,
+                               uint8_t *__restrict__ q, uint8_t *__restrict__ sf) {
+  // One warp per (dispatch position, 128-element K tile); 8 lanes per
+  // 32-element block, 4 elements per lane.
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int kt_n = kp / kMmaKT;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int pos = (int)(gw / kt_n), kt = (int)(gw - (int64_t)pos * kt_n);
   if (pos >= S_max || pos >= meta[1]) return;
+  const int b = kt * 4 + (lane >> 3);  // 32-element block of this lane group
   const int e = pos_expert[pos];
   const int j = pos - offsets[e];
-  const int row = pad_off[e] + (j / bn) * kMmaM + (j % bn);
+  const int slot = pad_off[e] + (j / bn) * kMmaM;  // this token tile's 128-row slot
   const int64_t srow = gather ? (int64_t)(perm[pos] / top_k) : (int64_t)pos;
-  const float *x = src + srow * stride;
-  const int nblk = kp / 32, kt_n = kp / kMmaKT, g = row / kMmaM, m = row % kMmaM;
-  for (int b = 0; b < nblk; ++b) {
-    float v = (b * 32 < K) ? x[b * 32 + lane] : 0.0f;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (b * 32 < K) v = *reinterpret_cast<const float4 *>(src + srow * stride + b * 32 + sub * 4);
 #pragma unroll
-    for (int t = 0; t < kActTerms; ++t) {
-      float amax = fabsf(v);
+  for (int t = 0; t < kActTerms; ++t) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-      int ex = -126;
-      if (amax > 0.0f) {
+    for (int off = 4; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    int ex = -126;
+    if (amax > 0.0f) {
+      if (!isfinite(amax)) {
+        ex = 120;
+      } else {
         int e2;
         const float mant = frexpf(amax * (1.0f / 448.0f), &e2);  // amax/448 = mant * 2^e2
         ex = (mant == 0.5f) ? e2 - 1 : e2;
         if (__fmul_rn(amax, exp2i(-ex)) > 448.0f) ex += 1;
         ex = max(-126, min(ex, 120));
       }
-      const float scaled = __fmul_rn(v, exp2i(-ex));
-      const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(scaled, __NV_SATFINITE, __NV_E4M3);
+    }
+    const float inv = exp2i(-ex), sc = exp2i(ex);
+    float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(__fmul_rn(vv[i], inv), __NV_SATFINITE, __NV_E4M3);
       const __half_raw hr = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
-      const float back = __fmul_rn(__half2float(__half(hr)), exp2i(ex));
-      q[((int64_t)t * rb + row) * kp + b * 32 + lane] = (uint8_t)code;
-      if (lane == 0)
-        sf[(((int64_t)t * (rb / kMmaM) + g) * kt_n + b / 4) * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] =
-            (uint8_t)(ex + 127);
-      v = __fsub_rn(v, back);
+      vv[i] = __fsub_rn(vv[i], __fmul_rn(__half2float(__half(hr)), sc));
+      packed |= (uint32_t)code << (8 * i);
+    }
+    v = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    // stacked: the three terms share the slot (rows t*bn + j%bn, one scale atom);
+    // otherwise each term has its own plane of rb rows and its own atom.
+    const int m = stacked ? t * bn + (j % bn) : (j % bn);
+    const int64_t row = (int64_t)slot + m;
+    const int64_t plane = stacked ? (int64_t)kt : (int64_t)kt * kActTerms + t;  // [kt][term] plane of rb rows
+    *reinterpret_cast<uint32_t *>(q + (plane * rb + row) * kMmaKT + (b % 4) * 32 + sub * 4) = packed;
+    if (sub == 0) {
+      const int64_t atom = (int64_t)(slot / kMmaM) * kt_n + kt;
+      const int64_t a2 = stacked ? atom : atom * kActTerms + t;
+      sf[a2 * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] = (uint8_t)(ex + 127);
     }
   }
 }
@@ -315,6 +377,31 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, void *dst, u
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap *map, void *dst, uint64_t *bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap *map, void *dst, uint64_t *bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -398,49 +485,75 @@ struct TileInfo {
   int e, mt, p0, nvalid, rowb;
 };
 
+constexpr int kMaxActive = 256;  // active experts per launch (the dispatch kernel's limit)
+
+// Per-launch tile tables, copied to shared memory once per CTA so that the
+// producer, MMA and epilogue roles decode tiles without global loads.
+struct TileTables {
+  int tile_off[kMaxActive + 1];  // first tile of each active expert
+  int e[kMaxActive];             // expert id
+  int p0[kMaxActive];            // first dispatch position
+  int n[kMaxActive];             // tokens
+  int pad[kMaxActive];           // first 128-row activation slot
+};
+
 template <int BN>
-__device__ __forceinline__ TileInfo tile_info(const MmaLaunch &a, const int32_t *tile_off, int tile,
-                                              int n_active) {
+__device__ __forceinline__ TileInfo tile_info(const TileTables &tt, int tile, int n_active, int mtiles) {
   int lo = 0, hi = n_active - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) / 2;
-    if (tile_off[mid] <= tile) lo = mid;
+    if (tt.tile_off[mid] <= tile) lo = mid;
     else hi = mid - 1;
   }
   TileInfo t;
-  t.e = a.act_list[lo];
-  const int local = tile - tile_off[lo];
-  const int n_e = a.offsets[t.e + 1] - a.offsets[t.e];
+  t.e = tt.e[lo];
+  const int local = tile - tt.tile_off[lo];
+  const int n_e = tt.n[lo];
   const int ntn = (n_e + BN - 1) / BN;
   t.mt = local / ntn;
   const int nt = local - t.mt * ntn;
-  t.p0 = a.offsets[t.e] + nt * BN;
+  t.p0 = tt.p0[lo] + nt * BN;
   t.nvalid = min(BN, n_e - nt * BN);
-  t.rowb = a.pad_off[t.e] + nt * kMmaM;
+  t.rowb = tt.pad[lo] + nt * kMmaM;
+  (void)mtiles;
   return t;
 }
 
-template <int BN>
+// STACK: the three activation terms are stacked along N in one tile
+// (N = 3*BN <= 128, one MMA per K-step, one scale atom); otherwise each term
+// is its own N = BN operand with its own atom (three MMAs per K-step).
+// STACK: the three activation terms are stacked along N in one tile
+// (N = 3*BN <= 128, one MMA per K-step, one scale atom); otherwise each term
+// is its own N = BN operand with its own atom (three MMAs per K-step).
+// KS: K tiles per pipeline stage.
+template <int BN, bool STACK, int KS>
 struct MmaShape {
-  static constexpr int kA = kMmaM * 128;            // 128 rows x 128 unpacked bytes
+  static constexpr int kA = kMmaM * 128;            // one K tile: 128 rows x 128 unpacked bytes
   static constexpr int kB = BN * 128;               // e4m3 tile of one term
-  static constexpr int kStage = ((kA + kActTerms * kB + 512 + kActTerms * 512) + 1023) / 1024 * 1024;
-  static constexpr int kStages = (BN >= 128) ? 3 : ((BN >= 64) ? 4 : 8);
-  static constexpr int kAccCols = 2 * BN;           // double-buffered accumulator
-  static constexpr int kSfCols = 4 + 4 * kActTerms; // SFA + 3 SFB atoms
+  static constexpr int kSfb = STACK ? 1 : kActTerms; // activation scale atoms per K tile
+  static constexpr int kN = STACK ? kActTerms * BN : BN;  // MMA N
+  // stage: A[KS] | B[KS][terms] | SFA[KS] | SFB[KS][kSfb]
+  static constexpr int kOffB = KS * kA;
+  static constexpr int kOffSfa = kOffB + KS * kActTerms * kB;
+  static constexpr int kOffSfb = kOffSfa + KS * 512;
+  static constexpr int kStage = ((kOffSfb + KS * kSfb * 512) + 1023) / 1024 * 1024;
+  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
+  static constexpr int kAccCols = 2 * kN;           // double-buffered accumulator
+  static constexpr int kSfCols = 4 + 4 * kSfb;      // SFA + SFB atoms of one K tile
   static constexpr int kCols = (kAccCols + kSfCols <= 32) ? 32
                                : (kAccCols + kSfCols <= 64) ? 64
                                : (kAccCols + kSfCols <= 128) ? 128
                                : (kAccCols + kSfCols <= 256) ? 256 : 512;
-  // Transaction bytes count the packed 4-bit source (8 KB per 128x128 box),
-  // not the 16 KB the TMA writes to shared memory.
-  static constexpr int kTx = kA / 2 + kActTerms * kB + 512 + kActTerms * 512;
-  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+  // Transaction bytes of one K tile; the weights count as their packed
+  // 4-bit source (8 KB per 128x128 box), not the 16 KB written to smem.
+  static constexpr int kTxTile = kA / 2 + kActTerms * kB + 512 + kSfb * 512;
+  static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/ +
+                               (int)sizeof(TileTables);
 };
 
-template <int BN>
+template <int BN, bool STACK, int KS>
 __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ MmaLaunch a) {
-  using S = MmaShape<BN>;
+  using S = MmaShape<BN, STACK, KS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kStages * S::kStage);
@@ -449,7 +562,20 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
   uint64_t *acce = accf + 2;
   uint64_t *drain = acce + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  TileTables &tt = *reinterpret_cast<TileTables *>(smem + S::kStages * S::kStage + 256);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const int na = a.meta[0];
+    for (int i = threadIdx.x; i < na && i < kMaxActive; i += blockDim.x) {
+      const int e = a.act_list[i];
+      tt.e[i] = e;
+      tt.p0[i] = a.offsets[e];
+      tt.n[i] = a.offsets[e + 1] - a.offsets[e];
+      tt.pad[i] = a.pad_off[e];
+      tt.tile_off[i] = a.tile_off[i];
+    }
+    if (threadIdx.x == 0) tt.tile_off[min(na, kMaxActive)] = a.tile_off[min(na, kMaxActive)];
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S::kStages; ++i) {
@@ -473,34 +599,65 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_active = a.meta[0];
-  const int32_t *tile_off = a.tile_off;
-  const int n_tiles = n_active > 0 ? tile_off[n_active] : 0;
+  const int n_active = min(a.meta[0], kMaxActive);
+  const int n_tiles = n_active > 0 ? tt.tile_off[n_active] : 0;
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
+    // Weight boxes are also prefetched into L2 kPrefetch stages ahead of the
+    // shared-memory ring, so more HBM traffic is in flight than the ring holds.
+    const int kPrefetch = a.prefetch;
     int s = 0;
     uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-      const TileInfo t = tile_info<BN>(a, tile_off, tile, n_active);
-      const int rowa = t.e * a.rows + t.mt * kMmaM;
+    const int kt_n = a.ktiles;
+    auto box_row = [&](const TileInfo &ti, int kt) { return ((ti.e * a.mtiles + ti.mt) * kt_n + kt) * kMmaM; };
+    int pf_tile = -1, pf_kt = 0;   // next (local tile, k-tile) to prefetch
+    TileInfo pf_info{};
+    auto prefetch_upto = [&](int local_limit, int kt_limit) {
+      // prefetch every (local tile, kt) < (local_limit, kt_limit) in order
+      while (pf_tile < local_limit || (pf_tile == local_limit && pf_kt < kt_limit)) {
+        if (pf_tile < 0 || pf_kt == kt_n) {
+          ++pf_tile;
+          pf_kt = 0;
+          const int tile = blockIdx.x + pf_tile * gridDim.x;
+          if (tile >= n_tiles) { pf_tile = 1 << 29; return; }
+          pf_info = tile_info<BN>(tt, tile, n_active, a.mtiles);
+          continue;
+        }
+        tma_prefetch_2d(&a.tmap_a1, 0, box_row(pf_info, pf_kt));
+        ++pf_kt;
+      }
+    };
+    int local = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
       const uint8_t *sfa = a.sfa + (((size_t)t.e * a.mtiles + t.mt) * a.ktiles) * 512;
+      const uint8_t *sfb = a.sfb + ((size_t)(t.rowb / kMmaM) * a.ktiles) * (S::kSfb * 512);
+      const int box0 = (t.e * a.mtiles + t.mt) * kt_n;
       bool ok = true;
-      for (int kt = 0; kt < a.ktiles; ++kt) {
+      for (int kt = 0; kt < a.ktiles; kt += KS) {
+        if (kPrefetch > 0) {
+          const int ahead = kt + kPrefetch;  // prefetch target, in (local, kt) order
+          prefetch_upto(local + ahead / kt_n, ahead % kt_n);
+        }
         if (!mbar_wait(&empty[s], phase ^ 1u, a.err, 1)) {
           ok = false;
           break;
         }
+        const int nk = min(KS, a.ktiles - kt);
         uint8_t *st = smem + s * S::kStage;
-        mbar_expect_tx(&full[s], S::kTx);
-        tma_load_2d(&a.tmap_a, st, &full[s], kt * kMmaKT, rowa);
-        for (int term = 0; term < kActTerms; ++term)
-          tma_load_2d(&a.tmap_b, st + S::kA + term * S::kB, &full[s], kt * kMmaKT, term * a.rb + t.rowb);
-        bulk_load(st + S::kA + kActTerms * S::kB, sfa + (size_t)kt * 512, 512, &full[s]);
-        for (int term = 0; term < kActTerms; ++term)
-          bulk_load(st + S::kA + kActTerms * S::kB + 512 + term * 512,
-                    a.sfb + (((size_t)term * (a.rb / kMmaM) + t.rowb / kMmaM) * a.ktiles + kt) * 512, 512,
-                    &full[s]);
+        mbar_expect_tx(&full[s], nk * S::kTxTile);
+        if (nk == KS && KS > 1) {
+          tma_load_3d(&a.tmap_a, st, &full[s], 0, 0, box0 + kt);
+          if (STACK) tma_load_3d(&a.tmap_b, st + S::kOffB, &full[s], 0, t.rowb, kt);
+          else tma_load_4d(&a.tmap_b, st + S::kOffB, &full[s], 0, t.rowb, 0, kt);
+        } else {
+          tma_load_2d(&a.tmap_a1, st, &full[s], 0, (box0 + kt) * kMmaM);
+          if (STACK) tma_load_3d(&a.tmap_b1, st + S::kOffB, &full[s], 0, t.rowb, kt);
+          else tma_load_4d(&a.tmap_b1, st + S::kOffB, &full[s], 0, t.rowb, 0, kt);
+        }
+        bulk_load(st + S::kOffSfa, sfa + (size_t)kt * 512, nk * 512, &full[s]);
+        bulk_load(st + S::kOffSfb, sfb + (size_t)kt * S::kSfb * 512, nk * S::kSfb * 512, &full[s]);
         if (++s == S::kStages) {
           s = 0;
           phase ^= 1u;
@@ -510,39 +667,57 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
+    // Descriptors are built once; per stage and K-step only their 14-bit start
+    // address fields advance (stage bases are 1024-byte aligned and the whole
+    // ring lies below 256 KB, so the adds never carry out of the field).
     int s = 0;
     uint32_t phase = 0;
     int local = 0;
-    const uint32_t sfa_t = tmem + 2 * BN;
+    const uint32_t sfa_t = tmem + 2 * S::kN;
     const uint32_t sfb_t = sfa_t + 4;
+    const uint32_t base = smem_u32(smem);
+    const uint64_t a_desc0 = smem_desc(base, 1024, 2);
+    const uint64_t b_desc0 = smem_desc(base + S::kOffB, 1024, 2);
+    const uint64_t sfa_desc0 = smem_desc(base + S::kOffSfa, 128, 0);
+    const uint64_t sfb_desc0 = smem_desc(base + S::kOffSfb, 128, 0);
+    constexpr uint64_t kStage16 = S::kStage >> 4, kA16 = S::kA >> 4, kB16 = S::kB >> 4;
+    uint32_t idesc[4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) idesc[ks] = idesc_mxf8f6f4(S::kN, ks, ks);
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t accph = (uint32_t)(local >> 1) & 1u;
       if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2)) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + buf * BN;
-      for (int kt = 0; kt < a.ktiles; ++kt) {
+      const uint32_t d_tmem = tmem + buf * S::kN;
+      uint32_t acc = 0u;
+      for (int kt = 0; kt < a.ktiles; kt += KS) {
         if (!mbar_wait(&full[s], phase, a.err, 3)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint8_t *st = smem + s * S::kStage;
-        const uint32_t a_addr = smem_u32(st);
-        const uint32_t sf_addr = smem_u32(st + S::kA + kActTerms * S::kB);
-        tc_cp_sf(sfa_t, smem_desc(sf_addr, 128, 0));
-        for (int term = 0; term < kActTerms; ++term)
-          tc_cp_sf(sfb_t + 4 * term, smem_desc(sf_addr + 512 + 512 * term, 128, 0));
+        const int nk = min(KS, a.ktiles - kt);
+        const uint64_t so = (uint64_t)s * kStage16;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t ad = smem_desc(a_addr + 32 * ks, 1024, 2);
+        for (int j = 0; j < KS; ++j) {
+          if (j < nk) {
+            tc_cp_sf(sfa_t, sfa_desc0 + so + 32 * j);
 #pragma unroll
-          for (int term = 0; term < kActTerms; ++term) {
-            const uint64_t bd = smem_desc(a_addr + S::kA + term * S::kB + 32 * ks, 1024, 2);
-            const uint32_t id = idesc_mxf8f6f4(BN, ks, ks);
-            tc_mma(d_tmem, ad, bd, id, sfa_t | ((uint32_t)ks << 30), (sfb_t + 4 * term) | ((uint32_t)ks << 30),
-                   (kt | ks | term) != 0);
+            for (int term = 0; term < S::kSfb; ++term)
+              tc_cp_sf(sfb_t + 4 * term, sfb_desc0 + so + 32 * (j * S::kSfb + term));
+            const uint64_t ad = a_desc0 + so + (uint64_t)j * kA16;
+            const uint64_t bd = b_desc0 + so + (uint64_t)j * kActTerms * kB16;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+              for (int term = 0; term < (STACK ? 1 : kActTerms); ++term) {
+                tc_mma(d_tmem, ad + 2 * ks, bd + term * kB16 + 2 * ks, idesc[ks], sfa_t | ((uint32_t)ks << 30),
+                       (sfb_t + 4 * term) | ((uint32_t)ks << 30), acc);
+                acc = 1u;
+              }
+            }
           }
         }
         tc_commit(&empty[s]);
@@ -562,7 +737,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
     const int row_local = quad * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
-      const TileInfo t = tile_info<BN>(a, tile_off, tile, n_active);
+      const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
       const int buf = local & 1;
       const uint32_t accph = (uint32_t)(local >> 1) & 1u;
       if (!mbar_wait(&accf[buf], accph, a.err, 5)) break;
@@ -570,7 +745,15 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
       const int r = t.mt * kMmaM + row_local;
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
-        tc_ld16(tmem + (uint32_t)(buf * BN + c0) + ((uint32_t)(quad * 32) << 16), v);
+        const uint32_t col = tmem + (uint32_t)(buf * S::kN + c0) + ((uint32_t)(quad * 32) << 16);
+        tc_ld16(col, v);
+        if (STACK) {  // the three term partial sums sit BN columns apart
+          float v1[16], v2[16];
+          tc_ld16(col + BN, v1);
+          tc_ld16(col + 2 * BN, v2);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = (v[j] + v1[j]) + v2[j];
+        }
         if (a.mode == 0) {
           const int d = r >> 1;
           const bool is_up = (r & 1) != 0;
@@ -602,18 +785,19 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
                  : "memory");
 }
 
-template <int BN>
+template <int BN, bool STACK, int KS>
 cudaError_t launch_gemm_bn(const MmaLaunch &a, int sm_count, cudaStream_t s) {
-  using Sh = MmaShape<BN>;
+  using Sh = MmaShape<BN, STACK, KS>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_mma_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_mma_gemm<BN, STACK, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Sh::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   int grid = a.max_tiles < sm_count ? a.max_tiles : sm_count;
   if (grid < 1) grid = 1;
-  k_mma_gemm<BN><<<grid, 192, Sh::kSmem, s>>>(a);
+  k_mma_gemm<BN, STACK, KS><<<grid, 192, Sh::kSmem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -660,15 +844,17 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
                                 int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s) {
   if (S_max <= 0) return cudaSuccess;
   const int threads = 256;
-  const int blocks = (S_max * 32 + threads - 1) / threads;
-  k_quantize_act<<<blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off,
-                                            pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
+  const int64_t warps = (int64_t)S_max * (kp / kMmaKT);
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  k_quantize_act<<<(unsigned)blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off,
+                                                      pos_expert, meta, S_max, K, kp, rb, bn, mma_stacked(bn) ? 1 : 0,
+                                                      q, sf);
   return cudaGetLastError();
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {
-  if (bn <= 16) return launch_gemm_bn<16>(a, sm_count, s);
-  return launch_gemm_bn<128>(a, sm_count, s);
+  if (bn <= 16) return launch_gemm_bn<16, true, kMmaStageTilesSmall>(a, sm_count, s);
+  return launch_gemm_bn<128, false, 1>(a, sm_count, s);
 }
 
 }  // namespace spt

@@ -9,18 +9,23 @@
 // inside the 1e-3 relative tolerance; one FP4 x FP8 product term would not.
 //
 // HBM layout of the MMA arena (one layer):
-//   gu_w   uint8 [E][2D][KP/2]   gate/up rows interleaved (row 2d = gate d,
-//                                row 2d+1 = up d), element k of a row at byte
-//                                k/2 (low nibble for even k); KP = K rounded
-//                                up to 128 (TMA 4-bit boxes are 128 wide),
-//                                pad elements are zero
+//   gu_w   uint8 [E][2D/128][KP/128][128][64]  tile-major packed e2m1: one
+//                                128-row x 128-element box is one contiguous
+//                                8 KB block (row r of the box at r*64, element
+//                                k of the row at byte k/2, low nibble for even
+//                                k); gate/up rows interleaved (row 2d = gate
+//                                d, row 2d+1 = up d); KP = K rounded up to 128
+//                                (4-bit TMA boxes are 128 wide), pads zero
 //   gu_sf  uint8 [E][2D/128][KP/128][512]  E8M0 scales in the tensor core's
 //                                scale-factor atom: row m of the tile, block
 //                                kb of the K tile at (m%32)*16 + (m/32)*4 + kb
-//   dn_w   uint8 [E][H][KPd/2], dn_sf [E][ceil(H/128)][KPd/128][512]
-// Activations (per call): q [3][RB][KP] e4m3 and sf [3][RB/128][KP/128][512].
-// Token j of expert e sits in row pad_off[e] + (j/BN)*128 + j%BN: every
-// BN-token tile owns one 128-row slot, so its scale atom starts at slot row 0.
+//   dn_w   uint8 [E][ceil(H/128)][KPd/128][128][64], dn_sf [E][ceil(H/128)][KPd/128][512]
+// Activations (per call), e4m3 in K-tile-major order plus scale atoms.  Every
+// BN-token tile owns one 128-row slot starting at pad_off[e] + (j/BN)*128 for
+// token j of expert e, so its scale atom starts at slot row 0.  BN = 16:
+// the three terms stack inside the slot (term t, token j at slot row
+// t*16 + j%16): q [KP/128][RB][128], sf [RB/128][KP/128][512].  BN = 128:
+// q [KP/128][3][RB][128], sf [RB/128][KP/128][3][512].
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -40,13 +45,21 @@ struct MmaMatrix {
   int kp = 0;                // K padded to 128
   int mtiles = 0;            // ceil(rows/128)
   int64_t experts = 0;
-  alignas(64) CUtensorMap tmap;  // 2D [kp elements, experts*rows] 16U4_ALIGN16B, box 128x128, SW128
+  alignas(64) CUtensorMap tmap;   // 2D [128 elements, boxes*128 rows] 16U4_ALIGN16B, box 128x128, SW128
+  alignas(64) CUtensorMap tmap2;  // 3D [128 elements, 128 rows, boxes], box 128x128x2 (two K tiles)
 };
 
-// Per-call operands of one grouped GEMM launch.
+// Per-call operands of one grouped GEMM launch.  Every copy operation costs
+// the SM's copy engine about the same time whatever its size, so a pipeline
+// stage moves `ks` K tiles of weights, activations (all terms) and scales in
+// four operations; the `*1` maps move the single K tile left at the end of a
+// tile when K/128 is odd.
 struct MmaLaunch {
-  alignas(64) CUtensorMap tmap_a;  // weights
-  alignas(64) CUtensorMap tmap_b;  // activations: 2D [kp bytes, 3*rb rows], box [128, BN], SW128
+  alignas(64) CUtensorMap tmap_a;   // weights, ks boxes
+  alignas(64) CUtensorMap tmap_a1;  // weights, 1 box
+  alignas(64) CUtensorMap tmap_b;   // activations, ks K tiles x all terms
+  alignas(64) CUtensorMap tmap_b1;  // activations, 1 K tile x all terms
+  int ks = 1;                       // K tiles per pipeline stage
   const uint8_t *sfa = nullptr;
   const uint8_t *sfb = nullptr;
   int rows = 0, kp = 0, mtiles = 0, ktiles = 0;
@@ -65,14 +78,26 @@ struct MmaLaunch {
   int y_stride = 0;                  // D (mode 0) or H (mode 1)
   int out_rows = 0;                  // D (mode 0) or H (mode 1)
   int32_t *err = nullptr;            // set nonzero when a bounded wait gives up
+  int prefetch = 0;                  // weight boxes prefetched into L2 ahead of the ring (0: off;
+                                     // measured slower on B200 at every distance tried)
 };
+
+// Token tiles of at most 16 tokens stack the three activation terms along N
+// and move two K tiles per pipeline stage; 128-token tiles move one.
+inline bool mma_stacked(int bn) { return bn <= 16; }
+constexpr int kMmaStageTilesSmall = 2;
+inline int mma_stage_tiles(int bn) { return bn <= 16 ? kMmaStageTilesSmall : 1; }
+// Activation rows of one TMA box: 3*bn when stacked, else bn.
+inline int mma_box_rows(int bn) { return mma_stacked(bn) ? kActTerms * bn : bn; }
 
 size_t mma_w_bytes(int64_t experts, int rows, int k);
 size_t mma_sf_bytes(int64_t experts, int rows, int k);
 
 // Encode the TMA map of a packed e2m1 matrix (returns false on failure).
 bool mma_encode_weights(MmaMatrix *m);
-bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn);
+// TMA map of the e4m3 activations stored K-tile-major [kt][terms][rb][128 B]
+// (terms = 1 when stacked): box 128 B x box_rows x terms x ktiles.
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int terms, int box_rows, int ktiles);
 
 cudaError_t launch_repack_mma_gu(const uint8_t *gate_gguf, const uint8_t *up_gguf, int64_t experts,
                                  int D, int K, MmaMatrix *m, cudaStream_t s);
