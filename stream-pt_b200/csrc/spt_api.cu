@@ -442,11 +442,11 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
   SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
   SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
-  SPT_CUDA(ctx, ctx->qx.ensure((size_t)kActTerms * rb * kph));
-  SPT_CUDA(ctx, ctx->sfx.ensure((size_t)kActTerms * (rb / kMmaM) * (kph / kMmaKT) * 512));
-  SPT_CUDA(ctx, ctx->qa.ensure((size_t)kActTerms * rb * kpd));
-  SPT_CUDA(ctx, ctx->sfa.ensure((size_t)kActTerms * (rb / kMmaM) * (kpd / kMmaKT) * 512));
-  const int terms = mma_stacked(bn) ? 1 : kActTerms;  // term planes in the activation layout
+  SPT_CUDA(ctx, ctx->qx.ensure(mma_act_bytes(bn, rb, kph)));
+  SPT_CUDA(ctx, ctx->sfx.ensure(mma_act_sf_bytes(bn, rb, kph)));
+  SPT_CUDA(ctx, ctx->qa.ensure(mma_act_bytes(bn, rb, kpd)));
+  SPT_CUDA(ctx, ctx->sfa.ensure(mma_act_sf_bytes(bn, rb, kpd)));
+  const bool fp4 = mma_fp4(bn);
   const int ks = mma_stage_tiles(bn);
   const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
   SPT_CUDA(ctx, launch_mma_plan(ctx->offsets.as<int32_t>(), ctx->act_list.as<int32_t>(), ctx->meta.as<int32_t>(),
@@ -458,11 +458,12 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
                                     ctx->sfx.as<uint8_t>(), s));
   MmaLaunch g;
   g.ks = ks;
-  g.tmap_a = ks > 1 ? L.gu_mma.tmap2 : L.gu_mma.tmap;
-  g.tmap_a1 = L.gu_mma.tmap;
-  if (!mma_encode_acts(&g.tmap_b, ctx->qx.as<uint8_t>(), kph, rb, terms, mma_box_rows(bn), ks) ||
-      !mma_encode_acts(&g.tmap_b1, ctx->qx.as<uint8_t>(), kph, rb, terms, mma_box_rows(bn), 1))
+  g.tmap_a = fp4 ? L.gu_mma.tmap_p : L.gu_mma.tmap;
+  g.tmap_a1 = fp4 ? L.gu_mma.tmap_p1 : L.gu_mma.tmap;
+  if (!mma_encode_acts(&g.tmap_b, ctx->qx.as<uint8_t>(), kph, rb, bn, ks) ||
+      !mma_encode_acts(&g.tmap_b1, ctx->qx.as<uint8_t>(), kph, rb, bn, 1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
+  g.w = L.gu_mma.w;
   g.sfa = L.gu_mma.sf;
   g.sfb = ctx->sfx.as<uint8_t>();
   g.rows = L.gu_mma.rows;
@@ -492,11 +493,12 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
                                     ctx->meta.as<int32_t>(), (int)S, D, kpd, rb, bn, ctx->qa.as<uint8_t>(),
                                     ctx->sfa.as<uint8_t>(), s));
   MmaLaunch dn = g;
-  dn.tmap_a = ks > 1 ? L.dn_mma.tmap2 : L.dn_mma.tmap;
-  dn.tmap_a1 = L.dn_mma.tmap;
-  if (!mma_encode_acts(&dn.tmap_b, ctx->qa.as<uint8_t>(), kpd, rb, terms, mma_box_rows(bn), ks) ||
-      !mma_encode_acts(&dn.tmap_b1, ctx->qa.as<uint8_t>(), kpd, rb, terms, mma_box_rows(bn), 1))
+  dn.tmap_a = fp4 ? L.dn_mma.tmap_p : L.dn_mma.tmap;
+  dn.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
+  if (!mma_encode_acts(&dn.tmap_b, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks) ||
+      !mma_encode_acts(&dn.tmap_b1, ctx->qa.as<uint8_t>(), kpd, rb, bn, 1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
+  dn.w = L.dn_mma.w;
   dn.sfa = L.dn_mma.sf;
   dn.sfb = ctx->sfa.as<uint8_t>();
   dn.rows = L.dn_mma.rows;

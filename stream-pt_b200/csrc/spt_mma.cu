@@ -68,32 +68,38 @@ bool mma_encode_weights(MmaMatrix *m) {
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
-  cuuint64_t dims3[3] = {(cuuint64_t)kMmaKT, (cuuint64_t)kMmaM, (cuuint64_t)boxes};
+  // Packed view for kind::mxf4: [boxes][128 rows][64 B], the 64-byte rows
+  // land in shared memory as they are (SW64).
+  cuuint64_t dims3[3] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)kMmaM, (cuuint64_t)boxes};
   cuuint64_t strides3[2] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)(kMmaKT / 2) * kMmaM};
-  cuuint32_t box3[3] = {128, 128, 2};
   cuuint32_t estr3[3] = {1, 1, 1};
-  r = fn(&m->tmap2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, m->w, dims3, strides3, box3, estr3,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  for (int one = 0; one < 2; ++one) {
+    cuuint32_t box3[3] = {(cuuint32_t)(kMmaKT / 2), (cuuint32_t)kMmaM, one ? 1u : (cuuint32_t)kMmaStageTilesFp4};
+    r = fn(one ? &m->tmap_p1 : &m->tmap_p, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, m->w, dims3, strides3, box3, estr3,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
+  return true;
 }
 
-bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int terms, int box_rows, int ktiles) {
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, int ktiles) {
   auto fn = encode_fn();
-  if (!fn || !q || box_rows < 1 || box_rows > 256 || (terms != 1 && terms != kActTerms)) return false;
+  const int box_rows = mma_box_rows(bn);
+  if (!fn || !q || box_rows < 1 || box_rows > 256 || ktiles < 1) return false;
   const cuuint64_t kt_n = (cuuint64_t)(kp / kMmaKT);
   CUresult r;
-  if (terms == 1) {
-    cuuint64_t dims[3] = {128, (cuuint64_t)rb, kt_n};
-    cuuint64_t strides[2] = {128, (cuuint64_t)rb * 128};
-    cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)ktiles};
+  if (mma_fp4(bn)) {
+    cuuint64_t dims[3] = {kMmaKT / 2, (cuuint64_t)rb, kt_n};
+    cuuint64_t strides[2] = {kMmaKT / 2, (cuuint64_t)rb * (kMmaKT / 2)};
+    cuuint32_t box[3] = {kMmaKT / 2, (cuuint32_t)box_rows, (cuuint32_t)ktiles};
     cuuint32_t estr[3] = {1, 1, 1};
     r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
-    cuuint64_t dims[4] = {128, (cuuint64_t)rb, (cuuint64_t)terms, kt_n};
-    cuuint64_t strides[3] = {128, (cuuint64_t)rb * 128, (cuuint64_t)rb * 128 * terms};
-    cuuint32_t box[4] = {128, (cuuint32_t)box_rows, (cuuint32_t)terms, (cuuint32_t)ktiles};
+    cuuint64_t dims[4] = {kMmaKT, (cuuint64_t)rb, (cuuint64_t)kActTerms, kt_n};
+    cuuint64_t strides[3] = {kMmaKT, (cuuint64_t)rb * kMmaKT, (cuuint64_t)rb * kMmaKT * kActTerms};
+    cuuint32_t box[4] = {kMmaKT, (cuuint32_t)box_rows, (cuuint32_t)kActTerms, (cuuint32_t)ktiles};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -253,17 +259,52 @@ __global__ void __launch_bounds__(1024) k_mma_plan(const int32_t *__restrict__ o
 }
 
 // ---------------------------------------------------------------------------
-// Activations -> three MXFP8 terms.  One warp per dispatch position; lane l
-// handles element l of every 32-element block.  Term scale: the smallest
-// power of two 2^e with max|block| / 2^e <= 448 (e4m3's largest finite), so
-// no element saturates; each residual is exact in fp32.
+// Activations -> block-scaled multi-term operands.  Each 32-element block is
+// written as a sum of terms q_t * 2^e_t, each term quantizing the residual
+// left by the previous ones; every residual is exact in fp32.  Term scale:
+// the smallest power of two 2^e with max|residual| / 2^e <= the format's
+// largest finite value, so no element saturates.
+//   FP4 (token tiles of <= 16): kFp4Terms e2m1 terms, stacked along N
+//     (term t, token j at slot row t*bn + j%bn); q [KP/128][RB][64 B].
+//   FP8 (128-token tiles): kActTerms e4m3 terms, each in its own plane of RB
+//     rows; q [KP/128][kActTerms][RB][128 B].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
 
+// Smallest e with amax / 2^e <= qmax (amax finite and > 0), clamped to the
+// E8M0 range the scale atoms hold.
+__device__ __forceinline__ int term_exponent(float amax, float qmax, float inv_qmax) {
+  if (!(amax > 0.0f)) return -126;
+  if (!isfinite(amax)) return 120;
+  int e2;
+  const float mant = frexpf(amax * inv_qmax, &e2);  // amax/qmax = mant * 2^e2, mant in [0.5, 1)
+  int ex = (mant == 0.5f) ? e2 - 1 : e2;
+  if (__fmul_rn(amax, exp2i(-ex)) > qmax) ex += 1;
+  return max(-126, min(ex, 120));
+}
+
+// e2m1 code -> value (sign in bit 3).
+__device__ __forceinline__ float e2m1_value(uint32_t code) {
+  const uint32_t c = code & 7u;  // 0, 0.5, 1, 1.5, 2, 3, 4, 6
+  const float mag = c < 2u ? 0.5f * (float)c : (float)(1u << ((c >> 1) - 1u)) * ((c & 1u) ? 1.5f : 1.0f);
+  return (code & 8u) ? -mag : mag;
+}
+
+// Two floats -> one byte of two e2m1 codes (lo in the low nibble), round to
+// nearest, saturating at 6.
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b;\n\tcvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n\tcvt.u32.u8 %0, b;\n\t}"
+      : "=r"(out)
+      : "f"(hi), "f"(lo));
+  return out;
+}
+
+template <bool FP4>
 __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
                                const int32_t *__restrict__ perm, int top_k, int gather,
                                const int32_t *__restrict__ offsets, const int32_t *__restrict__ pad_off,
                                const int32_t *__restrict__ pos_expert, const int32_t *__restrict__ meta,
-                               int S_max, int K, int kp, int rb, int bn, int stacked,
+                               int S_max, int K, int kp, int rb, int bn,
                                uint8_t *__restrict__ q, uint8_t *__restrict__ sf) {
   // One warp per (dispatch position, 128-element K tile); 8 lanes per
   // 32-element block, 4 elements per lane.
@@ -279,43 +320,42 @@ __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
   const int64_t srow = gather ? (int64_t)(perm[pos] / top_k) : (int64_t)pos;
   float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
   if (b * 32 < K) v = *reinterpret_cast<const float4 *>(src + srow * stride + b * 32 + sub * 4);
+  constexpr int kTerms = FP4 ? kFp4Terms : kActTerms;
+  constexpr float kQmax = FP4 ? 6.0f : 448.0f;
+  const int64_t atom = (int64_t)(slot / kMmaM) * kt_n + kt;
 #pragma unroll
-  for (int t = 0; t < kActTerms; ++t) {
+  for (int t = 0; t < kTerms; ++t) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int off = 4; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    int ex = -126;
-    if (amax > 0.0f) {
-      if (!isfinite(amax)) {
-        ex = 120;
-      } else {
-        int e2;
-        const float mant = frexpf(amax * (1.0f / 448.0f), &e2);  // amax/448 = mant * 2^e2
-        ex = (mant == 0.5f) ? e2 - 1 : e2;
-        if (__fmul_rn(amax, exp2i(-ex)) > 448.0f) ex += 1;
-        ex = max(-126, min(ex, 120));
-      }
-    }
+    const int ex = term_exponent(amax, kQmax, 1.0f / kQmax);
     const float inv = exp2i(-ex), sc = exp2i(ex);
     float vv[4] = {v.x, v.y, v.z, v.w};
-    uint32_t packed = 0;
+    const int m = FP4 ? t * bn + (j % bn) : (j % bn);  // row within the slot
+    if constexpr (FP4) {
+      const uint32_t c01 = e2m1x2(__fmul_rn(vv[0], inv), __fmul_rn(vv[1], inv));
+      const uint32_t c23 = e2m1x2(__fmul_rn(vv[2], inv), __fmul_rn(vv[3], inv));
+      const uint32_t codes[4] = {c01 & 15u, c01 >> 4, c23 & 15u, c23 >> 4};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(__fmul_rn(vv[i], inv), __NV_SATFINITE, __NV_E4M3);
-      const __half_raw hr = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
-      vv[i] = __fsub_rn(vv[i], __fmul_rn(__half2float(__half(hr)), sc));
-      packed |= (uint32_t)code << (8 * i);
+      for (int i = 0; i < 4; ++i) vv[i] = __fsub_rn(vv[i], __fmul_rn(e2m1_value(codes[i]), sc));
+      const int64_t row = (int64_t)kt * rb + slot + m;
+      *reinterpret_cast<uint16_t *>(q + row * (kMmaKT / 2) + (b % 4) * 16 + sub * 2) =
+          (uint16_t)(c01 | (c23 << 8));
+    } else {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(__fmul_rn(vv[i], inv), __NV_SATFINITE, __NV_E4M3);
+        const __half_raw hr = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
+        vv[i] = __fsub_rn(vv[i], __fmul_rn(__half2float(__half(hr)), sc));
+        packed |= (uint32_t)code << (8 * i);
+      }
+      const int64_t row = ((int64_t)kt * kActTerms + t) * rb + slot + m;
+      *reinterpret_cast<uint32_t *>(q + row * kMmaKT + (b % 4) * 32 + sub * 4) = packed;
     }
     v = make_float4(vv[0], vv[1], vv[2], vv[3]);
-    // stacked: the three terms share the slot (rows t*bn + j%bn, one scale atom);
-    // otherwise each term has its own plane of rb rows and its own atom.
-    const int m = stacked ? t * bn + (j % bn) : (j % bn);
-    const int64_t row = (int64_t)slot + m;
-    const int64_t plane = stacked ? (int64_t)kt : (int64_t)kt * kActTerms + t;  // [kt][term] plane of rb rows
-    *reinterpret_cast<uint32_t *>(q + (plane * rb + row) * kMmaKT + (b % 4) * 32 + sub * 4) = packed;
     if (sub == 0) {
-      const int64_t atom = (int64_t)(slot / kMmaM) * kt_n + kt;
-      const int64_t a2 = stacked ? atom : atom * kActTerms + t;
+      const int64_t a2 = FP4 ? atom : atom * kActTerms + t;
       sf[a2 * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] = (uint8_t)(ex + 127);
     }
   }
@@ -397,10 +437,8 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap *map, void *dst, u
       : "memory");
 }
 
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
                : "memory");
 }
 
@@ -452,6 +490,28 @@ __device__ __forceinline__ uint32_t idesc_mxf8f6f4(int n, uint32_t sfa_id, uint3
   return d;
 }
 
+// kind::mxf4: A and B e2m1 (format 1), E8M0 scales, K = 64 per MMA.
+__device__ __forceinline__ uint32_t idesc_mxf4(int n, uint32_t sfa_id, uint32_t sfb_id) {
+  uint32_t d = 0;
+  d |= (sfb_id & 3u) << 4;
+  d |= 1u << 7;                      // a_format E2M1
+  d |= 1u << 10;                     // b_format E2M1
+  d |= (uint32_t)(n >> 3) << 17;     // N
+  d |= 1u << 23;                     // scale format E8M0
+  d |= (uint32_t)(kMmaM >> 4) << 24; // M
+  d |= (sfa_id & 3u) << 29;
+  return d;                          // bit 31 = 0: K = 64
+}
+__device__ __forceinline__ void tc_mma_fp4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
   asm volatile(
@@ -519,41 +579,45 @@ __device__ __forceinline__ TileInfo tile_info(const TileTables &tt, int tile, in
   return t;
 }
 
-// STACK: the three activation terms are stacked along N in one tile
-// (N = 3*BN <= 128, one MMA per K-step, one scale atom); otherwise each term
-// is its own N = BN operand with its own atom (three MMAs per K-step).
-// STACK: the three activation terms are stacked along N in one tile
-// (N = 3*BN <= 128, one MMA per K-step, one scale atom); otherwise each term
-// is its own N = BN operand with its own atom (three MMAs per K-step).
-// KS: K tiles per pipeline stage.
-template <int BN, bool STACK, int KS>
+// FP4: kind::mxf4, packed weights (SW64), kFp4Terms e2m1 activation terms
+// stacked along N (N = kFp4Terms*BN, one scale atom per K tile, two K = 64
+// MMAs per K tile).  FP8: kind::mxf8f6f4, weights unpacked by the TMA
+// (SW128), kActTerms e4m3 terms each its own N = BN operand with its own atom
+// (four K = 32 MMAs per term per K tile).  KS: K tiles per pipeline stage.
+template <int BN, bool FP4, int KS>
 struct MmaShape {
-  static constexpr int kA = kMmaM * 128;            // one K tile: 128 rows x 128 unpacked bytes
-  static constexpr int kB = BN * 128;               // e4m3 tile of one term
-  static constexpr int kSfb = STACK ? 1 : kActTerms; // activation scale atoms per K tile
-  static constexpr int kN = STACK ? kActTerms * BN : BN;  // MMA N
-  // stage: A[KS] | B[KS][terms] | SFA[KS] | SFB[KS][kSfb]
+  static constexpr int kA = FP4 ? kMmaM * 64 : kMmaM * 128;     // smem bytes of one weight K tile
+  static constexpr int kATx = kMmaM * 64;                        // its transaction bytes (packed source)
+  static constexpr int kBTerm = FP4 ? BN * 64 : BN * 128;        // smem bytes of one term's K tile
+  static constexpr int kTerms = FP4 ? kFp4Terms : kActTerms;
+  static constexpr int kBt = kTerms * kBTerm;                    // all terms of one K tile
+  static constexpr int kSfb = FP4 ? 1 : kActTerms;               // activation scale atoms per K tile
+  static constexpr int kN = FP4 ? kFp4Terms * BN : BN;           // MMA N
+  static constexpr int kKSteps = FP4 ? 2 : 4;                    // MMAs (per term) per K tile
+  static constexpr uint32_t kLayout = FP4 ? 4u : 2u;             // smem descriptor: SW64 / SW128
+  static constexpr uint32_t kSbo = FP4 ? 512u : 1024u;           // 8-row swizzle atom
+  // stage: A[KS] | B[KS] | SFA[KS] | SFB[KS][kSfb]
   static constexpr int kOffB = KS * kA;
-  static constexpr int kOffSfa = kOffB + KS * kActTerms * kB;
+  static constexpr int kOffSfa = kOffB + KS * kBt;
   static constexpr int kOffSfb = kOffSfa + KS * 512;
   static constexpr int kStage = ((kOffSfb + KS * kSfb * 512) + 1023) / 1024 * 1024;
-  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
+  static constexpr int kStages = (200 * 1024) / kStage > 16 ? 16 : (200 * 1024) / kStage;
   static constexpr int kAccCols = 2 * kN;           // double-buffered accumulator
   static constexpr int kSfCols = 4 + 4 * kSfb;      // SFA + SFB atoms of one K tile
   static constexpr int kCols = (kAccCols + kSfCols <= 32) ? 32
                                : (kAccCols + kSfCols <= 64) ? 64
                                : (kAccCols + kSfCols <= 128) ? 128
                                : (kAccCols + kSfCols <= 256) ? 256 : 512;
-  // Transaction bytes of one K tile; the weights count as their packed
-  // 4-bit source (8 KB per 128x128 box), not the 16 KB written to smem.
-  static constexpr int kTxTile = kA / 2 + kActTerms * kB + 512 + kSfb * 512;
+  static constexpr int kTxTile = kATx + kBt + 512 + kSfb * 512;
   static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 256 /*barriers*/ +
                                (int)sizeof(TileTables);
+  static_assert(kBTerm % 512 == 0 && kA % 1024 == 0, "swizzle atoms must stay aligned");
+  static_assert(kAccCols + kSfCols <= 512, "TMEM columns");
 };
 
-template <int BN, bool STACK, int KS>
+template <int BN, bool FP4, int KS>
 __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ MmaLaunch a) {
-  using S = MmaShape<BN, STACK, KS>;
+  using S = MmaShape<BN, FP4, KS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kStages * S::kStage);
@@ -604,30 +668,24 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
-    // Weight boxes are also prefetched into L2 kPrefetch stages ahead of the
-    // shared-memory ring, so more HBM traffic is in flight than the ring holds.
-    const int kPrefetch = a.prefetch;
+    // Tile-major storage makes the kt_n weight boxes (and scale atoms) of one
+    // (expert, row tile) a single contiguous run, so one bulk L2 prefetch per
+    // tile, issued a.prefetch tiles ahead, has the next tiles' weights on
+    // their way from HBM while the ring streams the current one.  The ring's
+    // TMA loads then mostly hit L2, whose shorter latency lets the bytes the
+    // ring holds keep HBM busy.
     int s = 0;
     uint32_t phase = 0;
     const int kt_n = a.ktiles;
-    auto box_row = [&](const TileInfo &ti, int kt) { return ((ti.e * a.mtiles + ti.mt) * kt_n + kt) * kMmaM; };
-    int pf_tile = -1, pf_kt = 0;   // next (local tile, k-tile) to prefetch
-    TileInfo pf_info{};
-    auto prefetch_upto = [&](int local_limit, int kt_limit) {
-      // prefetch every (local tile, kt) < (local_limit, kt_limit) in order
-      while (pf_tile < local_limit || (pf_tile == local_limit && pf_kt < kt_limit)) {
-        if (pf_tile < 0 || pf_kt == kt_n) {
-          ++pf_tile;
-          pf_kt = 0;
-          const int tile = blockIdx.x + pf_tile * gridDim.x;
-          if (tile >= n_tiles) { pf_tile = 1 << 29; return; }
-          pf_info = tile_info<BN>(tt, tile, n_active, a.mtiles);
-          continue;
-        }
-        tma_prefetch_2d(&a.tmap_a1, 0, box_row(pf_info, pf_kt));
-        ++pf_kt;
-      }
+    const uint32_t w_tile_bytes = (uint32_t)kt_n * kMmaM * (kMmaKT / 2);
+    auto prefetch_tile = [&](int tile) {
+      if (tile >= n_tiles) return;
+      const TileInfo ti = tile_info<BN>(tt, tile, n_active, a.mtiles);
+      const size_t run = (size_t)ti.e * a.mtiles + ti.mt;
+      bulk_prefetch_l2(a.w + run * w_tile_bytes, w_tile_bytes);
+      bulk_prefetch_l2(a.sfa + run * kt_n * 512, (uint32_t)kt_n * 512);
     };
+    for (int d = 1; d < a.prefetch; ++d) prefetch_tile(blockIdx.x + d * gridDim.x);
     int local = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
@@ -635,11 +693,8 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
       const uint8_t *sfb = a.sfb + ((size_t)(t.rowb / kMmaM) * a.ktiles) * (S::kSfb * 512);
       const int box0 = (t.e * a.mtiles + t.mt) * kt_n;
       bool ok = true;
+      if (a.prefetch > 0) prefetch_tile(tile + a.prefetch * gridDim.x);
       for (int kt = 0; kt < a.ktiles; kt += KS) {
-        if (kPrefetch > 0) {
-          const int ahead = kt + kPrefetch;  // prefetch target, in (local, kt) order
-          prefetch_upto(local + ahead / kt_n, ahead % kt_n);
-        }
         if (!mbar_wait(&empty[s], phase ^ 1u, a.err, 1)) {
           ok = false;
           break;
@@ -647,14 +702,21 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
         const int nk = min(KS, a.ktiles - kt);
         uint8_t *st = smem + s * S::kStage;
         mbar_expect_tx(&full[s], nk * S::kTxTile);
-        if (nk == KS && KS > 1) {
-          tma_load_3d(&a.tmap_a, st, &full[s], 0, 0, box0 + kt);
-          if (STACK) tma_load_3d(&a.tmap_b, st + S::kOffB, &full[s], 0, t.rowb, kt);
-          else tma_load_4d(&a.tmap_b, st + S::kOffB, &full[s], 0, t.rowb, 0, kt);
-        } else {
-          tma_load_2d(&a.tmap_a1, st, &full[s], 0, (box0 + kt) * kMmaM);
-          if (STACK) tma_load_3d(&a.tmap_b1, st + S::kOffB, &full[s], 0, t.rowb, kt);
-          else tma_load_4d(&a.tmap_b1, st + S::kOffB, &full[s], 0, t.rowb, 0, kt);
+        // one operation per operand for the whole stage; single K tiles with
+        // the one-box maps at the end of an odd K
+        const bool whole = nk == KS;
+        const CUtensorMap *ma = whole ? &a.tmap_a : &a.tmap_a1;
+        const CUtensorMap *mb = whole ? &a.tmap_b : &a.tmap_b1;
+        for (int j = 0; j < (whole ? 1 : nk); ++j) {
+          uint8_t *aj = st + j * S::kA;
+          uint8_t *bj = st + S::kOffB + j * S::kBt;
+          if (FP4) {
+            tma_load_3d(ma, aj, &full[s], 0, 0, box0 + kt + j);
+            tma_load_3d(mb, bj, &full[s], 0, t.rowb, kt + j);
+          } else {
+            tma_load_2d(ma, aj, &full[s], 0, (box0 + kt + j) * kMmaM);
+            tma_load_4d(mb, bj, &full[s], 0, t.rowb, 0, kt + j);
+          }
         }
         bulk_load(st + S::kOffSfa, sfa + (size_t)kt * 512, nk * 512, &full[s]);
         bulk_load(st + S::kOffSfb, sfb + (size_t)kt * S::kSfb * 512, nk * S::kSfb * 512, &full[s]);
@@ -676,14 +738,17 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
     const uint32_t sfa_t = tmem + 2 * S::kN;
     const uint32_t sfb_t = sfa_t + 4;
     const uint32_t base = smem_u32(smem);
-    const uint64_t a_desc0 = smem_desc(base, 1024, 2);
-    const uint64_t b_desc0 = smem_desc(base + S::kOffB, 1024, 2);
+    const uint64_t a_desc0 = smem_desc(base, S::kSbo, S::kLayout);
+    const uint64_t b_desc0 = smem_desc(base + S::kOffB, S::kSbo, S::kLayout);
     const uint64_t sfa_desc0 = smem_desc(base + S::kOffSfa, 128, 0);
     const uint64_t sfb_desc0 = smem_desc(base + S::kOffSfb, 128, 0);
-    constexpr uint64_t kStage16 = S::kStage >> 4, kA16 = S::kA >> 4, kB16 = S::kB >> 4;
-    uint32_t idesc[4];
+    constexpr uint64_t kStage16 = S::kStage >> 4, kA16 = S::kA >> 4, kBt16 = S::kBt >> 4, kBTerm16 = S::kBTerm >> 4;
+    // K step ks reads 32 bytes further along each row; FP4 steps use scale
+    // bytes 2ks and 2ks+1 of the atom (two 32-blocks), FP8 steps byte ks.
+    uint32_t idesc[S::kKSteps];
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) idesc[ks] = idesc_mxf8f6f4(S::kN, ks, ks);
+    for (int ks = 0; ks < S::kKSteps; ++ks)
+      idesc[ks] = FP4 ? idesc_mxf4(S::kN, 2 * ks, 2 * ks) : idesc_mxf8f6f4(S::kN, ks, ks);
     bool ok = true;
     for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -708,13 +773,18 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
             for (int term = 0; term < S::kSfb; ++term)
               tc_cp_sf(sfb_t + 4 * term, sfb_desc0 + so + 32 * (j * S::kSfb + term));
             const uint64_t ad = a_desc0 + so + (uint64_t)j * kA16;
-            const uint64_t bd = b_desc0 + so + (uint64_t)j * kActTerms * kB16;
+            const uint64_t bd = b_desc0 + so + (uint64_t)j * kBt16;
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < S::kKSteps; ++ks) {
+              const uint32_t id = FP4 ? 2u * ks : (uint32_t)ks;
 #pragma unroll
-              for (int term = 0; term < (STACK ? 1 : kActTerms); ++term) {
-                tc_mma(d_tmem, ad + 2 * ks, bd + term * kB16 + 2 * ks, idesc[ks], sfa_t | ((uint32_t)ks << 30),
-                       (sfb_t + 4 * term) | ((uint32_t)ks << 30), acc);
+              for (int term = 0; term < (FP4 ? 1 : kActTerms); ++term) {
+                if (FP4)
+                  tc_mma_fp4(d_tmem, ad + 2 * ks, bd + 2 * ks, idesc[ks], sfa_t | (id << 30),
+                             sfb_t | (id << 30), acc);
+                else
+                  tc_mma(d_tmem, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_t | (id << 30),
+                         (sfb_t + 4 * term) | (id << 30), acc);
                 acc = 1u;
               }
             }
@@ -747,12 +817,14 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
         float v[16];
         const uint32_t col = tmem + (uint32_t)(buf * S::kN + c0) + ((uint32_t)(quad * 32) << 16);
         tc_ld16(col, v);
-        if (STACK) {  // the three term partial sums sit BN columns apart
-          float v1[16], v2[16];
-          tc_ld16(col + BN, v1);
-          tc_ld16(col + 2 * BN, v2);
+        if (FP4) {  // the term partial sums sit BN columns apart
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = (v[j] + v1[j]) + v2[j];
+          for (int term = 1; term < kFp4Terms; ++term) {
+            float w[16];
+            tc_ld16(col + term * BN, w);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += w[j];
+          }
         }
         if (a.mode == 0) {
           const int d = r >> 1;
@@ -785,19 +857,19 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
                  : "memory");
 }
 
-template <int BN, bool STACK, int KS>
+template <int BN, bool FP4, int KS>
 cudaError_t launch_gemm_bn(const MmaLaunch &a, int sm_count, cudaStream_t s) {
-  using Sh = MmaShape<BN, STACK, KS>;
+  using Sh = MmaShape<BN, FP4, KS>;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_mma_gemm<BN, STACK, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_mma_gemm<BN, FP4, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Sh::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
   int grid = a.max_tiles < sm_count ? a.max_tiles : sm_count;
   if (grid < 1) grid = 1;
-  k_mma_gemm<BN, STACK, KS><<<grid, 192, Sh::kSmem, s>>>(a);
+  k_mma_gemm<BN, FP4, KS><<<grid, 192, Sh::kSmem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -846,14 +918,17 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
   const int threads = 256;
   const int64_t warps = (int64_t)S_max * (kp / kMmaKT);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  k_quantize_act<<<(unsigned)blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off,
-                                                      pos_expert, meta, S_max, K, kp, rb, bn, mma_stacked(bn) ? 1 : 0,
-                                                      q, sf);
+  if (mma_fp4(bn))
+    k_quantize_act<true><<<(unsigned)blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets,
+                                                              pad_off, pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
+  else
+    k_quantize_act<false><<<(unsigned)blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets,
+                                                               pad_off, pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
   return cudaGetLastError();
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {
-  if (bn <= 16) return launch_gemm_bn<16, true, kMmaStageTilesSmall>(a, sm_count, s);
+  if (mma_fp4(bn)) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
   return launch_gemm_bn<128, false, 1>(a, sm_count, s);
 }
 

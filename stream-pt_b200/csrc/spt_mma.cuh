@@ -1,12 +1,18 @@
 // spt_mma.cuh -- tcgen05 block-scaled grouped GEMM for the MoE experts.
 //
 // D[rows, tokens] = W[rows, K] x X[tokens, K]^T per (expert, 128-row tile,
-// token tile) with kind::mxf8f6f4: A = the GGUF MXFP4 weights (e2m1 with the
-// GGUF E8M0 block scales, fed to the tensor core unchanged), B = activations
-// as three MXFP8 terms x = q1*s1 + q2*s2 + q3*s3 (e4m3 with per-32 E8M0
-// scales), accumulated in fp32 in TMEM.  Three terms keep the activation
-// error near 2^-12 of each 32-block's maximum, so block outputs stay well
-// inside the 1e-3 relative tolerance; one FP4 x FP8 product term would not.
+// token tile), accumulated in fp32 in TMEM.  A = the GGUF MXFP4 weights (e2m1
+// with the GGUF E8M0 block scales, fed to the tensor core unchanged); B = the
+// activations written as a sum of block-scaled terms (see k_quantize_act), so
+// that block outputs stay well inside the 1e-3 relative tolerance:
+//   token tiles of <= 16 (decode):  kind::mxf4, kFp4Terms e2m1 terms stacked
+//     along N (N = kFp4Terms*16), both operands packed 4-bit in shared memory;
+//   128-token tiles (prefill):      kind::mxf8f6f4, kActTerms e4m3 terms, one
+//     N = 128 MMA per term, the weights unpacked to one byte per element by
+//     the TMA (16U4_ALIGN16B).
+// Decode-sized tiles are bound by the weight stream: packed 4-bit weights need
+// half the shared memory per K tile, so the ring keeps twice as many bytes in
+// flight from HBM.
 //
 // HBM layout of the MMA arena (one layer):
 //   gu_w   uint8 [E][2D/128][KP/128][128][64]  tile-major packed e2m1: one
@@ -20,12 +26,12 @@
 //                                scale-factor atom: row m of the tile, block
 //                                kb of the K tile at (m%32)*16 + (m/32)*4 + kb
 //   dn_w   uint8 [E][ceil(H/128)][KPd/128][128][64], dn_sf [E][ceil(H/128)][KPd/128][512]
-// Activations (per call), e4m3 in K-tile-major order plus scale atoms.  Every
-// BN-token tile owns one 128-row slot starting at pad_off[e] + (j/BN)*128 for
-// token j of expert e, so its scale atom starts at slot row 0.  BN = 16:
-// the three terms stack inside the slot (term t, token j at slot row
-// t*16 + j%16): q [KP/128][RB][128], sf [RB/128][KP/128][512].  BN = 128:
-// q [KP/128][3][RB][128], sf [RB/128][KP/128][3][512].
+// Activations (per call), K-tile-major plus scale atoms.  Every BN-token tile
+// owns one 128-row slot starting at pad_off[e] + (j/BN)*128 for token j of
+// expert e, so its scale atom starts at slot row 0.
+//   FP4: term t, token j at slot row t*16 + j%16; q [KP/128][RB][64],
+//        sf [RB/128][KP/128][512].
+//   FP8: q [KP/128][kActTerms][RB][128], sf [RB/128][KP/128][kActTerms][512].
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -35,7 +41,9 @@ namespace spt {
 
 constexpr int kMmaM = 128;       // rows per tile (tcgen05 M for cta_group::1)
 constexpr int kMmaKT = 128;      // K elements per pipeline stage (one TMA box)
-constexpr int kActTerms = 3;     // MXFP8 terms of the activations
+constexpr int kActTerms = 3;     // e4m3 terms of the activations (128-token tiles)
+constexpr int kFp4Terms = 6;     // e2m1 terms of the activations (tiles of <= 16 tokens)
+constexpr int kMmaStageTilesFp4 = 2;  // K tiles per pipeline stage, FP4 mode
 
 struct MmaMatrix {
   uint8_t *w = nullptr;      // packed e2m1 rows
@@ -45,8 +53,9 @@ struct MmaMatrix {
   int kp = 0;                // K padded to 128
   int mtiles = 0;            // ceil(rows/128)
   int64_t experts = 0;
-  alignas(64) CUtensorMap tmap;   // 2D [128 elements, boxes*128 rows] 16U4_ALIGN16B, box 128x128, SW128
-  alignas(64) CUtensorMap tmap2;  // 3D [128 elements, 128 rows, boxes], box 128x128x2 (two K tiles)
+  alignas(64) CUtensorMap tmap;    // 2D [128 elements, boxes*128 rows] 16U4_ALIGN16B, box 128x128, SW128 (unpacked)
+  alignas(64) CUtensorMap tmap_p;  // 3D [64 B, 128 rows, boxes] UINT8, box 64x128xkMmaStageTilesFp4, SW64 (packed)
+  alignas(64) CUtensorMap tmap_p1; // same, one box
 };
 
 // Per-call operands of one grouped GEMM launch.  Every copy operation costs
@@ -60,6 +69,7 @@ struct MmaLaunch {
   alignas(64) CUtensorMap tmap_b;   // activations, ks K tiles x all terms
   alignas(64) CUtensorMap tmap_b1;  // activations, 1 K tile x all terms
   int ks = 1;                       // K tiles per pipeline stage
+  const uint8_t *w = nullptr;        // packed weights (tile-major), for L2 prefetch
   const uint8_t *sfa = nullptr;
   const uint8_t *sfb = nullptr;
   int rows = 0, kp = 0, mtiles = 0, ktiles = 0;
@@ -78,26 +88,33 @@ struct MmaLaunch {
   int y_stride = 0;                  // D (mode 0) or H (mode 1)
   int out_rows = 0;                  // D (mode 0) or H (mode 1)
   int32_t *err = nullptr;            // set nonzero when a bounded wait gives up
-  int prefetch = 0;                  // weight boxes prefetched into L2 ahead of the ring (0: off;
-                                     // measured slower on B200 at every distance tried)
+  int prefetch = 0;                  // whole weight tiles prefetched into L2 ahead (0: off)
 };
 
-// Token tiles of at most 16 tokens stack the three activation terms along N
-// and move two K tiles per pipeline stage; 128-token tiles move one.
-inline bool mma_stacked(int bn) { return bn <= 16; }
-constexpr int kMmaStageTilesSmall = 2;
-inline int mma_stage_tiles(int bn) { return bn <= 16 ? kMmaStageTilesSmall : 1; }
-// Activation rows of one TMA box: 3*bn when stacked, else bn.
-inline int mma_box_rows(int bn) { return mma_stacked(bn) ? kActTerms * bn : bn; }
+// Token tiles of at most 16 tokens run the FP4 mode (kFp4Terms e2m1 terms
+// stacked along N, kMmaStageTilesFp4 K tiles per stage); 128-token tiles run
+// the FP8 mode (one K tile per stage).
+inline bool mma_fp4(int bn) { return bn <= 16; }
+inline int mma_stage_tiles(int bn) { return mma_fp4(bn) ? kMmaStageTilesFp4 : 1; }
+// Activation rows of one TMA box.
+inline int mma_box_rows(int bn) { return mma_fp4(bn) ? kFp4Terms * bn : bn; }
+// Bytes of the activation buffers for rb rows per term and kp padded K.
+inline size_t mma_act_bytes(int bn, int rb, int kp) {
+  return mma_fp4(bn) ? (size_t)rb * (kp / 2) : (size_t)kActTerms * rb * kp;
+}
+inline size_t mma_act_sf_bytes(int bn, int rb, int kp) {
+  return (size_t)(mma_fp4(bn) ? 1 : kActTerms) * (rb / kMmaM) * (kp / kMmaKT) * 512;
+}
 
 size_t mma_w_bytes(int64_t experts, int rows, int k);
 size_t mma_sf_bytes(int64_t experts, int rows, int k);
 
 // Encode the TMA map of a packed e2m1 matrix (returns false on failure).
 bool mma_encode_weights(MmaMatrix *m);
-// TMA map of the e4m3 activations stored K-tile-major [kt][terms][rb][128 B]
-// (terms = 1 when stacked): box 128 B x box_rows x terms x ktiles.
-bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int terms, int box_rows, int ktiles);
+// TMA map of the activations in the layout of mode mma_fp4(bn): FP4
+// [kt][rb][64 B] with box 64 B x 6*bn rows x ktiles (SW64); FP8
+// [kt][kActTerms][rb][128 B] with box 128 B x bn rows x kActTerms x ktiles (SW128).
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, int ktiles);
 
 cudaError_t launch_repack_mma_gu(const uint8_t *gate_gguf, const uint8_t *up_gguf, int64_t experts,
                                  int D, int K, MmaMatrix *m, cudaStream_t s);
