@@ -67,53 +67,123 @@ def load_traffic(config):
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (every 200 ms)."""
+    """SM clock and throttle reasons sampled during the timed region.
+
+    NVML is polled every 2 ms from a thread (the timed regions here last from
+    milliseconds to seconds); without pynvml it falls back to nvidia-smi
+    every 200 ms.  Reads only: no GPU setting is touched.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # nvmlClocksEventReason bits: sw_power_cap 0x4, hw_slowdown 0x8,
+    # sw_thermal_slowdown 0x20, hw_thermal_slowdown 0x40
+    BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+            ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.rows = []
+    def __init__(self, cuda_index):
+        self.cuda_index = cuda_index
+        self.rows = []       # (sm_mhz, max_mhz, reasons set)
         self.proc = None
+        self.stop = threading.Event()
+        self.t = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.cuda_index)
+        uuid = getattr(props, "uuid", None)
+        if uuid is not None:
+            try:
+                return pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(uuid))
+            except Exception:
+                pass
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            try:
+                busid = "%08X:%02X:%02X.0" % (getattr(props, "pci_domain_id", 0), bus,
+                                               getattr(props, "pci_device_id", 0))
+                return pynvml.nvmlDeviceGetHandleByPciBusId(busid)
+            except Exception:
+                pass
+        return pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def _poll_nvml(self, h):
+        import pynvml
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        while True:
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(mx), {n for n, b in self.BITS if bits & b}))
+            except Exception:
+                pass
+            if self.stop.wait(0.002):
+                break
 
     def __enter__(self):
         try:
+            h = self._nvml_handle()
+            self.t = threading.Thread(target=self._poll_nvml, args=(h,), daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.t = None
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={self.cuda_index}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t = threading.Thread(target=self._read_smi, daemon=True)
             self.t.start()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
+        names = [n for n, _ in self.BITS]
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                self.rows.append((float(parts[1]), float(parts[2]) if parts[2].replace(".", "").isdigit() else None,
+                                  {names[i] for i in range(4) if parts[5 + i].lower() == "active"}))
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.t:
+            self.t.join(timeout=5)
 
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+        sm = [r[0] for r in self.rows]
+        mx = [r[1] for r in self.rows if r[1]]
+        reasons = sorted(set().union(*(r[2] for r in self.rows)))
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def mma_fp4(T):
+    """Token tiles of <= 16 (T*top_k <= 8*experts) run the kind::mxf4 GEMM."""
+    return T * K <= 8 * E
+
+
+def mma_kind(T):
+    return "kind::mxf4" if mma_fp4(T) else "kind::mxf8f6f4"
+
+
+def mma_dtype(T):
+    if mma_fp4(T):
+        return "mxfp4 weights x 6-term e2m1 activations -> f32 (tcgen05 kind::mxf4)"
+    return "mxfp4 weights x 3-term e4m3 activations -> f32 (tcgen05 kind::mxf8f6f4)"
 
 
 def dist_info():
@@ -282,7 +352,7 @@ def run_ours(args):
         "metric": "moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": ("mxfp4 x 3-term mxfp8 -> f32 (tcgen05)" if args.path == "mma" else "f32 (mxfp4 weights)"),
+        "dtype": mma_dtype(T) if args.path == "mma" else "f32 (mxfp4 weights)",
         "data": "synthetic",
         "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H,
                    "expert_path": args.path,
@@ -292,7 +362,7 @@ def run_ours(args):
                    "active_experts": n_active},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": load_traffic(args.config),
-                     "kernel": ("k_mma_gemm gate/up (tcgen05 mxf8f6f4, fused SwiGLU)" if args.path == "mma"
+                     "kernel": (f"k_mma_gemm gate/up (tcgen05 {mma_kind(T)}, fused SwiGLU)" if args.path == "mma"
                                 else "k_gemv<gate_up> (fused gate+up MXFP4 GEMV + SwiGLU)"),
                      "algorithmic_bytes": gu_bytes, "avg_ms": gu_ms, "peak_source": peak_src,
                      "down_kernel": {"achieved": dn_bytes / (dn_ms / 1e3) / 1e9, "avg_ms": dn_ms,

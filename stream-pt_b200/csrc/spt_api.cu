@@ -71,6 +71,13 @@ struct spt_context {
   int path = SPT_PATH_AUTO;
   int kernels_last = 0;
   DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
+  int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
+  // activation tensor maps of the last call (re-encoded when the buffers or shape change)
+  struct ActMaps {
+    const void *q = nullptr;
+    int kp = 0, rb = 0, bn = 0, ks = 0;
+    CUtensorMap m, m1;
+  } act_maps[2];
 };
 
 struct spt_arena {
@@ -421,6 +428,25 @@ int pick_mt(int64_t T, int64_t K, int64_t E) {
   return 8;
 }
 
+// Activation tensor maps for GEMM `which` (0 gate/up, 1 down), encoded only
+// when the buffer or the shape differs from the previous call.
+bool act_maps(spt_context *ctx, int which, uint8_t *q, int kp, int rb, int bn, int ks, CUtensorMap *m,
+              CUtensorMap *m1) {
+  auto &c = ctx->act_maps[which];
+  if (c.q != q || c.kp != kp || c.rb != rb || c.bn != bn || c.ks != ks) {
+    c.q = nullptr;
+    if (!mma_encode_acts(&c.m, q, kp, rb, bn, ks) || !mma_encode_acts(&c.m1, q, kp, rb, bn, 1)) return false;
+    c.q = q;
+    c.kp = kp;
+    c.rb = rb;
+    c.bn = bn;
+    c.ks = ks;
+  }
+  *m = c.m;
+  *m1 = c.m1;
+  return true;
+}
+
 int pick_bn(int64_t T, int64_t K, int64_t E) { return (T * K) <= 8 * E ? 16 : 128; }
 
 // Expert GEMMs on the tensor cores (after router/select/dispatch):
@@ -438,10 +464,6 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
     SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
     SPT_CUDA(ctx, cudaMemset(ctx->dev_err.p, 0, sizeof(int32_t)));
   }
-  SPT_CUDA(ctx, ctx->pad_off.ensure(sizeof(int32_t) * E));
-  SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
-  SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
-  SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
   SPT_CUDA(ctx, ctx->qx.ensure(mma_act_bytes(bn, rb, kph)));
   SPT_CUDA(ctx, ctx->sfx.ensure(mma_act_sf_bytes(bn, rb, kph)));
   SPT_CUDA(ctx, ctx->qa.ensure(mma_act_bytes(bn, rb, kpd)));
@@ -449,9 +471,8 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const bool fp4 = mma_fp4(bn);
   const int ks = mma_stage_tiles(bn);
   const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
-  SPT_CUDA(ctx, launch_mma_plan(ctx->offsets.as<int32_t>(), ctx->act_list.as<int32_t>(), ctx->meta.as<int32_t>(),
-                                E, bn, mt_gu, mt_dn, ctx->pad_off.as<int32_t>(), ctx->tile_gu.as<int32_t>(),
-                                ctx->tile_dn.as<int32_t>(), ctx->pos_expert.as<int32_t>(), s));
+  // pad_off, tile_gu, tile_dn and pos_expert come from the dispatch kernel
+
   SPT_CUDA(ctx, launch_quantize_act(x, H, ctx->perm.as<int32_t>(), K, true, ctx->offsets.as<int32_t>(),
                                     ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
                                     ctx->meta.as<int32_t>(), (int)S, H, kph, rb, bn, ctx->qx.as<uint8_t>(),
@@ -460,8 +481,7 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.ks = ks;
   g.tmap_a = fp4 ? L.gu_mma.tmap_p : L.gu_mma.tmap;
   g.tmap_a1 = fp4 ? L.gu_mma.tmap_p1 : L.gu_mma.tmap;
-  if (!mma_encode_acts(&g.tmap_b, ctx->qx.as<uint8_t>(), kph, rb, bn, ks) ||
-      !mma_encode_acts(&g.tmap_b1, ctx->qx.as<uint8_t>(), kph, rb, bn, 1))
+  if (!act_maps(ctx, 0, ctx->qx.as<uint8_t>(), kph, rb, bn, ks, &g.tmap_b, &g.tmap_b1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
   g.w = L.gu_mma.w;
   g.sfa = L.gu_mma.sf;
@@ -495,8 +515,7 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   MmaLaunch dn = g;
   dn.tmap_a = fp4 ? L.dn_mma.tmap_p : L.dn_mma.tmap;
   dn.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
-  if (!mma_encode_acts(&dn.tmap_b, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks) ||
-      !mma_encode_acts(&dn.tmap_b1, ctx->qa.as<uint8_t>(), kpd, rb, bn, 1))
+  if (!act_maps(ctx, 1, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks, &dn.tmap_b, &dn.tmap_b1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
   dn.w = L.dn_mma.w;
   dn.sfa = L.dn_mma.sf;
@@ -515,7 +534,7 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   dn.out_rows = H;
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[6], s));
   SPT_CUDA(ctx, launch_mma_gemm(dn, bn, ctx->sm_count, s));
-  ctx->kernels_last = 9;
+  ctx->kernels_last = 8;  // router, select, dispatch, quantize, gate/up, quantize, down, combine
   return SPT_OK;
 }
 
@@ -551,11 +570,6 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
   SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, ctx->sel_idx.as<int32_t>(),
                               ctx->sel_w.as<float>(), s));
   SPT_MARK(2);
-  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)(T * K), E,
-                                ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
-                                ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
-                                ctx->meta.as<int32_t>(), s));
-  SPT_MARK(3);
   const int max_active = (int)std::min<int64_t>(E, T * K);
   const bool use_mma = L.has_mma && (ctx->path == SPT_PATH_MMA || (ctx->path == SPT_PATH_AUTO)) &&
                        !(ctx->path == SPT_PATH_EXACT);
@@ -563,6 +577,26 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_MMA");
   if (!use_mma && !L.has_g8)
     return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_GEMV");
+  DispatchPlan plan;  // tensor-core tile layout, made by the dispatch kernel
+  if (use_mma) {
+    const int64_t S = T * K;
+    SPT_CUDA(ctx, ctx->pad_off.ensure(sizeof(int32_t) * E));
+    SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
+    SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
+    SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
+    plan.bn = pick_bn(T, K, E);
+    plan.mt_gu = L.gu_mma.mtiles;
+    plan.mt_dn = L.dn_mma.mtiles;
+    plan.pad_off = ctx->pad_off.as<int32_t>();
+    plan.tile_gu = ctx->tile_gu.as<int32_t>();
+    plan.tile_dn = ctx->tile_dn.as<int32_t>();
+    plan.pos_expert = ctx->pos_expert.as<int32_t>();
+  }
+  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)(T * K), E,
+                                ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
+                                ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
+                                ctx->meta.as<int32_t>(), s, use_mma ? &plan : nullptr));
+  SPT_MARK(3);
   if (use_mma) {
     if ((st = forward_mma(ctx, L, c, x, T, s))) return st;
   } else {
@@ -648,8 +682,22 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
   if ((st = forward_device(ctx, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch)))
     return st;
   SPT_CUDA(ctx, cudaMemcpyAsync(out, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  // The GEMM's error flag rides on the same stream, so one synchronisation
+  // covers the output and the flag.
+  const bool flag = ctx->dev_err.p != nullptr;
+  if (flag) {
+    if (!ctx->err_host) SPT_CUDA(ctx, cudaHostAlloc((void **)&ctx->err_host, sizeof(int32_t), cudaHostAllocDefault));
+    SPT_CUDA(ctx, cudaMemcpyAsync(ctx->err_host, ctx->dev_err.p, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                  ctx->stream));
+  }
   SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-  if ((st = check_device_error(ctx))) return st;
+  if (flag && *ctx->err_host != 0) {
+    const int32_t e = *ctx->err_host;
+    *ctx->err_host = 0;
+    SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
+    SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return fail(ctx, SPT_ERR_TIMEOUT, "tensor-core GEMM: bounded wait %d gave up", e);
+  }
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
   return SPT_OK;
 }
@@ -731,6 +779,7 @@ void spt_context_destroy(spt_context *ctx) {
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   }
   delete ctx;

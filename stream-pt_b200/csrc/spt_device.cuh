@@ -25,4 +25,15 @@ __device__ __forceinline__ float swiglu_ref(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, d), __fadd_rn(u, 1.0f));
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may begin while its predecessor is still
+// running.  pdl_wait() returns once the predecessor grid has completed and
+// its memory operations are visible (immediately when there is no such
+// dependency); pdl_trigger() then lets the next kernel start launching.  Every
+// forward-path kernel calls both, in that order, before touching global
+// memory, so at most two consecutive kernels overlap and each reads only
+// completed results.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace spt

@@ -21,6 +21,8 @@
 // reference's AVX2 dot (forward/mxfp4_amd64.go:11-26): accumulator register
 // a_q of that kernel, lane by lane.
 #pragma once
+#include <atomic>
+#include <utility>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -84,9 +86,18 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
                           float *logits, int portable_lanes, cudaStream_t stream);
 cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
                           float *sel_w, cudaStream_t stream);
+// Tensor-core tile layout computed by the dispatch kernel (bn = 0: none).
+struct DispatchPlan {
+  int bn = 0, mt_gu = 0, mt_dn = 0;  // tokens per tile, row tiles per expert
+  int32_t *pad_off = nullptr;        // [E] first 128-row activation slot
+  int32_t *tile_gu = nullptr;        // [E+1] gate/up tile prefix over active experts
+  int32_t *tile_dn = nullptr;        // [E+1] down tile prefix
+  int32_t *pos_expert = nullptr;     // [S] expert of each dispatch position
+};
 cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
                             int32_t *offsets, int32_t *perm, int32_t *slot_pos,
-                            int32_t *act_list, int32_t *meta, cudaStream_t stream);
+                            int32_t *act_list, int32_t *meta, cudaStream_t stream,
+                            const DispatchPlan *plan = nullptr);
 
 // Addressing of the token rows a GEMV launch reads and writes, per
 // dispatch position p of an expert segment:
@@ -133,5 +144,41 @@ cudaError_t launch_repack_g8(const uint8_t *gguf, int64_t experts, int rows, int
 cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int rows, int blocks,
                             uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
                             cudaStream_t stream);
+
+// Raise a kernel's dynamic shared-memory limit once per device (the setting
+// belongs to the device context that is current when it is made).
+template <typename Kernel>
+cudaError_t opt_in_smem(Kernel kernel, int bytes) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> done[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[dev].store(bytes, std::memory_order_release);
+  return e;
+}
+
+// Launch a kernel that begins with pdl_wait(); pdl_launches_enabled() (the
+// SPT_PDL environment variable, default on) decides whether it may overlap
+// the tail of the previous kernel on the stream.
+bool pdl_launches_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_launches_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace spt

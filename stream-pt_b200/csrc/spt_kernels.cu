@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "spt_device.cuh"
 #include "spt_internal.cuh"
@@ -109,6 +110,8 @@ __global__ void __launch_bounds__(32) k_router(const float *__restrict__ W,
                                                const float *__restrict__ x,
                                                const float *__restrict__ bias, int T, int H,
                                                int E, float *__restrict__ logits) {
+  pdl_wait();
+  pdl_trigger();
   const int e0 = blockIdx.x * ME, t0 = blockIdx.y * MTR, lane = threadIdx.x;
   const int nt = min(MTR, T - t0);
   const int ne = min(ME, E - e0);
@@ -176,12 +179,94 @@ __global__ void __launch_bounds__(32) k_router(const float *__restrict__ W,
   }
 }
 
+// Router with its operands staged in shared memory.  The CTA copies EG rows
+// of W and TG rows of x with cp.async, all in flight together (one memory
+// latency instead of one per 64-element chunk), then each warp computes one
+// token against up to four experts from shared memory, in k_router's order:
+// lane l runs chains l and l+32, the 32-element tail feeds chains 0..31, and
+// the same shuffle tree reduces them (vector_amd64.go:28-56).
+constexpr int kRouterSmemMax = 200 * 1024;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W,
+                                                     const float *__restrict__ x,
+                                                     const float *__restrict__ bias, int T, int H,
+                                                     int E, int EG, int TG,
+                                                     float *__restrict__ logits) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float4 router_smem[];
+  float *ws = reinterpret_cast<float *>(router_smem);  // [EG][H]
+  float *xs = ws + (size_t)EG * H;                     // [TG][H]
+  const int e0 = blockIdx.x * EG, t0 = blockIdx.y * TG;
+  const int ne = min(EG, E - e0), nt = min(TG, T - t0);
+  const int q = H / 4;  // 16-byte pieces per row
+  for (int i = threadIdx.x; i < (ne + nt) * q; i += blockDim.x) {
+    const int r = i / q, c = i - r * q;
+    const float *src = r < ne ? W + (size_t)(e0 + r) * H : x + (size_t)(t0 + r - ne) * H;
+    float *dst = r < ne ? ws + (size_t)r * H : xs + (size_t)(r - ne) * H;
+    cp_async16(dst + 4 * c, src + 4 * c);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = (ne + 3) / 4;
+  for (int item = warp; item < nt * groups; item += blockDim.x >> 5) {
+    const int j = item / groups, mb = (item - j * groups) * 4;
+    const float *xr = xs + (size_t)j * H;
+    const float *wr[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) wr[m] = ws + (size_t)min(mb + m, ne - 1) * H;
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f}, b[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int full = H / 64;
+    int o = 0;
+#pragma unroll 3
+    for (int c = 0; c < full; ++c, o += 64) {
+      const float x0 = xr[o + lane], x1 = xr[o + 32 + lane];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        a[m] = fmaf(wr[m][o + lane], x0, a[m]);
+        b[m] = fmaf(wr[m][o + 32 + lane], x1, b[m]);
+      }
+    }
+    if (o < H) {
+      const float x0 = xr[o + lane];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) a[m] = fmaf(wr[m][o + lane], x0, a[m]);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float a8 = __shfl_sync(kFull, a[m], (lane + 8) & 31);
+      const float a16 = __shfl_sync(kFull, a[m], (lane + 16) & 31);
+      const float a24 = __shfl_sync(kFull, a[m], (lane + 24) & 31);
+      const float b8 = __shfl_sync(kFull, b[m], (lane + 8) & 31);
+      const float b16 = __shfl_sync(kFull, b[m], (lane + 16) & 31);
+      const float b24 = __shfl_sync(kFull, b[m], (lane + 24) & 31);
+      const float s0 = ((a[m] + a8) + a16) + a24;
+      const float s1 = ((b[m] + b8) + b16) + b24;
+      const float sv = s0 + s1;
+      const float p = sv + __shfl_sync(kFull, sv, (lane + 4) & 31);
+      const float qv = p + __shfl_sync(kFull, p, (lane + 1) & 31);
+      const float r = qv + __shfl_sync(kFull, qv, (lane + 2) & 31);
+      if (lane == 0 && mb + m < ne) logits[(size_t)(t0 + j) * E + e0 + mb + m] = r + (bias ? bias[e0 + mb + m] : 0.0f);
+    }
+  }
+}
+
 // Router for hidden % 32 != 0: the portable simd.Float32s order with `lanes`
 // lanes (forward/moe_batch.go:228-302): lane l accumulates elements l,
 // l+lanes, ... (zero-padded tail), then the lanes are summed in order.
 __global__ void k_router_portable(const float *__restrict__ W, const float *__restrict__ x,
                                   const float *__restrict__ bias, int T, int H, int E,
                                   int lanes, float *__restrict__ logits) {
+  pdl_wait();
+  pdl_trigger();
   const int e = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
   float acc = 0.0f;
   if (lane < lanes) {
@@ -197,28 +282,49 @@ __global__ void k_router_portable(const float *__restrict__ W, const float *__re
 }
 
 // ---------------------------------------------------------------------------
-// selectMoEBatch: one warp per token.  Each pass takes the first strictly
-// greater logit among experts not yet chosen (lowest index wins ties, NaN
-// and -Inf never win); no candidate gives (index = pass, value 0).
+// selectMoEBatch: one warp per token, the token's logits held in registers
+// (expert lane + 32i in slot i).  Each pass takes the first strictly greater
+// logit among experts not yet chosen (lowest index wins ties, NaN and -Inf
+// never win); no candidate gives (index = pass, value 0), and that index
+// counts as chosen for the later passes.
 __global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits, int T, int E,
                                                 int K, int32_t *__restrict__ sel_idx,
                                                 float *__restrict__ sel_w) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int kPer = kDispatchMaxExperts / 32;
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (t >= T) return;
   const float *lg = logits + (size_t)t * E;
+  const bool in_regs = E <= 32 * kPer;  // else every pass reads the logits again
+  float lv[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) lv[i] = (in_regs && lane + 32 * i < E) ? lg[lane + 32 * i] : 0.0f;
+  uint32_t taken = 0;  // bit i: expert lane + 32i already chosen
   int chosen[kSelectMaxK];
   float val[kSelectMaxK];
   for (int r = 0; r < K; ++r) {
     int best = -1;
     float v = -INFINITY;
-    for (int e = lane; e < E; e += 32) {
-      bool already = false;
-      for (int p = 0; p < r; ++p) already |= (chosen[p] == e);
-      const float l = lg[e];
-      if (!already && l > v) {
-        v = l;
-        best = e;
+    if (in_regs) {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && !((taken >> i) & 1u) && lv[i] > v) {
+          v = lv[i];
+          best = e;
+        }
+      }
+    } else {
+      for (int e = lane; e < E; e += 32) {
+        bool already = false;
+        for (int p = 0; p < r; ++p) already |= (chosen[p] == e);
+        const float l = lg[e];
+        if (!already && l > v) {
+          v = l;
+          best = e;
+        }
       }
     }
 #pragma unroll
@@ -234,6 +340,7 @@ __global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits
       best = r;
       v = 0.0f;
     }
+    if ((best & 31) == lane && best < 32 * kPer) taken |= 1u << (best >> 5);
     chosen[r] = best;
     val[r] = v;
   }
@@ -262,20 +369,39 @@ __global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits
 // Dispatch: the reference pushes slot t*k+r (weight > 0 or NaN) onto the
 // front of its expert's list (moe_batch.go:142-159), so walking a list visits
 // that expert's slots in descending slot order.  One CTA turns that into a
-// stable counting sort: histogram, exclusive scan over experts, then chunks
-// of 1024 slots taken in descending order, ranked within a warp by
+// stable counting sort: histogram, block scan over experts, then chunks of
+// 1024 slots taken in descending order, ranked within a warp by
 // __match_any_sync and across warps by a per-warp count table.
+//
+// With plan.bn > 0 the same CTA also lays out the tensor-core GEMM tiles:
+// each active expert's tokens form ceil(n/bn) token tiles, each owning one
+// 128-row activation slot (pad_off), and gate/up and down tile prefixes over
+// the active experts (tile_gu, tile_dn), plus pos -> expert (pos_expert).
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(kFull, v, d);
+    if (lane >= d) v += o;
+  }
+  return v;
+}
+
 __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ sel_idx,
                                                    const float *__restrict__ sel_w, int S, int E,
                                                    int32_t *__restrict__ offsets,
                                                    int32_t *__restrict__ perm,
                                                    int32_t *__restrict__ slot_pos,
                                                    int32_t *__restrict__ act_list,
-                                                   int32_t *__restrict__ meta) {
+                                                   int32_t *__restrict__ meta, DispatchPlan plan) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int kScanWarps = kDispatchMaxExperts / 32;
+  constexpr int kVals = 5;  // tokens, active flag, slot rows, gate/up tiles, down tiles
   __shared__ int s_cnt[kDispatchMaxExperts];
   __shared__ int s_off[kDispatchMaxExperts + 1];
   __shared__ int s_run[kDispatchMaxExperts];
   __shared__ int s_w[32 * kDispatchMaxExperts];
+  __shared__ int s_tot[kScanWarps][kVals];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int e = tid; e < E; e += blockDim.x) {
     s_cnt[e] = 0;
@@ -285,19 +411,65 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
   for (int s = tid; s < S; s += blockDim.x)
     if (!(sel_w[s] <= 0.0f)) atomicAdd(&s_cnt[sel_idx[s]], 1);
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0, na = 0;
-    for (int e = 0; e < E; ++e) {
-      s_off[e] = acc;
-      acc += s_cnt[e];
-      if (s_cnt[e] > 0) act_list[na++] = e;
-    }
-    s_off[E] = acc;
-    meta[0] = na;
-    meta[1] = acc;
+  int v[kVals] = {0, 0, 0, 0, 0}, inc[kVals] = {0, 0, 0, 0, 0};
+  if (tid < kDispatchMaxExperts) {
+    const int cnt = tid < E ? s_cnt[tid] : 0;
+    const int nt = plan.bn > 0 ? (cnt + plan.bn - 1) / plan.bn : 0;
+    v[0] = cnt;
+    v[1] = cnt > 0 ? 1 : 0;
+    v[2] = nt * 128;
+    v[3] = nt * plan.mt_gu;
+    v[4] = nt * plan.mt_dn;
+#pragma unroll
+    for (int k = 0; k < kVals; ++k) inc[k] = warp_incl_scan(v[k], lane);
+    if (lane == 31)
+#pragma unroll
+      for (int k = 0; k < kVals; ++k) s_tot[warp][k] = inc[k];
   }
   __syncthreads();
-  for (int e = tid; e <= E; e += blockDim.x) offsets[e] = s_off[e];
+  if (tid < kDispatchMaxExperts) {
+#pragma unroll
+    for (int k = 0; k < kVals; ++k)
+      for (int w = 0; w < warp; ++w) inc[k] += s_tot[w][k];
+    const int e = tid;
+    if (e < E) {
+      const int off = inc[0] - v[0];
+      s_off[e] = off;
+      offsets[e] = off;
+      if (v[1]) {
+        const int ai = inc[1] - 1;
+        act_list[ai] = e;
+        if (plan.bn > 0) {
+          plan.pad_off[e] = inc[2] - v[2];
+          plan.tile_gu[ai] = inc[3] - v[3];
+          plan.tile_dn[ai] = inc[4] - v[4];
+        }
+      }
+    }
+    if (e == kDispatchMaxExperts - 1) {  // inclusive totals over every expert
+      s_off[E] = inc[0];
+      offsets[E] = inc[0];
+      meta[0] = inc[1];
+      meta[1] = inc[0];
+      if (plan.bn > 0) {
+        plan.tile_gu[inc[1]] = inc[3];
+        plan.tile_dn[inc[1]] = inc[4];
+      }
+    }
+  }
+  __syncthreads();
+  const int total = s_off[E];
+  if (plan.bn > 0) {
+    for (int p = tid; p < total; p += blockDim.x) {
+      int lo = 0, hi = E - 1;  // largest expert with offsets[e] <= p
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) / 2;
+        if (s_off[mid] <= p) lo = mid;
+        else hi = mid - 1;
+      }
+      plan.pos_expert[p] = lo;
+    }
+  }
   for (int base = 0; base < S; base += blockDim.x) {
     const int s = S - 1 - (base + tid);
     const bool valid = s >= 0;
@@ -341,6 +513,8 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
 // writes SwiGLU(gate+bias, up+bias).
 template <int MT, bool GU>
 __global__ void __launch_bounds__(128) k_gemv(const GemvLaunch a) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, i = lane >> 2, q = lane & 3;
   const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -456,6 +630,8 @@ __global__ void __launch_bounds__(128) k_gemv(const GemvLaunch a) {
 __global__ void k_combine(const float *__restrict__ res, const float *__restrict__ sel_w,
                           const int32_t *__restrict__ slot_pos, int T, int K, int H,
                           float *__restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.y;
   const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || h >= H) return;
@@ -583,20 +759,41 @@ inline unsigned grid_for(int64_t n, int threads, int64_t cap = 148 * 32) {
 // ---------------------------------------------------------------------------
 // launchers
 
+bool pdl_launches_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("SPT_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   if (H % 32 != 0) {
-    k_router_portable<<<dim3(E, T), 32, 0, stream>>>(W, x, bias, T, H, E, portable_lanes,
-                                                     logits);
+    return launch_pdl(k_router_portable, dim3(E, T), dim3(32), 0, stream, W, x, bias, T, H, E, portable_lanes,
+                      logits);
     return cudaGetLastError();
   }
-  if (T <= 2) {
-    k_router<2, 1, 9><<<dim3(E, (T + 1) / 2), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
-  } else if (T <= 64) {
-    k_router<4, 2, 3><<<dim3((E + 1) / 2, (T + 3) / 4), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+  // Shared-memory staged router when the rows are 16-byte aligned and fit.
+  int TG = T < 8 ? T : 8;
+  const int n_tg = (T + TG - 1) / TG;
+  int EG = 1;
+  while (EG < 8 && (int64_t)(E / (EG * 2)) * n_tg >= 120) EG *= 2;
+  auto bytes = [&](int eg, int tg) { return (int64_t)(eg + tg) * H * (int64_t)sizeof(float); };
+  while (EG > 1 && bytes(EG, TG) > kRouterSmemMax) EG /= 2;
+  while (TG > 1 && bytes(EG, TG) > kRouterSmemMax) TG /= 2;
+  // Beyond 64 tokens every CTA would restage the same rows many times over;
+  // the register-blocked kernel reads them through L1/L2 instead.
+  const bool aligned = ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
+  if (T <= 64 && aligned && bytes(EG, TG) <= kRouterSmemMax) {
+    cudaError_t e = opt_in_smem(k_router_smem, kRouterSmemMax);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_router_smem, dim3((E + EG - 1) / EG, (T + TG - 1) / TG), dim3(256), (size_t)bytes(EG, TG),
+                      stream, W, x, bias, T, H, E, EG, TG, logits);
   } else {
-    k_router<8, 4, 1><<<dim3((E + 3) / 4, (T + 7) / 8), 32, 0, stream>>>(W, x, bias, T, H, E, logits);
+    return launch_pdl(k_router<8, 4, 1>, dim3((E + 3) / 4, (T + 7) / 8), dim3(32), 0, stream, W, x, bias, T, H, E,
+                      logits);
   }
   return cudaGetLastError();
 }
@@ -604,21 +801,22 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
 cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
                           float *sel_w, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
-  k_select<<<(T + 3) / 4, 128, 0, stream>>>(logits, T, E, K, sel_idx, sel_w);
-  return cudaGetLastError();
+  return launch_pdl(k_select, dim3((T + 3) / 4), dim3(128), 0, stream, logits, T, E, K, sel_idx, sel_w);
 }
 
 cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
                             int32_t *offsets, int32_t *perm, int32_t *slot_pos,
-                            int32_t *act_list, int32_t *meta, cudaStream_t stream) {
-  k_dispatch<<<1, 1024, 0, stream>>>(sel_idx, sel_w, S, E, offsets, perm, slot_pos, act_list,
-                                     meta);
-  return cudaGetLastError();
+                            int32_t *act_list, int32_t *meta, cudaStream_t stream,
+                            const DispatchPlan *plan) {
+  if (E > kDispatchMaxExperts) return cudaErrorInvalidValue;
+  return launch_pdl(k_dispatch, dim3(1), dim3(1024), 0, stream, sel_idx, sel_w, S, E, offsets, perm, slot_pos,
+                    act_list, meta, plan ? *plan : DispatchPlan{});
 }
 
 template <int MT, bool GU>
 static cudaError_t gemv_inst(const GemvLaunch &a, unsigned grid, cudaStream_t stream) {
-  k_gemv<MT, GU><<<grid, 128, 0, stream>>>(a);
+  cudaError_t e = launch_pdl(k_gemv<MT, GU>, dim3(grid), dim3(128), 0, stream, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -642,7 +840,8 @@ cudaError_t launch_combine(const float *res, const float *sel_w, const int32_t *
   if (T <= 0) return cudaSuccess;
   const int threads = 128;
   dim3 grid((H / 4 + threads - 1) / threads, T);
-  k_combine<<<grid, threads, 0, stream>>>(res, sel_w, slot_pos, T, K, H, out);
+  cudaError_t e = launch_pdl(k_combine, dim3(grid), dim3(threads), 0, stream, res, sel_w, slot_pos, T, K, H, out);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -22,6 +22,7 @@
 
 #include "spt_device.cuh"
 #include "spt_mma.cuh"
+#include "spt_internal.cuh"
 #include "spt_philox.h"
 
 namespace spt {
@@ -206,59 +207,6 @@ unsigned grid_of(int64_t n) {
 }
 
 // ---------------------------------------------------------------------------
-// Tile plan after dispatch (one CTA).
-__global__ void __launch_bounds__(1024) k_mma_plan(const int32_t *__restrict__ offsets,
-                                                   const int32_t *__restrict__ act_list,
-                                                   const int32_t *__restrict__ meta, int E, int bn, int mt_gu,
-                                                   int mt_dn, int32_t *pad_off, int32_t *tile_gu,
-                                                   int32_t *tile_dn, int32_t *pos_expert) {
-  // Exclusive scans over the active experts (at most 1024) of: 128-row slots
-  // per token tile, gate/up tiles and down tiles.
-  __shared__ int sc[3][1024];
-  const int na = meta[0], total = meta[1], tid = threadIdx.x;
-  int e = -1, nt = 0;
-  if (tid < na) {
-    e = act_list[tid];
-    nt = (offsets[e + 1] - offsets[e] + bn - 1) / bn;
-  }
-  sc[0][tid] = tid < na ? nt * kMmaM : 0;
-  sc[1][tid] = tid < na ? nt * mt_gu : 0;
-  sc[2][tid] = tid < na ? nt * mt_dn : 0;
-  __syncthreads();
-  for (int d = 1; d < 1024; d <<= 1) {  // inclusive Hillis-Steele scan
-    int v0 = 0, v1 = 0, v2 = 0;
-    if (tid >= d) {
-      v0 = sc[0][tid - d];
-      v1 = sc[1][tid - d];
-      v2 = sc[2][tid - d];
-    }
-    __syncthreads();
-    sc[0][tid] += v0;
-    sc[1][tid] += v1;
-    sc[2][tid] += v2;
-    __syncthreads();
-  }
-  if (tid < na) {
-    pad_off[e] = sc[0][tid] - nt * kMmaM;
-    tile_gu[tid] = sc[1][tid] - nt * mt_gu;
-    tile_dn[tid] = sc[2][tid] - nt * mt_dn;
-  }
-  if (tid == 0) {
-    tile_gu[na] = na > 0 ? sc[1][na - 1] : 0;
-    tile_dn[na] = na > 0 ? sc[2][na - 1] : 0;
-  }
-  for (int p = tid; p < total; p += blockDim.x) {
-    int lo = 0, hi = E - 1;  // largest expert with offsets[e] <= p
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) / 2;
-      if (offsets[mid] <= p) lo = mid;
-      else hi = mid - 1;
-    }
-    pos_expert[p] = lo;
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Activations -> block-scaled multi-term operands.  Each 32-element block is
 // written as a sum of terms q_t * 2^e_t, each term quantizing the residual
 // left by the previous ones; every residual is exact in fp32.  Term scale:
@@ -306,6 +254,8 @@ __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
                                const int32_t *__restrict__ pos_expert, const int32_t *__restrict__ meta,
                                int S_max, int K, int kp, int rb, int bn,
                                uint8_t *__restrict__ q, uint8_t *__restrict__ sf) {
+  pdl_wait();
+  pdl_trigger();
   // One warp per (dispatch position, 128-element K tile); 8 lanes per
   // 32-element block, 4 elements per lane.
   const int lane = threadIdx.x & 31, sub = lane & 7;
@@ -603,7 +553,7 @@ struct MmaShape {
   static constexpr int kStage = ((kOffSfb + KS * kSfb * 512) + 1023) / 1024 * 1024;
   static constexpr int kStages = (200 * 1024) / kStage > 16 ? 16 : (200 * 1024) / kStage;
   static constexpr int kAccCols = 2 * kN;           // double-buffered accumulator
-  static constexpr int kSfCols = 4 + 4 * kSfb;      // SFA + SFB atoms of one K tile
+  static constexpr int kSfCols = KS * (4 + 4 * kSfb);  // SFA + SFB atoms of every K tile of a stage
   static constexpr int kCols = (kAccCols + kSfCols <= 32) ? 32
                                : (kAccCols + kSfCols <= 64) ? 64
                                : (kAccCols + kSfCols <= 128) ? 128
@@ -628,19 +578,6 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   TileTables &tt = *reinterpret_cast<TileTables *>(smem + S::kStages * S::kStage + 256);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  {
-    const int na = a.meta[0];
-    for (int i = threadIdx.x; i < na && i < kMaxActive; i += blockDim.x) {
-      const int e = a.act_list[i];
-      tt.e[i] = e;
-      tt.p0[i] = a.offsets[e];
-      tt.n[i] = a.offsets[e + 1] - a.offsets[e];
-      tt.pad[i] = a.pad_off[e];
-      tt.tile_off[i] = a.tile_off[i];
-    }
-    if (threadIdx.x == 0) tt.tile_off[min(na, kMaxActive)] = a.tile_off[min(na, kMaxActive)];
-  }
-
   if (threadIdx.x == 0) {
     for (int i = 0; i < S::kStages; ++i) {
       mbar_init(&full[i], 1);
@@ -659,6 +596,23 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  // Barriers and TMEM above need nothing from the previous kernel; the tile
+  // tables below are the dispatch kernel's output.
+  pdl_wait();
+  pdl_trigger();
+  {
+    const int na = a.meta[0];
+    for (int i = threadIdx.x; i < na && i < kMaxActive; i += blockDim.x) {
+      const int e = a.act_list[i];
+      tt.e[i] = e;
+      tt.p0[i] = a.offsets[e];
+      tt.n[i] = a.offsets[e + 1] - a.offsets[e];
+      tt.pad[i] = a.pad_off[e];
+      tt.tile_off[i] = a.tile_off[i];
+    }
+    if (threadIdx.x == 0) tt.tile_off[min(na, kMaxActive)] = a.tile_off[min(na, kMaxActive)];
+  }
+
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -735,8 +689,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
     int s = 0;
     uint32_t phase = 0;
     int local = 0;
-    const uint32_t sfa_t = tmem + 2 * S::kN;
-    const uint32_t sfb_t = sfa_t + 4;
+    const uint32_t sfa_t = tmem + 2 * S::kN;  // scale-factor columns after the two accumulators
     const uint32_t base = smem_u32(smem);
     const uint64_t a_desc0 = smem_desc(base, S::kSbo, S::kLayout);
     const uint64_t b_desc0 = smem_desc(base + S::kOffB, S::kSbo, S::kLayout);
@@ -765,13 +718,23 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
         tc_fence_after();
         const int nk = min(KS, a.ktiles - kt);
         const uint64_t so = (uint64_t)s * kStage16;
+        // All scale-factor copies of the stage first, each K tile into its own
+        // TMEM columns, then the MMAs: the copies' latency overlaps instead
+        // of sitting between dependent MMAs.
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
           if (j < nk) {
-            tc_cp_sf(sfa_t, sfa_desc0 + so + 32 * j);
+            const uint32_t sfa_j = sfa_t + j * (4 + 4 * S::kSfb), sfb_j = sfa_j + 4;
+            tc_cp_sf(sfa_j, sfa_desc0 + so + 32 * j);
 #pragma unroll
             for (int term = 0; term < S::kSfb; ++term)
-              tc_cp_sf(sfb_t + 4 * term, sfb_desc0 + so + 32 * (j * S::kSfb + term));
+              tc_cp_sf(sfb_j + 4 * term, sfb_desc0 + so + 32 * (j * S::kSfb + term));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+          if (j < nk) {
+            const uint32_t sfa_j = sfa_t + j * (4 + 4 * S::kSfb), sfb_j = sfa_j + 4;
             const uint64_t ad = a_desc0 + so + (uint64_t)j * kA16;
             const uint64_t bd = b_desc0 + so + (uint64_t)j * kBt16;
 #pragma unroll
@@ -780,11 +743,11 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
 #pragma unroll
               for (int term = 0; term < (FP4 ? 1 : kActTerms); ++term) {
                 if (FP4)
-                  tc_mma_fp4(d_tmem, ad + 2 * ks, bd + 2 * ks, idesc[ks], sfa_t | (id << 30),
-                             sfb_t | (id << 30), acc);
+                  tc_mma_fp4(d_tmem, ad + 2 * ks, bd + 2 * ks, idesc[ks], sfa_j | (id << 30),
+                             sfb_j | (id << 30), acc);
                 else
-                  tc_mma(d_tmem, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_t | (id << 30),
-                         (sfb_t + 4 * term) | (id << 30), acc);
+                  tc_mma(d_tmem, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_j | (id << 30),
+                         (sfb_j + 4 * term) | (id << 30), acc);
                 acc = 1u;
               }
             }
@@ -860,17 +823,11 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
 template <int BN, bool FP4, int KS>
 cudaError_t launch_gemm_bn(const MmaLaunch &a, int sm_count, cudaStream_t s) {
   using Sh = MmaShape<BN, FP4, KS>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_mma_gemm<BN, FP4, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Sh::kSmem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t e = opt_in_smem(k_mma_gemm<BN, FP4, KS>, Sh::kSmem);
+  if (e != cudaSuccess) return e;
   int grid = a.max_tiles < sm_count ? a.max_tiles : sm_count;
   if (grid < 1) grid = 1;
-  k_mma_gemm<BN, FP4, KS><<<grid, 192, Sh::kSmem, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(k_mma_gemm<BN, FP4, KS>, dim3(grid), dim3(192), (size_t)Sh::kSmem, s, a);
 }
 
 }  // namespace
@@ -902,14 +859,6 @@ cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t E, int R, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_mma_plan(const int32_t *offsets, const int32_t *act_list, const int32_t *meta, int E,
-                            int bn, int mt_gu, int mt_dn, int32_t *pad_off, int32_t *tile_gu,
-                            int32_t *tile_dn, int32_t *pos_expert, cudaStream_t s) {
-  k_mma_plan<<<1, 1024, 0, s>>>(offsets, act_list, meta, E, bn, mt_gu, mt_dn, pad_off, tile_gu, tile_dn,
-                                pos_expert);
-  return cudaGetLastError();
-}
-
 cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t *perm, int top_k,
                                 bool gather, const int32_t *offsets, const int32_t *pad_off,
                                 const int32_t *pos_expert, const int32_t *meta, int S_max, int K, int kp,
@@ -918,13 +867,9 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
   const int threads = 256;
   const int64_t warps = (int64_t)S_max * (kp / kMmaKT);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  if (mma_fp4(bn))
-    k_quantize_act<true><<<(unsigned)blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets,
-                                                              pad_off, pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
-  else
-    k_quantize_act<false><<<(unsigned)blocks, threads, 0, s>>>(src, stride, perm, top_k, gather ? 1 : 0, offsets,
-                                                               pad_off, pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
-  return cudaGetLastError();
+  return launch_pdl(mma_fp4(bn) ? k_quantize_act<true> : k_quantize_act<false>, dim3((unsigned)blocks),
+                    dim3(threads), 0, s, src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off, pos_expert, meta,
+                    S_max, K, kp, rb, bn, q, sf);
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {

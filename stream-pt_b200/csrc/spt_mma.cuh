@@ -43,7 +43,7 @@ constexpr int kMmaM = 128;       // rows per tile (tcgen05 M for cta_group::1)
 constexpr int kMmaKT = 128;      // K elements per pipeline stage (one TMA box)
 constexpr int kActTerms = 3;     // e4m3 terms of the activations (128-token tiles)
 constexpr int kFp4Terms = 6;     // e2m1 terms of the activations (tiles of <= 16 tokens)
-constexpr int kMmaStageTilesFp4 = 2;  // K tiles per pipeline stage, FP4 mode
+constexpr int kMmaStageTilesFp4 = 4;  // K tiles per pipeline stage, FP4 mode
 
 struct MmaMatrix {
   uint8_t *w = nullptr;      // packed e2m1 rows
@@ -124,13 +124,6 @@ cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tag_gate, uint32_t tag_u
                                 int D, int K, uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
 cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t experts, int rows, int K,
                              uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
-
-// Tile bookkeeping after dispatch: pad_off, tile_off (for BN tokens per tile
-// and `mtiles` row tiles per expert) and pos -> expert.
-cudaError_t launch_mma_plan(const int32_t *offsets, const int32_t *act_list, const int32_t *meta,
-                            int E, int bn, int mtiles_gu, int mtiles_dn, int32_t *pad_off,
-                            int32_t *tile_off_gu, int32_t *tile_off_dn, int32_t *pos_expert,
-                            cudaStream_t s);
 
 // Quantize rows to the three MXFP8 terms.  Source row of dispatch position
 // p: src[(gather ? perm[p]/top_k : p) * src_stride + k].
