@@ -13,8 +13,10 @@ The L2 (126 MB) is flushed between timed steps by writing a 256 MB buffer.
 
 Configs (BASELINE.json configs[i]): c0 T=1 decode, c1 T=32 prefill batch
 (default: the headline workload), c2 T=2048 Zipf-skewed routing.  Under
-torchrun every rank runs its own batch (token-sharded replicas, no collective
-on the data path): scaling is weak.
+torchrun (N > 1) the block runs expert-parallel: rank r holds experts
+[r*128/N, (r+1)*128/N), routes its own batch of the config's T tokens and
+exchanges token and result rows with the other ranks over NCCL (the layout
+of configs[3]); per-rank tokens are fixed, so scaling is weak.
 """
 from __future__ import annotations
 
@@ -256,7 +258,18 @@ def run_ours(args):
                              router_bias=c["router_bias"])
     ctx = spt.Context(local)
     flags = spt.ARENA_MMA if args.path == "mma" else spt.ARENA_GEMV
-    arena = ctx.synthetic_arena(cfg, params, flags=flags)
+    ep = None
+    if world > 1:
+        # expert parallelism: this rank holds experts [r*E/N, (r+1)*E/N) and
+        # the whole router; token rows cross NVLink through the library's NCCL
+        # exchange (the id of its communicator comes from rank 0)
+        experts = spt.ep_expert_range(E, world, rank)
+        arena = ctx.synthetic_arena(cfg, params, flags=flags, experts=experts)
+        uid = [spt.ep_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        ep = spt.ExpertParallel(ctx, uid[0], rank, world)
+    else:
+        arena = ctx.synthetic_arena(cfg, params, flags=flags)
     ctx.set_path(spt.PATH_MMA if args.path == "mma" else spt.PATH_EXACT)
     stream = torch.cuda.ExternalStream(ctx.stream)
     x_host = spt.synth_normal_host(c["seed"] + 7919 * rank, 1000, T * H)
@@ -265,14 +278,26 @@ def run_ours(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
 
     def step():
-        ctx.forward_moe_batch_device(arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
+        if ep is not None:
+            ctx.forward_moe_batch_ep_device(ep, arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
+        else:
+            ctx.forward_moe_batch_device(arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
+
+    def host_call(xn, on):
+        if ep is not None:
+            ctx.forward_moe_batch_ep(ep, arena, xn, T, out=on)
+        else:
+            ctx.forward_moe_batch(arena, xn, T, out=on)
 
     torch.cuda.synchronize()
     for _ in range(args.warmup):
         step()
     ctx.sync()
-    routing = ctx.last_routing(T, E, K)
-    n_active = int((routing["counts"] > 0).sum())
+    if ep is not None:
+        n_active = ctx.last_dispatch()[0]  # this rank's experts used by the rows it received
+    else:
+        routing = ctx.last_routing(T, E, K)
+        n_active = int((routing["counts"] > 0).sum())
 
     # ---- timed region: device-resident inputs ------------------------------
     # No host synchronisation inside the loop; the 256 MB L2 flush before each
@@ -316,7 +341,7 @@ def run_ours(args):
     out_pin = torch.empty_like(x_pin).pin_memory()
     xn, on = x_pin.numpy(), out_pin.numpy()
     for _ in range(max(1, args.warmup)):
-        ctx.forward_moe_batch(arena, xn, T, out=on)
+        host_call(xn, on)
     e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     if world > 1:
@@ -325,7 +350,7 @@ def run_ours(args):
         with torch.cuda.stream(stream):
             flush.fill_(i & 0xFF)
         e_st[i].record(stream)
-        ctx.forward_moe_batch(arena, xn, T, out=on)
+        host_call(xn, on)
         e_en[i].record(stream)
     torch.cuda.synchronize()
     e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_st, e_en))
@@ -357,7 +382,8 @@ def run_ours(args):
         "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H,
                    "expert_path": args.path,
                    "expert_dim": D, "experts": E, "top_k": K, "seed": c["seed"],
-                   "parallelism": f"token-sharded replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"ep{world}: {E // world} experts per GPU, {T} tokens per rank, NCCL "
+                                   "all-to-all dispatch/combine" if world > 1 else "single GPU"),
                    "l2": "256 MB buffer written between timed steps",
                    "active_experts": n_active},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -381,6 +407,10 @@ def run_ours(args):
     if rank == 0:
         line["clocks"] = clocks.summary()
         print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+    if ep is not None:
+        ep.close()
     arena.close()
     ctx.close()
     if world > 1:

@@ -275,6 +275,57 @@ spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len,
                        int64_t output, const float *x, float *y, int64_t *argmax,
                        float *best_logit);
 
+/* ---- Expert parallelism ---------------------------------------------------
+ * No counterpart in the reference, which runs the block on one host; the
+ * build's target asks for experts sharded 128/world per GPU with all-to-all
+ * dispatch and combine over NVLink.  Rank r of `world` holds experts
+ * [r*E/world, (r+1)*E/world) of every layer (an arena made with
+ * spt_arena_create_range or spt_arena_create_synthetic_range over
+ * spt_ep_expert_range) plus the whole router, and calls the forward with its
+ * own tokens; every rank must call it the same number of times, in the same
+ * order.  Results equal the single-GPU block's for those tokens (bit for bit
+ * on the exact path).  The exchange uses NCCL point-to-point calls on the
+ * context's stream; libnccl.so.2 is opened at run time. */
+#define SPT_EP_UNIQUE_ID_BYTES 128
+typedef struct spt_ep spt_ep;
+/* Experts of rank `rank`: [rank*E/world, (rank+1)*E/world). */
+void spt_ep_expert_range(int64_t num_experts, int32_t world, int32_t rank, int64_t *begin,
+                         int64_t *end);
+/* Rank 0 makes the id and hands it to the other ranks out of band. */
+spt_status spt_ep_unique_id(uint8_t id[SPT_EP_UNIQUE_ID_BYTES]);
+/* Collective over the `world` ranks (each on its own context and device). */
+spt_status spt_ep_create(spt_context *ctx, const uint8_t id[SPT_EP_UNIQUE_ID_BYTES], int32_t rank,
+                         int32_t world, spt_ep **out);
+void spt_ep_destroy(spt_ep *ep);
+/* Device pointers (16-byte aligned), this rank's `batch` tokens.  Enqueues on
+ * the context's stream and synchronises it once, after the per-rank row
+ * counts are exchanged. */
+spt_status spt_forward_moe_batch_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena,
+                                           int64_t layer, const float *x, float *out,
+                                           int64_t batch);
+/* Active experts and dispatched rows of the last dispatch this context ran
+ * (on an expert-parallel call: the rows this rank received and how many of
+ * its experts they used).  Synchronises the stream.  No counterpart in the
+ * reference (instrumentation for the benchmark). */
+spt_status spt_last_dispatch(spt_context *ctx, int64_t *active_experts, int64_t *dispatched);
+/* Host buffers, synchronous: the expert-parallel spt_forward_moe_batch. */
+spt_status spt_forward_moe_batch_ep(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t layer,
+                                    const float *x, int64_t x_len, float *out, int64_t out_len,
+                                    int64_t batch, const volatile int32_t *cancel);
+
+/* Arenas holding experts [expert_begin, expert_end) only (an expert-parallel
+ * shard; the router is always whole).  The single-GPU forward entry points
+ * refuse such an arena. */
+spt_status spt_arena_create_range(spt_context *ctx, const spt_reader *readers,
+                                  const spt_moe_config *cfg, const spt_layer_weights *layers,
+                                  int64_t n_layers, uint32_t flags, int64_t expert_begin,
+                                  int64_t expert_end, spt_arena **out);
+spt_status spt_arena_create_synthetic_range(spt_context *ctx, const spt_moe_config *cfg,
+                                            const spt_synth_params *params, int64_t n_layers,
+                                            uint32_t flags, int64_t expert_begin,
+                                            int64_t expert_end, spt_arena **out);
+void spt_arena_expert_range(const spt_arena *arena, int64_t *expert_begin, int64_t *expert_end);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,7 +15,7 @@ from __future__ import annotations
 import ctypes
 import os
 from dataclasses import dataclass, field
-from typing import Optional, Sequence
+from typing import Tuple, Optional, Sequence
 
 import numpy as np
 
@@ -208,6 +208,17 @@ def lib():
         "spt_combine_moe_batch": ([vp, vp, vp, i64, i64, i64, vp], st),
         "spt_rmsnorm": ([vp, vp, vp, i64, i64, f32, vp], st),
         "spt_mul_q80": ([vp, vp, ctypes.c_uint64, i64, i64, vp, vp, P(i64), P(f32)], st),
+        "spt_ep_expert_range": ([i64, i32, i32, P(i64), P(i64)], None),
+        "spt_last_dispatch": ([vp, P(i64), P(i64)], st),
+        "spt_ep_unique_id": ([vp], st),
+        "spt_ep_create": ([vp, vp, i32, i32, P(vp)], st),
+        "spt_ep_destroy": ([vp], None),
+        "spt_forward_moe_batch_ep_device": ([vp, vp, vp, i64, vp, vp, i64], st),
+        "spt_forward_moe_batch_ep": ([vp, vp, vp, i64, vp, i64, vp, i64, i64, vp], st),
+        "spt_arena_create_range": ([vp, vp, P(_Config), vp, i64, ctypes.c_uint32, i64, i64, P(vp)], st),
+        "spt_arena_create_synthetic_range": ([vp, P(_Config), P(_SynthParams), i64, ctypes.c_uint32, i64, i64,
+                                              P(vp)], st),
+        "spt_arena_expert_range": ([vp, P(i64), P(i64)], None),
         "spt_set_stage_timing": ([vp, ctypes.c_int], st),
         "spt_stage_times": ([vp, vp, ctypes.c_int], ctypes.c_int),
         "spt_kernels_per_forward": ([vp], ctypes.c_int),
@@ -311,12 +322,51 @@ class Context:
         return Arena(self, h, cfg, n, keep=(readers,))
 
     def synthetic_arena(self, cfg: Config, params: SynthParams, n_layers: int = 1,
-                        flags: int = ARENA_GEMV) -> "Arena":
+                        flags: int = ARENA_GEMV, experts: Optional[Tuple[int, int]] = None) -> "Arena":
+        """Seeded synthetic arena; `experts` = (begin, end) keeps only those
+        experts (an expert-parallel shard, same bytes as the full arena's)."""
         c, p = cfg._c(), params._c()
         h = ctypes.c_void_p()
-        self.check(lib().spt_arena_create_synthetic(self._h, ctypes.byref(c), ctypes.byref(p), n_layers,
-                                                    flags, ctypes.byref(h)))
+        if experts is None:
+            self.check(lib().spt_arena_create_synthetic(self._h, ctypes.byref(c), ctypes.byref(p), n_layers,
+                                                        flags, ctypes.byref(h)))
+        else:
+            self.check(lib().spt_arena_create_synthetic_range(self._h, ctypes.byref(c), ctypes.byref(p), n_layers,
+                                                              flags, experts[0], experts[1], ctypes.byref(h)))
         return Arena(self, h, cfg, n_layers)
+
+    def arena_range(self, readers: Sequence[Reader], cfg: Config, layers: Sequence[LayerWeights],
+                    experts: Tuple[int, int], flags: int = ARENA_GEMV) -> "Arena":
+        """spt_arena_create_range: GGUF arena holding experts [begin, end) only."""
+        n = len(layers)
+        rs = (_Reader * n)(*[r._c() for r in readers])
+        ls = (_LayerWeights * n)(*[l._c() for l in layers])
+        c = cfg._c()
+        h = ctypes.c_void_p()
+        self.check(lib().spt_arena_create_range(self._h, rs, ctypes.byref(c), ls, n, flags, experts[0], experts[1],
+                                                ctypes.byref(h)))
+        return Arena(self, h, cfg, n, keep=(readers,))
+
+    def last_dispatch(self) -> Tuple[int, int]:
+        """(active experts, dispatched rows) of the last dispatch this context ran."""
+        a, d = ctypes.c_int64(), ctypes.c_int64()
+        self.check(lib().spt_last_dispatch(self._h, ctypes.byref(a), ctypes.byref(d)))
+        return a.value, d.value
+
+    # ---- expert parallelism ------------------------------------------------
+    def forward_moe_batch_ep(self, ep: "ExpertParallel", arena: "Arena", x: np.ndarray, batch: int,
+                             layer: int = 0, out: Optional[np.ndarray] = None) -> np.ndarray:
+        x = _f32(x)
+        if out is None:
+            out = np.empty_like(x)
+        self.check(lib().spt_forward_moe_batch_ep(self._h, ep.handle, arena.handle, layer, _p(x), x.size, _p(out),
+                                                  out.size, batch, None))
+        return out
+
+    def forward_moe_batch_ep_device(self, ep: "ExpertParallel", arena: "Arena", x_ptr: int, out_ptr: int,
+                                    batch: int, layer: int = 0):
+        self.check(lib().spt_forward_moe_batch_ep_device(self._h, ep.handle, arena.handle, layer,
+                                                         ctypes.c_void_p(x_ptr), ctypes.c_void_p(out_ptr), batch))
 
     # ---- the block ----------------------------------------------------------
     def forward_moe_batch(self, arena: "Arena", x: np.ndarray, batch: int, layer: int = 0,
@@ -438,6 +488,49 @@ class Context:
         self.check(lib().spt_mul_q80(self._h, _p(data), data.size, input_, output, _p(x), _p(y),
                                      ctypes.byref(am), ctypes.byref(best)))
         return y, am.value, np.float32(best.value)
+
+
+def ep_expert_range(num_experts: int, world: int, rank: int) -> Tuple[int, int]:
+    """Experts held by `rank` of `world`: [rank*E/world, (rank+1)*E/world)."""
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    lib().spt_ep_expert_range(num_experts, world, rank, ctypes.byref(b), ctypes.byref(e))
+    return b.value, e.value
+
+
+def ep_unique_id() -> bytes:
+    """NCCL unique id for spt_ep_create (made on rank 0, shared out of band)."""
+    buf = (ctypes.c_uint8 * 128)()
+    st = lib().spt_ep_unique_id(buf)
+    if st != OK:
+        raise SptError(st, lib().spt_last_error(None).decode())
+    return bytes(buf)
+
+
+class ExpertParallel:
+    """spt_ep: this rank's member of an expert-parallel group (collective create)."""
+
+    def __init__(self, ctx: "Context", unique_id: bytes, rank: int, world: int):
+        if len(unique_id) != 128:
+            raise ValueError("unique id must be 128 bytes")
+        self.ctx, self.rank, self.world = ctx, rank, world
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
+        self._h = ctypes.c_void_p()
+        ctx.check(lib().spt_ep_create(ctx._h, buf, rank, world, ctypes.byref(self._h)))
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if self._h:
+            lib().spt_ep_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Arena:

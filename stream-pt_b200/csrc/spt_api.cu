@@ -83,6 +83,8 @@ struct spt_context {
 struct spt_arena {
   int device = -1;
   spt_moe_config cfg{};
+  int64_t expert_begin = 0;  // experts [expert_begin, expert_begin + expert_count) are resident
+  int64_t expert_count = 0;  // (every expert unless the arena is one rank's expert-parallel shard)
   std::vector<LayerDev> layers;
   std::vector<void *> allocs;
   uint64_t bytes = 0;
@@ -460,14 +462,7 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const int64_t na_max = std::min<int64_t>(E, S);
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
-  if (!ctx->dev_err.p) {
-    SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
-    SPT_CUDA(ctx, cudaMemset(ctx->dev_err.p, 0, sizeof(int32_t)));
-  }
-  SPT_CUDA(ctx, ctx->qx.ensure(mma_act_bytes(bn, rb, kph)));
-  SPT_CUDA(ctx, ctx->sfx.ensure(mma_act_sf_bytes(bn, rb, kph)));
-  SPT_CUDA(ctx, ctx->qa.ensure(mma_act_bytes(bn, rb, kpd)));
-  SPT_CUDA(ctx, ctx->sfa.ensure(mma_act_sf_bytes(bn, rb, kpd)));
+  // buffers: reserve_experts
   const bool fp4 = mma_fp4(bn);
   const int ks = mma_stage_tiles(bn);
   const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
@@ -549,41 +544,66 @@ spt_status check_device_error(spt_context *ctx) {
   return SPT_OK;
 }
 
-// The whole block on device pointers (enqueue only).
-spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
-                          float *out, int64_t T) {
-  const spt_moe_config &c = arena->cfg;
-  const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
-            K = (int)c.num_experts_used;
-  if (E > kDispatchMaxExperts || K > kSelectMaxK)
-    return fail(ctx, SPT_ERR_UNSUPPORTED, "experts %d > %d or top-k %d > %d unsupported", E,
-                kDispatchMaxExperts, K, kSelectMaxK);
-  spt_status st = ensure_scratch(ctx, T, c);
-  if (st) return st;
-  const LayerDev &L = arena->layers[(size_t)layer];
-  cudaStream_t s = ctx->stream;
-#define SPT_MARK(i) \
-  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[i], s))
-  SPT_MARK(0);
-  SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s));
-  SPT_MARK(1);
-  SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, ctx->sel_idx.as<int32_t>(),
-                              ctx->sel_w.as<float>(), s));
-  SPT_MARK(2);
-  const int max_active = (int)std::min<int64_t>(E, T * K);
-  const bool use_mma = L.has_mma && (ctx->path == SPT_PATH_MMA || (ctx->path == SPT_PATH_AUTO)) &&
-                       !(ctx->path == SPT_PATH_EXACT);
+// Expert GEMM path of this call: tensor cores when the arena has their
+// layout and the context allows it, else the exact CUDA-core GEMV.
+spt_status pick_path(spt_context *ctx, const LayerDev &L, bool *use_mma) {
+  *use_mma = L.has_mma && ctx->path != SPT_PATH_EXACT;
   if (ctx->path == SPT_PATH_MMA && !L.has_mma)
     return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_MMA");
-  if (!use_mma && !L.has_g8)
+  if (!*use_mma && !L.has_g8)
     return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_GEMV");
+  return SPT_OK;
+}
+
+// Every device buffer experts_combine needs for T tokens of config c.  It
+// allocates only here, so a caller can make the allocations before work that
+// must not overlap a cudaMalloc/cudaFree (an NCCL exchange in flight: their
+// implicit device synchronisation can deadlock against NCCL's progress).
+spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, int64_t T) {
+  spt_status st = ensure_scratch(ctx, T, c);
+  if (st) return st;
+  bool use_mma = false;
+  if ((st = pick_path(ctx, L, &use_mma))) return st;
+  if (!use_mma) return SPT_OK;
+  const int64_t E = c.num_experts, K = c.num_experts_used, S = T * K;
+  SPT_CUDA(ctx, ctx->pad_off.ensure(sizeof(int32_t) * E));
+  SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
+  SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
+  SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
+  const int bn = pick_bn(T, K, E);
+  const int64_t na_max = std::min<int64_t>(E, S);
+  const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
+  const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
+  if (!ctx->dev_err.p) {
+    SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
+    SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
+  }
+  SPT_CUDA(ctx, ctx->qx.ensure(mma_act_bytes(bn, rb, kph)));
+  SPT_CUDA(ctx, ctx->sfx.ensure(mma_act_sf_bytes(bn, rb, kph)));
+  SPT_CUDA(ctx, ctx->qa.ensure(mma_act_bytes(bn, rb, kpd)));
+  SPT_CUDA(ctx, ctx->sfa.ensure(mma_act_sf_bytes(bn, rb, kpd)));
+  return SPT_OK;
+}
+
+#define SPT_MARK(i) \
+  if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[i], s))
+
+// Dispatch, expert products and combine for selections already made
+// (sel_idx/sel_w [T*K], expert ids local to the arena): out[t] = sum over
+// ranks r of fma(result, weight, out[t]).  `c` gives the arena's experts
+// and top-k (the expert-parallel receive side passes its shard and top-k 1).
+spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
+                           int64_t T, const int32_t *sel_idx, const float *sel_w, float *out) {
+  const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
+            K = (int)c.num_experts_used;
+  cudaStream_t s = ctx->stream;
+  spt_status st = SPT_OK;
+  const int max_active = (int)std::min<int64_t>(E, T * K);
+  bool use_mma = false;
+  if ((st = pick_path(ctx, L, &use_mma))) return st;
+  if ((st = reserve_experts(ctx, L, c, T))) return st;
   DispatchPlan plan;  // tensor-core tile layout, made by the dispatch kernel
   if (use_mma) {
-    const int64_t S = T * K;
-    SPT_CUDA(ctx, ctx->pad_off.ensure(sizeof(int32_t) * E));
-    SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
-    SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
-    SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
     plan.bn = pick_bn(T, K, E);
     plan.mt_gu = L.gu_mma.mtiles;
     plan.mt_dn = L.dn_mma.mtiles;
@@ -592,7 +612,7 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     plan.tile_dn = ctx->tile_dn.as<int32_t>();
     plan.pos_expert = ctx->pos_expert.as<int32_t>();
   }
-  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)(T * K), E,
+  SPT_CUDA(ctx, launch_dispatch(sel_idx, sel_w, (int)(T * K), E,
                                 ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
                                 ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
                                 ctx->meta.as<int32_t>(), s, use_mma ? &plan : nullptr));
@@ -639,13 +659,48 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     ctx->kernels_last = 6;
   }
   SPT_MARK(7);
-  SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), ctx->sel_w.as<float>(),
-                               ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
+  SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
   SPT_MARK(8);
-#undef SPT_MARK
+  return SPT_OK;
+}
+
+// Router logits and top-k selections of T tokens (all experts of the layer).
+spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
+                        int64_t T, int32_t *sel_idx, float *sel_w) {
+  const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
+  cudaStream_t s = ctx->stream;
+  SPT_MARK(0);
+  SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s));
+  SPT_MARK(1);
+  SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
+  SPT_MARK(2);
+  return SPT_OK;
+}
+
+spt_status check_layer_limits(spt_context *ctx, const spt_moe_config &c) {
+  if (c.num_experts > kDispatchMaxExperts || c.num_experts_used > kSelectMaxK)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "experts %lld > %d or top-k %lld > %d unsupported",
+                (long long)c.num_experts, kDispatchMaxExperts, (long long)c.num_experts_used, kSelectMaxK);
+  return SPT_OK;
+}
+
+// The whole block on device pointers (enqueue only).
+spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
+                          float *out, int64_t T) {
+  const spt_moe_config &c = arena->cfg;
+  spt_status st = check_layer_limits(ctx, c);
+  if (st) return st;
+  if (arena->expert_count != c.num_experts)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "arena holds experts [%lld, %lld) of %lld: use the expert-parallel entry point",
+                (long long)arena->expert_begin, (long long)(arena->expert_begin + arena->expert_count),
+                (long long)c.num_experts);
+  if ((st = ensure_scratch(ctx, T, c))) return st;
+  const LayerDev &L = arena->layers[(size_t)layer];
+  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>()))) return st;
+  if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out))) return st;
   ctx->last_T = T;
-  ctx->last_E = E;
-  ctx->last_K = K;
+  ctx->last_E = c.num_experts;
+  ctx->last_K = c.num_experts_used;
   ctx->have_routing = true;
   return SPT_OK;
 }
@@ -837,9 +892,9 @@ spt_status spt_validate_moe_layer(spt_context *ctx, const spt_reader *reader,
   return validate_layer(ctx, reader, cfg, lw);
 }
 
-spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,
-                            const spt_layer_weights *layers, int64_t n_layers, uint32_t flags,
-                            spt_arena **out) {
+static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,
+                             const spt_layer_weights *layers, int64_t n_layers, uint32_t flags, int64_t e0,
+                             int64_t e1, spt_arena **out) {
   if (!out || !readers || !cfg || !layers || n_layers <= 0)
     return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
   *out = nullptr;
@@ -852,9 +907,14 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const s
   if (flags == 0) flags = SPT_ARENA_GEMV;
   const int64_t H = cfg->hidden_dim, D = cfg->expert_hidden_dim, E = cfg->num_experts;
   if (H > (1 << 30) || D > (1 << 30)) return fail(ctx, SPT_ERR_UNSUPPORTED, "dimensions too large");
+  if (e0 < 0 || e1 > E || e0 >= e1) return fail(ctx, SPT_ERR_DIMENSIONS, "expert range [%lld, %lld) outside [0, %lld)",
+                                                (long long)e0, (long long)e1, (long long)E);
+  const int64_t ne = e1 - e0;  // resident experts
   spt_arena *a = new spt_arena();
   a->device = ctx->device;
   a->cfg = *cfg;
+  a->expert_begin = e0;
+  a->expert_count = ne;
   a->flags = flags;
   a->layers.resize((size_t)n_layers);
   std::vector<float> tmp;
@@ -880,22 +940,23 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const s
     for (auto &b : biases) {
       tmp.assign((size_t)(E * b.dim), 0.0f);
       if (named(*b.t)) decode_floats(r.base + b.t->start, b.t->type, E * b.dim, tmp.data());
-      if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), b.dst))) break;
+      if ((st = upload_floats(ctx, a, tmp.data() + e0 * b.dim, (size_t)(ne * b.dim), b.dst))) break;
     }
     if (st) break;
     {
       DevBuf sg, su;
-      const size_t gu_raw = (size_t)E * D * (H / 32) * 17;
-      if ((st = stage_raw(ctx, &sg, r.base + w.ffn_gate_exps.start, gu_raw)) == SPT_OK &&
-          (st = stage_raw(ctx, &su, r.base + w.ffn_up_exps.start, gu_raw)) == SPT_OK) {
+      // expert e's matrix is the byte range [start + e * per_expert, + per_expert)
+      const size_t gu_per = (size_t)D * (H / 32) * 17, gu_raw = (size_t)ne * gu_per;
+      if ((st = stage_raw(ctx, &sg, r.base + w.ffn_gate_exps.start + e0 * gu_per, gu_raw)) == SPT_OK &&
+          (st = stage_raw(ctx, &su, r.base + w.ffn_up_exps.start + e0 * gu_per, gu_raw)) == SPT_OK) {
         if (flags & SPT_ARENA_GEMV) {
-          if (st == SPT_OK) st = repack_g8_from(ctx, a, sg.as<uint8_t>(), E, (int)D, (int)(H / 32), &L.gate);
-          if (st == SPT_OK) st = repack_g8_from(ctx, a, su.as<uint8_t>(), E, (int)D, (int)(H / 32), &L.up);
+          if (st == SPT_OK) st = repack_g8_from(ctx, a, sg.as<uint8_t>(), ne, (int)D, (int)(H / 32), &L.gate);
+          if (st == SPT_OK) st = repack_g8_from(ctx, a, su.as<uint8_t>(), ne, (int)D, (int)(H / 32), &L.up);
         }
         if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
-          st = alloc_mma(ctx, a, E, (int)(2 * D), (int)H, &L.gu_mma);
+          st = alloc_mma(ctx, a, ne, (int)(2 * D), (int)H, &L.gu_mma);
           if (st == SPT_OK) {
-            cudaError_t e = launch_repack_mma_gu(sg.as<uint8_t>(), su.as<uint8_t>(), E, (int)D, (int)H, &L.gu_mma, ctx->stream);
+            cudaError_t e = launch_repack_mma_gu(sg.as<uint8_t>(), su.as<uint8_t>(), ne, (int)D, (int)H, &L.gu_mma, ctx->stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
             if (e != cudaSuccess) st = cuda_fail(ctx, e, "repack mma gate/up");
           }
@@ -905,12 +966,13 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const s
       su.release();
       if (st) break;
       DevBuf sd;
-      if ((st = stage_raw(ctx, &sd, r.base + w.ffn_down_exps.start, (size_t)E * H * (D / 32) * 17)) == SPT_OK) {
-        if (flags & SPT_ARENA_GEMV) st = repack_g8_from(ctx, a, sd.as<uint8_t>(), E, (int)H, (int)(D / 32), &L.down);
+      const size_t dn_per = (size_t)H * (D / 32) * 17;
+      if ((st = stage_raw(ctx, &sd, r.base + w.ffn_down_exps.start + e0 * dn_per, (size_t)ne * dn_per)) == SPT_OK) {
+        if (flags & SPT_ARENA_GEMV) st = repack_g8_from(ctx, a, sd.as<uint8_t>(), ne, (int)H, (int)(D / 32), &L.down);
         if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
-          st = alloc_mma(ctx, a, E, (int)H, (int)D, &L.dn_mma);
+          st = alloc_mma(ctx, a, ne, (int)H, (int)D, &L.dn_mma);
           if (st == SPT_OK) {
-            cudaError_t e = launch_repack_mma(sd.as<uint8_t>(), E, (int)H, (int)D, &L.dn_mma, ctx->stream);
+            cudaError_t e = launch_repack_mma(sd.as<uint8_t>(), ne, (int)H, (int)D, &L.dn_mma, ctx->stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
             if (e != cudaSuccess) st = cuda_fail(ctx, e, "repack mma down");
           }
@@ -930,9 +992,20 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const s
   return SPT_OK;
 }
 
-spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cfg,
-                                      const spt_synth_params *p, int64_t n_layers, uint32_t flags,
-                                      spt_arena **out) {
+spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,
+                            const spt_layer_weights *layers, int64_t n_layers, uint32_t flags,
+                            spt_arena **out) {
+  return arena_create_impl(ctx, readers, cfg, layers, n_layers, flags, 0, cfg ? cfg->num_experts : 0, out);
+}
+
+spt_status spt_arena_create_range(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,
+                                  const spt_layer_weights *layers, int64_t n_layers, uint32_t flags,
+                                  int64_t expert_begin, int64_t expert_end, spt_arena **out) {
+  return arena_create_impl(ctx, readers, cfg, layers, n_layers, flags, expert_begin, expert_end, out);
+}
+
+static spt_status synth_create_impl(spt_context *ctx, const spt_moe_config *cfg, const spt_synth_params *p,
+                             int64_t n_layers, uint32_t flags, int64_t e0, int64_t e1, spt_arena **out) {
   if (!out || !cfg || !p || n_layers <= 0)
     return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
   *out = nullptr;
@@ -942,10 +1015,15 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
   if (H % 32 != 0 || D % 32 != 0)
     return fail(ctx, SPT_ERR_EXPERT, "expected MXFP4 expert tensor dimensions divisible by 32");
   if ((st = require_device(ctx))) return st;
+  if (e0 < 0 || e1 > E || e0 >= e1) return fail(ctx, SPT_ERR_DIMENSIONS, "expert range [%lld, %lld) outside [0, %lld)",
+                                                (long long)e0, (long long)e1, (long long)E);
+  const int64_t ne = e1 - e0;  // resident experts
   if (flags == 0) flags = SPT_ARENA_GEMV;
   spt_arena *a = new spt_arena();
   a->device = ctx->device;
   a->cfg = *cfg;
+  a->expert_begin = e0;
+  a->expert_count = ne;
   a->flags = flags;
   a->layers.resize((size_t)n_layers);
   std::vector<float> tmp;
@@ -966,7 +1044,7 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
     for (auto &b : biases) {
       tmp.assign((size_t)(E * b.dim), 0.0f);
       if (p->expert_bias) synth_normal(p->seed, synth_tag(l, b.kind), 0.0f, p->bias_std, tmp.data(), E * b.dim);
-      if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), b.dst))) break;
+      if ((st = upload_floats(ctx, a, tmp.data() + e0 * b.dim, (size_t)(ne * b.dim), b.dst))) break;
     }
     if (st) break;
     struct {
@@ -980,8 +1058,8 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
       if (!(flags & SPT_ARENA_GEMV)) break;
       uint4 *nib = nullptr;
       uint32_t *scl = nullptr;
-      if ((st = alloc_g8(ctx, a, E, m.rows, m.blocks, m.m, &nib, &scl))) break;
-      cudaError_t e = launch_synth_g8(p->seed, synth_tag(l, m.kind), E, m.rows, m.blocks,
+      if ((st = alloc_g8(ctx, a, ne, m.rows, m.blocks, m.m, &nib, &scl))) break;
+      cudaError_t e = launch_synth_g8(p->seed, synth_tag(l, m.kind), e0, ne, m.rows, m.blocks,
                                       p->scale_lo, p->scale_hi, nib, scl, ctx->stream);
       if (e != cudaSuccess) {
         st = cuda_fail(ctx, e, "synth");
@@ -990,15 +1068,15 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
     }
     if (st) break;
     if (flags & SPT_ARENA_MMA) {
-      if ((st = alloc_mma(ctx, a, E, (int)(2 * D), (int)H, &L.gu_mma))) break;
-      cudaError_t e = launch_synth_mma_gu(p->seed, synth_tag(l, kSynthGate), synth_tag(l, kSynthUp), E, (int)D,
+      if ((st = alloc_mma(ctx, a, ne, (int)(2 * D), (int)H, &L.gu_mma))) break;
+      cudaError_t e = launch_synth_mma_gu(p->seed, synth_tag(l, kSynthGate), synth_tag(l, kSynthUp), e0, ne, (int)D,
                                           (int)H, p->scale_lo, p->scale_hi, &L.gu_mma, ctx->stream);
       if (e != cudaSuccess) {
         st = cuda_fail(ctx, e, "synth mma");
         break;
       }
-      if ((st = alloc_mma(ctx, a, E, (int)H, (int)D, &L.dn_mma))) break;
-      e = launch_synth_mma(p->seed, synth_tag(l, kSynthDown), E, (int)H, (int)D, p->scale_lo, p->scale_hi,
+      if ((st = alloc_mma(ctx, a, ne, (int)H, (int)D, &L.dn_mma))) break;
+      e = launch_synth_mma(p->seed, synth_tag(l, kSynthDown), e0, ne, (int)H, (int)D, p->scale_lo, p->scale_hi,
                            &L.dn_mma, ctx->stream);
       if (e != cudaSuccess) {
         st = cuda_fail(ctx, e, "synth mma");
@@ -1018,6 +1096,22 @@ spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cf
   }
   *out = a;
   return SPT_OK;
+}
+
+spt_status spt_arena_create_synthetic(spt_context *ctx, const spt_moe_config *cfg, const spt_synth_params *p,
+                                      int64_t n_layers, uint32_t flags, spt_arena **out) {
+  return synth_create_impl(ctx, cfg, p, n_layers, flags, 0, cfg ? cfg->num_experts : 0, out);
+}
+
+spt_status spt_arena_create_synthetic_range(spt_context *ctx, const spt_moe_config *cfg,
+                                            const spt_synth_params *p, int64_t n_layers, uint32_t flags,
+                                            int64_t expert_begin, int64_t expert_end, spt_arena **out) {
+  return synth_create_impl(ctx, cfg, p, n_layers, flags, expert_begin, expert_end, out);
+}
+
+void spt_arena_expert_range(const spt_arena *arena, int64_t *expert_begin, int64_t *expert_end) {
+  if (expert_begin) *expert_begin = arena ? arena->expert_begin : 0;
+  if (expert_end) *expert_end = arena ? arena->expert_begin + arena->expert_count : 0;
 }
 
 void spt_arena_destroy(spt_arena *a) {
@@ -1430,6 +1524,8 @@ extern "C" spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_
                 (long long)kStaticMaxSlots, (long long)kStaticMaxDim, (long long)kStaticMaxExperts);
   spt_status st = require_device(ctx);
   if (st) return st;
+  if (arena->expert_count != E)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "arena holds only some of the experts (an expert-parallel shard)");
   const LayerDev &L = arena->layers[(size_t)layer];
   if (!L.has_g8) return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_GEMV");
   unsigned char *base = nullptr;
@@ -1490,3 +1586,424 @@ extern "C" spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_
   SPT_CUDA(ctx, launch_combine(res, sel_w, slot_pos, T, (int)K, (int)H, out, s));
   return SPT_OK;
 }
+
+// =========================================================================
+// Expert parallelism.  Rank r of `world` holds experts [r*E/world,
+// (r+1)*E/world) of every layer and the whole router; each rank routes its
+// own tokens, sends every dispatched slot's token row to the owner of its
+// expert, runs the expert products for the rows it receives, and returns the
+// result rows, which the sender combines in rank order exactly as the
+// single-GPU block does.  The exchange runs on NCCL point-to-point calls on
+// the context's stream; libnccl is opened at run time, so a process that has
+// already loaded one (a PyTorch process) shares it.
+
+#include <dlfcn.h>
+#include <nccl.h>
+#include <time.h>
+#include <unistd.h>
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  const char *(*error_string)(ncclResult_t) = nullptr;
+  std::string why;  // empty when loaded
+};
+
+const NcclApi &nccl() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      a.why = std::string("cannot open libnccl.so.2: ") + dlerror();
+      return a;
+    }
+    bool ok = true;
+    auto sym = [&](const char *name) {
+      void *f = dlsym(h, name);
+      if (!f) ok = false;
+      return f;
+    };
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(sym("ncclGetUniqueId"));
+    a.comm_init_rank_config = reinterpret_cast<decltype(a.comm_init_rank_config)>(sym("ncclCommInitRankConfig"));
+    a.comm_get_async_error = reinterpret_cast<decltype(a.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
+    a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(sym("ncclCommAbort"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(sym("ncclCommDestroy"));
+    a.send = reinterpret_cast<decltype(a.send)>(sym("ncclSend"));
+    a.recv = reinterpret_cast<decltype(a.recv)>(sym("ncclRecv"));
+    a.group_start = reinterpret_cast<decltype(a.group_start)>(sym("ncclGroupStart"));
+    a.group_end = reinterpret_cast<decltype(a.group_end)>(sym("ncclGroupEnd"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(sym("ncclGetErrorString"));
+    if (!ok) a.why = "libnccl is missing an expected symbol";
+    return a;
+  }();
+  return api;
+}
+
+}  // namespace
+
+struct spt_ep {
+  spt_context *ctx = nullptr;
+  int rank = 0, world = 1;
+  ncclComm_t comm = nullptr;
+  bool broken = false;   // aborted after a wait ran out; every later call fails
+  bool pending = false;  // the last result exchange may still be in flight
+  int64_t t_max = 0;     // largest batch so far (no buffer grows below it)
+  int64_t timeout_ms = 60000;
+  // send side (this rank's tokens)
+  DevBuf sel_w;          // [S] selection weights kept for the final combine
+  DevBuf send_off;       // [world+1] first send row of each destination rank
+  DevBuf send_perm;      // [S] send row -> slot
+  DevBuf send_pos;       // [S] slot -> send row, -1 if not dispatched
+  DevBuf dest_list, send_meta;
+  DevBuf xs, ms;         // send rows [S][H] and their local expert ids [S]
+  DevBuf ret;            // result rows returned to this rank [S][H]
+  DevBuf counts;         // [2*world] rows sent to / received from each rank
+  // receive side (rows other ranks send here)
+  DevBuf xr, mr;         // received rows [R][H] and local expert ids [R]
+  DevBuf rows_out;       // their results [R][H]
+  int32_t *counts_host = nullptr;  // pinned [2*world]
+  std::vector<int64_t> soff, roff;  // prefix offsets (rows) per rank
+};
+
+namespace {
+
+#define SPT_NCCL(ctx, call)                                                                        \
+  do {                                                                                             \
+    ncclResult_t _r = (call);                                                                      \
+    if (_r != ncclSuccess)                                                                         \
+      return fail((ctx), SPT_ERR_NCCL, "%s: %s", #call, nccl().error_string(_r));                  \
+  } while (0)
+
+// Bounded waits.  The communicator is non-blocking, so NCCL calls return
+// while their setup is in progress; a peer that never arrives would leave
+// both that and the exchange kernels on the stream waiting forever.  Each
+// wait below gives up after ep->timeout_ms, aborts the communicator (which
+// also ends its kernels) and marks the group broken.
+int64_t now_ms() {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (int64_t)ts.tv_sec * 1000 + ts.tv_nsec / 1000000;
+}
+
+spt_status ep_abort(spt_ep *ep, const char *what) {
+  if (ep->comm && !ep->broken) nccl().comm_abort(ep->comm);
+  ep->broken = true;
+  return fail(ep->ctx, SPT_ERR_NCCL, "expert-parallel %s: no progress within %lld ms; group aborted", what,
+              (long long)ep->timeout_ms);
+}
+
+spt_status wait_comm(spt_ep *ep, const char *what) {
+  const int64_t deadline = now_ms() + ep->timeout_ms;
+  for (;;) {
+    ncclResult_t state = ncclSuccess;
+    ncclResult_t r = nccl().comm_get_async_error(ep->comm, &state);
+    if (r != ncclSuccess) return fail(ep->ctx, SPT_ERR_NCCL, "ncclCommGetAsyncError: %s", nccl().error_string(r));
+    if (state == ncclSuccess) return SPT_OK;
+    if (state != ncclInProgress) {
+      spt_status st = fail(ep->ctx, SPT_ERR_NCCL, "%s: %s", what, nccl().error_string(state));
+      nccl().comm_abort(ep->comm);
+      ep->broken = true;
+      return st;
+    }
+    if (now_ms() > deadline) return ep_abort(ep, what);
+    usleep(50);
+  }
+}
+
+spt_status wait_stream(spt_ep *ep, const char *what) {
+  const int64_t deadline = now_ms() + ep->timeout_ms;
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(ep->ctx->stream);
+    if (e == cudaSuccess) return SPT_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(ep->ctx, e, what);
+    if (now_ms() > deadline) return ep_abort(ep, what);
+    usleep(20);
+  }
+}
+
+// One grouped exchange: for every peer, send cnt_s rows of `width` elements
+// starting at row soff and receive cnt_r rows at roff.
+spt_status exchange(spt_ep *ep, const void *send, void *recv, int64_t width, size_t elem, ncclDataType_t type,
+                    const std::vector<int64_t> &soff, const std::vector<int64_t> &roff) {
+  spt_context *ctx = ep->ctx;
+  const NcclApi &api = nccl();
+  if (ep->broken) return fail(ctx, SPT_ERR_NCCL, "expert-parallel group was aborted");
+  SPT_NCCL(ctx, api.group_start());
+  for (int j = 0; j < ep->world; ++j) {
+    const int64_t ns = soff[j + 1] - soff[j], nr = roff[j + 1] - roff[j];
+    if (ns > 0)
+      SPT_NCCL(ctx, api.send(static_cast<const uint8_t *>(send) + (size_t)soff[j] * width * elem,
+                             (size_t)(ns * width), type, j, ep->comm, ctx->stream));
+    if (nr > 0)
+      SPT_NCCL(ctx, api.recv(static_cast<uint8_t *>(recv) + (size_t)roff[j] * width * elem, (size_t)(nr * width),
+                             type, j, ep->comm, ctx->stream));
+  }
+  ncclResult_t r = api.group_end();
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ctx, SPT_ERR_NCCL, "ncclGroupEnd: %s", api.error_string(r));
+  return wait_comm(ep, "exchange");
+}
+
+// SPT_EP_TRACE=1 prints each phase of an expert-parallel call to stderr.
+void ep_trace(const spt_ep *ep, const char *fmt, ...) {
+  static const bool on = [] {
+    const char *v = getenv("SPT_EP_TRACE");
+    return v && v[0] == '1';
+  }();
+  if (!on) return;
+  char buf[256];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  fprintf(stderr, "[spt ep %d/%d %lld ms] %s\n", ep->rank, ep->world, (long long)(now_ms() % 1000000), buf);
+  fflush(stderr);
+}
+
+spt_status forward_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t layer, const float *x,
+                             float *out, int64_t T) {
+  const spt_moe_config &c = arena->cfg;
+  spt_status st = check_layer_limits(ctx, c);
+  if (st) return st;
+  const int64_t H = c.hidden_dim, E = c.num_experts, K = c.num_experts_used;
+  const int W = ep->world;
+  if (E % W != 0)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "%lld experts do not divide evenly over %d ranks", (long long)E, W);
+  const int64_t ne = E / W;
+  if (arena->expert_begin != ep->rank * ne || arena->expert_count != ne)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "arena holds experts [%lld, %lld), rank %d of %d owns [%lld, %lld)",
+                (long long)arena->expert_begin, (long long)(arena->expert_begin + arena->expert_count), ep->rank, W,
+                (long long)(ep->rank * ne), (long long)((ep->rank + 1) * ne));
+  if (H % 4 != 0) return fail(ctx, SPT_ERR_UNSUPPORTED, "hidden size %lld not a multiple of 4", (long long)H);
+  cudaStream_t s = ctx->stream;
+  const LayerDev &L = arena->layers[(size_t)layer];
+  const int64_t S = T * K;
+  // A previous call's result exchange may still be in flight (device entry
+  // point): let it finish before this call's buffers can grow.
+  if (ep->pending && T > ep->t_max && (st = wait_stream(ep, "previous exchange"))) return st;
+  ep->t_max = std::max(ep->t_max, T);
+  ep_trace(ep, "start T=%lld pending=%d", (long long)T, (int)ep->pending);
+  // 1. route this rank's tokens over all experts
+  if ((st = ensure_scratch(ctx, T, c))) return st;
+  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>()))) return st;
+  // 2. group the dispatched slots by owner rank, gather their rows
+  SPT_CUDA(ctx, ep->sel_w.ensure(sizeof(float) * std::max<int64_t>(S, 1)));
+  SPT_CUDA(ctx, ep->send_off.ensure(sizeof(int32_t) * (W + 1)));
+  SPT_CUDA(ctx, ep->send_perm.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
+  SPT_CUDA(ctx, ep->send_pos.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
+  SPT_CUDA(ctx, ep->dest_list.ensure(sizeof(int32_t) * W));
+  SPT_CUDA(ctx, ep->send_meta.ensure(sizeof(int32_t) * 4));
+  SPT_CUDA(ctx, ep->xs.ensure(sizeof(float) * std::max<int64_t>(S, 1) * H));
+  SPT_CUDA(ctx, ep->ms.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
+  SPT_CUDA(ctx, ep->ret.ensure(sizeof(float) * std::max<int64_t>(S, 1) * H));
+  SPT_CUDA(ctx, ep->counts.ensure(sizeof(int32_t) * 2 * W));
+  if (!ep->counts_host)
+    SPT_CUDA(ctx, cudaHostAlloc((void **)&ep->counts_host, sizeof(int32_t) * 2 * W, cudaHostAllocDefault));
+  SPT_CUDA(ctx, cudaMemcpyAsync(ep->sel_w.p, ctx->sel_w.p, sizeof(float) * S, cudaMemcpyDeviceToDevice, s));
+  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)S, W,
+                                ep->send_off.as<int32_t>(), ep->send_perm.as<int32_t>(), ep->send_pos.as<int32_t>(),
+                                ep->dest_list.as<int32_t>(), ep->send_meta.as<int32_t>(), s, nullptr, (int)ne));
+  SPT_CUDA(ctx, launch_ep_gather(x, ctx->sel_idx.as<int32_t>(), ep->send_perm.as<int32_t>(),
+                                 ep->send_meta.as<int32_t>(), (int)K, (int)ne, (int)H, (int)S, ep->xs.as<float>(),
+                                 ep->ms.as<int32_t>(), s));
+  SPT_CUDA(ctx, launch_ep_counts(ep->send_off.as<int32_t>(), W, ep->counts.as<int32_t>(), s));
+  // 3. exchange the row counts; the one host synchronisation of the call
+  {
+    std::vector<int64_t> one(W + 1);
+    for (int j = 0; j <= W; ++j) one[j] = j;
+    if ((st = exchange(ep, ep->counts.as<int32_t>(), ep->counts.as<int32_t>() + W, 1, sizeof(int32_t), ncclInt32,
+                       one, one)))
+      return st;
+  }
+  SPT_CUDA(ctx, cudaMemcpyAsync(ep->counts_host, ep->counts.p, sizeof(int32_t) * 2 * W, cudaMemcpyDeviceToHost, s));
+  if ((st = wait_stream(ep, "row-count exchange"))) return st;
+  ep->pending = false;
+  ep->soff.assign(W + 1, 0);
+  ep->roff.assign(W + 1, 0);
+  for (int j = 0; j < W; ++j) {
+    ep->soff[j + 1] = ep->soff[j] + ep->counts_host[j];
+    ep->roff[j + 1] = ep->roff[j] + ep->counts_host[W + j];
+  }
+  const int64_t R = ep->roff[W];
+  ep_trace(ep, "counts exchanged: send %lld rows, receive %lld", (long long)ep->soff[W], (long long)R);
+  bool counts_ok = ep->soff[W] <= S;  // a rank receives up to every other rank's slots
+  for (int j = 0; j < W; ++j) counts_ok = counts_ok && ep->counts_host[j] >= 0 && ep->counts_host[W + j] >= 0;
+  if (!counts_ok) {
+    // the peers post their row exchanges next: abort so that they fail too
+    // instead of waiting for this rank
+    if (ep->comm) nccl().comm_abort(ep->comm);
+    ep->broken = true;
+    return fail(ctx, SPT_ERR_NCCL, "expert-parallel row counts out of range (sent %lld of %lld slots); group aborted",
+                (long long)ep->soff[W], (long long)S);
+  }
+  // 4. token rows and local expert ids to their owners
+  // every allocation of the call happens before the exchanges below
+  spt_moe_config lc = c;  // receive side: top-1 over this rank's experts
+  lc.num_experts = ne;
+  lc.num_experts_used = 1;
+  SPT_CUDA(ctx, ep->xr.ensure(sizeof(float) * std::max<int64_t>(R, 1) * H));
+  SPT_CUDA(ctx, ep->mr.ensure(sizeof(int32_t) * std::max<int64_t>(R, 1)));
+  SPT_CUDA(ctx, ep->rows_out.ensure(sizeof(float) * std::max<int64_t>(R, 1) * H));
+  if (R > 0 && (st = reserve_experts(ctx, L, lc, R))) return st;
+  ep_trace(ep, "buffers reserved");
+  if ((st = exchange(ep, ep->xs.p, ep->xr.p, H, sizeof(float), ncclFloat32, ep->soff, ep->roff))) return st;
+  if ((st = exchange(ep, ep->ms.p, ep->mr.p, 1, sizeof(int32_t), ncclInt32, ep->soff, ep->roff))) return st;
+  ep_trace(ep, "rows exchange enqueued");
+  // 5. expert products for the received rows: top-1 selections of weight 1
+  //    over this rank's experts, "combined" into one result row each
+  if (R > 0) {
+    SPT_CUDA(ctx, launch_fill(ctx->sel_w.as<float>(), R, 1.0f, s));
+    if ((st = experts_combine(ctx, L, lc, ep->xr.as<float>(), R, ep->mr.as<int32_t>(), ctx->sel_w.as<float>(),
+                              ep->rows_out.as<float>())))
+      return st;
+  }
+  // 6. results back to the ranks that sent the rows, then the rank-ordered
+  //    combine over this rank's slots
+  ep_trace(ep, "experts enqueued");
+  if ((st = exchange(ep, ep->rows_out.p, ep->ret.p, H, sizeof(float), ncclFloat32, ep->roff, ep->soff))) return st;
+  ep->pending = true;
+  ep_trace(ep, "results exchange enqueued");
+  const int recv_kernels = R > 0 ? 1 + ctx->kernels_last - 2 : 0;  // fill + experts_combine's (no router/select)
+  SPT_CUDA(ctx, launch_combine(ep->ret.as<float>(), ep->sel_w.as<float>(), ep->send_pos.as<int32_t>(), (int)T, (int)K,
+                               (int)H, out, s));
+  // router, select, rank grouping, gather, counts, combine + the receive side
+  ctx->kernels_last = 6 + recv_kernels;
+  return SPT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void spt_ep_expert_range(int64_t num_experts, int32_t world, int32_t rank, int64_t *begin, int64_t *end) {
+  const bool ok = world > 0 && rank >= 0 && rank < world && num_experts > 0;
+  if (begin) *begin = ok ? rank * num_experts / world : 0;
+  if (end) *end = ok ? (rank + 1) * num_experts / world : 0;
+}
+
+spt_status spt_ep_unique_id(uint8_t id[SPT_EP_UNIQUE_ID_BYTES]) {
+  if (!id) return fail(nullptr, SPT_ERR_NULL_ARG, "nil id");
+  const NcclApi &api = nccl();
+  if (!api.why.empty()) return fail(nullptr, SPT_ERR_NCCL, "%s", api.why.c_str());
+  static_assert(sizeof(ncclUniqueId) == SPT_EP_UNIQUE_ID_BYTES, "ncclUniqueId size");
+  ncclUniqueId u;
+  ncclResult_t r = api.get_unique_id(&u);
+  if (r != ncclSuccess) return fail(nullptr, SPT_ERR_NCCL, "ncclGetUniqueId: %s", api.error_string(r));
+  memcpy(id, &u, sizeof u);
+  return SPT_OK;
+}
+
+spt_status spt_ep_create(spt_context *ctx, const uint8_t id[SPT_EP_UNIQUE_ID_BYTES], int32_t rank, int32_t world,
+                         spt_ep **out) {
+  if (!ctx || !id || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  *out = nullptr;
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "rank %d of world %d", rank, world);
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  const NcclApi &api = nccl();
+  if (!api.why.empty()) return fail(ctx, SPT_ERR_NCCL, "%s", api.why.c_str());
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof u);
+  spt_ep *ep = new spt_ep();
+  ep->ctx = ctx;
+  ep->rank = rank;
+  ep->world = world;
+  if (const char *t = getenv("SPT_EP_TIMEOUT_MS")) ep->timeout_ms = std::max<int64_t>(1, atoll(t));
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  ncclResult_t r = api.comm_init_rank_config(&ep->comm, world, u, rank, &config);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    delete ep;
+    return fail(ctx, SPT_ERR_NCCL, "ncclCommInitRankConfig: %s", api.error_string(r));
+  }
+  if ((st = wait_comm(ep, "communicator set-up"))) {
+    ep->comm = nullptr;  // aborted (freed) by the wait
+    delete ep;
+    return st;
+  }
+  *out = ep;
+  return SPT_OK;
+}
+
+void spt_ep_destroy(spt_ep *ep) {
+  if (!ep) return;
+  spt_context *ctx = ep->ctx;
+  if (ctx && ctx->has_device) {
+    cudaSetDevice(ctx->device);
+    // an exchange a peer never joins is aborted after the group's timeout
+    if (ctx->stream && !ep->broken) (void)wait_stream(ep, "exchange before destroy");
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  }
+  if (ep->comm && !ep->broken) nccl().comm_destroy(ep->comm);
+  for (DevBuf *b : {&ep->sel_w, &ep->send_off, &ep->send_perm, &ep->send_pos, &ep->dest_list, &ep->send_meta,
+                    &ep->xs, &ep->ms, &ep->ret, &ep->counts, &ep->xr, &ep->mr, &ep->rows_out})
+    b->release();
+  if (ep->counts_host) cudaFreeHost(ep->counts_host);
+  delete ep;
+}
+
+spt_status spt_last_dispatch(spt_context *ctx, int64_t *active_experts, int64_t *dispatched) {
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  if (!ctx->meta.p) return fail(ctx, SPT_ERR_DIMENSIONS, "no forward call yet");
+  int32_t meta[2];
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  SPT_CUDA(ctx, cudaMemcpy(meta, ctx->meta.p, sizeof meta, cudaMemcpyDeviceToHost));
+  if (active_experts) *active_experts = meta[0];
+  if (dispatched) *dispatched = meta[1];
+  return SPT_OK;
+}
+
+spt_status spt_forward_moe_batch_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t layer,
+                                           const float *x, float *out, int64_t batch) {
+  if (!ctx || !ep || !arena || !x || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (ep->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "expert-parallel group belongs to another context");
+  if (batch <= 0 || layer < 0 || layer >= (int64_t)arena->layers.size())
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "device x and out must be 16-byte aligned");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  return forward_ep_device(ctx, ep, arena, layer, x, out, batch);
+}
+
+spt_status spt_forward_moe_batch_ep(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t layer, const float *x,
+                                    int64_t x_len, float *out, int64_t out_len, int64_t batch,
+                                    const volatile int32_t *cancel) {
+  if (!ctx || !ep || !arena) return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
+  if (ep->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "expert-parallel group belongs to another context");
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  spt_status st = check_batch(ctx, arena->cfg, x, x_len, out, out_len, batch);
+  if (st) return st;
+  if (layer < 0 || layer >= (int64_t)arena->layers.size())
+    return fail(ctx, SPT_ERR_DIMENSIONS, "layer %lld out of range", (long long)layer);
+  if ((st = require_device(ctx))) return st;
+  const size_t bytes = sizeof(float) * (size_t)x_len;
+  SPT_CUDA(ctx, ctx->xdev.ensure(bytes));
+  SPT_CUDA(ctx, ctx->outdev.ensure(bytes));
+  SPT_CUDA(ctx, cudaMemcpyAsync(ctx->xdev.p, x, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  if ((st = forward_ep_device(ctx, ep, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch)))
+    return st;
+  // bounded wait for the exchanges first: a copy into pageable host memory
+  // would block until the stream drains, however long that takes
+  if ((st = wait_stream(ep, "result exchange"))) return st;
+  ep->pending = false;
+  SPT_CUDA(ctx, cudaMemcpyAsync(out, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if ((st = check_device_error(ctx))) return st;
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  return SPT_OK;
+}
+
+}  // extern "C"

@@ -97,7 +97,15 @@ struct DispatchPlan {
 cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
                             int32_t *offsets, int32_t *perm, int32_t *slot_pos,
                             int32_t *act_list, int32_t *meta, cudaStream_t stream,
-                            const DispatchPlan *plan = nullptr);
+                            const DispatchPlan *plan = nullptr, int key_div = 1);
+// Expert-parallel helpers: gather the send rows (token of slot perm[p], local
+// expert id sel_idx % experts_per_rank) for the meta[1] dispatched slots;
+// per-rank row counts from the rank offsets; fill a float array.
+cudaError_t launch_ep_gather(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *meta,
+                             int K, int experts_per_rank, int H, int S, float *xs, int32_t *ms,
+                             cudaStream_t stream);
+cudaError_t launch_ep_counts(const int32_t *offsets, int world, int32_t *counts, cudaStream_t stream);
+cudaError_t launch_fill(float *p, int64_t n, float v, cudaStream_t stream);
 
 // Addressing of the token rows a GEMV launch reads and writes, per
 // dispatch position p of an expert segment:
@@ -140,9 +148,10 @@ cudaError_t launch_add(float *dst, const float *src, int64_t n, cudaStream_t str
 // the G8 planes (which must be zeroed beforehand).
 cudaError_t launch_repack_g8(const uint8_t *gguf, int64_t experts, int rows, int blocks,
                              uint4 *nib, uint32_t *scl, cudaStream_t stream);
-// Generate synthetic MXFP4 blocks straight into the G8 planes.
-cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int rows, int blocks,
-                            uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
+// Generate synthetic MXFP4 blocks of experts [first_expert, first_expert +
+// experts) straight into the G8 planes (expert 0 of the planes = first_expert).
+cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t first_expert, int64_t experts, int rows,
+                            int blocks, uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
                             cudaStream_t stream);
 
 // Raise a kernel's dynamic shared-memory limit once per device (the setting

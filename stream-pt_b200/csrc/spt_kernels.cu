@@ -373,6 +373,9 @@ __global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits
 // 1024 slots taken in descending order, ranked within a warp by
 // __match_any_sync and across warps by a per-warp count table.
 //
+// The sort key is sel_idx / key_div: 1 groups slots by expert; the expert-
+// parallel path passes the experts per rank, grouping slots by owner rank.
+//
 // With plan.bn > 0 the same CTA also lays out the tensor-core GEMM tiles:
 // each active expert's tokens form ceil(n/bn) token tiles, each owning one
 // 128-row activation slot (pad_off), and gate/up and down tile prefixes over
@@ -392,7 +395,8 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
                                                    int32_t *__restrict__ perm,
                                                    int32_t *__restrict__ slot_pos,
                                                    int32_t *__restrict__ act_list,
-                                                   int32_t *__restrict__ meta, DispatchPlan plan) {
+                                                   int32_t *__restrict__ meta, DispatchPlan plan,
+                                                   int key_div) {
   pdl_wait();
   pdl_trigger();
   constexpr int kScanWarps = kDispatchMaxExperts / 32;
@@ -409,7 +413,7 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
   }
   __syncthreads();
   for (int s = tid; s < S; s += blockDim.x)
-    if (!(sel_w[s] <= 0.0f)) atomicAdd(&s_cnt[sel_idx[s]], 1);
+    if (!(sel_w[s] <= 0.0f)) atomicAdd(&s_cnt[sel_idx[s] / key_div], 1);
   __syncthreads();
   int v[kVals] = {0, 0, 0, 0, 0}, inc[kVals] = {0, 0, 0, 0, 0};
   if (tid < kDispatchMaxExperts) {
@@ -477,7 +481,7 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
     bool disp = false;
     if (valid) {
       disp = !(sel_w[s] <= 0.0f);
-      e = sel_idx[s];
+      e = sel_idx[s] / key_div;
     }
     const int key = disp ? e : -1;
     const unsigned m = __match_any_sync(kFull, key);
@@ -503,6 +507,43 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
     }
     __syncthreads();
   }
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel exchange helpers.
+//
+// Send-side gather: row p of the send buffer is the token of slot perm[p]
+// (slots grouped by owner rank), with the expert id local to that rank.
+__global__ void __launch_bounds__(256) k_ep_gather(const float *__restrict__ x,
+                                                   const int32_t *__restrict__ sel_idx,
+                                                   const int32_t *__restrict__ perm,
+                                                   const int32_t *__restrict__ meta, int K,
+                                                   int experts_per_rank, int H, int S,
+                                                   float *__restrict__ xs, int32_t *__restrict__ ms) {
+  pdl_wait();
+  pdl_trigger();
+  const int n = min(meta[1], S);
+  for (int p = blockIdx.x; p < n; p += gridDim.x) {
+    const int slot = perm[p];
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(slot / K) * H);
+    float4 *dst = reinterpret_cast<float4 *>(xs + (size_t)p * H);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+    if (threadIdx.x == 0) ms[p] = sel_idx[slot] % experts_per_rank;
+  }
+}
+
+// counts[r] = offsets[r+1] - offsets[r]: rows sent to each rank.
+__global__ void k_ep_counts(const int32_t *__restrict__ offsets, int world, int32_t *__restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
+  for (int r = threadIdx.x; r < world; r += blockDim.x) counts[r] = offsets[r + 1] - offsets[r];
+}
+
+__global__ void k_fill(float *__restrict__ p, int64_t n, float v) {
+  pdl_wait();
+  pdl_trigger();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
 }
 
 // ---------------------------------------------------------------------------
@@ -733,7 +774,7 @@ __global__ void k_repack_g8(const uint8_t *__restrict__ gguf, int64_t experts, i
 }
 
 __global__ void k_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int R, int NB,
-                           uint8_t lo, uint8_t hi, uint4 *nib, uint32_t *scl) {
+                           uint8_t lo, uint8_t hi, uint64_t counter0, uint4 *nib, uint32_t *scl) {
   const int64_t total = experts * R * NB;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -742,7 +783,7 @@ __global__ void k_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int R, 
     const int r = (int)(er % R);
     const int64_t e = er / R;
     uint8_t blk[17];
-    synth_mxfp4_block(seed, tag, (uint64_t)idx, lo, hi, blk);
+    synth_mxfp4_block(seed, tag, counter0 + (uint64_t)idx, lo, hi, blk);
     block_to_g8(blk, e, r, b, R, NB, nib, scl);
   }
 }
@@ -807,10 +848,30 @@ cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel
 cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
                             int32_t *offsets, int32_t *perm, int32_t *slot_pos,
                             int32_t *act_list, int32_t *meta, cudaStream_t stream,
-                            const DispatchPlan *plan) {
-  if (E > kDispatchMaxExperts) return cudaErrorInvalidValue;
+                            const DispatchPlan *plan, int key_div) {
+  if (E > kDispatchMaxExperts || key_div < 1) return cudaErrorInvalidValue;
   return launch_pdl(k_dispatch, dim3(1), dim3(1024), 0, stream, sel_idx, sel_w, S, E, offsets, perm, slot_pos,
-                    act_list, meta, plan ? *plan : DispatchPlan{});
+                    act_list, meta, plan ? *plan : DispatchPlan{}, key_div);
+}
+
+cudaError_t launch_ep_gather(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *meta,
+                             int K, int experts_per_rank, int H, int S, float *xs, int32_t *ms,
+                             cudaStream_t stream) {
+  if (S <= 0) return cudaSuccess;
+  if (H % 4 != 0) return cudaErrorInvalidValue;
+  const int grid = S < 148 * 8 ? S : 148 * 8;
+  return launch_pdl(k_ep_gather, dim3(grid), dim3(256), 0, stream, x, sel_idx, perm, meta, K, experts_per_rank, H,
+                    S, xs, ms);
+}
+
+cudaError_t launch_ep_counts(const int32_t *offsets, int world, int32_t *counts, cudaStream_t stream) {
+  return launch_pdl(k_ep_counts, dim3(1), dim3(256), 0, stream, offsets, world, counts);
+}
+
+cudaError_t launch_fill(float *p, int64_t n, float v, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t g = (n + 255) / 256;
+  return launch_pdl(k_fill, dim3((unsigned)(g < 148 * 16 ? g : 148 * 16)), dim3(256), 0, stream, p, n, v);
 }
 
 template <int MT, bool GU>
@@ -873,13 +934,13 @@ cudaError_t launch_repack_g8(const uint8_t *gguf, int64_t experts, int rows, int
   return cudaGetLastError();
 }
 
-cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t experts, int rows, int blocks,
-                            uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
+cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t first_expert, int64_t experts, int rows,
+                            int blocks, uint8_t scale_lo, uint8_t scale_hi, uint4 *nib, uint32_t *scl,
                             cudaStream_t stream) {
   const int64_t n = experts * rows * blocks;
   if (n <= 0) return cudaSuccess;
-  k_synth_g8<<<grid_for(n, 256), 256, 0, stream>>>(seed, tag, experts, rows, blocks, scale_lo,
-                                                   scale_hi, nib, scl);
+  k_synth_g8<<<grid_for(n, 256), 256, 0, stream>>>(seed, tag, experts, rows, blocks, scale_lo, scale_hi,
+                                                   (uint64_t)(first_expert * rows * blocks), nib, scl);
   return cudaGetLastError();
 }
 

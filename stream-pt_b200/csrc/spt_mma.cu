@@ -169,7 +169,7 @@ __global__ void k_repack_mma(const uint8_t *__restrict__ src, int64_t E, int R, 
 }
 
 __global__ void k_synth_mma_gu(uint64_t seed, uint32_t tg, uint32_t tu, int64_t E, int D, int NB,
-                               uint8_t lo, uint8_t hi, int kp, uint8_t *w, uint8_t *sf) {
+                               uint8_t lo, uint8_t hi, uint64_t counter0, int kp, uint8_t *w, uint8_t *sf) {
   const int64_t total = E * D * NB;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -178,15 +178,15 @@ __global__ void k_synth_mma_gu(uint64_t seed, uint32_t tg, uint32_t tu, int64_t 
     const int d = (int)(ed % D);
     const int64_t e = ed / D;
     uint8_t blk[17];
-    synth_mxfp4_block(seed, tg, (uint64_t)idx, lo, hi, blk);
+    synth_mxfp4_block(seed, tg, counter0 + (uint64_t)idx, lo, hi, blk);
     put_mma_block(blk, e, 2 * d, b, 2 * D, kp, w, sf);
-    synth_mxfp4_block(seed, tu, (uint64_t)idx, lo, hi, blk);
+    synth_mxfp4_block(seed, tu, counter0 + (uint64_t)idx, lo, hi, blk);
     put_mma_block(blk, e, 2 * d + 1, b, 2 * D, kp, w, sf);
   }
 }
 
 __global__ void k_synth_mma(uint64_t seed, uint32_t tag, int64_t E, int R, int NB, uint8_t lo,
-                            uint8_t hi, int kp, uint8_t *w, uint8_t *sf) {
+                            uint8_t hi, uint64_t counter0, int kp, uint8_t *w, uint8_t *sf) {
   const int64_t total = E * R * NB;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -195,7 +195,7 @@ __global__ void k_synth_mma(uint64_t seed, uint32_t tag, int64_t E, int R, int N
     const int r = (int)(er % R);
     const int64_t e = er / R;
     uint8_t blk[17];
-    synth_mxfp4_block(seed, tag, (uint64_t)idx, lo, hi, blk);
+    synth_mxfp4_block(seed, tag, counter0 + (uint64_t)idx, lo, hi, blk);
     put_mma_block(blk, e, r, b, R, kp, w, sf);
   }
 }
@@ -845,17 +845,19 @@ cudaError_t launch_repack_mma(const uint8_t *src, int64_t E, int R, int K, MmaMa
   return cudaGetLastError();
 }
 
-cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tg, uint32_t tu, int64_t E, int D, int K,
-                                uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s) {
+cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tg, uint32_t tu, int64_t first_expert, int64_t E, int D,
+                                int K, uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s) {
   const int NB = K / 32;
-  k_synth_mma_gu<<<grid_of(E * D * NB), 256, 0, s>>>(seed, tg, tu, E, D, NB, lo, hi, m->kp, m->w, m->sf);
+  k_synth_mma_gu<<<grid_of(E * D * NB), 256, 0, s>>>(seed, tg, tu, E, D, NB, lo, hi,
+                                                     (uint64_t)(first_expert * D * NB), m->kp, m->w, m->sf);
   return cudaGetLastError();
 }
 
-cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t E, int R, int K, uint8_t lo,
-                             uint8_t hi, MmaMatrix *m, cudaStream_t s) {
+cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t first_expert, int64_t E, int R, int K,
+                             uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s) {
   const int NB = K / 32;
-  k_synth_mma<<<grid_of(E * R * NB), 256, 0, s>>>(seed, tag, E, R, NB, lo, hi, m->kp, m->w, m->sf);
+  k_synth_mma<<<grid_of(E * R * NB), 256, 0, s>>>(seed, tag, E, R, NB, lo, hi, (uint64_t)(first_expert * R * NB),
+                                                  m->kp, m->w, m->sf);
   return cudaGetLastError();
 }
 

@@ -120,10 +120,14 @@ cudaError_t launch_repack_mma_gu(const uint8_t *gate_gguf, const uint8_t *up_ggu
                                  int D, int K, MmaMatrix *m, cudaStream_t s);
 cudaError_t launch_repack_mma(const uint8_t *gguf, int64_t experts, int rows, int K, MmaMatrix *m,
                               cudaStream_t s);
-cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tag_gate, uint32_t tag_up, int64_t experts,
-                                int D, int K, uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
-cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t experts, int rows, int K,
-                             uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
+// Synthetic weights of experts [first_expert, first_expert + experts) (the
+// Philox counters continue from first_expert, so a shard holds the same bytes
+// as the same experts of a full arena).
+cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tag_gate, uint32_t tag_up, int64_t first_expert,
+                                int64_t experts, int D, int K, uint8_t lo, uint8_t hi, MmaMatrix *m,
+                                cudaStream_t s);
+cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t first_expert, int64_t experts, int rows,
+                             int K, uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
 
 // Quantize rows to the three MXFP8 terms.  Source row of dispatch position
 // p: src[(gather ? perm[p]/top_k : p) * src_stride + k].
