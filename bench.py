@@ -268,6 +268,7 @@ def run_ours(args):
         uid = [spt.ep_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(uid, src=0)
         ep = spt.ExpertParallel(ctx, uid[0], rank, world)
+        ep.set_capacity(T)  # fixed-capacity exchange: no host synchronisation per step
     else:
         arena = ctx.synthetic_arena(cfg, params, flags=flags)
     ctx.set_path(spt.PATH_MMA if args.path == "mma" else spt.PATH_EXACT)
@@ -383,7 +384,7 @@ def run_ours(args):
                    "expert_path": args.path,
                    "expert_dim": D, "experts": E, "top_k": K, "seed": c["seed"],
                    "parallelism": (f"ep{world}: {E // world} experts per GPU, {T} tokens per rank, NCCL "
-                                   "all-to-all dispatch/combine" if world > 1 else "single GPU"),
+                                   "all-to-all dispatch/combine (fixed capacity)" if world > 1 else "single GPU"),
                    "l2": "256 MB buffer written between timed steps",
                    "active_experts": n_active},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

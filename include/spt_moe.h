@@ -297,9 +297,16 @@ spt_status spt_ep_unique_id(uint8_t id[SPT_EP_UNIQUE_ID_BYTES]);
 spt_status spt_ep_create(spt_context *ctx, const uint8_t id[SPT_EP_UNIQUE_ID_BYTES], int32_t rank,
                          int32_t world, spt_ep **out);
 void spt_ep_destroy(spt_ep *ep);
+/* Fixed-capacity exchange for decode-sized batches: every rank sends every
+ * peer a slot of max_tokens_per_rank * top-k rows per call, with the live row
+ * count in the same NCCL group, so no count reaches the host and a call never
+ * synchronises.  Every rank must set the same value, and calls with more
+ * tokens fail with SPT_ERR_DIMENSIONS.  0 (the default) exchanges counts
+ * first and sends only live rows (one host synchronisation per call). */
+spt_status spt_ep_set_capacity(spt_ep *ep, int64_t max_tokens_per_rank);
 /* Device pointers (16-byte aligned), this rank's `batch` tokens.  Enqueues on
- * the context's stream and synchronises it once, after the per-rank row
- * counts are exchanged. */
+ * the context's stream; without a capacity it synchronises the stream once,
+ * after the per-rank row counts are exchanged. */
 spt_status spt_forward_moe_batch_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena,
                                            int64_t layer, const float *x, float *out,
                                            int64_t batch);

@@ -213,6 +213,7 @@ def lib():
         "spt_ep_unique_id": ([vp], st),
         "spt_ep_create": ([vp, vp, i32, i32, P(vp)], st),
         "spt_ep_destroy": ([vp], None),
+        "spt_ep_set_capacity": ([vp, i64], st),
         "spt_forward_moe_batch_ep_device": ([vp, vp, vp, i64, vp, vp, i64], st),
         "spt_forward_moe_batch_ep": ([vp, vp, vp, i64, vp, i64, vp, i64, i64, vp], st),
         "spt_arena_create_range": ([vp, vp, P(_Config), vp, i64, ctypes.c_uint32, i64, i64, P(vp)], st),
@@ -520,6 +521,10 @@ class ExpertParallel:
     @property
     def handle(self):
         return self._h
+
+    def set_capacity(self, max_tokens_per_rank: int):
+        """Fixed-capacity exchange (no host synchronisation); same value on every rank."""
+        self.ctx.check(lib().spt_ep_set_capacity(self._h, max_tokens_per_rank))
 
     def close(self):
         if self._h:

@@ -14,6 +14,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <initializer_list>
 #include <limits>
 #include <mutex>
 #include <string>
@@ -454,11 +455,10 @@ int pick_bn(int64_t T, int64_t K, int64_t E) { return (T * K) <= 8 * E ? 16 : 12
 // Expert GEMMs on the tensor cores (after router/select/dispatch):
 // plan -> quantize x -> gate/up GEMM (+SwiGLU) -> quantize act -> down GEMM.
 spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                       int64_t T, cudaStream_t s) {
+                       int64_t T, cudaStream_t s, int bn) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   const int64_t S = T * K;
-  const int bn = pick_bn(T, K, E);
   const int64_t na_max = std::min<int64_t>(E, S);
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
@@ -559,7 +559,8 @@ spt_status pick_path(spt_context *ctx, const LayerDev &L, bool *use_mma) {
 // allocates only here, so a caller can make the allocations before work that
 // must not overlap a cudaMalloc/cudaFree (an NCCL exchange in flight: their
 // implicit device synchronisation can deadlock against NCCL's progress).
-spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, int64_t T) {
+spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, int64_t T,
+                           int bn_hint = 0) {
   spt_status st = ensure_scratch(ctx, T, c);
   if (st) return st;
   bool use_mma = false;
@@ -570,7 +571,7 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
   SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
   SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
   SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
-  const int bn = pick_bn(T, K, E);
+  const int bn = bn_hint ? bn_hint : pick_bn(T, K, E);
   const int64_t na_max = std::min<int64_t>(E, S);
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
@@ -593,7 +594,7 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // ranks r of fma(result, weight, out[t]).  `c` gives the arena's experts
 // and top-k (the expert-parallel receive side passes its shard and top-k 1).
 spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                           int64_t T, const int32_t *sel_idx, const float *sel_w, float *out) {
+                           int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
@@ -601,10 +602,10 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   const int max_active = (int)std::min<int64_t>(E, T * K);
   bool use_mma = false;
   if ((st = pick_path(ctx, L, &use_mma))) return st;
-  if ((st = reserve_experts(ctx, L, c, T))) return st;
+  if ((st = reserve_experts(ctx, L, c, T, bn_hint))) return st;
   DispatchPlan plan;  // tensor-core tile layout, made by the dispatch kernel
   if (use_mma) {
-    plan.bn = pick_bn(T, K, E);
+    plan.bn = bn_hint ? bn_hint : pick_bn(T, K, E);
     plan.mt_gu = L.gu_mma.mtiles;
     plan.mt_dn = L.dn_mma.mtiles;
     plan.pad_off = ctx->pad_off.as<int32_t>();
@@ -618,7 +619,7 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
                                 ctx->meta.as<int32_t>(), s, use_mma ? &plan : nullptr));
   SPT_MARK(3);
   if (use_mma) {
-    if ((st = forward_mma(ctx, L, c, x, T, s))) return st;
+    if ((st = forward_mma(ctx, L, c, x, T, s, plan.bn))) return st;
   } else {
     const int mt = pick_mt(T, K, E);
     GemvLaunch gu;
@@ -1657,6 +1658,7 @@ struct spt_ep {
   ncclComm_t comm = nullptr;
   bool broken = false;   // aborted after a wait ran out; every later call fails
   bool pending = false;  // the last result exchange may still be in flight
+  int64_t cap_tokens = 0;  // > 0: fixed-capacity exchange, at most this many tokens per rank and call
   int64_t t_max = 0;     // largest batch so far (no buffer grows below it)
   int64_t timeout_ms = 60000;
   // send side (this rank's tokens)
@@ -1770,6 +1772,92 @@ void ep_trace(const spt_ep *ep, const char *fmt, ...) {
   fflush(stderr);
 }
 
+// One grouped exchange of fixed-size pieces: for every peer j and every item,
+// send `count` elements at send + j*count and receive them at recv + j*count.
+struct FixedItem {
+  const void *send;
+  void *recv;
+  size_t count, elem;
+  ncclDataType_t type;
+};
+spt_status exchange_fixed(spt_ep *ep, std::initializer_list<FixedItem> items) {
+  spt_context *ctx = ep->ctx;
+  const NcclApi &api = nccl();
+  if (ep->broken) return fail(ctx, SPT_ERR_NCCL, "expert-parallel group was aborted");
+  SPT_NCCL(ctx, api.group_start());
+  for (int j = 0; j < ep->world; ++j)
+    for (const FixedItem &it : items) {
+      SPT_NCCL(ctx, api.send(static_cast<const uint8_t *>(it.send) + (size_t)j * it.count * it.elem, it.count,
+                             it.type, j, ep->comm, ctx->stream));
+      SPT_NCCL(ctx, api.recv(static_cast<uint8_t *>(it.recv) + (size_t)j * it.count * it.elem, it.count, it.type, j,
+                             ep->comm, ctx->stream));
+    }
+  ncclResult_t r = api.group_end();
+  if (r != ncclSuccess && r != ncclInProgress)
+    return fail(ctx, SPT_ERR_NCCL, "ncclGroupEnd: %s", api.error_string(r));
+  return wait_comm(ep, "exchange");
+}
+
+// Fixed-capacity variant: every rank sends every peer a slot of cap =
+// cap_tokens * K rows (the live count travels in the same group), so no count
+// reaches the host and the call never synchronises.  The receiving rank
+// weights padding rows 0, which the dispatch kernel never dispatches.
+spt_status forward_ep_cap(spt_context *ctx, spt_ep *ep, const LayerDev &L, const spt_moe_config &c, const float *x,
+                          float *out, int64_t T) {
+  const int64_t H = c.hidden_dim, E = c.num_experts, K = c.num_experts_used;
+  const int W = ep->world;
+  const int64_t ne = E / W, cap = ep->cap_tokens * K, rows = W * cap, S = T * K;
+  cudaStream_t s = ctx->stream;
+  spt_moe_config lc = c;  // receive side: top-1 over this rank's experts
+  lc.num_experts = ne;
+  lc.num_experts_used = 1;
+  // token tiles sized for the rows a rank receives on average (its own slot count)
+  const int bn_hint = pick_bn(S, 1, ne);
+  // every buffer at its full size before anything is enqueued: none grows later
+  spt_status st = ensure_scratch(ctx, ep->cap_tokens, c);
+  if (st) return st;
+  if ((st = reserve_experts(ctx, L, lc, rows, bn_hint))) return st;
+  SPT_CUDA(ctx, ep->sel_w.ensure(sizeof(float) * cap));
+  SPT_CUDA(ctx, ep->send_off.ensure(sizeof(int32_t) * (W + 1)));
+  SPT_CUDA(ctx, ep->send_perm.ensure(sizeof(int32_t) * cap));
+  SPT_CUDA(ctx, ep->send_pos.ensure(sizeof(int32_t) * cap));
+  SPT_CUDA(ctx, ep->dest_list.ensure(sizeof(int32_t) * W));
+  SPT_CUDA(ctx, ep->send_meta.ensure(sizeof(int32_t) * 4));
+  SPT_CUDA(ctx, ep->counts.ensure(sizeof(int32_t) * 2 * W));
+  for (DevBuf *b : {&ep->xs, &ep->xr, &ep->rows_out, &ep->ret}) SPT_CUDA(ctx, b->ensure(sizeof(float) * rows * H));
+  for (DevBuf *b : {&ep->ms, &ep->mr}) SPT_CUDA(ctx, b->ensure(sizeof(int32_t) * rows));
+  ep_trace(ep, "fixed-capacity call T=%lld, %lld rows per peer", (long long)T, (long long)cap);
+  // 1. route, group by owner rank, gather into each rank's slot
+  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>()))) return st;
+  SPT_CUDA(ctx, cudaMemcpyAsync(ep->sel_w.p, ctx->sel_w.p, sizeof(float) * S, cudaMemcpyDeviceToDevice, s));
+  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)S, W,
+                                ep->send_off.as<int32_t>(), ep->send_perm.as<int32_t>(), ep->send_pos.as<int32_t>(),
+                                ep->dest_list.as<int32_t>(), ep->send_meta.as<int32_t>(), s, nullptr, (int)ne));
+  SPT_CUDA(ctx, launch_ep_gather_cap(x, ctx->sel_idx.as<int32_t>(), ep->send_perm.as<int32_t>(),
+                                     ep->send_off.as<int32_t>(), ep->send_meta.as<int32_t>(), (int)K, (int)ne, (int)H,
+                                     (int)S, W, (int)cap, ep->xs.as<float>(), ep->ms.as<int32_t>(),
+                                     ep->counts.as<int32_t>(), ep->send_pos.as<int32_t>(), s));
+  // 2. rows, local expert ids and counts to every peer, one group
+  if ((st = exchange_fixed(ep, {{ep->xs.p, ep->xr.p, (size_t)(cap * H), sizeof(float), ncclFloat32},
+                                {ep->ms.p, ep->mr.p, (size_t)cap, sizeof(int32_t), ncclInt32},
+                                {ep->counts.p, ep->counts.as<int32_t>() + W, 1, sizeof(int32_t), ncclInt32}})))
+    return st;
+  // 3. expert products for the live received rows
+  SPT_CUDA(ctx, launch_ep_recv_weights(ep->counts.as<int32_t>() + W, (int)cap, W, ctx->sel_w.as<float>(), s));
+  if ((st = experts_combine(ctx, L, lc, ep->xr.as<float>(), rows, ep->mr.as<int32_t>(), ctx->sel_w.as<float>(),
+                            ep->rows_out.as<float>(), bn_hint)))
+    return st;
+  const int recv_kernels = 1 + ctx->kernels_last - 2;  // weights + experts_combine's (no router/select)
+  // 4. result rows back into each sender's slot, rank-ordered combine
+  if ((st = exchange_fixed(ep, {{ep->rows_out.p, ep->ret.p, (size_t)(cap * H), sizeof(float), ncclFloat32}})))
+    return st;
+  ep->pending = true;
+  SPT_CUDA(ctx, launch_combine(ep->ret.as<float>(), ep->sel_w.as<float>(), ep->send_pos.as<int32_t>(), (int)T, (int)K,
+                               (int)H, out, s));
+  ctx->kernels_last = 5 + recv_kernels;  // router, select, rank grouping, gather, combine + receive side
+  return SPT_OK;
+}
+
 spt_status forward_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t layer, const float *x,
                              float *out, int64_t T) {
   const spt_moe_config &c = arena->cfg;
@@ -1788,6 +1876,12 @@ spt_status forward_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int
   cudaStream_t s = ctx->stream;
   const LayerDev &L = arena->layers[(size_t)layer];
   const int64_t S = T * K;
+  if (ep->cap_tokens > 0) {
+    if (T > ep->cap_tokens)
+      return fail(ctx, SPT_ERR_DIMENSIONS, "batch %lld exceeds the group's capacity of %lld tokens per rank",
+                  (long long)T, (long long)ep->cap_tokens);
+    return forward_ep_cap(ctx, ep, L, c, x, out, T);
+  }
   // A previous call's result exchange may still be in flight (device entry
   // point): let it finish before this call's buffers can grow.
   if (ep->pending && T > ep->t_max && (st = wait_stream(ep, "previous exchange"))) return st;
@@ -1951,6 +2045,19 @@ void spt_ep_destroy(spt_ep *ep) {
     b->release();
   if (ep->counts_host) cudaFreeHost(ep->counts_host);
   delete ep;
+}
+
+spt_status spt_ep_set_capacity(spt_ep *ep, int64_t max_tokens_per_rank) {
+  if (!ep) return fail(nullptr, SPT_ERR_NULL_ARG, "nil expert-parallel group");
+  if (max_tokens_per_rank < 0 || max_tokens_per_rank > (1 << 20))
+    return fail(ep->ctx, SPT_ERR_DIMENSIONS, "capacity %lld tokens out of range", (long long)max_tokens_per_rank);
+  if (ep->pending) {  // the previous call's buffers may still be in use
+    spt_status st = wait_stream(ep, "exchange before a capacity change");
+    if (st) return st;
+    ep->pending = false;
+  }
+  ep->cap_tokens = max_tokens_per_rank;
+  return SPT_OK;
 }
 
 spt_status spt_last_dispatch(spt_context *ctx, int64_t *active_experts, int64_t *dispatched) {

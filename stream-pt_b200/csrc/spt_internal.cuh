@@ -105,6 +105,11 @@ cudaError_t launch_ep_gather(const float *x, const int32_t *sel_idx, const int32
                              int K, int experts_per_rank, int H, int S, float *xs, int32_t *ms,
                              cudaStream_t stream);
 cudaError_t launch_ep_counts(const int32_t *offsets, int world, int32_t *counts, cudaStream_t stream);
+// Fixed-capacity exchange layout: rows for rank r at [r*cap, r*cap + count).
+cudaError_t launch_ep_gather_cap(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *offsets,
+                                 const int32_t *meta, int K, int experts_per_rank, int H, int S, int world, int cap,
+                                 float *xs, int32_t *ms, int32_t *counts, int32_t *slot_pos, cudaStream_t stream);
+cudaError_t launch_ep_recv_weights(const int32_t *counts, int cap, int world, float *w, cudaStream_t stream);
 cudaError_t launch_fill(float *p, int64_t n, float v, cudaStream_t stream);
 
 // Addressing of the token rows a GEMV launch reads and writes, per

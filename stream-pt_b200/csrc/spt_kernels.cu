@@ -532,6 +532,55 @@ __global__ void __launch_bounds__(256) k_ep_gather(const float *__restrict__ x,
   }
 }
 
+// Fixed-capacity layout (no host round trip): rank `dest`'s rows go to send
+// rows [dest*cap, dest*cap + count).  Writes the rows, their local expert
+// ids, the per-rank counts, and rewrites slot_pos (the dispatch kernel's
+// compact position) to the row in this layout.
+__global__ void __launch_bounds__(256) k_ep_gather_cap(const float *__restrict__ x,
+                                                       const int32_t *__restrict__ sel_idx,
+                                                       const int32_t *__restrict__ perm,
+                                                       const int32_t *__restrict__ offsets,
+                                                       const int32_t *__restrict__ meta, int K,
+                                                       int experts_per_rank, int H, int S, int world,
+                                                       int cap, float *__restrict__ xs,
+                                                       int32_t *__restrict__ ms, int32_t *__restrict__ counts,
+                                                       int32_t *__restrict__ slot_pos) {
+  pdl_wait();
+  pdl_trigger();
+  if (blockIdx.x == 0)
+    for (int r = threadIdx.x; r < world; r += blockDim.x) counts[r] = offsets[r + 1] - offsets[r];
+  const int n = min(meta[1], S);
+  for (int p = blockIdx.x; p < n; p += gridDim.x) {
+    int lo = 0, hi = world - 1;  // destination rank: largest r with offsets[r] <= p
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (offsets[mid] <= p) lo = mid;
+      else hi = mid - 1;
+    }
+    const int row = lo * cap + (p - offsets[lo]);
+    const int slot = perm[p];
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(slot / K) * H);
+    float4 *dst = reinterpret_cast<float4 *>(xs + (size_t)row * H);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+    if (threadIdx.x == 0) {
+      ms[row] = sel_idx[slot] % experts_per_rank;
+      slot_pos[slot] = row;
+    }
+  }
+}
+
+// Receive side of the fixed-capacity layout: row j (from rank j / cap) is
+// live when j % cap < that rank's count; live rows get weight 1, padding 0
+// (never dispatched).
+__global__ void k_ep_recv_weights(const int32_t *__restrict__ counts, int cap, int world,
+                                  float *__restrict__ w) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n = (int64_t)cap * world;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
+    w[j] = (j % cap) < counts[j / cap] ? 1.0f : 0.0f;
+}
+
 // counts[r] = offsets[r+1] - offsets[r]: rows sent to each rank.
 __global__ void k_ep_counts(const int32_t *__restrict__ offsets, int world, int32_t *__restrict__ counts) {
   pdl_wait();
@@ -862,6 +911,23 @@ cudaError_t launch_ep_gather(const float *x, const int32_t *sel_idx, const int32
   const int grid = S < 148 * 8 ? S : 148 * 8;
   return launch_pdl(k_ep_gather, dim3(grid), dim3(256), 0, stream, x, sel_idx, perm, meta, K, experts_per_rank, H,
                     S, xs, ms);
+}
+
+cudaError_t launch_ep_gather_cap(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *offsets,
+                                 const int32_t *meta, int K, int experts_per_rank, int H, int S, int world, int cap,
+                                 float *xs, int32_t *ms, int32_t *counts, int32_t *slot_pos, cudaStream_t stream) {
+  if (H % 4 != 0 || world < 1) return cudaErrorInvalidValue;
+  const int grid = S < 1 ? 1 : (S < 148 * 8 ? S : 148 * 8);
+  return launch_pdl(k_ep_gather_cap, dim3(grid), dim3(256), 0, stream, x, sel_idx, perm, offsets, meta, K,
+                    experts_per_rank, H, S, world, cap, xs, ms, counts, slot_pos);
+}
+
+cudaError_t launch_ep_recv_weights(const int32_t *counts, int cap, int world, float *w, cudaStream_t stream) {
+  const int64_t n = (int64_t)cap * world;
+  if (n <= 0) return cudaSuccess;
+  const int64_t g = (n + 255) / 256;
+  return launch_pdl(k_ep_recv_weights, dim3((unsigned)(g < 148 * 8 ? g : 148 * 8)), dim3(256), 0, stream, counts,
+                    cap, world, w);
 }
 
 cudaError_t launch_ep_counts(const int32_t *offsets, int world, int32_t *counts, cudaStream_t stream) {

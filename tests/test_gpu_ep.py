@@ -53,12 +53,14 @@ def _rank_main(rank, world, uid_q, results):
         _log(rank, "arenas ready")
         ep = spt.ExpertParallel(ctx, uid, rank, world)
         _log(rank, "group ready")
-        for call, T in enumerate(TOKENS[rank]):
+        # counts exchanged per call, then the fixed-capacity exchange
+        for mode, capacity in (("counts", 0), ("capacity", 300)):
+          ep.set_capacity(capacity)
+          for call, T in enumerate(TOKENS[rank]):
             x = spt.synth_normal_host(50 + rank, call, T * 2880)
             for path, name in ((spt.PATH_EXACT, "exact"), (spt.PATH_MMA, "mma")):
                 ctx.set_path(path)
                 got = ctx.forward_moe_batch_ep(ep, shard, x, T)
-                _log(rank, f"call {call} T={T} {name}: expert-parallel forward returned")
                 want = ctx.forward_moe_batch(full, x, T)
                 if name == "exact":
                     ok = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
@@ -66,8 +68,8 @@ def _rank_main(rank, world, uid_q, results):
                 else:
                     err = float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-30))
                     ok = bool(np.isfinite(got).all() and err <= 1e-3)
-                out[(call, name)] = (ok, err)
-                _log(rank, f"call {call} T={T} {name}: ok={ok} err={err:.3g}")
+                out[(mode, call, name)] = (ok, err)
+                _log(rank, f"{mode} call {call} T={T} {name}: ok={ok} err={err:.3g}")
         results.put((rank, out, None))
     except Exception as exc:
         _log(rank, f"error: {exc!r}")
@@ -103,4 +105,4 @@ def test_expert_parallel_matches_single_gpu():
         assert err is None, (rank, err)
         for key, (ok, e) in res.items():
             assert ok, (rank, key, e)
-        assert len(res) == 2 * len(TOKENS[rank])
+        assert len(res) == 2 * 2 * len(TOKENS[rank])
