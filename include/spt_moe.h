@@ -269,11 +269,26 @@ spt_status spt_combine_moe_batch(spt_context *ctx, const float *results, const f
 /* normBatch RMSNorm with an F32 weight vector, 8 accumulation lanes. */
 spt_status spt_rmsnorm(spt_context *ctx, const float *x, const float *weight, int64_t batch,
                        int64_t dim, float eps, float *y);
-/* MulQ80Into + MulQ80Argmax: Q8_0 matrix [output rows x input/32 34-byte
- * blocks]; y may be NULL; *argmax gets the lowest row of the maximum. */
+/* MulQ80Into + MulQ80Argmax (forward/q80.go:22-148): Q8_0 matrix [output
+ * rows x input/32 34-byte blocks] in host memory, uploaded for this call;
+ * y may be NULL; *argmax gets the lowest row of the largest logit (NaN never
+ * wins; 0 when no logit beats -Inf), *best_logit that logit. */
 spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len, int64_t input,
                        int64_t output, const float *x, float *y, int64_t *argmax,
                        float *best_logit);
+/* The same with the matrix resident in HBM: uploaded once (the reference
+ * streams it from the mmap window for every token, q80.go:86-104). */
+typedef struct spt_q80_matrix spt_q80_matrix;
+spt_status spt_q80_matrix_create(spt_context *ctx, const uint8_t *data, uint64_t data_len,
+                                 int64_t input, int64_t output, spt_q80_matrix **out);
+void spt_q80_matrix_destroy(spt_q80_matrix *m);
+/* Host x [input] / y [output] (y may be NULL), synchronous. */
+spt_status spt_mul_q80_matrix(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y,
+                              int64_t *argmax, float *best_logit);
+/* Device pointers; enqueue only.  y, argmax (one int64) and best_logit (one
+ * float) may each be NULL. */
+spt_status spt_mul_q80_matrix_device(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y,
+                                     int64_t *argmax, float *best_logit);
 
 /* ---- Expert parallelism ---------------------------------------------------
  * No counterpart in the reference, which runs the block on one host; the

@@ -208,6 +208,10 @@ def lib():
         "spt_combine_moe_batch": ([vp, vp, vp, i64, i64, i64, vp], st),
         "spt_rmsnorm": ([vp, vp, vp, i64, i64, f32, vp], st),
         "spt_mul_q80": ([vp, vp, ctypes.c_uint64, i64, i64, vp, vp, P(i64), P(f32)], st),
+        "spt_q80_matrix_create": ([vp, vp, ctypes.c_uint64, i64, i64, P(vp)], st),
+        "spt_q80_matrix_destroy": ([vp], None),
+        "spt_mul_q80_matrix": ([vp, vp, vp, vp, P(i64), P(f32)], st),
+        "spt_mul_q80_matrix_device": ([vp, vp, vp, vp, vp, vp], st),
         "spt_ep_expert_range": ([i64, i32, i32, P(i64), P(i64)], None),
         "spt_last_dispatch": ([vp, P(i64), P(i64)], st),
         "spt_ep_unique_id": ([vp], st),
@@ -489,6 +493,46 @@ class Context:
         self.check(lib().spt_mul_q80(self._h, _p(data), data.size, input_, output, _p(x), _p(y),
                                      ctypes.byref(am), ctypes.byref(best)))
         return y, am.value, np.float32(best.value)
+
+    def q80_matrix(self, data: np.ndarray, input_: int, output: int) -> "Q80Matrix":
+        """Upload a Q8_0 matrix once (spt_q80_matrix_create)."""
+        return Q80Matrix(self, data, input_, output)
+
+
+class Q80Matrix:
+    """HBM-resident Q8_0 matrix (LM head): y = W x and its argmax."""
+
+    def __init__(self, ctx: "Context", data: np.ndarray, input_: int, output: int):
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        self.ctx, self.input, self.output = ctx, input_, output
+        self._h = ctypes.c_void_p()
+        ctx.check(lib().spt_q80_matrix_create(ctx._h, _p(data), data.size, input_, output, ctypes.byref(self._h)))
+
+    def mul(self, x: np.ndarray, want_y: bool = True):
+        """(y or None, argmax row, best logit) for host x."""
+        x = _f32(x)
+        y = np.empty(self.output, np.float32) if want_y else None
+        am, best = ctypes.c_int64(), ctypes.c_float()
+        self.ctx.check(lib().spt_mul_q80_matrix(self.ctx._h, self._h, _p(x), _p(y), ctypes.byref(am),
+                                                ctypes.byref(best)))
+        return y, am.value, np.float32(best.value)
+
+    def mul_device(self, x_ptr: int, y_ptr: int = 0, argmax_ptr: int = 0, logit_ptr: int = 0):
+        self.ctx.check(lib().spt_mul_q80_matrix_device(self.ctx._h, self._h, ctypes.c_void_p(x_ptr),
+                                                       ctypes.c_void_p(y_ptr or None),
+                                                       ctypes.c_void_p(argmax_ptr or None),
+                                                       ctypes.c_void_p(logit_ptr or None)))
+
+    def close(self):
+        if self._h:
+            lib().spt_q80_matrix_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def ep_expert_range(num_experts: int, world: int, rank: int) -> Tuple[int, int]:

@@ -81,6 +81,15 @@ struct spt_context {
   } act_maps[2];
 };
 
+struct spt_q80_matrix {
+  spt_context *ctx = nullptr;
+  int64_t input = 0, output = 0;
+  DevBuf w;            // rows x input/32 x 34 bytes, + padding
+  DevBuf best, err;    // argmax key, bounded-wait flag
+  DevBuf res;          // argmax (int64) + logit (float) of the host path
+  DevBuf xdev, ydev;   // host-path staging
+};
+
 struct spt_arena {
   int device = -1;
   spt_moe_config cfg{};
@@ -1443,10 +1452,101 @@ spt_status spt_rmsnorm(spt_context *ctx, const float *x, const float *weight, in
   return SPT_OK;
 }
 
+spt_status spt_q80_matrix_create(spt_context *ctx, const uint8_t *data, uint64_t data_len, int64_t input,
+                                 int64_t output, spt_q80_matrix **out) {
+  if (!ctx || !data || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil context, data or output");
+  *out = nullptr;
+  // q80Shape (forward/q80.go:150-170)
+  if (input <= 0 || output <= 0 || input % 32 != 0)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid Q8_0 shape [%lld %lld]", (long long)input, (long long)output);
+  if (input > (1 << 24) || output > 0xffffffffll)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "matrix dimensions exceed platform limits");
+  const uint64_t row_bytes = (uint64_t)input / 32 * 34;
+  if (data_len != row_bytes * (uint64_t)output) return fail(ctx, SPT_ERR_FILE_RANGE, "invalid byte range");
+  if (q80_rows_per_chunk((int)input) <= 0)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "Q8_0 rows of %lld elements exceed the shared-memory ring", (long long)input);
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  spt_q80_matrix *m = new spt_q80_matrix();
+  m->ctx = ctx;
+  m->input = input;
+  m->output = output;
+  cudaError_t e = m->w.ensure(data_len + 64);  // the last chunk's copy rounds up to 16 bytes
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->w.p, 0, data_len + 64, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->w.p, data, data_len, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = m->best.ensure(sizeof(unsigned long long));
+  if (e == cudaSuccess) e = m->err.ensure(sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->err.p, 0, sizeof(int32_t), ctx->stream);
+  if (e == cudaSuccess) e = m->res.ensure(16);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    spt_q80_matrix_destroy(m);
+    return cuda_fail(ctx, e, "Q8_0 matrix upload");
+  }
+  *out = m;
+  return SPT_OK;
+}
+
+void spt_q80_matrix_destroy(spt_q80_matrix *m) {
+  if (!m) return;
+  if (m->ctx && m->ctx->has_device) {
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+  }
+  for (DevBuf *b : {&m->w, &m->best, &m->err, &m->res, &m->xdev, &m->ydev}) b->release();
+  delete m;
+}
+
+spt_status spt_mul_q80_matrix_device(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y, int64_t *argmax,
+                                     float *best_logit) {
+  if (!ctx || !m || !x) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (m->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "Q8_0 matrix belongs to another context");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  SPT_CUDA(ctx, launch_q80(m->w.as<uint8_t>(), m->output, (int)m->input, x, y, m->best.as<unsigned long long>(),
+                           argmax, best_logit, m->err.as<int32_t>(), ctx->sm_count, ctx->stream));
+  ctx->kernels_last = 3;  // key init, GEMV, decode
+  return SPT_OK;
+}
+
+spt_status spt_mul_q80_matrix(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y, int64_t *argmax,
+                              float *best_logit) {
+  if (!ctx || !m || !x) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (m->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "Q8_0 matrix belongs to another context");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  cudaStream_t s = ctx->stream;
+  SPT_CUDA(ctx, m->xdev.ensure(sizeof(float) * m->input));
+  if (y) SPT_CUDA(ctx, m->ydev.ensure(sizeof(float) * m->output));
+  SPT_CUDA(ctx, cudaMemcpyAsync(m->xdev.p, x, sizeof(float) * m->input, cudaMemcpyHostToDevice, s));
+  int64_t *d_arg = m->res.as<int64_t>();
+  float *d_logit = reinterpret_cast<float *>(m->res.as<uint8_t>() + 8);
+  if ((st = spt_mul_q80_matrix_device(ctx, m, m->xdev.as<float>(), y ? m->ydev.as<float>() : nullptr, d_arg,
+                                      d_logit)))
+    return st;
+  if (y) SPT_CUDA(ctx, cudaMemcpyAsync(y, m->ydev.p, sizeof(float) * m->output, cudaMemcpyDeviceToHost, s));
+  uint8_t res[16];
+  SPT_CUDA(ctx, cudaMemcpyAsync(res, m->res.p, 16, cudaMemcpyDeviceToHost, s));
+  int32_t err = 0;
+  SPT_CUDA(ctx, cudaMemcpyAsync(&err, m->err.p, sizeof err, cudaMemcpyDeviceToHost, s));
+  SPT_CUDA(ctx, cudaStreamSynchronize(s));
+  if (err) {
+    SPT_CUDA(ctx, cudaMemset(m->err.p, 0, sizeof err));
+    return fail(ctx, SPT_ERR_TIMEOUT, "Q8_0 GEMV: bounded wait gave up");
+  }
+  if (argmax) memcpy(argmax, res, 8);
+  if (best_logit) memcpy(best_logit, res + 8, 4);
+  return SPT_OK;
+}
+
 spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len, int64_t input,
                        int64_t output, const float *x, float *y, int64_t *argmax, float *best_logit) {
-  (void)data; (void)data_len; (void)input; (void)output; (void)x; (void)y; (void)argmax; (void)best_logit;
-  return fail(ctx, SPT_ERR_UNSUPPORTED, "Q8_0 LM-head kernel not built in this version");
+  spt_q80_matrix *m = nullptr;
+  spt_status st = spt_q80_matrix_create(ctx, data, data_len, input, output, &m);
+  if (st) return st;
+  st = spt_mul_q80_matrix(ctx, m, x, y, argmax, best_logit);
+  spt_q80_matrix_destroy(m);
+  return st;
 }
 
 }  // extern "C"

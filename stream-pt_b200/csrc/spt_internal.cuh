@@ -195,4 +195,12 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Q8_0 GEMV + argmax (spt_q80.cu): y[r] = dot(row r, x) for `rows` rows of
+// input/32 34-byte blocks (w padded by >= 16 bytes); best = packed argmax
+// key, decoded into argmax/logit (either may be null).
+cudaError_t launch_q80(const uint8_t *w, int64_t rows, int input, const float *x, float *y,
+                       unsigned long long *best, int64_t *argmax, float *logit, int32_t *err, int sm_count,
+                       cudaStream_t stream);
+int q80_rows_per_chunk(int input);
+
 }  // namespace spt

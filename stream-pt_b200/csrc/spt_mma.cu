@@ -22,6 +22,7 @@
 
 #include "spt_device.cuh"
 #include "spt_mma.cuh"
+#include "spt_ptx.cuh"
 #include "spt_internal.cuh"
 #include "spt_philox.h"
 
@@ -312,53 +313,7 @@ __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
 }
 
 // ---------------------------------------------------------------------------
-// PTX helpers (sm_100a).
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: gives up after ~2^31 clock cycles (about a second at the
-// B200's clock) and records `code` in err.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
-  if (mbar_try(bar, parity)) return true;
-  const long long t0 = clock64();
-  for (uint32_t i = 0;; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*(volatile int32_t *)err != 0) return false;  // another role already gave up
-      if (clock64() - t0 > (1ll << 31)) {
-        atomicCAS(err, 0, code);
-        return false;
-      }
-    }
-  }
-}
+// GEMM-specific PTX helpers (sm_100a); the generic ones are in spt_ptx.cuh.
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, void *dst, uint64_t *bar, int c0,
                                             int c1) {
@@ -392,13 +347,6 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes
                : "memory");
 }
 
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -13,6 +13,7 @@ takes:
 from __future__ import annotations
 
 import importlib
+import struct
 import os
 import sys
 
@@ -177,3 +178,37 @@ def bits_equal(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     a = np.asarray(a, np.float32)
     b = np.asarray(b, np.float32)
     return (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
+
+
+# ---- Q8_0 fixtures (tests/testdata/forward/quant_optimization_test.go:25-55,
+# 115-125; sampling_test.go:179-185) ----------------------------------------
+_Q80_SCALES = (0x3C00, 0xB800, 0x3400, 0x0001, 0x03FF, 0x0400, 0x7BFF, 0x8000)
+
+
+def q80_fixture(input_, output, x_kind="opt"):
+    """quantOptimizationFixture(8, input, output) bytes and the test's x."""
+    nb = input_ // 32 * output
+    data = np.zeros(nb * 34, np.uint8)
+    for block in range(nb):
+        b = data[block * 34:(block + 1) * 34]
+        b[0:2] = np.frombuffer(struct.pack("<H", _Q80_SCALES[block % len(_Q80_SCALES)]), np.uint8)
+        for i in range(2, 34):
+            b[i] = (block * 13 + i * 7) & 0xFF
+    i = np.arange(input_)
+    if x_kind == "opt":
+        x = ((i % 23 - 11) / 32).astype(np.float32)
+    else:
+        x = ((i % 7 - 3) / 8).astype(np.float32)
+    return data, x
+
+
+def q80_reference_dot(row, x):
+    """referenceQ80Optimization: sequential float32 sum of scale*q*x."""
+    s = np.float32(0)
+    for block in range(len(row) // 34):
+        b = row[block * 34:(block + 1) * 34]
+        scale = np.frombuffer(bytes(b[0:2]), np.float16)[0].astype(np.float32)
+        q = b[2:].view(np.int8).astype(np.float32)
+        for i in range(32):
+            s = np.float32(s + np.float32(np.float32(scale * q[i]) * x[block * 32 + i]))
+    return s
