@@ -48,7 +48,10 @@ CONFIGS = {
                desc="prefill batch T=32 (BASELINE configs[1])"),
     "c2": dict(T=2048, seed=2, zipf_s=1.1, zipf_beta=0.9, router_bias=True,
                desc="prefill T=2048, Zipf(1.1)-skewed router bias (BASELINE configs[2])"),
+    "c4": dict(T=64, seed=4, zipf_s=0.0, zipf_beta=0.0, router_bias=True, layers=36,
+               desc="36-layer stack, RMSNorm + MoE + residual per layer, 64 token rows (BASELINE configs[4])"),
 }
+EPS = 1e-5
 
 
 def load_peaks():
@@ -207,21 +210,33 @@ def cpu_baseline(cfg_name, seconds=12.0, workers=None):
     host = spt.synth_layer_host(cfg, params)
     w = oracle.Weights(H, D, E, K, host["router"], host["router_bias"], host["gate"], host["up"],
                        host["down"], host["gate_bias"], host["up_bias"], host["down_bias"])
+    norm = spt.synth_norm_host(params, 0, H)
+    layers = c.get("layers", 1)
     workers = workers or os.cpu_count() or 1
     T = c["T"]
-    # bounded sample: at most 64 tokens of the workload per repetition
+    # bounded sample: at most 64 tokens of the workload per repetition, one
+    # layer (a stack's time is the per-layer time times its depth)
     Ts = min(T, 64)
     x = spt.synth_normal_host(c["seed"], 1000, Ts * H)
-    oracle.forward_moe_batch(w, x, Ts, workers)  # warm
+
+    def one():
+        xin = oracle.rmsnorm(x, norm, Ts, H, EPS) if layers > 1 else x
+        out = oracle.forward_moe_batch(w, xin, Ts, workers)
+        if layers > 1:
+            out = out + x.reshape(Ts, H)
+        return out
+
+    one()  # warm
     reps, t0 = 0, time.perf_counter()
     while True:
-        oracle.forward_moe_batch(w, x, Ts, workers)
+        one()
         reps += 1
         el = time.perf_counter() - t0
         if el >= seconds or reps >= 1000:
             break
-    tps = reps * Ts / el
-    return tps, workers, f"{reps} x {Ts} tokens of {cfg_name} ({el:.1f} s, memory-resident weights)"
+    tps = reps * Ts / el / layers
+    what = f"{reps} x {Ts} tokens x 1 of {layers} layers" if layers > 1 else f"{reps} x {Ts} tokens"
+    return tps, workers, f"{what} of {cfg_name} ({el:.1f} s, memory-resident weights)"
 
 
 def run_reference(args):
@@ -258,19 +273,20 @@ def run_ours(args):
                              router_bias=c["router_bias"])
     ctx = spt.Context(local)
     flags = spt.ARENA_MMA if args.path == "mma" else spt.ARENA_GEMV
+    layers = c.get("layers", 1)
     ep = None
     if world > 1:
         # expert parallelism: this rank holds experts [r*E/N, (r+1)*E/N) and
         # the whole router; token rows cross NVLink through the library's NCCL
         # exchange (the id of its communicator comes from rank 0)
         experts = spt.ep_expert_range(E, world, rank)
-        arena = ctx.synthetic_arena(cfg, params, flags=flags, experts=experts)
+        arena = ctx.synthetic_arena(cfg, params, n_layers=layers, flags=flags, experts=experts)
         uid = [spt.ep_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(uid, src=0)
         ep = spt.ExpertParallel(ctx, uid[0], rank, world)
         ep.set_capacity(T)  # fixed-capacity exchange: no host synchronisation per step
     else:
-        arena = ctx.synthetic_arena(cfg, params, flags=flags)
+        arena = ctx.synthetic_arena(cfg, params, n_layers=layers, flags=flags)
     ctx.set_path(spt.PATH_MMA if args.path == "mma" else spt.PATH_EXACT)
     stream = torch.cuda.ExternalStream(ctx.stream)
     x_host = spt.synth_normal_host(c["seed"] + 7919 * rank, 1000, T * H)
@@ -279,13 +295,21 @@ def run_ours(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
 
     def step():
-        if ep is not None:
+        if layers > 1:
+            # the stack updates the residual stream in place: every step starts
+            # from the same input rows (a 737 KB device copy, part of the step)
+            with torch.cuda.stream(stream):
+                out_dev.copy_(x_dev)
+            ctx.forward_stack_device(arena, out_dev.data_ptr(), T, eps=EPS, ep=ep)
+        elif ep is not None:
             ctx.forward_moe_batch_ep_device(ep, arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
         else:
             ctx.forward_moe_batch_device(arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
 
     def host_call(xn, on):
-        if ep is not None:
+        if layers > 1:
+            ctx.forward_stack(arena, xn, T, eps=EPS, ep=ep, out=on)
+        elif ep is not None:
             ctx.forward_moe_batch_ep(ep, arena, xn, T, out=on)
         else:
             ctx.forward_moe_batch(arena, xn, T, out=on)
@@ -373,14 +397,14 @@ def run_ours(args):
     dn_bytes = n_active * MATRIX_BYTES
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     stages_avg = {k: round(sum(s[k] for s in stage_ms) / len(stage_ms), 5) for k in stage_ms[0]} if stage_ms else {}
-    step_bytes = ROUTER_BYTES + 3 * n_active * MATRIX_BYTES
+    step_bytes = layers * (ROUTER_BYTES + 3 * n_active * MATRIX_BYTES)  # n_active of the last layer
     line = {
         "metric": "moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": mma_dtype(T) if args.path == "mma" else "f32 (mxfp4 weights)",
         "data": "synthetic",
-        "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H,
+        "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H, "layers": layers,
                    "expert_path": args.path,
                    "expert_dim": D, "experts": E, "top_k": K, "seed": c["seed"],
                    "parallelism": (f"ep{world}: {E // world} experts per GPU, {T} tokens per rank, NCCL "
@@ -419,19 +443,106 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+Q80_ROWS, Q80_IN = 201088, 2880  # GPT-OSS output head (vocabulary x hidden)
+
+
+def run_q80(args):
+    """--config q80: the Q8_0 LM head (MulQ80Argmax, forward/q80.go:22-105),
+    one token per step: argmax over W x for a 201,088 x 2,880 Q8_0 matrix
+    resident in HBM.  Synthetic bytes (uniform int8, float16 scales
+    N(0, 0.01)); 615 MB per step, larger than L2."""
+    import torch
+    rank, world, local = dist_info()
+    torch.cuda.set_device(local)
+    spt = importlib.import_module("stream-pt_b200")
+    rng = np.random.default_rng(80)
+    nb = Q80_IN // 32
+    data = rng.integers(0, 256, size=(Q80_ROWS, nb, 34), dtype=np.uint8)
+    data[:, :, :2] = (rng.standard_normal((Q80_ROWS, nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(
+        Q80_ROWS, nb, 2)
+    data = data.reshape(-1)
+    ctx = spt.Context(local)
+    m = ctx.q80_matrix(data, Q80_IN, Q80_ROWS)
+    x_host = spt.synth_normal_host(80, 1, Q80_IN)
+    x_dev = torch.from_numpy(x_host).to(f"cuda:{local}")
+    res = torch.zeros(2, dtype=torch.int64, device=f"cuda:{local}")
+    stream = torch.cuda.ExternalStream(ctx.stream)
+
+    def step():
+        m.mul_device(x_dev.data_ptr(), 0, res.data_ptr(), res.data_ptr() + 8)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                starts[i].record(stream)
+                step()
+                ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    e_ms = []
+    for i in range(args.warmup + args.steps):
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record(stream)
+        _, idx, logit = m.mul(x_host, want_y=False)
+        en.record(stream)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            e_ms.append(st.elapsed_time(en))
+    e2e_ms = sum(e_ms) / len(e_ms)
+    peak, peak_src = load_peaks()
+    nbytes = Q80_ROWS * nb * 34
+    line = {"metric": "lm_head_tokens_per_s", "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights x f32 -> f32 (CUDA cores, bit-exact)",
+            "data": "synthetic",
+            "config": {"workload": "q80: Q8_0 LM head argmax, 201088 x 2880 (north_star q80.go)",
+                       "rows": Q80_ROWS, "input": Q80_IN, "l2": "615 MB matrix > L2"},
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "kernel": "k_q80_gemv",
+                         "algorithmic_bytes": nbytes, "avg_ms": ms, "peak_source": peak_src},
+            "e2e": {"value": 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": Q80_IN * 4,
+                    "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps * 3, "argmax": int(idx), "clocks": clocks.summary()}
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+        workers = os.cpu_count() or 1
+        oracle.mul_q80(data, Q80_IN, Q80_ROWS, x_host, workers)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 and reps < 100:
+            oracle.mul_q80(data, Q80_IN, Q80_ROWS, x_host, workers)
+            reps += 1
+        el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": reps / el, "unit": "tokens/s", "cores": workers, "kind": "port",
+                                "sample": f"{reps} full passes over the head ({el:.1f} s)"}
+    print(json.dumps(line), flush=True)
+    m.close()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["q80"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="mma", choices=["mma", "exact"],
                     help="expert GEMMs on tcgen05 (mma) or the bit-exact CUDA-core GEMV (exact)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
+    if args.config == "q80":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the q80 mode times the LM head only through "
+                              "its cpu_baseline (the oracle port) in the same line"}), flush=True)
+        else:
+            run_q80(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -88,6 +88,10 @@ typedef struct spt_layer_weights {
   spt_tensor ffn_gate_exps, ffn_gate_exps_bias;
   spt_tensor ffn_up_exps, ffn_up_exps_bias;
   spt_tensor ffn_down_exps, ffn_down_exps_bias;
+  /* LayerWeights.PostAttnNorm (blk.N.post_attention_norm.weight, F32, F16 or
+   * BF16 [hidden]): the RMSNorm in front of the block (layer_batch.go:102).
+   * Optional; only the layer-stack entry points use it. */
+  spt_tensor post_attention_norm;
 } spt_layer_weights;
 
 typedef struct spt_context spt_context;
@@ -289,6 +293,24 @@ spt_status spt_mul_q80_matrix(spt_context *ctx, spt_q80_matrix *m, const float *
  * float) may each be NULL. */
 spt_status spt_mul_q80_matrix_device(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y,
                                      int64_t *argmax, float *best_logit);
+
+/* ---- Layer stack -------------------------------------
+ * The MoE half of forwardLayerBatch (forward/layer_batch.go:102-120) over
+ * layers [first_layer, first_layer + n_layers): for each layer,
+ *   normed = normBatch(post_attention_norm, x, eps)  (8 lanes, layer_batch.go:139-195)
+ *   ffn    = the MoE block of `normed`
+ *   x     += ffn                                     (addVector, layer.go:305-340)
+ * x is the residual stream, updated in place.  `ep` may be NULL; otherwise
+ * every layer's block runs expert-parallel (the arena is this rank's shard).
+ * Synthetic arenas carry N(1, 0.02) norm weights (spt_synth_norm_host). */
+spt_status spt_forward_stack_device(spt_context *ctx, struct spt_ep *ep, spt_arena *arena,
+                                    int64_t first_layer, int64_t n_layers, float *x, int64_t batch,
+                                    float eps);
+spt_status spt_forward_stack(spt_context *ctx, struct spt_ep *ep, spt_arena *arena, int64_t first_layer,
+                             int64_t n_layers, float *x, int64_t x_len, int64_t batch, float eps,
+                             const volatile int32_t *cancel);
+/* Host copy of a synthetic layer's norm weights [dim]. */
+spt_status spt_synth_norm_host(const spt_synth_params *params, int64_t layer, int64_t dim, float *out);
 
 /* ---- Expert parallelism ---------------------------------------------------
  * No counterpart in the reference, which runs the block on one host; the

@@ -62,7 +62,7 @@ class _Config(ctypes.Structure):
 class _LayerWeights(ctypes.Structure):
     _fields_ = [(n, _Tensor) for n in (
         "ffn_gate_inp", "ffn_gate_inp_bias", "ffn_gate_exps", "ffn_gate_exps_bias",
-        "ffn_up_exps", "ffn_up_exps_bias", "ffn_down_exps", "ffn_down_exps_bias")]
+        "ffn_up_exps", "ffn_up_exps_bias", "ffn_down_exps", "ffn_down_exps_bias", "post_attention_norm")]
 
 
 class _SynthParams(ctypes.Structure):
@@ -124,6 +124,7 @@ class LayerWeights:
     ffn_up_exps_bias: Tensor = field(default_factory=Tensor)
     ffn_down_exps: Tensor = field(default_factory=Tensor)
     ffn_down_exps_bias: Tensor = field(default_factory=Tensor)
+    post_attention_norm: Tensor = field(default_factory=Tensor)
 
     def _c(self) -> _LayerWeights:
         lw = _LayerWeights()
@@ -208,6 +209,9 @@ def lib():
         "spt_combine_moe_batch": ([vp, vp, vp, i64, i64, i64, vp], st),
         "spt_rmsnorm": ([vp, vp, vp, i64, i64, f32, vp], st),
         "spt_mul_q80": ([vp, vp, ctypes.c_uint64, i64, i64, vp, vp, P(i64), P(f32)], st),
+        "spt_forward_stack_device": ([vp, vp, vp, i64, i64, vp, i64, f32], st),
+        "spt_forward_stack": ([vp, vp, vp, i64, i64, vp, i64, i64, f32, vp], st),
+        "spt_synth_norm_host": ([P(_SynthParams), i64, i64, vp], st),
         "spt_q80_matrix_create": ([vp, vp, ctypes.c_uint64, i64, i64, P(vp)], st),
         "spt_q80_matrix_destroy": ([vp], None),
         "spt_mul_q80_matrix": ([vp, vp, vp, vp, P(i64), P(f32)], st),
@@ -357,6 +361,29 @@ class Context:
         a, d = ctypes.c_int64(), ctypes.c_int64()
         self.check(lib().spt_last_dispatch(self._h, ctypes.byref(a), ctypes.byref(d)))
         return a.value, d.value
+
+    # ---- layer stack ---------------------------------------------------------
+    def forward_stack(self, arena: "Arena", x: np.ndarray, batch: int, first_layer: int = 0,
+                      n_layers: Optional[int] = None, eps: float = 1e-5,
+                      ep: Optional["ExpertParallel"] = None, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Residual stream after layers [first, first+n): x += MoE(RMSNorm(x)).
+        Returns a new array, or `out` (float32, x's size) filled in place."""
+        if out is None:
+            x = np.array(_f32(x), copy=True)
+        else:
+            np.copyto(out.reshape(-1), np.asarray(x, np.float32).reshape(-1))
+            x = out
+        n = arena.n_layers - first_layer if n_layers is None else n_layers
+        self.check(lib().spt_forward_stack(self._h, ep.handle if ep else None, arena.handle, first_layer, n, _p(x),
+                                           x.size, batch, eps, None))
+        return x
+
+    def forward_stack_device(self, arena: "Arena", x_ptr: int, batch: int, first_layer: int = 0,
+                             n_layers: Optional[int] = None, eps: float = 1e-5,
+                             ep: Optional["ExpertParallel"] = None):
+        n = arena.n_layers - first_layer if n_layers is None else n_layers
+        self.check(lib().spt_forward_stack_device(self._h, ep.handle if ep else None, arena.handle, first_layer, n,
+                                                  ctypes.c_void_p(x_ptr), batch, eps))
 
     # ---- expert parallelism ------------------------------------------------
     def forward_moe_batch_ep(self, ep: "ExpertParallel", arena: "Arena", x: np.ndarray, batch: int,
@@ -627,6 +654,16 @@ def synth_layer_host(cfg: Config, params: SynthParams, layer: int = 0) -> dict:
         raise SptError(st, lib().spt_last_error(None).decode())
     return dict(router=router, router_bias=rb, gate=gate, up=up, down=down, gate_bias=gb,
                 up_bias=ub, down_bias=db)
+
+
+def synth_norm_host(params: SynthParams, layer: int, dim: int) -> np.ndarray:
+    """Norm weights [dim] of a synthetic layer (same values as the arena's)."""
+    out = np.empty(dim, np.float32)
+    p = params._c()
+    st = lib().spt_synth_norm_host(ctypes.byref(p), layer, dim, _p(out))
+    if st != OK:
+        raise SptError(st, lib().spt_last_error(None).decode())
+    return out
 
 
 def synth_normal_host(seed: int, stream: int, n: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:

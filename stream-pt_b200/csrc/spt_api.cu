@@ -72,6 +72,7 @@ struct spt_context {
   int path = SPT_PATH_AUTO;
   int kernels_last = 0;
   DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
+  DevBuf stack_norm, stack_ffn;  // layer stack: normed rows and block output [T][H]
   int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
   // activation tensor maps of the last call (re-encoded when the buffers or shape change)
   struct ActMaps {
@@ -102,6 +103,8 @@ struct spt_arena {
 };
 
 namespace {
+
+constexpr float kSynthNormStd = 0.02f;  // RMSNorm weights ~ N(1, 0.02)
 
 spt_status fail(spt_context *ctx, spt_status st, const char *fmt, ...) {
   char buf[512];
@@ -212,6 +215,16 @@ spt_status validate_layer(spt_context *ctx, const spt_reader *reader, const spt_
   if ((st = validate_bias(ctx, lw->ffn_gate_exps_bias, d, e))) return st;
   if ((st = validate_bias(ctx, lw->ffn_up_exps_bias, d, e))) return st;
   if ((st = validate_bias(ctx, lw->ffn_down_exps_bias, h, e))) return st;
+  // normBatch weight (layer_batch.go:145-155): F32, F16 or BF16 (tag 28), 1-D [hidden]
+  if (named(lw->post_attention_norm)) {
+    const spt_tensor &t = lw->post_attention_norm;
+    const int64_t width = t.type == 0 ? 4 : 2;
+    if (t.type != 0 && t.type != 1 && t.type != 28)
+      return fail(ctx, SPT_ERR_BIAS, "\"%s\": unsupported normalization weight type %u", tname(t), t.type);
+    if (t.n_dims != 1 || t.shape[0] != (uint64_t)h || t.end < t.start || t.end - t.start != (uint64_t)(h * width))
+      return fail(ctx, SPT_ERR_BIAS, "\"%s\": invalid float vector shape or range", tname(t));
+    if ((st = validate_file_range(ctx, reader, t))) return st;
+  }
   // readFloatVector on the router bias needs a 1-D [E] tensor (layer.go:285-289)
   if (named(lw->ffn_gate_inp_bias) && lw->ffn_gate_inp_bias.n_dims != 1)
     return fail(ctx, SPT_ERR_BIAS, "\"%s\": invalid float vector shape or range",
@@ -840,7 +853,8 @@ void spt_context_destroy(spt_context *ctx) {
     for (DevBuf *b : {&ctx->logits, &ctx->sel_idx, &ctx->sel_w, &ctx->offsets, &ctx->perm,
                       &ctx->slot_pos, &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res,
                       &ctx->xdev, &ctx->outdev, &ctx->dev_err, &ctx->pad_off, &ctx->tile_gu,
-                      &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa})
+                      &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa,
+                      &ctx->stack_norm, &ctx->stack_ffn})
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
@@ -940,6 +954,12 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
     if (named(w.ffn_gate_inp_bias))
       decode_floats(r.base + w.ffn_gate_inp_bias.start, w.ffn_gate_inp_bias.type, E, tmp.data());
     if ((st = upload_floats(ctx, a, tmp.data(), (size_t)E, &L.router_bias))) break;
+    if (named(w.post_attention_norm)) {
+      tmp.assign((size_t)H, 0.0f);
+      const uint32_t ty = w.post_attention_norm.type == 28 ? 30u : w.post_attention_norm.type;  // RMSNorm's BF16 tag
+      decode_floats(r.base + w.post_attention_norm.start, ty, H, tmp.data());
+      if ((st = upload_floats(ctx, a, tmp.data(), (size_t)H, &L.norm))) break;
+    }
     struct {
       const spt_tensor *t;
       int64_t dim;
@@ -1045,6 +1065,9 @@ static spt_status synth_create_impl(spt_context *ctx, const spt_moe_config *cfg,
     tmp.resize((size_t)E);
     synth_router_bias(cfg, p, l, tmp.data());
     if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), &L.router_bias))) break;
+    tmp.resize((size_t)H);
+    synth_normal(p->seed, synth_tag(l, kSynthNormWeight), 1.0f, kSynthNormStd, tmp.data(), H);
+    if ((st = upload_floats(ctx, a, tmp.data(), tmp.size(), &L.norm))) break;
     struct {
       uint32_t kind;
       int64_t dim;
@@ -1168,6 +1191,12 @@ spt_status spt_synth_layer_host(const spt_moe_config *cfg, const spt_synth_param
     for (int64_t i = 0; i < n; ++i)
       synth_mxfp4_block(p->seed, synth_tag(layer, m.kind), (uint64_t)i, p->scale_lo, p->scale_hi, m.dst + 17 * i);
   }
+  return SPT_OK;
+}
+
+spt_status spt_synth_norm_host(const spt_synth_params *p, int64_t layer, int64_t dim, float *out) {
+  if (!p || !out || dim <= 0) return fail(nullptr, SPT_ERR_NULL_ARG, "nil argument");
+  synth_normal(p->seed, synth_tag(layer, kSynthNormWeight), 1.0f, kSynthNormStd, out, dim);
   return SPT_OK;
 }
 
@@ -2207,6 +2236,89 @@ spt_status spt_forward_moe_batch_ep(spt_context *ctx, spt_ep *ep, spt_arena *are
   if ((st = wait_stream(ep, "result exchange"))) return st;
   ep->pending = false;
   SPT_CUDA(ctx, cudaMemcpyAsync(out, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if ((st = check_device_error(ctx))) return st;
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  return SPT_OK;
+}
+
+}  // extern "C"
+
+// =========================================================================
+// Layer stack: the MoE half of forwardLayerBatch (forward/layer_batch.go:
+// 102-120) repeated over consecutive layers on the residual stream x.
+namespace {
+
+spt_status forward_stack_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t first, int64_t n, float *x,
+                                int64_t T, float eps) {
+  const spt_moe_config &c = arena->cfg;
+  const int64_t H = c.hidden_dim;
+  if (first < 0 || n <= 0 || first + n > (int64_t)arena->layers.size())
+    return fail(ctx, SPT_ERR_DIMENSIONS, "layers [%lld, %lld) outside the arena's %zu", (long long)first,
+                (long long)(first + n), arena->layers.size());
+  if (!(eps >= 0.0f) || isinf(eps)) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid epsilon: %g", (double)eps);
+  for (int64_t l = first; l < first + n; ++l)
+    if (!arena->layers[(size_t)l].norm)
+      return fail(ctx, SPT_ERR_BIAS, "layer %lld has no post-attention norm weights", (long long)l);
+  // both buffers exist before any work is enqueued; growing them while an
+  // expert-parallel exchange is in flight could deadlock, so wait for it first
+  const size_t need = sizeof(float) * (size_t)(T * H);
+  if (ep && ep->pending && (ctx->stack_norm.bytes < need || ctx->stack_ffn.bytes < need)) {
+    spt_status st = wait_stream(ep, "previous exchange");
+    if (st) return st;
+    ep->pending = false;
+  }
+  SPT_CUDA(ctx, ctx->stack_norm.ensure(need));
+  SPT_CUDA(ctx, ctx->stack_ffn.ensure(need));
+  float *normed = ctx->stack_norm.as<float>(), *ffn = ctx->stack_ffn.as<float>();
+  int kernels = 0;
+  for (int64_t l = first; l < first + n; ++l) {
+    const LayerDev &L = arena->layers[(size_t)l];
+    SPT_CUDA(ctx, launch_rmsnorm(x, L.norm, (int)T, (int)H, eps, normed, 8, ctx->stream));
+    spt_status st = ep ? forward_ep_device(ctx, ep, arena, l, normed, ffn, T)
+                       : forward_device(ctx, arena, l, normed, ffn, T);
+    if (st) return st;
+    SPT_CUDA(ctx, launch_add(x, ffn, T * H, ctx->stream));
+    kernels += 2 + ctx->kernels_last;
+  }
+  ctx->kernels_last = kernels;
+  return SPT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+spt_status spt_forward_stack_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t first_layer,
+                                    int64_t n_layers, float *x, int64_t batch, float eps) {
+  if (!ctx || !arena || !x) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (ep && ep->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "expert-parallel group belongs to another context");
+  if (batch <= 0) return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(ctx, SPT_ERR_DIMENSIONS, "device x must be 16-byte aligned");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  return forward_stack_device(ctx, ep, arena, first_layer, n_layers, x, batch, eps);
+}
+
+spt_status spt_forward_stack(spt_context *ctx, spt_ep *ep, spt_arena *arena, int64_t first_layer, int64_t n_layers,
+                             float *x, int64_t x_len, int64_t batch, float eps, const volatile int32_t *cancel) {
+  if (!ctx || !arena || !x) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (ep && ep->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "expert-parallel group belongs to another context");
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  int64_t n = 0;
+  if (batch <= 0 || !product({batch, arena->cfg.hidden_dim}, &n) || x_len != n)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid MoE batch dimensions");
+  spt_status st = require_device(ctx);
+  if (st) return st;
+  const size_t bytes = sizeof(float) * (size_t)x_len;
+  SPT_CUDA(ctx, ctx->xdev.ensure(bytes));
+  SPT_CUDA(ctx, cudaMemcpyAsync(ctx->xdev.p, x, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  if ((st = forward_stack_device(ctx, ep, arena, first_layer, n_layers, ctx->xdev.as<float>(), batch, eps))) return st;
+  if (ep) {
+    if ((st = wait_stream(ep, "result exchange"))) return st;
+    ep->pending = false;
+  }
+  SPT_CUDA(ctx, cudaMemcpyAsync(x, ctx->xdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
   SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   if ((st = check_device_error(ctx))) return st;
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");

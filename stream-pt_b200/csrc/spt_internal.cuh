@@ -60,6 +60,7 @@ struct LayerDev {
   bool has_g8 = false;                 // CUDA-core GEMV planes present
   bool has_mma = false;                // tcgen05 planes present
   MmaMatrix gu_mma, dn_mma;            // gate/up interleaved [E][2D][KP/2]; down [E][H][KPd/2]
+  const float *norm = nullptr;         // post-attention RMSNorm weight [H] (layer stack), or null
 };
 
 // Per-call device scratch (owned by the context, grown on demand).

@@ -99,6 +99,7 @@ func arenaFor(ctx *C.spt_context, reader *ggufmmap.Reader, cfg *Config, lw *Laye
 		ffn_gate_exps: sptTensor(lw.FFNGateExps, &names), ffn_gate_exps_bias: sptTensor(lw.FFNGateExpsBias, &names),
 		ffn_up_exps: sptTensor(lw.FFNUpExps, &names), ffn_up_exps_bias: sptTensor(lw.FFNUpExpsBias, &names),
 		ffn_down_exps: sptTensor(lw.FFNDownExps, &names), ffn_down_exps_bias: sptTensor(lw.FFNDownExpsBias, &names),
+		post_attention_norm: sptTensor(lw.PostAttnNorm, &names),
 	}
 	var arena *C.spt_arena
 	err := reader.WithFile(lw.FFNGateInp.Range.File, func(file []byte) error {
