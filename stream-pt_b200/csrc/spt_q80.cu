@@ -9,11 +9,14 @@
 // with quantSumAVX2.  Here one lane runs one chain.
 //
 // The matrix (615 MB for GPT-OSS's 201,088 x 2,880 output head) streams
-// through shared memory in chunks of rows_per_chunk rows, one bulk copy each,
-// double-buffered; each chunk's block scales are decoded once into shared
-// memory (the reference's float16 decode, NaN payloads included); each warp
-// runs two rows at a time.  int8 -> float uses the exact magic-number form
-// (0x4B000000 | (b ^ 0x80)) - 8388736 instead of the quarter-rate convert.
+// through a four-stage shared-memory ring of 16-row stages, filled by a
+// producer warp with 8-row bulk copies (up to eight in flight) and released
+// per stage through mbarriers; four groups of four consumer warps take the
+// stages in turn, each warp decoding its rows' block scales (the reference's
+// float16 decode, NaN payloads included) and running four rows at a time on
+// packed fp32 pairs (one x load per four rows).  int8 -> float uses the exact
+// magic-number form (0x4B000000 | (b ^ 0x80)) - 8388736 instead of the
+// quarter-rate convert.
 // The argmax packs (order-preserving logit bits, ~row) into 64 bits and
 // keeps the maximum with atomicMax: largest logit, lowest row on ties, NaN
 // never chosen, -0 equal to +0, and row 0 when nothing beats -Inf.
@@ -28,7 +31,7 @@ namespace spt {
 
 namespace {
 
-constexpr int kQ80Threads = 512;  // 16 warps, two rows each per chunk
+constexpr int kQ80Threads = 544;  // 16 consumer warps + 1 producer warp
 
 // quantFloat16Bits (forward/quant_portable.go:20-35).
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
@@ -47,10 +50,6 @@ __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
   return __uint_as_float(bits);
 }
 
-__device__ __forceinline__ float int8_to_f32(uint32_t byte) {
-  return __fsub_rn(__uint_as_float(0x4B000000u | (byte ^ 0x80u)), 8388736.0f);
-}
-
 // AVX2 reduction of the 32 chains held one per lane; valid in lane 0.
 __device__ __forceinline__ float reduce_chains(float v, int lane) {
   const float v8 = __shfl_sync(0xffffffffu, v, (lane + 8) & 31);
@@ -62,6 +61,27 @@ __device__ __forceinline__ float reduce_chains(float v, int lane) {
   return __fadd_rn(q, __shfl_sync(0xffffffffu, q, (lane + 2) & 31));          // lane 0
 }
 
+// Packed fp32 pairs (sm_100a f32x2): two independent IEEE round-to-nearest
+// operations per instruction, so results equal the scalar ones.
+__device__ __forceinline__ void add2(float &a0, float &a1, float b) {
+  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %2};\n\t"
+      "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b));
+}
+__device__ __forceinline__ void mul2(float &a0, float &a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "mul.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fma2(float &c0, float &c1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%0, %1};\n\tfma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+
 __device__ __forceinline__ unsigned long long argmax_key(float logit, int64_t row) {
   uint32_t bits = __float_as_uint(logit == 0.0f ? 0.0f : logit);  // -0 ties with +0
   bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);      // order-preserving
@@ -71,92 +91,135 @@ __device__ __forceinline__ unsigned long long argmax_key(float logit, int64_t ro
 struct Q80Launch {
   const uint8_t *w;          // rows x row_bytes (+ at least 16 bytes of padding)
   int64_t rows;
-  int input, row_bytes, blocks, rows_per_chunk;
+  int input, row_bytes, blocks, rows_per_stage;
   const float *x;            // [input]
   float *y;                  // [rows] or null
   unsigned long long *best;  // argmax key
   int32_t *err;
 };
 
+// Warp roles: warps 0..15 consume (four groups of 4 taking the stages in
+// turn, four rows per warp), warp 16 produces (its lane 0 issues the copies).
+// Stage s is filled through full[s] (transaction bytes) and released through
+// empty[s] (one arrival per consumer warp of the group that read it), so the
+// copies of later stages run while earlier ones are computed.
+constexpr int kQ80Stages = 4;
+constexpr int kQ80Consumers = 16;
+constexpr int kQ80Group = 4;              // consumer warps per stage (4 rows each)
+constexpr int kQ80Groups = kQ80Consumers / kQ80Group;
+constexpr int kQ80RowsPerCopy = 8;        // one bulk copy moves up to 8 rows (16-byte aligned)
+
 __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_constant__ Q80Launch a) {
   extern __shared__ __align__(128) uint8_t q80_smem[];
-  const int rpc = a.rows_per_chunk, rb = a.row_bytes, nb = a.blocks;
-  const uint32_t chunk_bytes = (uint32_t)((int64_t)rpc * rb);
-  float *xs = reinterpret_cast<float *>(q80_smem + 2 * (size_t)chunk_bytes);
-  float *scl = xs + a.input;                       // [rpc][nb]
-  uint64_t *bar = reinterpret_cast<uint64_t *>(scl + (size_t)rpc * nb);  // [2]
-  unsigned long long *wbest = reinterpret_cast<unsigned long long *>(bar + 2);  // [warps]
+  const int rps = a.rows_per_stage, rb = a.row_bytes, nb = a.blocks;
+  const uint32_t stage_bytes = (uint32_t)((int64_t)rps * rb);
+  float *xs = reinterpret_cast<float *>(q80_smem + (size_t)kQ80Stages * stage_bytes);
+  float *wscale = xs + a.input;                                               // [16][nb][4]
+  uint64_t *full = reinterpret_cast<uint64_t *>(wscale + (size_t)kQ80Consumers * 4 * nb);
+  uint64_t *empty = full + kQ80Stages;
+  unsigned long long *wbest = reinterpret_cast<unsigned long long *>(empty + kQ80Stages);  // [16]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t n_chunks = (a.rows + rpc - 1) / rpc;
+  const int64_t n_chunks = (a.rows + rps - 1) / rps;
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int s = 0; s < kQ80Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kQ80Group);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   pdl_wait();
   pdl_trigger();
-  auto issue = [&](int64_t chunk, int slot) {
-    const int64_t r0 = chunk * rpc;
-    const int64_t nr = a.rows - r0 < rpc ? a.rows - r0 : rpc;
-    const uint32_t bytes = (uint32_t)((nr * rb + 15) & ~15ll);  // padding rows of the buffer cover the round-up
-    mbar_expect_tx(&bar[slot], bytes);
-    bulk_load(q80_smem + (size_t)slot * chunk_bytes, a.w + r0 * rb, bytes, &bar[slot]);
-  };
-  if (tid == 0) {
-    if ((int64_t)blockIdx.x < n_chunks) issue(blockIdx.x, 0);
-    if ((int64_t)blockIdx.x + gridDim.x < n_chunks) issue(blockIdx.x + gridDim.x, 1);
-  }
   for (int i = tid; i < a.input; i += blockDim.x) xs[i] = a.x[i];
+  __syncthreads();
   unsigned long long best = 0ull;
-  int it = 0;
-  for (int64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x, ++it) {
-    const int slot = it & 1;
-    const uint32_t parity = (uint32_t)(it >> 1) & 1u;
-    if (!mbar_wait(&bar[slot], parity, a.err, 1)) break;  // every thread waits: the buffer is shared
-    const uint8_t *cb = q80_smem + (size_t)slot * chunk_bytes;
-    const int64_t r0 = chunk * rpc;
-    const int nr = (int)(a.rows - r0 < rpc ? a.rows - r0 : rpc);
-    for (int i = tid; i < nr * nb; i += blockDim.x) {
-      const int r = i / nb, b = i - r * nb;
-      const uint8_t *blk = cb + (size_t)r * rb + (size_t)b * 34;
-      scl[i] = f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
-    }
-    __syncthreads();
-    for (int r = 2 * warp; r < nr; r += 2 * (blockDim.x >> 5)) {
-      const bool two = r + 1 < nr;
-      const uint8_t *q0 = cb + (size_t)r * rb + 2 + lane;
-      const uint8_t *q1 = q0 + (two ? rb : 0);
-      const float *s0 = scl + (size_t)r * nb;
-      const float *s1 = s0 + (two ? nb : 0);
-      float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll 6
-      for (int b = 0; b < nb; ++b) {
-        const float xv = xs[b * 32 + lane];
-        const float w0 = __fmul_rn(int8_to_f32(q0[b * 34]), s0[b]);
-        const float w1 = __fmul_rn(int8_to_f32(q1[b * 34]), s1[b]);
-        acc0 = fmaf(w0, xv, acc0);
-        acc1 = fmaf(w1, xv, acc1);
-      }
-      const float y0 = reduce_chains(acc0, lane);
-      const float y1 = reduce_chains(acc1, lane);
-      if (lane == 0) {
-        if (a.y) {
-          a.y[r0 + r] = y0;
-          if (two) a.y[r0 + r + 1] = y1;
+  if (warp == kQ80Consumers) {
+    // ---- producer ----
+    if (lane == 0) {
+      int it = 0;
+      for (int64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x, ++it) {
+        const int s = it % kQ80Stages, use = it / kQ80Stages;
+        if (use > 0 && !mbar_wait(&empty[s], (uint32_t)(use - 1) & 1u, a.err, 2)) break;
+        const int64_t r0 = chunk * rps;
+        const int nr = (int)(a.rows - r0 < rps ? a.rows - r0 : rps);
+        uint32_t tx = 0;
+        for (int p = 0; p < nr; p += kQ80RowsPerCopy)
+          tx += (uint32_t)((int64_t)(min(kQ80RowsPerCopy, nr - p) * rb + 15) & ~15ll);
+        mbar_expect_tx(&full[s], tx);
+        uint8_t *dst = q80_smem + (size_t)s * stage_bytes;
+        for (int p = 0; p < nr; p += kQ80RowsPerCopy) {
+          // the last copy rounds up to 16 bytes: the matrix buffer is padded
+          const uint32_t bytes = (uint32_t)((int64_t)(min(kQ80RowsPerCopy, nr - p) * rb + 15) & ~15ll);
+          bulk_load(dst + (size_t)p * rb, a.w + (r0 + p) * rb, bytes, &full[s]);
         }
-        if (!isnan(y0)) best = max(best, argmax_key(y0, r0 + r));
-        if (two && !isnan(y1)) best = max(best, argmax_key(y1, r0 + r + 1));
       }
     }
-    __syncthreads();  // buffer `slot` and the scales are free again
-    if (tid == 0 && chunk + 2 * (int64_t)gridDim.x < n_chunks) issue(chunk + 2 * gridDim.x, slot);
+  } else {
+    // ---- consumers: group g takes stages it = g, g + 4, ...; each warp
+    // runs four rows of the stage at once ----
+    const int group = warp / kQ80Group, wi = warp % kQ80Group;
+    float4 *sc = reinterpret_cast<float4 *>(wscale) + (size_t)warp * nb;  // [nb] x 4 rows
+    int it = group;
+    for (int64_t chunk = blockIdx.x + (int64_t)group * gridDim.x; chunk < n_chunks;
+         chunk += (int64_t)kQ80Groups * gridDim.x, it += kQ80Groups) {
+      const int s = it % kQ80Stages, use = it / kQ80Stages;
+      if (!mbar_wait(&full[s], (uint32_t)use & 1u, a.err, 1)) break;
+      const uint8_t *cb = q80_smem + (size_t)s * stage_bytes;
+      const int64_t r0 = chunk * rps;
+      const int nr = (int)(a.rows - r0 < rps ? a.rows - r0 : rps);
+      for (int r = 4 * wi; r < nr; r += 4 * kQ80Group) {
+        const int live = min(4, nr - r);  // rows past the end repeat the last live row
+        const uint8_t *row[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) row[k] = cb + (size_t)(r + min(k, live - 1)) * rb;
+        for (int b = lane; b < nb; b += 32) {
+          float4 v;
+          v.x = f16_bits_to_f32((uint32_t)row[0][b * 34] | ((uint32_t)row[0][b * 34 + 1] << 8));
+          v.y = f16_bits_to_f32((uint32_t)row[1][b * 34] | ((uint32_t)row[1][b * 34 + 1] << 8));
+          v.z = f16_bits_to_f32((uint32_t)row[2][b * 34] | ((uint32_t)row[2][b * 34 + 1] << 8));
+          v.w = f16_bits_to_f32((uint32_t)row[3][b * 34] | ((uint32_t)row[3][b * 34 + 1] << 8));
+          sc[b] = v;
+        }
+        __syncwarp();
+        const uint8_t *q0 = row[0] + 2 + lane, *q1 = row[1] + 2 + lane, *q2 = row[2] + 2 + lane,
+                      *q3 = row[3] + 2 + lane;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 5
+        for (int b = 0; b < nb; ++b) {
+          const float xv = xs[b * 32 + lane];
+          const float4 sv = sc[b];
+          // int8 -> float: (0x4B000000 | (byte ^ 0x80)) - 8388736, exact
+          float w0 = __uint_as_float(0x4B000000u | ((uint32_t)q0[b * 34] ^ 0x80u));
+          float w1 = __uint_as_float(0x4B000000u | ((uint32_t)q1[b * 34] ^ 0x80u));
+          float w2 = __uint_as_float(0x4B000000u | ((uint32_t)q2[b * 34] ^ 0x80u));
+          float w3 = __uint_as_float(0x4B000000u | ((uint32_t)q3[b * 34] ^ 0x80u));
+          add2(w0, w1, -8388736.0f);
+          add2(w2, w3, -8388736.0f);
+          mul2(w0, w1, sv.x, sv.y);  // weight = int8 * scale (exact)
+          mul2(w2, w3, sv.z, sv.w);
+          fma2(a0, a1, w0, w1, xv);
+          fma2(a2, a3, w2, w3, xv);
+        }
+        const float y[4] = {reduce_chains(a0, lane), reduce_chains(a1, lane), reduce_chains(a2, lane),
+                            reduce_chains(a3, lane)};
+        if (lane == 0) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (k >= live) break;
+            if (a.y) a.y[r0 + r + k] = y[k];
+            if (!isnan(y[k])) best = max(best, argmax_key(y[k], r0 + r + k));
+          }
+        }
+        __syncwarp();  // the next rows' scales overwrite these
+      }
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (lane == 0) wbest[warp] = best;
   }
-  if (lane == 0) wbest[warp] = best;
   __syncthreads();
   if (tid == 0) {
     unsigned long long b = 0ull;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = max(b, wbest[w]);
+    for (int w = 0; w < kQ80Consumers; ++w) b = max(b, wbest[w]);
     if (b) atomicMax(a.best, b);
   }
 }
@@ -179,21 +242,18 @@ __global__ void k_q80_finalize(const unsigned long long *best, int64_t *argmax, 
 
 }  // namespace
 
-int q80_rows_per_chunk(int input) {
+size_t q80_smem_bytes(int input, int rps) {
   const int64_t rb = (int64_t)input / 32 * 34;
-  // two chunk buffers + x + the chunk's scales within ~200 KB; a multiple of 8
-  // rows keeps every chunk start 16-byte aligned
-  for (int rpc = 32; rpc >= 8; rpc -= 8) {
-    const int64_t bytes = 2 * rpc * rb + (int64_t)input * 4 + (int64_t)rpc * (input / 32) * 4 + 16 + 8 * 32;
-    if (bytes <= 200 * 1024) return rpc;
-  }
-  return 0;
+  return (size_t)((int64_t)kQ80Stages * rps * rb + (int64_t)input * 4 + (int64_t)kQ80Consumers * 4 * (input / 32) * 4 +
+                  16 * kQ80Stages + 8 * kQ80Consumers);
 }
 
-size_t q80_smem_bytes(int input, int rpc) {
-  const int64_t rb = (int64_t)input / 32 * 34;
-  return (size_t)(2 * rpc * rb + (int64_t)input * 4 + (int64_t)rpc * (input / 32) * 4 + 16 +
-                  8 * (kQ80Threads / 32));
+int q80_rows_per_chunk(int input) {
+  // rows per stage: a multiple of 8 (16-byte aligned copies), 16 when the
+  // four-stage ring fits (the per-CTA maximum is 227 KB)
+  for (int rps = 16; rps >= 8; rps -= 8)
+    if (q80_smem_bytes(input, rps) <= 226 * 1024) return rps;
+  return 0;
 }
 
 cudaError_t launch_q80(const uint8_t *w, int64_t rows, int input, const float *x, float *y,
@@ -210,7 +270,7 @@ cudaError_t launch_q80(const uint8_t *w, int64_t rows, int input, const float *x
   a.input = input;
   a.row_bytes = input / 32 * 34;
   a.blocks = input / 32;
-  a.rows_per_chunk = rpc;
+  a.rows_per_stage = rpc;
   a.x = x;
   a.y = y;
   a.best = best;
