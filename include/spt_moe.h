@@ -53,7 +53,8 @@ typedef enum spt_status {
   SPT_ERR_NCCL = 11,         /* NCCL failure in the expert-parallel path */
   SPT_ERR_TIMEOUT = 12,      /* a bounded device wait gave up */
   SPT_ERR_UNSUPPORTED = 13,  /* shape or option this build does not implement */
-  SPT_ERR_NO_DEVICE = 14     /* no CUDA device / extension unusable */
+  SPT_ERR_NO_DEVICE = 14,    /* no CUDA device / extension unusable */
+  SPT_ERR_FORMAT = 15        /* malformed or inconsistent GGUF model files */
 } spt_status;
 
 /* ggufindex.Tensor (ggufindex/index.go:15-26): name, GGML type, shape with
@@ -293,6 +294,30 @@ spt_status spt_mul_q80_matrix(spt_context *ctx, spt_q80_matrix *m, const float *
  * float) may each be NULL. */
 spt_status spt_mul_q80_matrix_device(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y,
                                      int64_t *argmax, float *best_logit);
+
+/* ---- GGUF model files -------------------------------------------------------
+ * ggufindex.Open (ggufindex/index.go:55-575): headers, metadata and tensor
+ * directories of one model, split files in any order, each file mapped
+ * read-only for the life of the handle; the same validation and error
+ * messages (SPT_ERR_FORMAT; the text is in spt_last_error(NULL)). */
+typedef struct spt_gguf spt_gguf;
+spt_status spt_gguf_open(const char *const *paths, int64_t n_paths, spt_gguf **out);
+void spt_gguf_close(spt_gguf *g);
+int64_t spt_gguf_layer_count(const spt_gguf *g);
+/* NewConfig's MoE fields (forward/config.go:56-125): the gpt-oss.* metadata
+ * when present and positive, else GPT-OSS-120B's defaults. */
+spt_status spt_gguf_config(const spt_gguf *g, spt_moe_config *cfg, float *rms_eps);
+/* NewLayerWeights (forward/layer.go:39-86) for one layer: the MoE tensors and
+ * post_attention_norm with absolute byte ranges, and the reader of the file
+ * that holds them (all of a layer's MoE tensors must lie in one file).
+ * Tensor names point into the handle. */
+spt_status spt_gguf_layer(const spt_gguf *g, int64_t layer, spt_layer_weights *lw, spt_reader *reader);
+/* Any tensor by name (e.g. "output.weight" for the LM head) and its file. */
+spt_status spt_gguf_tensor(const spt_gguf *g, const char *name, spt_tensor *t, spt_reader *reader);
+/* spt_arena_create_range over layers [first_layer, first_layer + n_layers)
+ * of a GGUF model (expert_end 0: every expert). */
+spt_status spt_arena_create_gguf(spt_context *ctx, const spt_gguf *g, int64_t first_layer, int64_t n_layers,
+                                 uint32_t flags, int64_t expert_begin, int64_t expert_end, spt_arena **out);
 
 /* ---- Layer stack -------------------------------------
  * The MoE half of forwardLayerBatch (forward/layer_batch.go:102-120) over

@@ -28,6 +28,7 @@ ERR_FILE_RANGE, ERR_SCRATCH, ERR_CANCELED, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT = ran
 ERR_UNSUPPORTED, ERR_NO_DEVICE = 13, 14
 
 ARENA_GEMV, ARENA_MMA = 1, 2
+ERR_FORMAT = 15
 PATH_AUTO, PATH_EXACT, PATH_MMA = 0, 1, 2
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
@@ -209,6 +210,13 @@ def lib():
         "spt_combine_moe_batch": ([vp, vp, vp, i64, i64, i64, vp], st),
         "spt_rmsnorm": ([vp, vp, vp, i64, i64, f32, vp], st),
         "spt_mul_q80": ([vp, vp, ctypes.c_uint64, i64, i64, vp, vp, P(i64), P(f32)], st),
+        "spt_gguf_open": ([P(ctypes.c_char_p), i64, P(vp)], st),
+        "spt_gguf_close": ([vp], None),
+        "spt_gguf_layer_count": ([vp], i64),
+        "spt_gguf_config": ([vp, P(_Config), P(f32)], st),
+        "spt_gguf_layer": ([vp, i64, P(_LayerWeights), P(_Reader)], st),
+        "spt_gguf_tensor": ([vp, ctypes.c_char_p, P(_Tensor), P(_Reader)], st),
+        "spt_arena_create_gguf": ([vp, vp, i64, i64, ctypes.c_uint32, i64, i64, P(vp)], st),
         "spt_forward_stack_device": ([vp, vp, vp, i64, i64, vp, i64, f32], st),
         "spt_forward_stack": ([vp, vp, vp, i64, i64, vp, i64, i64, f32, vp], st),
         "spt_synth_norm_host": ([P(_SynthParams), i64, i64, vp], st),
@@ -343,6 +351,16 @@ class Context:
             self.check(lib().spt_arena_create_synthetic_range(self._h, ctypes.byref(c), ctypes.byref(p), n_layers,
                                                               flags, experts[0], experts[1], ctypes.byref(h)))
         return Arena(self, h, cfg, n_layers)
+
+    def arena_from_gguf(self, g: "Gguf", first_layer: int = 0, n_layers: Optional[int] = None,
+                        flags: int = ARENA_GEMV, experts: Optional[Tuple[int, int]] = None) -> "Arena":
+        """spt_arena_create_gguf: layers [first, first + n) of a GGUF model."""
+        n = g.layer_count - first_layer if n_layers is None else n_layers
+        cfg, _ = g.config()
+        b, e = experts if experts is not None else (0, 0)
+        h = ctypes.c_void_p()
+        self.check(lib().spt_arena_create_gguf(self._h, g.handle, first_layer, n, flags, b, e, ctypes.byref(h)))
+        return Arena(self, h, cfg, n, keep=(g,))
 
     def arena_range(self, readers: Sequence[Reader], cfg: Config, layers: Sequence[LayerWeights],
                     experts: Tuple[int, int], flags: int = ARENA_GEMV) -> "Arena":
@@ -524,6 +542,61 @@ class Context:
     def q80_matrix(self, data: np.ndarray, input_: int, output: int) -> "Q80Matrix":
         """Upload a Q8_0 matrix once (spt_q80_matrix_create)."""
         return Q80Matrix(self, data, input_, output)
+
+
+def _tensor_view(t: "_Tensor") -> Tensor:
+    return Tensor(t.name.decode() if t.name else "", t.type, tuple(t.shape[i] for i in range(min(t.n_dims, 4))),
+                  t.start, t.end)
+
+
+class Gguf:
+    """spt_gguf: a GGUF model (split files in any order), mapped read-only."""
+
+    def __init__(self, paths: Sequence[str]):
+        arr = (ctypes.c_char_p * len(paths))(*[os.fsencode(p) for p in paths])
+        self._h = ctypes.c_void_p()
+        st = lib().spt_gguf_open(arr, len(paths), ctypes.byref(self._h))
+        if st != OK:
+            raise SptError(st, lib().spt_last_error(None).decode())
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def layer_count(self) -> int:
+        return lib().spt_gguf_layer_count(self._h)
+
+    def config(self) -> Tuple[Config, float]:
+        c, eps = _Config(), ctypes.c_float()
+        self._check(lib().spt_gguf_config(self._h, ctypes.byref(c), ctypes.byref(eps)))
+        return Config(c.hidden_dim, c.expert_hidden_dim, c.num_experts, c.num_experts_used), float(eps.value)
+
+    def layer(self, layer: int) -> dict:
+        """NewLayerWeights of one layer: field -> Tensor (name '' when absent)."""
+        lw, rd = _LayerWeights(), _Reader()
+        self._check(lib().spt_gguf_layer(self._h, layer, ctypes.byref(lw), ctypes.byref(rd)))
+        return {name: _tensor_view(getattr(lw, name)) for name, _ in _LayerWeights._fields_}
+
+    def tensor(self, name: str) -> Tensor:
+        t, rd = _Tensor(), _Reader()
+        self._check(lib().spt_gguf_tensor(self._h, name.encode(), ctypes.byref(t), ctypes.byref(rd)))
+        return _tensor_view(t)
+
+    def _check(self, st):
+        if st != OK:
+            raise SptError(st, lib().spt_last_error(None).decode())
+
+    def close(self):
+        if self._h:
+            lib().spt_gguf_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Q80Matrix:

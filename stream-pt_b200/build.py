@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libspt_moe.so")
 BUILD = os.path.join(HERE, "_build")
 
-SOURCES = ["spt_kernels.cu", "spt_mma.cu", "spt_q80.cu", "spt_api.cu"]
+SOURCES = ["spt_kernels.cu", "spt_mma.cu", "spt_q80.cu", "spt_gguf.cpp", "spt_api.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -47,7 +47,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
-        o = os.path.join(BUILD, src.replace(".cu", ".o"))
+        o = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
         objs.append(o)
         if force or _stale(o, [s] + headers):
             cmd = [nvcc(), *NVCC_FLAGS, "-c", s, "-o", o]

@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "../../include/spt_moe.h"
+#include "spt_gguf.h"
 #include "spt_internal.cuh"
 #include "spt_philox.h"
 
@@ -813,6 +814,7 @@ const char *spt_status_string(spt_status s) {
     case SPT_ERR_TIMEOUT: return "device wait timed out";
     case SPT_ERR_UNSUPPORTED: return "unsupported";
     case SPT_ERR_NO_DEVICE: return "no CUDA device";
+    case SPT_ERR_FORMAT: return "invalid GGUF model";
   }
   return "unknown status";
 }
@@ -2323,6 +2325,153 @@ spt_status spt_forward_stack(spt_context *ctx, spt_ep *ep, spt_arena *arena, int
   if ((st = check_device_error(ctx))) return st;
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
   return SPT_OK;
+}
+
+}  // extern "C"
+
+// =========================================================================
+// GGUF model files (the parser is in spt_gguf.cpp).
+struct spt_gguf {
+  spt::GgufModel m;
+};
+
+namespace {
+
+spt_tensor tensor_fact(const spt::GgufModel &m, size_t idx) {
+  const spt::GgufTensor &t = m.tensors[idx];
+  spt_tensor c{};
+  c.name = t.name.c_str();
+  c.type = t.type;
+  c.n_dims = (uint32_t)t.shape.size();
+  for (size_t i = 0; i < t.shape.size() && i < 4; ++i) c.shape[i] = t.shape[i];
+  c.start = t.start;
+  c.end = t.end;
+  return c;
+}
+
+bool ends_with(const std::string &s, const char *suffix) {
+  const size_t n = strlen(suffix);
+  return s.size() >= n && s.compare(s.size() - n, n, suffix) == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+spt_status spt_gguf_open(const char *const *paths, int64_t n_paths, spt_gguf **out) {
+  if (!out || (!paths && n_paths > 0) || n_paths < 0) return fail(nullptr, SPT_ERR_NULL_ARG, "nil argument");
+  *out = nullptr;
+  std::vector<std::string> ps;
+  for (int64_t i = 0; i < n_paths; ++i) {
+    if (!paths[i]) return fail(nullptr, SPT_ERR_NULL_ARG, "nil path");
+    ps.emplace_back(paths[i]);
+  }
+  spt_gguf *g = new spt_gguf();
+  std::string err;
+  if (!spt::gguf_open(ps, &g->m, &err)) {
+    delete g;
+    return fail(nullptr, SPT_ERR_FORMAT, "%s", err.c_str());
+  }
+  *out = g;
+  return SPT_OK;
+}
+
+void spt_gguf_close(spt_gguf *g) {
+  if (!g) return;
+  spt::gguf_close(&g->m);
+  delete g;
+}
+
+int64_t spt_gguf_layer_count(const spt_gguf *g) { return g ? g->m.layer_count : 0; }
+
+spt_status spt_gguf_config(const spt_gguf *g, spt_moe_config *cfg, float *rms_eps) {
+  if (!g || !cfg) return fail(nullptr, SPT_ERR_NULL_ARG, "nil argument");
+  int64_t v = 0;
+  cfg->hidden_dim = 2880;  // NewConfig defaults (forward/config.go:57-75)
+  cfg->expert_hidden_dim = 2880;
+  cfg->num_experts = 128;
+  cfg->num_experts_used = 4;
+  if (spt::gguf_meta_int(g->m, "gpt-oss.embedding_length", &v) && v > 0) cfg->hidden_dim = v;
+  if (spt::gguf_meta_int(g->m, "gpt-oss.expert_count", &v) && v > 0) cfg->num_experts = v;
+  if (spt::gguf_meta_int(g->m, "gpt-oss.expert_used_count", &v) && v > 0) cfg->num_experts_used = v;
+  if (spt::gguf_meta_int(g->m, "gpt-oss.expert_feed_forward_length", &v) && v > 0) cfg->expert_hidden_dim = v;
+  if (rms_eps) {
+    double e = 0;
+    *rms_eps = 1e-5f;
+    if (spt::gguf_meta_float(g->m, "gpt-oss.attention.layer_norm_rms_epsilon", &e) && (float)e > 0) *rms_eps = (float)e;
+  }
+  return SPT_OK;
+}
+
+spt_status spt_gguf_layer(const spt_gguf *g, int64_t layer, spt_layer_weights *lw, spt_reader *reader) {
+  if (!g || !lw) return fail(nullptr, SPT_ERR_NULL_ARG, "nil argument");
+  if (layer < 0 || layer >= g->m.layer_count)
+    return fail(nullptr, SPT_ERR_DIMENSIONS, "layer %lld out of range", (long long)layer);
+  *lw = spt_layer_weights{};
+  int file = -1;
+  // NewLayerWeights' suffix cases (forward/layer.go:42-83), MoE tensors only
+  struct Case {
+    const char *suffix;
+    spt_tensor *dst;
+  } cases[] = {{"post_attention_norm.weight", &lw->post_attention_norm},
+               {"ffn_gate_inp.weight", &lw->ffn_gate_inp},
+               {"ffn_gate_inp.bias", &lw->ffn_gate_inp_bias},
+               {"ffn_gate_exps.weight", &lw->ffn_gate_exps},
+               {"ffn_gate_exps.bias", &lw->ffn_gate_exps_bias},
+               {"ffn_up_exps.weight", &lw->ffn_up_exps},
+               {"ffn_up_exps.bias", &lw->ffn_up_exps_bias},
+               {"ffn_down_exps.weight", &lw->ffn_down_exps},
+               {"ffn_down_exps.bias", &lw->ffn_down_exps_bias}};
+  for (size_t idx : g->m.layers[(size_t)layer]) {
+    const spt::GgufTensor &t = g->m.tensors[idx];
+    for (const Case &c : cases) {
+      if (!ends_with(t.name, c.suffix)) continue;
+      if (t.shape.size() > 4)
+        return fail(nullptr, SPT_ERR_FORMAT, "tensor \"%s\": more than 4 dimensions", t.name.c_str());
+      if (file >= 0 && t.file != file)
+        return fail(nullptr, SPT_ERR_FILE_RANGE, "layer %lld: MoE tensors span several files", (long long)layer);
+      file = t.file;
+      *c.dst = tensor_fact(g->m, idx);
+      break;
+    }
+  }
+  if (reader) {
+    const spt::GgufFile &f = g->m.files[(size_t)(file < 0 ? 0 : file)];
+    reader->base = f.base;
+    reader->size = f.size;
+  }
+  return SPT_OK;
+}
+
+spt_status spt_gguf_tensor(const spt_gguf *g, const char *name, spt_tensor *t, spt_reader *reader) {
+  if (!g || !name || !t) return fail(nullptr, SPT_ERR_NULL_ARG, "nil argument");
+  auto it = g->m.by_name.find(name);
+  if (it == g->m.by_name.end()) return fail(nullptr, SPT_ERR_FORMAT, "no tensor \"%s\"", name);
+  *t = tensor_fact(g->m, it->second);
+  if (reader) {
+    const spt::GgufFile &f = g->m.files[(size_t)g->m.tensors[it->second].file];
+    reader->base = f.base;
+    reader->size = f.size;
+  }
+  return SPT_OK;
+}
+
+spt_status spt_arena_create_gguf(spt_context *ctx, const spt_gguf *g, int64_t first_layer, int64_t n_layers,
+                                 uint32_t flags, int64_t expert_begin, int64_t expert_end, spt_arena **out) {
+  if (!ctx || !g || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil argument");
+  if (first_layer < 0 || n_layers <= 0 || first_layer + n_layers > g->m.layer_count)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "layers [%lld, %lld) outside the model's %lld", (long long)first_layer,
+                (long long)(first_layer + n_layers), (long long)g->m.layer_count);
+  spt_moe_config cfg;
+  spt_status st = spt_gguf_config(g, &cfg, nullptr);
+  if (st) return st;
+  std::vector<spt_reader> readers((size_t)n_layers);
+  std::vector<spt_layer_weights> lws((size_t)n_layers);
+  for (int64_t l = 0; l < n_layers; ++l)
+    if ((st = spt_gguf_layer(g, first_layer + l, &lws[(size_t)l], &readers[(size_t)l])))
+      return fail(ctx, st, "%s", spt_last_error(nullptr));
+  if (expert_end == 0) expert_end = cfg.num_experts;
+  return arena_create_impl(ctx, readers.data(), &cfg, lws.data(), n_layers, flags, expert_begin, expert_end, out);
 }
 
 }  // extern "C"
