@@ -12,14 +12,15 @@
 // through a four-stage shared-memory ring of 16-row stages, filled by a
 // producer warp with 8-row bulk copies (up to eight in flight) and released
 // per stage through mbarriers; four groups of four consumer warps take the
-// stages in turn, each warp decoding its rows' block scales (the reference's
-// float16 decode, NaN payloads included) and running four rows at a time on
+// stages in turn, each warp decoding its rows' block scales (float16 ->
+// float32, exact like the reference's decode) and running four rows at a time on
 // packed fp32 pairs (one x load per four rows).  int8 -> float uses the exact
 // magic-number form (0x4B000000 | (b ^ 0x80)) - 8388736 instead of the
 // quarter-rate convert.
 // The argmax packs (order-preserving logit bits, ~row) into 64 bits and
 // keeps the maximum with atomicMax: largest logit, lowest row on ties, NaN
 // never chosen, -0 equal to +0, and row 0 when nothing beats -Inf.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -32,23 +33,6 @@ namespace spt {
 namespace {
 
 constexpr int kQ80Threads = 544;  // 16 consumer warps + 1 producer warp
-
-// quantFloat16Bits (forward/quant_portable.go:20-35).
-__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
-  const uint32_t sign = (h & 0x8000u) << 16, exponent = (h >> 10) & 31u, fraction = h & 1023u;
-  uint32_t bits;
-  if (exponent == 31u) {
-    bits = sign | 0x7f800000u | fraction << 13;
-  } else if (exponent != 0u) {
-    bits = sign | (exponent + 112u) << 23 | fraction << 13;
-  } else if (fraction == 0u) {
-    bits = sign;
-  } else {
-    const uint32_t shift = (uint32_t)__clz(fraction) - 21u;
-    bits = sign | (113u - shift) << 23 | ((fraction << shift) & 1023u) << 13;
-  }
-  return __uint_as_float(bits);
-}
 
 // AVX2 reduction of the 32 chains held one per lane; valid in lane 0.
 __device__ __forceinline__ float reduce_chains(float v, int lane) {
@@ -173,11 +157,13 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
 #pragma unroll
         for (int k = 0; k < 4; ++k) row[k] = cb + (size_t)(r + min(k, live - 1)) * rb;
         for (int b = lane; b < nb; b += 32) {
+          // float16 -> float32 is exact for every finite value and infinity
+          // (quantFloat16Bits); a NaN scale gives a NaN either way
           float4 v;
-          v.x = f16_bits_to_f32((uint32_t)row[0][b * 34] | ((uint32_t)row[0][b * 34 + 1] << 8));
-          v.y = f16_bits_to_f32((uint32_t)row[1][b * 34] | ((uint32_t)row[1][b * 34 + 1] << 8));
-          v.z = f16_bits_to_f32((uint32_t)row[2][b * 34] | ((uint32_t)row[2][b * 34 + 1] << 8));
-          v.w = f16_bits_to_f32((uint32_t)row[3][b * 34] | ((uint32_t)row[3][b * 34 + 1] << 8));
+          v.x = __half2float(*reinterpret_cast<const __half *>(row[0] + b * 34));
+          v.y = __half2float(*reinterpret_cast<const __half *>(row[1] + b * 34));
+          v.z = __half2float(*reinterpret_cast<const __half *>(row[2] + b * 34));
+          v.w = __half2float(*reinterpret_cast<const __half *>(row[3] + b * 34));
           sc[b] = v;
         }
         __syncwarp();
