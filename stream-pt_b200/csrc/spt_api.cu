@@ -616,8 +616,11 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // (sel_idx/sel_w [T*K], expert ids local to the arena): out[t] = sum over
 // ranks r of fma(result, weight, out[t]).  `c` gives the arena's experts
 // and top-k (the expert-parallel receive side passes its shard and top-k 1).
+// With `logits` (one device, T <= kSelectDispatchMaxTokens) the top-k
+// selection runs inside the dispatch kernel and writes sel_idx / sel_w there.
 spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                           int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0) {
+                           int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0,
+                           const float *logits = nullptr) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
@@ -636,10 +639,18 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
     plan.tile_dn = ctx->tile_dn.as<int32_t>();
     plan.pos_expert = ctx->pos_expert.as<int32_t>();
   }
-  SPT_CUDA(ctx, launch_dispatch(sel_idx, sel_w, (int)(T * K), E,
-                                ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
-                                ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
-                                ctx->meta.as<int32_t>(), s, use_mma ? &plan : nullptr));
+  if (logits) {
+    SPT_CUDA(ctx, launch_select_dispatch(logits, (int)T, E, K, const_cast<int32_t *>(sel_idx),
+                                         const_cast<float *>(sel_w), ctx->offsets.as<int32_t>(),
+                                         ctx->perm.as<int32_t>(), ctx->slot_pos.as<int32_t>(),
+                                         ctx->act_list.as<int32_t>(), ctx->meta.as<int32_t>(), s,
+                                         use_mma ? &plan : nullptr));
+  } else {
+    SPT_CUDA(ctx, launch_dispatch(sel_idx, sel_w, (int)(T * K), E,
+                                  ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
+                                  ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
+                                  ctx->meta.as<int32_t>(), s, use_mma ? &plan : nullptr));
+  }
   SPT_MARK(3);
   if (use_mma) {
     if ((st = forward_mma(ctx, L, c, x, T, s, plan.bn))) return st;
@@ -685,18 +696,20 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   SPT_MARK(7);
   SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
   SPT_MARK(8);
+  if (logits) ctx->kernels_last -= 1;  // no separate selection launch
   return SPT_OK;
 }
 
 // Router logits and top-k selections of T tokens (all experts of the layer).
+// select = false leaves the selection to the fused dispatch kernel.
 spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                        int64_t T, int32_t *sel_idx, float *sel_w) {
+                        int64_t T, int32_t *sel_idx, float *sel_w, bool select = true) {
   const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
   SPT_MARK(0);
   SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s));
   SPT_MARK(1);
-  SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
+  if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
   return SPT_OK;
 }
@@ -720,8 +733,11 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
                 (long long)c.num_experts);
   if ((st = ensure_scratch(ctx, T, c))) return st;
   const LayerDev &L = arena->layers[(size_t)layer];
-  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>()))) return st;
-  if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out))) return st;
+  const bool fuse = T <= kSelectDispatchMaxTokens && fused_select_enabled();
+  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse))) return st;
+  if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out, 0,
+                            fuse ? ctx->logits.as<float>() : nullptr)))
+    return st;
   ctx->last_T = T;
   ctx->last_E = c.num_experts;
   ctx->last_K = c.num_experts_used;

@@ -99,6 +99,17 @@ cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, i
                             int32_t *offsets, int32_t *perm, int32_t *slot_pos,
                             int32_t *act_list, int32_t *meta, cudaStream_t stream,
                             const DispatchPlan *plan = nullptr, int key_div = 1);
+// Top-k selection fused into the dispatch CTA (one device, T <= the limit):
+// writes sel_idx / sel_w as launch_select does, then dispatches as above, one
+// launch fewer.  Measured on B200 (GPT-OSS layer): T=1 0.8 us faster per
+// block; T=32 and T=64 about 1% slower (the selection then sits serially in
+// the one dispatch CTA), hence the small limit.
+constexpr int kSelectDispatchMaxTokens = 8;
+// SPT_FUSED_SELECT=0 keeps the separate selection launch (same results).
+bool fused_select_enabled();
+cudaError_t launch_select_dispatch(const float *logits, int T, int E, int K, int32_t *sel_idx, float *sel_w,
+                                   int32_t *offsets, int32_t *perm, int32_t *slot_pos, int32_t *act_list,
+                                   int32_t *meta, cudaStream_t stream, const DispatchPlan *plan = nullptr);
 // Expert-parallel helpers: gather the send rows (token of slot perm[p], local
 // expert id sel_idx % experts_per_rank) for the meta[1] dispatched slots;
 // per-rank row counts from the rank offsets; fill a float array.

@@ -287,15 +287,9 @@ __global__ void k_router_portable(const float *__restrict__ W, const float *__re
 // logit among experts not yet chosen (lowest index wins ties, NaN and -Inf
 // never win); no candidate gives (index = pass, value 0), and that index
 // counts as chosen for the later passes.
-__global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits, int T, int E,
-                                                int K, int32_t *__restrict__ sel_idx,
-                                                float *__restrict__ sel_w) {
-  pdl_wait();
-  pdl_trigger();
+__device__ __forceinline__ void select_token(const float *__restrict__ logits, int t, int E, int K, int lane,
+                                             int32_t *__restrict__ sel_idx, float *__restrict__ sel_w) {
   constexpr int kPer = kDispatchMaxExperts / 32;
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (t >= T) return;
   const float *lg = logits + (size_t)t * E;
   const bool in_regs = E <= 32 * kPer;  // else every pass reads the logits again
   float lv[kPer];
@@ -365,6 +359,15 @@ __global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits
   }
 }
 
+__global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits, int T, int E,
+                                                int K, int32_t *__restrict__ sel_idx,
+                                                float *__restrict__ sel_w) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t < T) select_token(logits, t, E, K, threadIdx.x & 31, sel_idx, sel_w);
+}
+
 // ---------------------------------------------------------------------------
 // Dispatch: the reference pushes slot t*k+r (weight > 0 or NaN) onto the
 // front of its expert's list (moe_batch.go:142-159), so walking a list visits
@@ -389,14 +392,14 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
   return v;
 }
 
-__global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ sel_idx,
-                                                   const float *__restrict__ sel_w, int S, int E,
+__global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_w, int S, int E,
                                                    int32_t *__restrict__ offsets,
                                                    int32_t *__restrict__ perm,
                                                    int32_t *__restrict__ slot_pos,
                                                    int32_t *__restrict__ act_list,
                                                    int32_t *__restrict__ meta, DispatchPlan plan,
-                                                   int key_div) {
+                                                   int key_div, const float *__restrict__ logits, int T,
+                                                   int topk) {
   pdl_wait();
   pdl_trigger();
   constexpr int kScanWarps = kDispatchMaxExperts / 32;
@@ -407,6 +410,15 @@ __global__ void __launch_bounds__(1024) k_dispatch(const int32_t *__restrict__ s
   __shared__ int s_w[32 * kDispatchMaxExperts];
   __shared__ int s_tot[kScanWarps][kVals];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (logits) {
+    // selectMoEBatch for small batches (single device, key_div 1), one warp
+    // per token, before the sort; the selections also go to global memory for
+    // the later kernels, and __syncthreads makes them visible to this block.
+    // sel_idx / sel_w are plain pointers here: no read-only cache path.
+    for (int t = warp; t < T; t += (int)(blockDim.x >> 5))
+      select_token(logits, t, E, topk, lane, sel_idx, sel_w);
+    __syncthreads();
+  }
   for (int e = tid; e < E; e += blockDim.x) {
     s_cnt[e] = 0;
     s_run[e] = 0;
@@ -857,6 +869,11 @@ bool pdl_launches_enabled() {
   return on;
 }
 
+bool fused_select_enabled() {
+  const char *v = getenv("SPT_FUSED_SELECT");  // read per call: both paths stay testable
+  return !(v && v[0] == '0');
+}
+
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
@@ -899,8 +916,19 @@ cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, i
                             int32_t *act_list, int32_t *meta, cudaStream_t stream,
                             const DispatchPlan *plan, int key_div) {
   if (E > kDispatchMaxExperts || key_div < 1) return cudaErrorInvalidValue;
-  return launch_pdl(k_dispatch, dim3(1), dim3(1024), 0, stream, sel_idx, sel_w, S, E, offsets, perm, slot_pos,
-                    act_list, meta, plan ? *plan : DispatchPlan{}, key_div);
+  // the kernel only writes sel_idx / sel_w when given logits
+  return launch_pdl(k_dispatch, dim3(1), dim3(1024), 0, stream, const_cast<int32_t *>(sel_idx),
+                    const_cast<float *>(sel_w), S, E, offsets, perm, slot_pos, act_list, meta,
+                    plan ? *plan : DispatchPlan{}, key_div, (const float *)nullptr, 0, 0);
+}
+
+cudaError_t launch_select_dispatch(const float *logits, int T, int E, int K, int32_t *sel_idx, float *sel_w,
+                                   int32_t *offsets, int32_t *perm, int32_t *slot_pos, int32_t *act_list,
+                                   int32_t *meta, cudaStream_t stream, const DispatchPlan *plan) {
+  if (E > kDispatchMaxExperts || T < 0 || T > kSelectDispatchMaxTokens || K < 1 || K > E || K > kSelectMaxK)
+    return cudaErrorInvalidValue;
+  return launch_pdl(k_dispatch, dim3(1), dim3(1024), 0, stream, sel_idx, sel_w, T * K, E, offsets, perm,
+                    slot_pos, act_list, meta, plan ? *plan : DispatchPlan{}, 1, logits, T, K);
 }
 
 cudaError_t launch_ep_gather(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *meta,

@@ -57,6 +57,29 @@ def test_block_bit_exact_sweep(ctx, experts, bias_type):
                 assert np.array_equal(x.view(np.uint32), orig.view(np.uint32))
 
 
+def test_fused_selection_matches_separate(ctx, monkeypatch):
+    """Up to 8 tokens the top-k selection runs inside the dispatch kernel;
+    SPT_FUSED_SELECT=0 keeps the separate selection launch.  Both give the
+    same output bits and routing, over every router mode of the sweep."""
+    for experts, top_k in ((7, 2), (33, 4), (128, 32)):
+        for mode in refdata.ROUTER_MODES:
+            fx = refdata.moe_batch_fixture(96, 64, experts, top_k, 1, mode)
+            for batch in (1, 5, 8):
+                x = refdata.moe_batch_x(batch, 96, mode)
+                got = {}
+                for fused in ("1", "0"):
+                    monkeypatch.setenv("SPT_FUSED_SELECT", fused)
+                    out, r, _ = _run_block(ctx, fx, x, batch)
+                    got[fused] = (out, r, ctx.kernels_per_forward())
+                tag = (experts, top_k, mode, batch)
+                (a, ra, ka), (b, rb, kb) = got["1"], got["0"]
+                assert bits_equal(a, b).all(), tag
+                assert np.array_equal(ra["sel_idx"], rb["sel_idx"]), tag
+                assert bits_equal(ra["sel_w"], rb["sel_w"]).all(), tag
+                assert np.array_equal(ra["perm"], rb["perm"]), tag
+                assert ka == kb - 1, tag
+
+
 @pytest.mark.parametrize("mode", ["ties", "normal", "underflow"])
 @pytest.mark.parametrize("k", [1, 2, 8])
 def test_sparse_independent_reference(ctx, mode, k):
