@@ -473,7 +473,18 @@ bool act_maps(spt_context *ctx, int which, uint8_t *q, int kp, int rb, int bn, i
   return true;
 }
 
-int pick_bn(int64_t T, int64_t K, int64_t E) { return (T * K) <= 8 * E ? 16 : 128; }
+// Tokens per tensor-core tile from the mean tokens per expert: decode batches
+// (<= 2 per expert) take 8-token tiles, whose smaller activation stages let
+// the weight ring hold four stages; up to 8 per expert 16-token tiles; larger
+// batches 128-token tiles.  SPT_MMA_BN (8, 16 or 128) fixes the choice.
+int pick_bn(int64_t T, int64_t K, int64_t E) {
+  if (const char *v = getenv("SPT_MMA_BN")) {
+    const int b = atoi(v);
+    if (b == 8 || b == 16 || b == 128) return b;
+  }
+  const int64_t S = T * K;
+  return S <= 2 * E ? 8 : S <= 8 * E ? 16 : 128;
+}
 
 // Expert GEMMs on the tensor cores (after router/select/dispatch):
 // plan -> quantize x -> gate/up GEMM (+SwiGLU) -> quantize act -> down GEMM.

@@ -172,19 +172,13 @@ cudaError_t launch_synth_g8(uint64_t seed, uint32_t tag, int64_t first_expert, i
                             cudaStream_t stream);
 
 // Raise a kernel's dynamic shared-memory limit once per device (the setting
-// belongs to the device context that is current when it is made).
+// belongs to the device context that is current when it is made).  The
+// record is keyed by the kernel's address: template instances share one C++
+// type, and each needs its own attribute.
+cudaError_t opt_in_smem_raw(const void *kernel, int bytes);
 template <typename Kernel>
 cudaError_t opt_in_smem(Kernel kernel, int bytes) {
-  constexpr int kMaxDevices = 64;
-  static std::atomic<int> done[kMaxDevices];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) done[dev].store(bytes, std::memory_order_release);
-  return e;
+  return opt_in_smem_raw(reinterpret_cast<const void *>(kernel), bytes);
 }
 
 // Launch a kernel that begins with pdl_wait(); pdl_launches_enabled() (the

@@ -16,6 +16,8 @@
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <map>
+#include <mutex>
 
 #include "spt_device.cuh"
 #include "spt_internal.cuh"
@@ -867,6 +869,20 @@ bool pdl_launches_enabled() {
     return !(v && v[0] == '0');
   }();
   return on;
+}
+
+cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void *>, int> done;  // (device, kernel) -> bytes set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({dev, kernel});
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[{dev, kernel}] = bytes;
+  return e;
 }
 
 bool fused_select_enabled() {

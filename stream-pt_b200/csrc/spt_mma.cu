@@ -425,6 +425,26 @@ __device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float v[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]);
+// Columns [taddr, taddr + C) of this warp's 32 TMEM lanes, C = 8 or 16.
+template <int C>
+__device__ __forceinline__ void tc_ld(uint32_t taddr, float *v) {
+  static_assert(C == 8 || C == 16, "TMEM load width");
+  if constexpr (C == 8) tc_ld8(taddr, v);
+  else tc_ld16(taddr, v);
+}
+
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]) {
   uint32_t r[16];
   asm volatile(
@@ -500,7 +520,8 @@ struct MmaShape {
   static constexpr int kOffSfb = kOffSfa + KS * 512;
   static constexpr int kStage = ((kOffSfb + KS * kSfb * 512) + 1023) / 1024 * 1024;
   static constexpr int kStages = (200 * 1024) / kStage > 16 ? 16 : (200 * 1024) / kStage;
-  static constexpr int kAccCols = 2 * kN;           // double-buffered accumulator
+  static constexpr int kAccStride = (kN + 31) / 32 * 32;  // TMEM columns between the two accumulators
+  static constexpr int kAccCols = 2 * kAccStride;   // double-buffered accumulator
   static constexpr int kSfCols = KS * (4 + 4 * kSfb);  // SFA + SFB atoms of every K tile of a stage
   static constexpr int kCols = (kAccCols + kSfCols <= 32) ? 32
                                : (kAccCols + kSfCols <= 64) ? 64
@@ -637,7 +658,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
     int s = 0;
     uint32_t phase = 0;
     int local = 0;
-    const uint32_t sfa_t = tmem + 2 * S::kN;  // scale-factor columns after the two accumulators
+    const uint32_t sfa_t = tmem + S::kAccCols;  // scale-factor columns after the two accumulators
     const uint32_t base = smem_u32(smem);
     const uint64_t a_desc0 = smem_desc(base, S::kSbo, S::kLayout);
     const uint64_t b_desc0 = smem_desc(base + S::kOffB, S::kSbo, S::kLayout);
@@ -656,7 +677,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
       const uint32_t accph = (uint32_t)(local >> 1) & 1u;
       if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2)) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + buf * S::kN;
+      const uint32_t d_tmem = tmem + buf * S::kAccStride;
       uint32_t acc = 0u;
       for (int kt = 0; kt < a.ktiles; kt += KS) {
         if (!mbar_wait(&full[s], phase, a.err, 3)) {
@@ -724,17 +745,18 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
       if (!mbar_wait(&accf[buf], accph, a.err, 5)) break;
       tc_fence_after();
       const int r = t.mt * kMmaM + row_local;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        const uint32_t col = tmem + (uint32_t)(buf * S::kN + c0) + ((uint32_t)(quad * 32) << 16);
-        tc_ld16(col, v);
+      constexpr int kC = BN < 16 ? BN : 16;  // accumulator columns per TMEM load
+      for (int c0 = 0; c0 < BN; c0 += kC) {
+        float v[kC];
+        const uint32_t col = tmem + (uint32_t)(buf * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
+        tc_ld<kC>(col, v);
         if (FP4) {  // the term partial sums sit BN columns apart
 #pragma unroll
           for (int term = 1; term < kFp4Terms; ++term) {
-            float w[16];
-            tc_ld16(col + term * BN, w);
+            float w[kC];
+            tc_ld<kC>(col + term * BN, w);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += w[j];
+            for (int j = 0; j < kC; ++j) v[j] += w[j];
           }
         }
         if (a.mode == 0) {
@@ -743,7 +765,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
           const float bias = is_up ? (a.bias1 ? a.bias1[(size_t)t.e * a.out_rows + d] : 0.0f)
                                    : (a.bias0 ? a.bias0[(size_t)t.e * a.out_rows + d] : 0.0f);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < kC; ++j) {
             const float val = v[j] + bias;
             const float other = __shfl_xor_sync(0xffffffffu, val, 1);
             if (!is_up && c0 + j < t.nvalid && d < a.out_rows)
@@ -752,7 +774,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
         } else if (r < a.out_rows) {
           const float bias = a.bias0 ? a.bias0[(size_t)t.e * a.out_rows + r] : 0.0f;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
+          for (int j = 0; j < kC; ++j)
             if (c0 + j < t.nvalid) a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + r] = v[j] + bias;
         }
       }
@@ -823,8 +845,10 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {
-  if (mma_fp4(bn)) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
-  return launch_gemm_bn<128, false, 1>(a, sm_count, s);
+  if (bn == 8) return launch_gemm_bn<8, true, kMmaStageTilesFp4>(a, sm_count, s);
+  if (bn == 16) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
+  if (bn == 128) return launch_gemm_bn<128, false, 1>(a, sm_count, s);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace spt

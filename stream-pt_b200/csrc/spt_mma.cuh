@@ -5,8 +5,9 @@
 // with the GGUF E8M0 block scales, fed to the tensor core unchanged); B = the
 // activations written as a sum of block-scaled terms (see k_quantize_act), so
 // that block outputs stay well inside the 1e-3 relative tolerance:
-//   token tiles of <= 16 (decode):  kind::mxf4, kFp4Terms e2m1 terms stacked
-//     along N (N = kFp4Terms*16), both operands packed 4-bit in shared memory;
+//   token tiles of 8 or 16 (decode):  kind::mxf4, kFp4Terms e2m1 terms
+//     stacked along N (N = kFp4Terms*BN), both operands packed 4-bit in
+//     shared memory;
 //   128-token tiles (prefill):      kind::mxf8f6f4, kActTerms e4m3 terms, one
 //     N = 128 MMA per term, the weights unpacked to one byte per element by
 //     the TMA (16U4_ALIGN16B).
@@ -91,9 +92,9 @@ struct MmaLaunch {
   int prefetch = 0;                  // whole weight tiles prefetched into L2 ahead (0: off)
 };
 
-// Token tiles of at most 16 tokens run the FP4 mode (kFp4Terms e2m1 terms
+// Token tiles of 8 or 16 tokens run the FP4 mode (kFp4Terms e2m1 terms
 // stacked along N, kMmaStageTilesFp4 K tiles per stage); 128-token tiles run
-// the FP8 mode (one K tile per stage).
+// the FP8 mode (one K tile per stage).  launch_mma_gemm takes bn 8, 16 or 128.
 inline bool mma_fp4(int bn) { return bn <= 16; }
 inline int mma_stage_tiles(int bn) { return mma_fp4(bn) ? kMmaStageTilesFp4 : 1; }
 // Activation rows of one TMA box.

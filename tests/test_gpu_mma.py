@@ -67,9 +67,15 @@ def test_mma_block_matches_oracle(ctx, mma_layer, T):
     assert refdata.bits_equal(exact, want["out"].ravel()).all()
 
 
+@pytest.mark.parametrize("bn", [None, "8", "16", "128"])
 @pytest.mark.parametrize("mode", ["normal", "ties", "underflow", "clamp"])
 @pytest.mark.parametrize("experts,k", [(4, 2), (7, 7), (8, 1)])
-def test_mma_reference_fixtures(ctx, mode, experts, k):
+def test_mma_reference_fixtures(ctx, monkeypatch, mode, experts, k, bn):
+    """Every token-tile width (SPT_MMA_BN; None: the size rule) on the
+    reference's fixtures; 37 tokens over 4-8 experts put up to 37 tokens on
+    one expert, so the 8- and 16-token tiles split experts into several."""
+    if bn is not None:
+        monkeypatch.setenv("SPT_MMA_BN", bn)
     fx = refdata.moe_batch_fixture(96, 64, experts, k, 0, mode)
     batch = 37
     x = refdata.moe_batch_x(batch, 96, mode)
@@ -81,7 +87,27 @@ def test_mma_reference_fixtures(ctx, mode, experts, k):
         ctx.set_path(spt.PATH_AUTO)
         arena.close()
     want = oracle.forward_moe_batch(fx.dense, x, batch)
-    _check_close(got, want, (mode, experts, k))
+    _check_close(got, want, (mode, experts, k, bn))
+
+
+@pytest.mark.parametrize("bn", ["8", "16"])
+def test_mma_decode_tile_widths(ctx, monkeypatch, mma_layer, bn):
+    """GPT-OSS layer at decode sizes with each FP4 tile width: against the
+    oracle, and the two widths agree with each other within the tolerance."""
+    cfg, dense, arena = mma_layer
+    ctx.set_path(spt.PATH_MMA)
+    try:
+        for T in (1, 32, 64):
+            x = spt.synth_normal_host(T, 3000, T * 2880)
+            monkeypatch.setenv("SPT_MMA_BN", bn)
+            got = ctx.forward_moe_batch(arena, x, T)
+            n = min(T, 8)
+            want = oracle.forward_moe_batch(dense, x[: n * 2880], n, workers=8)
+            _check_close(got[: n * 2880], want, (bn, T))
+            monkeypatch.setenv("SPT_MMA_BN", "128")
+            _check_close(got, ctx.forward_moe_batch(arena, x, T), (bn, T, "vs 128"))
+    finally:
+        ctx.set_path(spt.PATH_AUTO)
 
 
 def test_mma_large_batch_properties(ctx, mma_layer):
