@@ -236,8 +236,23 @@ spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index,
 #define SPT_NUM_STAGES 8
 spt_status spt_set_stage_timing(spt_context *ctx, int enable);
 int spt_stage_times(spt_context *ctx, float *ms, int n);
-/* Number of kernels the last forward call launched. */
+/* Number of kernels the last forward call launched (1: the single-launch
+ * decode kernel, used for batch x top-k <= 64 on the tensor-core path when
+ * the environment variable SPT_DECODE_KERNEL=1 opts in). */
 int spt_kernels_per_forward(spt_context *ctx);
+/* Phase stamps of the last decode launch made with stage timing on: per CTA
+ * SPT_DECODE_TRACE_SLOTS %globaltimer values (ns): 0 entry, 1 router done,
+ * 2 barrier 1 passed, 3 routing done, 4 gate/up operands done, 5 barrier 2
+ * passed, 6 gate/up GEMM done, 7 barrier 3 passed, 8 down operands done,
+ * 9 barrier 4 passed, 10 down GEMM done, 11 barrier 5 passed, 12 combine
+ * done; 13 logits staged, 14 selection done, 17 dispatch done, 18/19 and
+ * 20/21 start/end of warp 0's first operand item in the two quantisation
+ * phases (0 when it had none; other slots unused).  Returns the values written, minus the count needed
+ * when stamps is NULL or cap is too small, or 0 when there is no traced
+ * launch.  With such a
+ * launch spt_stage_times derives its stages from these stamps. */
+#define SPT_DECODE_TRACE_SLOTS 24
+int64_t spt_decode_trace(spt_context *ctx, uint64_t *stamps, int64_t cap);
 
 /* ---- stage entry points (host pointers, synchronous) -------------------- */
 

@@ -239,6 +239,7 @@ def lib():
         "spt_set_stage_timing": ([vp, ctypes.c_int], st),
         "spt_stage_times": ([vp, vp, ctypes.c_int], ctypes.c_int),
         "spt_kernels_per_forward": ([vp], ctypes.c_int),
+        "spt_decode_trace": ([vp, vp, ctypes.c_int64], ctypes.c_int64),
         "spt_context_set_path": ([vp, ctypes.c_int], st),
     }
     for name, (args, res) in sigs.items():
@@ -317,6 +318,18 @@ class Context:
 
     def kernels_per_forward(self) -> int:
         return int(lib().spt_kernels_per_forward(self._h))
+
+    DECODE_TRACE_SLOTS = 24
+
+    def decode_trace(self) -> Optional[np.ndarray]:
+        """Per-CTA phase stamps (ns) of the last decode launch made with stage
+        timing on, shape [grid, 24] (spt_decode_trace), or None."""
+        need = -int(lib().spt_decode_trace(self._h, None, 0))
+        if need <= 0:
+            return None
+        out = np.zeros(need, np.uint64)
+        n = int(lib().spt_decode_trace(self._h, _p(out), out.size))
+        return out.reshape(-1, self.DECODE_TRACE_SLOTS) if n == need else None
 
     def set_path(self, path: int):
         """PATH_EXACT (CUDA-core, bit-exact), PATH_MMA (tcgen05) or PATH_AUTO."""

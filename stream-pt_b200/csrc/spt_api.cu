@@ -74,6 +74,11 @@ struct spt_context {
   int kernels_last = 0;
   DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
   DevBuf stack_norm, stack_ffn;  // layer stack: normed rows and block output [T][H]
+  DevBuf gbar;                   // decode kernel's grid-barrier counters (zero between launches)
+  DevBuf partial;                // decode kernel's split-K part sums
+  int decode_grid = -1;          // co-resident grid of the decode kernel (-1: not queried, 0: none)
+  DevBuf trace;                  // decode kernel's per-CTA phase stamps (stage timing on)
+  bool decode_traced = false;    // the last forward was a traced decode launch
   int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
   // activation tensor maps of the last call (re-encoded when the buffers or shape change)
   struct ActMaps {
@@ -486,27 +491,20 @@ int pick_bn(int64_t T, int64_t K, int64_t E) {
   return S <= 2 * E ? 8 : S <= 8 * E ? 16 : 128;
 }
 
-// Expert GEMMs on the tensor cores (after router/select/dispatch):
-// plan -> quantize x -> gate/up GEMM (+SwiGLU) -> quantize act -> down GEMM.
-spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                       int64_t T, cudaStream_t s, int bn) {
+// Launch parameters of the two tensor-core GEMMs of one forward (T tokens,
+// bn-token tiles); the tile tables they point at are the dispatch kernel's.
+spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, int64_t T, int bn,
+                       MmaLaunch *gu, MmaLaunch *dn, int *rb_out) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   const int64_t S = T * K;
   const int64_t na_max = std::min<int64_t>(E, S);
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
-  // buffers: reserve_experts
   const bool fp4 = mma_fp4(bn);
   const int ks = mma_stage_tiles(bn);
   const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
-  // pad_off, tile_gu, tile_dn and pos_expert come from the dispatch kernel
-
-  SPT_CUDA(ctx, launch_quantize_act(x, H, ctx->perm.as<int32_t>(), K, true, ctx->offsets.as<int32_t>(),
-                                    ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
-                                    ctx->meta.as<int32_t>(), (int)S, H, kph, rb, bn, ctx->qx.as<uint8_t>(),
-                                    ctx->sfx.as<uint8_t>(), s));
-  MmaLaunch g;
+  MmaLaunch &g = *gu;
   g.ks = ks;
   g.tmap_a = fp4 ? L.gu_mma.tmap_p : L.gu_mma.tmap;
   g.tmap_a1 = fp4 ? L.gu_mma.tmap_p1 : L.gu_mma.tmap;
@@ -534,33 +532,54 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.out_rows = D;
   g.err = ctx->dev_err.as<int32_t>();
   if (const char *pf = getenv("SPT_MMA_PREFETCH")) g.prefetch = atoi(pf);
+  MmaLaunch &d = *dn;
+  d = g;
+  d.tmap_a = fp4 ? L.dn_mma.tmap_p : L.dn_mma.tmap;
+  d.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
+  if (!act_maps(ctx, 1, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks, &d.tmap_b, &d.tmap_b1))
+    return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
+  d.w = L.dn_mma.w;
+  d.sfa = L.dn_mma.sf;
+  d.sfb = ctx->sfa.as<uint8_t>();
+  d.rows = L.dn_mma.rows;
+  d.kp = kpd;
+  d.mtiles = mt_dn;
+  d.ktiles = kpd / kMmaKT;
+  d.tile_off = ctx->tile_dn.as<int32_t>();
+  d.max_tiles = (int)std::min<int64_t>((int64_t)mt_dn * (na_max + S / bn + 1), 1 << 30);
+  d.mode = 1;
+  d.bias0 = L.down_bias;
+  d.bias1 = nullptr;
+  d.y = ctx->res.as<float>();
+  d.y_stride = H;
+  d.out_rows = H;
+  if (rb_out) *rb_out = rb;
+  return SPT_OK;
+}
+
+// Expert GEMMs on the tensor cores (after router/select/dispatch):
+// plan -> quantize x -> gate/up GEMM (+SwiGLU) -> quantize act -> down GEMM.
+spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
+                       int64_t T, cudaStream_t s, int bn) {
+  const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, K = (int)c.num_experts_used;
+  const int64_t S = T * K;
+  // buffers: reserve_experts; pad_off, tile_gu, tile_dn and pos_expert come
+  // from the dispatch kernel
+  MmaLaunch g, dn;
+  int rb = 0;
+  spt_status st = build_gemms(ctx, L, c, T, bn, &g, &dn, &rb);
+  if (st) return st;
+  SPT_CUDA(ctx, launch_quantize_act(x, H, ctx->perm.as<int32_t>(), K, true, ctx->offsets.as<int32_t>(),
+                                    ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
+                                    ctx->meta.as<int32_t>(), (int)S, H, g.kp, rb, bn, ctx->qx.as<uint8_t>(),
+                                    ctx->sfx.as<uint8_t>(), s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[4], s));
   SPT_CUDA(ctx, launch_mma_gemm(g, bn, ctx->sm_count, s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[5], s));
   SPT_CUDA(ctx, launch_quantize_act(ctx->act.as<float>(), D, nullptr, K, false, ctx->offsets.as<int32_t>(),
                                     ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
-                                    ctx->meta.as<int32_t>(), (int)S, D, kpd, rb, bn, ctx->qa.as<uint8_t>(),
+                                    ctx->meta.as<int32_t>(), (int)S, D, dn.kp, rb, bn, ctx->qa.as<uint8_t>(),
                                     ctx->sfa.as<uint8_t>(), s));
-  MmaLaunch dn = g;
-  dn.tmap_a = fp4 ? L.dn_mma.tmap_p : L.dn_mma.tmap;
-  dn.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
-  if (!act_maps(ctx, 1, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks, &dn.tmap_b, &dn.tmap_b1))
-    return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
-  dn.w = L.dn_mma.w;
-  dn.sfa = L.dn_mma.sf;
-  dn.sfb = ctx->sfa.as<uint8_t>();
-  dn.rows = L.dn_mma.rows;
-  dn.kp = kpd;
-  dn.mtiles = mt_dn;
-  dn.ktiles = kpd / kMmaKT;
-  dn.tile_off = ctx->tile_dn.as<int32_t>();
-  dn.max_tiles = (int)std::min<int64_t>((int64_t)mt_dn * (na_max + S / bn + 1), 1 << 30);
-  dn.mode = 1;
-  dn.bias0 = L.down_bias;
-  dn.bias1 = nullptr;
-  dn.y = ctx->res.as<float>();
-  dn.y_stride = H;
-  dn.out_rows = H;
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[6], s));
   SPT_CUDA(ctx, launch_mma_gemm(dn, bn, ctx->sm_count, s));
   ctx->kernels_last = 8;  // router, select, dispatch, quantize, gate/up, quantize, down, combine
@@ -732,6 +751,77 @@ spt_status check_layer_limits(spt_context *ctx, const spt_moe_config &c) {
   return SPT_OK;
 }
 
+// Single-launch decode block (k_moe_decode) for this call?  Opt-in with
+// SPT_DECODE_KERNEL=1: measured on B200 it is slower than the separate
+// PDL-chained kernels at every decode size (GPT-OSS layer, 256 MB L2 flush
+// between steps: T=1 66.9 vs 59.9 us, T=4 99.9 vs 93.7, T=8 138.6 vs
+// 125.7).  Then: tensor-core path with 8-token tiles, at most kDecodeMaxSlots
+// slots, the router's 32-lane order (H % 32 == 0), rows that fit its staging
+// and a co-resident grid.  With stage timing on, the kernel stamps its
+// phases instead of the per-kernel events.
+bool decode_eligible(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x, int64_t T) {
+  const int64_t H = c.hidden_dim, D = c.expert_hidden_dim, E = c.num_experts, K = c.num_experts_used;
+  if (!L.has_mma || ctx->path == SPT_PATH_EXACT || !L.router) return false;
+  const char *opt = getenv("SPT_DECODE_KERNEL");  // read per call: both paths stay testable
+  if (!opt || opt[0] != '1') return false;
+  if (T < 1 || T * K > kDecodeMaxSlots || E > kDispatchMaxExperts || H % 32 != 0 || D % 4 != 0) return false;
+  if (pick_bn(T, K, E) != kDecodeBn || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(L.router)) & 15) != 0)
+    return false;
+  if ((size_t)(1 + T) * H * 4 > decode_ring_bytes() || (size_t)(T * E) * 4 > decode_ring_bytes()) return false;
+  if (ctx->decode_grid < 0) ctx->decode_grid = decode_max_grid(ctx->sm_count);
+  return ctx->decode_grid > 0;
+}
+
+spt_status forward_decode(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
+                          float *out, int64_t T) {
+  spt_status st = reserve_experts(ctx, L, c, T, kDecodeBn);
+  if (st) return st;
+  if (!ctx->gbar.p) {
+    SPT_CUDA(ctx, ctx->gbar.ensure(2 * sizeof(uint32_t)));
+    SPT_CUDA(ctx, cudaMemsetAsync(ctx->gbar.p, 0, 2 * sizeof(uint32_t), ctx->stream));
+  }
+  SPT_CUDA(ctx, ctx->partial.ensure(decode_partial_bytes(ctx->decode_grid)));
+  DecodeLaunch d;
+  if ((st = build_gemms(ctx, L, c, T, kDecodeBn, &d.gu, &d.dn, &d.rb))) return st;
+  d.partial = ctx->partial.as<float>();
+  d.x = x;
+  d.router_w = L.router;
+  d.router_b = L.router_bias;
+  d.T = (int)T;
+  d.H = (int)c.hidden_dim;
+  d.D = (int)c.expert_hidden_dim;
+  d.E = (int)c.num_experts;
+  d.K = (int)c.num_experts_used;
+  d.logits = ctx->logits.as<float>();
+  d.sel_idx = ctx->sel_idx.as<int32_t>();
+  d.sel_w = ctx->sel_w.as<float>();
+  d.offsets = ctx->offsets.as<int32_t>();
+  d.perm = ctx->perm.as<int32_t>();
+  d.slot_pos = ctx->slot_pos.as<int32_t>();
+  d.act_list = ctx->act_list.as<int32_t>();
+  d.meta = ctx->meta.as<int32_t>();
+  d.qx = ctx->qx.as<uint8_t>();
+  d.sfx = ctx->sfx.as<uint8_t>();
+  d.qa = ctx->qa.as<uint8_t>();
+  d.sfa = ctx->sfa.as<uint8_t>();
+  d.out = out;
+  d.gbar = ctx->gbar.as<uint32_t>();
+  d.err = ctx->dev_err.as<int32_t>();
+  cudaStream_t s = ctx->stream;
+  if (ctx->timing) {
+    const size_t tb = sizeof(uint64_t) * kDecodeTraceSlots * ctx->decode_grid;
+    SPT_CUDA(ctx, ctx->trace.ensure(tb));
+    SPT_CUDA(ctx, cudaMemsetAsync(ctx->trace.p, 0, tb, s));
+    d.trace = ctx->trace.as<uint64_t>();
+  }
+  SPT_MARK(0);
+  SPT_CUDA(ctx, launch_moe_decode(d, ctx->decode_grid, s));
+  SPT_MARK(SPT_NUM_STAGES);
+  ctx->decode_traced = ctx->timing;
+  ctx->kernels_last = 1;
+  return SPT_OK;
+}
+
 // The whole block on device pointers (enqueue only).
 spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
                           float *out, int64_t T) {
@@ -744,6 +834,15 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
                 (long long)c.num_experts);
   if ((st = ensure_scratch(ctx, T, c))) return st;
   const LayerDev &L = arena->layers[(size_t)layer];
+  if (decode_eligible(ctx, L, c, x, T)) {
+    if ((st = forward_decode(ctx, L, c, x, out, T))) return st;
+    ctx->last_T = T;
+    ctx->last_E = c.num_experts;
+    ctx->last_K = c.num_experts_used;
+    ctx->have_routing = true;
+    return SPT_OK;
+  }
+  ctx->decode_traced = false;
   const bool fuse = T <= kSelectDispatchMaxTokens && fused_select_enabled();
   if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse))) return st;
   if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out, 0,
@@ -883,7 +982,7 @@ void spt_context_destroy(spt_context *ctx) {
                       &ctx->slot_pos, &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res,
                       &ctx->xdev, &ctx->outdev, &ctx->dev_err, &ctx->pad_off, &ctx->tile_gu,
                       &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa,
-                      &ctx->stack_norm, &ctx->stack_ffn})
+                      &ctx->stack_norm, &ctx->stack_ffn, &ctx->gbar, &ctx->trace, &ctx->partial})
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
@@ -903,9 +1002,35 @@ spt_status spt_set_stage_timing(spt_context *ctx, int enable) {
   return SPT_OK;
 }
 
+// Stage times of a traced decode launch from its per-CTA stamps: each stage
+// is the growth of the latest CTA's stamp from one phase end to the next
+// (barrier waits included), so the stages add up to the launch.
+int decode_stage_times(spt_context *ctx, float *ms, int n) {
+  const int grid = ctx->decode_grid;
+  std::vector<uint64_t> tr((size_t)grid * kDecodeTraceSlots);
+  if (cudaMemcpy(tr.data(), ctx->trace.p, tr.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return 0;
+  uint64_t t[kDecodeTracePoints];
+  for (int k = 0; k < kDecodeTracePoints; ++k) {
+    t[k] = k == 0 ? UINT64_MAX : 0;
+    for (int b = 0; b < grid; ++b) {
+      const uint64_t v = tr[(size_t)b * kDecodeTraceSlots + k];
+      t[k] = k == 0 ? std::min(t[k], v) : std::max(t[k], v);
+    }
+  }
+  // router, select, dispatch, quantize x, gate/up, quantize act, down, combine
+  const double st[SPT_NUM_STAGES] = {double(t[1] - t[0]), 0.0, double(t[3] - t[1]), double(t[5] - t[3]),
+                                     double(t[7] - t[5]), double(t[9] - t[7]), double(t[11] - t[9]),
+                                     double(t[12] - t[11])};
+  int w = 0;
+  for (int i = 0; i < SPT_NUM_STAGES && i < n; ++i, ++w) ms[i] = (float)(st[i] * 1e-6);
+  return w;
+}
+
 int spt_stage_times(spt_context *ctx, float *ms, int n) {
   if (!ctx || !ctx->timing || !ms) return 0;
   if (cudaEventSynchronize(ctx->ev[SPT_NUM_STAGES]) != cudaSuccess) return 0;
+  if (ctx->decode_traced) return decode_stage_times(ctx, ms, n);
   int w = 0;
   for (int i = 0; i < SPT_NUM_STAGES && i < n; ++i, ++w)
     if (cudaEventElapsedTime(&ms[i], ctx->ev[i], ctx->ev[i + 1]) != cudaSuccess) ms[i] = -1.0f;
@@ -913,6 +1038,16 @@ int spt_stage_times(spt_context *ctx, float *ms, int n) {
 }
 
 int spt_kernels_per_forward(spt_context *ctx) { return ctx ? ctx->kernels_last : 0; }
+
+int64_t spt_decode_trace(spt_context *ctx, uint64_t *stamps, int64_t cap) {
+  if (!ctx || !ctx->decode_traced || !ctx->trace.p) return 0;
+  const int64_t n = (int64_t)ctx->decode_grid * kDecodeTraceSlots;
+  if (!stamps || cap < n) return -n;
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return 0;
+  if (cudaMemcpy(stamps, ctx->trace.p, (size_t)n * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return 0;
+  return n;
+}
 
 const char *spt_last_error(const spt_context *ctx) {
   return ctx ? ctx->err.c_str() : g_tls_error.c_str();

@@ -22,6 +22,7 @@
 #include "spt_device.cuh"
 #include "spt_internal.cuh"
 #include "spt_philox.h"
+#include "spt_route.cuh"
 
 namespace spt {
 
@@ -281,84 +282,6 @@ __global__ void k_router_portable(const float *__restrict__ W, const float *__re
   float sum = 0.0f;
   for (int l = 0; l < lanes; ++l) sum += __shfl_sync(kFull, acc, l);
   if (lane == 0) logits[(size_t)t * E + e] = sum + (bias ? bias[e] : 0.0f);
-}
-
-// ---------------------------------------------------------------------------
-// selectMoEBatch: one warp per token, the token's logits held in registers
-// (expert lane + 32i in slot i).  Each pass takes the first strictly greater
-// logit among experts not yet chosen (lowest index wins ties, NaN and -Inf
-// never win); no candidate gives (index = pass, value 0), and that index
-// counts as chosen for the later passes.
-__device__ __forceinline__ void select_token(const float *__restrict__ logits, int t, int E, int K, int lane,
-                                             int32_t *__restrict__ sel_idx, float *__restrict__ sel_w) {
-  constexpr int kPer = kDispatchMaxExperts / 32;
-  const float *lg = logits + (size_t)t * E;
-  const bool in_regs = E <= 32 * kPer;  // else every pass reads the logits again
-  float lv[kPer];
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) lv[i] = (in_regs && lane + 32 * i < E) ? lg[lane + 32 * i] : 0.0f;
-  uint32_t taken = 0;  // bit i: expert lane + 32i already chosen
-  int chosen[kSelectMaxK];
-  float val[kSelectMaxK];
-  for (int r = 0; r < K; ++r) {
-    int best = -1;
-    float v = -INFINITY;
-    if (in_regs) {
-#pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !((taken >> i) & 1u) && lv[i] > v) {
-          v = lv[i];
-          best = e;
-        }
-      }
-    } else {
-      for (int e = lane; e < E; e += 32) {
-        bool already = false;
-        for (int p = 0; p < r; ++p) already |= (chosen[p] == e);
-        const float l = lg[e];
-        if (!already && l > v) {
-          v = l;
-          best = e;
-        }
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(kFull, v, off);
-      const int ob = __shfl_xor_sync(kFull, best, off);
-      if (ob >= 0 && (best < 0 || ov > v || (ov == v && ob < best))) {
-        v = ov;
-        best = ob;
-      }
-    }
-    if (best < 0) {
-      best = r;
-      v = 0.0f;
-    }
-    if ((best & 31) == lane && best < 32 * kPer) taken |= 1u << (best >> 5);
-    chosen[r] = best;
-    val[r] = v;
-  }
-  if (lane == 0) {
-    float m = -INFINITY;
-    for (int r = 0; r < K; ++r)
-      if (val[r] > m) m = val[r];
-    float sum = 0.0f;
-    for (int r = 0; r < K; ++r) {
-      const float d = __fsub_rn(val[r], m);
-      val[r] = (float)exp((double)d);
-      sum = __fadd_rn(sum, val[r]);
-    }
-    if (sum > 0.0f) {
-      const float inv = __fdiv_rn(1.0f, sum);
-      for (int r = 0; r < K; ++r) val[r] = __fmul_rn(val[r], inv);
-    }
-    for (int r = 0; r < K; ++r) {
-      sel_idx[(size_t)t * K + r] = chosen[r];
-      sel_w[(size_t)t * K + r] = val[r];
-    }
-  }
 }
 
 __global__ void __launch_bounds__(128) k_select(const float *__restrict__ logits, int T, int E,

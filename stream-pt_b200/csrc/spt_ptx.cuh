@@ -61,5 +61,10 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared memory (L2 only).
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+
 }  // namespace
 }  // namespace spt
