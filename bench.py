@@ -187,7 +187,7 @@ def mma_kind(T):
 
 def mma_dtype(T):
     if mma_fp4(T):
-        return "mxfp4 weights x 6-term e2m1 activations -> f32 (tcgen05 kind::mxf4)"
+        return "mxfp4 weights x 4-term e2m1 activations -> f32 (tcgen05 kind::mxf4)"
     return "mxfp4 weights x 3-term e4m3 activations -> f32 (tcgen05 kind::mxf8f6f4)"
 
 

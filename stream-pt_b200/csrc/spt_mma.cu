@@ -488,6 +488,22 @@ __device__ __forceinline__ void tc_ld48(uint32_t taddr, float v[48]) {
   for (int i = 0; i < 48; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float v[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]);
 // Columns [taddr, taddr + C) of this warp's 32 TMEM lanes, C = 8 or 16.
 template <int C>
@@ -827,10 +843,11 @@ struct GemmCta {
       for (int c0 = 0; c0 < BN; c0 += kC) {
         float v[kC];
         const uint32_t col = tmem + (uint32_t)(buf * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
-        if constexpr (FP4 && BN == 8 && kFp4Terms == 6) {
-          // the six term partial sums are 48 consecutive columns: one round trip
-          float w[48];
-          tc_ld48(col, w);
+        if constexpr (FP4 && BN == 8 && (kFp4Terms == 6 || kFp4Terms == 4)) {
+          // the term partial sums are consecutive columns: one round trip
+          float w[kFp4Terms * 8];
+          if constexpr (kFp4Terms == 6) tc_ld48(col, w);
+          else tc_ld32(col, w);
 #pragma unroll
           for (int j = 0; j < kC; ++j) v[j] = w[j];
 #pragma unroll

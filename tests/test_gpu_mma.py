@@ -128,13 +128,14 @@ def test_mma_large_batch_properties(ctx, mma_layer):
     ctx.set_path(spt.PATH_AUTO)
 
 
-@pytest.mark.parametrize("T", [1, 3, 8, 16])
+@pytest.mark.parametrize("T", [1, 3, 8, 12])
 def test_decode_kernel_matches_separate_kernels(ctx, monkeypatch, mma_layer, T):
     """The single-launch decode block (k_moe_decode) against the separate
     tensor-core kernels with the same 8-token tiles: identical routing, and
     identical output bits where no GEMM is split along K (T >= 8 here: at
     least 4 tiles per CTA); split GEMMs add their K parts in another order,
-    so T = 1 and 3 agree to rounding.  Repeated launches check that the
+    so T = 1 and 3 agree to rounding (1e-4 of the largest output, a tenth
+    of the block tolerance).  Repeated launches check that the
     grid-barrier counters reset between launches."""
     cfg, dense, arena = mma_layer
     ctx.set_path(spt.PATH_MMA)
@@ -155,7 +156,7 @@ def test_decode_kernel_matches_separate_kernels(ctx, monkeypatch, mma_layer, T):
                 assert refdata.bits_equal(got, want).all(), (T, rep)
             else:
                 err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
-                assert err <= 1e-5, (T, rep, err)
+                assert err <= 1e-4, (T, rep, err)
             assert refdata.bits_equal(r1["logits"], r0["logits"]).all()
             assert np.array_equal(r1["sel_idx"], r0["sel_idx"])
             assert refdata.bits_equal(r1["sel_w"], r0["sel_w"]).all()
