@@ -493,8 +493,9 @@ int pick_bn(int64_t T, int64_t K, int64_t E) {
 
 // Launch parameters of the two tensor-core GEMMs of one forward (T tokens,
 // bn-token tiles); the tile tables they point at are the dispatch kernel's.
+// ks_fixed > 0 fixes the K tiles per stage (the decode kernel's GEMMs).
 spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, int64_t T, int bn,
-                       MmaLaunch *gu, MmaLaunch *dn, int *rb_out) {
+                       MmaLaunch *gu, MmaLaunch *dn, int *rb_out, int ks_fixed = 0) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   const int64_t S = T * K;
@@ -502,11 +503,17 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
   const bool fp4 = mma_fp4(bn);
-  const int ks = mma_stage_tiles(bn);
   const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
+  // one stage size for both GEMMs (they share the activation map cache), from
+  // an estimate of the down GEMM's row tiles: its host bound halved (the bound
+  // puts every slot on its own expert and counts partial token tiles twice)
+  const int ks = ks_fixed > 0 ? ks_fixed
+                              : mma_stage_tiles(bn, (int64_t)std::min(mt_gu, mt_dn) * (na_max + S / bn + 1) / 2,
+                                                ctx->sm_count);
+  const bool wide = ks == kMmaStageTilesWide && fp4;
   MmaLaunch &g = *gu;
   g.ks = ks;
-  g.tmap_a = fp4 ? L.gu_mma.tmap_p : L.gu_mma.tmap;
+  g.tmap_a = fp4 ? (wide ? L.gu_mma.tmap_pw : L.gu_mma.tmap_p) : L.gu_mma.tmap;
   g.tmap_a1 = fp4 ? L.gu_mma.tmap_p1 : L.gu_mma.tmap;
   if (!act_maps(ctx, 0, ctx->qx.as<uint8_t>(), kph, rb, bn, ks, &g.tmap_b, &g.tmap_b1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
@@ -534,7 +541,7 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   if (const char *pf = getenv("SPT_MMA_PREFETCH")) g.prefetch = atoi(pf);
   MmaLaunch &d = *dn;
   d = g;
-  d.tmap_a = fp4 ? L.dn_mma.tmap_p : L.dn_mma.tmap;
+  d.tmap_a = fp4 ? (wide ? L.dn_mma.tmap_pw : L.dn_mma.tmap_p) : L.dn_mma.tmap;
   d.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
   if (!act_maps(ctx, 1, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks, &d.tmap_b, &d.tmap_b1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
@@ -782,7 +789,7 @@ spt_status forward_decode(spt_context *ctx, const LayerDev &L, const spt_moe_con
   }
   SPT_CUDA(ctx, ctx->partial.ensure(decode_partial_bytes(ctx->decode_grid)));
   DecodeLaunch d;
-  if ((st = build_gemms(ctx, L, c, T, kDecodeBn, &d.gu, &d.dn, &d.rb))) return st;
+  if ((st = build_gemms(ctx, L, c, T, kDecodeBn, &d.gu, &d.dn, &d.rb, kMmaStageTilesFp4))) return st;
   d.partial = ctx->partial.as<float>();
   d.x = x;
   d.router_w = L.router;

@@ -76,9 +76,11 @@ bool mma_encode_weights(MmaMatrix *m) {
   cuuint64_t dims3[3] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)kMmaM, (cuuint64_t)boxes};
   cuuint64_t strides3[2] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)(kMmaKT / 2) * kMmaM};
   cuuint32_t estr3[3] = {1, 1, 1};
-  for (int one = 0; one < 2; ++one) {
-    cuuint32_t box3[3] = {(cuuint32_t)(kMmaKT / 2), (cuuint32_t)kMmaM, one ? 1u : (cuuint32_t)kMmaStageTilesFp4};
-    r = fn(one ? &m->tmap_p1 : &m->tmap_p, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, m->w, dims3, strides3, box3, estr3,
+  for (int which = 0; which < 3; ++which) {
+    const cuuint32_t nbox = which == 0 ? kMmaStageTilesFp4 : which == 1 ? 1u : (cuuint32_t)kMmaStageTilesWide;
+    cuuint32_t box3[3] = {(cuuint32_t)(kMmaKT / 2), (cuuint32_t)kMmaM, nbox};
+    CUtensorMap *map = which == 0 ? &m->tmap_p : which == 1 ? &m->tmap_p1 : &m->tmap_pw;
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, m->w, dims3, strides3, box3, estr3,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;
@@ -1461,8 +1463,9 @@ cudaError_t launch_moe_decode(const DecodeLaunch &d, int grid, cudaStream_t s) {
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {
-  if (bn == 8) return launch_gemm_bn<8, true, kMmaStageTilesFp4>(a, sm_count, s);
-  if (bn == 16) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
+  if (bn == 8 && a.ks == kMmaStageTilesWide) return launch_gemm_bn<8, true, kMmaStageTilesWide>(a, sm_count, s);
+  if (bn == 8 && a.ks == kMmaStageTilesFp4) return launch_gemm_bn<8, true, kMmaStageTilesFp4>(a, sm_count, s);
+  if (bn == 16 && a.ks == kMmaStageTilesFp4) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
   if (bn == 128) return launch_gemm_bn<128, false, 1>(a, sm_count, s);
   return cudaErrorInvalidValue;
 }
