@@ -478,17 +478,20 @@ bool act_maps(spt_context *ctx, int which, uint8_t *q, int kp, int rb, int bn, i
   return true;
 }
 
-// Tokens per tensor-core tile from the mean tokens per expert: decode batches
-// (<= 2 per expert) take 8-token tiles, whose smaller activation stages let
-// the weight ring hold four stages; up to 8 per expert 16-token tiles; larger
-// batches 128-token tiles.  SPT_MMA_BN (8, 16 or 128) fixes the choice.
+// Tokens per tensor-core tile from the mean tokens per expert: up to 5 per
+// expert 8-token tiles (smaller activation stages; an expert with more tokens
+// takes a second tile, whose weights mostly come from L2), up to 8 per expert
+// 16-token tiles, larger batches 128-token tiles.  Measured on B200 (GPT-OSS
+// layer, 8 vs 16 tokens): T=96 378.6 vs 410.5 us, T=128 389.1 vs 417.5,
+// T=192 433.9 vs 434.6, T=256 514.9 vs 451.5.  SPT_MMA_BN (8, 16 or 128)
+// fixes the choice.
 int pick_bn(int64_t T, int64_t K, int64_t E) {
   if (const char *v = getenv("SPT_MMA_BN")) {
     const int b = atoi(v);
     if (b == 8 || b == 16 || b == 128) return b;
   }
   const int64_t S = T * K;
-  return S <= 2 * E ? 8 : S <= 8 * E ? 16 : 128;
+  return S <= 5 * E ? 8 : S <= 8 * E ? 16 : 128;
 }
 
 // Launch parameters of the two tensor-core GEMMs of one forward (T tokens,
