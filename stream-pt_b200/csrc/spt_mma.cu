@@ -1,19 +1,22 @@
 // spt_mma.cu -- tcgen05 block-scaled grouped GEMM for the MoE experts
 // (layouts and numerics: spt_mma.cuh).
 //
-// One persistent CTA per SM, 6 warps:
-//   warp 0  TMA producer: weight tile (e2m1, unpacked to 16-byte groups by the
-//           TMA) + three activation tiles (e4m3) + their E8M0 scale atoms,
-//           into an NS-stage shared-memory ring guarded by mbarriers;
+// One persistent CTA per SM, 6 warps (GemmCta):
+//   warp 0  TMA producer: per stage `ks` K tiles of the weight tile (packed
+//           e2m1 for kind::mxf4, or unpacked to 16-byte groups by the TMA for
+//           kind::mxf8f6f4), the activation terms and their E8M0 scale atoms,
+//           into a shared-memory ring guarded by mbarriers;
 //   warp 1  TMEM owner and single-thread MMA issuer: per stage it copies the
-//           scale atoms to TMEM (tcgen05.cp) and issues 4 K-steps x 3
-//           activation terms of tcgen05.mma.kind::mxf8f6f4.block_scale into a
-//           double-buffered fp32 accumulator;
+//           scale atoms to TMEM (tcgen05.cp) and issues the block-scaled MMAs
+//           (kind::mxf4: the terms stacked along N; kind::mxf8f6f4: one MMA
+//           per term) into a double-buffered fp32 accumulator;
 //   warps 2-5 epilogue: tcgen05.ld of the accumulator (lane = output row),
-//           bias, fused SwiGLU (gate/up rows are interleaved, so a row pair
-//           sits in neighbouring lanes) or the down projection, fp32 stores.
+//           the term sums, bias, fused SwiGLU (gate/up rows are interleaved,
+//           so a row pair sits in neighbouring lanes) or the down projection,
+//           fp32 stores.
 // Every mbarrier wait is bounded; on timeout the CTA records an error code
-// in `err`, drains its tensor-core work and exits.
+// in `err`, drains its tensor-core work and exits.  The same roles run the
+// two GEMMs of the single-launch decode kernel (k_moe_decode, below).
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>

@@ -30,7 +30,7 @@
 // Activations (per call), K-tile-major plus scale atoms.  Every BN-token tile
 // owns one 128-row slot starting at pad_off[e] + (j/BN)*128 for token j of
 // expert e, so its scale atom starts at slot row 0.
-//   FP4: term t, token j at slot row t*16 + j%16; q [KP/128][RB][64],
+//   FP4: term t, token j at slot row t*BN + j%BN; q [KP/128][RB][64],
 //        sf [RB/128][KP/128][512].
 //   FP8: q [KP/128][kActTerms][RB][128], sf [RB/128][KP/128][kActTerms][512].
 #pragma once
@@ -127,7 +127,7 @@ size_t mma_sf_bytes(int64_t experts, int rows, int k);
 // Encode the TMA map of a packed e2m1 matrix (returns false on failure).
 bool mma_encode_weights(MmaMatrix *m);
 // TMA map of the activations in the layout of mode mma_fp4(bn): FP4
-// [kt][rb][64 B] with box 64 B x 6*bn rows x ktiles (SW64); FP8
+// [kt][rb][64 B] with box 64 B x kFp4Terms*bn rows x ktiles (SW64); FP8
 // [kt][kActTerms][rb][128 B] with box 128 B x bn rows x kActTerms x ktiles (SW128).
 bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, int ktiles);
 
@@ -159,7 +159,9 @@ cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream
 // the activation operands, the gate/up GEMM with SwiGLU, the SwiGLU
 // operands, the down GEMM and the combine, separated by grid barriers.
 // Same arithmetic as the separate kernels of the tensor-core path with
-// kDecodeBn-token tiles, so the two paths give identical bits.
+// kDecodeBn-token tiles and four K tiles per stage, so the two paths give
+// identical bits, except that a GEMM with fewer than 4 tiles per CTA is split
+// along K (its part sums add in another order: equal to rounding).
 constexpr int kDecodeBn = 8;
 constexpr int kDecodeMaxSlots = 64;  // tokens x top-k
 struct DecodeLaunch {
