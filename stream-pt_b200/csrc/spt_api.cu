@@ -746,6 +746,7 @@ spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_confi
                         int64_t T, int32_t *sel_idx, float *sel_w, bool select = true) {
   const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
+  ctx->decode_traced = false;  // this forward's stage times come from its events
   SPT_MARK(0);
   SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s));
   SPT_MARK(1);
@@ -852,7 +853,6 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     ctx->have_routing = true;
     return SPT_OK;
   }
-  ctx->decode_traced = false;
   const bool fuse = T <= kSelectDispatchMaxTokens && fused_select_enabled();
   if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse))) return st;
   if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out, 0,
