@@ -272,7 +272,7 @@ def run_ours(args):
     params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
                              router_bias=c["router_bias"])
     ctx = spt.Context(local)
-    flags = spt.ARENA_MMA if args.path == "mma" else spt.ARENA_GEMV
+    flags = spt.ARENA_GEMV if args.path == "exact" else spt.ARENA_MMA
     layers = c.get("layers", 1)
     ep = None
     if world > 1:
@@ -287,7 +287,7 @@ def run_ours(args):
         ep.set_capacity(T)  # fixed-capacity exchange: no host synchronisation per step
     else:
         arena = ctx.synthetic_arena(cfg, params, n_layers=layers, flags=flags)
-    ctx.set_path(spt.PATH_MMA if args.path == "mma" else spt.PATH_EXACT)
+    ctx.set_path({"mma": spt.PATH_MMA, "exact": spt.PATH_EXACT, "auto": spt.PATH_AUTO, "gemv16": spt.PATH_GEMV16}[args.path])
     stream = torch.cuda.ExternalStream(ctx.stream)
     x_host = spt.synth_normal_host(c["seed"] + 7919 * rank, 1000, T * H)
     x_dev = torch.from_numpy(x_host).to(f"cuda:{local}")
@@ -544,7 +544,7 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["q80"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--path", default="mma", choices=["mma", "exact"],
+    ap.add_argument("--path", default="auto", choices=["auto", "mma", "gemv16", "exact"],
                     help="expert GEMMs on tcgen05 (mma) or the bit-exact CUDA-core GEMV (exact)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

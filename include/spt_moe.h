@@ -171,14 +171,50 @@ spt_status spt_synth_normal_host(uint64_t seed, uint64_t stream, float mean, flo
 
 /* SPT_PATH_EXACT: CUDA-core MXFP4 GEMV reproducing the reference's AVX2
  * arithmetic bit for bit (needs an SPT_ARENA_GEMV arena).
- * SPT_PATH_MMA: tcgen05 block-scaled GEMM, FP4 weights x 3-term MXFP8
- * activations, fp32 accumulation; routing stays bit-exact, block outputs
- * agree with the reference to ~1e-5 relative (needs SPT_ARENA_MMA).
- * SPT_PATH_AUTO (default): MMA when the arena has it, else EXACT. */
+ * SPT_PATH_MMA: tcgen05 block-scaled grouped GEMM on the packed FP4 weights,
+ * activations written as block-scaled terms (4 e2m1 terms for token tiles of
+ * 8 or 16, 3 e4m3 terms for 128-token tiles), fp32 accumulation; routing
+ * stays bit-exact, block outputs agree with the reference to a few 1e-4 of
+ * the largest output (needs SPT_ARENA_MMA).
+ * SPT_PATH_GEMV16: decode GEMV on the same packed weights: in-register
+ * dequantisation to f16, activations as two f16 terms, fp32 sums; block
+ * outputs agree with the reference to ~1e-6 (needs SPT_ARENA_MMA with every
+ * E8M0 scale byte in [104, 140], K <= 3072).
+ * SPT_PATH_AUTO (default): on an SPT_ARENA_MMA arena, the decode GEMV while
+ * batch x top-k <= SPT_OPT_GEMV16_SLOTS (and the layer's scales allow it),
+ * the tcgen05 GEMM above; else EXACT. */
 #define SPT_PATH_AUTO 0
 #define SPT_PATH_EXACT 1
 #define SPT_PATH_MMA 2
+#define SPT_PATH_GEMV16 3
 spt_status spt_context_set_path(spt_context *ctx, int path);
+
+/* Per-context tuning and test options.  Values are seeded once, when the
+ * context is created, from the environment variable named beside each.
+ *   SPT_OPT_TILE_TOKENS   tcgen05 token-tile width 8, 16 or 128; 0 picks it
+ *                         from the batch (SPT_MMA_BN)
+ *   SPT_OPT_FUSED_SELECT  1: top-k selection runs inside the dispatch kernel
+ *                         for batches of up to 8 tokens; 0: its own launch
+ *                         (SPT_FUSED_SELECT)
+ *   SPT_OPT_L2_PREFETCH   tcgen05 weight tiles prefetched into L2 ahead of
+ *                         the ring, 0 off (SPT_MMA_PREFETCH)
+ *   SPT_OPT_GEMV16_SLOTS  SPT_PATH_AUTO runs the decode GEMV while
+ *                         batch x top-k <= value (default 16;
+ *                         SPT_GEMV16_SLOTS)
+ *   SPT_OPT_WAIT_LIMIT    every bounded device wait gives up after about
+ *                         2^value clock cycles, 10..31 (default 31, about a
+ *                         second) and the call returns SPT_ERR_TIMEOUT
+ *   SPT_OPT_FAULT_STAGE   test hook, -1 off: the tcgen05 producer of CTA 0
+ *                         skips this pipeline stage, so the MMA issuer's wait
+ *                         for it runs out (the failure path without a fault) */
+#define SPT_OPT_TILE_TOKENS 1
+#define SPT_OPT_FUSED_SELECT 2
+#define SPT_OPT_L2_PREFETCH 3
+#define SPT_OPT_GEMV16_SLOTS 4
+#define SPT_OPT_WAIT_LIMIT 5
+#define SPT_OPT_FAULT_STAGE 6
+spt_status spt_context_set_option(spt_context *ctx, int option, int64_t value);
+int64_t spt_context_get_option(const spt_context *ctx, int option);
 
 /* ---- the block ----------------------------------------------------------- */
 
@@ -229,30 +265,16 @@ spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index,
 /* Per-stage device timing of the block.  When enabled, every forward call
  * records CUDA events on the context stream around its stages; spt_stage_times
  * returns the durations (ms) of the last call:
- * [0] router, [1] select, [2] dispatch, [3] tile plan + activation quantisation,
- * [4] gate/up + SwiGLU, [5] quantisation of the SwiGLU output, [6] down,
- * [7] combine (stages 3 and 5 are empty on the exact path).
+ * [0] router, [1] select, [2] dispatch, [3] activation operand (tcgen05:
+ * quantisation into terms; decode GEMV: the f16 split), [4] gate/up +
+ * SwiGLU, [5] quantisation of the SwiGLU output (tcgen05 only), [6] down,
+ * [7] combine (stage 3 is empty on the exact path, stage 5 on the others).
  * Returns the number of stages written (<= n). */
 #define SPT_NUM_STAGES 8
 spt_status spt_set_stage_timing(spt_context *ctx, int enable);
 int spt_stage_times(spt_context *ctx, float *ms, int n);
-/* Number of kernels the last forward call launched (1: the single-launch
- * decode kernel, used for batch x top-k <= 64 on the tensor-core path when
- * the environment variable SPT_DECODE_KERNEL=1 opts in). */
+/* Number of kernels the last forward call launched. */
 int spt_kernels_per_forward(spt_context *ctx);
-/* Phase stamps of the last decode launch made with stage timing on: per CTA
- * SPT_DECODE_TRACE_SLOTS %globaltimer values (ns): 0 entry, 1 router done,
- * 2 barrier 1 passed, 3 routing done, 4 gate/up operands done, 5 barrier 2
- * passed, 6 gate/up GEMM done, 7 barrier 3 passed, 8 down operands done,
- * 9 barrier 4 passed, 10 down GEMM done, 11 barrier 5 passed, 12 combine
- * done; 13 logits staged, 14 selection done, 17 dispatch done, 18/19 and
- * 20/21 start/end of warp 0's first operand item in the two quantisation
- * phases (0 when it had none; other slots unused).  Returns the values written, minus the count needed
- * when stamps is NULL or cap is too small, or 0 when there is no traced
- * launch.  With such a
- * launch spt_stage_times derives its stages from these stamps. */
-#define SPT_DECODE_TRACE_SLOTS 24
-int64_t spt_decode_trace(spt_context *ctx, uint64_t *stamps, int64_t cap);
 
 /* ---- stage entry points (host pointers, synchronous) -------------------- */
 

@@ -37,6 +37,19 @@ class MoEWeights(ctypes.Structure):
     ]
 
 
+class SynthParams(ctypes.Structure):
+    """The benchmark's synthetic-layer parameters (spo_synth_params)."""
+    _fields_ = [("seed", ctypes.c_uint64), ("router_std", ctypes.c_float), ("bias_std", ctypes.c_float),
+                ("scale_lo", ctypes.c_uint8), ("scale_hi", ctypes.c_uint8), ("expert_bias", ctypes.c_uint8),
+                ("router_bias", ctypes.c_uint8), ("zipf_s", ctypes.c_float), ("zipf_beta", ctypes.c_float)]
+
+
+def synth_params(seed=0, router_std=0.02, bias_std=0.01, scale_lo=119, scale_hi=123, expert_bias=True,
+                 router_bias=True, zipf_s=0.0, zipf_beta=0.0) -> SynthParams:
+    return SynthParams(seed, router_std, bias_std, scale_lo, scale_hi, int(expert_bias), int(router_bias),
+                       zipf_s, zipf_beta)
+
+
 _lib = None
 
 
@@ -75,6 +88,13 @@ def lib():
         L.spo_dot_q80.argtypes = [vp, vp, i64]; L.spo_dot_q80.restype = f32
         L.spo_mul_q80.argtypes = [vp, i64, i64, vp, vp, vp, i32]; L.spo_mul_q80.restype = i64
         L.spo_has_avx2.restype = i32
+        L.spo_synth_layer.argtypes = [ctypes.POINTER(SynthParams), i64, i64, i64, i64, vp, vp, vp, vp, vp, vp,
+                                      vp, vp, i32]
+        L.spo_synth_layer.restype = i32
+        L.spo_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint32, f32, f32, vp, i64]
+        L.spo_synth_normal.restype = None
+        L.spo_synth_norm.argtypes = [ctypes.c_uint64, i64, i64, vp]
+        L.spo_synth_norm.restype = None
         L.spo_fmaf_vec.argtypes = [vp, vp, vp, vp, i64]; L.spo_fmaf_vec.restype = None
         L.spo_init()
         _lib = L
@@ -216,4 +236,39 @@ def fmaf(a, b, c) -> np.ndarray:
     a, b, c = (np.ascontiguousarray(v, dtype=np.float32) for v in (a, b, c))
     out = np.empty(a.shape, np.float32)
     lib().spo_fmaf_vec(_p(a), _p(b), _p(c), _p(out), out.size)
+    return out
+
+
+def synth_layer(hidden, expert_dim, experts, params: SynthParams, layer=0, threads=None) -> dict:
+    """One synthetic layer in GGUF tensor layout, generated by the oracle
+    (same bytes as the CUDA library's generator)."""
+    H, D, E = hidden, expert_dim, experts
+    out = dict(router=np.empty(E * H * 4, np.uint8), router_bias=np.empty(E, np.float32),
+               gate=np.empty(E * D * (H // 32) * 17, np.uint8), up=np.empty(E * D * (H // 32) * 17, np.uint8),
+               down=np.empty(E * H * (D // 32) * 17, np.uint8), gate_bias=np.empty(E * D, np.float32),
+               up_bias=np.empty(E * D, np.float32), down_bias=np.empty(E * H, np.float32))
+    o = out
+    r = lib().spo_synth_layer(ctypes.byref(params), H, D, E, layer, _p(o["router"]), _p(o["router_bias"]),
+                              _p(o["gate"]), _p(o["up"]), _p(o["down"]), _p(o["gate_bias"]), _p(o["up_bias"]),
+                              _p(o["down_bias"]), threads or os.cpu_count() or 1)
+    if r != 0:
+        raise ValueError("invalid synthetic layer dimensions")
+    return out
+
+
+def synth_weights(hidden, expert_dim, experts, top_k, params: SynthParams, layer=0, threads=None) -> Weights:
+    h = synth_layer(hidden, expert_dim, experts, params, layer, threads)
+    return Weights(hidden, expert_dim, experts, top_k, h["router"], h["router_bias"], h["gate"], h["up"],
+                   h["down"], h["gate_bias"], h["up_bias"], h["down_bias"])
+
+
+def synth_normal(seed, stream, n, mean=0.0, std=1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().spo_synth_normal(seed, stream & 0xFFFFFFFF, mean, std, _p(out), n)
+    return out
+
+
+def synth_norm(seed, layer, dim) -> np.ndarray:
+    out = np.empty(dim, np.float32)
+    lib().spo_synth_norm(seed, layer, dim, _p(out))
     return out

@@ -139,6 +139,27 @@ int64_t spo_mul_q80(const uint8_t *data, int64_t input, int64_t output, const fl
 /* out[i] = fmaf(a[i], b[i], c[i]) (single rounding), for test references. */
 void spo_fmaf_vec(const float *a, const float *b, const float *c, float *out, int64_t n);
 
+/* ---- the benchmark's synthetic layer (spt_synth.c) ----------------------
+ * Seeded GPT-OSS-style weights with the same bytes as the CUDA library's own
+ * generator, so the CPU baseline needs nothing from the library under test. */
+typedef struct spo_synth_params {
+  uint64_t seed;
+  float router_std, bias_std;
+  uint8_t scale_lo, scale_hi;
+  uint8_t expert_bias, router_bias;
+  float zipf_s, zipf_beta;
+} spo_synth_params;
+/* One layer in GGUF tensor layout (any output may be NULL); MXFP4 tensors
+ * are generated on `threads` threads.  Returns 0, or -1 on bad dimensions. */
+int spo_synth_layer(const spo_synth_params *p, int64_t hidden, int64_t expert_dim, int64_t experts,
+                    int64_t layer, uint8_t *router, float *router_bias, uint8_t *gate, uint8_t *up,
+                    uint8_t *down, float *gate_bias, float *up_bias, float *down_bias, int threads);
+void spo_synth_router_bias(const spo_synth_params *p, int64_t experts, int64_t layer, float *bias);
+/* n Gaussians N(mean, sd) of tensor tag `tag` (activations: tag = stream). */
+void spo_synth_normal(uint64_t seed, uint32_t tag, float mean, float sd, float *out, int64_t n);
+/* RMSNorm weights N(1, 0.02) of a synthetic layer. */
+void spo_synth_norm(uint64_t seed, int64_t layer, int64_t dim, float *out);
+
 /* 1 if this build's AVX2 kernels are in use, else 0 (scalar fallback). */
 int spo_has_avx2(void);
 

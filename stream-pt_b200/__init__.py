@@ -29,7 +29,9 @@ ERR_UNSUPPORTED, ERR_NO_DEVICE = 13, 14
 
 ARENA_GEMV, ARENA_MMA = 1, 2
 ERR_FORMAT = 15
-PATH_AUTO, PATH_EXACT, PATH_MMA = 0, 1, 2
+PATH_AUTO, PATH_EXACT, PATH_MMA, PATH_GEMV16 = 0, 1, 2, 3
+# spt_context_set_option (include/spt_moe.h)
+OPT_TILE_TOKENS, OPT_FUSED_SELECT, OPT_L2_PREFETCH, OPT_GEMV16_SLOTS, OPT_WAIT_LIMIT, OPT_FAULT_STAGE = 1, 2, 3, 4, 5, 6
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
 
@@ -239,8 +241,9 @@ def lib():
         "spt_set_stage_timing": ([vp, ctypes.c_int], st),
         "spt_stage_times": ([vp, vp, ctypes.c_int], ctypes.c_int),
         "spt_kernels_per_forward": ([vp], ctypes.c_int),
-        "spt_decode_trace": ([vp, vp, ctypes.c_int64], ctypes.c_int64),
         "spt_context_set_path": ([vp, ctypes.c_int], st),
+        "spt_context_set_option": ([vp, ctypes.c_int, i64], st),
+        "spt_context_get_option": ([vp, ctypes.c_int], i64),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -319,21 +322,17 @@ class Context:
     def kernels_per_forward(self) -> int:
         return int(lib().spt_kernels_per_forward(self._h))
 
-    DECODE_TRACE_SLOTS = 24
-
-    def decode_trace(self) -> Optional[np.ndarray]:
-        """Per-CTA phase stamps (ns) of the last decode launch made with stage
-        timing on, shape [grid, 24] (spt_decode_trace), or None."""
-        need = -int(lib().spt_decode_trace(self._h, None, 0))
-        if need <= 0:
-            return None
-        out = np.zeros(need, np.uint64)
-        n = int(lib().spt_decode_trace(self._h, _p(out), out.size))
-        return out.reshape(-1, self.DECODE_TRACE_SLOTS) if n == need else None
-
     def set_path(self, path: int):
-        """PATH_EXACT (CUDA-core, bit-exact), PATH_MMA (tcgen05) or PATH_AUTO."""
+        """PATH_EXACT (CUDA-core, bit-exact), PATH_MMA (tcgen05), PATH_GEMV16
+        (decode GEMV on the packed planes) or PATH_AUTO."""
         self.check(lib().spt_context_set_path(self._h, path))
+
+    def set_option(self, option: int, value: int):
+        """spt_context_set_option (OPT_* constants)."""
+        self.check(lib().spt_context_set_option(self._h, option, int(value)))
+
+    def get_option(self, option: int) -> int:
+        return int(lib().spt_context_get_option(self._h, option))
 
     # ---- validation -----------------------------------------------------
     def validate(self, reader: Reader, cfg: Config, lw: LayerWeights):

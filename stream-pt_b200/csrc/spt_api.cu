@@ -74,12 +74,16 @@ struct spt_context {
   int kernels_last = 0;
   DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
   DevBuf stack_norm, stack_ffn;  // layer stack: normed rows and block output [T][H]
-  DevBuf gbar;                   // decode kernel's grid-barrier counters (zero between launches)
-  DevBuf partial;                // decode kernel's split-K part sums
-  int decode_grid = -1;          // co-resident grid of the decode kernel (-1: not queried, 0: none)
-  DevBuf trace;                  // decode kernel's per-CTA phase stamps (stage timing on)
-  bool decode_traced = false;    // the last forward was a traced decode launch
+  DevBuf xq, xe, actq, act_off;  // decode GEMV: split x rows, their exponents, split SwiGLU rows,
+                                 // first dispatch position of each active expert
   int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
+  // tuning options (spt_context_set_option), seeded from the environment once
+  int opt_tile_tokens = 0;      // tcgen05 token-tile width (0: from the batch)
+  int opt_fused_select = 1;     // top-k inside the dispatch kernel for T <= kSelectDispatchMaxTokens
+  int opt_prefetch = 0;         // tcgen05 weight tiles prefetched into L2 ahead
+  int opt_gemv16_slots = 16;    // SPT_PATH_AUTO: decode GEMV while batch x top-k <= this
+  int opt_wait_shift = 31;      // bounded device waits give up after 2^shift clock cycles
+  int opt_fault_stage = -1;     // failure injection: the tcgen05 producer skips this stage (tests)
   // activation tensor maps of the last call (re-encoded when the buffers or shape change)
   struct ActMaps {
     const void *q = nullptr;
@@ -125,6 +129,10 @@ spt_status fail(spt_context *ctx, spt_status st, const char *fmt, ...) {
 
 spt_status cuda_fail(spt_context *ctx, cudaError_t e, const char *what) {
   return fail(ctx, SPT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+spt_status cuda_ok(spt_context *ctx, cudaError_t e, const char *what) {
+  return e == cudaSuccess ? SPT_OK : cuda_fail(ctx, e, what);
 }
 
 #define SPT_CUDA(ctx, call)                                  \
@@ -483,13 +491,10 @@ bool act_maps(spt_context *ctx, int which, uint8_t *q, int kp, int rb, int bn, i
 // takes a second tile, whose weights mostly come from L2), up to 8 per expert
 // 16-token tiles, larger batches 128-token tiles.  Measured on B200 (GPT-OSS
 // layer, 8 vs 16 tokens): T=96 378.6 vs 410.5 us, T=128 389.1 vs 417.5,
-// T=192 433.9 vs 434.6, T=256 514.9 vs 451.5.  SPT_MMA_BN (8, 16 or 128)
-// fixes the choice.
-int pick_bn(int64_t T, int64_t K, int64_t E) {
-  if (const char *v = getenv("SPT_MMA_BN")) {
-    const int b = atoi(v);
-    if (b == 8 || b == 16 || b == 128) return b;
-  }
+// T=192 433.9 vs 434.6, T=256 514.9 vs 451.5.  The context option
+// SPT_OPT_TILE_TOKENS (8, 16 or 128) fixes the choice.
+int pick_bn(const spt_context *ctx, int64_t T, int64_t K, int64_t E) {
+  if (ctx->opt_tile_tokens) return ctx->opt_tile_tokens;
   const int64_t S = T * K;
   return S <= 5 * E ? 8 : S <= 8 * E ? 16 : 128;
 }
@@ -541,7 +546,9 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.y_stride = D;
   g.out_rows = D;
   g.err = ctx->dev_err.as<int32_t>();
-  if (const char *pf = getenv("SPT_MMA_PREFETCH")) g.prefetch = atoi(pf);
+  g.prefetch = ctx->opt_prefetch;
+  g.wait_shift = ctx->opt_wait_shift;
+  g.fault_stage = ctx->opt_fault_stage;
   MmaLaunch &d = *dn;
   d = g;
   d.tmap_a = fp4 ? (wide ? L.dn_mma.tmap_pw : L.dn_mma.tmap_p) : L.dn_mma.tmap;
@@ -607,13 +614,33 @@ spt_status check_device_error(spt_context *ctx) {
   return SPT_OK;
 }
 
-// Expert GEMM path of this call: tensor cores when the arena has their
-// layout and the context allows it, else the exact CUDA-core GEMV.
-spt_status pick_path(spt_context *ctx, const LayerDev &L, bool *use_mma) {
-  *use_mma = L.has_mma && ctx->path != SPT_PATH_EXACT;
+// Expert products of this call.  Arenas with the tensor-core planes run
+// them there: the decode GEMV (k_gemv16) for batches of at most
+// opt_gemv16_slots slots (batch x top-k), the tcgen05 GEMM above that
+// (SPT_PATH_MMA and SPT_PATH_GEMV16 force one of the two); arenas with only
+// the G8 planes, or SPT_PATH_EXACT, run the bit-exact CUDA-core GEMV.
+enum ExpertPath { kPathExact = 0, kPathTcgen05 = 1, kPathGemv16 = 2 };
+
+bool gemv16_fits(const LayerDev &L) {
+  return L.has_mma && L.gemv16_ok && L.gu_mma.kp / kMmaKT <= kGemv16MaxKtiles &&
+         L.dn_mma.kp / kMmaKT <= kGemv16MaxKtiles;
+}
+
+spt_status pick_path(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, int64_t T, ExpertPath *path) {
+  *path = kPathExact;
   if (ctx->path == SPT_PATH_MMA && !L.has_mma)
     return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_MMA");
-  if (!*use_mma && !L.has_g8)
+  if (ctx->path == SPT_PATH_GEMV16 && !gemv16_fits(L))
+    return fail(ctx, SPT_ERR_UNSUPPORTED,
+                "decode GEMV needs SPT_ARENA_MMA planes with every scale byte in [%d, %d] and K <= %d",
+                kF16ScaleLo, kF16ScaleHi, kGemv16MaxKtiles * kMmaKT);
+  if (ctx->path != SPT_PATH_EXACT && L.has_mma) {
+    if (ctx->path == SPT_PATH_GEMV16) *path = kPathGemv16;
+    else if (ctx->path == SPT_PATH_MMA) *path = kPathTcgen05;
+    else *path = gemv16_fits(L) && T * c.num_experts_used <= (int64_t)ctx->opt_gemv16_slots ? kPathGemv16
+                                                                                                 : kPathTcgen05;
+  }
+  if (*path == kPathExact && !L.has_g8)
     return fail(ctx, SPT_ERR_UNSUPPORTED, "arena was created without SPT_ARENA_GEMV");
   return SPT_OK;
 }
@@ -626,15 +653,23 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
                            int bn_hint = 0) {
   spt_status st = ensure_scratch(ctx, T, c);
   if (st) return st;
-  bool use_mma = false;
-  if ((st = pick_path(ctx, L, &use_mma))) return st;
-  if (!use_mma) return SPT_OK;
+  ExpertPath path;
+  if ((st = pick_path(ctx, L, c, T, &path))) return st;
+  if (path == kPathExact) return SPT_OK;
   const int64_t E = c.num_experts, K = c.num_experts_used, S = T * K;
+  if (path == kPathGemv16) {
+    const int64_t kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
+    SPT_CUDA(ctx, ctx->xq.ensure(sizeof(__half) * 2 * kph * std::max<int64_t>(T, 1)));
+    SPT_CUDA(ctx, ctx->xe.ensure(sizeof(int32_t) * std::max<int64_t>(T, 1)));
+    SPT_CUDA(ctx, ctx->act_off.ensure(sizeof(int32_t) * (E + 1)));
+    SPT_CUDA(ctx, ctx->actq.ensure(sizeof(__half) * 2 * kpd * std::max<int64_t>(S, 1)));
+    return SPT_OK;
+  }
   SPT_CUDA(ctx, ctx->pad_off.ensure(sizeof(int32_t) * E));
   SPT_CUDA(ctx, ctx->tile_gu.ensure(sizeof(int32_t) * (E + 1)));
   SPT_CUDA(ctx, ctx->tile_dn.ensure(sizeof(int32_t) * (E + 1)));
   SPT_CUDA(ctx, ctx->pos_expert.ensure(sizeof(int32_t) * std::max<int64_t>(S, 1)));
-  const int bn = bn_hint ? bn_hint : pick_bn(T, K, E);
+  const int bn = bn_hint ? bn_hint : pick_bn(ctx, T, K, E);
   const int64_t na_max = std::min<int64_t>(E, S);
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
@@ -660,18 +695,20 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // selection runs inside the dispatch kernel and writes sel_idx / sel_w there.
 spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
                            int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0,
-                           const float *logits = nullptr) {
+                           const float *logits = nullptr, bool x_split_done = false) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
   spt_status st = SPT_OK;
   const int max_active = (int)std::min<int64_t>(E, T * K);
-  bool use_mma = false;
-  if ((st = pick_path(ctx, L, &use_mma))) return st;
+  ExpertPath path;
+  if ((st = pick_path(ctx, L, c, T, &path))) return st;
   if ((st = reserve_experts(ctx, L, c, T, bn_hint))) return st;
+  const bool use_mma = path == kPathTcgen05;
   DispatchPlan plan;  // tensor-core tile layout, made by the dispatch kernel
+  if (path == kPathGemv16) plan.act_off = ctx->act_off.as<int32_t>();
   if (use_mma) {
-    plan.bn = bn_hint ? bn_hint : pick_bn(T, K, E);
+    plan.bn = bn_hint ? bn_hint : pick_bn(ctx, T, K, E);
     plan.mt_gu = L.gu_mma.mtiles;
     plan.mt_dn = L.dn_mma.mtiles;
     plan.pad_off = ctx->pad_off.as<int32_t>();
@@ -684,15 +721,67 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
                                          const_cast<float *>(sel_w), ctx->offsets.as<int32_t>(),
                                          ctx->perm.as<int32_t>(), ctx->slot_pos.as<int32_t>(),
                                          ctx->act_list.as<int32_t>(), ctx->meta.as<int32_t>(), s,
-                                         use_mma ? &plan : nullptr));
+                                         path != kPathExact ? &plan : nullptr));
   } else {
     SPT_CUDA(ctx, launch_dispatch(sel_idx, sel_w, (int)(T * K), E,
                                   ctx->offsets.as<int32_t>(), ctx->perm.as<int32_t>(),
                                   ctx->slot_pos.as<int32_t>(), ctx->act_list.as<int32_t>(),
-                                  ctx->meta.as<int32_t>(), s, use_mma ? &plan : nullptr));
+                                  ctx->meta.as<int32_t>(), s, path != kPathExact ? &plan : nullptr));
   }
   SPT_MARK(3);
-  if (use_mma) {
+  if (path == kPathGemv16) {
+    const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
+    __half *xq = ctx->xq.as<__half>(), *actq = ctx->actq.as<__half>();
+    // the tokens' split operand, unless the router made it already
+    if (!x_split_done)
+      SPT_CUDA(ctx, launch_split_rows(x, H, (int)T, H, kph, nullptr, 1, nullptr, xq, ctx->xe.as<int32_t>(), s));
+    Gemv16Launch g;
+    g.w = L.gu_mma.w;
+    g.sf = L.gu_mma.sf;
+    g.rows = L.gu_mma.rows;
+    g.out_rows = D;
+    g.mtiles = L.gu_mma.mtiles;
+    g.ktiles = kph / kMmaKT;
+    g.kp = kph;
+    g.xq = xq;
+    g.xq_stride = 2 * (int64_t)kph;
+    g.xe = ctx->xe.as<int32_t>();
+    g.perm = ctx->perm.as<int32_t>();
+    g.top_k = K;
+    g.act_list = ctx->act_list.as<int32_t>();
+    g.act_off = ctx->act_off.as<int32_t>();
+    g.meta = ctx->meta.as<int32_t>();
+    g.bias0 = L.gate_bias;
+    g.bias1 = L.up_bias;
+    g.actq = actq;
+    g.actq_stride = 2 * (int64_t)kpd;
+    g.actq_kp = kpd;
+    SPT_MARK(4);
+    SPT_CUDA(ctx, launch_gemv16(g, 0, max_active, s));
+    SPT_MARK(5);
+    Gemv16Launch d = g;
+    d.w = L.dn_mma.w;
+    d.sf = L.dn_mma.sf;
+    d.rows = L.dn_mma.rows;
+    d.out_rows = H;
+    d.mtiles = L.dn_mma.mtiles;
+    d.ktiles = kpd / kMmaKT;
+    d.kp = kpd;
+    d.xq = actq;
+    d.xq_stride = 2 * (int64_t)kpd;
+    d.xe = nullptr;
+    d.perm = nullptr;
+    d.top_k = 1;
+    d.bias0 = L.down_bias;
+    d.bias1 = nullptr;
+    d.actq = nullptr;
+    d.y = ctx->res.as<float>();
+    d.y_stride = H;
+    SPT_MARK(6);
+    SPT_CUDA(ctx, launch_gemv16(d, 1, max_active, s));
+    // router, select, dispatch, [split x], gate/up, down, combine
+    ctx->kernels_last = x_split_done ? 6 : 7;
+  } else if (use_mma) {
     if ((st = forward_mma(ctx, L, c, x, T, s, plan.bn))) return st;
   } else {
     const int mt = pick_mt(T, K, E);
@@ -743,12 +832,13 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // Router logits and top-k selections of T tokens (all experts of the layer).
 // select = false leaves the selection to the fused dispatch kernel.
 spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                        int64_t T, int32_t *sel_idx, float *sel_w, bool select = true) {
+                        int64_t T, int32_t *sel_idx, float *sel_w, bool select = true,
+                        const RouterSplit *split = nullptr, bool *split_done = nullptr) {
   const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
-  ctx->decode_traced = false;  // this forward's stage times come from its events
   SPT_MARK(0);
-  SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s));
+  SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s, split,
+                              split_done));
   SPT_MARK(1);
   if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
@@ -759,77 +849,6 @@ spt_status check_layer_limits(spt_context *ctx, const spt_moe_config &c) {
   if (c.num_experts > kDispatchMaxExperts || c.num_experts_used > kSelectMaxK)
     return fail(ctx, SPT_ERR_UNSUPPORTED, "experts %lld > %d or top-k %lld > %d unsupported",
                 (long long)c.num_experts, kDispatchMaxExperts, (long long)c.num_experts_used, kSelectMaxK);
-  return SPT_OK;
-}
-
-// Single-launch decode block (k_moe_decode) for this call?  Opt-in with
-// SPT_DECODE_KERNEL=1: measured on B200 it is slower than the separate
-// PDL-chained kernels at every decode size (GPT-OSS layer, 256 MB L2 flush
-// between steps: T=1 66.9 vs 59.9 us, T=4 99.9 vs 93.7, T=8 138.6 vs
-// 125.7).  Then: tensor-core path with 8-token tiles, at most kDecodeMaxSlots
-// slots, the router's 32-lane order (H % 32 == 0), rows that fit its staging
-// and a co-resident grid.  With stage timing on, the kernel stamps its
-// phases instead of the per-kernel events.
-bool decode_eligible(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x, int64_t T) {
-  const int64_t H = c.hidden_dim, D = c.expert_hidden_dim, E = c.num_experts, K = c.num_experts_used;
-  if (!L.has_mma || ctx->path == SPT_PATH_EXACT || !L.router) return false;
-  const char *opt = getenv("SPT_DECODE_KERNEL");  // read per call: both paths stay testable
-  if (!opt || opt[0] != '1') return false;
-  if (T < 1 || T * K > kDecodeMaxSlots || E > kDispatchMaxExperts || H % 32 != 0 || D % 4 != 0) return false;
-  if (pick_bn(T, K, E) != kDecodeBn || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(L.router)) & 15) != 0)
-    return false;
-  if ((size_t)(1 + T) * H * 4 > decode_ring_bytes() || (size_t)(T * E) * 4 > decode_ring_bytes()) return false;
-  if (ctx->decode_grid < 0) ctx->decode_grid = decode_max_grid(ctx->sm_count);
-  return ctx->decode_grid > 0;
-}
-
-spt_status forward_decode(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
-                          float *out, int64_t T) {
-  spt_status st = reserve_experts(ctx, L, c, T, kDecodeBn);
-  if (st) return st;
-  if (!ctx->gbar.p) {
-    SPT_CUDA(ctx, ctx->gbar.ensure(2 * sizeof(uint32_t)));
-    SPT_CUDA(ctx, cudaMemsetAsync(ctx->gbar.p, 0, 2 * sizeof(uint32_t), ctx->stream));
-  }
-  SPT_CUDA(ctx, ctx->partial.ensure(decode_partial_bytes(ctx->decode_grid)));
-  DecodeLaunch d;
-  if ((st = build_gemms(ctx, L, c, T, kDecodeBn, &d.gu, &d.dn, &d.rb, kMmaStageTilesFp4))) return st;
-  d.partial = ctx->partial.as<float>();
-  d.x = x;
-  d.router_w = L.router;
-  d.router_b = L.router_bias;
-  d.T = (int)T;
-  d.H = (int)c.hidden_dim;
-  d.D = (int)c.expert_hidden_dim;
-  d.E = (int)c.num_experts;
-  d.K = (int)c.num_experts_used;
-  d.logits = ctx->logits.as<float>();
-  d.sel_idx = ctx->sel_idx.as<int32_t>();
-  d.sel_w = ctx->sel_w.as<float>();
-  d.offsets = ctx->offsets.as<int32_t>();
-  d.perm = ctx->perm.as<int32_t>();
-  d.slot_pos = ctx->slot_pos.as<int32_t>();
-  d.act_list = ctx->act_list.as<int32_t>();
-  d.meta = ctx->meta.as<int32_t>();
-  d.qx = ctx->qx.as<uint8_t>();
-  d.sfx = ctx->sfx.as<uint8_t>();
-  d.qa = ctx->qa.as<uint8_t>();
-  d.sfa = ctx->sfa.as<uint8_t>();
-  d.out = out;
-  d.gbar = ctx->gbar.as<uint32_t>();
-  d.err = ctx->dev_err.as<int32_t>();
-  cudaStream_t s = ctx->stream;
-  if (ctx->timing) {
-    const size_t tb = sizeof(uint64_t) * kDecodeTraceSlots * ctx->decode_grid;
-    SPT_CUDA(ctx, ctx->trace.ensure(tb));
-    SPT_CUDA(ctx, cudaMemsetAsync(ctx->trace.p, 0, tb, s));
-    d.trace = ctx->trace.as<uint64_t>();
-  }
-  SPT_MARK(0);
-  SPT_CUDA(ctx, launch_moe_decode(d, ctx->decode_grid, s));
-  SPT_MARK(SPT_NUM_STAGES);
-  ctx->decode_traced = ctx->timing;
-  ctx->kernels_last = 1;
   return SPT_OK;
 }
 
@@ -845,18 +864,23 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
                 (long long)c.num_experts);
   if ((st = ensure_scratch(ctx, T, c))) return st;
   const LayerDev &L = arena->layers[(size_t)layer];
-  if (decode_eligible(ctx, L, c, x, T)) {
-    if ((st = forward_decode(ctx, L, c, x, out, T))) return st;
-    ctx->last_T = T;
-    ctx->last_E = c.num_experts;
-    ctx->last_K = c.num_experts_used;
-    ctx->have_routing = true;
-    return SPT_OK;
+  const bool fuse = T <= kSelectDispatchMaxTokens && ctx->opt_fused_select;
+  // the decode GEMV's split operand comes out of the router when it can
+  ExpertPath path;
+  if ((st = pick_path(ctx, L, c, T, &path))) return st;
+  if ((st = reserve_experts(ctx, L, c, T))) return st;
+  RouterSplit rs;
+  if (path == kPathGemv16) {
+    rs.xq = ctx->xq.as<__half>();
+    rs.xe = ctx->xe.as<int32_t>();
+    rs.kp = L.gu_mma.kp;
   }
-  const bool fuse = T <= kSelectDispatchMaxTokens && fused_select_enabled();
-  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse))) return st;
+  bool split_done = false;
+  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse,
+                         path == kPathGemv16 ? &rs : nullptr, &split_done)))
+    return st;
   if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out, 0,
-                            fuse ? ctx->logits.as<float>() : nullptr)))
+                            fuse ? ctx->logits.as<float>() : nullptr, split_done)))
     return st;
   ctx->last_T = T;
   ctx->last_E = c.num_experts;
@@ -917,6 +941,22 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
   return SPT_OK;
 }
 
+// Options from the environment, read once per context (spt_context_set_option
+// changes them afterwards).
+void seed_options(spt_context *ctx) {
+  auto env = [](const char *name, int *dst, int lo, int hi) {
+    const char *v = getenv(name);
+    if (!v || !*v) return;
+    const long x = strtol(v, nullptr, 10);
+    if (x >= lo && x <= hi) *dst = (int)x;
+  };
+  env("SPT_MMA_BN", &ctx->opt_tile_tokens, 0, 128);
+  if (ctx->opt_tile_tokens != 8 && ctx->opt_tile_tokens != 16 && ctx->opt_tile_tokens != 128) ctx->opt_tile_tokens = 0;
+  env("SPT_FUSED_SELECT", &ctx->opt_fused_select, 0, 1);
+  env("SPT_MMA_PREFETCH", &ctx->opt_prefetch, 0, 64);
+  env("SPT_GEMV16_SLOTS", &ctx->opt_gemv16_slots, 0, 1 << 20);
+}
+
 // Temporary device buffer for stage entry points.
 struct Tmp {
   void *p = nullptr;
@@ -975,6 +1015,7 @@ spt_status spt_context_create(int device, spt_context **out) {
       return st;
     }
     cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    seed_options(ctx);
     ctx->device = device;
     ctx->has_device = true;
     ctx->stream = ctx->own_stream;
@@ -992,7 +1033,7 @@ void spt_context_destroy(spt_context *ctx) {
                       &ctx->slot_pos, &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res,
                       &ctx->xdev, &ctx->outdev, &ctx->dev_err, &ctx->pad_off, &ctx->tile_gu,
                       &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa,
-                      &ctx->stack_norm, &ctx->stack_ffn, &ctx->gbar, &ctx->trace, &ctx->partial})
+                      &ctx->stack_norm, &ctx->stack_ffn, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off})
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
@@ -1012,35 +1053,9 @@ spt_status spt_set_stage_timing(spt_context *ctx, int enable) {
   return SPT_OK;
 }
 
-// Stage times of a traced decode launch from its per-CTA stamps: each stage
-// is the growth of the latest CTA's stamp from one phase end to the next
-// (barrier waits included), so the stages add up to the launch.
-int decode_stage_times(spt_context *ctx, float *ms, int n) {
-  const int grid = ctx->decode_grid;
-  std::vector<uint64_t> tr((size_t)grid * kDecodeTraceSlots);
-  if (cudaMemcpy(tr.data(), ctx->trace.p, tr.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
-    return 0;
-  uint64_t t[kDecodeTracePoints];
-  for (int k = 0; k < kDecodeTracePoints; ++k) {
-    t[k] = k == 0 ? UINT64_MAX : 0;
-    for (int b = 0; b < grid; ++b) {
-      const uint64_t v = tr[(size_t)b * kDecodeTraceSlots + k];
-      t[k] = k == 0 ? std::min(t[k], v) : std::max(t[k], v);
-    }
-  }
-  // router, select, dispatch, quantize x, gate/up, quantize act, down, combine
-  const double st[SPT_NUM_STAGES] = {double(t[1] - t[0]), 0.0, double(t[3] - t[1]), double(t[5] - t[3]),
-                                     double(t[7] - t[5]), double(t[9] - t[7]), double(t[11] - t[9]),
-                                     double(t[12] - t[11])};
-  int w = 0;
-  for (int i = 0; i < SPT_NUM_STAGES && i < n; ++i, ++w) ms[i] = (float)(st[i] * 1e-6);
-  return w;
-}
-
 int spt_stage_times(spt_context *ctx, float *ms, int n) {
   if (!ctx || !ctx->timing || !ms) return 0;
   if (cudaEventSynchronize(ctx->ev[SPT_NUM_STAGES]) != cudaSuccess) return 0;
-  if (ctx->decode_traced) return decode_stage_times(ctx, ms, n);
   int w = 0;
   for (int i = 0; i < SPT_NUM_STAGES && i < n; ++i, ++w)
     if (cudaEventElapsedTime(&ms[i], ctx->ev[i], ctx->ev[i + 1]) != cudaSuccess) ms[i] = -1.0f;
@@ -1048,16 +1063,6 @@ int spt_stage_times(spt_context *ctx, float *ms, int n) {
 }
 
 int spt_kernels_per_forward(spt_context *ctx) { return ctx ? ctx->kernels_last : 0; }
-
-int64_t spt_decode_trace(spt_context *ctx, uint64_t *stamps, int64_t cap) {
-  if (!ctx || !ctx->decode_traced || !ctx->trace.p) return 0;
-  const int64_t n = (int64_t)ctx->decode_grid * kDecodeTraceSlots;
-  if (!stamps || cap < n) return -n;
-  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return 0;
-  if (cudaMemcpy(stamps, ctx->trace.p, (size_t)n * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
-    return 0;
-  return n;
-}
 
 const char *spt_last_error(const spt_context *ctx) {
   return ctx ? ctx->err.c_str() : g_tls_error.c_str();
@@ -1080,9 +1085,55 @@ spt_status spt_context_sync(spt_context *ctx) {
 
 spt_status spt_context_set_path(spt_context *ctx, int path) {
   if (!ctx) return fail(nullptr, SPT_ERR_NULL_ARG, "nil context");
-  if (path < SPT_PATH_AUTO || path > SPT_PATH_MMA) return fail(ctx, SPT_ERR_UNSUPPORTED, "unknown path %d", path);
+  if (path < SPT_PATH_AUTO || path > SPT_PATH_GEMV16) return fail(ctx, SPT_ERR_UNSUPPORTED, "unknown path %d", path);
   ctx->path = path;
   return SPT_OK;
+}
+
+spt_status spt_context_set_option(spt_context *ctx, int option, int64_t v) {
+  if (!ctx) return fail(nullptr, SPT_ERR_NULL_ARG, "nil context");
+  switch (option) {
+    case SPT_OPT_TILE_TOKENS:
+      if (v != 0 && v != 8 && v != 16 && v != 128) break;
+      ctx->opt_tile_tokens = (int)v;
+      return SPT_OK;
+    case SPT_OPT_FUSED_SELECT:
+      if (v != 0 && v != 1) break;
+      ctx->opt_fused_select = (int)v;
+      return SPT_OK;
+    case SPT_OPT_L2_PREFETCH:
+      if (v < 0 || v > 64) break;
+      ctx->opt_prefetch = (int)v;
+      return SPT_OK;
+    case SPT_OPT_GEMV16_SLOTS:
+      if (v < 0 || v > (1 << 20)) break;
+      ctx->opt_gemv16_slots = (int)v;
+      return SPT_OK;
+    case SPT_OPT_WAIT_LIMIT:
+      if (v < 10 || v > 31) break;
+      ctx->opt_wait_shift = (int)v;
+      return SPT_OK;
+    case SPT_OPT_FAULT_STAGE:
+      if (v < -1 || v > (1 << 20)) break;
+      ctx->opt_fault_stage = (int)v;
+      return SPT_OK;
+    default:
+      return fail(ctx, SPT_ERR_UNSUPPORTED, "unknown option %d", option);
+  }
+  return fail(ctx, SPT_ERR_DIMENSIONS, "option %d: value %lld out of range", option, (long long)v);
+}
+
+int64_t spt_context_get_option(const spt_context *ctx, int option) {
+  if (!ctx) return -1;
+  switch (option) {
+    case SPT_OPT_TILE_TOKENS: return ctx->opt_tile_tokens;
+    case SPT_OPT_FUSED_SELECT: return ctx->opt_fused_select;
+    case SPT_OPT_L2_PREFETCH: return ctx->opt_prefetch;
+    case SPT_OPT_GEMV16_SLOTS: return ctx->opt_gemv16_slots;
+    case SPT_OPT_WAIT_LIMIT: return ctx->opt_wait_shift;
+    case SPT_OPT_FAULT_STAGE: return ctx->opt_fault_stage;
+  }
+  return -1;
 }
 
 spt_status spt_validate_moe_layer(spt_context *ctx, const spt_reader *reader,
@@ -1116,6 +1167,7 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
   a->flags = flags;
   a->layers.resize((size_t)n_layers);
   std::vector<float> tmp;
+  DevBuf range;  // smallest and largest E8M0 byte of a layer's expert blocks
   for (int64_t l = 0; l < n_layers && st == SPT_OK; ++l) {
     const spt_reader &r = readers[l];
     const spt_layer_weights &w = layers[l];
@@ -1147,6 +1199,11 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
       if ((st = upload_floats(ctx, a, tmp.data() + e0 * b.dim, (size_t)(ne * b.dim), b.dst))) break;
     }
     if (st) break;
+    if ((flags & SPT_ARENA_MMA) && (st = cuda_ok(ctx, range.ensure(2 * sizeof(int32_t)), "scale range")) == SPT_OK) {
+      const int32_t init[2] = {255, 0};
+      st = cuda_ok(ctx, cudaMemcpy(range.p, init, sizeof init, cudaMemcpyHostToDevice), "scale range");
+    }
+    if (st) break;
     {
       DevBuf sg, su;
       // expert e's matrix is the byte range [start + e * per_expert, + per_expert)
@@ -1160,7 +1217,11 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
         if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
           st = alloc_mma(ctx, a, ne, (int)(2 * D), (int)H, &L.gu_mma);
           if (st == SPT_OK) {
-            cudaError_t e = launch_repack_mma_gu(sg.as<uint8_t>(), su.as<uint8_t>(), ne, (int)D, (int)H, &L.gu_mma, ctx->stream);
+            cudaError_t e = launch_scale_range(sg.as<uint8_t>(), (int64_t)(gu_raw / 17), range.as<int32_t>(), ctx->stream);
+            if (e == cudaSuccess)
+              e = launch_scale_range(su.as<uint8_t>(), (int64_t)(gu_raw / 17), range.as<int32_t>(), ctx->stream);
+            if (e == cudaSuccess)
+              e = launch_repack_mma_gu(sg.as<uint8_t>(), su.as<uint8_t>(), ne, (int)D, (int)H, &L.gu_mma, ctx->stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
             if (e != cudaSuccess) st = cuda_fail(ctx, e, "repack mma gate/up");
           }
@@ -1176,7 +1237,9 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
         if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
           st = alloc_mma(ctx, a, ne, (int)H, (int)D, &L.dn_mma);
           if (st == SPT_OK) {
-            cudaError_t e = launch_repack_mma(sd.as<uint8_t>(), ne, (int)H, (int)D, &L.dn_mma, ctx->stream);
+            cudaError_t e = launch_scale_range(sd.as<uint8_t>(), (int64_t)(ne * dn_per / 17), range.as<int32_t>(),
+                                               ctx->stream);
+            if (e == cudaSuccess) e = launch_repack_mma(sd.as<uint8_t>(), ne, (int)H, (int)D, &L.dn_mma, ctx->stream);
             if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
             if (e != cudaSuccess) st = cuda_fail(ctx, e, "repack mma down");
           }
@@ -1186,8 +1249,14 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
       if (st) break;
       L.has_g8 = (flags & SPT_ARENA_GEMV) != 0;
       L.has_mma = (flags & SPT_ARENA_MMA) != 0;
+      if (L.has_mma) {
+        int32_t r[2] = {0, 255};
+        if ((st = cuda_ok(ctx, cudaMemcpy(r, range.p, sizeof r, cudaMemcpyDeviceToHost), "scale range"))) break;
+        L.gemv16_ok = r[0] >= kF16ScaleLo && r[1] <= kF16ScaleHi;
+      }
     }
   }
+  range.release();
   if (st) {
     spt_arena_destroy(a);
     return st;
@@ -1292,6 +1361,7 @@ static spt_status synth_create_impl(spt_context *ctx, const spt_moe_config *cfg,
     }
     L.has_g8 = (flags & SPT_ARENA_GEMV) != 0;
     L.has_mma = (flags & SPT_ARENA_MMA) != 0;
+    L.gemv16_ok = p->scale_lo >= kF16ScaleLo && p->scale_hi <= kF16ScaleHi;
   }
   if (st == SPT_OK) {
     cudaError_t e = cudaStreamSynchronize(ctx->stream);
@@ -2115,7 +2185,7 @@ spt_status forward_ep_cap(spt_context *ctx, spt_ep *ep, const LayerDev &L, const
   lc.num_experts = ne;
   lc.num_experts_used = 1;
   // token tiles sized for the rows a rank receives on average (its own slot count)
-  const int bn_hint = pick_bn(S, 1, ne);
+  const int bn_hint = pick_bn(ctx, S, 1, ne);
   // every buffer at its full size before anything is enqueued: none grows later
   spt_status st = ensure_scratch(ctx, ep->cap_tokens, c);
   if (st) return st;

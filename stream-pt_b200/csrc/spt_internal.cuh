@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "spt_gemv16.cuh"
 #include "spt_mma.cuh"
 
 namespace spt {
@@ -60,6 +61,7 @@ struct LayerDev {
   bool has_g8 = false;                 // CUDA-core GEMV planes present
   bool has_mma = false;                // tcgen05 planes present
   MmaMatrix gu_mma, dn_mma;            // gate/up interleaved [E][2D][KP/2]; down [E][H][KPd/2]
+  bool gemv16_ok = false;              // every scale byte in [kF16ScaleLo, kF16ScaleHi] (decode GEMV usable)
   const float *norm = nullptr;         // post-attention RMSNorm weight [H] (layer stack), or null
 };
 
@@ -83,8 +85,19 @@ struct Dims {
 
 // ---- launchers (spt_kernels.cu); all enqueue on `stream` ----------------
 
+// Optional output of the router launch: the decode GEMV's split operand of
+// the T input rows (token order, [T][2][kp] halves) and their exponents,
+// made from the rows the shared-memory router stages anyway.  *split_done
+// tells whether this launch wrote them (else the caller runs
+// launch_split_rows).
+struct RouterSplit {
+  __half *xq = nullptr;
+  int32_t *xe = nullptr;
+  int kp = 0;
+};
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
-                          float *logits, int portable_lanes, cudaStream_t stream);
+                          float *logits, int portable_lanes, cudaStream_t stream,
+                          const RouterSplit *split = nullptr, bool *split_done = nullptr);
 cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
                           float *sel_w, cudaStream_t stream);
 // Tensor-core tile layout computed by the dispatch kernel (bn = 0: none).
@@ -94,6 +107,10 @@ struct DispatchPlan {
   int32_t *tile_gu = nullptr;        // [E+1] gate/up tile prefix over active experts
   int32_t *tile_dn = nullptr;        // [E+1] down tile prefix
   int32_t *pos_expert = nullptr;     // [S] expert of each dispatch position
+  // [E+1] first dispatch position of each active expert (act_off[i] =
+  // offsets[act_list[i]]; the entry after the last active expert is the
+  // dispatched count), written whenever non-null (bn may be 0)
+  int32_t *act_off = nullptr;
 };
 cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, int E,
                             int32_t *offsets, int32_t *perm, int32_t *slot_pos,
@@ -105,8 +122,8 @@ cudaError_t launch_dispatch(const int32_t *sel_idx, const float *sel_w, int S, i
 // block; T=32 and T=64 about 1% slower (the selection then sits serially in
 // the one dispatch CTA), hence the small limit.
 constexpr int kSelectDispatchMaxTokens = 8;
-// SPT_FUSED_SELECT=0 keeps the separate selection launch (same results).
-bool fused_select_enabled();
+// The context option SPT_OPT_FUSED_SELECT = 0 keeps the separate selection
+// launch (same results).
 cudaError_t launch_select_dispatch(const float *logits, int T, int E, int K, int32_t *sel_idx, float *sel_w,
                                    int32_t *offsets, int32_t *perm, int32_t *slot_pos, int32_t *act_list,
                                    int32_t *meta, cudaStream_t stream, const DispatchPlan *plan = nullptr);

@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
                                                      const float *__restrict__ x,
                                                      const float *__restrict__ bias, int T, int H,
                                                      int E, int EG, int TG,
-                                                     float *__restrict__ logits) {
+                                                     float *__restrict__ logits, __half *__restrict__ xq,
+                                                     int32_t *__restrict__ xe, int KP) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 router_smem[];
@@ -219,6 +220,35 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (xq) {
+    // The decode GEMV's split operand of these tokens (spt_gemv16.cuh), made
+    // here from the staged rows: CTA bx writes K tiles bx, bx + gridDim.x, ...
+    __shared__ float s_red[8];
+    for (int j = 0; j < nt; ++j) {
+      const float *xr = xs + (size_t)j * H;
+      float m = 0.0f;
+      for (int k = threadIdx.x; k < H; k += blockDim.x) m = fmaxf(m, fabsf(xr[k]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+      if (lane == 0) s_red[warp] = m;
+      __syncthreads();
+      m = s_red[0];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_red[w]);
+      __syncthreads();
+      const int ex = split_exponent(m);
+      const float f = __int_as_float((127 - ex) << 23);
+      if (blockIdx.x == 0 && threadIdx.x == 0) xe[t0 + j] = ex;
+      __half *hi = xq + (size_t)(t0 + j) * 2 * KP, *lo = hi + KP;
+      for (int kt = blockIdx.x; kt * kMmaKT < KP; kt += gridDim.x)
+        for (int i = threadIdx.x; i < kMmaKT; i += blockDim.x) {
+          const int k = kt * kMmaKT + i;
+          __half h, l;
+          split_f16(k < H ? __fmul_rn(xr[k], f) : 0.0f, &h, &l);
+          hi[k] = h;
+          lo[k] = l;
+        }
+    }
+  }
   const int groups = (ne + 3) / 4;
   for (int item = warp; item < nt * groups; item += blockDim.x >> 5) {
     const int j = item / groups, mb = (item - j * groups) * 4;
@@ -380,6 +410,7 @@ __global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_
       if (v[1]) {
         const int ai = inc[1] - 1;
         act_list[ai] = e;
+        if (plan.act_off) plan.act_off[ai] = off;
         if (plan.bn > 0) {
           plan.pad_off[e] = inc[2] - v[2];
           plan.tile_gu[ai] = inc[3] - v[3];
@@ -392,6 +423,7 @@ __global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_
       offsets[E] = inc[0];
       meta[0] = inc[1];
       meta[1] = inc[0];
+      if (plan.act_off) plan.act_off[inc[1]] = inc[0];
       if (plan.bn > 0) {
         plan.tile_gu[inc[1]] = inc[3];
         plan.tile_dn[inc[1]] = inc[4];
@@ -808,13 +840,10 @@ cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
   return e;
 }
 
-bool fused_select_enabled() {
-  const char *v = getenv("SPT_FUSED_SELECT");  // read per call: both paths stay testable
-  return !(v && v[0] == '0');
-}
-
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
-                          float *logits, int portable_lanes, cudaStream_t stream) {
+                          float *logits, int portable_lanes, cudaStream_t stream, const RouterSplit *split,
+                          bool *split_done) {
+  if (split_done) *split_done = false;
   if (T <= 0) return cudaSuccess;
   if (H % 32 != 0) {
     return launch_pdl(k_router_portable, dim3(E, T), dim3(32), 0, stream, W, x, bias, T, H, E, portable_lanes,
@@ -835,8 +864,11 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
   if (T <= 64 && aligned && bytes(EG, TG) <= kRouterSmemMax) {
     cudaError_t e = opt_in_smem(k_router_smem, kRouterSmemMax);
     if (e != cudaSuccess) return e;
+    const bool do_split = split && split->xq && (E + EG - 1) / EG > 0;
+    if (split_done) *split_done = do_split;
     return launch_pdl(k_router_smem, dim3((E + EG - 1) / EG, (T + TG - 1) / TG), dim3(256), (size_t)bytes(EG, TG),
-                      stream, W, x, bias, T, H, E, EG, TG, logits);
+                      stream, W, x, bias, T, H, E, EG, TG, logits, do_split ? split->xq : (__half *)nullptr,
+                      do_split ? split->xe : (int32_t *)nullptr, do_split ? split->kp : 0);
   } else {
     return launch_pdl(k_router<8, 4, 1>, dim3((E + 3) / 4, (T + 7) / 8), dim3(32), 0, stream, W, x, bias, T, H, E,
                       logits);

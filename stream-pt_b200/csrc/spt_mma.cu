@@ -14,9 +14,9 @@
 //           the term sums, bias, fused SwiGLU (gate/up rows are interleaved,
 //           so a row pair sits in neighbouring lanes) or the down projection,
 //           fp32 stores.
-// Every mbarrier wait is bounded; on timeout the CTA records an error code
-// in `err`, drains its tensor-core work and exits.  The same roles run the
-// two GEMMs of the single-launch decode kernel (k_moe_decode, below).
+// Every mbarrier wait is bounded (~2^wait_shift clocks); on timeout the CTA
+// records an error code in `err`, waits for its own copies and tensor-core
+// work in flight, frees its tensor memory and exits.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -471,28 +471,6 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float v[8]) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Columns [taddr, taddr + 48) of this warp's 32 TMEM lanes in one round
-// trip (one wait for both loads).
-__device__ __forceinline__ void tc_ld48(uint32_t taddr, float v[48]) {
-  uint32_t r[48];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%48];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, "
-      "%45, %46, %47}, [%49];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
-      : "r"(taddr), "r"(taddr + 32u)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 48; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float v[32]) {
   uint32_t r[32];
   asm volatile(
@@ -607,20 +585,10 @@ struct MmaShape {
   static_assert(kAccCols + kSfCols <= 512, "TMEM columns");
 };
 
-// K tiles [lo, hi) of part `part` of `parts` of a tile with kt_n K tiles:
-// the tile's pipeline stages (ks K tiles each) split evenly, so every part
-// starts on a stage boundary.
-__device__ __forceinline__ void part_ktiles(int kt_n, int ks, int part, int parts, int *lo, int *hi) {
-  const int n_st = (kt_n + ks - 1) / ks;
-  *lo = (part * n_st / parts) * ks;
-  *hi = min(((part + 1) * n_st / parts) * ks, kt_n);
-}
-
 // One GEMM CTA: the shared-memory stage ring, its mbarriers, the TMEM
 // accumulators, and the three roles.  Each role runs in its own thread(s)
 // and keeps its ring slot, parity and tile count in that thread's copy of
-// this struct, so one CTA can run several GEMMs back to back (the decode
-// kernel runs gate/up, then down) with the barrier phases carried over.
+// this struct.
 template <int BN, bool FP4, int KS>
 struct GemmCta {
   using S = MmaShape<BN, FP4, KS>;
@@ -673,9 +641,12 @@ struct GemmCta {
   // (expert, row tile) a single contiguous run, so one bulk L2 prefetch per
   // tile, issued a.prefetch tiles ahead, can have the next tiles' weights on
   // their way from HBM while the ring streams the current one.
-  // parts > 1 (decode kernel): work units are (tile, K part), unit u =
-  // tile * parts + part, each streaming its part's K tiles.
-  __device__ bool produce(const MmaLaunch &a, const TileTables &tt, int n_active, int n_tiles, int parts = 1) {
+  // On an error (a wait that ran out, here or in another role) the producer
+  // stops issuing and waits for the copies it already started, so that none
+  // lands in shared memory after the CTA has gone.  a.fault_stage >= 0 (a
+  // test of that path) makes CTA 0 skip the whole of that stage: the MMA
+  // issuer's wait for it runs out.
+  __device__ bool produce(const MmaLaunch &a, const TileTables &tt, int n_active, int n_tiles) {
     const int kt_n = a.ktiles;
     const uint32_t w_tile_bytes = (uint32_t)kt_n * kMmaM * (kMmaKT / 2);
     auto prefetch_tile = [&](int tile) {
@@ -685,66 +656,70 @@ struct GemmCta {
       bulk_prefetch_l2(a.w + run * w_tile_bytes, w_tile_bytes);
       bulk_prefetch_l2(a.sfa + run * kt_n * 512, (uint32_t)kt_n * 512);
     };
+    uint32_t issued = 0;  // bit i: ring slot i holds a stage whose copies may still be in flight
+    uint32_t slot_phase = 0;  // bit i: the parity of that stage
+    int stage = 0;
+    bool ok = true;
     for (int d = 1; d < a.prefetch; ++d) prefetch_tile(blockIdx.x + d * gridDim.x);
-    for (int u = blockIdx.x; u < n_tiles * parts; u += gridDim.x) {
-      const int tile = u / parts;
-      int kt_lo, kt_hi;
-      part_ktiles(kt_n, KS, u - tile * parts, parts, &kt_lo, &kt_hi);
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
       const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
       const uint8_t *sfa = a.sfa + (((size_t)t.e * a.mtiles + t.mt) * a.ktiles) * 512;
       const uint8_t *sfb = a.sfb + ((size_t)(t.rowb / kMmaM) * a.ktiles) * (S::kSfb * 512);
       const int box0 = (t.e * a.mtiles + t.mt) * kt_n;
-      if (a.prefetch > 0 && parts == 1) prefetch_tile(tile + a.prefetch * gridDim.x);
-      for (int kt = kt_lo; kt < kt_hi; kt += KS) {
-        if (!mbar_wait(&empty[s], phase ^ 1u, a.err, 1)) return false;
-        const int nk = min(KS, kt_hi - kt);
-        uint8_t *st = smem + s * S::kStage;
-        mbar_expect_tx(&full[s], nk * S::kTxTile);
-        // one operation per operand for the whole stage; single K tiles with
-        // the one-box maps at the end of an odd K
-        const bool whole = nk == KS;
-        const CUtensorMap *ma = whole ? &a.tmap_a : &a.tmap_a1;
-        const CUtensorMap *mb = whole ? &a.tmap_b : &a.tmap_b1;
-        for (int j = 0; j < (whole ? 1 : nk); ++j) {
-          uint8_t *aj = st + j * S::kA;
-          uint8_t *bj = st + S::kOffB + j * S::kBt;
-          if (FP4) {
-            tma_load_3d(ma, aj, &full[s], 0, 0, box0 + kt + j);
-            tma_load_3d(mb, bj, &full[s], 0, t.rowb, kt + j);
-          } else {
-            tma_load_2d(ma, aj, &full[s], 0, (box0 + kt + j) * kMmaM);
-            tma_load_4d(mb, bj, &full[s], 0, t.rowb, 0, kt + j);
-          }
+      if (a.prefetch > 0) prefetch_tile(tile + a.prefetch * gridDim.x);
+      for (int kt = 0; kt < kt_n; kt += KS, ++stage) {
+        if (!mbar_wait(&empty[s], phase ^ 1u, a.err, 1, a.wait_shift)) {
+          ok = false;
+          break;
         }
-        bulk_load(st + S::kOffSfa, sfa + (size_t)kt * 512, nk * 512, &full[s]);
-        bulk_load(st + S::kOffSfb, sfb + (size_t)kt * S::kSfb * 512, nk * S::kSfb * 512, &full[s]);
+        const int nk = min(KS, kt_n - kt);
+        if (!(a.fault_stage == stage && blockIdx.x == 0)) {
+          uint8_t *st = smem + s * S::kStage;
+          mbar_expect_tx(&full[s], nk * S::kTxTile);
+          // one operation per operand for the whole stage; single K tiles with
+          // the one-box maps at the end of an odd K
+          const bool whole = nk == KS;
+          const CUtensorMap *ma = whole ? &a.tmap_a : &a.tmap_a1;
+          const CUtensorMap *mb = whole ? &a.tmap_b : &a.tmap_b1;
+          for (int j = 0; j < (whole ? 1 : nk); ++j) {
+            uint8_t *aj = st + j * S::kA;
+            uint8_t *bj = st + S::kOffB + j * S::kBt;
+            if (FP4) {
+              tma_load_3d(ma, aj, &full[s], 0, 0, box0 + kt + j);
+              tma_load_3d(mb, bj, &full[s], 0, t.rowb, kt + j);
+            } else {
+              tma_load_2d(ma, aj, &full[s], 0, (box0 + kt + j) * kMmaM);
+              tma_load_4d(mb, bj, &full[s], 0, t.rowb, 0, kt + j);
+            }
+          }
+          bulk_load(st + S::kOffSfa, sfa + (size_t)kt * 512, nk * 512, &full[s]);
+          bulk_load(st + S::kOffSfb, sfb + (size_t)kt * S::kSfb * 512, nk * S::kSfb * 512, &full[s]);
+          issued |= 1u << s;
+          slot_phase = (slot_phase & ~(1u << s)) | (phase << s);
+        } else {
+          issued &= ~(1u << s);  // nothing of this stage is in flight
+        }
         if (++s == S::kStages) {
           s = 0;
           phase ^= 1u;
         }
       }
     }
-    return true;
-  }
-
-  // L2 prefetch of every weight tile (and its scale atoms) this CTA will
-  // stream in a GEMM, issued as soon as the tile tables exist (one thread).
-  __device__ void prefetch_all(const MmaLaunch &a, const TileTables &tt, int n_active, int n_tiles) const {
-    const int kt_n = a.ktiles;
-    const uint32_t w_tile_bytes = (uint32_t)kt_n * kMmaM * (kMmaKT / 2);
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-      const TileInfo ti = tile_info<BN>(tt, tile, n_active, a.mtiles);
-      const size_t run = (size_t)ti.e * a.mtiles + ti.mt;
-      bulk_prefetch_l2(a.w + run * w_tile_bytes, w_tile_bytes);
-      bulk_prefetch_l2(a.sfa + run * kt_n * 512, (uint32_t)kt_n * 512);
+    if (!ok) {
+      // the last stage issued into each slot is the only one that can still
+      // be in flight there (an earlier one was consumed before the slot was
+      // reused); its full barrier completes when its bytes have landed
+      for (int i = 0; i < S::kStages; ++i)
+        if ((issued >> i) & 1u) mbar_wait_own(&full[i], (slot_phase >> i) & 1u, a.wait_shift);
     }
+    return ok;
   }
 
   // ---------------- MMA issuer (one thread) ----------------
   // Descriptors are built once; per stage and K-step only their 14-bit start
   // address fields advance (stage bases are 1024-byte aligned and the whole
   // ring lies below 256 KB, so the adds never carry out of the field).
-  __device__ bool mma(const MmaLaunch &a, int n_tiles, int parts = 1) {
+  __device__ bool mma(const MmaLaunch &a, int n_tiles) {
     const uint32_t sfa_t = tmem + S::kAccCols;  // scale-factor columns after the two accumulators
     const uint32_t base = smem_u32(smem);
     const uint64_t a_desc0 = smem_desc(base, S::kSbo, S::kLayout);
@@ -758,18 +733,16 @@ struct GemmCta {
 #pragma unroll
     for (int ks = 0; ks < S::kKSteps; ++ks)
       idesc[ks] = FP4 ? idesc_mxf4(S::kN, 2 * ks, 2 * ks) : idesc_mxf8f6f4(S::kN, ks, ks);
-    for (int u = blockIdx.x; u < n_tiles * parts; u += gridDim.x, ++local) {
-      const int tile = u / parts;
-      int kt_lo, kt_hi;
-      part_ktiles(a.ktiles, KS, u - tile * parts, parts, &kt_lo, &kt_hi);
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      const int kt_lo = 0, kt_hi = a.ktiles;
       const int buf = local & 1;
       const uint32_t accph = (uint32_t)(local >> 1) & 1u;
-      if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2)) return false;
+      if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2, a.wait_shift)) return false;
       tc_fence_after();
       const uint32_t d_tmem = tmem + buf * S::kAccStride;
       uint32_t acc = 0u;
       for (int kt = kt_lo; kt < kt_hi; kt += KS) {
-        if (!mbar_wait(&full[s], phase, a.err, 3)) return false;
+        if (!mbar_wait(&full[s], phase, a.err, 3, a.wait_shift)) return false;
         tc_fence_after();
         const int nk = min(KS, kt_hi - kt);
         const uint64_t so = (uint64_t)s * kStage16;
@@ -819,40 +792,36 @@ struct GemmCta {
     return true;
   }
 
-  // Wait until every tensor-core operation this thread issued has finished.
-  __device__ void drain_mma(int32_t *err) {
+  // Wait until every tensor-core operation this thread issued has finished
+  // (also after an error: the accumulators' TMEM is freed after this).
+  __device__ void drain_mma(int32_t *err, int shift) {
     tc_commit(drain);
-    mbar_wait(drain, 0, err, 4);
+    if (!mbar_wait_own(drain, 0, shift)) atomicCAS(err, 0, 4);
   }
 
   // ---------------- epilogue (warps 2-5) ----------------
   // tcgen05.ld of the accumulator (lane = output row), bias, fused SwiGLU
   // (gate/up rows are interleaved, so a row pair sits in neighbouring lanes)
   // or the down projection, fp32 stores.
-  // With `partial` (parts > 1) each unit's sums, all BN columns, go to
-  // partial[tile][128][BN][parts] as they are; the reader adds the parts in
-  // part order and applies the bias (and SwiGLU).
   __device__ bool epilogue(const MmaLaunch &a, const TileTables &tt, int n_active, int n_tiles, int warp,
-                           int lane, int parts = 1, float *partial = nullptr) {
+                           int lane) {
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_local = quad * 32 + lane;
-    for (int u = blockIdx.x; u < n_tiles * parts; u += gridDim.x, ++local) {
-      const int tile = u / parts;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
       const int buf = local & 1;
       const uint32_t accph = (uint32_t)(local >> 1) & 1u;
-      if (!mbar_wait(&accf[buf], accph, a.err, 5)) return false;
+      if (!mbar_wait(&accf[buf], accph, a.err, 5, a.wait_shift)) return false;
       tc_fence_after();
       const int r = t.mt * kMmaM + row_local;
       constexpr int kC = BN < 16 ? BN : 16;  // accumulator columns per TMEM load
       for (int c0 = 0; c0 < BN; c0 += kC) {
         float v[kC];
         const uint32_t col = tmem + (uint32_t)(buf * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
-        if constexpr (FP4 && BN == 8 && (kFp4Terms == 6 || kFp4Terms == 4)) {
+        if constexpr (FP4 && BN == 8 && kFp4Terms == 4) {
           // the term partial sums are consecutive columns: one round trip
           float w[kFp4Terms * 8];
-          if constexpr (kFp4Terms == 6) tc_ld48(col, w);
-          else tc_ld32(col, w);
+          tc_ld32(col, w);
 #pragma unroll
           for (int j = 0; j < kC; ++j) v[j] = w[j];
 #pragma unroll
@@ -871,12 +840,7 @@ struct GemmCta {
             }
           }
         }
-        if (partial) {
-          const int part = u - tile * parts;
-          float *dst = partial + (((size_t)tile * kMmaM + row_local) * BN + c0) * parts + part;
-#pragma unroll
-          for (int j = 0; j < kC; ++j) dst[(size_t)j * parts] = v[j];
-        } else if (a.mode == 0) {
+        if (a.mode == 0) {
           const int d = r >> 1;
           const bool is_up = (r & 1) != 0;
           const float bias = is_up ? (a.bias1 ? a.bias1[(size_t)t.e * a.out_rows + d] : 0.0f)
@@ -941,7 +905,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
     g.produce(a, tt, n_active, n_tiles);
   } else if (warp == 1 && lane == 0) {
     g.mma(a, n_tiles);
-    g.drain_mma(a.err);
+    g.drain_mma(a.err, a.wait_shift);
   } else if (warp >= 2) {
     g.epilogue(a, tt, n_active, n_tiles, warp, lane);
   }
@@ -949,431 +913,6 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
   __syncthreads();
   tc_fence_after();
   if (warp == 1) g.dealloc_tmem();
-}
-
-// ---------------------------------------------------------------------------
-// Single-launch decode block (DecodeLaunch).
-
-// Routing tables of one decode batch, rebuilt in every CTA's shared memory.
-struct DecodeRouting {
-  int32_t sel_idx[kDecodeMaxSlots];
-  float sel_w[kDecodeMaxSlots];
-  int32_t perm[kDecodeMaxSlots];
-  int32_t slot_pos[kDecodeMaxSlots];
-  int32_t pos_expert[kDecodeMaxSlots];
-  int32_t cnt[kDispatchMaxExperts];
-  int32_t offsets[kDispatchMaxExperts + 1];
-  int32_t pad_off[kDispatchMaxExperts];
-  int32_t act_list[kDispatchMaxExperts];
-  int32_t act_idx[kDispatchMaxExperts];  // expert -> index in act_list (active experts)
-  int32_t tile_gu[kDispatchMaxExperts + 1];
-  int32_t tile_dn[kDispatchMaxExperts + 1];
-  int32_t meta[2];
-};
-
-using DecodeGemm = GemmCta<kDecodeBn, true, kMmaStageTilesFp4>;
-using DecodeShape = DecodeGemm::S;
-
-// Grid barrier over the co-resident CTAs of a cooperative launch: every CTA
-// adds one to the counter and waits until it reaches `target` (the number of
-// barriers so far times the grid).  The wait is bounded (~2^31 clocks) and
-// ends early once any role has recorded an error; every CTA arrives at every
-// barrier, so the counter always ends a launch at barriers x grid.  The proxy
-// fences order generic-proxy writes before tensor-memory-access (TMA) reads
-// of the same bytes in any CTA after the barrier.
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Stamps of the optional trace (thread 0 of each CTA): `in` when this CTA's
-// phase work is done, `out` when the barrier lets it go.
-__device__ __forceinline__ void grid_sync(uint32_t *count, uint32_t target, int32_t *err, int code,
-                                          uint64_t *in = nullptr, uint64_t *out = nullptr) {
-  asm volatile("fence.proxy.async;" ::: "memory");
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    if (in) *in = global_ns();
-    __threadfence();
-    atomicAdd(count, 1u);
-    const long long t0 = clock64();
-    for (uint32_t i = 0;; ++i) {
-      uint32_t v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
-      if (v >= target) break;
-      if ((i & 63u) == 0u) {
-        if (*(volatile int32_t *)err != 0) break;
-        if (clock64() - t0 > (1ll << 31)) {
-          atomicCAS(err, 0, code);
-          break;
-        }
-      }
-      __nanosleep(32);
-    }
-    __threadfence();
-    if (out) *out = global_ns();
-  }
-  __syncthreads();
-  asm volatile("fence.proxy.async;" ::: "memory");
-}
-
-// Dispatch of at most kDecodeMaxSlots slots by one warp, with the results of
-// k_dispatch: slot s is dispatched when !(weight <= 0); expert segments in
-// expert order; inside a segment the slots in descending slot order; per
-// active expert ceil(n/bn) token tiles, each with a 128-row activation slot
-// (pad_off) and mt_gu / mt_dn row tiles (tile prefixes over active experts).
-__device__ void dispatch_warp(DecodeRouting &rt, int S, int E, int bn, int mt_gu, int mt_dn, int lane) {
-  for (int e = lane; e < kDispatchMaxExperts; e += 32) rt.cnt[e] = 0;
-  __syncwarp();
-  for (int s = lane; s < S; s += 32)
-    if (!(rt.sel_w[s] <= 0.0f)) atomicAdd(&rt.cnt[rt.sel_idx[s]], 1);
-  __syncwarp();
-  constexpr int kPer = kDispatchMaxExperts / 32;  // experts lane*kPer .. lane*kPer + kPer-1
-  int v[5] = {0, 0, 0, 0, 0};  // tokens, active, slot rows, gate/up tiles, down tiles
-#pragma unroll 1
-  for (int i = 0; i < kPer; ++i) {
-    const int e = lane * kPer + i;
-    const int c = e < E ? rt.cnt[e] : 0;
-    const int nt = (c + bn - 1) / bn;
-    v[0] += c;
-    v[1] += c > 0 ? 1 : 0;
-    v[2] += nt * kMmaM;
-    v[3] += nt * mt_gu;
-    v[4] += nt * mt_dn;
-  }
-  int ex[5], tot[5];
-#pragma unroll
-  for (int k = 0; k < 5; ++k) {
-    int inc = v[k];
-#pragma unroll
-    for (int dlt = 1; dlt < 32; dlt <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, inc, dlt);
-      if (lane >= dlt) inc += o;
-    }
-    ex[k] = inc - v[k];
-    tot[k] = __shfl_sync(0xffffffffu, inc, 31);
-  }
-#pragma unroll 1
-  for (int i = 0; i < kPer; ++i) {
-    const int e = lane * kPer + i;
-    if (e < E) {
-      const int c = rt.cnt[e];
-      const int nt = (c + bn - 1) / bn;
-      rt.offsets[e] = ex[0];
-      if (c > 0) {
-        rt.act_list[ex[1]] = e;
-        rt.act_idx[e] = ex[1];
-        rt.pad_off[e] = ex[2];
-        rt.tile_gu[ex[1]] = ex[3];
-        rt.tile_dn[ex[1]] = ex[4];
-      }
-      ex[0] += c;
-      ex[1] += c > 0 ? 1 : 0;
-      ex[2] += nt * kMmaM;
-      ex[3] += nt * mt_gu;
-      ex[4] += nt * mt_dn;
-    }
-  }
-  if (lane == 0) {
-    rt.offsets[E] = tot[0];
-    rt.meta[0] = tot[1];
-    rt.meta[1] = tot[0];
-    rt.tile_gu[tot[1]] = tot[3];
-    rt.tile_dn[tot[1]] = tot[4];
-  }
-  __syncwarp();
-  for (int s = lane; s < S; s += 32) {
-    if (!(rt.sel_w[s] <= 0.0f)) {
-      const int e = rt.sel_idx[s];
-      int before = 0;  // dispatched slots of the same expert after s
-      for (int s2 = s + 1; s2 < S; ++s2) before += (rt.sel_idx[s2] == e && !(rt.sel_w[s2] <= 0.0f)) ? 1 : 0;
-      const int pos = rt.offsets[e] + before;
-      rt.perm[pos] = s;
-      rt.slot_pos[s] = pos;
-      rt.pos_expert[pos] = e;
-    } else {
-      rt.slot_pos[s] = -1;
-    }
-  }
-  __syncwarp();
-}
-
-// K parts per tile of a decode GEMM with n_tiles tiles on `grid` CTAs: 1 when
-// there are at least 4 tiles per CTA, else the smallest divisor of the stage
-// count giving 4 units per CTA, within kDecodeMaxUnitsPerCta units per CTA.
-__device__ __forceinline__ int pick_parts(int n_tiles, int kt_n, int ks, int grid) {
-  const int n_st = (kt_n + ks - 1) / ks;
-  if (n_tiles <= 0 || n_tiles >= 4 * grid) return 1;
-  const int want = (4 * grid + n_tiles - 1) / n_tiles, cap = kDecodeMaxUnitsPerCta * grid;
-  int best = 1;
-  for (int p = 1; p <= n_st && p <= kDecodeMaxParts; ++p) {
-    if (n_st % p != 0 || n_tiles * p > cap) continue;
-    best = p;
-    if (p >= want) break;
-  }
-  return best;
-}
-
-// Sum of the parts of one element of a split GEMM, in part order, from
-// partial[tile][row][col][parts]: the loads are issued together, then added.
-__device__ __forceinline__ float sum_parts(const float *partial, int tile, int parts, int row, int col) {
-  const float *q = partial + (((size_t)tile * kMmaM + row) * kDecodeBn + col) * parts;
-  float pv[kDecodeMaxParts];
-#pragma unroll
-  for (int p = 0; p < kDecodeMaxParts; ++p) pv[p] = p < parts ? __ldcg(q + p) : 0.0f;
-  float v = pv[0];
-#pragma unroll
-  for (int p = 1; p < kDecodeMaxParts; ++p)
-    if (p < parts) v += pv[p];
-  return v;
-}
-
-__device__ __forceinline__ void fill_tiles(TileTables &tt, const DecodeRouting &rt, const int32_t *tile_off,
-                                           int na) {
-  for (int i = threadIdx.x; i < na; i += blockDim.x) {
-    const int e = rt.act_list[i];
-    tt.e[i] = e;
-    tt.p0[i] = rt.offsets[e];
-    tt.n[i] = rt.cnt[e];
-    tt.pad[i] = rt.pad_off[e];
-    tt.tile_off[i] = tile_off[i];
-  }
-  if (threadIdx.x == 0) tt.tile_off[na] = tile_off[na];
-}
-
-__global__ void __launch_bounds__(192, 1) k_moe_decode(const __grid_constant__ DecodeLaunch d) {
-  using G = DecodeGemm;
-  using S = DecodeShape;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  G g(smem);
-  TileTables &ttg = *reinterpret_cast<TileTables *>(smem + S::kRing + G::kBarBytes);
-  TileTables &ttd = *(&ttg + 1);
-  DecodeRouting &rt = *reinterpret_cast<DecodeRouting *>(&ttd + 1);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int T = d.T, H = d.H, D = d.D, E = d.E, K = d.K, nS = T * K;
-  uint32_t nbar = 0;
-  uint64_t *tr = d.trace ? d.trace + (size_t)blockIdx.x * kDecodeTraceSlots : nullptr;
-  if (tr && threadIdx.x == 0) tr[0] = global_ns();
-  if (threadIdx.x == 0) {
-    g.init_barriers();
-    // the GEMM phases' tensor maps, fetched while the router runs
-    for (const CUtensorMap *m : {&d.gu.tmap_a, &d.gu.tmap_a1, &d.gu.tmap_b, &d.gu.tmap_b1, &d.dn.tmap_a,
-                                 &d.dn.tmap_a1, &d.dn.tmap_b, &d.dn.tmap_b1})
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
-  }
-  if (warp == 1) g.alloc_tmem();
-
-  // ---- 1. router logits: CTA c computes experts c, c + grid, ... for every
-  // token from rows staged in the (still idle) stage ring
-  {
-    float *ws = reinterpret_cast<float *>(smem);  // [H] router row
-    float *xs = ws + H;                           // [T][H] input rows
-    const int q = H / 4;
-    bool have_x = false;
-    for (int e = blockIdx.x; e < E; e += gridDim.x) {
-      const int rows = have_x ? 1 : 1 + T;
-      for (int i = threadIdx.x; i < rows * q; i += blockDim.x) {
-        const int r = i / q, c = i - r * q;
-        const float *src = r == 0 ? d.router_w + (size_t)e * H : d.x + (size_t)(r - 1) * H;
-        float *dst = r == 0 ? ws : xs + (size_t)(r - 1) * H;
-        cp_async16(dst + 4 * c, src + 4 * c);
-      }
-      asm volatile("cp.async.wait_all;" ::: "memory");
-      __syncthreads();
-      have_x = true;
-      for (int t = warp; t < T; t += nwarps) {
-        const float r = router_dot(ws, xs + (size_t)t * H, H, lane);
-        if (lane == 0) d.logits[(size_t)t * E + e] = r + (d.router_b ? d.router_b[e] : 0.0f);
-      }
-      __syncthreads();
-    }
-  }
-  tc_fence_before();  // the TMEM address written by tcgen05.alloc, read below by every thread
-  ++nbar;
-  grid_sync(d.gbar, nbar * gridDim.x, d.err, 5 + (int)nbar, tr ? tr + 1 : nullptr, tr ? tr + 2 : nullptr);
-  tc_fence_after();
-  g.tmem = *g.tmem_slot;
-
-  // ---- 2. selection and dispatch, in every CTA
-  {
-    float *lg = reinterpret_cast<float *>(smem);  // [T][E] logits (written by every CTA above)
-    for (int i = threadIdx.x; i < T * E; i += blockDim.x) lg[i] = __ldcg(d.logits + i);
-    __syncthreads();
-    if (tr && threadIdx.x == 0) tr[13] = global_ns();
-    for (int t = warp; t < T; t += nwarps) select_token(lg, t, E, K, lane, rt.sel_idx, rt.sel_w);
-    __syncthreads();
-    if (tr && threadIdx.x == 0) tr[14] = global_ns();
-    if (warp == 0) dispatch_warp(rt, nS, E, kDecodeBn, d.gu.mtiles, d.dn.mtiles, lane);
-    __syncthreads();
-    if (tr && threadIdx.x == 0) tr[17] = global_ns();
-    const int na = rt.meta[0];
-    fill_tiles(ttg, rt, rt.tile_gu, na);
-    fill_tiles(ttd, rt, rt.tile_dn, na);
-    __syncthreads();
-    // The experts are known: start this CTA's weight tiles of both GEMMs on
-    // their way into L2 now, so the GEMMs stream them from L2 instead of
-    // paying the cold DRAM latency per tile.
-    if (threadIdx.x == 0) {
-      g.prefetch_all(d.gu, ttg, na, na > 0 ? ttg.tile_off[na] : 0);
-      g.prefetch_all(d.dn, ttd, na, na > 0 ? ttd.tile_off[na] : 0);
-    }
-    if (blockIdx.x == 0) {  // the same routing outputs as the separate kernels
-      const int total = rt.meta[1];
-      for (int i = threadIdx.x; i < nS; i += blockDim.x) {
-        d.sel_idx[i] = rt.sel_idx[i];
-        d.sel_w[i] = rt.sel_w[i];
-        d.slot_pos[i] = rt.slot_pos[i];
-        if (i < total) d.perm[i] = rt.perm[i];
-      }
-      for (int i = threadIdx.x; i <= E; i += blockDim.x) d.offsets[i] = rt.offsets[i];
-      for (int i = threadIdx.x; i < na; i += blockDim.x) d.act_list[i] = rt.act_list[i];
-      if (threadIdx.x == 0) {
-        d.meta[0] = rt.meta[0];
-        d.meta[1] = rt.meta[1];
-      }
-    }
-    __syncthreads();
-    if (tr && threadIdx.x == 0) tr[3] = global_ns();
-  }
-  const int na = rt.meta[0], total = rt.meta[1];
-  const int n_tiles_gu = na > 0 ? ttg.tile_off[na] : 0, n_tiles_dn = na > 0 ? ttd.tile_off[na] : 0;
-  const int parts_gu = pick_parts(n_tiles_gu, d.gu.ktiles, kMmaStageTilesFp4, gridDim.x);
-  const int parts_dn = pick_parts(n_tiles_dn, d.dn.ktiles, kMmaStageTilesFp4, gridDim.x);
-
-  // ---- 3. gate/up activation operands: warp items (position, K tile)
-  {
-    // items spread over the CTAs first: a small batch uses many SMs
-    const int kt_n = d.gu.ktiles;
-    for (int it = blockIdx.x + warp * gridDim.x; it < total * kt_n; it += gridDim.x * nwarps) {
-      const int pos = it / kt_n, kt = it - pos * kt_n;
-      const int e = rt.pos_expert[pos], j = pos - rt.offsets[e];
-      const int slot = rt.pad_off[e] + (j / kDecodeBn) * kMmaM;
-      if (tr && threadIdx.x == 0 && it == (int)blockIdx.x) tr[18] = global_ns();
-      quantize_ktile<true, false>(d.x + (size_t)(rt.perm[pos] / K) * H, H, kt, kt_n, j, slot, kDecodeBn, d.rb,
-                                  d.qx, d.sfx, lane);
-      if (tr && threadIdx.x == 0 && it == (int)blockIdx.x) tr[19] = global_ns();
-    }
-  }
-  ++nbar;
-  grid_sync(d.gbar, nbar * gridDim.x, d.err, 5 + (int)nbar, tr ? tr + 4 : nullptr, tr ? tr + 5 : nullptr);
-
-  // ---- 4. gate/up GEMM + SwiGLU -> d.gu.y (split: part sums -> d.partial)
-  {
-    float *ws = parts_gu > 1 ? d.partial : nullptr;
-    if (warp == 0 && lane == 0) g.produce(d.gu, ttg, na, n_tiles_gu, parts_gu);
-    else if (warp == 1 && lane == 0) g.mma(d.gu, n_tiles_gu, parts_gu);
-    else if (warp >= 2) g.epilogue(d.gu, ttg, na, n_tiles_gu, warp, lane, parts_gu, ws);
-  }
-  tc_fence_before();
-  ++nbar;
-  grid_sync(d.gbar, nbar * gridDim.x, d.err, 5 + (int)nbar, tr ? tr + 6 : nullptr, tr ? tr + 7 : nullptr);
-  tc_fence_after();
-
-  // ---- 5. down activation operands from the SwiGLU rows (L2 reads)
-  {
-    const int kt_n = d.dn.ktiles;
-    for (int it = blockIdx.x + warp * gridDim.x; it < total * kt_n; it += gridDim.x * nwarps) {
-      const int pos = it / kt_n, kt = it - pos * kt_n;
-      const int e = rt.pos_expert[pos], j = pos - rt.offsets[e];
-      const int slot = rt.pad_off[e] + (j / kDecodeBn) * kMmaM;
-      if (tr && threadIdx.x == 0 && it == (int)blockIdx.x) tr[20] = global_ns();
-      if (parts_gu == 1) {
-        quantize_ktile<true, true>(d.gu.y + (size_t)pos * D, D, kt, kt_n, j, slot, kDecodeBn, d.rb, d.qa, d.sfa,
-                                   lane);
-      } else {
-        // SwiGLU of the summed parts: gate row 2dd and up row 2dd+1 of the
-        // tile's 128-row block, column j % kDecodeBn
-        const int ai = rt.act_idx[e], ntn = (rt.cnt[e] + kDecodeBn - 1) / kDecodeBn, nt = j / kDecodeBn;
-        const int d0 = kt * kMmaKT + (lane >> 3) * 32 + (lane & 7) * 4;
-        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (d0 < D) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int dd = d0 + i, rg = 2 * dd;
-            const int tile = ttg.tile_off[ai] + (rg / kMmaM) * ntn + nt;
-            const float gsum = sum_parts(d.partial, tile, parts_gu, rg % kMmaM, j % kDecodeBn);
-            const float usum = sum_parts(d.partial, tile, parts_gu, rg % kMmaM + 1, j % kDecodeBn);
-            const float vg = gsum + (d.gu.bias0 ? d.gu.bias0[(size_t)e * D + dd] : 0.0f);
-            const float vu = usum + (d.gu.bias1 ? d.gu.bias1[(size_t)e * D + dd] : 0.0f);
-            a4[i] = swiglu_ref(vg, vu);
-          }
-        }
-        quantize_vals<true>(make_float4(a4[0], a4[1], a4[2], a4[3]), kt, kt_n, j, slot, kDecodeBn, d.rb, d.qa,
-                            d.sfa, lane);
-      }
-      if (tr && threadIdx.x == 0 && it == (int)blockIdx.x) tr[21] = global_ns();
-    }
-  }
-  ++nbar;
-  grid_sync(d.gbar, nbar * gridDim.x, d.err, 5 + (int)nbar, tr ? tr + 8 : nullptr, tr ? tr + 9 : nullptr);
-
-  // ---- 6. down GEMM -> d.dn.y (split: part sums -> d.partial)
-  {
-    float *ws = parts_dn > 1 ? d.partial : nullptr;
-    if (warp == 0 && lane == 0) {
-      g.produce(d.dn, ttd, na, n_tiles_dn, parts_dn);
-    } else if (warp == 1 && lane == 0) {
-      g.mma(d.dn, n_tiles_dn, parts_dn);
-      g.drain_mma(d.err);
-    } else if (warp >= 2) {
-      g.epilogue(d.dn, ttd, na, n_tiles_dn, warp, lane, parts_dn, ws);
-    }
-  }
-  tc_fence_before();
-  ++nbar;
-  grid_sync(d.gbar, nbar * gridDim.x, d.err, 5 + (int)nbar, tr ? tr + 10 : nullptr, tr ? tr + 11 : nullptr);
-  tc_fence_after();
-
-  // ---- 7. combine: out[t] = sum over r of fma(row, weight, out[t]) (k_combine)
-  {
-    const int q = H / 4;
-    for (int i = blockIdx.x + threadIdx.x * gridDim.x; i < T * q; i += gridDim.x * blockDim.x) {
-      const int t = i / q, h = (i - t * q) * 4;
-      float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      for (int r = 0; r < K; ++r) {
-        const int sl = t * K + r;
-        const float w = rt.sel_w[sl];
-        if (w <= 0.0f) continue;
-        const int pos = rt.slot_pos[sl];
-        float4 v;
-        if (parts_dn == 1) {
-          v = __ldcg(reinterpret_cast<const float4 *>(d.dn.y + (size_t)pos * H + h));
-        } else {  // the down row: summed parts + bias (rows h..h+3 share a 128-row block)
-          const int e = rt.pos_expert[pos], j = pos - rt.offsets[e];
-          const int ntn = (rt.cnt[e] + kDecodeBn - 1) / kDecodeBn;
-          const int tile = ttd.tile_off[rt.act_idx[e]] + (h / kMmaM) * ntn + j / kDecodeBn;
-          float r4[4];
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            r4[c] = sum_parts(d.partial, tile, parts_dn, (h + c) % kMmaM, j % kDecodeBn) +
-                    (d.dn.bias0 ? d.dn.bias0[(size_t)e * H + h + c] : 0.0f);
-          v = make_float4(r4[0], r4[1], r4[2], r4[3]);
-        }
-        o.x = fmaf(v.x, w, o.x);
-        o.y = fmaf(v.y, w, o.y);
-        o.z = fmaf(v.z, w, o.z);
-        o.w = fmaf(v.w, w, o.w);
-      }
-      *reinterpret_cast<float4 *>(d.out + (size_t)t * H + h) = o;
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (tr && threadIdx.x == 0) tr[12] = global_ns();
-  if (warp == 1) g.dealloc_tmem();
-  if (threadIdx.x == 0) {
-    // every CTA has passed the last barrier: the last one out resets the
-    // counters for the next launch
-    __threadfence();
-    if (atomicAdd(&d.gbar[1], 1u) == gridDim.x - 1) {
-      atomicExch(&d.gbar[0], 0u);
-      atomicExch(&d.gbar[1], 0u);
-    }
-  }
 }
 
 template <int BN, bool FP4, int KS>
@@ -1428,41 +967,6 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
   return launch_pdl(mma_fp4(bn) ? k_quantize_act<true> : k_quantize_act<false>, dim3((unsigned)blocks),
                     dim3(threads), 0, s, src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off, pos_expert, meta,
                     S_max, K, kp, rb, bn, q, sf);
-}
-
-size_t decode_ring_bytes() { return (size_t)DecodeShape::kRing; }
-size_t decode_smem_bytes() {
-  return (size_t)DecodeShape::kRing + 1024 /*align*/ + DecodeGemm::kBarBytes + 2 * sizeof(TileTables) +
-         sizeof(DecodeRouting);
-}
-
-int decode_max_grid(int sm_count) {
-  if (opt_in_smem(k_moe_decode, (int)decode_smem_bytes()) != cudaSuccess) return 0;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_moe_decode, 192, decode_smem_bytes()) !=
-      cudaSuccess)
-    return 0;
-  return per_sm >= 1 ? sm_count : 0;
-}
-
-cudaError_t launch_moe_decode(const DecodeLaunch &d, int grid, cudaStream_t s) {
-  if (grid < 1 || d.T < 1 || d.T * d.K > kDecodeMaxSlots || d.E > kDispatchMaxExperts || d.H % 32 != 0 ||
-      d.D % 4 != 0 || (size_t)(1 + d.T) * d.H * 4 > decode_ring_bytes() ||
-      (size_t)d.T * d.E * 4 > decode_ring_bytes() || (reinterpret_cast<uintptr_t>(d.x) & 15) != 0)
-    return cudaErrorInvalidValue;
-  cudaError_t e = opt_in_smem(k_moe_decode, (int)decode_smem_bytes());
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(192);
-  cfg.dynamicSmemBytes = decode_smem_bytes();
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid barriers need it
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_moe_decode, d);
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {

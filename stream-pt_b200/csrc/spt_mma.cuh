@@ -99,6 +99,8 @@ struct MmaLaunch {
   int out_rows = 0;                  // D (mode 0) or H (mode 1)
   int32_t *err = nullptr;            // set nonzero when a bounded wait gives up
   int prefetch = 0;                  // whole weight tiles prefetched into L2 ahead (0: off)
+  int wait_shift = 31;               // bounded waits give up after ~2^wait_shift clocks
+  int fault_stage = -1;              // failure injection (tests): CTA 0's producer skips this stage
 };
 
 // Token tiles of 8 or 16 tokens run the FP4 mode (kFp4Terms e2m1 terms
@@ -152,64 +154,5 @@ cudaError_t launch_quantize_act(const float *src, int64_t src_stride, const int3
                                 int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s);
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s);
-
-// The whole MoE block for decode-sized batches in one cooperative launch
-// (k_moe_decode, one CTA per SM): router logits, top-k selection and
-// dispatch (recomputed in every CTA from the logits, published by CTA 0),
-// the activation operands, the gate/up GEMM with SwiGLU, the SwiGLU
-// operands, the down GEMM and the combine, separated by grid barriers.
-// Same arithmetic as the separate kernels of the tensor-core path with
-// kDecodeBn-token tiles and four K tiles per stage, so the two paths give
-// identical bits, except that a GEMM with fewer than 4 tiles per CTA is split
-// along K (its part sums add in another order: equal to rounding).
-constexpr int kDecodeBn = 8;
-constexpr int kDecodeMaxSlots = 64;  // tokens x top-k
-struct DecodeLaunch {
-  MmaLaunch gu, dn;                // the two GEMMs (tile tables are built in each CTA)
-  const float *x = nullptr;        // [T][H] input rows (16-byte aligned)
-  const float *router_w = nullptr; // [E][H]
-  const float *router_b = nullptr; // [E] or null
-  int T = 0, H = 0, D = 0, E = 0, K = 0;
-  int rb = 0;                      // activation rows per term
-  float *logits = nullptr;         // [T][E]
-  int32_t *sel_idx = nullptr;      // [T*K]; these five as the dispatch kernel writes them
-  float *sel_w = nullptr;          // [T*K]
-  int32_t *offsets = nullptr;      // [E+1]
-  int32_t *perm = nullptr;         // [T*K]
-  int32_t *slot_pos = nullptr;     // [T*K]
-  int32_t *act_list = nullptr;     // [E]
-  int32_t *meta = nullptr;         // [2] active experts, dispatched slots
-  uint8_t *qx = nullptr, *sfx = nullptr, *qa = nullptr, *sfa = nullptr;
-  float *out = nullptr;            // [T][H]
-  uint32_t *gbar = nullptr;        // [2] grid-barrier counters, zero between launches
-  int32_t *err = nullptr;          // set nonzero when a bounded wait gives up
-  uint64_t *trace = nullptr;       // [grid][kDecodeTraceSlots] %globaltimer stamps, or null
-  float *partial = nullptr;        // split-K sums: kDecodeMaxUnitsPerCta * grid units x 128 x kDecodeBn
-};
-// Split-K (decode kernel): when a GEMM has fewer than 4 tiles per CTA its
-// tiles are cut into K parts on pipeline-stage boundaries, at most
-// kDecodeMaxUnitsPerCta (tile, part) units per CTA in all.
-constexpr int kDecodeMaxUnitsPerCta = 8;
-constexpr int kDecodeMaxParts = 8;
-inline size_t decode_partial_bytes(int grid) {
-  return (size_t)kDecodeMaxUnitsPerCta * grid * kMmaM * kDecodeBn * sizeof(float);
-}
-// Trace slots per CTA: 0 entry, 1 router done, 2 barrier 1 passed, 3 routing
-// done, 4 gate/up operands done, 5 barrier 2 passed, 6 gate/up GEMM done, 7
-// barrier 3 passed, 8 down operands done, 9 barrier 4 passed, 10 down GEMM
-// done, 11 barrier 5 passed, 12 combine done; finer points: 13 logits
-// staged, 14 selection done, 17 dispatch done, 18/19 and 20/21 start and end
-// of the first operand item of warp 0 in the two quantisation phases.
-constexpr int kDecodeTraceSlots = 24;
-constexpr int kDecodeTracePoints = 13;
-// Shared-memory bytes of the decode kernel, and the bytes of its stage ring,
-// which also holds the router's staged rows ((1 + T) * H floats) and the
-// logits (T * E floats) before the GEMMs use it.
-size_t decode_smem_bytes();
-size_t decode_ring_bytes();
-// Largest co-resident grid for the decode kernel on the current device (0:
-// it cannot run there).
-int decode_max_grid(int sm_count);
-cudaError_t launch_moe_decode(const DecodeLaunch &d, int grid, cudaStream_t s);
 
 }  // namespace spt

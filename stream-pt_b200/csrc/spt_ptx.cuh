@@ -36,20 +36,32 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after ~2^31 clock cycles (about a second at the
-// B200's clock) and records `code` in err.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
+// Bounded wait: gives up after ~2^shift clock cycles (2^31: about a second
+// at the B200's clock) and records `code` in err.  It also gives up at once
+// when another role of the kernel has recorded an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code, int shift = 31) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*(volatile int32_t *)err != 0) return false;  // another role already gave up
-      if (clock64() - t0 > (1ll << 31)) {
+      if (clock64() - t0 > (1ll << shift)) {
         atomicCAS(err, 0, code);
         return false;
       }
     }
+  }
+}
+
+// Bounded wait for work this thread started itself (copies or tensor-core
+// operations in flight) on the way out after an error: unlike mbar_wait it
+// does not stop when an error is recorded, only after ~2^shift clocks.
+__device__ __forceinline__ bool mbar_wait_own(uint64_t *bar, uint32_t parity, int shift = 31) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255u) == 0u && clock64() - t0 > (1ll << shift)) return false;
   }
 }
 

@@ -1,5 +1,6 @@
-"""GPU parity of the tcgen05 path (FP4 weights x three MXFP8 activation
-terms on the tensor cores).
+"""GPU parity of the tcgen05 path (packed FP4 weights x block-scaled
+activation terms on the tensor cores: four e2m1 terms for token tiles of 8
+or 16, three e4m3 terms for 128-token tiles).
 
 Routing and dispatch are computed by the same bit-exact kernels as the exact
 path and must match the oracle bit for bit.  Block outputs are checked at
@@ -70,12 +71,11 @@ def test_mma_block_matches_oracle(ctx, mma_layer, T):
 @pytest.mark.parametrize("bn", [None, "8", "16", "128"])
 @pytest.mark.parametrize("mode", ["normal", "ties", "underflow", "clamp"])
 @pytest.mark.parametrize("experts,k", [(4, 2), (7, 7), (8, 1)])
-def test_mma_reference_fixtures(ctx, monkeypatch, mode, experts, k, bn):
-    """Every token-tile width (SPT_MMA_BN; None: the size rule) on the
-    reference's fixtures; 37 tokens over 4-8 experts put up to 37 tokens on
-    one expert, so the 8- and 16-token tiles split experts into several."""
-    if bn is not None:
-        monkeypatch.setenv("SPT_MMA_BN", bn)
+def test_mma_reference_fixtures(ctx, mode, experts, k, bn):
+    """Every token-tile width (SPT_OPT_TILE_TOKENS; None: the size rule) on
+    the reference's fixtures; 37 tokens over 4-8 experts put up to 37 tokens
+    on one expert, so the 8- and 16-token tiles split experts into several."""
+    ctx.set_option(spt.OPT_TILE_TOKENS, int(bn or 0))
     fx = refdata.moe_batch_fixture(96, 64, experts, k, 0, mode)
     batch = 37
     x = refdata.moe_batch_x(batch, 96, mode)
@@ -85,13 +85,14 @@ def test_mma_reference_fixtures(ctx, monkeypatch, mode, experts, k, bn):
         got = ctx.forward_moe_batch(arena, x, batch)
     finally:
         ctx.set_path(spt.PATH_AUTO)
+        ctx.set_option(spt.OPT_TILE_TOKENS, 0)
         arena.close()
     want = oracle.forward_moe_batch(fx.dense, x, batch)
     _check_close(got, want, (mode, experts, k, bn))
 
 
 @pytest.mark.parametrize("bn", ["8", "16"])
-def test_mma_decode_tile_widths(ctx, monkeypatch, mma_layer, bn):
+def test_mma_decode_tile_widths(ctx, mma_layer, bn):
     """GPT-OSS layer at decode sizes with each FP4 tile width: against the
     oracle, and the two widths agree with each other within the tolerance."""
     cfg, dense, arena = mma_layer
@@ -99,15 +100,16 @@ def test_mma_decode_tile_widths(ctx, monkeypatch, mma_layer, bn):
     try:
         for T in (1, 32, 64):
             x = spt.synth_normal_host(T, 3000, T * 2880)
-            monkeypatch.setenv("SPT_MMA_BN", bn)
+            ctx.set_option(spt.OPT_TILE_TOKENS, int(bn))
             got = ctx.forward_moe_batch(arena, x, T)
             n = min(T, 8)
             want = oracle.forward_moe_batch(dense, x[: n * 2880], n, workers=8)
             _check_close(got[: n * 2880], want, (bn, T))
-            monkeypatch.setenv("SPT_MMA_BN", "128")
+            ctx.set_option(spt.OPT_TILE_TOKENS, 128)
             _check_close(got, ctx.forward_moe_batch(arena, x, T), (bn, T, "vs 128"))
     finally:
         ctx.set_path(spt.PATH_AUTO)
+        ctx.set_option(spt.OPT_TILE_TOKENS, 0)
 
 
 def test_mma_large_batch_properties(ctx, mma_layer):
@@ -126,75 +128,3 @@ def test_mma_large_batch_properties(ctx, mma_layer):
     gp = ctx.forward_moe_batch(arena, x.reshape(T, 2880)[perm].ravel(), T).reshape(T, 2880)
     _check_close(gp, got[perm], "perm")
     ctx.set_path(spt.PATH_AUTO)
-
-
-@pytest.mark.parametrize("T", [1, 3, 8, 12])
-def test_decode_kernel_matches_separate_kernels(ctx, monkeypatch, mma_layer, T):
-    """The single-launch decode block (k_moe_decode) against the separate
-    tensor-core kernels with the same 8-token tiles: identical routing, and
-    identical output bits where no GEMM is split along K (T >= 8 here: at
-    least 4 tiles per CTA); split GEMMs add their K parts in another order,
-    so T = 1 and 3 agree to rounding (1e-4 of the largest output, a tenth
-    of the block tolerance).  Repeated launches check that the
-    grid-barrier counters reset between launches."""
-    cfg, dense, arena = mma_layer
-    ctx.set_path(spt.PATH_MMA)
-    try:
-        for rep in range(3):
-            x = spt.synth_normal_host(T + 10 * rep, 4000, T * 2880)
-            monkeypatch.setenv("SPT_DECODE_KERNEL", "1")
-            got = ctx.forward_moe_batch(arena, x, T)
-            assert ctx.kernels_per_forward() == 1
-            r1 = ctx.last_routing(T, 128, 4)
-            monkeypatch.setenv("SPT_DECODE_KERNEL", "0")
-            monkeypatch.setenv("SPT_MMA_BN", "8")
-            want = ctx.forward_moe_batch(arena, x, T)
-            assert ctx.kernels_per_forward() > 1
-            r0 = ctx.last_routing(T, 128, 4)
-            monkeypatch.delenv("SPT_MMA_BN")
-            if T >= 8:
-                assert refdata.bits_equal(got, want).all(), (T, rep)
-            else:
-                err = np.abs(got.astype(np.float64) - want).max() / np.abs(want).max()
-                assert err <= 1e-4, (T, rep, err)
-            assert refdata.bits_equal(r1["logits"], r0["logits"]).all()
-            assert np.array_equal(r1["sel_idx"], r0["sel_idx"])
-            assert refdata.bits_equal(r1["sel_w"], r0["sel_w"]).all()
-            assert np.array_equal(r1["perm"], r0["perm"])
-            assert np.array_equal(r1["counts"], r0["counts"])
-        n = min(T, 4)
-        want = oracle.forward_moe_batch(dense, x[: n * 2880], n, workers=8)
-        _check_close(got[: n * 2880], want, T)
-    finally:
-        ctx.set_path(spt.PATH_AUTO)
-
-
-@pytest.mark.parametrize("mode", ["normal", "ties", "nonfinite", "mixed-nan", "underflow", "clamp"])
-@pytest.mark.parametrize("experts,k,batch", [(4, 2, 5), (7, 7, 9), (8, 1, 16), (8, 4, 16)])
-def test_decode_kernel_reference_fixtures(ctx, monkeypatch, mode, experts, k, batch):
-    """The reference's fixtures (router modes with ties, NaN and infinite
-    logits) through the decode kernel: routing bit-exact against the oracle,
-    the block within the tolerance, and equal to the separate kernels."""
-    fx = refdata.moe_batch_fixture(96, 64, experts, k, 0, mode)
-    x = refdata.moe_batch_x(batch, 96, mode)
-    arena = ctx.arena([fx.reader], fx.cfg, [fx.lw], flags=spt.ARENA_MMA)
-    try:
-        ctx.set_path(spt.PATH_MMA)
-        monkeypatch.setenv("SPT_MMA_BN", "8")
-        monkeypatch.setenv("SPT_DECODE_KERNEL", "1")
-        got = ctx.forward_moe_batch(arena, x, batch)
-        fused = ctx.kernels_per_forward()
-        r = ctx.last_routing(batch, experts, k)
-        monkeypatch.setenv("SPT_DECODE_KERNEL", "0")
-        sep = ctx.forward_moe_batch(arena, x, batch)
-    finally:
-        ctx.set_path(spt.PATH_AUTO)
-        arena.close()
-    assert fused == (1 if batch * k <= 64 else 8)
-    want = oracle.forward_moe_batch(fx.dense, x, batch, want_internals=True)
-    assert np.array_equal(r["sel_idx"], want["sel_idx"]), mode
-    assert refdata.bits_equal(r["sel_w"], want["sel_w"]).all(), mode
-    assert np.array_equal(r["perm"], want["perm"]), mode
-    assert refdata.bits_equal(got, sep).all(), mode
-    if np.isfinite(want["out"]).all():
-        _check_close(got, want["out"], (mode, experts, k, batch))

@@ -57,9 +57,10 @@ def test_block_bit_exact_sweep(ctx, experts, bias_type):
                 assert np.array_equal(x.view(np.uint32), orig.view(np.uint32))
 
 
-def test_fused_selection_matches_separate(ctx, monkeypatch):
+def test_fused_selection_matches_separate(ctx):
     """Up to 8 tokens the top-k selection runs inside the dispatch kernel;
-    SPT_FUSED_SELECT=0 keeps the separate selection launch.  Both give the
+    the context option SPT_OPT_FUSED_SELECT = 0 keeps the separate selection
+    launch.  Both give the
     same output bits and routing, over every router mode of the sweep."""
     for experts, top_k in ((7, 2), (33, 4), (128, 32)):
         for mode in refdata.ROUTER_MODES:
@@ -68,9 +69,10 @@ def test_fused_selection_matches_separate(ctx, monkeypatch):
                 x = refdata.moe_batch_x(batch, 96, mode)
                 got = {}
                 for fused in ("1", "0"):
-                    monkeypatch.setenv("SPT_FUSED_SELECT", fused)
+                    ctx.set_option(spt.OPT_FUSED_SELECT, int(fused))
                     out, r, _ = _run_block(ctx, fx, x, batch)
                     got[fused] = (out, r, ctx.kernels_per_forward())
+                ctx.set_option(spt.OPT_FUSED_SELECT, 1)
                 tag = (experts, top_k, mode, batch)
                 (a, ra, ka), (b, rb, kb) = got["1"], got["0"]
                 assert bits_equal(a, b).all(), tag
