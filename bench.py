@@ -1,22 +1,35 @@
 """Benchmark of the B200 MoE FFN block (GPT-OSS-120B shapes).
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--impl ours|reference]
+                [--path auto|mma|gemv16|exact] [--no-extras] [--no-cpu-baseline]
 
 Prints ONE JSON line (rank 0).  A step is one forward of the MoE block over
-one batch of synthetic tokens (seeded Philox weights generated on the device,
-N(0,1) activations).  `value` times the device path with inputs resident in
-HBM; `e2e` times the C-ABI host call (pinned host x -> H2D -> block -> D2H).
+one batch of synthetic tokens: seeded Philox weights with GPT-OSS shapes
+generated on the device, N(0, 1) activations (the real checkpoint is not in
+the image; no dataset is involved).  `value` times the device path with
+inputs resident in HBM (CUDA events on the library's stream); `e2e` times the
+C-ABI host call a caller makes (spt_forward_moe_batch: host x -> device ->
+block -> host out, returned after completion) on the host clock, after a
+synchronised L2 flush, so validation, launch, copies and waiting all count.
 The L2 (126 MB) is flushed between timed steps by writing a 256 MB buffer.
 
---impl reference times the CPU restatement of the reference's AVX2 path
-(oracle/, all host threads) on the same config; rank 0 only.
+The line's workload is --config (default c1).  With one
+GPU the line also carries the other configs under "configs" (c0 decode, c2
+Zipf prefill, c3 T=8192, c4 36-layer stack), each measured in the same
+process with its own parity check.  Under torchrun (N > 1) the block runs
+expert-parallel: rank r holds experts [r*128/N, (r+1)*128/N); the line's
+workload keeps c1's 32 tokens per rank (weak scaling, fixed-capacity
+exchange), and "configs" carries c3 (T = 8192 in total, 8192/N per rank:
+strong scaling) and c4 (64 rows in total).
 
-Configs (BASELINE.json configs[i]): c0 T=1 decode, c1 T=32 prefill batch
-(default: the headline workload), c2 T=2048 Zipf-skewed routing.  Under
-torchrun (N > 1) the block runs expert-parallel: rank r holds experts
-[r*128/N, (r+1)*128/N), routes its own batch of the config's T tokens and
-exchanges token and result rows with the other ranks over NCCL (the layout
-of configs[3]); per-rank tokens are fixed, so scaling is weak.
+Every line has a "parity" object: tokens of the timed workload recomputed by
+the CPU oracle (oracle/, the C restatement of the reference's path) outside
+the timed region, with routing (selected ids, dispatch permutation) compared
+bit for bit and block outputs by max|err|/max|ref| and cosine.
+
+--impl reference times the oracle on the host cores on the same workload
+(rank 0 only): the reference is a Go module that cannot be built here, and
+its C restatement is what runs; it never loads the CUDA library.
 """
 from __future__ import annotations
 
@@ -40,6 +53,9 @@ E, K = 128, 4
 MATRIX_BYTES = 2880 * (2880 // 32) * 17          # one MXFP4 expert matrix, GGUF bytes
 ROUTER_BYTES = E * H * 4
 L2_BYTES = 126 << 20
+FLUSH_BYTES = 256 << 20
+EPS = 1e-5
+MAX_REL, MIN_COS = 1e-3, 0.99999                  # the block's tolerance (north_star)
 
 CONFIGS = {
     "c0": dict(T=1, seed=0, zipf_s=0.0, zipf_beta=0.0, router_bias=True,
@@ -48,27 +64,60 @@ CONFIGS = {
                desc="prefill batch T=32 (BASELINE configs[1])"),
     "c2": dict(T=2048, seed=2, zipf_s=1.1, zipf_beta=0.9, router_bias=True,
                desc="prefill T=2048, Zipf(1.1)-skewed router bias (BASELINE configs[2])"),
-    "c4": dict(T=64, seed=4, zipf_s=0.0, zipf_beta=0.0, router_bias=True, layers=36,
+    "c3": dict(T=8192, seed=3, zipf_s=0.0, zipf_beta=0.0, router_bias=False, strong=True,
+               desc="T=8192 in total, balanced routing (zero router bias), tokens sharded over ranks "
+                    "(BASELINE configs[3])"),
+    "c4": dict(T=64, seed=4, zipf_s=0.0, zipf_beta=0.0, router_bias=True, layers=36, strong=True,
                desc="36-layer stack, RMSNorm + MoE + residual per layer, 64 token rows (BASELINE configs[4])"),
 }
-EPS = 1e-5
+
+
+def dist_info():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def tokens(name, world):
+    """(tokens per rank, tokens in total) of config `name` on `world` ranks."""
+    c = CONFIGS[name]
+    if c.get("strong"):
+        return max(1, c["T"] // world), max(1, c["T"] // world) * world
+    return c["T"], c["T"] * world
+
+
+def workload_config(name, world, ep_mode=None):
+    """The `config` object of a line: identical in both arms for the same
+    workload (it names only the workload, nothing measured)."""
+    c = CONFIGS[name]
+    t_rank, t_all = tokens(name, world)
+    if world == 1:
+        par = "single GPU"
+    else:
+        par = (f"ep{world}: {E // world} experts per GPU, {t_rank} tokens per rank, NCCL dispatch/combine "
+               f"({ep_mode})")
+    return {"workload": f"{name}: {c['desc']}", "tokens_per_step": t_all, "tokens_per_rank": t_rank,
+            "hidden": H, "expert_dim": D, "experts": E, "top_k": K, "layers": c.get("layers", 1),
+            "seed": c["seed"], "router_bias": c["router_bias"], "zipf_s": c["zipf_s"], "zipf_beta": c["zipf_beta"],
+            "scale_bytes": "uniform 119..123", "parallelism": par,
+            "l2": "256 MB buffer written between timed steps"}
 
 
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
-    return 6650.0, "fallback (6.65 TB/s)"
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 0.0)), "measured (MEASURED_PEAKS.json)"
+    return 6650.0, 1590.0, "fallback (6.65 TB/s, 1.59 PFLOP/s)"
 
 
-def load_traffic(config, key="gate_up_dram_bytes"):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+def load_traffic(key):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     if not os.path.exists(p):
         return None
-    d = json.load(open(p))
-    return d.get(config, {}).get(key)
+    return json.load(open(p)).get(key)
 
 
 class ClockSampler:
@@ -176,48 +225,172 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def mma_fp4(T):
-    """Token tiles of <= 16 (T*top_k <= 8*experts) run the kind::mxf4 GEMM."""
-    return T * K <= 8 * E
+# ---------------------------------------------------------------------------
+# the oracle side (CPU): weights, parity, CPU baseline
 
-
-def mma_kind(T):
-    return "kind::mxf4" if mma_fp4(T) else "kind::mxf8f6f4"
-
-
-def mma_dtype(T):
-    if mma_fp4(T):
-        return "mxfp4 weights x 4-term e2m1 activations -> f32 (tcgen05 kind::mxf4)"
-    return "mxfp4 weights x 3-term e4m3 activations -> f32 (tcgen05 kind::mxf8f6f4)"
-
-
-def dist_info():
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
-
-
-def cpu_baseline(cfg_name, seconds=12.0, workers=None):
-    """The oracle (C restatement of the reference's AVX2 path) on the same
-    workload, all host threads.  Returns (tokens/s, cores, sample text)."""
+def oracle_params(name):
     from oracle import oracle
-    spt = importlib.import_module("stream-pt_b200")
-    c = CONFIGS[cfg_name]
-    cfg = spt.Config(H, D, E, K)
-    params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
-                             router_bias=c["router_bias"])
-    host = spt.synth_layer_host(cfg, params)
-    w = oracle.Weights(H, D, E, K, host["router"], host["router_bias"], host["gate"], host["up"],
-                       host["down"], host["gate_bias"], host["up_bias"], host["down_bias"])
-    norm = spt.synth_norm_host(params, 0, H)
+    c = CONFIGS[name]
+    return oracle.synth_params(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
+                               router_bias=c["router_bias"])
+
+
+_WEIGHTS = {}
+
+
+def oracle_weights(name, layer=0):
+    """The whole synthetic layer, generated by the oracle (cached)."""
+    from oracle import oracle
+    key = (CONFIGS[name]["seed"], name, layer)
+    if key not in _WEIGHTS:
+        _WEIGHTS.clear()
+        _WEIGHTS[key] = oracle.synth_weights(H, D, E, K, oracle_params(name), layer)
+    return _WEIGHTS[key]
+
+
+def x_rows(name, rank):
+    from oracle import oracle
+    t_rank, _ = tokens(name, int(os.environ.get("WORLD_SIZE", "1")))
+    return oracle.synth_normal(CONFIGS[name]["seed"] + 7919 * rank, 1000, t_rank * H)
+
+
+def compare(got, want):
+    got = np.asarray(got, np.float64).ravel()
+    want = np.asarray(want, np.float64).ravel()
+    finite = bool(np.isfinite(got).all())
+    err = float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30)) if finite else float("inf")
+    cos = float(np.dot(got, want) / (np.linalg.norm(got) * np.linalg.norm(want) + 1e-300)) if finite else 0.0
+    return err, cos
+
+
+def parity_block(name, x, T, got, routing=None, sample=64):
+    """Sampled tokens of one block against the oracle.  With `routing` (the
+    library's logits, selections and dispatch of the same call) the routing
+    of every token is compared bit for bit; near-ties (the two logits around
+    the k-th choice within 1e-6) are counted."""
+    from oracle import oracle
+    w = oracle_weights(name)
+    x = np.asarray(x, np.float32).reshape(T, H)
+    got = np.asarray(got, np.float32).reshape(T, H)
+    out = {"tokens": T}
+    top = None
+    if routing is not None:
+        lg = oracle.route_threads(w.arrays["router"], x, w.arrays["router_bias"], T, H, E)
+        sel = [oracle.select(lg[t], K) for t in range(T)]
+        sel_idx = np.array([[i for i, _ in s] for s in sel], np.int32)
+        sel_w = np.array([[v for _, v in s] for s in sel], np.float32)
+        perm, counts = oracle.dispatch_perm(sel_idx, sel_w, E)
+        out["logits_bit_exact"] = bool(np.array_equal(lg.view(np.uint32), routing["logits"].view(np.uint32)))
+        out["ids_equal"] = bool(np.array_equal(sel_idx, routing["sel_idx"]))
+        out["weights_bit_exact"] = bool(np.array_equal(sel_w.view(np.uint32), routing["sel_w"].view(np.uint32)))
+        out["perm_equal"] = bool(np.array_equal(perm, routing["perm"]))
+        srt = np.sort(lg, axis=1)[:, ::-1]
+        out["near_ties_1e-6"] = int(np.sum(np.abs(srt[:, K - 1] - srt[:, K]) <= 1e-6))
+        top = int(np.argmax(counts))
+        out["top_expert_share"] = round(float(counts.max() / max(counts.sum(), 1)), 4)
+    # sampled tokens: every 2nd of the first 16 routed to the top expert, the rest spread evenly
+    if T <= sample:
+        idx = list(range(T))
+    else:
+        idx = []
+        if top is not None:
+            idx = [t for t in range(T) if top in routing["sel_idx"][t]][:sample // 4]
+        rest = np.linspace(0, T - 1, sample - len(idx)).astype(int).tolist()
+        idx = sorted(set(idx + rest))
+    want = oracle.forward_moe_batch(w, x[idx].ravel(), len(idx), workers=os.cpu_count() or 8)
+    err, cos = compare(got[idx], want)
+    out.update({"checked_tokens": len(idx), "max_rel": err, "cos": cos,
+                "ok": bool(err <= MAX_REL and cos >= MIN_COS and out.get("ids_equal", True)
+                           and out.get("perm_equal", True))})
+    return out
+
+
+def oracle_stack_layer(name, l, xs, rows):
+    """One layer of the oracle's stack (RMSNorm -> block -> residual add) on
+    `rows` rows; returns (new rows, the rows' selected ids, the gap between
+    the k-th and (k+1)-th largest logit of each row).  Only the experts the
+    rows select are generated."""
+    from oracle import oracle
+    c = CONFIGS[name]
+    p = oracle_params(name)
+    norm = oracle.synth_norm(c["seed"], l, H)
+    normed = oracle.rmsnorm(xs, norm, rows, H, EPS)
+    head = oracle.synth_layer_experts(H, D, E, p, l, [])
+    lg = oracle.route(head["router"], normed, head["router_bias"], rows, H, E)
+    ids = np.array([[i for i, _ in oracle.select(lg[t], K)] for t in range(rows)], np.int32)
+    srt = np.sort(lg, axis=1)[:, ::-1]
+    gap = srt[:, K - 1] - srt[:, K]
+    w = oracle.weights_of(oracle.synth_layer_experts(H, D, E, p, l, sorted(set(ids.ravel().tolist()))), H, D, E, K)
+    out = (xs + oracle.forward_moe_batch(w, normed, rows, workers=os.cpu_count() or 8)).astype(np.float32)
+    return out, ids, gap
+
+
+def parity_stack(name, runner, got, rows=2):
+    """The first `rows` rows of a stack step against the oracle's composition
+    RMSNorm -> block -> residual add, two ways:
+      teacher-forced: each layer of the library (its timed expert path) on
+        the oracle's input to that layer, against the oracle's output; the
+        block tolerance applies per layer and the routing must be bit-exact;
+      free-running: the timed step's final rows against the oracle's own 36
+        layers.  The library's rows are also run layer by layer on their own
+        outputs to find where a row's selected experts first differ from the
+        oracle's; each such divergence is logged with the oracle's gap
+        between the k-th and (k+1)-th logit of that row (a near-tie that the
+        path's rounding tipped over)."""
+    ctx, spt = runner.ctx, runner.spt
+    layers = CONFIGS[name].get("layers", 1)
+    x0 = np.array(np.asarray(runner.x_host, np.float32).reshape(runner.T, H)[:rows], copy=True)
+    path, _ = ctx.last_expert_path()
+    saved = ctx.get_option(spt.OPT_GEMV16_SLOTS)
+    if path == "tcgen05":
+        ctx.set_option(spt.OPT_GEMV16_SLOTS, 0)  # the rows alone would take the decode GEMV
+    worst, worst_cos, ids_ok = 0.0, 1.0, True
+    xo, xg = x0, x0.copy()
+    divergence = {}
+    try:
+        for l in range(layers):
+            nxt, ids, gap = oracle_stack_layer(name, l, xo, rows)
+            tf = ctx.forward_stack(runner.arena, xo, rows, first_layer=l, n_layers=1, eps=EPS).reshape(rows, H)
+            r = ctx.last_routing(rows, E, K)
+            ids_ok = ids_ok and bool(np.array_equal(r["sel_idx"], ids))
+            err, cos = compare(tf, nxt)
+            worst, worst_cos = max(worst, err), min(worst_cos, cos)
+            xg = ctx.forward_stack(runner.arena, xg, rows, first_layer=l, n_layers=1, eps=EPS).reshape(rows, H)
+            gids = ctx.last_routing(rows, E, K)["sel_idx"]
+            for t in range(rows):
+                if t not in divergence and not np.array_equal(gids[t], ids[t]):
+                    divergence[t] = {"layer": l, "oracle_gap": float(gap[t])}
+            xo = nxt
+    finally:
+        ctx.set_option(spt.OPT_GEMV16_SLOTS, saved)
+    final = np.asarray(got, np.float32).reshape(runner.T, H)[:rows]
+    err, cos = compare(final, xo)
+    # rows that kept the oracle's experts in every layer stay close; only a
+    # logged divergence may explain a row that does not
+    ok_free = all(t in divergence for t in range(rows) if not compare(final[t], xo[t])[0] <= 1e-2)
+    return {"tokens": runner.T, "checked_tokens": rows, "layers": layers,
+            "teacher_forced": {"max_rel": worst, "min_cos": worst_cos, "ids_equal": ids_ok},
+            "free_running": {"max_rel": err, "cos": cos, "diverged_rows": divergence},
+            "max_rel": worst, "cos": worst_cos,
+            "ok": bool(worst <= MAX_REL and worst_cos >= MIN_COS and ids_ok and ok_free)}
+
+
+def cpu_baseline(name, seconds=12.0, workers=None):
+    """The oracle (C restatement of the reference's AVX2 path, row-partitioned
+    threads like mulMoEBatchExpert) on the same workload, all host threads,
+    memory-resident weights generated by the oracle itself (the CUDA library
+    is never loaded).  Returns (tokens/s, cores, sample text)."""
+    from oracle import oracle
+    c = CONFIGS[name]
+    w = oracle_weights(name)
     layers = c.get("layers", 1)
     workers = workers or os.cpu_count() or 1
-    T = c["T"]
+    t_rank, _ = tokens(name, 1)
     # bounded sample: at most 64 tokens of the workload per repetition, one
     # layer (a stack's time is the per-layer time times its depth)
-    Ts = min(T, 64)
-    x = spt.synth_normal_host(c["seed"], 1000, Ts * H)
+    Ts = min(t_rank, 64)
+    x = oracle.synth_normal(c["seed"], 1000, Ts * H)
+    norm = oracle.synth_norm(c["seed"], 0, H)
 
     def one():
         xin = oracle.rmsnorm(x, norm, Ts, H, EPS) if layers > 1 else x
@@ -236,7 +409,7 @@ def cpu_baseline(cfg_name, seconds=12.0, workers=None):
             break
     tps = reps * Ts / el / layers
     what = f"{reps} x {Ts} tokens x 1 of {layers} layers" if layers > 1 else f"{reps} x {Ts} tokens"
-    return tps, workers, f"{what} of {cfg_name} ({el:.1f} s, memory-resident weights)"
+    return tps, workers, f"{what} of {name} ({el:.1f} s, memory-resident weights, oracle-generated)"
 
 
 def run_reference(args):
@@ -244,16 +417,217 @@ def run_reference(args):
     if rank != 0:
         return
     tps, cores, sample = cpu_baseline(args.config, seconds=max(3.0, 2.0 * args.steps))
+    t_rank, t_all = tokens(args.config, world)
     line = {"metric": "moe_block_tokens_per_s", "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * CONFIGS[args.config]["T"] / tps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (mxfp4 weights)",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{args.config}: {CONFIGS[args.config]['desc']}",
-                       "tokens_per_step": CONFIGS[args.config]["T"], "hidden": H, "experts": E, "top_k": K},
-            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_all / tps,
+            "higher_is_better": True, "scaling": "strong" if CONFIGS[args.config].get("strong") else "weak",
+            "vs_baseline": None, "dtype": "f32 (mxfp4 weights)", "data": "synthetic", "impl": "reference",
+            "config": workload_config(args.config, world, ep_mode(args.config)),
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def ep_mode(name):
+    return "counts-first, live rows only" if tokens(name, 1)[0] > 256 else "fixed capacity"
+
+
+# ---------------------------------------------------------------------------
+# the GPU side
+
+class Runner:
+    """One workload on this rank: arena, inputs, the step and the host call."""
+
+    def __init__(self, spt, torch, ctx, name, args, rank, world, local):
+        self.spt, self.torch, self.ctx, self.name = spt, torch, ctx, name
+        self.rank, self.world, self.local = rank, world, local
+        c = CONFIGS[name]
+        self.layers = c.get("layers", 1)
+        self.T, self.T_all = tokens(name, world)
+        cfg = spt.Config(H, D, E, K)
+        params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
+                                 router_bias=c["router_bias"])
+        flags = spt.ARENA_GEMV if args.path == "exact" else spt.ARENA_MMA
+        self.ep = None
+        if world > 1:
+            # expert parallelism: this rank holds experts [r*E/N, (r+1)*E/N)
+            # and the whole router; token rows cross NVLink through the
+            # library's NCCL exchange (the id of its communicator comes from
+            # rank 0)
+            experts = spt.ep_expert_range(E, world, rank)
+            self.arena = ctx.synthetic_arena(cfg, params, n_layers=self.layers, flags=flags, experts=experts)
+            uid = [spt.ep_unique_id() if rank == 0 else None]
+            torch.distributed.broadcast_object_list(uid, src=0)
+            self.ep = spt.ExpertParallel(ctx, uid[0], rank, world)
+            if ep_mode(name) == "fixed capacity":
+                self.ep.set_capacity(self.T)  # no host synchronisation per step
+        else:
+            self.arena = ctx.synthetic_arena(cfg, params, n_layers=self.layers, flags=flags)
+        self.stream = torch.cuda.ExternalStream(ctx.stream)
+        self.x_host = x_rows(name, rank)
+        dev = f"cuda:{local}"
+        self.x_dev = torch.from_numpy(self.x_host).to(dev)
+        self.out_dev = torch.empty_like(self.x_dev)
+        self.flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.x_pin = torch.from_numpy(self.x_host).pin_memory()
+        self.out_pin = torch.empty_like(self.x_pin).pin_memory()
+
+    def step(self):
+        ctx, T = self.ctx, self.T
+        if self.layers > 1:
+            # the stack updates the residual stream in place: every step
+            # starts from the same input rows (a device copy, part of the step)
+            with self.torch.cuda.stream(self.stream):
+                self.out_dev.copy_(self.x_dev)
+            ctx.forward_stack_device(self.arena, self.out_dev.data_ptr(), T, eps=EPS, ep=self.ep)
+        elif self.ep is not None:
+            ctx.forward_moe_batch_ep_device(self.ep, self.arena, self.x_dev.data_ptr(), self.out_dev.data_ptr(), T)
+        else:
+            ctx.forward_moe_batch_device(self.arena, self.x_dev.data_ptr(), self.out_dev.data_ptr(), T)
+
+    def host_call(self):
+        """The caller-facing C-ABI call: host buffers in, host buffers out."""
+        ctx, T = self.ctx, self.T
+        xn, on = self.x_pin.numpy(), self.out_pin.numpy()
+        if self.layers > 1:
+            ctx.forward_stack(self.arena, xn, T, eps=EPS, ep=self.ep, out=on)
+        elif self.ep is not None:
+            ctx.forward_moe_batch_ep(self.ep, self.arena, xn, T, out=on)
+        else:
+            ctx.forward_moe_batch(self.arena, xn, T, out=on)
+
+    def do_flush(self, i):
+        with self.torch.cuda.stream(self.stream):
+            self.flush.fill_(i & 0xFF)
+
+    def barrier(self):
+        if self.world > 1:
+            self.torch.distributed.barrier()
+
+    def max_over_ranks(self, v):
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device=f"cuda:{self.local}", dtype=self.torch.float64)
+        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        self.torch.cuda.synchronize()
+        if self.ep is not None:
+            self.ep.close()
+        self.arena.close()
+
+
+def measure(spt, torch, ctx, name, args, rank, world, local, steps, warmup, clocks=None):
+    """Device throughput, per-kernel times, host-call e2e and parity of one
+    workload.  Returns the fields of its line."""
+    r = Runner(spt, torch, ctx, name, args, rank, world, local)
+    T, T_all, layers = r.T, r.T_all, r.layers
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        r.step()
+    ctx.sync()
+    kernels = ctx.kernels_per_forward()
+    if r.ep is not None:
+        n_active = ctx.last_dispatch()[0]  # this rank's experts used by the rows it received
+        routing = None
+    else:
+        routing = ctx.last_routing(T, E, K)
+        n_active = int((routing["counts"] > 0).sum())
+
+    # ---- device time: inputs resident in HBM --------------------------------
+    # No host synchronisation inside the loop; the 256 MB flush before each
+    # step lets the host enqueue the step's kernels ahead of the GPU.
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    r.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.__enter__()
+    with torch.cuda.stream(r.stream):
+        for i in range(steps):
+            r.flush.fill_(i & 0xFF)
+            starts[i].record(r.stream)
+            r.step()
+            ends[i].record(r.stream)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.__exit__(None, None, None)
+    r.barrier()
+    total_ms = r.max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
+    ms_per_step = total_ms / steps
+    value = T_all * steps / (total_ms / 1e3)
+    device_out = r.out_dev.cpu().numpy()
+
+    # ---- per-kernel durations for the roofline (events around each stage on
+    # the launching stream; a separate pass) ----------------------------------
+    ctx.set_stage_timing(True)
+    stage_ms = []
+    for i in range(steps):
+        r.do_flush(i)
+        r.step()
+        stage_ms.append(ctx.stage_times())
+    ctx.set_stage_timing(False)
+    stages = {k: sum(s[k] for s in stage_ms) / len(stage_ms) for k in stage_ms[0]} if stage_ms else {}
+
+    # ---- e2e: the host call on the host clock --------------------------------
+    for _ in range(max(1, warmup)):
+        r.host_call()
+    e2e_s = 0.0
+    for i in range(steps):
+        r.do_flush(i)
+        torch.cuda.synchronize()
+        r.barrier()
+        t0 = time.perf_counter()
+        r.host_call()
+        e2e_s += time.perf_counter() - t0
+    e2e_s = r.max_over_ranks(e2e_s)
+    host_out = r.out_pin.numpy().copy()
+    same = bool(np.array_equal(host_out.view(np.uint32), device_out.view(np.uint32)) or
+                np.array_equal(np.nan_to_num(host_out), np.nan_to_num(device_out)))
+
+    # ---- roofline of the dominant kernel (gate/up + SwiGLU) ------------------
+    peak_gbs, peak_bf16, peak_src = load_peaks()
+    gu_ms, dn_ms = stages.get("gate_up", float("nan")), stages.get("down", float("nan"))
+    gu_bytes, dn_bytes = n_active * 2 * MATRIX_BYTES, n_active * MATRIX_BYTES
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    step_bytes = layers * (ROUTER_BYTES + 3 * n_active * MATRIX_BYTES)  # n_active of the last layer
+    dispatched = T * K if r.ep is None else ctx.last_dispatch()[1]
+    gu_flops = 2.0 * (2 * D) * H * dispatched
+    path, bn = ctx.last_expert_path()
+    kind = "kind::mxf4, 4 e2m1 activation terms" if bn <= 16 else "kind::mxf8f6f4, 3 e4m3 activation terms"
+    kernel = {"gemv16": "k_gemv16<0> gate/up (e2m1 -> f16 in registers, mma.sync f16 -> f32, fused SwiGLU)",
+              "tcgen05": f"k_mma_gemm<{bn}> gate/up (tcgen05 {kind}, fused SwiGLU)",
+              "exact": "k_gemv gate/up (bit-exact CUDA-core MXFP4 GEMV, fused SwiGLU)"}[path]
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs,
+            "traffic": load_traffic(f"{name}:{path}:gate_up_dram_bytes"), "kernel": kernel,
+            "algorithmic_bytes": gu_bytes, "avg_ms": gu_ms, "peak_source": peak_src,
+            "tflops": gu_flops / (gu_ms / 1e3) / 1e12,
+            "down_kernel": {"achieved": dn_bytes / (dn_ms / 1e3) / 1e9, "avg_ms": dn_ms, "algorithmic_bytes": dn_bytes},
+            "step_hbm_fraction": step_bytes / (ms_per_step / 1e3) / 1e9 / peak_gbs}
+
+    # ---- parity (outside the timed regions) ----------------------------------
+    parity = None
+    if rank == 0 and not args.no_parity:
+        if layers > 1:
+            parity = parity_stack(name, r, device_out) if r.ep is None else None
+        else:
+            parity = parity_block(name, r.x_host, T, device_out, routing)
+    r.close()
+    return {"value": value, "unit": "tokens/s", "ms_per_step": ms_per_step, "tokens_per_step": T_all,
+            "expert_path": path, "active_experts": n_active, "kernels_per_step": kernels,
+            "gpu_launches": steps * kernels, "stages_ms": {k: round(v, 5) for k, v in stages.items()},
+            "roofline": roof,
+            "e2e": {"value": T_all * steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4, "ms_per_step": 1e3 * e2e_s / steps,
+                    "clock": "host (perf_counter) around the C-ABI call, after a synchronised L2 flush",
+                    "matches_device_path": same},
+            "parity": parity}
+
+
+DTYPES = {"gemv16": "mxfp4 weights (f16 in registers) x 2-term f16 activations -> f32 (mma.sync)",
+          "tcgen05": "mxfp4 weights x block-scaled activation terms -> f32 (tcgen05)",
+          "exact": "f32 (mxfp4 weights), the reference's AVX2 order"}
 
 
 def run_ours(args):
@@ -266,189 +640,37 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
     spt = importlib.import_module("stream-pt_b200")
-    c = CONFIGS[args.config]
-    T = c["T"]
-    cfg = spt.Config(H, D, E, K)
-    params = spt.SynthParams(seed=c["seed"], zipf_s=c["zipf_s"], zipf_beta=c["zipf_beta"],
-                             router_bias=c["router_bias"])
     ctx = spt.Context(local)
-    flags = spt.ARENA_GEMV if args.path == "exact" else spt.ARENA_MMA
-    layers = c.get("layers", 1)
-    ep = None
-    if world > 1:
-        # expert parallelism: this rank holds experts [r*E/N, (r+1)*E/N) and
-        # the whole router; token rows cross NVLink through the library's NCCL
-        # exchange (the id of its communicator comes from rank 0)
-        experts = spt.ep_expert_range(E, world, rank)
-        arena = ctx.synthetic_arena(cfg, params, n_layers=layers, flags=flags, experts=experts)
-        uid = [spt.ep_unique_id() if rank == 0 else None]
-        torch.distributed.broadcast_object_list(uid, src=0)
-        ep = spt.ExpertParallel(ctx, uid[0], rank, world)
-        ep.set_capacity(T)  # fixed-capacity exchange: no host synchronisation per step
-    else:
-        arena = ctx.synthetic_arena(cfg, params, n_layers=layers, flags=flags)
-    ctx.set_path({"mma": spt.PATH_MMA, "exact": spt.PATH_EXACT, "auto": spt.PATH_AUTO, "gemv16": spt.PATH_GEMV16}[args.path])
-    stream = torch.cuda.ExternalStream(ctx.stream)
-    x_host = spt.synth_normal_host(c["seed"] + 7919 * rank, 1000, T * H)
-    x_dev = torch.from_numpy(x_host).to(f"cuda:{local}")
-    out_dev = torch.empty_like(x_dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
-
-    def step():
-        if layers > 1:
-            # the stack updates the residual stream in place: every step starts
-            # from the same input rows (a 737 KB device copy, part of the step)
-            with torch.cuda.stream(stream):
-                out_dev.copy_(x_dev)
-            ctx.forward_stack_device(arena, out_dev.data_ptr(), T, eps=EPS, ep=ep)
-        elif ep is not None:
-            ctx.forward_moe_batch_ep_device(ep, arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
-        else:
-            ctx.forward_moe_batch_device(arena, x_dev.data_ptr(), out_dev.data_ptr(), T)
-
-    def host_call(xn, on):
-        if layers > 1:
-            ctx.forward_stack(arena, xn, T, eps=EPS, ep=ep, out=on)
-        elif ep is not None:
-            ctx.forward_moe_batch_ep(ep, arena, xn, T, out=on)
-        else:
-            ctx.forward_moe_batch(arena, xn, T, out=on)
-
-    torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        step()
-    ctx.sync()
-    if ep is not None:
-        n_active = ctx.last_dispatch()[0]  # this rank's experts used by the rows it received
-    else:
-        routing = ctx.last_routing(T, E, K)
-        n_active = int((routing["counts"] > 0).sum())
-
-    # ---- timed region: device-resident inputs ------------------------------
-    # No host synchronisation inside the loop; the 256 MB L2 flush before each
-    # step also lets the host enqueue the step's kernels ahead of the GPU.
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                flush.fill_(i & 0xFF)
-                starts[i].record(stream)
-                step()
-                ends[i].record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    if world > 1:
-        t = torch.tensor([total_ms], device=f"cuda:{local}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms = float(t.item())
-    ms_per_step = total_ms / args.steps
-    value = world * T * args.steps / (total_ms / 1e3)
-    kernels_per_step = ctx.kernels_per_forward()
-    # one launch per step: the single-launch decode kernel is the whole block
-    decode_kernel = kernels_per_step == 1 and layers == 1 and ep is None
-
-    # ---- per-kernel durations (same workload, CUDA events around each stage
-    # on the launching stream; per-stage timing runs the separate kernels)
-    # for the roofline ------------------------------------------------------
-    ctx.set_stage_timing(True)
-    stage_ms = []
-    for i in range(args.steps):
-        with torch.cuda.stream(stream):
-            flush.fill_(i & 0xFF)
-        step()
-        stage_ms.append(ctx.stage_times())
-    ctx.set_stage_timing(False)
-
-    # ---- e2e through the C ABI with pinned host buffers --------------------
-    x_pin = torch.from_numpy(x_host).pin_memory()
-    out_pin = torch.empty_like(x_pin).pin_memory()
-    xn, on = x_pin.numpy(), out_pin.numpy()
-    for _ in range(max(1, args.warmup)):
-        host_call(xn, on)
-    e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        torch.distributed.barrier()
-    for i in range(args.steps):
-        with torch.cuda.stream(stream):
-            flush.fill_(i & 0xFF)
-        e_st[i].record(stream)
-        host_call(xn, on)
-        e_en[i].record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_st, e_en))
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=f"cuda:{local}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
-    ok = bool(np.array_equal(on.view(np.uint32), out_dev.cpu().numpy().view(np.uint32)) or
-              np.array_equal(np.nan_to_num(on), np.nan_to_num(out_dev.cpu().numpy())))
-
-    # ---- roofline of the dominant kernel (gate/up GEMV + SwiGLU) -----------
-    peak, peak_src = load_peaks()
-    gu = [s["gate_up"] for s in stage_ms if s]
-    dn = [s["down"] for s in stage_ms if s]
-    gu_ms = sum(gu) / len(gu) if gu else float("nan")
-    dn_ms = sum(dn) / len(dn) if dn else float("nan")
-    gu_bytes = n_active * 2 * MATRIX_BYTES
-    dn_bytes = n_active * MATRIX_BYTES
-    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
-    stages_avg = {k: round(sum(s[k] for s in stage_ms) / len(stage_ms), 5) for k in stage_ms[0]} if stage_ms else {}
-    step_bytes = layers * (ROUTER_BYTES + 3 * n_active * MATRIX_BYTES)  # n_active of the last layer
-    line = {
-        "metric": "moe_block_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": mma_dtype(T) if args.path == "mma" else "f32 (mxfp4 weights)",
-        "data": "synthetic",
-        "config": {"workload": f"{args.config}: {c['desc']}", "tokens_per_step": T, "hidden": H, "layers": layers,
-                   "expert_path": args.path,
-                   "expert_dim": D, "experts": E, "top_k": K, "seed": c["seed"],
-                   "parallelism": (f"ep{world}: {E // world} experts per GPU, {T} tokens per rank, NCCL "
-                                   "all-to-all dispatch/combine (fixed capacity)" if world > 1 else "single GPU"),
-                   "l2": "256 MB buffer written between timed steps",
-                   "active_experts": n_active},
-        "roofline": ({"bound": "hbm", "achieved": step_bytes / (ms_per_step / 1e3) / 1e9, "peak": peak,
-                      "unit": "GB/s", "frac": step_bytes / (ms_per_step / 1e3) / 1e9 / peak,
-                      "traffic": load_traffic(args.config, "decode_dram_bytes"),
-                      "kernel": "k_moe_decode (whole block in one cooperative launch, tcgen05 kind::mxf4)",
-                      "algorithmic_bytes": step_bytes, "avg_ms": ms_per_step, "peak_source": peak_src,
-                      "separate_kernels": {"gate_up_achieved": achieved, "gate_up_ms": gu_ms,
-                                           "down_ms": dn_ms}}
-                     if decode_kernel else
-                     {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                      "frac": achieved / peak, "traffic": load_traffic(args.config),
-                      "kernel": (f"k_mma_gemm gate/up (tcgen05 {mma_kind(T)}, fused SwiGLU)" if args.path == "mma"
-                                 else "k_gemv<gate_up> (fused gate+up MXFP4 GEMV + SwiGLU)"),
-                      "algorithmic_bytes": gu_bytes, "avg_ms": gu_ms, "peak_source": peak_src,
-                      "down_kernel": {"achieved": dn_bytes / (dn_ms / 1e3) / 1e9, "avg_ms": dn_ms,
-                                      "algorithmic_bytes": dn_bytes},
-                      "step_hbm_fraction": step_bytes / (ms_per_step / 1e3) / 1e9 / peak}),
-        "stages_ms": stages_avg,
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 4,
-                "d2h_bytes_per_step": T * H * 4, "ms_per_step": e2e_ms / args.steps,
-                "matches_device_path": ok},
-        "gpu_launches": args.steps * kernels_per_step,
-    }
+    ctx.set_path({"mma": spt.PATH_MMA, "exact": spt.PATH_EXACT, "auto": spt.PATH_AUTO,
+                  "gemv16": spt.PATH_GEMV16}[args.path])
+    clocks = ClockSampler(local)
+    main = measure(spt, torch, ctx, args.config, args, rank, world, local, args.steps, args.warmup, clocks)
+    extras = {}
+    if not args.no_extras:
+        names = ["c0", "c2", "c3", "c4"] if world == 1 else ["c3", "c4"]
+        for n in names:
+            if n == args.config:
+                continue
+            extras[n] = measure(spt, torch, ctx, n, args, rank, world, local, min(args.steps, 10),
+                                max(3, min(args.warmup, 5)))
+            extras[n]["workload"] = workload_config(n, world, ep_mode(n))["workload"]
+            extras[n]["scaling"] = "strong" if CONFIGS[n].get("strong") else "weak"
+    line = {"metric": "moe_block_tokens_per_s", "value": main["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": main["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong" if CONFIGS[args.config].get("strong") else "weak",
+            "vs_baseline": None, "dtype": DTYPES[main["expert_path"]], "data": "synthetic",
+            "config": workload_config(args.config, world, ep_mode(args.config)),
+            "expert_path": main["expert_path"], "active_experts": main["active_experts"],
+            "roofline": main["roofline"], "stages_ms": main["stages_ms"], "e2e": main["e2e"],
+            "parity": main["parity"], "gpu_launches": main["gpu_launches"]}
+    if extras:
+        line["configs"] = extras
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tps, cores, sample = cpu_baseline(args.config)
-        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-                                "sample": sample}
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         line["clocks"] = clocks.summary()
         print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.barrier()
-    if ep is not None:
-        ep.close()
-    arena.close()
     ctx.close()
     if world > 1:
         torch.distributed.barrier()
@@ -506,7 +728,7 @@ def run_q80(args):
         if i >= args.warmup:
             e_ms.append(st.elapsed_time(en))
     e2e_ms = sum(e_ms) / len(e_ms)
-    peak, peak_src = load_peaks()
+    peak, _, peak_src = load_peaks()
     nbytes = Q80_ROWS * nb * 34
     line = {"metric": "lm_head_tokens_per_s", "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -543,9 +765,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["q80"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="auto", choices=["auto", "mma", "gemv16", "exact"],
-                    help="expert GEMMs on tcgen05 (mma) or the bit-exact CUDA-core GEMV (exact)")
+                    help="expert products: the library's choice (auto), tcgen05 (mma), the decode GEMV "
+                         "(gemv16) or the bit-exact CUDA-core GEMV (exact)")
+    ap.add_argument("--no-extras", action="store_true", help="only the --config workload")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "q80":

@@ -240,9 +240,13 @@ spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int6
  * intermediates in one static device array of about 2.2 MB, held by every GPU
  * that loads the library.  Limits: batch x top-k <= 64, hidden and expert
  * dimensions <= 4096, experts <= 256 (SPT_ERR_UNSUPPORTED otherwise); needs an
- * SPT_ARENA_GEMV arena.  The first call on a device looks up the array's
- * device address (make it before any stream capture).  All calls share the
- * array: calls that overlap on the GPU race and must be serialised. */
+ * SPT_ARENA_GEMV arena.  spt_context_create looks up the array's device
+ * address, which loads the library's device code and the array on that
+ * device: create the context before reserving the rest of HBM (and before
+ * any stream capture).  All calls share the array: calls that overlap on the
+ * GPU race and must be serialised.  The call's routing stays in the array, so
+ * spt_last_routing and spt_stage_times refuse after it (until the next
+ * allocating forward). */
 spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_arena *arena, int64_t layer,
                                                const float *x, float *out, int64_t batch);
 
@@ -254,9 +258,11 @@ spt_status spt_forward_moe_batch_reader(spt_context *ctx, const spt_reader *read
                                         int64_t x_len, float *out, int64_t out_len,
                                         int64_t batch, const volatile int32_t *cancel);
 
-/* Intermediates of the last spt_forward_moe_batch* call (host copies, for
- * parity tests): logits [batch*E], selected index/weight [batch*k],
- * dispatch permutation perm [dispatched] and per-expert counts [E].
+/* Intermediates of the last single-GPU spt_forward_moe_batch* call (host
+ * copies, for parity tests): logits [batch*E], selected index/weight
+ * [batch*k], dispatch permutation perm [dispatched] and per-expert counts [E].
+ * Refused (SPT_ERR_DIMENSIONS) after an allocation-free or expert-parallel
+ * call, whose intermediates live elsewhere.
  * Any pointer may be NULL.  *dispatched receives the dispatched slot count. */
 spt_status spt_last_routing(spt_context *ctx, float *logits, int32_t *sel_index,
                             float *sel_weight, int32_t *perm, int32_t *expert_count,
@@ -275,6 +281,11 @@ spt_status spt_set_stage_timing(spt_context *ctx, int enable);
 int spt_stage_times(spt_context *ctx, float *ms, int n);
 /* Number of kernels the last forward call launched. */
 int spt_kernels_per_forward(spt_context *ctx);
+/* Expert path the last forward call took: SPT_PATH_EXACT, SPT_PATH_MMA or
+ * SPT_PATH_GEMV16; *tile_tokens (may be NULL) gets the tcgen05 token-tile
+ * width (8, 16 or 128; 0 on the other paths).  Instrumentation, no
+ * counterpart in the reference. */
+int spt_last_expert_path(spt_context *ctx, int *tile_tokens);
 
 /* ---- stage entry points (host pointers, synchronous) -------------------- */
 

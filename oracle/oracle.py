@@ -93,6 +93,8 @@ def lib():
         L.spo_synth_layer.restype = i32
         L.spo_synth_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint32, f32, f32, vp, i64]
         L.spo_synth_normal.restype = None
+        L.spo_synth_experts.argtypes = [ctypes.POINTER(SynthParams), i64, i64, i64, i64, vp, i64, vp, vp, vp, i32]
+        L.spo_synth_experts.restype = i32
         L.spo_synth_norm.argtypes = [ctypes.c_uint64, i64, i64, vp]
         L.spo_synth_norm.restype = None
         L.spo_fmaf_vec.argtypes = [vp, vp, vp, vp, i64]; L.spo_fmaf_vec.restype = None
@@ -254,6 +256,56 @@ def synth_layer(hidden, expert_dim, experts, params: SynthParams, layer=0, threa
     if r != 0:
         raise ValueError("invalid synthetic layer dimensions")
     return out
+
+
+def synth_layer_experts(hidden, expert_dim, experts, params: SynthParams, layer, ids, threads=None) -> dict:
+    """A synthetic layer whose expert tensors hold only the experts `ids`
+    (the others stay zero; the forward reads only the selected experts):
+    for checking a few tokens of a deep stack without generating 1.7 GB per
+    layer.  Router and biases are complete."""
+    H, D, E = hidden, expert_dim, experts
+    out = dict(router=np.empty(E * H * 4, np.uint8), router_bias=np.empty(E, np.float32),
+               gate=np.zeros(E * D * (H // 32) * 17, np.uint8), up=np.zeros(E * D * (H // 32) * 17, np.uint8),
+               down=np.zeros(E * H * (D // 32) * 17, np.uint8), gate_bias=np.empty(E * D, np.float32),
+               up_bias=np.empty(E * D, np.float32), down_bias=np.empty(E * H, np.float32))
+    o = out
+    r = lib().spo_synth_layer(ctypes.byref(params), H, D, E, layer, _p(o["router"]), _p(o["router_bias"]), None,
+                              None, None, _p(o["gate_bias"]), _p(o["up_bias"]), _p(o["down_bias"]), 1)
+    ids = np.ascontiguousarray(sorted(set(int(i) for i in ids)), dtype=np.int32)
+    if r == 0 and ids.size:
+        r = lib().spo_synth_experts(ctypes.byref(params), H, D, E, layer, _p(ids), ids.size, _p(o["gate"]),
+                                    _p(o["up"]), _p(o["down"]), threads or os.cpu_count() or 1)
+    if r != 0:
+        raise ValueError("invalid synthetic layer dimensions")
+    return out
+
+
+def weights_of(layer: dict, hidden, expert_dim, experts, top_k) -> "Weights":
+    return Weights(hidden, expert_dim, experts, top_k, layer["router"], layer["router_bias"], layer["gate"],
+                   layer["up"], layer["down"], layer["gate_bias"], layer["up_bias"], layer["down_bias"])
+
+
+def route_threads(router_bytes, x, bias, batch, hidden, experts, threads=None) -> np.ndarray:
+    """route() over token chunks on several threads (same values)."""
+    from concurrent.futures import ThreadPoolExecutor
+    x = _f32(x).reshape(batch, hidden)
+    n = max(1, min(threads or os.cpu_count() or 1, batch))
+    chunks = [(i * batch // n, (i + 1) * batch // n) for i in range(n)]
+    with ThreadPoolExecutor(n) as ex:
+        parts = list(ex.map(lambda c: route(router_bytes, x[c[0]:c[1]], bias, c[1] - c[0], hidden, experts), chunks))
+    return np.concatenate(parts, axis=0)
+
+
+def dispatch_perm(sel_idx, sel_w, experts) -> tuple:
+    """The reference's dispatch order (moe_batch.go:142-159): slots whose
+    weight is > 0 or NaN, grouped by expert ascending, each expert's slots in
+    descending slot order.  Returns (perm, per-expert counts)."""
+    idx = np.asarray(sel_idx).ravel()
+    w = np.asarray(sel_w, np.float32).ravel()
+    live = ~(w <= 0)
+    slots = np.nonzero(live)[0]
+    order = np.lexsort((-slots, idx[slots]))
+    return slots[order].astype(np.int32), np.bincount(idx[slots], minlength=experts).astype(np.int32)
 
 
 def synth_weights(hidden, expert_dim, experts, top_k, params: SynthParams, layer=0, threads=None) -> Weights:

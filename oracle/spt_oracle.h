@@ -155,6 +155,11 @@ int spo_synth_layer(const spo_synth_params *p, int64_t hidden, int64_t expert_di
                     int64_t layer, uint8_t *router, float *router_bias, uint8_t *gate, uint8_t *up,
                     uint8_t *down, float *gate_bias, float *up_bias, float *down_bias, int threads);
 void spo_synth_router_bias(const spo_synth_params *p, int64_t experts, int64_t layer, float *bias);
+/* The MXFP4 blocks of experts ids[0..n_ids) only, written at their places in
+ * whole-tensor buffers (gate/up E*D*(H/32)*17 bytes, down E*H*(D/32)*17;
+ * any may be NULL); the rest is left untouched.  Returns 0 or -1. */
+int spo_synth_experts(const spo_synth_params *p, int64_t hidden, int64_t expert_dim, int64_t experts, int64_t layer,
+                      const int32_t *ids, int64_t n_ids, uint8_t *gate, uint8_t *up, uint8_t *down, int threads);
 /* n Gaussians N(mean, sd) of tensor tag `tag` (activations: tag = stream). */
 void spo_synth_normal(uint64_t seed, uint32_t tag, float mean, float sd, float *out, int64_t n);
 /* RMSNorm weights N(1, 0.02) of a synthetic layer. */

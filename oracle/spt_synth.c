@@ -183,6 +183,48 @@ int spo_synth_layer(const spo_synth_params *p, int64_t hidden, int64_t expert_di
   return 0;
 }
 
+int spo_synth_experts(const spo_synth_params *p, int64_t hidden, int64_t expert_dim, int64_t experts, int64_t layer,
+                      const int32_t *ids, int64_t n_ids, uint8_t *gate, uint8_t *up, uint8_t *down, int threads) {
+  const int64_t H = hidden, D = expert_dim, E = experts;
+  if (!p || H <= 0 || D <= 0 || E <= 0 || H % 32 != 0 || D % 32 != 0) return -1;
+  const int64_t gu = D * (H / 32), dn = H * (D / 32);  // blocks per expert
+  for (int64_t i = 0; i < n_ids; ++i) {
+    const int64_t e = ids[i];
+    if (e < 0 || e >= E) return -1;
+    /* block b of expert e is block e * per + b of the tensor: same bytes as the whole-tensor generator */
+    struct {
+      uint32_t kind;
+      int64_t per;
+      uint8_t *dst;
+    } mats[3] = {{kGate, gu, gate}, {kUp, gu, up}, {kDown, dn, down}};
+    for (int m = 0; m < 3; ++m) {
+      if (!mats[m].dst) continue;
+      blocks_job j = {p->seed, tag_of(layer, mats[m].kind), p->scale_lo, p->scale_hi, mats[m].dst,
+                      e * mats[m].per, (e + 1) * mats[m].per};
+      if (threads > 1) {
+        /* split this expert's blocks over threads */
+        const int64_t n = mats[m].per;
+        pthread_t tid[64];
+        int made[64];
+        blocks_job job[64];
+        int th = threads > 64 ? 64 : threads;
+        for (int t = 0; t < th; ++t) {
+          job[t] = j;
+          job[t].begin = e * n + n * t / th;
+          job[t].end = e * n + n * (t + 1) / th;
+          made[t] = pthread_create(&tid[t], NULL, blocks_run, &job[t]) == 0;
+          if (!made[t]) blocks_run(&job[t]);
+        }
+        for (int t = 0; t < th; ++t)
+          if (made[t]) pthread_join(tid[t], NULL);
+      } else {
+        blocks_run(&j);
+      }
+    }
+  }
+  return 0;
+}
+
 void spo_synth_norm(uint64_t seed, int64_t layer, int64_t dim, float *out) {
   spo_synth_normal(seed, tag_of(layer, kNormWeight), 1.0f, 0.02f, out, dim);
 }

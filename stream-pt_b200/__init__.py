@@ -243,6 +243,7 @@ def lib():
         "spt_kernels_per_forward": ([vp], ctypes.c_int),
         "spt_context_set_path": ([vp, ctypes.c_int], st),
         "spt_context_set_option": ([vp, ctypes.c_int, i64], st),
+        "spt_last_expert_path": ([vp, P(ctypes.c_int)], ctypes.c_int),
         "spt_context_get_option": ([vp, ctypes.c_int], i64),
     }
     for name, (args, res) in sigs.items():
@@ -326,6 +327,12 @@ class Context:
         """PATH_EXACT (CUDA-core, bit-exact), PATH_MMA (tcgen05), PATH_GEMV16
         (decode GEMV on the packed planes) or PATH_AUTO."""
         self.check(lib().spt_context_set_path(self._h, path))
+
+    def last_expert_path(self) -> Tuple[str, int]:
+        """("exact" | "tcgen05" | "gemv16", tcgen05 token-tile width) of the last forward."""
+        bn = ctypes.c_int()
+        p = int(lib().spt_last_expert_path(self._h, ctypes.byref(bn)))
+        return {PATH_EXACT: "exact", PATH_MMA: "tcgen05", PATH_GEMV16: "gemv16"}.get(p, "exact"), bn.value
 
     def set_option(self, option: int, value: int):
         """spt_context_set_option (OPT_* constants)."""

@@ -84,6 +84,9 @@ struct spt_context {
   int opt_gemv16_slots = 16;    // SPT_PATH_AUTO: decode GEMV while batch x top-k <= this
   int opt_wait_shift = 31;      // bounded device waits give up after 2^shift clock cycles
   int opt_fault_stage = -1;     // failure injection: the tcgen05 producer skips this stage (tests)
+  int last_path = SPT_PATH_EXACT;  // expert path of the last forward (SPT_PATH_EXACT / _MMA / _GEMV16)
+  bool timed_last = false;         // the last forward recorded stage events
+  int last_bn = 0;                 // its tcgen05 token-tile width
   // activation tensor maps of the last call (re-encoded when the buffers or shape change)
   struct ActMaps {
     const void *q = nullptr;
@@ -115,6 +118,10 @@ struct spt_arena {
 namespace {
 
 constexpr float kSynthNormStd = 0.02f;  // RMSNorm weights ~ N(1, 0.02)
+
+// Device address of the allocation-free entry point's static scratch on
+// ctx's device (defined with that entry point below).
+spt_status static_scratch(spt_context *ctx, unsigned char **out);
 
 spt_status fail(spt_context *ctx, spt_status st, const char *fmt, ...) {
   char buf[512];
@@ -705,10 +712,13 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   if ((st = pick_path(ctx, L, c, T, &path))) return st;
   if ((st = reserve_experts(ctx, L, c, T, bn_hint))) return st;
   const bool use_mma = path == kPathTcgen05;
+  ctx->last_path = path == kPathGemv16 ? SPT_PATH_GEMV16 : use_mma ? SPT_PATH_MMA : SPT_PATH_EXACT;
+  ctx->last_bn = 0;
   DispatchPlan plan;  // tensor-core tile layout, made by the dispatch kernel
   if (path == kPathGemv16) plan.act_off = ctx->act_off.as<int32_t>();
   if (use_mma) {
     plan.bn = bn_hint ? bn_hint : pick_bn(ctx, T, K, E);
+    ctx->last_bn = plan.bn;
     plan.mt_gu = L.gu_mma.mtiles;
     plan.mt_dn = L.dn_mma.mtiles;
     plan.pad_off = ctx->pad_off.as<int32_t>();
@@ -865,6 +875,7 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
   if ((st = ensure_scratch(ctx, T, c))) return st;
   const LayerDev &L = arena->layers[(size_t)layer];
   const bool fuse = T <= kSelectDispatchMaxTokens && ctx->opt_fused_select;
+  ctx->timed_last = ctx->timing;
   // the decode GEMV's split operand comes out of the router when it can
   ExpertPath path;
   if ((st = pick_path(ctx, L, c, T, &path))) return st;
@@ -1019,6 +1030,18 @@ spt_status spt_context_create(int device, spt_context **out) {
     ctx->device = device;
     ctx->has_device = true;
     ctx->stream = ctx->own_stream;
+    // Resolve the static scratch of spt_forward_moe_batch_device_static now:
+    // it loads this library's device code on the device (CUDA loads modules
+    // lazily) and with it the array, so a caller that creates its context
+    // before reserving the rest of HBM has that memory in place from the start.
+    unsigned char *scratch = nullptr;
+    spt_status sst = static_scratch(ctx, &scratch);
+    if (sst != SPT_OK) {
+      const std::string why = ctx->err;
+      cudaStreamDestroy(ctx->own_stream);
+      delete ctx;
+      return fail(nullptr, sst, "%s", why.c_str());
+    }
   }
   *out = ctx;
   return SPT_OK;
@@ -1054,7 +1077,7 @@ spt_status spt_set_stage_timing(spt_context *ctx, int enable) {
 }
 
 int spt_stage_times(spt_context *ctx, float *ms, int n) {
-  if (!ctx || !ctx->timing || !ms) return 0;
+  if (!ctx || !ctx->timing || !ctx->timed_last || !ms) return 0;
   if (cudaEventSynchronize(ctx->ev[SPT_NUM_STAGES]) != cudaSuccess) return 0;
   int w = 0;
   for (int i = 0; i < SPT_NUM_STAGES && i < n; ++i, ++w)
@@ -1063,6 +1086,11 @@ int spt_stage_times(spt_context *ctx, float *ms, int n) {
 }
 
 int spt_kernels_per_forward(spt_context *ctx) { return ctx ? ctx->kernels_last : 0; }
+
+int spt_last_expert_path(spt_context *ctx, int *tile_tokens) {
+  if (tile_tokens) *tile_tokens = ctx ? ctx->last_bn : 0;
+  return ctx ? ctx->last_path : -1;
+}
 
 const char *spt_last_error(const spt_context *ctx) {
   return ctx ? ctx->err.c_str() : g_tls_error.c_str();
@@ -1958,6 +1986,14 @@ extern "C" spt_status spt_forward_moe_batch_device_static(spt_context *ctx, spt_
   dn.mt = mt;
   SPT_CUDA(ctx, launch_gemv(dn, ctx->sm_count, s));
   SPT_CUDA(ctx, launch_combine(res, sel_w, slot_pos, T, (int)K, (int)H, out, s));
+  // This call's routing lives in the static array, not in the context's
+  // buffers, and it records no stage events: spt_last_routing and
+  // spt_stage_times refuse until the next allocating forward.
+  ctx->have_routing = false;
+  ctx->timed_last = false;
+  ctx->kernels_last = 6;  // router, select, dispatch, gate/up, down, combine
+  ctx->last_path = SPT_PATH_EXACT;
+  ctx->last_bn = 0;
   return SPT_OK;
 }
 
@@ -2248,6 +2284,8 @@ spt_status forward_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int
   if (H % 4 != 0) return fail(ctx, SPT_ERR_UNSUPPORTED, "hidden size %lld not a multiple of 4", (long long)H);
   cudaStream_t s = ctx->stream;
   const LayerDev &L = arena->layers[(size_t)layer];
+  ctx->timed_last = ctx->timing;
+  ctx->have_routing = false;  // the context's dispatch buffers describe the rows this rank received
   const int64_t S = T * K;
   if (ep->cap_tokens > 0) {
     if (T > ep->cap_tokens)

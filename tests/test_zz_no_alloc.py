@@ -43,6 +43,11 @@ def test_static_scratch_matches_allocating_entry_point():
             g, w = got.cpu().numpy(), want.cpu().numpy()
             assert np.isfinite(w).all(), call
             assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), call
+            # the static call's routing stays in the static array: the
+            # context's routing record refuses rather than report the
+            # previous allocating call
+            with pytest.raises(spt.SptError):
+                ctx.last_routing(T, 128, 4)
         # sizes beyond the static array are refused before any device work
         x = torch.zeros(17 * 2880, device="cuda")
         with pytest.raises(spt.SptError) as e:
