@@ -133,6 +133,23 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers,
                             const spt_moe_config *cfg, const spt_layer_weights *layers,
                             int64_t n_layers, uint32_t flags, spt_arena **out);
 
+/* The same from per-tensor views, for readers that hand out each tensor's
+ * bytes separately (ggufmap.Reader.WithTensor, ggufmap/mmap_linux.go:210:
+ * a read-only slice valid inside its callback): data->X points at the first
+ * byte of tensor layers->X ([start, end) of its file), NULL for an absent
+ * optional tensor.  The views need to stay valid only for the duration of
+ * the call; the library keeps nothing of them.  expert_end 0: every expert. */
+typedef struct spt_layer_data {
+  const uint8_t *ffn_gate_inp, *ffn_gate_inp_bias;
+  const uint8_t *ffn_gate_exps, *ffn_gate_exps_bias;
+  const uint8_t *ffn_up_exps, *ffn_up_exps_bias;
+  const uint8_t *ffn_down_exps, *ffn_down_exps_bias;
+  const uint8_t *post_attention_norm;
+} spt_layer_data;
+spt_status spt_arena_create_views(spt_context *ctx, const spt_moe_config *cfg, const spt_layer_weights *layers,
+                                  const spt_layer_data *data, int64_t n_layers, uint32_t flags, int64_t expert_begin,
+                                  int64_t expert_end, spt_arena **out);
+
 /* Seeded synthetic GPT-OSS-style weights generated on the device
  * (counter-based Philox4x32-10; identical bytes from
  * spt_synth_layer_host).  Not a reference interface: benchmark input. */

@@ -68,6 +68,10 @@ class _LayerWeights(ctypes.Structure):
         "ffn_up_exps", "ffn_up_exps_bias", "ffn_down_exps", "ffn_down_exps_bias", "post_attention_norm")]
 
 
+class _LayerData(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n, _ in _LayerWeights._fields_]
+
+
 class _SynthParams(ctypes.Structure):
     _fields_ = [("seed", ctypes.c_uint64), ("router_std", ctypes.c_float),
                 ("bias_std", ctypes.c_float), ("scale_lo", ctypes.c_uint8),
@@ -244,6 +248,7 @@ def lib():
         "spt_context_set_path": ([vp, ctypes.c_int], st),
         "spt_context_set_option": ([vp, ctypes.c_int, i64], st),
         "spt_last_expert_path": ([vp, P(ctypes.c_int)], ctypes.c_int),
+        "spt_arena_create_views": ([vp, P(_Config), vp, vp, i64, ctypes.c_uint32, i64, i64, P(vp)], st),
         "spt_context_get_option": ([vp, ctypes.c_int], i64),
     }
     for name, (args, res) in sigs.items():
@@ -356,6 +361,28 @@ class Context:
         h = ctypes.c_void_p()
         self.check(lib().spt_arena_create(self._h, rs, ctypes.byref(c), ls, n, flags, ctypes.byref(h)))
         return Arena(self, h, cfg, n, keep=(readers,))
+
+    def arena_views(self, readers: Sequence[Reader], cfg: Config, layers: Sequence[LayerWeights],
+                    flags: int = ARENA_GEMV) -> "Arena":
+        """spt_arena_create_views: every tensor handed over as its own buffer
+        (a copy of its [start, end) bytes here), as a reader that maps tensors
+        one by one (ggufmap's WithTensor) would."""
+        n = len(layers)
+        ls = (_LayerWeights * n)(*[l._c() for l in layers])
+        ds = (_LayerData * n)()
+        keep = []
+        for i, (r, lw) in enumerate(zip(readers, layers)):
+            raw = r.buf
+            for name, _ in _LayerWeights._fields_:
+                t = getattr(lw, name)
+                if t.name:
+                    buf = np.array(raw[t.start:t.end], copy=True)
+                    keep.append(buf)
+                    setattr(ds[i], name, buf.ctypes.data)
+        c = cfg._c()
+        h = ctypes.c_void_p()
+        self.check(lib().spt_arena_create_views(self._h, ctypes.byref(c), ls, ds, n, flags, 0, 0, ctypes.byref(h)))
+        return Arena(self, h, cfg, n)
 
     def synthetic_arena(self, cfg: Config, params: SynthParams, n_layers: int = 1,
                         flags: int = ARENA_GEMV, experts: Optional[Tuple[int, int]] = None) -> "Arena":

@@ -77,6 +77,8 @@ struct spt_context {
   DevBuf xq, xe, actq, act_off;  // decode GEMV: split x rows, their exponents, split SwiGLU rows,
                                  // first dispatch position of each active expert
   int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
+  void *hx = nullptr, *hout = nullptr;  // pinned staging of pageable caller x / out (host entry points)
+  size_t hx_bytes = 0, hout_bytes = 0;
   // tuning options (spt_context_set_option), seeded from the environment once
   int opt_tile_tokens = 0;      // tcgen05 token-tile width (0: from the batch)
   int opt_fused_select = 1;     // top-k inside the dispatch kernel for T <= kSelectDispatchMaxTokens
@@ -914,6 +916,26 @@ spt_status check_batch(spt_context *ctx, const spt_moe_config &c, const float *x
   return SPT_OK;
 }
 
+// Whether host memory p is page-locked (copies from it can be asynchronous).
+bool host_pinned(const void *p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
+spt_status ensure_pinned(spt_context *ctx, void **buf, size_t *have, size_t want) {
+  if (*have >= want) return SPT_OK;
+  if (*buf) cudaFreeHost(*buf);
+  *buf = nullptr;
+  *have = 0;
+  SPT_CUDA(ctx, cudaHostAlloc(buf, want, cudaHostAllocDefault));
+  *have = want;
+  return SPT_OK;
+}
+
 spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
                         int64_t x_len, float *out, int64_t out_len, int64_t batch,
                         const volatile int32_t *cancel) {
@@ -927,12 +949,22 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
   const size_t bytes = sizeof(float) * (size_t)x_len;
   SPT_CUDA(ctx, ctx->xdev.ensure(bytes));
   SPT_CUDA(ctx, ctx->outdev.ensure(bytes));
-  SPT_CUDA(ctx, cudaMemcpyAsync(ctx->xdev.p, x, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  // Pageable caller memory (a Go slice) goes through the context's pinned
+  // buffers, so both copies are asynchronous and the call synchronises once.
+  const bool x_pinned = host_pinned(x), out_pinned = host_pinned(out);
+  const float *xsrc = x;
+  if (!x_pinned) {
+    if ((st = ensure_pinned(ctx, &ctx->hx, &ctx->hx_bytes, bytes))) return st;
+    memcpy(ctx->hx, x, bytes);
+    xsrc = static_cast<const float *>(ctx->hx);
+  }
+  if (!out_pinned && (st = ensure_pinned(ctx, &ctx->hout, &ctx->hout_bytes, bytes))) return st;
+  SPT_CUDA(ctx, cudaMemcpyAsync(ctx->xdev.p, xsrc, bytes, cudaMemcpyHostToDevice, ctx->stream));
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
   if ((st = forward_device(ctx, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch)))
     return st;
-  SPT_CUDA(ctx, cudaMemcpyAsync(out, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
-  // The GEMM's error flag rides on the same stream, so one synchronisation
+  SPT_CUDA(ctx, cudaMemcpyAsync(out_pinned ? (void *)out : ctx->hout, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost,
+                                ctx->stream));  // The GEMM's error flag rides on the same stream, so one synchronisation
   // covers the output and the flag.
   const bool flag = ctx->dev_err.p != nullptr;
   if (flag) {
@@ -941,6 +973,7 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
                                   ctx->stream));
   }
   SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (!out_pinned) memcpy(out, ctx->hout, bytes);
   if (flag && *ctx->err_host != 0) {
     const int32_t e = *ctx->err_host;
     *ctx->err_host = 0;
@@ -1061,6 +1094,8 @@ void spt_context_destroy(spt_context *ctx) {
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
+    if (ctx->hx) cudaFreeHost(ctx->hx);
+    if (ctx->hout) cudaFreeHost(ctx->hout);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   }
   delete ctx;
@@ -1169,15 +1204,33 @@ spt_status spt_validate_moe_layer(spt_context *ctx, const spt_reader *reader,
   return validate_layer(ctx, reader, cfg, lw);
 }
 
+// With `views` (spt_arena_create_views) every tensor's bytes come from its
+// own pointer instead of reader.base + start; the caller's reader validated
+// the file ranges.
 static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,
                              const spt_layer_weights *layers, int64_t n_layers, uint32_t flags, int64_t e0,
-                             int64_t e1, spt_arena **out) {
-  if (!out || !readers || !cfg || !layers || n_layers <= 0)
+                             int64_t e1, spt_arena **out, const spt_layer_data *views = nullptr) {
+  if (!out || (!readers && !views) || !cfg || !layers || n_layers <= 0)
     return fail(ctx, SPT_ERR_NULL_ARG, "nil MoE context, reader, configuration or weights");
   *out = nullptr;
   for (int64_t l = 0; l < n_layers; ++l) {
-    spt_status st = validate_layer(ctx, &readers[l], cfg, &layers[l]);
+    static const uint8_t kAny = 0;
+    const spt_reader whole = {&kAny, UINT64_MAX};  // ranges were checked by the caller's reader
+    spt_status st = validate_layer(ctx, views ? &whole : &readers[l], cfg, &layers[l]);
     if (st) return st;
+    if (views) {
+      const spt_layer_weights &w = layers[l];
+      const spt_layer_data &v = views[l];
+      const std::pair<const spt_tensor *, const uint8_t *> need[] = {
+          {&w.ffn_gate_inp, v.ffn_gate_inp},         {&w.ffn_gate_inp_bias, v.ffn_gate_inp_bias},
+          {&w.ffn_gate_exps, v.ffn_gate_exps},       {&w.ffn_gate_exps_bias, v.ffn_gate_exps_bias},
+          {&w.ffn_up_exps, v.ffn_up_exps},           {&w.ffn_up_exps_bias, v.ffn_up_exps_bias},
+          {&w.ffn_down_exps, v.ffn_down_exps},       {&w.ffn_down_exps_bias, v.ffn_down_exps_bias},
+          {&w.post_attention_norm, v.post_attention_norm}};
+      for (const auto &n : need)
+        if (named(*n.first) && !n.second)
+          return fail(ctx, SPT_ERR_NULL_ARG, "tensor \"%s\": no data", tname(*n.first));
+    }
   }
   spt_status st = require_device(ctx);
   if (st) return st;
@@ -1197,33 +1250,39 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
   std::vector<float> tmp;
   DevBuf range;  // smallest and largest E8M0 byte of a layer's expert blocks
   for (int64_t l = 0; l < n_layers && st == SPT_OK; ++l) {
-    const spt_reader &r = readers[l];
     const spt_layer_weights &w = layers[l];
+    // first byte of tensor t of this layer (views: the caller's pointer)
+    auto src = [&](const spt_tensor &t, const uint8_t *view) -> const uint8_t * {
+      return views ? view : readers[l].base + t.start;
+    };
+    const spt_layer_data nov{};
+    const spt_layer_data &v = views ? views[l] : nov;
     LayerDev &L = a->layers[(size_t)l];
     float *router = nullptr;
     if ((st = arena_alloc(ctx, a, (size_t)(E * H), &router))) break;
-    if ((st = upload(ctx, router, r.base + w.ffn_gate_inp.start, (size_t)(E * H * 4)))) break;
+    if ((st = upload(ctx, router, src(w.ffn_gate_inp, v.ffn_gate_inp), (size_t)(E * H * 4)))) break;
     L.router = router;
     tmp.assign((size_t)E, 0.0f);
     if (named(w.ffn_gate_inp_bias))
-      decode_floats(r.base + w.ffn_gate_inp_bias.start, w.ffn_gate_inp_bias.type, E, tmp.data());
+      decode_floats(src(w.ffn_gate_inp_bias, v.ffn_gate_inp_bias), w.ffn_gate_inp_bias.type, E, tmp.data());
     if ((st = upload_floats(ctx, a, tmp.data(), (size_t)E, &L.router_bias))) break;
     if (named(w.post_attention_norm)) {
       tmp.assign((size_t)H, 0.0f);
       const uint32_t ty = w.post_attention_norm.type == 28 ? 30u : w.post_attention_norm.type;  // RMSNorm's BF16 tag
-      decode_floats(r.base + w.post_attention_norm.start, ty, H, tmp.data());
+      decode_floats(src(w.post_attention_norm, v.post_attention_norm), ty, H, tmp.data());
       if ((st = upload_floats(ctx, a, tmp.data(), (size_t)H, &L.norm))) break;
     }
     struct {
       const spt_tensor *t;
+      const uint8_t *view;
       int64_t dim;
       const float **dst;
-    } biases[] = {{&w.ffn_gate_exps_bias, D, &L.gate_bias},
-                  {&w.ffn_up_exps_bias, D, &L.up_bias},
-                  {&w.ffn_down_exps_bias, H, &L.down_bias}};
+    } biases[] = {{&w.ffn_gate_exps_bias, v.ffn_gate_exps_bias, D, &L.gate_bias},
+                  {&w.ffn_up_exps_bias, v.ffn_up_exps_bias, D, &L.up_bias},
+                  {&w.ffn_down_exps_bias, v.ffn_down_exps_bias, H, &L.down_bias}};
     for (auto &b : biases) {
       tmp.assign((size_t)(E * b.dim), 0.0f);
-      if (named(*b.t)) decode_floats(r.base + b.t->start, b.t->type, E * b.dim, tmp.data());
+      if (named(*b.t)) decode_floats(src(*b.t, b.view), b.t->type, E * b.dim, tmp.data());
       if ((st = upload_floats(ctx, a, tmp.data() + e0 * b.dim, (size_t)(ne * b.dim), b.dst))) break;
     }
     if (st) break;
@@ -1236,8 +1295,8 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
       DevBuf sg, su;
       // expert e's matrix is the byte range [start + e * per_expert, + per_expert)
       const size_t gu_per = (size_t)D * (H / 32) * 17, gu_raw = (size_t)ne * gu_per;
-      if ((st = stage_raw(ctx, &sg, r.base + w.ffn_gate_exps.start + e0 * gu_per, gu_raw)) == SPT_OK &&
-          (st = stage_raw(ctx, &su, r.base + w.ffn_up_exps.start + e0 * gu_per, gu_raw)) == SPT_OK) {
+      if ((st = stage_raw(ctx, &sg, src(w.ffn_gate_exps, v.ffn_gate_exps) + e0 * gu_per, gu_raw)) == SPT_OK &&
+          (st = stage_raw(ctx, &su, src(w.ffn_up_exps, v.ffn_up_exps) + e0 * gu_per, gu_raw)) == SPT_OK) {
         if (flags & SPT_ARENA_GEMV) {
           if (st == SPT_OK) st = repack_g8_from(ctx, a, sg.as<uint8_t>(), ne, (int)D, (int)(H / 32), &L.gate);
           if (st == SPT_OK) st = repack_g8_from(ctx, a, su.as<uint8_t>(), ne, (int)D, (int)(H / 32), &L.up);
@@ -1260,7 +1319,7 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
       if (st) break;
       DevBuf sd;
       const size_t dn_per = (size_t)H * (D / 32) * 17;
-      if ((st = stage_raw(ctx, &sd, r.base + w.ffn_down_exps.start + e0 * dn_per, (size_t)ne * dn_per)) == SPT_OK) {
+      if ((st = stage_raw(ctx, &sd, src(w.ffn_down_exps, v.ffn_down_exps) + e0 * dn_per, (size_t)ne * dn_per)) == SPT_OK) {
         if (flags & SPT_ARENA_GEMV) st = repack_g8_from(ctx, a, sd.as<uint8_t>(), ne, (int)H, (int)(D / 32), &L.down);
         if (st == SPT_OK && (flags & SPT_ARENA_MMA)) {
           st = alloc_mma(ctx, a, ne, (int)H, (int)D, &L.dn_mma);
@@ -1297,6 +1356,14 @@ spt_status spt_arena_create(spt_context *ctx, const spt_reader *readers, const s
                             const spt_layer_weights *layers, int64_t n_layers, uint32_t flags,
                             spt_arena **out) {
   return arena_create_impl(ctx, readers, cfg, layers, n_layers, flags, 0, cfg ? cfg->num_experts : 0, out);
+}
+
+spt_status spt_arena_create_views(spt_context *ctx, const spt_moe_config *cfg, const spt_layer_weights *layers,
+                                  const spt_layer_data *data, int64_t n_layers, uint32_t flags, int64_t expert_begin,
+                                  int64_t expert_end, spt_arena **out) {
+  if (!data) return fail(ctx, SPT_ERR_NULL_ARG, "nil tensor data");
+  if (expert_end == 0 && cfg) expert_end = cfg->num_experts;
+  return arena_create_impl(ctx, nullptr, cfg, layers, n_layers, flags, expert_begin, expert_end, out, data);
 }
 
 spt_status spt_arena_create_range(spt_context *ctx, const spt_reader *readers, const spt_moe_config *cfg,

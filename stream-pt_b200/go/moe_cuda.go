@@ -1,21 +1,30 @@
 //go:build goexperiment.simd && sptcuda
 
-// Package forward, CUDA build: forwardMoEBatch and its stages call the
-// sm_100a library libspt_moe.so through its C ABI (include/spt_moe.h)
-// instead of the Go SIMD kernels.  Build with
+// Package forward, CUDA build: forwardMoEBatch calls the sm_100a library
+// libspt_moe.so through its C ABI (include/spt_moe.h) instead of the Go SIMD
+// kernels.  Build with
 //
 //	CGO_CFLAGS=-I<repo>/include CGO_LDFLAGS="-L<repo>/stream-pt_b200 -lspt_moe" \
 //	GOEXPERIMENT=simd go build -tags sptcuda ./...
 //
-// and drop this file into forward/ in place of the pure-Go definitions of
-// forwardMoEBatch (forward/moe_batch.go:78-194); the function signature and
-// error behaviour are unchanged.  Experts are uploaded once per
-// (reader, LayerWeights) into an HBM arena (replacing ggufmap's expert
-// window, cache and lookahead) and reused by every later call.
+// and drop this file into forward/ in place of the pure-Go definition of
+// forwardMoEBatch (forward/moe_batch.go:78-194); the signature and the error
+// behaviour are unchanged, and forwardMoE (forward/moe.go:28-64) reaches it
+// as before.
+//
+// Each layer's MoE tensors are uploaded once into an HBM arena, with both
+// the bit-exact CUDA-core layout and the tensor-core layout, read through
+// the Reader's own WithTensor (ggufmap/mmap_linux.go:210): the slices are
+// handed to the library while their callbacks run, and the library keeps
+// nothing of them.  The arena replaces the expert window, hot-expert cache
+// and lookahead of WithExpertRanges.  Arenas are keyed by the reader and the
+// byte ranges of the layer's tensors, so forwardMoE's per-call LayerWeights
+// values reuse the arena of their layer.
 package forward
 
 /*
 #cgo LDFLAGS: -lspt_moe
+#include <stdint.h>
 #include <stdlib.h>
 #include "spt_moe.h"
 */
@@ -26,18 +35,30 @@ import (
 	"errors"
 	"fmt"
 	"sync"
+	"sync/atomic"
 	"unsafe"
 
 	"Stream-PT/ggufindex"
 	ggufmmap "Stream-PT/ggufmap"
 )
 
+// arenaKey identifies a layer's MoE weights: the reader and the byte ranges
+// of every tensor the arena holds.
+type arenaKey struct {
+	reader                                          *ggufmmap.Reader
+	router, routerBias, gate, gateBias, up, upBias  ggufindex.Range
+	down, downBias, norm                            ggufindex.Range
+}
+
 var (
-	sptOnce  sync.Once
-	sptCtx   *C.spt_context
-	sptErr   error
-	sptMu    sync.Mutex
-	sptArena = map[*LayerWeights]*C.spt_arena{}
+	sptOnce   sync.Once
+	sptCtx    *C.spt_context
+	sptErr    error
+	sptArenaM sync.Mutex
+	sptArena  = map[arenaKey]*C.spt_arena{}
+	// sptCallM serialises forward calls: they share the context's stream and
+	// device buffers (the reference gives each caller its own scratch).
+	sptCallM sync.Mutex
 )
 
 func sptContext() (*C.spt_context, error) {
@@ -77,13 +98,36 @@ func sptTensor(t ggufindex.Tensor, names *[]*C.char) C.spt_tensor {
 	return c
 }
 
-// arenaFor uploads the layer once.  The reader's mapped file view is passed
-// as the spt_reader (ggufmap exposes it through WithTensor for the whole
-// file range).
+// withTensors opens every named tensor of ts through reader.WithTensor,
+// nested, and calls fn with all of their slices (nil for unnamed ones) while
+// every mapping is alive.
+func withTensors(reader *ggufmmap.Reader, ts []ggufindex.Tensor, views [][]byte, fn func([][]byte) error) error {
+	if len(ts) == 0 {
+		return fn(views)
+	}
+	if ts[0].Name == "" {
+		return withTensors(reader, ts[1:], append(views, nil), fn)
+	}
+	return reader.WithTensor(ts[0], func(data []byte) error {
+		return withTensors(reader, ts[1:], append(views, data), fn)
+	})
+}
+
+func first(b []byte) *C.uint8_t {
+	if len(b) == 0 {
+		return nil
+	}
+	return (*C.uint8_t)(unsafe.Pointer(&b[0]))
+}
+
+// arenaFor uploads the layer once and returns its arena afterwards.
 func arenaFor(ctx *C.spt_context, reader *ggufmmap.Reader, cfg *Config, lw *LayerWeights) (*C.spt_arena, error) {
-	sptMu.Lock()
-	defer sptMu.Unlock()
-	if a, ok := sptArena[lw]; ok {
+	key := arenaKey{reader, lw.FFNGateInp.Range, lw.FFNGateInpBias.Range, lw.FFNGateExps.Range,
+		lw.FFNGateExpsBias.Range, lw.FFNUpExps.Range, lw.FFNUpExpsBias.Range, lw.FFNDownExps.Range,
+		lw.FFNDownExpsBias.Range, lw.PostAttnNorm.Range}
+	sptArenaM.Lock()
+	defer sptArenaM.Unlock()
+	if a, ok := sptArena[key]; ok {
 		return a, nil
 	}
 	var names []*C.char
@@ -94,28 +138,40 @@ func arenaFor(ctx *C.spt_context, reader *ggufmmap.Reader, cfg *Config, lw *Laye
 	}()
 	c := C.spt_moe_config{C.int64_t(cfg.HiddenDim), C.int64_t(cfg.ExpertHiddenDim),
 		C.int64_t(cfg.NumExperts), C.int64_t(cfg.NumExpertsUsed)}
+	ts := []ggufindex.Tensor{lw.FFNGateInp, lw.FFNGateInpBias, lw.FFNGateExps, lw.FFNGateExpsBias,
+		lw.FFNUpExps, lw.FFNUpExpsBias, lw.FFNDownExps, lw.FFNDownExpsBias, lw.PostAttnNorm}
 	w := C.spt_layer_weights{
-		ffn_gate_inp: sptTensor(lw.FFNGateInp, &names), ffn_gate_inp_bias: sptTensor(lw.FFNGateInpBias, &names),
-		ffn_gate_exps: sptTensor(lw.FFNGateExps, &names), ffn_gate_exps_bias: sptTensor(lw.FFNGateExpsBias, &names),
-		ffn_up_exps: sptTensor(lw.FFNUpExps, &names), ffn_up_exps_bias: sptTensor(lw.FFNUpExpsBias, &names),
-		ffn_down_exps: sptTensor(lw.FFNDownExps, &names), ffn_down_exps_bias: sptTensor(lw.FFNDownExpsBias, &names),
-		post_attention_norm: sptTensor(lw.PostAttnNorm, &names),
+		ffn_gate_inp: sptTensor(ts[0], &names), ffn_gate_inp_bias: sptTensor(ts[1], &names),
+		ffn_gate_exps: sptTensor(ts[2], &names), ffn_gate_exps_bias: sptTensor(ts[3], &names),
+		ffn_up_exps: sptTensor(ts[4], &names), ffn_up_exps_bias: sptTensor(ts[5], &names),
+		ffn_down_exps: sptTensor(ts[6], &names), ffn_down_exps_bias: sptTensor(ts[7], &names),
+		post_attention_norm: sptTensor(ts[8], &names),
 	}
 	var arena *C.spt_arena
-	err := reader.WithFile(lw.FFNGateInp.Range.File, func(file []byte) error {
-		r := C.spt_reader{base: (*C.uint8_t)(unsafe.Pointer(&file[0])), size: C.uint64_t(len(file))}
-		return sptError(ctx, C.spt_arena_create(ctx, &r, &c, &w, 1, C.SPT_ARENA_GEMV, &arena))
+	err := withTensors(reader, ts, nil, func(v [][]byte) error {
+		// the slices are mmap views, not Go heap memory: C may read them
+		// during this call and keeps no reference afterwards
+		d := C.spt_layer_data{
+			ffn_gate_inp: first(v[0]), ffn_gate_inp_bias: first(v[1]),
+			ffn_gate_exps: first(v[2]), ffn_gate_exps_bias: first(v[3]),
+			ffn_up_exps: first(v[4]), ffn_up_exps_bias: first(v[5]),
+			ffn_down_exps: first(v[6]), ffn_down_exps_bias: first(v[7]),
+			post_attention_norm: first(v[8]),
+		}
+		return sptError(ctx, C.spt_arena_create_views(ctx, &c, &w, &d, 1, C.SPT_ARENA_GEMV|C.SPT_ARENA_MMA, 0, 0,
+			&arena))
 	})
 	if err != nil {
 		return nil, err
 	}
-	sptArena[lw] = arena
+	sptArena[key] = arena
 	return arena, nil
 }
 
 // forwardMoEBatch: same contract as forward/moe_batch.go:78-194.  x and out
 // hold no Go pointers, so passing &x[0] / &out[0] to C is legal; C keeps
-// neither after returning.
+// neither after returning (pageable memory is staged through the library's
+// pinned buffers).
 func forwardMoEBatch(ctx context.Context, reader *ggufmmap.Reader, x []float32, cfg *Config,
 	lw *LayerWeights, out []float32, batch int, options Q40Options, scratch *moeBatchScratch,
 ) error {
@@ -136,19 +192,26 @@ func forwardMoEBatch(ctx context.Context, reader *ggufmmap.Reader, x []float32, 
 	if err != nil {
 		return err
 	}
-	var cancel C.int32_t
-	done := make(chan struct{})
+	// The cancel flag lives in C memory: C polls it while a goroutine may set
+	// it, so it is written with an atomic store and never through Go memory.
+	cancel := (*C.int32_t)(C.calloc(1, C.size_t(unsafe.Sizeof(C.int32_t(0)))))
+	stop, exited := make(chan struct{}), make(chan struct{})
 	go func() { // context cancellation -> the library's cancel flag
+		defer close(exited)
 		select {
 		case <-ctx.Done():
-			cancel = 1
-		case <-done:
+			atomic.StoreInt32((*int32)(unsafe.Pointer(cancel)), 1)
+		case <-stop:
 		}
 	}()
+	sptCallM.Lock()
 	st := C.spt_forward_moe_batch(sctx, arena, 0,
 		(*C.float)(unsafe.Pointer(&x[0])), C.int64_t(len(x)),
 		(*C.float)(unsafe.Pointer(&out[0])), C.int64_t(len(out)),
-		C.int64_t(batch), &cancel)
-	close(done)
+		C.int64_t(batch), cancel)
+	sptCallM.Unlock()
+	close(stop)
+	<-exited // the goroutine no longer touches the flag
+	C.free(unsafe.Pointer(cancel))
 	return sptError(sctx, st)
 }

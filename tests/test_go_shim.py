@@ -1,0 +1,74 @@
+"""The cgo shim (stream-pt_b200/go/moe_cuda.go) against the reference's Go
+API and the C ABI, without a Go toolchain (none is installed here).
+
+Every identifier the shim takes from package forward, ggufindex or ggufmap
+must exist in the reference (tests/golden/go_api.json, written from the
+reference sources by tests/golden/make_go_api.py), forwardMoEBatch must keep
+the reference's parameter list, and every C function and struct field it
+uses must be declared in include/spt_moe.h.
+"""
+import json
+import os
+import re
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SHIM = open(os.path.join(ROOT, "stream-pt_b200", "go", "moe_cuda.go")).read()
+API = json.load(open(os.path.join(ROOT, "tests", "golden", "go_api.json")))
+HEADER = open(os.path.join(ROOT, "include", "spt_moe.h")).read()
+CODE = re.sub(r"//[^\n]*", "", SHIM)  # comments out
+
+
+def test_imports_name_the_reference_packages():
+    imports = dict((alias or path.split("/")[-1], path) for alias, path in
+                   re.findall(r'^\s*(\w+)?\s*"([^"]+)"$', CODE.split("import (", 1)[1].split(")", 1)[0], re.M))
+    assert imports["ggufindex"] == API["module"] + "/ggufindex"
+    assert imports[API["packages"]["ggufmap"]] == API["module"] + "/ggufmap"
+
+
+def test_reader_methods_exist():
+    used = set(re.findall(r"\breader\.(\w+)\(", CODE))
+    assert used and used <= set(API["reader_methods"]), used - set(API["reader_methods"])
+    assert "WithFile" not in used
+    # WithTensor's callback is func(data []byte) error
+    assert API["with_tensor"] == "t ggufindex.Tensor, fn func(data []byte) error"
+    assert re.search(r"reader\.WithTensor\(\w+\[0\], func\(data \[\]byte\) error \{", CODE)
+
+
+def test_fields_exist():
+    checks = [(r"\blw\.(\w+)", "layer_weights_fields"), (r"\bcfg\.(\w+)", "config_fields"),
+              (r"\bt\.(\w+)", "tensor_fields"), (r"\bts\[\d+\]\.(\w+)", "tensor_fields"),
+              (r"\.Range\.(\w+)", "range_fields")]
+    for pat, key in checks:
+        used = set(re.findall(pat, CODE))
+        assert used <= set(API[key]), (key, used - set(API[key]))
+    for pkg, key in (("ggufindex", "ggufindex_exported"), (API["packages"]["ggufmap"], "ggufmap_exported")):
+        used = set(re.findall(r"\b%s\.(\w+)" % pkg, CODE))
+        assert used <= set(API[key]), (pkg, used - set(API[key]))
+    for typ in ("Config", "LayerWeights", "Q40Options", "moeBatchScratch"):
+        assert typ in API["forward_types"]
+
+
+def test_forward_moe_batch_signature_unchanged():
+    sig = re.search(r"func forwardMoEBatch\((.*?)\) error \{", CODE, re.S).group(1)
+    assert " ".join(sig.split()) == API["forward_moe_batch_params"]
+
+
+def test_c_symbols_and_fields_are_declared():
+    funcs = set(re.findall(r"\b(spt_\w+)\s*\(", HEADER))
+    consts = set(re.findall(r"#define (SPT_\w+)", HEADER)) | set(re.findall(r"\b(SPT_(?:OK|ERR_\w+))\b", HEADER))
+    types = set(re.findall(r"typedef struct (spt_\w+)", HEADER))
+    used_funcs = set(re.findall(r"\bC\.(spt_[a-z_]+)\(", CODE)) - types
+    assert used_funcs and used_funcs <= funcs, used_funcs - funcs
+    used_consts = set(re.findall(r"\bC\.(SPT_\w+)", CODE))
+    assert used_consts <= consts, used_consts - consts
+    for typ in set(re.findall(r"(?<!\*)\bC\.(spt_\w+)\{", CODE)):  # composite literals (not map[..]*C.x{})
+        body = re.search(r"typedef struct %s \{(.*?)\}" % typ, HEADER, re.S).group(1)
+        fields = set(re.findall(r"\b([a-z_]\w*)\s*[,;\[]", body))
+        for m in re.finditer(r"C\.%s\{" % typ, CODE):
+            depth, i = 1, m.end()
+            while depth:  # the literal's own braces
+                depth += {"{": 1, "}": -1}.get(CODE[i], 0)
+                i += 1
+            block = CODE[m.end():i - 1]
+            named = set(re.findall(r"\b([a-z_]\w*):", block))
+            assert named <= fields, (typ, named - fields)

@@ -61,3 +61,28 @@ def test_gguf_arena_matches_synthetic(ctx, spt, tmp_path):
         from_file.close()
         synth.close()
         g.close()
+
+
+@pytest.mark.parametrize("flags", ["gemv", "both"])
+def test_arena_from_tensor_views_matches_reader_arena(ctx, spt, flags):
+    import refdata
+    """spt_arena_create_views (each tensor handed over as its own buffer, the
+    way the Go shim passes ggufmap.Reader.WithTensor slices) builds the same
+    arena as spt_arena_create over the whole file: identical outputs on the
+    exact path, and on the tensor-core path when both layouts are built."""
+    f = spt.ARENA_GEMV if flags == "gemv" else spt.ARENA_GEMV | spt.ARENA_MMA
+    for bias in (-1, 1, 30):
+        fx = refdata.moe_batch_fixture(96, 64, 7, 2, bias, "normal")
+        x = refdata.moe_batch_x(9, 96, "normal")
+        a = ctx.arena([fx.reader], fx.cfg, [fx.lw], flags=f)
+        b = ctx.arena_views([fx.reader], fx.cfg, [fx.lw], flags=f)
+        try:
+            for path in ([spt.PATH_EXACT] if flags == "gemv" else [spt.PATH_EXACT, spt.PATH_MMA, spt.PATH_GEMV16]):
+                ctx.set_path(path)
+                ya = ctx.forward_moe_batch(a, x, 9)
+                yb = ctx.forward_moe_batch(b, x, 9)
+                assert refdata.bits_equal(ya, yb).all(), (bias, path)
+        finally:
+            ctx.set_path(spt.PATH_AUTO)
+            a.close()
+            b.close()
