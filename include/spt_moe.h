@@ -223,13 +223,20 @@ spt_status spt_context_set_path(spt_context *ctx, int path);
  *                         second) and the call returns SPT_ERR_TIMEOUT
  *   SPT_OPT_FAULT_STAGE   test hook, -1 off: the tcgen05 producer of CTA 0
  *                         skips this pipeline stage, so the MMA issuer's wait
- *                         for it runs out (the failure path without a fault) */
+ *                         for it runs out (the failure path without a fault)
+ *   SPT_OPT_HOST_GRAPHS   1 (default): spt_forward_moe_batch / spt_forward_moe
+ *                         capture the block's kernels into a CUDA graph on the
+ *                         second call with the same arena, layer, batch and
+ *                         options, and replay it afterwards (one launch
+ *                         instead of five to eight); 0: plain launches
+ *                         (SPT_HOST_GRAPHS) */
 #define SPT_OPT_TILE_TOKENS 1
 #define SPT_OPT_FUSED_SELECT 2
 #define SPT_OPT_L2_PREFETCH 3
 #define SPT_OPT_GEMV16_SLOTS 4
 #define SPT_OPT_WAIT_LIMIT 5
 #define SPT_OPT_FAULT_STAGE 6
+#define SPT_OPT_HOST_GRAPHS 7
 spt_status spt_context_set_option(spt_context *ctx, int option, int64_t value);
 int64_t spt_context_get_option(const spt_context *ctx, int option);
 

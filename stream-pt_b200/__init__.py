@@ -32,6 +32,7 @@ ERR_FORMAT = 15
 PATH_AUTO, PATH_EXACT, PATH_MMA, PATH_GEMV16 = 0, 1, 2, 3
 # spt_context_set_option (include/spt_moe.h)
 OPT_TILE_TOKENS, OPT_FUSED_SELECT, OPT_L2_PREFETCH, OPT_GEMV16_SLOTS, OPT_WAIT_LIMIT, OPT_FAULT_STAGE = 1, 2, 3, 4, 5, 6
+OPT_HOST_GRAPHS = 7
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
 
@@ -688,8 +689,27 @@ def ep_expert_range(num_experts: int, world: int, rank: int) -> Tuple[int, int]:
     return b.value, e.value
 
 
+def _nccl_library():
+    """Point the library at PyTorch's NCCL (the pip nvidia-nccl package) when
+    that is installed and no NCCL is named yet: whichever NCCL the process
+    loads first is the one every later user of the soname gets."""
+    if os.environ.get("SPT_NCCL_LIBRARY"):
+        return
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        spec = None
+    for base in (spec.submodule_search_locations if spec else []) or []:
+        path = os.path.join(base, "lib", "libnccl.so.2")
+        if os.path.exists(path):
+            os.environ["SPT_NCCL_LIBRARY"] = path
+            return
+
+
 def ep_unique_id() -> bytes:
     """NCCL unique id for spt_ep_create (made on rank 0, shared out of band)."""
+    _nccl_library()
     buf = (ctypes.c_uint8 * 128)()
     st = lib().spt_ep_unique_id(buf)
     if st != OK:
@@ -704,6 +724,7 @@ class ExpertParallel:
         if len(unique_id) != 128:
             raise ValueError("unique id must be 128 bytes")
         self.ctx, self.rank, self.world = ctx, rank, world
+        _nccl_library()
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
         self._h = ctypes.c_void_p()
         ctx.check(lib().spt_ep_create(ctx._h, buf, rank, world, ctypes.byref(self._h)))

@@ -86,6 +86,21 @@ struct spt_context {
   int opt_gemv16_slots = 16;    // SPT_PATH_AUTO: decode GEMV while batch x top-k <= this
   int opt_wait_shift = 31;      // bounded device waits give up after 2^shift clock cycles
   int opt_fault_stage = -1;     // failure injection: the tcgen05 producer skips this stage (tests)
+  int opt_host_graphs = 1;      // replay repeated host calls from captured CUDA graphs
+  // Host-call graphs: the block's kernels captured once per (arena, layer,
+  // batch, path and options) and replayed by the host entry points; `bufs`
+  // is the device buffers the capture used (a grown buffer invalidates it).
+  struct HostGraph {
+    uint64_t arena = 0;
+    int64_t layer = 0, T = 0;
+    std::vector<int64_t> opts;
+    std::vector<const void *> bufs;
+    cudaGraphExec_t exec = nullptr;
+    bool warm = false;  // ran once uncaptured with this key (its buffers exist)
+    uint64_t used = 0;
+  };
+  std::vector<HostGraph> graphs;
+  uint64_t graph_clock = 0;
   int last_path = SPT_PATH_EXACT;  // expert path of the last forward (SPT_PATH_EXACT / _MMA / _GEMV16)
   bool timed_last = false;         // the last forward recorded stage events
   int last_bn = 0;                 // its tcgen05 token-tile width
@@ -107,6 +122,7 @@ struct spt_q80_matrix {
 };
 
 struct spt_arena {
+  uint64_t id = 0;           // unique per arena in the process (keys the context's call graphs)
   int device = -1;
   spt_moe_config cfg{};
   int64_t expert_begin = 0;  // experts [expert_begin, expert_begin + expert_count) are resident
@@ -120,6 +136,13 @@ struct spt_arena {
 namespace {
 
 constexpr float kSynthNormStd = 0.02f;  // RMSNorm weights ~ N(1, 0.02)
+
+spt_arena *new_arena() {
+  static std::atomic<uint64_t> next{1};
+  spt_arena *a = new spt_arena();
+  a->id = next.fetch_add(1);
+  return a;
+}
 
 // Device address of the allocation-free entry point's static scratch on
 // ctx's device (defined with that entry point below).
@@ -916,6 +939,47 @@ spt_status check_batch(spt_context *ctx, const spt_moe_config &c, const float *x
   return SPT_OK;
 }
 
+
+// Device buffers a captured block touches.
+std::vector<const void *> call_buffers(const spt_context *ctx) {
+  std::vector<const void *> v;
+  for (const DevBuf *b : {&ctx->logits, &ctx->sel_idx, &ctx->sel_w, &ctx->offsets, &ctx->perm, &ctx->slot_pos,
+                          &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res, &ctx->xdev, &ctx->outdev, &ctx->dev_err,
+                          &ctx->pad_off, &ctx->tile_gu, &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx,
+                          &ctx->qa, &ctx->sfa, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off})
+    v.push_back(b->p);
+  return v;
+}
+
+std::vector<int64_t> call_options(const spt_context *ctx) {
+  return {ctx->path, ctx->opt_tile_tokens, ctx->opt_fused_select, ctx->opt_prefetch, ctx->opt_gemv16_slots,
+          ctx->opt_wait_shift, ctx->opt_fault_stage, (int64_t)(uintptr_t)ctx->stream};
+}
+
+// Capture the block on the context's device buffers into a graph (after a
+// warm uncaptured run made every buffer).  On any failure the capture is
+// dropped and the caller launches the kernels itself.
+bool capture_block(spt_context *ctx, spt_arena *arena, int64_t layer, int64_t batch, cudaGraphExec_t *exec) {
+  *exec = nullptr;
+  if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const std::string saved = ctx->err;
+  const spt_status st = forward_device(ctx, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  bool ok = st == SPT_OK && e == cudaSuccess && graph;
+  if (ok) ok = cudaGraphInstantiate(exec, graph, 0) == cudaSuccess;
+  if (graph) cudaGraphDestroy(graph);
+  if (!ok) {
+    cudaGetLastError();
+    *exec = nullptr;
+    ctx->err = saved;
+  }
+  return ok;
+}
+
 // Whether host memory p is page-locked (copies from it can be asynchronous).
 bool host_pinned(const void *p) {
   cudaPointerAttributes a;
@@ -949,32 +1013,62 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
   const size_t bytes = sizeof(float) * (size_t)x_len;
   SPT_CUDA(ctx, ctx->xdev.ensure(bytes));
   SPT_CUDA(ctx, ctx->outdev.ensure(bytes));
+  if (!ctx->err_host) SPT_CUDA(ctx, cudaHostAlloc((void **)&ctx->err_host, sizeof(int32_t), cudaHostAllocDefault));
   // Pageable caller memory (a Go slice) goes through the context's pinned
   // buffers, so both copies are asynchronous and the call synchronises once.
   const bool x_pinned = host_pinned(x), out_pinned = host_pinned(out);
-  const float *xsrc = x;
+  const void *xsrc = x;
   if (!x_pinned) {
     if ((st = ensure_pinned(ctx, &ctx->hx, &ctx->hx_bytes, bytes))) return st;
     memcpy(ctx->hx, x, bytes);
-    xsrc = static_cast<const float *>(ctx->hx);
+    xsrc = ctx->hx;
   }
   if (!out_pinned && (st = ensure_pinned(ctx, &ctx->hout, &ctx->hout_bytes, bytes))) return st;
   SPT_CUDA(ctx, cudaMemcpyAsync(ctx->xdev.p, xsrc, bytes, cudaMemcpyHostToDevice, ctx->stream));
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
-  if ((st = forward_device(ctx, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch)))
-    return st;
+  // The block: replayed from a captured graph on repeated calls (not while
+  // stage timing records events), else launched kernel by kernel.
+  spt_context::HostGraph *g = nullptr;
+  if (ctx->opt_host_graphs && !ctx->timing) {
+    const std::vector<int64_t> opts = call_options(ctx);
+    for (auto &h : ctx->graphs)
+      if (h.arena == arena->id && h.layer == layer && h.T == batch && h.opts == opts) g = &h;
+    if (g && g->exec && g->bufs != call_buffers(ctx)) {  // a buffer moved: capture again
+      cudaGraphExecDestroy(g->exec);
+      g->exec = nullptr;
+    }
+    if (!g) {
+      if (ctx->graphs.size() >= 16) {  // evict the least recently used
+        auto lru = std::min_element(ctx->graphs.begin(), ctx->graphs.end(),
+                                    [](const auto &p, const auto &q) { return p.used < q.used; });
+        if (lru->exec) cudaGraphExecDestroy(lru->exec);
+        ctx->graphs.erase(lru);
+      }
+      ctx->graphs.push_back({});
+      g = &ctx->graphs.back();
+      g->arena = arena->id;
+      g->layer = layer;
+      g->T = batch;
+      g->opts = opts;
+    }
+    g->used = ++ctx->graph_clock;
+    if (!g->exec && g->warm && capture_block(ctx, arena, layer, batch, &g->exec)) g->bufs = call_buffers(ctx);
+  }
+  if (g && g->exec) {
+    SPT_CUDA(ctx, cudaGraphLaunch(g->exec, ctx->stream));
+  } else {
+    if ((st = forward_device(ctx, arena, layer, ctx->xdev.as<float>(), ctx->outdev.as<float>(), batch))) return st;
+    if (g) g->warm = true;
+  }
   SPT_CUDA(ctx, cudaMemcpyAsync(out_pinned ? (void *)out : ctx->hout, ctx->outdev.p, bytes, cudaMemcpyDeviceToHost,
-                                ctx->stream));  // The GEMM's error flag rides on the same stream, so one synchronisation
-  // covers the output and the flag.
-  const bool flag = ctx->dev_err.p != nullptr;
-  if (flag) {
-    if (!ctx->err_host) SPT_CUDA(ctx, cudaHostAlloc((void **)&ctx->err_host, sizeof(int32_t), cudaHostAllocDefault));
+                                ctx->stream));
+  // the GEMM's error flag comes back with the output: one synchronisation
+  if (ctx->dev_err.p)
     SPT_CUDA(ctx, cudaMemcpyAsync(ctx->err_host, ctx->dev_err.p, sizeof(int32_t), cudaMemcpyDeviceToHost,
                                   ctx->stream));
-  }
   SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   if (!out_pinned) memcpy(out, ctx->hout, bytes);
-  if (flag && *ctx->err_host != 0) {
+  if (ctx->dev_err.p && *ctx->err_host != 0) {
     const int32_t e = *ctx->err_host;
     *ctx->err_host = 0;
     SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
@@ -999,6 +1093,7 @@ void seed_options(spt_context *ctx) {
   env("SPT_FUSED_SELECT", &ctx->opt_fused_select, 0, 1);
   env("SPT_MMA_PREFETCH", &ctx->opt_prefetch, 0, 64);
   env("SPT_GEMV16_SLOTS", &ctx->opt_gemv16_slots, 0, 1 << 20);
+  env("SPT_HOST_GRAPHS", &ctx->opt_host_graphs, 0, 1);
 }
 
 // Temporary device buffer for stage entry points.
@@ -1093,6 +1188,8 @@ void spt_context_destroy(spt_context *ctx) {
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
+    for (auto &g : ctx->graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->hx) cudaFreeHost(ctx->hx);
     if (ctx->hout) cudaFreeHost(ctx->hout);
@@ -1180,6 +1277,10 @@ spt_status spt_context_set_option(spt_context *ctx, int option, int64_t v) {
       if (v < -1 || v > (1 << 20)) break;
       ctx->opt_fault_stage = (int)v;
       return SPT_OK;
+    case SPT_OPT_HOST_GRAPHS:
+      if (v != 0 && v != 1) break;
+      ctx->opt_host_graphs = (int)v;
+      return SPT_OK;
     default:
       return fail(ctx, SPT_ERR_UNSUPPORTED, "unknown option %d", option);
   }
@@ -1195,6 +1296,7 @@ int64_t spt_context_get_option(const spt_context *ctx, int option) {
     case SPT_OPT_GEMV16_SLOTS: return ctx->opt_gemv16_slots;
     case SPT_OPT_WAIT_LIMIT: return ctx->opt_wait_shift;
     case SPT_OPT_FAULT_STAGE: return ctx->opt_fault_stage;
+    case SPT_OPT_HOST_GRAPHS: return ctx->opt_host_graphs;
   }
   return -1;
 }
@@ -1240,7 +1342,7 @@ static spt_status arena_create_impl(spt_context *ctx, const spt_reader *readers,
   if (e0 < 0 || e1 > E || e0 >= e1) return fail(ctx, SPT_ERR_DIMENSIONS, "expert range [%lld, %lld) outside [0, %lld)",
                                                 (long long)e0, (long long)e1, (long long)E);
   const int64_t ne = e1 - e0;  // resident experts
-  spt_arena *a = new spt_arena();
+  spt_arena *a = new_arena();
   a->device = ctx->device;
   a->cfg = *cfg;
   a->expert_begin = e0;
@@ -1387,7 +1489,7 @@ static spt_status synth_create_impl(spt_context *ctx, const spt_moe_config *cfg,
                                                 (long long)e0, (long long)e1, (long long)E);
   const int64_t ne = e1 - e0;  // resident experts
   if (flags == 0) flags = SPT_ARENA_GEMV;
-  spt_arena *a = new spt_arena();
+  spt_arena *a = new_arena();
   a->device = ctx->device;
   a->cfg = *cfg;
   a->expert_begin = e0;
@@ -2098,8 +2200,15 @@ struct NcclApi {
 const NcclApi &nccl() {
   static NcclApi api = [] {
     NcclApi a;
-    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    // An NCCL already in the process (PyTorch's) is found by its soname and
+    // shared.
+    // SPT_NCCL_LIBRARY names the NCCL to use (the Python mirror points it at
+    // PyTorch's, so that a later `import torch` finds the same one already
+    // loaded under the soname it links against).
+    void *h = nullptr;
+    if (const char *path = getenv("SPT_NCCL_LIBRARY")) h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
     if (!h) {
       a.why = std::string("cannot open libnccl.so.2: ") + dlerror();
       return a;
@@ -2180,8 +2289,13 @@ spt_status ep_abort(spt_ep *ep, const char *what) {
               (long long)ep->timeout_ms);
 }
 
+// The waits spin for their first couple of milliseconds (an exchange's
+// enqueue normally completes within microseconds, and a sleep would put tens
+// of microseconds on every call), then back off to short sleeps.
+constexpr int64_t kSpinMs = 2;
+
 spt_status wait_comm(spt_ep *ep, const char *what) {
-  const int64_t deadline = now_ms() + ep->timeout_ms;
+  const int64_t start = now_ms(), deadline = start + ep->timeout_ms;
   for (;;) {
     ncclResult_t state = ncclSuccess;
     ncclResult_t r = nccl().comm_get_async_error(ep->comm, &state);
@@ -2193,19 +2307,21 @@ spt_status wait_comm(spt_ep *ep, const char *what) {
       ep->broken = true;
       return st;
     }
-    if (now_ms() > deadline) return ep_abort(ep, what);
-    usleep(50);
+    const int64_t t = now_ms();
+    if (t > deadline) return ep_abort(ep, what);
+    if (t - start >= kSpinMs) usleep(50);
   }
 }
 
 spt_status wait_stream(spt_ep *ep, const char *what) {
-  const int64_t deadline = now_ms() + ep->timeout_ms;
+  const int64_t start = now_ms(), deadline = start + ep->timeout_ms;
   for (;;) {
     cudaError_t e = cudaStreamQuery(ep->ctx->stream);
     if (e == cudaSuccess) return SPT_OK;
     if (e != cudaErrorNotReady) return cuda_fail(ep->ctx, e, what);
-    if (now_ms() > deadline) return ep_abort(ep, what);
-    usleep(20);
+    const int64_t t = now_ms();
+    if (t > deadline) return ep_abort(ep, what);
+    if (t - start >= kSpinMs) usleep(20);
   }
 }
 
@@ -2227,8 +2343,8 @@ spt_status exchange(spt_ep *ep, const void *send, void *recv, int64_t width, siz
                              type, j, ep->comm, ctx->stream));
   }
   ncclResult_t r = api.group_end();
-  if (r != ncclSuccess && r != ncclInProgress)
-    return fail(ctx, SPT_ERR_NCCL, "ncclGroupEnd: %s", api.error_string(r));
+  if (r == ncclSuccess) return SPT_OK;
+  if (r != ncclInProgress) return fail(ctx, SPT_ERR_NCCL, "ncclGroupEnd: %s", api.error_string(r));
   return wait_comm(ep, "exchange");
 }
 
@@ -2269,8 +2385,8 @@ spt_status exchange_fixed(spt_ep *ep, std::initializer_list<FixedItem> items) {
                              ep->comm, ctx->stream));
     }
   ncclResult_t r = api.group_end();
-  if (r != ncclSuccess && r != ncclInProgress)
-    return fail(ctx, SPT_ERR_NCCL, "ncclGroupEnd: %s", api.error_string(r));
+  if (r == ncclSuccess) return SPT_OK;
+  if (r != ncclInProgress) return fail(ctx, SPT_ERR_NCCL, "ncclGroupEnd: %s", api.error_string(r));
   return wait_comm(ep, "exchange");
 }
 

@@ -355,3 +355,31 @@ def test_gpt_oss_large_batch_properties(ctx, gpt_oss):
     xp = x.reshape(T, 2880)[perm].ravel()
     gp = ctx.forward_moe_batch(arena, xp, T).reshape(T, 2880)
     assert bits_equal(gp, got[perm]).all()
+
+
+def test_host_call_graph_replay_matches_launches(ctx):
+    """spt_forward_moe_batch replays a captured graph of its device work from
+    the second call with the same arena, layer and batch on: the outputs of
+    replays equal plain launches bit for bit, on every expert path, and a
+    new batch size or option captures anew."""
+    cfg = spt.Config(512, 256, 16, 4)
+    arena = ctx.synthetic_arena(cfg, spt.SynthParams(seed=31), flags=spt.ARENA_GEMV | spt.ARENA_MMA)
+    try:
+        for path in (spt.PATH_EXACT, spt.PATH_MMA, spt.PATH_GEMV16, spt.PATH_AUTO):
+            ctx.set_path(path)
+            for T in (1, 3, 40):
+                ctx.set_option(spt.OPT_HOST_GRAPHS, 0)
+                want = ctx.forward_moe_batch(arena, spt.synth_normal_host(T, 9, T * 512), T)
+                ctx.set_option(spt.OPT_HOST_GRAPHS, 1)
+                for rep in range(4):  # plain, capture, replay, replay
+                    x = spt.synth_normal_host(T + 100 * rep, 9, T * 512)
+                    got = ctx.forward_moe_batch(arena, x, T)
+                    ctx.set_option(spt.OPT_HOST_GRAPHS, 0)
+                    ref = ctx.forward_moe_batch(arena, x, T)
+                    ctx.set_option(spt.OPT_HOST_GRAPHS, 1)
+                    assert bits_equal(got, ref).all(), (path, T, rep)
+                # the first input again, through the replayed graph
+                assert bits_equal(ctx.forward_moe_batch(arena, spt.synth_normal_host(T, 9, T * 512), T), want).all()
+    finally:
+        ctx.set_path(spt.PATH_AUTO)
+        arena.close()
