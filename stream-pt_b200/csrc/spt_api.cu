@@ -543,7 +543,8 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
   const bool fp4 = mma_fp4(bn);
-  const int mt_gu = L.gu_mma.mtiles, mt_dn = L.dn_mma.mtiles;
+  // work units per token tile (row tiles, or groups of them for 128-token tiles)
+  const int mt_gu = mma_row_units(bn, L.gu_mma.mtiles), mt_dn = mma_row_units(bn, L.dn_mma.mtiles);
   // one stage size for both GEMMs (they share the activation map cache), from
   // an estimate of the down GEMM's row tiles: its host bound halved (the bound
   // puts every slot on its own expert and counts partial token tiles twice)
@@ -553,8 +554,9 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const bool wide = ks == kMmaStageTilesWide && fp4;
   MmaLaunch &g = *gu;
   g.ks = ks;
-  g.tmap_a = fp4 ? (wide ? L.gu_mma.tmap_pw : L.gu_mma.tmap_p) : L.gu_mma.tmap;
+  g.tmap_a = fp4 ? (wide ? L.gu_mma.tmap_pw : L.gu_mma.tmap_p) : L.gu_mma.tmap_g;
   g.tmap_a1 = fp4 ? L.gu_mma.tmap_p1 : L.gu_mma.tmap;
+  g.tmap_sfa = L.gu_mma.tmap_sfg;
   if (!act_maps(ctx, 0, ctx->qx.as<uint8_t>(), kph, rb, bn, ks, &g.tmap_b, &g.tmap_b1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
   g.w = L.gu_mma.w;
@@ -562,7 +564,7 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.sfb = ctx->sfx.as<uint8_t>();
   g.rows = L.gu_mma.rows;
   g.kp = kph;
-  g.mtiles = mt_gu;
+  g.mtiles = L.gu_mma.mtiles;
   g.ktiles = kph / kMmaKT;
   g.rb = rb;
   g.offsets = ctx->offsets.as<int32_t>();
@@ -583,8 +585,9 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.fault_stage = ctx->opt_fault_stage;
   MmaLaunch &d = *dn;
   d = g;
-  d.tmap_a = fp4 ? (wide ? L.dn_mma.tmap_pw : L.dn_mma.tmap_p) : L.dn_mma.tmap;
+  d.tmap_a = fp4 ? (wide ? L.dn_mma.tmap_pw : L.dn_mma.tmap_p) : L.dn_mma.tmap_g;
   d.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
+  d.tmap_sfa = L.dn_mma.tmap_sfg;
   if (!act_maps(ctx, 1, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks, &d.tmap_b, &d.tmap_b1))
     return fail(ctx, SPT_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed");
   d.w = L.dn_mma.w;
@@ -592,7 +595,7 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   d.sfb = ctx->sfa.as<uint8_t>();
   d.rows = L.dn_mma.rows;
   d.kp = kpd;
-  d.mtiles = mt_dn;
+  d.mtiles = L.dn_mma.mtiles;
   d.ktiles = kpd / kMmaKT;
   d.tile_off = ctx->tile_dn.as<int32_t>();
   d.max_tiles = (int)std::min<int64_t>((int64_t)mt_dn * (na_max + S / bn + 1), 1 << 30);
@@ -744,8 +747,8 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   if (use_mma) {
     plan.bn = bn_hint ? bn_hint : pick_bn(ctx, T, K, E);
     ctx->last_bn = plan.bn;
-    plan.mt_gu = L.gu_mma.mtiles;
-    plan.mt_dn = L.dn_mma.mtiles;
+    plan.mt_gu = mma_row_units(plan.bn, L.gu_mma.mtiles);
+    plan.mt_dn = mma_row_units(plan.bn, L.dn_mma.mtiles);
     plan.pad_off = ctx->pad_off.as<int32_t>();
     plan.tile_gu = ctx->tile_gu.as<int32_t>();
     plan.tile_dn = ctx->tile_dn.as<int32_t>();

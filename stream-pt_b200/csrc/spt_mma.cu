@@ -61,8 +61,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 bool mma_encode_weights(MmaMatrix *m) {
   auto fn = encode_fn();
-  if (!fn || !m->w) return false;
-  if (m->kp % 128 != 0 || (reinterpret_cast<uintptr_t>(m->w) & 31) != 0) return false;
+  if (!fn || !m->w || !m->sf) return false;
+  if (m->kp % 128 != 0 || ((reinterpret_cast<uintptr_t>(m->w) | reinterpret_cast<uintptr_t>(m->sf)) & 31) != 0)
+    return false;
   // Tile-major: every 128-row x 128-element box is one contiguous 8 KB block,
   // so the map is [rows = boxes * 128][128 elements] with a 64-byte pitch.
   const uint64_t boxes = (uint64_t)m->experts * m->mtiles * (m->kp / kMmaKT);
@@ -88,7 +89,26 @@ bool mma_encode_weights(MmaMatrix *m) {
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;
   }
-  return true;
+  // Row-tile groups for 128-token tiles: the same bytes as [row tiles][K
+  // tiles][128 rows][64 B]; a box takes one K tile of kPrefillRowTiles row
+  // tiles (past the last row tile of the matrix the copy fills zeros).
+  const cuuint64_t kt_n = (cuuint64_t)(m->kp / kMmaKT), runs = (cuuint64_t)m->experts * m->mtiles;
+  cuuint64_t dims4[4] = {(cuuint64_t)kMmaKT, (cuuint64_t)kMmaM, kt_n, runs};
+  cuuint64_t strides4[3] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)(kMmaKT / 2) * kMmaM,
+                            kt_n * (kMmaKT / 2) * kMmaM};
+  cuuint32_t box4[4] = {128, 128, 1, (cuuint32_t)kPrefillRowTiles};
+  cuuint32_t estr4[4] = {1, 1, 1, 1};
+  r = fn(&m->tmap_g, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, m->w, dims4, strides4, box4, estr4,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  cuuint64_t sdims[3] = {128, kt_n, runs};  // 32-bit words: an atom is 128 of them
+  cuuint64_t sstrides[2] = {512, kt_n * 512};
+  cuuint32_t sbox[3] = {128, 1, (cuuint32_t)kPrefillRowTiles};
+  r = fn(&m->tmap_sfg, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, m->sf, sdims, sstrides, sbox, estr4,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, int ktiles) {
@@ -553,7 +573,10 @@ __device__ __forceinline__ TileInfo tile_info(const TileTables &tt, int tile, in
 // MMAs per K tile).  FP8: kind::mxf8f6f4, weights unpacked by the TMA
 // (SW128), kActTerms e4m3 terms each its own N = BN operand with its own atom
 // (four K = 32 MMAs per term per K tile).  KS: K tiles per pipeline stage.
-template <int BN, bool FP4, int KS>
+// MG row tiles share each activation K tile (FP8 mode: kPrefillRowTiles;
+// their MG accumulators are single-buffered), else one row tile per unit with
+// a double-buffered accumulator.
+template <int BN, bool FP4, int KS, int MG = 1>
 struct MmaShape {
   static constexpr int kA = FP4 ? kMmaM * 64 : kMmaM * 128;     // smem bytes of one weight K tile
   static constexpr int kATx = kMmaM * 64;                        // its transaction bytes (packed source)
@@ -565,33 +588,43 @@ struct MmaShape {
   static constexpr int kKSteps = FP4 ? 2 : 4;                    // MMAs (per term) per K tile
   static constexpr uint32_t kLayout = FP4 ? 4u : 2u;             // smem descriptor: SW64 / SW128
   static constexpr uint32_t kSbo = FP4 ? 512u : 1024u;           // 8-row swizzle atom
-  // stage: A[KS] | B[KS] | SFA[KS] | SFB[KS][kSfb]
-  static constexpr int kOffB = KS * kA;
+  // stage: A[KS][MG] | B[KS] | SFA[MG][KS] | SFB[KS][kSfb]
+  static constexpr int kOffB = KS * MG * kA;
   static constexpr int kOffSfa = kOffB + KS * kBt;
-  static constexpr int kOffSfb = kOffSfa + KS * 512;
+  static constexpr int kOffSfb = kOffSfa + KS * MG * 512;
   static constexpr int kStage = ((kOffSfb + KS * kSfb * 512) + 1023) / 1024 * 1024;
   static constexpr int kStages = (200 * 1024) / kStage > 16 ? 16 : (200 * 1024) / kStage;
-  static constexpr int kAccStride = (kN + 31) / 32 * 32;  // TMEM columns between the two accumulators
-  static constexpr int kAccCols = 2 * kAccStride;   // double-buffered accumulator
-  static constexpr int kSfCols = KS * (4 + 4 * kSfb);  // SFA + SFB atoms of every K tile of a stage
+  static constexpr int kAccStride = (kN + 31) / 32 * 32;  // TMEM columns of one accumulator
+  static constexpr int kAccBufs = MG > 1 ? 1 : 2;         // accumulator sets (double-buffered with one row tile)
+  static constexpr int kAccCols = kAccBufs * MG * kAccStride;
+  static constexpr int kSfCols = KS * (4 * MG + 4 * kSfb);  // SFA + SFB atoms of every K tile of a stage
   static constexpr int kCols = (kAccCols + kSfCols <= 32) ? 32
                                : (kAccCols + kSfCols <= 64) ? 64
                                : (kAccCols + kSfCols <= 128) ? 128
                                : (kAccCols + kSfCols <= 256) ? 256 : 512;
-  static constexpr int kTxTile = kATx + kBt + 512 + kSfb * 512;
+  // transaction bytes of one K tile of a unit with nm row tiles
+  static __device__ __forceinline__ int tx_ktile(int nm) { return nm * (kATx + 512) + kBt + kSfb * 512; }
   static constexpr int kRing = kStages * kStage;
   static constexpr int kSmem = kRing + 1024 /*align*/ + 256 /*barriers*/ + (int)sizeof(TileTables);
   static_assert(kBTerm % 512 == 0 && kA % 1024 == 0, "swizzle atoms must stay aligned");
   static_assert(kAccCols + kSfCols <= 512, "TMEM columns");
+  static_assert(kStages >= 2, "stage ring");
+  static_assert(MG == 1 || (KS == 1 && !FP4), "row-tile groups: one K tile per stage, 128-token tiles");
+  // epilogue warps: two per TMEM lane quadrant (each takes half of the
+  // columns) with row-tile groups, whose single-buffered accumulators wait
+  // for the epilogue; one per quadrant otherwise
+  static constexpr int kEpiWarps = MG > 1 ? 8 : 4;
+  static constexpr int kThreads = 32 * (2 + kEpiWarps);
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 // One GEMM CTA: the shared-memory stage ring, its mbarriers, the TMEM
 // accumulators, and the three roles.  Each role runs in its own thread(s)
 // and keeps its ring slot, parity and tile count in that thread's copy of
 // this struct.
-template <int BN, bool FP4, int KS>
+template <int BN, bool FP4, int KS, int MG = 1>
 struct GemmCta {
-  using S = MmaShape<BN, FP4, KS>;
+  using S = MmaShape<BN, FP4, KS, MG>;
   static constexpr int kBarBytes = 256;
   static_assert((2 * S::kStages + 5) * 8 + 4 <= kBarBytes, "mbarrier area");
   uint8_t *smem;  // 1024-byte aligned ring
@@ -619,7 +652,7 @@ struct GemmCta {
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 128);
+      mbar_init(&acce[i], 32 * S::kEpiWarps);
     }
     mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -660,13 +693,16 @@ struct GemmCta {
     uint32_t slot_phase = 0;  // bit i: the parity of that stage
     int stage = 0;
     bool ok = true;
-    for (int d = 1; d < a.prefetch; ++d) prefetch_tile(blockIdx.x + d * gridDim.x);
+    const int pf = MG == 1 ? a.prefetch : 0;  // whole-tile prefetch: one row tile per unit only
+    for (int d = 1; d < pf; ++d) prefetch_tile(blockIdx.x + d * gridDim.x);
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
       const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
-      const uint8_t *sfa = a.sfa + (((size_t)t.e * a.mtiles + t.mt) * a.ktiles) * 512;
+      const int mt0 = t.mt * MG;                    // first row tile of the unit
+      const int nm = min(MG, a.mtiles - mt0);       // its row tiles
+      const uint8_t *sfa = a.sfa + (((size_t)t.e * a.mtiles + mt0) * a.ktiles) * 512;
       const uint8_t *sfb = a.sfb + ((size_t)(t.rowb / kMmaM) * a.ktiles) * (S::kSfb * 512);
-      const int box0 = (t.e * a.mtiles + t.mt) * kt_n;
-      if (a.prefetch > 0) prefetch_tile(tile + a.prefetch * gridDim.x);
+      const int box0 = (t.e * a.mtiles + mt0) * kt_n;
+      if (pf > 0) prefetch_tile(tile + pf * gridDim.x);
       for (int kt = 0; kt < kt_n; kt += KS, ++stage) {
         if (!mbar_wait(&empty[s], phase ^ 1u, a.err, 1, a.wait_shift)) {
           ok = false;
@@ -675,24 +711,34 @@ struct GemmCta {
         const int nk = min(KS, kt_n - kt);
         if (!(a.fault_stage == stage && blockIdx.x == 0)) {
           uint8_t *st = smem + s * S::kStage;
-          mbar_expect_tx(&full[s], nk * S::kTxTile);
+          // a group short of MG row tiles still copies MG (the extra ones,
+          // zeros or the next expert's rows, are never multiplied)
+          mbar_expect_tx(&full[s], MG > 1 ? S::tx_ktile(MG) : nk * S::tx_ktile(nm));
           // one operation per operand for the whole stage; single K tiles with
           // the one-box maps at the end of an odd K
           const bool whole = nk == KS;
           const CUtensorMap *ma = whole ? &a.tmap_a : &a.tmap_a1;
           const CUtensorMap *mb = whole ? &a.tmap_b : &a.tmap_b1;
-          for (int j = 0; j < (whole ? 1 : nk); ++j) {
-            uint8_t *aj = st + j * S::kA;
-            uint8_t *bj = st + S::kOffB + j * S::kBt;
-            if (FP4) {
-              tma_load_3d(ma, aj, &full[s], 0, 0, box0 + kt + j);
-              tma_load_3d(mb, bj, &full[s], 0, t.rowb, kt + j);
-            } else {
-              tma_load_2d(ma, aj, &full[s], 0, (box0 + kt + j) * kMmaM);
-              tma_load_4d(mb, bj, &full[s], 0, t.rowb, 0, kt + j);
+          if constexpr (MG > 1) {
+            // one K tile (KS == 1) of MG row tiles and their scale atoms in
+            // one copy each
+            tma_load_4d(&a.tmap_a, st, &full[s], 0, 0, kt, t.e * a.mtiles + mt0);
+            tma_load_4d(mb, st + S::kOffB, &full[s], 0, t.rowb, 0, kt);
+            tma_load_3d(&a.tmap_sfa, st + S::kOffSfa, &full[s], 0, kt, t.e * a.mtiles + mt0);
+          } else {
+            for (int j = 0; j < (whole ? 1 : nk); ++j) {
+              uint8_t *aj = st + j * S::kA;
+              uint8_t *bj = st + S::kOffB + j * S::kBt;
+              if (FP4) {
+                tma_load_3d(ma, aj, &full[s], 0, 0, box0 + kt + j);
+                tma_load_3d(mb, bj, &full[s], 0, t.rowb, kt + j);
+              } else {
+                tma_load_2d(ma, aj, &full[s], 0, (box0 + kt + j) * kMmaM);
+                tma_load_4d(mb, bj, &full[s], 0, t.rowb, 0, kt + j);
+              }
             }
+            bulk_load(st + S::kOffSfa, sfa + (size_t)kt * 512, nk * 512, &full[s]);
           }
-          bulk_load(st + S::kOffSfa, sfa + (size_t)kt * 512, nk * 512, &full[s]);
           bulk_load(st + S::kOffSfb, sfb + (size_t)kt * S::kSfb * 512, nk * S::kSfb * 512, &full[s]);
           issued |= 1u << s;
           slot_phase = (slot_phase & ~(1u << s)) | (phase << s);
@@ -719,8 +765,8 @@ struct GemmCta {
   // Descriptors are built once; per stage and K-step only their 14-bit start
   // address fields advance (stage bases are 1024-byte aligned and the whole
   // ring lies below 256 KB, so the adds never carry out of the field).
-  __device__ bool mma(const MmaLaunch &a, int n_tiles) {
-    const uint32_t sfa_t = tmem + S::kAccCols;  // scale-factor columns after the two accumulators
+  __device__ bool mma(const MmaLaunch &a, const TileTables &tt, int n_active, int n_tiles) {
+    const uint32_t sfa_t = tmem + S::kAccCols;  // scale-factor columns after the accumulators
     const uint32_t base = smem_u32(smem);
     const uint64_t a_desc0 = smem_desc(base, S::kSbo, S::kLayout);
     const uint64_t b_desc0 = smem_desc(base + S::kOffB, S::kSbo, S::kLayout);
@@ -735,12 +781,12 @@ struct GemmCta {
       idesc[ks] = FP4 ? idesc_mxf4(S::kN, 2 * ks, 2 * ks) : idesc_mxf8f6f4(S::kN, ks, ks);
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const int kt_lo = 0, kt_hi = a.ktiles;
-      const int buf = local & 1;
-      const uint32_t accph = (uint32_t)(local >> 1) & 1u;
+      const int nm = MG == 1 ? 1 : min(MG, a.mtiles - tile_info<BN>(tt, tile, n_active, a.mtiles).mt * MG);
+      const int buf = local % S::kAccBufs;
+      const uint32_t accph = (uint32_t)(local / S::kAccBufs) & 1u;
       if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2, a.wait_shift)) return false;
       tc_fence_after();
-      const uint32_t d_tmem = tmem + buf * S::kAccStride;
-      uint32_t acc = 0u;
+      const uint32_t d_tmem = tmem + buf * MG * S::kAccStride;
       for (int kt = kt_lo; kt < kt_hi; kt += KS) {
         if (!mbar_wait(&full[s], phase, a.err, 3, a.wait_shift)) return false;
         tc_fence_after();
@@ -752,8 +798,10 @@ struct GemmCta {
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
           if (j < nk) {
-            const uint32_t sfa_j = sfa_t + j * (4 + 4 * S::kSfb), sfb_j = sfa_j + 4;
-            tc_cp_sf(sfa_j, sfa_desc0 + so + 32 * j);
+            const uint32_t sf_j = sfa_t + j * (4 * MG + 4 * S::kSfb), sfb_j = sf_j + 4 * MG;
+#pragma unroll
+            for (int m = 0; m < MG; ++m)
+              if (m < nm) tc_cp_sf(sf_j + 4 * m, sfa_desc0 + so + 32 * (m * KS + j));
 #pragma unroll
             for (int term = 0; term < S::kSfb; ++term)
               tc_cp_sf(sfb_j + 4 * term, sfb_desc0 + so + 32 * (j * S::kSfb + term));
@@ -762,21 +810,27 @@ struct GemmCta {
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
           if (j < nk) {
-            const uint32_t sfa_j = sfa_t + j * (4 + 4 * S::kSfb), sfb_j = sfa_j + 4;
-            const uint64_t ad = a_desc0 + so + (uint64_t)j * kA16;
+            const uint32_t sf_j = sfa_t + j * (4 * MG + 4 * S::kSfb), sfb_j = sf_j + 4 * MG;
             const uint64_t bd = b_desc0 + so + (uint64_t)j * kBt16;
 #pragma unroll
-            for (int ks = 0; ks < S::kKSteps; ++ks) {
-              const uint32_t id = FP4 ? 2u * ks : (uint32_t)ks;
+            for (int m = 0; m < MG; ++m) {
+              if (m >= nm) continue;
+              const uint64_t ad = a_desc0 + so + (uint64_t)(j * MG + m) * kA16;
+              const uint32_t dm = d_tmem + m * S::kAccStride, sfa_m = sf_j + 4 * m;
 #pragma unroll
-              for (int term = 0; term < (FP4 ? 1 : kActTerms); ++term) {
-                if (FP4)
-                  tc_mma_fp4(d_tmem, ad + 2 * ks, bd + 2 * ks, idesc[ks], sfa_j | (id << 30),
-                             sfb_j | (id << 30), acc);
-                else
-                  tc_mma(d_tmem, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_j | (id << 30),
-                         (sfb_j + 4 * term) | (id << 30), acc);
-                acc = 1u;
+              for (int ks = 0; ks < S::kKSteps; ++ks) {
+                const uint32_t id = FP4 ? 2u * ks : (uint32_t)ks;
+#pragma unroll
+                for (int term = 0; term < (FP4 ? 1 : kActTerms); ++term) {
+                  // the unit's first product into each accumulator overwrites it
+                  const uint32_t acc = (kt == kt_lo && j == 0 && ks == 0 && term == 0) ? 0u : 1u;
+                  if (FP4)
+                    tc_mma_fp4(dm, ad + 2 * ks, bd + 2 * ks, idesc[ks], sfa_m | (id << 30), sfb_j | (id << 30),
+                               acc);
+                  else
+                    tc_mma(dm, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_m | (id << 30),
+                           (sfb_j + 4 * term) | (id << 30), acc);
+                }
               }
             }
           }
@@ -807,17 +861,21 @@ struct GemmCta {
                            int lane) {
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_local = quad * 32 + lane;
+    const int half = S::kEpiWarps == 8 ? (warp - 2) / 4 : 0;  // column half of this warp (8 epilogue warps)
+    constexpr int kCols = S::kEpiWarps == 8 ? BN / 2 : BN;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
-      const int buf = local & 1;
-      const uint32_t accph = (uint32_t)(local >> 1) & 1u;
+      const int buf = local % S::kAccBufs;
+      const uint32_t accph = (uint32_t)(local / S::kAccBufs) & 1u;
       if (!mbar_wait(&accf[buf], accph, a.err, 5, a.wait_shift)) return false;
       tc_fence_after();
-      const int r = t.mt * kMmaM + row_local;
+      const int nm = min(MG, a.mtiles - t.mt * MG);
+      for (int m = 0; m < nm; ++m) {
+      const int r = (t.mt * MG + m) * kMmaM + row_local;
       constexpr int kC = BN < 16 ? BN : 16;  // accumulator columns per TMEM load
-      for (int c0 = 0; c0 < BN; c0 += kC) {
+      for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += kC) {
         float v[kC];
-        const uint32_t col = tmem + (uint32_t)(buf * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
+        const uint32_t col = tmem + (uint32_t)((buf * MG + m) * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
         if constexpr (FP4 && BN == 8 && kFp4Terms == 4) {
           // the term partial sums are consecutive columns: one round trip
           float w[kFp4Terms * 8];
@@ -850,7 +908,7 @@ struct GemmCta {
             const float val = v[j] + bias;
             const float other = __shfl_xor_sync(0xffffffffu, val, 1);
             if (!is_up && c0 + j < t.nvalid && d < a.out_rows)
-              a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + d] = swiglu_ref(val, other);
+              a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + d] = swiglu_f32(val, other);
           }
         } else if (r < a.out_rows) {
           const float bias = a.bias0 ? a.bias0[(size_t)t.e * a.out_rows + r] : 0.0f;
@@ -859,6 +917,7 @@ struct GemmCta {
             if (c0 + j < t.nvalid) a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + r] = v[j] + bias;
         }
       }
+      }
       tc_fence_before();
       mbar_arrive(&acce[buf]);
     }
@@ -866,9 +925,9 @@ struct GemmCta {
   }
 };
 
-template <int BN, bool FP4, int KS>
-__global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ MmaLaunch a) {
-  using G = GemmCta<BN, FP4, KS>;
+template <int BN, bool FP4, int KS, int MG>
+__global__ void __launch_bounds__(MmaShape<BN, FP4, KS, MG>::kThreads, 1) k_mma_gemm(const __grid_constant__ MmaLaunch a) {
+  using G = GemmCta<BN, FP4, KS, MG>;
   using S = typename G::S;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -904,7 +963,7 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
   if (warp == 0 && lane == 0) {
     g.produce(a, tt, n_active, n_tiles);
   } else if (warp == 1 && lane == 0) {
-    g.mma(a, n_tiles);
+    g.mma(a, tt, n_active, n_tiles);
     g.drain_mma(a.err, a.wait_shift);
   } else if (warp >= 2) {
     g.epilogue(a, tt, n_active, n_tiles, warp, lane);
@@ -915,14 +974,14 @@ __global__ void __launch_bounds__(192, 1) k_mma_gemm(const __grid_constant__ Mma
   if (warp == 1) g.dealloc_tmem();
 }
 
-template <int BN, bool FP4, int KS>
+template <int BN, bool FP4, int KS, int MG = 1>
 cudaError_t launch_gemm_bn(const MmaLaunch &a, int sm_count, cudaStream_t s) {
-  using Sh = MmaShape<BN, FP4, KS>;
-  cudaError_t e = opt_in_smem(k_mma_gemm<BN, FP4, KS>, Sh::kSmem);
+  using Sh = MmaShape<BN, FP4, KS, MG>;
+  cudaError_t e = opt_in_smem(k_mma_gemm<BN, FP4, KS, MG>, Sh::kSmem);
   if (e != cudaSuccess) return e;
   int grid = a.max_tiles < sm_count ? a.max_tiles : sm_count;
   if (grid < 1) grid = 1;
-  return launch_pdl(k_mma_gemm<BN, FP4, KS>, dim3(grid), dim3(192), (size_t)Sh::kSmem, s, a);
+  return launch_pdl(k_mma_gemm<BN, FP4, KS, MG>, dim3(grid), dim3(Sh::kThreads), (size_t)Sh::kSmem, s, a);
 }
 
 }  // namespace
@@ -973,7 +1032,7 @@ cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream
   if (bn == 8 && a.ks == kMmaStageTilesWide) return launch_gemm_bn<8, true, kMmaStageTilesWide>(a, sm_count, s);
   if (bn == 8 && a.ks == kMmaStageTilesFp4) return launch_gemm_bn<8, true, kMmaStageTilesFp4>(a, sm_count, s);
   if (bn == 16 && a.ks == kMmaStageTilesFp4) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
-  if (bn == 128) return launch_gemm_bn<128, false, 1>(a, sm_count, s);
+  if (bn == 128) return launch_gemm_bn<128, false, 1, kPrefillRowTiles>(a, sm_count, s);
   return cudaErrorInvalidValue;
 }
 

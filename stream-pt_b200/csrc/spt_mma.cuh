@@ -53,6 +53,15 @@ constexpr int kMmaStageTilesFp4 = 4;  // K tiles per pipeline stage, FP4 mode
 // (three stages in the ring, fewer copy operations per byte); measured on
 // B200: c1 +2 %, c4 +2.6 %, but c0 (one or two tiles per SM) -4 %.
 constexpr int kMmaStageTilesWide = 6;
+// 128-token tiles: each CTA unit covers this many 128-row weight tiles of
+// one expert against one token tile, so every activation K tile it loads
+// (3 e4m3 terms, 48 KB) feeds three row tiles' MMAs instead of one; the
+// shared-memory and TMEM copy traffic per output falls by about half.
+constexpr int kPrefillRowTiles = 3;
+// Units of one token tile: row tiles, or groups of kPrefillRowTiles of them.
+inline int mma_row_units(int bn, int mtiles) {
+  return bn == 128 ? (mtiles + kPrefillRowTiles - 1) / kPrefillRowTiles : mtiles;
+}
 
 struct MmaMatrix {
   uint8_t *w = nullptr;      // packed e2m1 rows
@@ -66,6 +75,12 @@ struct MmaMatrix {
   alignas(64) CUtensorMap tmap_p;  // 3D [64 B, 128 rows, boxes] UINT8, box 64x128xkMmaStageTilesFp4, SW64 (packed)
   alignas(64) CUtensorMap tmap_p1; // same, one box
   alignas(64) CUtensorMap tmap_pw; // same, kMmaStageTilesWide boxes
+  // 128-token tiles: one K tile of kPrefillRowTiles consecutive row tiles in
+  // one copy each -- 4D [128 elements, 128 rows, K tiles, row tiles]
+  // 16U4_ALIGN16B (unpacked, SW128), and their scale atoms, 3D [128 words,
+  // K tiles, row tiles] UINT32
+  alignas(64) CUtensorMap tmap_g;
+  alignas(64) CUtensorMap tmap_sfg;
 };
 
 // Per-call operands of one grouped GEMM launch.  Every copy operation costs
@@ -78,6 +93,7 @@ struct MmaLaunch {
   alignas(64) CUtensorMap tmap_a1;  // weights, 1 box
   alignas(64) CUtensorMap tmap_b;   // activations, ks K tiles x all terms
   alignas(64) CUtensorMap tmap_b1;  // activations, 1 K tile x all terms
+  alignas(64) CUtensorMap tmap_sfa; // scale atoms of a row-tile group (MmaMatrix::tmap_sfg), 128-token tiles
   int ks = 1;                       // K tiles per pipeline stage
   const uint8_t *w = nullptr;        // packed weights (tile-major), for L2 prefetch
   const uint8_t *sfa = nullptr;
