@@ -621,10 +621,10 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   int rb = 0;
   spt_status st = build_gemms(ctx, L, c, T, bn, &g, &dn, &rb);
   if (st) return st;
-  SPT_CUDA(ctx, launch_quantize_act(x, H, ctx->perm.as<int32_t>(), K, true, ctx->offsets.as<int32_t>(),
-                                    ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
-                                    ctx->meta.as<int32_t>(), (int)S, H, g.kp, rb, bn, ctx->qx.as<uint8_t>(),
-                                    ctx->sfx.as<uint8_t>(), s));
+  // each token's row once, stored at every position it was dispatched to
+  SPT_CUDA(ctx, launch_quantize_tokens(x, H, (int)T, K, ctx->slot_pos.as<int32_t>(), ctx->offsets.as<int32_t>(),
+                                       ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(), H, g.kp, rb, bn,
+                                       ctx->qx.as<uint8_t>(), ctx->sfx.as<uint8_t>(), s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[4], s));
   SPT_CUDA(ctx, launch_mma_gemm(g, bn, ctx->sm_count, s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[5], s));

@@ -274,57 +274,36 @@ __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
   return out;
 }
 
-// One (dispatch row, 128-element K tile) of the activation operand, one warp:
-// row j of its token tile, whose 128-row activation slot starts at `slot`;
-// 8 lanes per 32-element block, 4 elements per lane.  kCoherent reads the
-// source through L2 only (rows written earlier by the same kernel).
-template <bool FP4>
-__device__ __forceinline__ void quantize_vals(float4 v, int kt, int kt_n, int j, int slot, int bn, int rb,
-                                              uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int lane);
-
-template <bool FP4, bool kCoherent>
-__device__ __forceinline__ void quantize_ktile(const float *src_row, int K, int kt, int kt_n, int j, int slot,
-                                               int bn, int rb, uint8_t *__restrict__ q, uint8_t *__restrict__ sf,
-                                               int lane) {
-  const int sub = lane & 7;
-  const int b = kt * 4 + (lane >> 3);  // 32-element block of this lane group
-  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (b * 32 < K) {
-    const float4 *p = reinterpret_cast<const float4 *>(src_row + b * 32 + sub * 4);
-    v = kCoherent ? __ldcg(p) : *p;
-  }
-  quantize_vals<FP4>(v, kt, kt_n, j, slot, bn, rb, q, sf, lane);
-}
-
 // The terms of elements kt*128 + (lane/8)*32 + (lane%8)*4 + [0, 4) of one row
-// (values v), written as quantize_ktile describes.
+// (values v): per term the four codes (FP4: two bytes, FP8: four) and the
+// block's E8M0 exponent (shared by the 8 lanes of the block).
 template <bool FP4>
-__device__ __forceinline__ void quantize_vals(float4 v, int kt, int kt_n, int j, int slot, int bn, int rb,
-                                              uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int lane) {
-  const int sub = lane & 7;
-  const int b = kt * 4 + (lane >> 3);
-  constexpr int kTerms = FP4 ? kFp4Terms : kActTerms;
+struct Terms {
+  static constexpr int kN = FP4 ? kFp4Terms : kActTerms;
+  uint32_t code[kN];
+  int ex[kN];
+};
+
+template <bool FP4>
+__device__ __forceinline__ Terms<FP4> quantize_terms(float4 v) {
+  Terms<FP4> r;
   constexpr float kQmax = FP4 ? 6.0f : 448.0f;
-  const int64_t atom = (int64_t)(slot / kMmaM) * kt_n + kt;
   // not unrolled: the loop body is the code a cold instruction cache fetches
 #pragma unroll 1
-  for (int t = 0; t < kTerms; ++t) {
+  for (int t = 0; t < Terms<FP4>::kN; ++t) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int off = 4; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     const int ex = term_exponent(amax, kQmax, 1.0f / kQmax);
     const float inv = exp2i(-ex), sc = exp2i(ex);
     float vv[4] = {v.x, v.y, v.z, v.w};
-    const int m = FP4 ? t * bn + (j % bn) : (j % bn);  // row within the slot
     if constexpr (FP4) {
       const uint32_t c01 = e2m1x2(__fmul_rn(vv[0], inv), __fmul_rn(vv[1], inv));
       const uint32_t c23 = e2m1x2(__fmul_rn(vv[2], inv), __fmul_rn(vv[3], inv));
       const uint32_t codes[4] = {c01 & 15u, c01 >> 4, c23 & 15u, c23 >> 4};
 #pragma unroll
       for (int i = 0; i < 4; ++i) vv[i] = __fsub_rn(vv[i], __fmul_rn(e2m1_value(codes[i]), sc));
-      const int64_t row = (int64_t)kt * rb + slot + m;
-      *reinterpret_cast<uint16_t *>(q + row * (kMmaKT / 2) + (b % 4) * 16 + sub * 2) =
-          (uint16_t)(c01 | (c23 << 8));
+      r.code[t] = c01 | (c23 << 8);
     } else {
       uint32_t packed = 0;
 #pragma unroll
@@ -334,16 +313,75 @@ __device__ __forceinline__ void quantize_vals(float4 v, int kt, int kt_n, int j,
         vv[i] = __fsub_rn(vv[i], __fmul_rn(__half2float(__half(hr)), sc));
         packed |= (uint32_t)code << (8 * i);
       }
-      const int64_t row = ((int64_t)kt * kActTerms + t) * rb + slot + m;
-      *reinterpret_cast<uint32_t *>(q + row * kMmaKT + (b % 4) * 32 + sub * 4) = packed;
+      r.code[t] = packed;
     }
+    r.ex[t] = ex;
     v = make_float4(vv[0], vv[1], vv[2], vv[3]);
+  }
+  return r;
+}
+
+// Store the terms of one (dispatch row, 128-element K tile): row j of its
+// token tile, whose 128-row activation slot starts at `slot`; 8 lanes per
+// 32-element block, 4 elements per lane (the layouts of spt_mma.cuh).
+template <bool FP4>
+__device__ __forceinline__ void store_terms(const Terms<FP4> &r, int kt, int kt_n, int j, int slot, int bn, int rb,
+                                            uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int lane) {
+  const int sub = lane & 7;
+  const int b = kt * 4 + (lane >> 3);
+  const int64_t atom = (int64_t)(slot / kMmaM) * kt_n + kt;
+#pragma unroll
+  for (int t = 0; t < Terms<FP4>::kN; ++t) {
+    const int m = FP4 ? t * bn + (j % bn) : (j % bn);  // row within the slot
+    if constexpr (FP4) {
+      const int64_t row = (int64_t)kt * rb + slot + m;
+      *reinterpret_cast<uint16_t *>(q + row * (kMmaKT / 2) + (b % 4) * 16 + sub * 2) = (uint16_t)r.code[t];
+    } else {
+      const int64_t row = ((int64_t)kt * kActTerms + t) * rb + slot + m;
+      *reinterpret_cast<uint32_t *>(q + row * kMmaKT + (b % 4) * 32 + sub * 4) = r.code[t];
+    }
     if (sub == 0) {
       const int64_t a2 = FP4 ? atom : atom * kActTerms + t;
-      sf[a2 * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] = (uint8_t)(ex + 127);
+      sf[a2 * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] = (uint8_t)(r.ex[t] + 127);
     }
   }
 }
+
+template <bool FP4>
+__device__ __forceinline__ void quantize_vals(float4 v, int kt, int kt_n, int j, int slot, int bn, int rb,
+                                              uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int lane) {
+  store_terms<FP4>(quantize_terms<FP4>(v), kt, kt_n, j, slot, bn, rb, q, sf, lane);
+}
+
+// The tokens' rows, each quantized once and stored at every dispatch
+// position of the token (top_k slots, each in its expert's token tile): one
+// warp per (token, 128-element K tile).
+template <bool FP4>
+__global__ void k_quantize_tokens(const float *__restrict__ x, int64_t stride, int T, int top_k,
+                                  const int32_t *__restrict__ slot_pos, const int32_t *__restrict__ offsets,
+                                  const int32_t *__restrict__ pad_off, const int32_t *__restrict__ pos_expert,
+                                  int K, int kp, int rb, int bn, uint8_t *__restrict__ q, uint8_t *__restrict__ sf) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int kt_n = kp / kMmaKT;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int t = (int)(gw / kt_n), kt = (int)(gw - (int64_t)t * kt_n);
+  if (t >= T) return;
+  const int b = kt * 4 + (lane >> 3);
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (b * 32 < K) v = *reinterpret_cast<const float4 *>(x + (int64_t)t * stride + b * 32 + (lane & 7) * 4);
+  const Terms<FP4> r = quantize_terms<FP4>(v);
+  for (int k = 0; k < top_k; ++k) {
+    const int pos = slot_pos[(int64_t)t * top_k + k];
+    if (pos < 0) continue;
+    const int e = pos_expert[pos];
+    const int j = pos - offsets[e];
+    store_terms<FP4>(r, kt, kt_n, j, pad_off[e] + (j / bn) * kMmaM, bn, rb, q, sf, lane);
+  }
+}
+
+constexpr int kQuantKt = 4;  // K tiles per warp of k_quantize_act
 
 template <bool FP4>
 __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
@@ -351,20 +389,31 @@ __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
                                const int32_t *__restrict__ offsets, const int32_t *__restrict__ pad_off,
                                const int32_t *__restrict__ pos_expert, const int32_t *__restrict__ meta,
                                int S_max, int K, int kp, int rb, int bn,
-                               uint8_t *__restrict__ q, uint8_t *__restrict__ sf) {
+                               uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int ktw) {
   pdl_wait();
   pdl_trigger();
-  // One warp per (dispatch position, 128-element K tile).
+  // One warp per (dispatch position, group of ktw <= kQuantKt K tiles): the
+  // group's loads are all in flight before the first term is computed.
   const int lane = threadIdx.x & 31;
-  const int kt_n = kp / kMmaKT;
+  const int kt_n = kp / kMmaKT, groups = (kt_n + ktw - 1) / ktw;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int pos = (int)(gw / kt_n), kt = (int)(gw - (int64_t)pos * kt_n);
+  const int pos = (int)(gw / groups), kt0 = (int)(gw - (int64_t)pos * groups) * ktw;
   if (pos >= S_max || pos >= meta[1]) return;
   const int e = pos_expert[pos];
   const int j = pos - offsets[e];
   const int slot = pad_off[e] + (j / bn) * kMmaM;  // this token tile's 128-row slot
   const int64_t srow = gather ? (int64_t)(perm[pos] / top_k) : (int64_t)pos;
-  quantize_ktile<FP4, false>(src + srow * stride, K, kt, kt_n, j, slot, bn, rb, q, sf, lane);
+  const float *row = src + srow * stride;
+  float4 v[kQuantKt];
+#pragma unroll
+  for (int i = 0; i < kQuantKt; ++i) {
+    const int b = (kt0 + i) * 4 + (lane >> 3);
+    v[i] = (i < ktw && kt0 + i < kt_n && b * 32 < K) ? __ldcs(reinterpret_cast<const float4 *>(row + b * 32 + (lane & 7) * 4))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < kQuantKt; ++i)
+    if (i < ktw && kt0 + i < kt_n) quantize_vals<FP4>(v[i], kt0 + i, kt_n, j, slot, bn, rb, q, sf, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -1015,17 +1064,32 @@ cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t first_expert, 
   return cudaGetLastError();
 }
 
+cudaError_t launch_quantize_tokens(const float *x, int64_t stride, int T, int top_k, const int32_t *slot_pos,
+                                   const int32_t *offsets, const int32_t *pad_off, const int32_t *pos_expert, int K,
+                                   int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t warps = (int64_t)T * (kp / kMmaKT);
+  const int64_t blocks = (warps * 32 + threads - 1) / threads;
+  return launch_pdl(mma_fp4(bn) ? k_quantize_tokens<true> : k_quantize_tokens<false>, dim3((unsigned)blocks),
+                    dim3(threads), 0, s, x, stride, T, top_k, slot_pos, offsets, pad_off, pos_expert, K, kp, rb, bn,
+                    q, sf);
+}
+
 cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t *perm, int top_k,
                                 bool gather, const int32_t *offsets, const int32_t *pad_off,
                                 const int32_t *pos_expert, const int32_t *meta, int S_max, int K, int kp,
                                 int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s) {
   if (S_max <= 0) return cudaSuccess;
   const int threads = 256;
-  const int64_t warps = (int64_t)S_max * (kp / kMmaKT);
+  // large batches: several K tiles per warp (memory parallelism); small ones
+  // one (more warps)
+  const int ktw = S_max >= 2048 ? kQuantKt : 1;
+  const int64_t warps = (int64_t)S_max * ((kp / kMmaKT + ktw - 1) / ktw);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
   return launch_pdl(mma_fp4(bn) ? k_quantize_act<true> : k_quantize_act<false>, dim3((unsigned)blocks),
                     dim3(threads), 0, s, src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off, pos_expert, meta,
-                    S_max, K, kp, rb, bn, q, sf);
+                    S_max, K, kp, rb, bn, q, sf, ktw);
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {

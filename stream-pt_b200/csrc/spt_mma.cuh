@@ -164,6 +164,11 @@ cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t first_expert, 
 
 // Quantize rows to the three MXFP8 terms.  Source row of dispatch position
 // p: src[(gather ? perm[p]/top_k : p) * src_stride + k].
+// The same for T token rows quantized once each and stored at every dispatch
+// position of the token (slot_pos[t*top_k + r], -1: not dispatched).
+cudaError_t launch_quantize_tokens(const float *x, int64_t stride, int T, int top_k, const int32_t *slot_pos,
+                                   const int32_t *offsets, const int32_t *pad_off, const int32_t *pos_expert, int K,
+                                   int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s);
 cudaError_t launch_quantize_act(const float *src, int64_t src_stride, const int32_t *perm, int top_k,
                                 bool gather, const int32_t *offsets, const int32_t *pad_off,
                                 const int32_t *pos_expert, const int32_t *meta, int S_max, int K,
