@@ -266,8 +266,7 @@ spt_status spt_forward_moe_batch_device(spt_context *ctx, spt_arena *arena, int6
  * dimensions <= 4096, experts <= 256 (SPT_ERR_UNSUPPORTED otherwise); needs an
  * SPT_ARENA_GEMV arena.  spt_context_create looks up the array's device
  * address, which loads the library's device code and the array on that
- * device: create the context before reserving the rest of HBM (and before
- * any stream capture).  All calls share the array: calls that overlap on the
+ * device: create the context before reserving the rest of HBM.  All calls share the array: calls that overlap on the
  * GPU race and must be serialised.  The call's routing stays in the array, so
  * spt_last_routing and spt_stage_times refuse after it (until the next
  * allocating forward). */
