@@ -595,7 +595,8 @@ def measure(spt, torch, ctx, name, args, rank, world, local, steps, warmup, cloc
     dispatched = T * K if r.ep is None else ctx.last_dispatch()[1]
     gu_flops = 2.0 * (2 * D) * H * dispatched
     path, bn = ctx.last_expert_path()
-    kind = "kind::mxf4, 4 e2m1 activation terms" if bn <= 16 else "kind::mxf8f6f4, 3 e4m3 activation terms"
+    kind = ("kind::mxf8f6f4, 3 e4m3 activation terms" if bn > 16 and ctx.get_option(spt.OPT_PREFILL_FP8)
+            else "kind::mxf4, 4 e2m1 activation terms")
     kernel = {"gemv16": "k_gemv16<0> gate/up (e2m1 -> f16 in registers, mma.sync f16 -> f32, fused SwiGLU)",
               "tcgen05": f"k_mma_gemm<{bn}> gate/up (tcgen05 {kind}, fused SwiGLU)",
               "exact": "k_gemv gate/up (bit-exact CUDA-core MXFP4 GEMV, fused SwiGLU)"}[path]

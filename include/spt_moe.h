@@ -229,7 +229,11 @@ spt_status spt_context_set_path(spt_context *ctx, int path);
  *                         second call with the same arena, layer, batch and
  *                         options, and replay it afterwards (one launch
  *                         instead of five to eight); 0: plain launches
- *                         (SPT_HOST_GRAPHS) */
+ *                         (SPT_HOST_GRAPHS)
+ *   SPT_OPT_PREFILL_FP8   0 (default): 128-token tensor-core tiles take the
+ *                         activations as four e2m1 terms (kind::mxf4); 1:
+ *                         three e4m3 terms (kind::mxf8f6f4, about ten times
+ *                         finer, more time) (SPT_PREFILL_FP8) */
 #define SPT_OPT_TILE_TOKENS 1
 #define SPT_OPT_FUSED_SELECT 2
 #define SPT_OPT_L2_PREFETCH 3
@@ -237,6 +241,7 @@ spt_status spt_context_set_path(spt_context *ctx, int path);
 #define SPT_OPT_WAIT_LIMIT 5
 #define SPT_OPT_FAULT_STAGE 6
 #define SPT_OPT_HOST_GRAPHS 7
+#define SPT_OPT_PREFILL_FP8 8
 spt_status spt_context_set_option(spt_context *ctx, int option, int64_t value);
 int64_t spt_context_get_option(const spt_context *ctx, int option);
 

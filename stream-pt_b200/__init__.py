@@ -33,6 +33,7 @@ PATH_AUTO, PATH_EXACT, PATH_MMA, PATH_GEMV16 = 0, 1, 2, 3
 # spt_context_set_option (include/spt_moe.h)
 OPT_TILE_TOKENS, OPT_FUSED_SELECT, OPT_L2_PREFETCH, OPT_GEMV16_SLOTS, OPT_WAIT_LIMIT, OPT_FAULT_STAGE = 1, 2, 3, 4, 5, 6
 OPT_HOST_GRAPHS = 7
+OPT_PREFILL_FP8 = 8
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
 

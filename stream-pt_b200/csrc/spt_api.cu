@@ -87,6 +87,7 @@ struct spt_context {
   int opt_wait_shift = 31;      // bounded device waits give up after 2^shift clock cycles
   int opt_fault_stage = -1;     // failure injection: the tcgen05 producer skips this stage (tests)
   int opt_host_graphs = 1;      // replay repeated host calls from captured CUDA graphs
+  int opt_prefill_fp8 = 0;      // 128-token tiles: e4m3 activation terms instead of e2m1
   // Host-call graphs: the block's kernels captured once per (arena, layer,
   // batch, path and options) and replayed by the host entry points; `bufs`
   // is the device buffers the capture used (a grown buffer invalidates it).
@@ -108,6 +109,7 @@ struct spt_context {
   struct ActMaps {
     const void *q = nullptr;
     int kp = 0, rb = 0, bn = 0, ks = 0;
+    ActFmt fmt = ActFmt::kFp4Stack;
     CUtensorMap m, m1;
   } act_maps[2];
 };
@@ -504,9 +506,11 @@ int pick_mt(int64_t T, int64_t K, int64_t E) {
 bool act_maps(spt_context *ctx, int which, uint8_t *q, int kp, int rb, int bn, int ks, CUtensorMap *m,
               CUtensorMap *m1) {
   auto &c = ctx->act_maps[which];
-  if (c.q != q || c.kp != kp || c.rb != rb || c.bn != bn || c.ks != ks) {
+  const ActFmt f = mma_act_fmt(bn, ctx->opt_prefill_fp8 != 0);
+  if (c.q != q || c.kp != kp || c.rb != rb || c.bn != bn || c.ks != ks || c.fmt != f) {
     c.q = nullptr;
-    if (!mma_encode_acts(&c.m, q, kp, rb, bn, ks) || !mma_encode_acts(&c.m1, q, kp, rb, bn, 1)) return false;
+    if (!mma_encode_acts(&c.m, q, kp, rb, bn, f, ks) || !mma_encode_acts(&c.m1, q, kp, rb, bn, f, 1)) return false;
+    c.fmt = f;
     c.q = q;
     c.kp = kp;
     c.rb = rb;
@@ -542,7 +546,8 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const int64_t na_max = std::min<int64_t>(E, S);
   const int rb = (int)((int64_t)kMmaM * (S / bn + na_max + 1));
   const int kph = L.gu_mma.kp, kpd = L.dn_mma.kp;
-  const bool fp4 = mma_fp4(bn);
+  const ActFmt fmt = mma_act_fmt(bn, ctx->opt_prefill_fp8 != 0);
+  const bool fp4 = fmt == ActFmt::kFp4Stack;  // decode-sized tiles, several K tiles per stage
   // work units per token tile (row tiles, or groups of them for 128-token tiles)
   const int mt_gu = mma_row_units(bn, L.gu_mma.mtiles), mt_dn = mma_row_units(bn, L.dn_mma.mtiles);
   // one stage size for both GEMMs (they share the activation map cache), from
@@ -554,7 +559,8 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   const bool wide = ks == kMmaStageTilesWide && fp4;
   MmaLaunch &g = *gu;
   g.ks = ks;
-  g.tmap_a = fp4 ? (wide ? L.gu_mma.tmap_pw : L.gu_mma.tmap_p) : L.gu_mma.tmap_g;
+  g.tmap_a = fp4 ? (wide ? L.gu_mma.tmap_pw : L.gu_mma.tmap_p)
+                 : fmt == ActFmt::kFp4Planes ? L.gu_mma.tmap_gp : L.gu_mma.tmap_g;
   g.tmap_a1 = fp4 ? L.gu_mma.tmap_p1 : L.gu_mma.tmap;
   g.tmap_sfa = L.gu_mma.tmap_sfg;
   if (!act_maps(ctx, 0, ctx->qx.as<uint8_t>(), kph, rb, bn, ks, &g.tmap_b, &g.tmap_b1))
@@ -585,7 +591,8 @@ spt_status build_gemms(spt_context *ctx, const LayerDev &L, const spt_moe_config
   g.fault_stage = ctx->opt_fault_stage;
   MmaLaunch &d = *dn;
   d = g;
-  d.tmap_a = fp4 ? (wide ? L.dn_mma.tmap_pw : L.dn_mma.tmap_p) : L.dn_mma.tmap_g;
+  d.tmap_a = fp4 ? (wide ? L.dn_mma.tmap_pw : L.dn_mma.tmap_p)
+                 : fmt == ActFmt::kFp4Planes ? L.dn_mma.tmap_gp : L.dn_mma.tmap_g;
   d.tmap_a1 = fp4 ? L.dn_mma.tmap_p1 : L.dn_mma.tmap;
   d.tmap_sfa = L.dn_mma.tmap_sfg;
   if (!act_maps(ctx, 1, ctx->qa.as<uint8_t>(), kpd, rb, bn, ks, &d.tmap_b, &d.tmap_b1))
@@ -621,19 +628,20 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   int rb = 0;
   spt_status st = build_gemms(ctx, L, c, T, bn, &g, &dn, &rb);
   if (st) return st;
+  const ActFmt fmt = mma_act_fmt(bn, ctx->opt_prefill_fp8 != 0);
   // each token's row once, stored at every position it was dispatched to
   SPT_CUDA(ctx, launch_quantize_tokens(x, H, (int)T, K, ctx->slot_pos.as<int32_t>(), ctx->offsets.as<int32_t>(),
                                        ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(), H, g.kp, rb, bn,
-                                       ctx->qx.as<uint8_t>(), ctx->sfx.as<uint8_t>(), s));
+                                       fmt, ctx->qx.as<uint8_t>(), ctx->sfx.as<uint8_t>(), s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[4], s));
-  SPT_CUDA(ctx, launch_mma_gemm(g, bn, ctx->sm_count, s));
+  SPT_CUDA(ctx, launch_mma_gemm(g, bn, fmt, ctx->sm_count, s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[5], s));
   SPT_CUDA(ctx, launch_quantize_act(ctx->act.as<float>(), D, nullptr, K, false, ctx->offsets.as<int32_t>(),
                                     ctx->pad_off.as<int32_t>(), ctx->pos_expert.as<int32_t>(),
-                                    ctx->meta.as<int32_t>(), (int)S, D, dn.kp, rb, bn, ctx->qa.as<uint8_t>(),
+                                    ctx->meta.as<int32_t>(), (int)S, D, dn.kp, rb, bn, fmt, ctx->qa.as<uint8_t>(),
                                     ctx->sfa.as<uint8_t>(), s));
   if (ctx->timing) SPT_CUDA(ctx, cudaEventRecord(ctx->ev[6], s));
-  SPT_CUDA(ctx, launch_mma_gemm(dn, bn, ctx->sm_count, s));
+  SPT_CUDA(ctx, launch_mma_gemm(dn, bn, fmt, ctx->sm_count, s));
   ctx->kernels_last = 8;  // router, select, dispatch, quantize, gate/up, quantize, down, combine
   return SPT_OK;
 }
@@ -712,10 +720,11 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
     SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
     SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
   }
-  SPT_CUDA(ctx, ctx->qx.ensure(mma_act_bytes(bn, rb, kph)));
-  SPT_CUDA(ctx, ctx->sfx.ensure(mma_act_sf_bytes(bn, rb, kph)));
-  SPT_CUDA(ctx, ctx->qa.ensure(mma_act_bytes(bn, rb, kpd)));
-  SPT_CUDA(ctx, ctx->sfa.ensure(mma_act_sf_bytes(bn, rb, kpd)));
+  const ActFmt fmt = mma_act_fmt(bn, ctx->opt_prefill_fp8 != 0);
+  SPT_CUDA(ctx, ctx->qx.ensure(mma_act_bytes(fmt, rb, kph)));
+  SPT_CUDA(ctx, ctx->sfx.ensure(mma_act_sf_bytes(fmt, rb, kph)));
+  SPT_CUDA(ctx, ctx->qa.ensure(mma_act_bytes(fmt, rb, kpd)));
+  SPT_CUDA(ctx, ctx->sfa.ensure(mma_act_sf_bytes(fmt, rb, kpd)));
   return SPT_OK;
 }
 
@@ -956,7 +965,7 @@ std::vector<const void *> call_buffers(const spt_context *ctx) {
 
 std::vector<int64_t> call_options(const spt_context *ctx) {
   return {ctx->path, ctx->opt_tile_tokens, ctx->opt_fused_select, ctx->opt_prefetch, ctx->opt_gemv16_slots,
-          ctx->opt_wait_shift, ctx->opt_fault_stage, (int64_t)(uintptr_t)ctx->stream};
+          ctx->opt_wait_shift, ctx->opt_fault_stage, ctx->opt_prefill_fp8, (int64_t)(uintptr_t)ctx->stream};
 }
 
 // Capture the block on the context's device buffers into a graph (after a
@@ -1097,6 +1106,7 @@ void seed_options(spt_context *ctx) {
   env("SPT_MMA_PREFETCH", &ctx->opt_prefetch, 0, 64);
   env("SPT_GEMV16_SLOTS", &ctx->opt_gemv16_slots, 0, 1 << 20);
   env("SPT_HOST_GRAPHS", &ctx->opt_host_graphs, 0, 1);
+  env("SPT_PREFILL_FP8", &ctx->opt_prefill_fp8, 0, 1);
 }
 
 // Temporary device buffer for stage entry points.
@@ -1284,6 +1294,10 @@ spt_status spt_context_set_option(spt_context *ctx, int option, int64_t v) {
       if (v != 0 && v != 1) break;
       ctx->opt_host_graphs = (int)v;
       return SPT_OK;
+    case SPT_OPT_PREFILL_FP8:
+      if (v != 0 && v != 1) break;
+      ctx->opt_prefill_fp8 = (int)v;
+      return SPT_OK;
     default:
       return fail(ctx, SPT_ERR_UNSUPPORTED, "unknown option %d", option);
   }
@@ -1300,6 +1314,7 @@ int64_t spt_context_get_option(const spt_context *ctx, int option) {
     case SPT_OPT_WAIT_LIMIT: return ctx->opt_wait_shift;
     case SPT_OPT_FAULT_STAGE: return ctx->opt_fault_stage;
     case SPT_OPT_HOST_GRAPHS: return ctx->opt_host_graphs;
+    case SPT_OPT_PREFILL_FP8: return ctx->opt_prefill_fp8;
   }
   return -1;
 }

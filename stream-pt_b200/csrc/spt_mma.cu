@@ -102,6 +102,13 @@ bool mma_encode_weights(MmaMatrix *m) {
          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
+  // the same groups packed (kind::mxf4): 64-byte rows as they are (SW64)
+  cuuint64_t dims4p[4] = {(cuuint64_t)(kMmaKT / 2), (cuuint64_t)kMmaM, kt_n, runs};
+  cuuint32_t box4p[4] = {(cuuint32_t)(kMmaKT / 2), 128, 1, (cuuint32_t)kPrefillRowTiles};
+  r = fn(&m->tmap_gp, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, m->w, dims4p, strides4, box4p, estr4,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
   cuuint64_t sdims[3] = {128, kt_n, runs};  // 32-bit words: an atom is 128 of them
   cuuint64_t sstrides[2] = {512, kt_n * 512};
   cuuint32_t sbox[3] = {128, 1, (cuuint32_t)kPrefillRowTiles};
@@ -111,13 +118,20 @@ bool mma_encode_weights(MmaMatrix *m) {
   return r == CUDA_SUCCESS;
 }
 
-bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, int ktiles) {
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, ActFmt f, int ktiles) {
   auto fn = encode_fn();
-  const int box_rows = mma_box_rows(bn);
+  const int box_rows = mma_box_rows(f, bn);
   if (!fn || !q || box_rows < 1 || box_rows > 256 || ktiles < 1) return false;
   const cuuint64_t kt_n = (cuuint64_t)(kp / kMmaKT);
   CUresult r;
-  if (mma_fp4(bn)) {
+  if (f == ActFmt::kFp4Planes) {
+    cuuint64_t dims[4] = {kMmaKT / 2, (cuuint64_t)rb, (cuuint64_t)kFp4Terms, kt_n};
+    cuuint64_t strides[3] = {kMmaKT / 2, (cuuint64_t)rb * (kMmaKT / 2), (cuuint64_t)rb * (kMmaKT / 2) * kFp4Terms};
+    cuuint32_t box[4] = {kMmaKT / 2, (cuuint32_t)box_rows, (cuuint32_t)kFp4Terms, (cuuint32_t)ktiles};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, q, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (f == ActFmt::kFp4Stack) {
     cuuint64_t dims[3] = {kMmaKT / 2, (cuuint64_t)rb, kt_n};
     cuuint64_t strides[2] = {kMmaKT / 2, (cuuint64_t)rb * (kMmaKT / 2)};
     cuuint32_t box[3] = {kMmaKT / 2, (cuuint32_t)box_rows, (cuuint32_t)ktiles};
@@ -323,25 +337,27 @@ __device__ __forceinline__ Terms<FP4> quantize_terms(float4 v) {
 
 // Store the terms of one (dispatch row, 128-element K tile): row j of its
 // token tile, whose 128-row activation slot starts at `slot`; 8 lanes per
-// 32-element block, 4 elements per lane (the layouts of spt_mma.cuh).
+// 32-element block, 4 elements per lane (the layouts of spt_mma.cuh: FP4
+// terms stacked along the slot for bn <= 16, else one plane per term).
 template <bool FP4>
 __device__ __forceinline__ void store_terms(const Terms<FP4> &r, int kt, int kt_n, int j, int slot, int bn, int rb,
                                             uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int lane) {
   const int sub = lane & 7;
   const int b = kt * 4 + (lane >> 3);
   const int64_t atom = (int64_t)(slot / kMmaM) * kt_n + kt;
+  const bool stacked = FP4 && bn <= 16;
 #pragma unroll
   for (int t = 0; t < Terms<FP4>::kN; ++t) {
-    const int m = FP4 ? t * bn + (j % bn) : (j % bn);  // row within the slot
+    const int m = stacked ? t * bn + (j % bn) : (j % bn);  // row within the slot
     if constexpr (FP4) {
-      const int64_t row = (int64_t)kt * rb + slot + m;
+      const int64_t row = stacked ? (int64_t)kt * rb + slot + m : ((int64_t)kt * kFp4Terms + t) * rb + slot + m;
       *reinterpret_cast<uint16_t *>(q + row * (kMmaKT / 2) + (b % 4) * 16 + sub * 2) = (uint16_t)r.code[t];
     } else {
       const int64_t row = ((int64_t)kt * kActTerms + t) * rb + slot + m;
       *reinterpret_cast<uint32_t *>(q + row * kMmaKT + (b % 4) * 32 + sub * 4) = r.code[t];
     }
     if (sub == 0) {
-      const int64_t a2 = FP4 ? atom : atom * kActTerms + t;
+      const int64_t a2 = stacked ? atom : atom * Terms<FP4>::kN + t;
       sf[a2 * 512 + (m % 32) * 16 + (m / 32) * 4 + (b % 4)] = (uint8_t)(r.ex[t] + 127);
     }
   }
@@ -617,23 +633,26 @@ __device__ __forceinline__ TileInfo tile_info(const TileTables &tt, int tile, in
   return t;
 }
 
-// FP4: kind::mxf4, packed weights (SW64), kFp4Terms e2m1 activation terms
-// stacked along N (N = kFp4Terms*BN, one scale atom per K tile, two K = 64
-// MMAs per K tile).  FP8: kind::mxf8f6f4, weights unpacked by the TMA
-// (SW128), kActTerms e4m3 terms each its own N = BN operand with its own atom
-// (four K = 32 MMAs per term per K tile).  KS: K tiles per pipeline stage.
-// MG row tiles share each activation K tile (FP8 mode: kPrefillRowTiles;
-// their MG accumulators are single-buffered), else one row tile per unit with
-// a double-buffered accumulator.
+// FP4: kind::mxf4, packed weights (SW64), kFp4Terms e2m1 activation terms:
+// for BN <= 16 stacked along N (N = kFp4Terms*BN, one scale atom per K tile,
+// the term partial sums added in the epilogue), for 128-token tiles one
+// N = BN operand and atom per term, all into one accumulator; two K = 64
+// MMAs (per term) per K tile.  FP8: kind::mxf8f6f4, weights unpacked by the
+// TMA (SW128), kActTerms e4m3 terms each its own N = BN operand with its own
+// atom (four K = 32 MMAs per term per K tile).  KS: K tiles per pipeline
+// stage.  MG row tiles share each activation K tile (128-token tiles:
+// kPrefillRowTiles; their MG accumulators are single-buffered), else one row
+// tile per unit with a double-buffered accumulator.
 template <int BN, bool FP4, int KS, int MG = 1>
 struct MmaShape {
+  static constexpr bool kStacked = FP4 && BN <= 16;              // FP4 terms stacked along N
   static constexpr int kA = FP4 ? kMmaM * 64 : kMmaM * 128;     // smem bytes of one weight K tile
   static constexpr int kATx = kMmaM * 64;                        // its transaction bytes (packed source)
   static constexpr int kBTerm = FP4 ? BN * 64 : BN * 128;        // smem bytes of one term's K tile
   static constexpr int kTerms = FP4 ? kFp4Terms : kActTerms;
   static constexpr int kBt = kTerms * kBTerm;                    // all terms of one K tile
-  static constexpr int kSfb = FP4 ? 1 : kActTerms;               // activation scale atoms per K tile
-  static constexpr int kN = FP4 ? kFp4Terms * BN : BN;           // MMA N
+  static constexpr int kSfb = kStacked ? 1 : kTerms;             // activation scale atoms per K tile
+  static constexpr int kN = kStacked ? kFp4Terms * BN : BN;      // MMA N
   static constexpr int kKSteps = FP4 ? 2 : 4;                    // MMAs (per term) per K tile
   static constexpr uint32_t kLayout = FP4 ? 4u : 2u;             // smem descriptor: SW64 / SW128
   static constexpr uint32_t kSbo = FP4 ? 512u : 1024u;           // 8-row swizzle atom
@@ -658,7 +677,7 @@ struct MmaShape {
   static_assert(kBTerm % 512 == 0 && kA % 1024 == 0, "swizzle atoms must stay aligned");
   static_assert(kAccCols + kSfCols <= 512, "TMEM columns");
   static_assert(kStages >= 2, "stage ring");
-  static_assert(MG == 1 || (KS == 1 && !FP4), "row-tile groups: one K tile per stage, 128-token tiles");
+  static_assert(MG == 1 || (KS == 1 && BN == 128), "row-tile groups: one K tile per stage, 128-token tiles");
   // epilogue warps: two per TMEM lane quadrant (each takes half of the
   // columns) with row-tile groups, whose single-buffered accumulators wait
   // for the epilogue; one per quadrant otherwise
@@ -870,12 +889,12 @@ struct GemmCta {
               for (int ks = 0; ks < S::kKSteps; ++ks) {
                 const uint32_t id = FP4 ? 2u * ks : (uint32_t)ks;
 #pragma unroll
-                for (int term = 0; term < (FP4 ? 1 : kActTerms); ++term) {
+                for (int term = 0; term < (S::kStacked ? 1 : S::kTerms); ++term) {
                   // the unit's first product into each accumulator overwrites it
                   const uint32_t acc = (kt == kt_lo && j == 0 && ks == 0 && term == 0) ? 0u : 1u;
                   if (FP4)
-                    tc_mma_fp4(dm, ad + 2 * ks, bd + 2 * ks, idesc[ks], sfa_m | (id << 30), sfb_j | (id << 30),
-                               acc);
+                    tc_mma_fp4(dm, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_m | (id << 30),
+                               (sfb_j + 4 * term) | (id << 30), acc);
                   else
                     tc_mma(dm, ad + 2 * ks, bd + term * kBTerm16 + 2 * ks, idesc[ks], sfa_m | (id << 30),
                            (sfb_j + 4 * term) | (id << 30), acc);
@@ -937,7 +956,7 @@ struct GemmCta {
             for (int j = 0; j < kC; ++j) v[j] += w[term * BN + j];
         } else {
           tc_ld<kC>(col, v);
-          if (FP4) {  // the term partial sums sit BN columns apart
+          if (S::kStacked) {  // the term partial sums sit BN columns apart
 #pragma unroll
             for (int term = 1; term < kFp4Terms; ++term) {
               float w[kC];
@@ -1066,12 +1085,12 @@ cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t first_expert, 
 
 cudaError_t launch_quantize_tokens(const float *x, int64_t stride, int T, int top_k, const int32_t *slot_pos,
                                    const int32_t *offsets, const int32_t *pad_off, const int32_t *pos_expert, int K,
-                                   int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s) {
+                                   int kp, int rb, int bn, ActFmt f, uint8_t *q, uint8_t *sf, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   const int threads = 256;
   const int64_t warps = (int64_t)T * (kp / kMmaKT);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  return launch_pdl(mma_fp4(bn) ? k_quantize_tokens<true> : k_quantize_tokens<false>, dim3((unsigned)blocks),
+  return launch_pdl(mma_fp4(f) ? k_quantize_tokens<true> : k_quantize_tokens<false>, dim3((unsigned)blocks),
                     dim3(threads), 0, s, x, stride, T, top_k, slot_pos, offsets, pad_off, pos_expert, K, kp, rb, bn,
                     q, sf);
 }
@@ -1079,7 +1098,7 @@ cudaError_t launch_quantize_tokens(const float *x, int64_t stride, int T, int to
 cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t *perm, int top_k,
                                 bool gather, const int32_t *offsets, const int32_t *pad_off,
                                 const int32_t *pos_expert, const int32_t *meta, int S_max, int K, int kp,
-                                int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s) {
+                                int rb, int bn, ActFmt f, uint8_t *q, uint8_t *sf, cudaStream_t s) {
   if (S_max <= 0) return cudaSuccess;
   const int threads = 256;
   // large batches: several K tiles per warp (memory parallelism); small ones
@@ -1087,16 +1106,17 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
   const int ktw = S_max >= 2048 ? kQuantKt : 1;
   const int64_t warps = (int64_t)S_max * ((kp / kMmaKT + ktw - 1) / ktw);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  return launch_pdl(mma_fp4(bn) ? k_quantize_act<true> : k_quantize_act<false>, dim3((unsigned)blocks),
+  return launch_pdl(mma_fp4(f) ? k_quantize_act<true> : k_quantize_act<false>, dim3((unsigned)blocks),
                     dim3(threads), 0, s, src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off, pos_expert, meta,
                     S_max, K, kp, rb, bn, q, sf, ktw);
 }
 
-cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s) {
+cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, ActFmt f, int sm_count, cudaStream_t s) {
   if (bn == 8 && a.ks == kMmaStageTilesWide) return launch_gemm_bn<8, true, kMmaStageTilesWide>(a, sm_count, s);
   if (bn == 8 && a.ks == kMmaStageTilesFp4) return launch_gemm_bn<8, true, kMmaStageTilesFp4>(a, sm_count, s);
   if (bn == 16 && a.ks == kMmaStageTilesFp4) return launch_gemm_bn<16, true, kMmaStageTilesFp4>(a, sm_count, s);
-  if (bn == 128) return launch_gemm_bn<128, false, 1, kPrefillRowTiles>(a, sm_count, s);
+  if (bn == 128 && f == ActFmt::kFp4Planes) return launch_gemm_bn<128, true, 1, kPrefillRowTiles>(a, sm_count, s);
+  if (bn == 128 && f == ActFmt::kFp8Planes) return launch_gemm_bn<128, false, 1, kPrefillRowTiles>(a, sm_count, s);
   return cudaErrorInvalidValue;
 }
 

@@ -8,9 +8,12 @@
 //   token tiles of 8 or 16 (decode):  kind::mxf4, kFp4Terms e2m1 terms
 //     stacked along N (N = kFp4Terms*BN), both operands packed 4-bit in
 //     shared memory;
-//   128-token tiles (prefill):      kind::mxf8f6f4, kActTerms e4m3 terms, one
-//     N = 128 MMA per term, the weights unpacked to one byte per element by
-//     the TMA (16U4_ALIGN16B).
+//   128-token tiles (prefill):      kind::mxf4, kFp4Terms e2m1 terms, one
+//     N = 128 MMA per term into the same accumulator, both operands packed
+//     (ActFmt::kFp4Planes, the default); or kind::mxf8f6f4 with kActTerms
+//     e4m3 terms, the weights unpacked to one byte per element by the TMA
+//     (16U4_ALIGN16B) (ActFmt::kFp8Planes, the context option
+//     SPT_OPT_PREFILL_FP8).
 // Decode-sized tiles are bound by the weight stream: packed 4-bit weights need
 // half the shared memory per K tile, so the ring keeps twice as many bytes in
 // flight from HBM.
@@ -30,9 +33,10 @@
 // Activations (per call), K-tile-major plus scale atoms.  Every BN-token tile
 // owns one 128-row slot starting at pad_off[e] + (j/BN)*128 for token j of
 // expert e, so its scale atom starts at slot row 0.
-//   FP4: term t, token j at slot row t*BN + j%BN; q [KP/128][RB][64],
-//        sf [RB/128][KP/128][512].
-//   FP8: q [KP/128][kActTerms][RB][128], sf [RB/128][KP/128][kActTerms][512].
+//   kFp4Stack:  term t, token j at slot row t*BN + j%BN; q [KP/128][RB][64],
+//               sf [RB/128][KP/128][512].
+//   kFp4Planes: q [KP/128][kFp4Terms][RB][64], sf [RB/128][KP/128][kFp4Terms][512].
+//   kFp8Planes: q [KP/128][kActTerms][RB][128], sf [RB/128][KP/128][kActTerms][512].
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -55,8 +59,9 @@ constexpr int kMmaStageTilesFp4 = 4;  // K tiles per pipeline stage, FP4 mode
 constexpr int kMmaStageTilesWide = 6;
 // 128-token tiles: each CTA unit covers this many 128-row weight tiles of
 // one expert against one token tile, so every activation K tile it loads
-// (3 e4m3 terms, 48 KB) feeds three row tiles' MMAs instead of one; the
-// shared-memory and TMEM copy traffic per output falls by about half.
+// (all terms: 32 KB of e2m1 or 48 KB of e4m3) feeds three row tiles' MMAs
+// instead of one; the shared-memory and TMEM copy traffic per output falls
+// by about half.
 constexpr int kPrefillRowTiles = 3;
 // Units of one token tile: row tiles, or groups of kPrefillRowTiles of them.
 inline int mma_row_units(int bn, int mtiles) {
@@ -77,9 +82,11 @@ struct MmaMatrix {
   alignas(64) CUtensorMap tmap_pw; // same, kMmaStageTilesWide boxes
   // 128-token tiles: one K tile of kPrefillRowTiles consecutive row tiles in
   // one copy each -- 4D [128 elements, 128 rows, K tiles, row tiles]
-  // 16U4_ALIGN16B (unpacked, SW128), and their scale atoms, 3D [128 words,
-  // K tiles, row tiles] UINT32
+  // 16U4_ALIGN16B (unpacked, SW128; kFp8Planes) or 4D [64 B, 128 rows, K
+  // tiles, row tiles] UINT8 (packed, SW64; kFp4Planes), and their scale
+  // atoms, 3D [128 words, K tiles, row tiles] UINT32
   alignas(64) CUtensorMap tmap_g;
+  alignas(64) CUtensorMap tmap_gp;
   alignas(64) CUtensorMap tmap_sfg;
 };
 
@@ -119,24 +126,33 @@ struct MmaLaunch {
   int fault_stage = -1;              // failure injection (tests): CTA 0's producer skips this stage
 };
 
-// Token tiles of 8 or 16 tokens run the FP4 mode (kFp4Terms e2m1 terms
-// stacked along N, kMmaStageTilesFp4 K tiles per stage); 128-token tiles run
-// the FP8 mode (one K tile per stage).  launch_mma_gemm takes bn 8, 16 or 128.
-inline bool mma_fp4(int bn) { return bn <= 16; }
+// Activation operand formats.  Token tiles of 8 or 16 tokens: kFp4Stack
+// (kFp4Terms e2m1 terms stacked along N, kMmaStageTilesFp4 K tiles per
+// stage); 128-token tiles: kFp4Planes (kFp4Terms e2m1 terms, one plane and
+// one N = 128 MMA each) or kFp8Planes (kActTerms e4m3 terms), one K tile per
+// stage.  launch_mma_gemm takes bn 8, 16 or 128.
+enum class ActFmt { kFp4Stack, kFp4Planes, kFp8Planes };
+inline ActFmt mma_act_fmt(int bn, bool fp8_prefill) {
+  return bn <= 16 ? ActFmt::kFp4Stack : fp8_prefill ? ActFmt::kFp8Planes : ActFmt::kFp4Planes;
+}
+inline bool mma_fp4(ActFmt f) { return f != ActFmt::kFp8Planes; }
+inline int mma_terms(ActFmt f) { return f == ActFmt::kFp8Planes ? kActTerms : kFp4Terms; }
 // K tiles per stage for bn-token tiles when a launch has up to max_tiles row
 // tiles on sm_count SMs.
 inline int mma_stage_tiles(int bn, int64_t max_tiles = 0, int sm_count = 148) {
-  if (!mma_fp4(bn)) return 1;
+  if (bn > 16) return 1;
   return (bn == 8 && max_tiles >= 2 * (int64_t)sm_count) ? kMmaStageTilesWide : kMmaStageTilesFp4;
 }
-// Activation rows of one TMA box.
-inline int mma_box_rows(int bn) { return mma_fp4(bn) ? kFp4Terms * bn : bn; }
+// Activation rows of one TMA box (per term plane for the plane formats).
+inline int mma_box_rows(ActFmt f, int bn) { return f == ActFmt::kFp4Stack ? kFp4Terms * bn : bn; }
 // Bytes of the activation buffers for rb rows per term and kp padded K.
-inline size_t mma_act_bytes(int bn, int rb, int kp) {
-  return mma_fp4(bn) ? (size_t)rb * (kp / 2) : (size_t)kActTerms * rb * kp;
+inline size_t mma_act_bytes(ActFmt f, int rb, int kp) {
+  return f == ActFmt::kFp4Stack    ? (size_t)rb * (kp / 2)
+         : f == ActFmt::kFp4Planes ? (size_t)kFp4Terms * rb * (kp / 2)
+                                   : (size_t)kActTerms * rb * kp;
 }
-inline size_t mma_act_sf_bytes(int bn, int rb, int kp) {
-  return (size_t)(mma_fp4(bn) ? 1 : kActTerms) * (rb / kMmaM) * (kp / kMmaKT) * 512;
+inline size_t mma_act_sf_bytes(ActFmt f, int rb, int kp) {
+  return (size_t)(f == ActFmt::kFp4Stack ? 1 : mma_terms(f)) * (rb / kMmaM) * (kp / kMmaKT) * 512;
 }
 
 size_t mma_w_bytes(int64_t experts, int rows, int k);
@@ -144,10 +160,11 @@ size_t mma_sf_bytes(int64_t experts, int rows, int k);
 
 // Encode the TMA map of a packed e2m1 matrix (returns false on failure).
 bool mma_encode_weights(MmaMatrix *m);
-// TMA map of the activations in the layout of mode mma_fp4(bn): FP4
-// [kt][rb][64 B] with box 64 B x kFp4Terms*bn rows x ktiles (SW64); FP8
+// TMA map of the activations in format f: kFp4Stack [kt][rb][64 B] with box
+// 64 B x kFp4Terms*bn rows x ktiles (SW64); kFp4Planes [kt][kFp4Terms][rb][64 B]
+// with box 64 B x bn rows x kFp4Terms x ktiles (SW64); kFp8Planes
 // [kt][kActTerms][rb][128 B] with box 128 B x bn rows x kActTerms x ktiles (SW128).
-bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, int ktiles);
+bool mma_encode_acts(CUtensorMap *map, uint8_t *q, int kp, int rb, int bn, ActFmt f, int ktiles);
 
 cudaError_t launch_repack_mma_gu(const uint8_t *gate_gguf, const uint8_t *up_gguf, int64_t experts,
                                  int D, int K, MmaMatrix *m, cudaStream_t s);
@@ -162,18 +179,19 @@ cudaError_t launch_synth_mma_gu(uint64_t seed, uint32_t tag_gate, uint32_t tag_u
 cudaError_t launch_synth_mma(uint64_t seed, uint32_t tag, int64_t first_expert, int64_t experts, int rows,
                              int K, uint8_t lo, uint8_t hi, MmaMatrix *m, cudaStream_t s);
 
-// Quantize rows to the three MXFP8 terms.  Source row of dispatch position
-// p: src[(gather ? perm[p]/top_k : p) * src_stride + k].
-// The same for T token rows quantized once each and stored at every dispatch
-// position of the token (slot_pos[t*top_k + r], -1: not dispatched).
+// Quantize T token rows to the activation terms of format f, each row once,
+// stored at every dispatch position of the token (slot_pos[t*top_k + r], -1:
+// not dispatched).
 cudaError_t launch_quantize_tokens(const float *x, int64_t stride, int T, int top_k, const int32_t *slot_pos,
                                    const int32_t *offsets, const int32_t *pad_off, const int32_t *pos_expert, int K,
-                                   int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s);
+                                   int kp, int rb, int bn, ActFmt f, uint8_t *q, uint8_t *sf, cudaStream_t s);
+// The same per dispatch position p, source row src[(gather ? perm[p]/top_k :
+// p) * src_stride + k].
 cudaError_t launch_quantize_act(const float *src, int64_t src_stride, const int32_t *perm, int top_k,
                                 bool gather, const int32_t *offsets, const int32_t *pad_off,
                                 const int32_t *pos_expert, const int32_t *meta, int S_max, int K,
-                                int kp, int rb, int bn, uint8_t *q, uint8_t *sf, cudaStream_t s);
+                                int kp, int rb, int bn, ActFmt f, uint8_t *q, uint8_t *sf, cudaStream_t s);
 
-cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, int sm_count, cudaStream_t s);
+cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, ActFmt f, int sm_count, cudaStream_t s);
 
 }  // namespace spt

@@ -1,6 +1,7 @@
 """GPU parity of the tcgen05 path (packed FP4 weights x block-scaled
 activation terms on the tensor cores: four e2m1 terms for token tiles of 8
-or 16, three e4m3 terms for 128-token tiles).
+or 16 stacked along N; for 128-token tiles four e2m1 terms, one MMA each
+(the default), or three e4m3 terms (SPT_OPT_PREFILL_FP8)).
 
 Routing and dispatch are computed by the same bit-exact kernels as the exact
 path and must match the oracle bit for bit.  Block outputs are checked at
@@ -68,14 +69,16 @@ def test_mma_block_matches_oracle(ctx, mma_layer, T):
     assert refdata.bits_equal(exact, want["out"].ravel()).all()
 
 
-@pytest.mark.parametrize("bn", [None, "8", "16", "128"])
+@pytest.mark.parametrize("bn", [None, "8", "16", "128", "128fp8"])
 @pytest.mark.parametrize("mode", ["normal", "ties", "underflow", "clamp"])
 @pytest.mark.parametrize("experts,k", [(4, 2), (7, 7), (8, 1)])
 def test_mma_reference_fixtures(ctx, mode, experts, k, bn):
-    """Every token-tile width (SPT_OPT_TILE_TOKENS; None: the size rule) on
-    the reference's fixtures; 37 tokens over 4-8 experts put up to 37 tokens
-    on one expert, so the 8- and 16-token tiles split experts into several."""
-    ctx.set_option(spt.OPT_TILE_TOKENS, int(bn or 0))
+    """Every token-tile width (SPT_OPT_TILE_TOKENS; None: the size rule) and
+    both 128-token activation formats on the reference's fixtures; 37 tokens
+    over 4-8 experts put up to 37 tokens on one expert, so the 8- and
+    16-token tiles split experts into several."""
+    ctx.set_option(spt.OPT_TILE_TOKENS, int((bn or "0").replace("fp8", "")))
+    ctx.set_option(spt.OPT_PREFILL_FP8, 1 if bn == "128fp8" else 0)
     fx = refdata.moe_batch_fixture(96, 64, experts, k, 0, mode)
     batch = 37
     x = refdata.moe_batch_x(batch, 96, mode)
@@ -86,6 +89,7 @@ def test_mma_reference_fixtures(ctx, mode, experts, k, bn):
     finally:
         ctx.set_path(spt.PATH_AUTO)
         ctx.set_option(spt.OPT_TILE_TOKENS, 0)
+        ctx.set_option(spt.OPT_PREFILL_FP8, 0)
         arena.close()
     want = oracle.forward_moe_batch(fx.dense, x, batch)
     _check_close(got, want, (mode, experts, k, bn))
@@ -112,19 +116,24 @@ def test_mma_decode_tile_widths(ctx, mma_layer, bn):
         ctx.set_option(spt.OPT_TILE_TOKENS, 0)
 
 
-def test_mma_large_batch_properties(ctx, mma_layer):
-    """T=2048 (128-token tiles): sampled tokens against the oracle and
-    permutation invariance of the batch (each token's result does not depend
-    on its neighbours)."""
+@pytest.mark.parametrize("fp8", [0, 1])
+def test_mma_large_batch_properties(ctx, mma_layer, fp8):
+    """T=2048 (128-token tiles, both activation formats): sampled tokens
+    against the oracle and permutation invariance of the batch (each token's
+    result does not depend on its neighbours)."""
     cfg, dense, arena = mma_layer
     T = 2048
     x = spt.synth_normal_host(5, 2000, T * 2880)
     ctx.set_path(spt.PATH_MMA)
-    got = ctx.forward_moe_batch(arena, x, T).reshape(T, 2880)
-    for t in (0, 5, 1023, 2047):
-        want = oracle.forward_moe_batch(dense, x[t * 2880:(t + 1) * 2880], 1, workers=8)
-        _check_close(got[t], want, t)
-    perm = np.random.default_rng(1).permutation(T)
-    gp = ctx.forward_moe_batch(arena, x.reshape(T, 2880)[perm].ravel(), T).reshape(T, 2880)
-    _check_close(gp, got[perm], "perm")
-    ctx.set_path(spt.PATH_AUTO)
+    ctx.set_option(spt.OPT_PREFILL_FP8, fp8)
+    try:
+        got = ctx.forward_moe_batch(arena, x, T).reshape(T, 2880)
+        for t in (0, 5, 1023, 2047):
+            want = oracle.forward_moe_batch(dense, x[t * 2880:(t + 1) * 2880], 1, workers=8)
+            _check_close(got[t], want, t)
+        perm = np.random.default_rng(1).permutation(T)
+        gp = ctx.forward_moe_batch(arena, x.reshape(T, 2880)[perm].ravel(), T).reshape(T, 2880)
+        _check_close(gp, got[perm], "perm")
+    finally:
+        ctx.set_path(spt.PATH_AUTO)
+        ctx.set_option(spt.OPT_PREFILL_FP8, 0)
