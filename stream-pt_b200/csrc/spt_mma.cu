@@ -259,23 +259,18 @@ unsigned grid_of(int64_t n) {
 //     rows; q [KP/128][kActTerms][RB][128 B].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
 
-// Smallest e with amax / 2^e <= qmax (amax finite and > 0), clamped to the
-// E8M0 range the scale atoms hold.
-__device__ __forceinline__ int term_exponent(float amax, float qmax, float inv_qmax) {
+// Smallest e with amax / 2^e <= qmax, clamped to the E8M0 range the scale
+// atoms hold (-126 for amax 0, subnormal or NaN, 120 for Inf).  qmax =
+// qm * 2^QE with qm = 1 + QF/2^23 (e2m1: 6 = 1.5 * 2^2; e4m3: 448 = 1.75 *
+// 2^8): for amax = 1.f * 2^E the answer is E - QE, plus one when 1.f > qm.
+template <int QE, uint32_t QF>
+__device__ __forceinline__ int term_exponent(float amax) {
   if (!(amax > 0.0f)) return -126;
-  if (!isfinite(amax)) return 120;
-  int e2;
-  const float mant = frexpf(amax * inv_qmax, &e2);  // amax/qmax = mant * 2^e2, mant in [0.5, 1)
-  int ex = (mant == 0.5f) ? e2 - 1 : e2;
-  if (__fmul_rn(amax, exp2i(-ex)) > qmax) ex += 1;
+  const uint32_t bits = __float_as_uint(amax);
+  const int E = (int)(bits >> 23) - 127;
+  if (E == 128) return 120;
+  const int ex = E - QE + ((bits & 0x7fffffu) > QF ? 1 : 0);
   return max(-126, min(ex, 120));
-}
-
-// e2m1 code -> value (sign in bit 3).
-__device__ __forceinline__ float e2m1_value(uint32_t code) {
-  const uint32_t c = code & 7u;  // 0, 0.5, 1, 1.5, 2, 3, 4, 6
-  const float mag = c < 2u ? 0.5f * (float)c : (float)(1u << ((c >> 1) - 1u)) * ((c & 1u) ? 1.5f : 1.0f);
-  return (code & 8u) ? -mag : mag;
 }
 
 // Two floats -> one byte of two e2m1 codes (lo in the low nibble), round to
@@ -298,41 +293,64 @@ struct Terms {
   int ex[kN];
 };
 
-template <bool FP4>
-__device__ __forceinline__ Terms<FP4> quantize_terms(float4 v) {
-  Terms<FP4> r;
-  constexpr float kQmax = FP4 ? 6.0f : 448.0f;
-  // not unrolled: the loop body is the code a cold instruction cache fetches
-#pragma unroll 1
-  for (int t = 0; t < Terms<FP4>::kN; ++t) {
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+// Byte of two e2m1 codes -> their values (lo: low nibble) as two floats.
+__device__ __forceinline__ float2 e2m1x2_values(uint32_t byte) {
+  uint32_t h2;
+  asm("{\n\t.reg .b8 b;\n\tcvt.u8.u32 b, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b;\n\t}" : "=r"(h2) : "r"(byte));
+  return __half22float2(*reinterpret_cast<const __half2 *>(&h2));
+}
+
+// The terms of N independent (row, K tile) items at once: term t of every
+// item before term t + 1 of any, so the items' shuffle and conversion chains
+// overlap.
+template <bool FP4, int N>
+__device__ __forceinline__ void quantize_term(float4 (&v)[N], Terms<FP4> (&r)[N], int t) {
 #pragma unroll
-    for (int off = 4; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    const int ex = term_exponent(amax, kQmax, 1.0f / kQmax);
-    const float inv = exp2i(-ex), sc = exp2i(ex);
-    float vv[4] = {v.x, v.y, v.z, v.w};
-    if constexpr (FP4) {
-      const uint32_t c01 = e2m1x2(__fmul_rn(vv[0], inv), __fmul_rn(vv[1], inv));
-      const uint32_t c23 = e2m1x2(__fmul_rn(vv[2], inv), __fmul_rn(vv[3], inv));
-      const uint32_t codes[4] = {c01 & 15u, c01 >> 4, c23 & 15u, c23 >> 4};
+    for (int i = 0; i < N; ++i) {
+      float amax = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
 #pragma unroll
-      for (int i = 0; i < 4; ++i) vv[i] = __fsub_rn(vv[i], __fmul_rn(e2m1_value(codes[i]), sc));
-      r.code[t] = c01 | (c23 << 8);
-    } else {
-      uint32_t packed = 0;
+      for (int off = 4; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      const int ex = FP4 ? term_exponent<2, 0x400000u>(amax) : term_exponent<8, 0x600000u>(amax);
+      const float inv = exp2i(-ex), sc = exp2i(ex);
+      float vv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      if constexpr (FP4) {
+        const uint32_t c01 = e2m1x2(__fmul_rn(vv[0], inv), __fmul_rn(vv[1], inv));
+        const uint32_t c23 = e2m1x2(__fmul_rn(vv[2], inv), __fmul_rn(vv[3], inv));
+        // the residuals v - q * 2^ex are exact in fp32: one rounding-free FMA each
+        const float2 q01 = e2m1x2_values(c01), q23 = e2m1x2_values(c23);
+        vv[0] = __fmaf_rn(-q01.x, sc, vv[0]);
+        vv[1] = __fmaf_rn(-q01.y, sc, vv[1]);
+        vv[2] = __fmaf_rn(-q23.x, sc, vv[2]);
+        vv[3] = __fmaf_rn(-q23.y, sc, vv[3]);
+        r[i].code[t] = c01 | (c23 << 8);
+      } else {
+        uint32_t packed = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(__fmul_rn(vv[i], inv), __NV_SATFINITE, __NV_E4M3);
-        const __half_raw hr = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
-        vv[i] = __fsub_rn(vv[i], __fmul_rn(__half2float(__half(hr)), sc));
-        packed |= (uint32_t)code << (8 * i);
+        for (int k = 0; k < 4; ++k) {
+          const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(__fmul_rn(vv[k], inv), __NV_SATFINITE, __NV_E4M3);
+          const __half_raw hr = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
+          vv[k] = __fsub_rn(vv[k], __fmul_rn(__half2float(__half(hr)), sc));
+          packed |= (uint32_t)code << (8 * k);
+        }
+        r[i].code[t] = packed;
       }
-      r.code[t] = packed;
+      r[i].ex[t] = ex;
+      v[i] = make_float4(vv[0], vv[1], vv[2], vv[3]);
     }
-    r.ex[t] = ex;
-    v = make_float4(vv[0], vv[1], vv[2], vv[3]);
+}
+
+template <bool FP4, int N>
+__device__ __forceinline__ void quantize_terms_n(float4 (&v)[N], Terms<FP4> (&r)[N]) {
+  if constexpr (N > 1) {
+    // large batches: every term unrolled (the terms stay in registers)
+#pragma unroll
+    for (int t = 0; t < Terms<FP4>::kN; ++t) quantize_term<FP4, N>(v, r, t);
+  } else {
+    // decode sizes: one copy of the body, the code a cold instruction cache
+    // fetches
+#pragma unroll 1
+    for (int t = 0; t < Terms<FP4>::kN; ++t) quantize_term<FP4, N>(v, r, t);
   }
-  return r;
 }
 
 // Store the terms of one (dispatch row, 128-element K tile): row j of its
@@ -363,16 +381,12 @@ __device__ __forceinline__ void store_terms(const Terms<FP4> &r, int kt, int kt_
   }
 }
 
-template <bool FP4>
-__device__ __forceinline__ void quantize_vals(float4 v, int kt, int kt_n, int j, int slot, int bn, int rb,
-                                              uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int lane) {
-  store_terms<FP4>(quantize_terms<FP4>(v), kt, kt_n, j, slot, bn, rb, q, sf, lane);
-}
+constexpr int kQuantKt = 4;  // K tiles per warp for large batches
 
 // The tokens' rows, each quantized once and stored at every dispatch
 // position of the token (top_k slots, each in its expert's token tile): one
-// warp per (token, 128-element K tile).
-template <bool FP4>
+// warp per (token, group of KTW 128-element K tiles).
+template <bool FP4, int KTW>
 __global__ void k_quantize_tokens(const float *__restrict__ x, int64_t stride, int T, int top_k,
                                   const int32_t *__restrict__ slot_pos, const int32_t *__restrict__ offsets,
                                   const int32_t *__restrict__ pad_off, const int32_t *__restrict__ pos_expert,
@@ -380,56 +394,64 @@ __global__ void k_quantize_tokens(const float *__restrict__ x, int64_t stride, i
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
-  const int kt_n = kp / kMmaKT;
+  const int kt_n = kp / kMmaKT, groups = (kt_n + KTW - 1) / KTW;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int t = (int)(gw / kt_n), kt = (int)(gw - (int64_t)t * kt_n);
+  const int t = (int)(gw / groups), kt0 = (int)(gw - (int64_t)t * groups) * KTW;
   if (t >= T) return;
-  const int b = kt * 4 + (lane >> 3);
-  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (b * 32 < K) v = *reinterpret_cast<const float4 *>(x + (int64_t)t * stride + b * 32 + (lane & 7) * 4);
-  const Terms<FP4> r = quantize_terms<FP4>(v);
+  float4 v[KTW];
+  Terms<FP4> r[KTW];
+#pragma unroll
+  for (int i = 0; i < KTW; ++i) {
+    const int b = (kt0 + i) * 4 + (lane >> 3);
+    v[i] = (kt0 + i < kt_n && b * 32 < K)
+               ? *reinterpret_cast<const float4 *>(x + (int64_t)t * stride + b * 32 + (lane & 7) * 4)
+               : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  quantize_terms_n<FP4, KTW>(v, r);
   for (int k = 0; k < top_k; ++k) {
     const int pos = slot_pos[(int64_t)t * top_k + k];
     if (pos < 0) continue;
     const int e = pos_expert[pos];
     const int j = pos - offsets[e];
-    store_terms<FP4>(r, kt, kt_n, j, pad_off[e] + (j / bn) * kMmaM, bn, rb, q, sf, lane);
+#pragma unroll
+    for (int i = 0; i < KTW; ++i)
+      if (kt0 + i < kt_n) store_terms<FP4>(r[i], kt0 + i, kt_n, j, pad_off[e] + (j / bn) * kMmaM, bn, rb, q, sf, lane);
   }
 }
 
-constexpr int kQuantKt = 4;  // K tiles per warp of k_quantize_act
-
-template <bool FP4>
+template <bool FP4, int KTW>
 __global__ void k_quantize_act(const float *__restrict__ src, int64_t stride,
                                const int32_t *__restrict__ perm, int top_k, int gather,
                                const int32_t *__restrict__ offsets, const int32_t *__restrict__ pad_off,
                                const int32_t *__restrict__ pos_expert, const int32_t *__restrict__ meta,
                                int S_max, int K, int kp, int rb, int bn,
-                               uint8_t *__restrict__ q, uint8_t *__restrict__ sf, int ktw) {
+                               uint8_t *__restrict__ q, uint8_t *__restrict__ sf) {
   pdl_wait();
   pdl_trigger();
-  // One warp per (dispatch position, group of ktw <= kQuantKt K tiles): the
-  // group's loads are all in flight before the first term is computed.
+  // One warp per (dispatch position, group of KTW K tiles): the group's loads
+  // are all in flight, and its term chains interleaved.
   const int lane = threadIdx.x & 31;
-  const int kt_n = kp / kMmaKT, groups = (kt_n + ktw - 1) / ktw;
+  const int kt_n = kp / kMmaKT, groups = (kt_n + KTW - 1) / KTW;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int pos = (int)(gw / groups), kt0 = (int)(gw - (int64_t)pos * groups) * ktw;
+  const int pos = (int)(gw / groups), kt0 = (int)(gw - (int64_t)pos * groups) * KTW;
   if (pos >= S_max || pos >= meta[1]) return;
   const int e = pos_expert[pos];
   const int j = pos - offsets[e];
   const int slot = pad_off[e] + (j / bn) * kMmaM;  // this token tile's 128-row slot
   const int64_t srow = gather ? (int64_t)(perm[pos] / top_k) : (int64_t)pos;
   const float *row = src + srow * stride;
-  float4 v[kQuantKt];
+  float4 v[KTW];
+  Terms<FP4> r[KTW];
 #pragma unroll
-  for (int i = 0; i < kQuantKt; ++i) {
+  for (int i = 0; i < KTW; ++i) {
     const int b = (kt0 + i) * 4 + (lane >> 3);
-    v[i] = (i < ktw && kt0 + i < kt_n && b * 32 < K) ? __ldcs(reinterpret_cast<const float4 *>(row + b * 32 + (lane & 7) * 4))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[i] = (kt0 + i < kt_n && b * 32 < K) ? __ldcs(reinterpret_cast<const float4 *>(row + b * 32 + (lane & 7) * 4))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  quantize_terms_n<FP4, KTW>(v, r);
 #pragma unroll
-  for (int i = 0; i < kQuantKt; ++i)
-    if (i < ktw && kt0 + i < kt_n) quantize_vals<FP4>(v[i], kt0 + i, kt_n, j, slot, bn, rb, q, sf, lane);
+  for (int i = 0; i < KTW; ++i)
+    if (kt0 + i < kt_n) store_terms<FP4>(r[i], kt0 + i, kt_n, j, slot, bn, rb, q, sf, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -1088,11 +1110,16 @@ cudaError_t launch_quantize_tokens(const float *x, int64_t stride, int T, int to
                                    int kp, int rb, int bn, ActFmt f, uint8_t *q, uint8_t *sf, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   const int threads = 256;
-  const int64_t warps = (int64_t)T * (kp / kMmaKT);
+  // large batches: several K tiles per warp (their chains overlap); small
+  // ones one (more warps)
+  const bool wide = T >= 512;
+  const int ktw = wide ? kQuantKt : 1;
+  const int64_t warps = (int64_t)T * ((kp / kMmaKT + ktw - 1) / ktw);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  return launch_pdl(mma_fp4(f) ? k_quantize_tokens<true> : k_quantize_tokens<false>, dim3((unsigned)blocks),
-                    dim3(threads), 0, s, x, stride, T, top_k, slot_pos, offsets, pad_off, pos_expert, K, kp, rb, bn,
-                    q, sf);
+  auto k = mma_fp4(f) ? (wide ? k_quantize_tokens<true, kQuantKt> : k_quantize_tokens<true, 1>)
+                      : (wide ? k_quantize_tokens<false, kQuantKt> : k_quantize_tokens<false, 1>);
+  return launch_pdl(k, dim3((unsigned)blocks), dim3(threads), 0, s, x, stride, T, top_k, slot_pos, offsets, pad_off,
+                    pos_expert, K, kp, rb, bn, q, sf);
 }
 
 cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t *perm, int top_k,
@@ -1103,12 +1130,14 @@ cudaError_t launch_quantize_act(const float *src, int64_t stride, const int32_t 
   const int threads = 256;
   // large batches: several K tiles per warp (memory parallelism); small ones
   // one (more warps)
-  const int ktw = S_max >= 2048 ? kQuantKt : 1;
+  const bool wide = S_max >= 2048;
+  const int ktw = wide ? kQuantKt : 1;
   const int64_t warps = (int64_t)S_max * ((kp / kMmaKT + ktw - 1) / ktw);
   const int64_t blocks = (warps * 32 + threads - 1) / threads;
-  return launch_pdl(mma_fp4(f) ? k_quantize_act<true> : k_quantize_act<false>, dim3((unsigned)blocks),
-                    dim3(threads), 0, s, src, stride, perm, top_k, gather ? 1 : 0, offsets, pad_off, pos_expert, meta,
-                    S_max, K, kp, rb, bn, q, sf, ktw);
+  auto k = mma_fp4(f) ? (wide ? k_quantize_act<true, kQuantKt> : k_quantize_act<true, 1>)
+                      : (wide ? k_quantize_act<false, kQuantKt> : k_quantize_act<false, 1>);
+  return launch_pdl(k, dim3((unsigned)blocks), dim3(threads), 0, s, src, stride, perm, top_k, gather ? 1 : 0, offsets,
+                    pad_off, pos_expert, meta, S_max, K, kp, rb, bn, q, sf);
 }
 
 cudaError_t launch_mma_gemm(const MmaLaunch &a, int bn, ActFmt f, int sm_count, cudaStream_t s) {
