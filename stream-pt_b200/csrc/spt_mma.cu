@@ -594,6 +594,26 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float v[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 64 columns of this warp's 32 TMEM lanes in one load (and its wait).
+__device__ __forceinline__ void tc_ld64(uint32_t taddr, float v[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float v[16]);
 // Columns [taddr, taddr + C) of this warp's 32 TMEM lanes, C = 8 or 16.
 template <int C>
@@ -863,15 +883,19 @@ struct GemmCta {
     const uint64_t sfa_desc0 = smem_desc(base + S::kOffSfa, 128, 0);
     const uint64_t sfb_desc0 = smem_desc(base + S::kOffSfb, 128, 0);
     constexpr uint64_t kStage16 = S::kStage >> 4, kA16 = S::kA >> 4, kBt16 = S::kBt >> 4, kBTerm16 = S::kBTerm >> 4;
-    // K step ks reads 32 bytes further along each row; FP4 steps use scale
-    // bytes 2ks and 2ks+1 of the atom (two 32-blocks), FP8 steps byte ks.
-    uint32_t idesc[S::kKSteps];
-#pragma unroll
-    for (int ks = 0; ks < S::kKSteps; ++ks)
-      idesc[ks] = FP4 ? idesc_mxf4(S::kN, 2 * ks, 2 * ks) : idesc_mxf8f6f4(S::kN, ks, ks);
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const int kt_lo = 0, kt_hi = a.ktiles;
-      const int nm = MG == 1 ? 1 : min(MG, a.mtiles - tile_info<BN>(tt, tile, n_active, a.mtiles).mt * MG);
+      const TileInfo ti = tile_info<BN>(tt, tile, n_active, a.mtiles);
+      const int nm = MG == 1 ? 1 : min(MG, a.mtiles - ti.mt * MG);
+      // K step ks reads 32 bytes further along each row; FP4 steps use scale
+      // bytes 2ks and 2ks+1 of the atom (two 32-blocks), FP8 steps byte ks.
+      // With one operand per term the MMAs cover only the unit's tokens,
+      // rounded up to 16 (the last token tile of an expert is often short).
+      const int n_mma = S::kStacked ? S::kN : min(S::kN, (ti.nvalid + 15) & ~15);
+      uint32_t idesc[S::kKSteps];
+#pragma unroll
+      for (int ks = 0; ks < S::kKSteps; ++ks)
+        idesc[ks] = FP4 ? idesc_mxf4(n_mma, 2 * ks, 2 * ks) : idesc_mxf8f6f4(n_mma, ks, ks);
       const int buf = local % S::kAccBufs;
       const uint32_t accph = (uint32_t)(local / S::kAccBufs) & 1u;
       if (!mbar_wait(&acce[buf], accph ^ 1u, a.err, 2, a.wait_shift)) return false;
@@ -960,10 +984,49 @@ struct GemmCta {
       if (!mbar_wait(&accf[buf], accph, a.err, 5, a.wait_shift)) return false;
       tc_fence_after();
       const int nm = min(MG, a.mtiles - t.mt * MG);
+      if constexpr (!S::kStacked) {
+        // Prefill tiles: this warp's half of the columns in one TMEM load per
+        // row tile.  Gate/up: rows 2d (gate) and 2d+1 (up) sit in neighbouring
+        // lanes; per pair of columns (c, c+1) each lane sends its partner the
+        // value the partner lacks, the gate lane finishes column c and the up
+        // lane column c+1 -- every lane computes SwiGLU, for half the columns.
+        constexpr int kG = kCols >= 64 ? 64 : 32;
+        static_assert(kCols % kG == 0, "epilogue column groups");
+        for (int m = 0; m < nm; ++m) {
+          const int r = (t.mt * MG + m) * kMmaM + row_local;
+          const bool is_up = (r & 1) != 0;
+          const int d = a.mode == 0 ? r >> 1 : r;
+          const float *bsrc = a.mode == 0 ? (is_up ? a.bias1 : a.bias0) : a.bias0;
+          const float bias = (bsrc && d < a.out_rows) ? bsrc[(size_t)t.e * a.out_rows + d] : 0.0f;
+          for (int c0 = half * kCols; c0 < (half + 1) * kCols && c0 < t.nvalid; c0 += kG) {
+            float v[kG];
+            const uint32_t col =
+                tmem + (uint32_t)((buf * MG + m) * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
+            if constexpr (kG == 64) tc_ld64(col, v);
+            else tc_ld32(col, v);
+            if (a.mode == 0) {
+#pragma unroll
+              for (int j = 0; j < kG; j += 2) {
+                const float v0 = v[j] + bias, v1 = v[j + 1] + bias;
+                const float recv = __shfl_xor_sync(0xffffffffu, is_up ? v0 : v1, 1);
+                const float g = is_up ? recv : v0, u = is_up ? v1 : recv;
+                const int c = c0 + j + (is_up ? 1 : 0);
+                if (c < t.nvalid && d < a.out_rows)
+                  a.y[(size_t)(t.p0 + c) * a.y_stride + d] = swiglu_f32(g, u);
+              }
+            } else if (r < a.out_rows) {
+#pragma unroll
+              for (int j = 0; j < kG; ++j)
+                if (c0 + j < t.nvalid) a.y[(size_t)(t.p0 + c0 + j) * a.y_stride + r] = v[j] + bias;
+            }
+          }
+        }
+      } else
       for (int m = 0; m < nm; ++m) {
       const int r = (t.mt * MG + m) * kMmaM + row_local;
       constexpr int kC = BN < 16 ? BN : 16;  // accumulator columns per TMEM load
-      for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += kC) {
+      // columns past the unit's tokens were not written by the MMAs
+      for (int c0 = half * kCols; c0 < (half + 1) * kCols && c0 < t.nvalid; c0 += kC) {
         float v[kC];
         const uint32_t col = tmem + (uint32_t)((buf * MG + m) * S::kAccStride + c0) + ((uint32_t)(quad * 32) << 16);
         if constexpr (FP4 && BN == 8 && kFp4Terms == 4) {
