@@ -25,14 +25,14 @@ __device__ __forceinline__ float swiglu_ref(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, d), __fadd_rn(u, 1.0f));
 }
 
-// The same activation with a float exponential (CUDA's expf, within a few
-// ulp of the double-precision value the reference rounds): for the tensor-core
-// paths, whose products already differ from the reference's by far more.
+// The same activation with the fast float exponential and division
+// intrinsics (relative error about 1e-6): for the tensor-core path, whose
+// products already differ from the reference's by about 1e-4 of each block.
 __device__ __forceinline__ float swiglu_f32(float g, float u) {
   g = go_min(g, 7.0f);
   u = go_max(-7.0f, go_min(u, 7.0f));
-  const float e = expf(__fmul_rn(-1.702f, g));
-  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), __fadd_rn(u, 1.0f));
+  const float e = __expf(-1.702f * g);
+  return __fdividef(g, 1.0f + e) * (u + 1.0f);
 }
 
 // Programmatic dependent launch.  A kernel launched with the programmatic
