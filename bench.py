@@ -412,6 +412,20 @@ def cpu_baseline(name, seconds=12.0, workers=None):
     return tps, workers, f"{what} of {name} ({el:.1f} s, memory-resident weights, oracle-generated)"
 
 
+def native_libraries():
+    """Shared objects of this repository mapped into the process."""
+    found = set()
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                path = line.split()[-1] if line.strip() else ""
+                if path.endswith(".so") and os.path.realpath(path).startswith(os.path.realpath(ROOT) + os.sep):
+                    found.add(os.path.relpath(os.path.realpath(path), os.path.realpath(ROOT)))
+    except OSError:
+        return None
+    return sorted(found)
+
+
 def run_reference(args):
     rank, world, _ = dist_info()
     if rank != 0:
@@ -424,7 +438,8 @@ def run_reference(args):
             "vs_baseline": None, "dtype": "f32 (mxfp4 weights)", "data": "synthetic", "impl": "reference",
             "config": workload_config(args.config, world, ep_mode(args.config)),
             "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
-            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "native_so_loaded": native_libraries()}
     print(json.dumps(line), flush=True)
 
 
@@ -671,6 +686,7 @@ def run_ours(args):
         line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         line["clocks"] = clocks.summary()
+        line["native_so_loaded"] = native_libraries()
         print(json.dumps(line), flush=True)
     ctx.close()
     if world > 1:
