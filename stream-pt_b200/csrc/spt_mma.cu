@@ -720,10 +720,10 @@ struct MmaShape {
   static_assert(kAccCols + kSfCols <= 512, "TMEM columns");
   static_assert(kStages >= 2, "stage ring");
   static_assert(MG == 1 || (KS == 1 && BN == 128), "row-tile groups: one K tile per stage, 128-token tiles");
-  // epilogue warps: two per TMEM lane quadrant (each takes half of the
-  // columns) with row-tile groups, whose single-buffered accumulators wait
-  // for the epilogue; one per quadrant otherwise
-  static constexpr int kEpiWarps = MG > 1 ? 8 : 4;
+  // epilogue warps: with row-tile groups, whose single-buffered accumulators
+  // make the next unit's MMAs wait for the epilogue, four per TMEM lane
+  // quadrant (each takes a quarter of the columns); one per quadrant otherwise
+  static constexpr int kEpiWarps = MG > 1 ? 16 : 4;
   static constexpr int kThreads = 32 * (2 + kEpiWarps);
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
@@ -975,8 +975,9 @@ struct GemmCta {
                            int lane) {
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_local = quad * 32 + lane;
-    const int half = S::kEpiWarps == 8 ? (warp - 2) / 4 : 0;  // column half of this warp (8 epilogue warps)
-    constexpr int kCols = S::kEpiWarps == 8 ? BN / 2 : BN;
+    constexpr int kParts = S::kEpiWarps / 4;  // epilogue warps per TMEM lane quadrant
+    const int half = (warp - 2) / 4;          // this warp's share of the columns
+    constexpr int kCols = BN / kParts;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const TileInfo t = tile_info<BN>(tt, tile, n_active, a.mtiles);
       const int buf = local % S::kAccBufs;
@@ -985,7 +986,7 @@ struct GemmCta {
       tc_fence_after();
       const int nm = min(MG, a.mtiles - t.mt * MG);
       if constexpr (!S::kStacked) {
-        // Prefill tiles: this warp's half of the columns in one TMEM load per
+        // Prefill tiles: this warp's share of the columns in one TMEM load per
         // row tile.  Gate/up: rows 2d (gate) and 2d+1 (up) sit in neighbouring
         // lanes; per pair of columns (c, c+1) each lane sends its partner the
         // value the partner lacks, the gate lane finishes column c and the up
