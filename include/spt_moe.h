@@ -189,8 +189,8 @@ spt_status spt_synth_normal_host(uint64_t seed, uint64_t stream, float mean, flo
 /* SPT_PATH_EXACT: CUDA-core MXFP4 GEMV reproducing the reference's AVX2
  * arithmetic bit for bit (needs an SPT_ARENA_GEMV arena).
  * SPT_PATH_MMA: tcgen05 block-scaled grouped GEMM on the packed FP4 weights,
- * activations written as block-scaled terms (4 e2m1 terms for token tiles of
- * 8 or 16, 3 e4m3 terms for 128-token tiles), fp32 accumulation; routing
+ * activations written as block-scaled terms (4 e2m1 terms; 3 e4m3 terms for
+ * 128-token tiles with SPT_OPT_PREFILL_FP8), fp32 accumulation; routing
  * stays bit-exact, block outputs agree with the reference to a few 1e-4 of
  * the largest output (needs SPT_ARENA_MMA).
  * SPT_PATH_GEMV16: decode GEMV on the same packed weights: in-register
