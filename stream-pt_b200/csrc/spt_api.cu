@@ -74,6 +74,7 @@ struct spt_context {
   int kernels_last = 0;
   DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
   DevBuf stack_norm, stack_ffn;  // layer stack: normed rows and block output [T][H]
+  DevBuf g16_count;  // decode GEMV: arrivals per down row group of the fused combine (zero between launches)
   DevBuf xq, xe, actq, act_off;  // decode GEMV: split x rows, their exponents, split SwiGLU rows,
                                  // first dispatch position of each active expert
   int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
@@ -705,6 +706,11 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
     SPT_CUDA(ctx, ctx->xq.ensure(sizeof(__half) * 2 * kph * std::max<int64_t>(T, 1)));
     SPT_CUDA(ctx, ctx->xe.ensure(sizeof(int32_t) * std::max<int64_t>(T, 1)));
     SPT_CUDA(ctx, ctx->act_off.ensure(sizeof(int32_t) * (E + 1)));
+    const size_t cnt = sizeof(int32_t) * 4 * (size_t)L.dn_mma.mtiles;
+    if (ctx->g16_count.bytes < cnt) {
+      SPT_CUDA(ctx, ctx->g16_count.ensure(cnt));
+      SPT_CUDA(ctx, cudaMemsetAsync(ctx->g16_count.p, 0, ctx->g16_count.bytes, ctx->stream));
+    }
     SPT_CUDA(ctx, ctx->actq.ensure(sizeof(__half) * 2 * kpd * std::max<int64_t>(S, 1)));
     return SPT_OK;
   }
@@ -737,6 +743,10 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // and top-k (the expert-parallel receive side passes its shard and top-k 1).
 // With `logits` (one device, T <= kSelectDispatchMaxTokens) the top-k
 // selection runs inside the dispatch kernel and writes sel_idx / sel_w there.
+// Decode GEMV batches of up to this many slots combine inside the down
+// launch (one launch fewer; the last CTA of each row group does the sums).
+constexpr int64_t kFusedCombineSlots = 64;
+
 spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
                            int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0,
                            const float *logits = nullptr, bool x_split_done = false) {
@@ -745,6 +755,7 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   cudaStream_t s = ctx->stream;
   spt_status st = SPT_OK;
   const int max_active = (int)std::min<int64_t>(E, T * K);
+  bool fused_combine = false;  // the decode GEMV's down launch also combines
   ExpertPath path;
   if ((st = pick_path(ctx, L, c, T, &path))) return st;
   if ((st = reserve_experts(ctx, L, c, T, bn_hint))) return st;
@@ -824,10 +835,20 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
     d.actq = nullptr;
     d.y = ctx->res.as<float>();
     d.y_stride = H;
+    // decode batches: the combine runs in the down launch's last CTAs
+    fused_combine = T * K <= kFusedCombineSlots;
+    if (fused_combine) {
+      d.cw = sel_w;
+      d.cslot = ctx->slot_pos.as<int32_t>();
+      d.ct = (int)T;
+      d.ck = K;
+      d.cout = out;
+      d.ccount = ctx->g16_count.as<int32_t>();
+    }
     SPT_MARK(6);
     SPT_CUDA(ctx, launch_gemv16(d, 1, max_active, s));
-    // router, select, dispatch, [split x], gate/up, down, combine
-    ctx->kernels_last = x_split_done ? 6 : 7;
+    // router, select, dispatch, [split x], gate/up, down, [combine]
+    ctx->kernels_last = (x_split_done ? 6 : 7) - (fused_combine ? 1 : 0);
   } else if (use_mma) {
     if ((st = forward_mma(ctx, L, c, x, T, s, plan.bn))) return st;
   } else {
@@ -870,7 +891,8 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
     ctx->kernels_last = 6;
   }
   SPT_MARK(7);
-  SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
+  if (!fused_combine)
+    SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
   SPT_MARK(8);
   if (logits) ctx->kernels_last -= 1;  // no separate selection launch
   return SPT_OK;
@@ -958,7 +980,7 @@ std::vector<const void *> call_buffers(const spt_context *ctx) {
   for (const DevBuf *b : {&ctx->logits, &ctx->sel_idx, &ctx->sel_w, &ctx->offsets, &ctx->perm, &ctx->slot_pos,
                           &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res, &ctx->xdev, &ctx->outdev, &ctx->dev_err,
                           &ctx->pad_off, &ctx->tile_gu, &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx,
-                          &ctx->qa, &ctx->sfa, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off})
+                          &ctx->qa, &ctx->sfa, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off, &ctx->g16_count})
     v.push_back(b->p);
   return v;
 }
@@ -1197,7 +1219,8 @@ void spt_context_destroy(spt_context *ctx) {
                       &ctx->slot_pos, &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res,
                       &ctx->xdev, &ctx->outdev, &ctx->dev_err, &ctx->pad_off, &ctx->tile_gu,
                       &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa,
-                      &ctx->stack_norm, &ctx->stack_ffn, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off})
+                      &ctx->stack_norm, &ctx->stack_ffn, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off,
+                      &ctx->g16_count})
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);

@@ -335,6 +335,34 @@ __global__ void __launch_bounds__(256, 2) k_gemv16(const __grid_constant__ Gemv1
     }
     __syncthreads();
   }
+  // Fused combine (down GEMV): the CTA that finishes its row group last
+  // combines that group's rows of every token, in k_combine's arithmetic.
+  if (MODE == 1 && a.cout) {
+    __shared__ int s_last;
+    __threadfence();  // this CTA's y rows, before its arrival is counted
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int prev = atomicAdd(a.ccount + grp, 1);
+      s_last = prev == n_active - 1;
+      if (s_last) a.ccount[grp] = 0;  // every arrival counted: ready for the next launch
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      for (int i = threadIdx.x; i < a.ct * kRowsPerCta; i += blockDim.x) {
+        const int t = i / kRowsPerCta, r = row0 + i % kRowsPerCta;
+        if (r >= a.out_rows) continue;
+        float o = 0.0f;
+        for (int k = 0; k < a.ck; ++k) {
+          const int s = t * a.ck + k;
+          const float w = a.cw[s];
+          if (w <= 0.0f) continue;
+          o = fmaf(__ldcg(a.y + (size_t)a.cslot[s] * a.y_stride + r), w, o);
+        }
+        a.cout[(size_t)t * a.out_rows + r] = o;
+      }
+    }
+  }
 }
 
 // Smallest and largest E8M0 byte of n 17-byte GGUF blocks (byte 0 of each):

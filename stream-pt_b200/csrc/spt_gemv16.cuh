@@ -52,6 +52,15 @@ struct Gemv16Launch {
   int actq_kp = 0;
   float *y = nullptr;            // down output rows [pos][y_stride]
   int64_t y_stride = 0;
+  // down only, optional: the combine of k_combine fused in.  The last CTA
+  // of each 32-row group (counted in ccount[group], which it resets to 0)
+  // writes out[t][rows] = sum over ranks r in order of fma(y[slot_pos[t*K+r]],
+  // sel_w[t*K+r], .) for the ct tokens.
+  const float *cw = nullptr;        // sel_w [ct * ck]
+  const int32_t *cslot = nullptr;   // slot_pos [ct * ck]
+  int ct = 0, ck = 0;
+  float *cout = nullptr;            // [ct][out_rows]
+  int32_t *ccount = nullptr;        // [mtiles * 4], zero between launches
 };
 
 // mode 0: gate/up + SwiGLU -> actq; mode 1: down -> y.  Grid: (32-row groups,
