@@ -749,7 +749,8 @@ constexpr int64_t kFusedCombineSlots = 64;
 
 spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
                            int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0,
-                           const float *logits = nullptr, bool x_split_done = false) {
+                           const float *logits = nullptr, bool x_split_done = false,
+                           const float *resid = nullptr) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
@@ -843,6 +844,7 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
       d.ct = (int)T;
       d.ck = K;
       d.cout = out;
+      d.cresid = resid;
       d.ccount = ctx->g16_count.as<int32_t>();
     }
     SPT_MARK(6);
@@ -892,7 +894,8 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   }
   SPT_MARK(7);
   if (!fused_combine)
-    SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s));
+    SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s,
+                                 resid));
   SPT_MARK(8);
   if (logits) ctx->kernels_last -= 1;  // no separate selection launch
   return SPT_OK;
@@ -922,8 +925,10 @@ spt_status check_layer_limits(spt_context *ctx, const spt_moe_config &c) {
 }
 
 // The whole block on device pointers (enqueue only).
+// With resid, out = resid + block(x) (the layer stack's residual add; out
+// may be resid).
 spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
-                          float *out, int64_t T) {
+                          float *out, int64_t T, const float *resid = nullptr) {
   const spt_moe_config &c = arena->cfg;
   spt_status st = check_layer_limits(ctx, c);
   if (st) return st;
@@ -950,7 +955,7 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
                          path == kPathGemv16 ? &rs : nullptr, &split_done)))
     return st;
   if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out, 0,
-                            fuse ? ctx->logits.as<float>() : nullptr, split_done)))
+                            fuse ? ctx->logits.as<float>() : nullptr, split_done, resid)))
     return st;
   ctx->last_T = T;
   ctx->last_E = c.num_experts;
@@ -2781,11 +2786,17 @@ spt_status forward_stack_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, 
   for (int64_t l = first; l < first + n; ++l) {
     const LayerDev &L = arena->layers[(size_t)l];
     SPT_CUDA(ctx, launch_rmsnorm(x, L.norm, (int)T, (int)H, eps, normed, 8, ctx->stream));
-    spt_status st = ep ? forward_ep_device(ctx, ep, arena, l, normed, ffn, T)
-                       : forward_device(ctx, arena, l, normed, ffn, T);
-    if (st) return st;
-    SPT_CUDA(ctx, launch_add(x, ffn, T * H, ctx->stream));
-    kernels += 2 + ctx->kernels_last;
+    if (ep) {
+      spt_status st = forward_ep_device(ctx, ep, arena, l, normed, ffn, T);
+      if (st) return st;
+      SPT_CUDA(ctx, launch_add(x, ffn, T * H, ctx->stream));
+      kernels += 2 + ctx->kernels_last;
+    } else {
+      // the residual add happens in the block's combine: x = x + block(normed)
+      spt_status st = forward_device(ctx, arena, l, normed, x, T, x);
+      if (st) return st;
+      kernels += 1 + ctx->kernels_last;
+    }
   }
   ctx->kernels_last = kernels;
   return SPT_OK;

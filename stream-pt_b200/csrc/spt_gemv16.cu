@@ -184,6 +184,7 @@ __global__ void __launch_bounds__(256, 2) k_gemv16(const __grid_constant__ Gemv1
   if (ai >= n_active) return;
   const int e = e_raw;  // expert ids are local to the arena's planes (an expert-parallel shard's too)
   const int n_tok = p1 - p0;
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int nkt = a.ktiles > warp ? (a.ktiles - warp + kWarps - 1) / kWarps : 0;
   const int nk = min(nkt, kMaxKtPerWarp);  // the launcher refuses longer K
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(256, 2) k_gemv16(const __grid_constant__ Gemv1
           if (w <= 0.0f) continue;
           o = fmaf(__ldcg(a.y + (size_t)a.cslot[s] * a.y_stride + r), w, o);
         }
+        if (a.cresid) o = __fadd_rn(a.cresid[(size_t)t * a.out_rows + r], o);
         a.cout[(size_t)t * a.out_rows + r] = o;
       }
     }

@@ -60,6 +60,7 @@ struct Gemv16Launch {
   const int32_t *cslot = nullptr;   // slot_pos [ct * ck]
   int ct = 0, ck = 0;
   float *cout = nullptr;            // [ct][out_rows]
+  const float *cresid = nullptr;    // optional [ct][out_rows] added to the sums (may be cout)
   int32_t *ccount = nullptr;        // [mtiles * 4], zero between launches
 };
 

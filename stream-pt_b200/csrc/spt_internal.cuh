@@ -170,8 +170,10 @@ struct GemvLaunch {
 };
 cudaError_t launch_gemv(const GemvLaunch &a, int sm_count, cudaStream_t stream);
 
+// out[t] = sum over ranks of fma(res[slot], w, .) (+ resid[t] when given;
+// out may alias resid).
 cudaError_t launch_combine(const float *res, const float *sel_w, const int32_t *slot_pos, int T,
-                           int K, int H, float *out, cudaStream_t stream);
+                           int K, int H, float *out, cudaStream_t stream, const float *resid = nullptr);
 cudaError_t launch_swiglu(const float *g, const float *u, float *act, int64_t n,
                           cudaStream_t stream);
 cudaError_t launch_rmsnorm(const float *x, const float *w, int T, int dim, float eps, float *y,

@@ -686,9 +686,12 @@ __global__ void __launch_bounds__(128) k_gemv(const GemvLaunch a) {
 // ---------------------------------------------------------------------------
 // Combine: out[t,h] = 0, then for r = 0..K-1 with weight > 0 or NaN,
 // out = fma(res[slot], w, out) (forward/moe_batch.go:163-192).
+// With resid the sum is added to resid (the residual stream of the layer
+// stack, addVector forward/layer.go:305-340: out = resid + sum, one rounding);
+// out may be resid itself (each element is read and written by one thread).
 __global__ void k_combine(const float *__restrict__ res, const float *__restrict__ sel_w,
                           const int32_t *__restrict__ slot_pos, int T, int K, int H,
-                          float *__restrict__ out) {
+                          const float *resid, float *out) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.y;
@@ -705,6 +708,10 @@ __global__ void k_combine(const float *__restrict__ res, const float *__restrict
     o.y = fmaf(v.y, w, o.y);
     o.z = fmaf(v.z, w, o.z);
     o.w = fmaf(v.w, w, o.w);
+  }
+  if (resid) {
+    const float4 x = *reinterpret_cast<const float4 *>(resid + (size_t)t * H + h);
+    o = make_float4(__fadd_rn(x.x, o.x), __fadd_rn(x.y, o.y), __fadd_rn(x.z, o.z), __fadd_rn(x.w, o.w));
   }
   *reinterpret_cast<float4 *>(out + (size_t)t * H + h) = o;
 }
@@ -962,11 +969,12 @@ cudaError_t launch_gemv(const GemvLaunch &a, int sm_count, cudaStream_t stream) 
 }
 
 cudaError_t launch_combine(const float *res, const float *sel_w, const int32_t *slot_pos, int T,
-                           int K, int H, float *out, cudaStream_t stream) {
+                           int K, int H, float *out, cudaStream_t stream, const float *resid) {
   if (T <= 0) return cudaSuccess;
   const int threads = 128;
   dim3 grid((H / 4 + threads - 1) / threads, T);
-  cudaError_t e = launch_pdl(k_combine, dim3(grid), dim3(threads), 0, stream, res, sel_w, slot_pos, T, K, H, out);
+  cudaError_t e = launch_pdl(k_combine, dim3(grid), dim3(threads), 0, stream, res, sel_w, slot_pos, T, K, H, resid,
+                             out);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
