@@ -95,8 +95,7 @@ def workload_config(name, world, ep_mode=None):
     if world == 1:
         par = "single GPU"
     else:
-        par = (f"ep{world}: {E // world} experts per GPU, {t_rank} tokens per rank, NCCL dispatch/combine "
-               f"({ep_mode})")
+        par = f"ep{world}: {E // world} experts per GPU, {t_rank} tokens per rank, dispatch/combine ({ep_mode})"
     return {"workload": f"{name}: {c['desc']}", "tokens_per_step": t_all, "tokens_per_rank": t_rank,
             "hidden": H, "expert_dim": D, "experts": E, "top_k": K, "layers": c.get("layers", 1),
             "seed": c["seed"], "router_bias": c["router_bias"], "zipf_s": c["zipf_s"], "zipf_beta": c["zipf_beta"],
@@ -444,7 +443,9 @@ def run_reference(args):
 
 
 def ep_mode(name):
-    return "counts-first, live rows only" if tokens(name, 1)[0] > 256 else "fixed capacity"
+    """Every config uses the fixed-capacity exchange: through the NVLink peer
+    windows only live rows move and no call synchronises with the host."""
+    return "fixed capacity, NVLink peer windows, live rows only"
 
 
 # ---------------------------------------------------------------------------
@@ -474,8 +475,7 @@ class Runner:
             uid = [spt.ep_unique_id() if rank == 0 else None]
             torch.distributed.broadcast_object_list(uid, src=0)
             self.ep = spt.ExpertParallel(ctx, uid[0], rank, world)
-            if ep_mode(name) == "fixed capacity":
-                self.ep.set_capacity(self.T)  # no host synchronisation per step
+            self.ep.set_capacity(self.T)  # no host synchronisation per step
         else:
             self.arena = ctx.synthetic_arena(cfg, params, n_layers=self.layers, flags=flags)
         self.stream = torch.cuda.ExternalStream(ctx.stream)

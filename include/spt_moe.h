@@ -442,6 +442,18 @@ void spt_ep_destroy(spt_ep *ep);
  * tokens fail with SPT_ERR_DIMENSIONS.  0 (the default) exchanges counts
  * first and sends only live rows (one host synchronisation per call). */
 spt_status spt_ep_set_capacity(spt_ep *ep, int64_t max_tokens_per_rank);
+/* Transport of the fixed-capacity exchange.  SPT_EP_EXCHANGE_PEER (the
+ * default, when every rank has its own GPU): each rank's receive window is
+ * mapped into every other rank (CUDA IPC, set up by the first fixed-capacity
+ * call, collectively); senders write their live rows straight into the
+ * owners' windows over NVLink and publish a sequence number, receivers wait
+ * on it on the device (bounded by SPT_OPT_WAIT_LIMIT, SPT_ERR_TIMEOUT at the
+ * next synchronisation): no NCCL call and no padding rows per call.  Ranks
+ * that share a GPU fall back to SPT_EP_EXCHANGE_NCCL (grouped send/receive of
+ * full slots).  Every rank must choose the same transport. */
+#define SPT_EP_EXCHANGE_PEER 0
+#define SPT_EP_EXCHANGE_NCCL 1
+spt_status spt_ep_set_exchange(spt_ep *ep, int32_t exchange);
 /* Device pointers (16-byte aligned), this rank's `batch` tokens.  Enqueues on
  * the context's stream; without a capacity it synchronises the stream once,
  * after the per-rank row counts are exchanged. */

@@ -34,6 +34,7 @@ PATH_AUTO, PATH_EXACT, PATH_MMA, PATH_GEMV16 = 0, 1, 2, 3
 OPT_TILE_TOKENS, OPT_FUSED_SELECT, OPT_L2_PREFETCH, OPT_GEMV16_SLOTS, OPT_WAIT_LIMIT, OPT_FAULT_STAGE = 1, 2, 3, 4, 5, 6
 OPT_HOST_GRAPHS = 7
 OPT_PREFILL_FP8 = 8
+EP_EXCHANGE_PEER, EP_EXCHANGE_NCCL = 0, 1
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16, GGML_MXFP4 = 0, 1, 8, 30, 39
 
@@ -238,6 +239,7 @@ def lib():
         "spt_ep_create": ([vp, vp, i32, i32, P(vp)], st),
         "spt_ep_destroy": ([vp], None),
         "spt_ep_set_capacity": ([vp, i64], st),
+        "spt_ep_set_exchange": ([vp, i32], st),
         "spt_forward_moe_batch_ep_device": ([vp, vp, vp, i64, vp, vp, i64], st),
         "spt_forward_moe_batch_ep": ([vp, vp, vp, i64, vp, i64, vp, i64, i64, vp], st),
         "spt_arena_create_range": ([vp, vp, P(_Config), vp, i64, ctypes.c_uint32, i64, i64, P(vp)], st),
@@ -737,6 +739,11 @@ class ExpertParallel:
     def set_capacity(self, max_tokens_per_rank: int):
         """Fixed-capacity exchange (no host synchronisation); same value on every rank."""
         self.ctx.check(lib().spt_ep_set_capacity(self._h, max_tokens_per_rank))
+
+    def set_exchange(self, exchange: int):
+        """spt_ep_set_exchange: EP_EXCHANGE_PEER (NVLink peer windows) or
+        EP_EXCHANGE_NCCL for the fixed-capacity exchange."""
+        self.ctx.check(lib().spt_ep_set_exchange(self._h, exchange))
 
     def close(self):
         if self._h:

@@ -653,7 +653,8 @@ spt_status check_device_error(spt_context *ctx) {
   SPT_CUDA(ctx, cudaMemcpy(&e, ctx->dev_err.p, sizeof e, cudaMemcpyDeviceToHost));
   if (e != 0) {
     cudaMemset(ctx->dev_err.p, 0, sizeof e);
-    return fail(ctx, SPT_ERR_TIMEOUT, "tensor-core GEMM: bounded wait %d gave up", e);
+    return fail(ctx, SPT_ERR_TIMEOUT, "%s: bounded wait %d gave up",
+                e >= 20 ? "expert-parallel peer exchange" : "tensor-core GEMM", e);
   }
   return SPT_OK;
 }
@@ -1112,7 +1113,8 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
     *ctx->err_host = 0;
     SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
     SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-    return fail(ctx, SPT_ERR_TIMEOUT, "tensor-core GEMM: bounded wait %d gave up", e);
+    return fail(ctx, SPT_ERR_TIMEOUT, "%s: bounded wait %d gave up",
+                e >= 20 ? "expert-parallel peer exchange" : "tensor-core GEMM", e);
   }
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
   return SPT_OK;
@@ -2306,6 +2308,14 @@ struct spt_ep {
   DevBuf rows_out;       // their results [R][H]
   int32_t *counts_host = nullptr;  // pinned [2*world]
   std::vector<int64_t> soff, roff;  // prefix offsets (rows) per rank
+  // peer-memory exchange of the fixed-capacity layout (one GPU per rank)
+  int exchange = SPT_EP_EXCHANGE_PEER;  // transport of the fixed-capacity exchange
+  bool peer_tried = false;  // set-up attempted for the current window shape
+  bool peer_ok = false;     // windows mapped: the fixed-capacity calls use them
+  EpPeerLayout lay;         // base[] = every rank's window in this process
+  void *win = nullptr;      // this rank's window (cudaMalloc, shared by IPC)
+  DevBuf arrive;            // [2] arrival counters of the send and return kernels
+  uint64_t seq = 0;         // calls made through the windows
 };
 
 namespace {
@@ -2436,6 +2446,191 @@ spt_status exchange_fixed(spt_ep *ep, std::initializer_list<FixedItem> items) {
   return wait_comm(ep, "exchange");
 }
 
+// ---- peer-memory windows ---------------------------------------------------
+// One record per rank, exchanged once over the communicator: its window's
+// IPC handle and its device's UUID (peer mode needs one GPU per rank).
+struct PeerRecord {
+  cudaIpcMemHandle_t handle;
+  unsigned char uuid[16];
+  int64_t bytes;
+  unsigned char pad[128 - sizeof(cudaIpcMemHandle_t) - 16 - sizeof(int64_t)];
+};
+static_assert(sizeof(PeerRecord) == 128, "peer record");
+
+void ep_peer_release(spt_ep *ep) {
+  if (!ep->win) return;
+  if (ep->ctx && ep->ctx->stream) cudaStreamSynchronize(ep->ctx->stream);
+  for (int r = 0; r < ep->world; ++r)
+    if (r != ep->rank && ep->lay.base[r]) cudaIpcCloseMemHandle(ep->lay.base[r]);
+  cudaFree(ep->win);
+  ep->win = nullptr;
+  ep->peer_ok = false;
+  for (int r = 0; r < kEpMaxPeers; ++r) ep->lay.base[r] = nullptr;
+}
+
+// Collective (every rank at the same call): windows for cap rows per peer and
+// hidden width H, mapped into every process.  Leaves peer_ok false (the NCCL
+// exchange is used) when two ranks share a GPU or the set-up fails on a rank;
+// every rank reaches the same decision from the same records.
+spt_status ep_peer_setup(spt_ep *ep, int64_t cap, int64_t H) {
+  spt_context *ctx = ep->ctx;
+  const int W = ep->world;
+  if (ep->peer_tried && (!ep->peer_ok || (ep->lay.cap >= cap && ep->lay.hidden == H))) return SPT_OK;
+  ep_peer_release(ep);
+  ep->peer_tried = true;
+  if (W > kEpMaxPeers || ep->exchange != SPT_EP_EXCHANGE_PEER) return SPT_OK;
+  EpPeerLayout L;
+  L.world = W;
+  L.rank = ep->rank;
+  L.cap = (int)cap;
+  L.hidden = (int)H;
+  auto align = [](int64_t v) { return (v + 255) / 256 * 256; };
+  int64_t off = 0;
+  L.rows_off = off;
+  off = align(off + 2 * W * cap * H * (int64_t)sizeof(float));
+  L.ret_off = off;
+  off = align(off + 2 * W * cap * H * (int64_t)sizeof(float));
+  L.ids_off = off;
+  off = align(off + 2 * W * cap * (int64_t)sizeof(int32_t));
+  L.cnt_off = off;
+  off = align(off + 2 * W * (int64_t)sizeof(int32_t));
+  L.ffwd_off = off;
+  off = align(off + W * (int64_t)sizeof(uint64_t));
+  L.fret_off = off;
+  off = align(off + W * (int64_t)sizeof(uint64_t));
+  L.bytes = off;
+  // this rank's record; a failed allocation still takes part (bytes = 0)
+  PeerRecord mine;
+  memset(&mine, 0, sizeof mine);
+  cudaDeviceProp prop;
+  SPT_CUDA(ctx, cudaGetDeviceProperties(&prop, ctx->device));
+  memcpy(mine.uuid, &prop.uuid, 16);
+  if (cudaMalloc(&ep->win, (size_t)L.bytes) == cudaSuccess &&
+      cudaMemset(ep->win, 0, (size_t)L.bytes) == cudaSuccess &&
+      cudaIpcGetMemHandle(&mine.handle, ep->win) == cudaSuccess) {
+    mine.bytes = L.bytes;
+  } else {
+    cudaGetLastError();
+    if (ep->win) cudaFree(ep->win);
+    ep->win = nullptr;
+  }
+  SPT_CUDA(ctx, cudaDeviceSynchronize());
+  DevBuf send, recv;
+  SPT_CUDA(ctx, send.ensure(sizeof(PeerRecord) * W));
+  SPT_CUDA(ctx, recv.ensure(sizeof(PeerRecord) * W));
+  for (int r = 0; r < W; ++r)
+    SPT_CUDA(ctx, cudaMemcpy(send.as<uint8_t>() + sizeof(PeerRecord) * r, &mine, sizeof mine, cudaMemcpyHostToDevice));
+  spt_status st = exchange_fixed(ep, {{send.p, recv.p, sizeof(PeerRecord), 1, ncclUint8}});
+  if (!st) st = wait_stream(ep, "peer window exchange");
+  std::vector<PeerRecord> rec(W);
+  if (!st) SPT_CUDA(ctx, cudaMemcpy(rec.data(), recv.p, sizeof(PeerRecord) * W, cudaMemcpyDeviceToHost));
+  send.release();
+  recv.release();
+  if (st) return st;
+  bool usable = true;
+  for (int r = 0; r < W; ++r) {
+    usable = usable && rec[r].bytes == L.bytes;
+    for (int q = 0; q < r; ++q) usable = usable && memcmp(rec[r].uuid, rec[q].uuid, 16) != 0;
+  }
+  if (usable) {
+    for (int r = 0; r < W; ++r) {
+      if (r == ep->rank) {
+        L.base[r] = static_cast<uint8_t *>(ep->win);
+        continue;
+      }
+      void *p = nullptr;
+      if (cudaIpcOpenMemHandle(&p, rec[r].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        usable = false;  // (a rank that fails here fails every later peer call: see below)
+        break;
+      }
+      L.base[r] = static_cast<uint8_t *>(p);
+    }
+  }
+  ep->lay = L;
+  if (!usable) {
+    // a mapping that failed on one rank only would leave the ranks on
+    // different transports; keep the group consistent by failing instead
+    bool all_distinct = true;
+    for (int r = 0; r < W; ++r)
+      for (int q = 0; q < r; ++q) all_distinct = all_distinct && memcmp(rec[r].uuid, rec[q].uuid, 16) != 0;
+    bool all_alloc = true;
+    for (int r = 0; r < W; ++r) all_alloc = all_alloc && rec[r].bytes == L.bytes;
+    ep_peer_release(ep);
+    ep->lay.cap = (int)cap;
+    ep->lay.hidden = (int)H;
+    if (all_distinct && all_alloc)
+      return fail(ctx, SPT_ERR_CUDA, "cudaIpcOpenMemHandle failed for a peer's expert-parallel window");
+    return SPT_OK;  // shared GPU or an allocation failed: every rank falls back to NCCL
+  }
+  SPT_CUDA(ctx, ep->arrive.ensure(sizeof(int32_t) * 2));
+  SPT_CUDA(ctx, cudaMemset(ep->arrive.p, 0, sizeof(int32_t) * 2));
+  ep->seq = 0;
+  ep->peer_ok = true;
+  ep_trace(ep, "peer windows mapped: %lld bytes each", (long long)L.bytes);
+  return SPT_OK;
+}
+
+// The fixed-capacity call through the peer windows: no NCCL call and no host
+// synchronisation; only live rows cross NVLink.
+spt_status forward_ep_peer(spt_context *ctx, spt_ep *ep, const LayerDev &L, const spt_moe_config &c, const float *x,
+                           float *out, int64_t T) {
+  const int64_t H = c.hidden_dim, E = c.num_experts, K = c.num_experts_used;
+  const int W = ep->world;
+  const int64_t ne = E / W, cap = ep->cap_tokens * K, rows = W * cap, S = T * K;
+  cudaStream_t s = ctx->stream;
+  spt_moe_config lc = c;  // receive side: top-1 over this rank's experts
+  lc.num_experts = ne;
+  lc.num_experts_used = 1;
+  const int bn_hint = pick_bn(ctx, S, 1, ne);
+  spt_status st = ensure_scratch(ctx, ep->cap_tokens, c);
+  if (st) return st;
+  if ((st = reserve_experts(ctx, L, lc, rows, bn_hint))) return st;
+  SPT_CUDA(ctx, ep->sel_w.ensure(sizeof(float) * cap));
+  SPT_CUDA(ctx, ep->send_off.ensure(sizeof(int32_t) * (W + 1)));
+  SPT_CUDA(ctx, ep->send_perm.ensure(sizeof(int32_t) * cap));
+  SPT_CUDA(ctx, ep->send_pos.ensure(sizeof(int32_t) * cap));
+  SPT_CUDA(ctx, ep->dest_list.ensure(sizeof(int32_t) * W));
+  SPT_CUDA(ctx, ep->send_meta.ensure(sizeof(int32_t) * 4));
+  SPT_CUDA(ctx, ep->rows_out.ensure(sizeof(float) * rows * H));
+  if (!ctx->dev_err.p) {  // the device waits' error flag
+    SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
+    SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
+  }
+  const EpPeerLayout &lay = ep->lay;
+  const uint64_t seq = ++ep->seq;
+  const int par = (int)(seq & 1u);
+  int32_t *err = ctx->dev_err.as<int32_t>();
+  ep_trace(ep, "peer call %llu T=%lld, %lld rows per peer", (unsigned long long)seq, (long long)T, (long long)cap);
+  // 1. route, group by owner rank, rows straight into the owners' windows
+  if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>()))) return st;
+  SPT_CUDA(ctx, cudaMemcpyAsync(ep->sel_w.p, ctx->sel_w.p, sizeof(float) * S, cudaMemcpyDeviceToDevice, s));
+  SPT_CUDA(ctx, launch_dispatch(ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), (int)S, W,
+                                ep->send_off.as<int32_t>(), ep->send_perm.as<int32_t>(), ep->send_pos.as<int32_t>(),
+                                ep->dest_list.as<int32_t>(), ep->send_meta.as<int32_t>(), s, nullptr, (int)ne));
+  SPT_CUDA(ctx, launch_ep_send_peer(x, ctx->sel_idx.as<int32_t>(), ep->send_perm.as<int32_t>(),
+                                    ep->send_off.as<int32_t>(), ep->send_meta.as<int32_t>(), (int)K, (int)ne, (int)S,
+                                    lay, par, seq, ep->send_pos.as<int32_t>(), ep->arrive.as<int32_t>(), s));
+  // 2. every sender's rows for this call have landed here
+  SPT_CUDA(ctx, launch_ep_wait(lay, lay.ffwd_off, seq, ctx->opt_wait_shift, err, 20, s));
+  // 3. expert products for the live received rows
+  const float *xr = reinterpret_cast<const float *>(lay.base[lay.rank] + lay.rows_off) + (size_t)par * rows * H;
+  const int32_t *mr = reinterpret_cast<const int32_t *>(lay.base[lay.rank] + lay.ids_off) + (size_t)par * rows;
+  SPT_CUDA(ctx, launch_ep_recv_weights_peer(lay, par, ctx->sel_w.as<float>(), s));
+  if ((st = experts_combine(ctx, L, lc, xr, rows, mr, ctx->sel_w.as<float>(), ep->rows_out.as<float>(), bn_hint)))
+    return st;
+  const int recv_kernels = 2 + ctx->kernels_last - 2;  // wait, weights + experts_combine's (no router/select)
+  // 4. results straight back into the senders' windows, then the rank-ordered
+  //    combine once every owner's results have landed here
+  SPT_CUDA(ctx, launch_ep_return_peer(ep->rows_out.as<float>(), lay, par, seq, ep->arrive.as<int32_t>() + 1, s));
+  SPT_CUDA(ctx, launch_ep_wait(lay, lay.fret_off, seq, ctx->opt_wait_shift, err, 21, s));
+  ep->pending = true;
+  const float *ret = reinterpret_cast<const float *>(lay.base[lay.rank] + lay.ret_off) + (size_t)par * rows * H;
+  SPT_CUDA(ctx, launch_combine(ret, ep->sel_w.as<float>(), ep->send_pos.as<int32_t>(), (int)T, (int)K, (int)H, out, s));
+  ctx->kernels_last = 6 + recv_kernels;  // router, select, rank grouping, send, return, wait, combine + receive side
+  return SPT_OK;
+}
+
 // Fixed-capacity variant: every rank sends every peer a slot of cap =
 // cap_tokens * K rows (the live count travels in the same group), so no count
 // reaches the host and the call never synchronises.  The receiving rank
@@ -2520,7 +2715,8 @@ spt_status forward_ep_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, int
     if (T > ep->cap_tokens)
       return fail(ctx, SPT_ERR_DIMENSIONS, "batch %lld exceeds the group's capacity of %lld tokens per rank",
                   (long long)T, (long long)ep->cap_tokens);
-    return forward_ep_cap(ctx, ep, L, c, x, out, T);
+    if ((st = ep_peer_setup(ep, ep->cap_tokens * K, H))) return st;
+    return ep->peer_ok ? forward_ep_peer(ctx, ep, L, c, x, out, T) : forward_ep_cap(ctx, ep, L, c, x, out, T);
   }
   // A previous call's result exchange may still be in flight (device entry
   // point): let it finish before this call's buffers can grow.
@@ -2679,9 +2875,10 @@ void spt_ep_destroy(spt_ep *ep) {
     if (ctx->stream && !ep->broken) (void)wait_stream(ep, "exchange before destroy");
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   }
+  ep_peer_release(ep);
   if (ep->comm && !ep->broken) nccl().comm_destroy(ep->comm);
   for (DevBuf *b : {&ep->sel_w, &ep->send_off, &ep->send_perm, &ep->send_pos, &ep->dest_list, &ep->send_meta,
-                    &ep->xs, &ep->ms, &ep->ret, &ep->counts, &ep->xr, &ep->mr, &ep->rows_out})
+                    &ep->xs, &ep->ms, &ep->ret, &ep->counts, &ep->xr, &ep->mr, &ep->rows_out, &ep->arrive})
     b->release();
   if (ep->counts_host) cudaFreeHost(ep->counts_host);
   delete ep;
@@ -2697,6 +2894,22 @@ spt_status spt_ep_set_capacity(spt_ep *ep, int64_t max_tokens_per_rank) {
     ep->pending = false;
   }
   ep->cap_tokens = max_tokens_per_rank;
+  return SPT_OK;
+}
+
+spt_status spt_ep_set_exchange(spt_ep *ep, int32_t exchange) {
+  if (!ep) return fail(nullptr, SPT_ERR_NULL_ARG, "nil expert-parallel group");
+  if (exchange != SPT_EP_EXCHANGE_PEER && exchange != SPT_EP_EXCHANGE_NCCL)
+    return fail(ep->ctx, SPT_ERR_UNSUPPORTED, "unknown exchange %d", exchange);
+  if (exchange == ep->exchange) return SPT_OK;
+  if (ep->pending) {
+    spt_status st = wait_stream(ep, "exchange before a transport change");
+    if (st) return st;
+    ep->pending = false;
+  }
+  ep->exchange = exchange;
+  ep->peer_tried = false;  // the next fixed-capacity call sets up (or drops) the windows
+  ep_peer_release(ep);
   return SPT_OK;
 }
 

@@ -139,6 +139,32 @@ cudaError_t launch_ep_gather_cap(const float *x, const int32_t *sel_idx, const i
                                  const int32_t *meta, int K, int experts_per_rank, int H, int S, int world, int cap,
                                  float *xs, int32_t *ms, int32_t *counts, int32_t *slot_pos, cudaStream_t stream);
 cudaError_t launch_ep_recv_weights(const int32_t *counts, int cap, int world, float *w, cudaStream_t stream);
+
+// Peer-memory exchange of the fixed-capacity layout (one GPU per rank).  The
+// window of every rank, at the same byte offsets (base[r] = rank r's window as
+// mapped in this process):
+//   rows [2][world][cap][hidden] f32  token rows sent here, [call parity][sender][j]
+//   ret  [2][world][cap][hidden] f32  result rows of this rank's slots, [parity][owner][j]
+//   ids  [2][world][cap] i32          local expert id of each row in `rows`
+//   cnt  [2][world] i32               rows each sender sent here
+//   ffwd [world] u64, fret [world] u64  last call (sequence number) whose rows /
+//                                     results from each rank have landed
+constexpr int kEpMaxPeers = 32;
+struct EpPeerLayout {
+  uint8_t *base[kEpMaxPeers];
+  int64_t rows_off = 0, ret_off = 0, ids_off = 0, cnt_off = 0, ffwd_off = 0, fret_off = 0, bytes = 0;
+  int world = 1, rank = 0, cap = 0, hidden = 0;
+};
+cudaError_t launch_ep_send_peer(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *offsets,
+                                const int32_t *meta, int K, int experts_per_rank, int S, const EpPeerLayout &L, int par,
+                                uint64_t seq, int32_t *slot_pos, int32_t *arrive, cudaStream_t stream);
+cudaError_t launch_ep_return_peer(const float *rows_out, const EpPeerLayout &L, int par, uint64_t seq, int32_t *arrive,
+                                  cudaStream_t stream);
+// bounded wait (about 2^shift clocks) for every rank's flag at flag_off to reach
+// seq; on timeout *err = code
+cudaError_t launch_ep_wait(const EpPeerLayout &L, int64_t flag_off, uint64_t seq, int shift, int32_t *err, int code,
+                           cudaStream_t stream);
+cudaError_t launch_ep_recv_weights_peer(const EpPeerLayout &L, int par, float *w, cudaStream_t stream);
 cudaError_t launch_fill(float *p, int64_t n, float v, cudaStream_t stream);
 
 // Addressing of the token rows a GEMV launch reads and writes, per

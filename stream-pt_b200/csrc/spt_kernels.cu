@@ -550,6 +550,130 @@ __global__ void k_ep_recv_weights(const int32_t *__restrict__ counts, int cap, i
     w[j] = (j % cap) < counts[j / cap] ? 1.0f : 0.0f;
 }
 
+// ---------------------------------------------------------------------------
+// Peer-memory exchange of the fixed-capacity layout.  Every rank's window
+// (EpPeerLayout) is mapped into every other rank's address space (CUDA IPC,
+// one GPU per rank); a sender writes its live rows straight into the owner's
+// window over NVLink and then publishes the call's sequence number in the
+// owner's flag for it, a receiver waits (bounded) until every sender's flag
+// has reached the sequence number.  Windows are double-buffered by call
+// parity.
+
+// 64-bit flag store with release semantics at system scope.
+__device__ __forceinline__ void flag_release(uint8_t *p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(reinterpret_cast<uint64_t *>(p)), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t flag_acquire(const uint8_t *p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(reinterpret_cast<const uint64_t *>(p)) : "memory");
+  return v;
+}
+
+// The CTA that arrives last (counted in *arrive, which it resets) after
+// every CTA's peer writes: sets flag[me] = seq in every rank's window.
+__device__ __forceinline__ void signal_peers(const EpPeerLayout &L, int64_t flag_off, uint64_t seq, int32_t *arrive) {
+  __shared__ int s_last;
+  __threadfence_system();  // this thread's writes to the peers, before the arrival
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(arrive, 1);
+    s_last = prev == (int)gridDim.x - 1;
+    if (s_last) *arrive = 0;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x < L.world) {
+    __threadfence_system();
+    flag_release(L.base[threadIdx.x] + flag_off + 8 * (int64_t)L.rank, seq);
+  }
+}
+
+// Send side: slot groups by owner rank (the dispatch kernel keyed by expert /
+// experts-per-rank), row j of the group for rank `dest` into dest's window at
+// rows[par][me][j], its local expert id, this rank's count in dest's window,
+// and slot_pos[slot] = dest*cap + j (where the result comes back).
+__global__ void __launch_bounds__(256) k_ep_send_peer(const float *__restrict__ x, const int32_t *__restrict__ sel_idx,
+                                                      const int32_t *__restrict__ perm,
+                                                      const int32_t *__restrict__ offsets,
+                                                      const int32_t *__restrict__ meta, int K, int experts_per_rank,
+                                                      int S, EpPeerLayout L, int par, uint64_t seq,
+                                                      int32_t *__restrict__ slot_pos, int32_t *arrive) {
+  pdl_wait();
+  pdl_trigger();
+  const int W = L.world, me = L.rank, cap = L.cap, H = L.hidden;
+  if (blockIdx.x == 0)
+    for (int r = threadIdx.x; r < W; r += blockDim.x)
+      reinterpret_cast<int32_t *>(L.base[r] + L.cnt_off)[par * W + me] = offsets[r + 1] - offsets[r];
+  const int n = min(meta[1], S);
+  for (int p = blockIdx.x; p < n; p += gridDim.x) {
+    int lo = 0, hi = W - 1;  // destination rank: largest r with offsets[r] <= p
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (offsets[mid] <= p) lo = mid;
+      else hi = mid - 1;
+    }
+    const int j = p - offsets[lo];
+    const int slot = perm[p];
+    const int64_t row = ((int64_t)par * W + me) * cap + j;
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(slot / K) * H);
+    float4 *dst = reinterpret_cast<float4 *>(L.base[lo] + L.rows_off) + row * (H / 4);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+    if (threadIdx.x == 0) {
+      reinterpret_cast<int32_t *>(L.base[lo] + L.ids_off)[row] = sel_idx[slot] % experts_per_rank;
+      slot_pos[slot] = lo * cap + j;
+    }
+  }
+  signal_peers(L, L.ffwd_off, seq, arrive);
+}
+
+// Receive side, results: row src*cap + j of rows_out (j < src's count) back
+// into src's window at ret[par][me][j].
+__global__ void __launch_bounds__(256) k_ep_return_peer(const float *__restrict__ rows_out, EpPeerLayout L, int par,
+                                                        uint64_t seq, int32_t *arrive) {
+  pdl_wait();
+  pdl_trigger();
+  const int W = L.world, me = L.rank, cap = L.cap, H = L.hidden;
+  const int32_t *cnt = reinterpret_cast<const int32_t *>(L.base[me] + L.cnt_off) + par * W;
+  for (int64_t p = blockIdx.x; p < (int64_t)W * cap; p += gridDim.x) {
+    const int src = (int)(p / cap), j = (int)(p - (int64_t)src * cap);
+    if (j >= cnt[src]) continue;
+    const float4 *from = reinterpret_cast<const float4 *>(rows_out + (size_t)p * H);
+    float4 *dst = reinterpret_cast<float4 *>(L.base[src] + L.ret_off) + (((int64_t)par * W + me) * cap + j) * (H / 4);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = from[i];
+  }
+  signal_peers(L, L.fret_off, seq, arrive);
+}
+
+// Wait until every rank's flag in this rank's window has reached seq, at most
+// about 2^shift clock cycles; then *err = code and return.
+__global__ void k_ep_wait(EpPeerLayout L, int64_t flag_off, uint64_t seq, int shift, int32_t *err, int code) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = threadIdx.x;
+  if (r < L.world) {
+    const uint8_t *f = L.base[L.rank] + flag_off + 8 * (int64_t)r;
+    const long long t0 = clock64();
+    for (uint32_t i = 0;; ++i) {
+      if (flag_acquire(f) >= seq) break;
+      if ((i & 63u) == 0u && clock64() - t0 > (1ll << shift)) {
+        atomicCAS(err, 0, code);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Receive side weights of the peer layout: row j of rank j / cap is live when
+// j % cap < that rank's count in this rank's window.
+__global__ void k_ep_recv_weights_peer(EpPeerLayout L, int par, float *__restrict__ w) {
+  pdl_wait();
+  pdl_trigger();
+  const int32_t *cnt = reinterpret_cast<const int32_t *>(L.base[L.rank] + L.cnt_off) + par * L.world;
+  const int64_t n = (int64_t)L.cap * L.world;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
+    w[j] = (j % L.cap) < cnt[j / L.cap] ? 1.0f : 0.0f;
+}
+
 // counts[r] = offsets[r+1] - offsets[r]: rows sent to each rank.
 __global__ void k_ep_counts(const int32_t *__restrict__ offsets, int world, int32_t *__restrict__ counts) {
   pdl_wait();
@@ -938,6 +1062,37 @@ cudaError_t launch_ep_recv_weights(const int32_t *counts, int cap, int world, fl
 
 cudaError_t launch_ep_counts(const int32_t *offsets, int world, int32_t *counts, cudaStream_t stream) {
   return launch_pdl(k_ep_counts, dim3(1), dim3(256), 0, stream, offsets, world, counts);
+}
+
+cudaError_t launch_ep_send_peer(const float *x, const int32_t *sel_idx, const int32_t *perm, const int32_t *offsets,
+                                const int32_t *meta, int K, int experts_per_rank, int S, const EpPeerLayout &L, int par,
+                                uint64_t seq, int32_t *slot_pos, int32_t *arrive, cudaStream_t stream) {
+  if (L.hidden % 4 != 0 || L.world < 1 || L.world > kEpMaxPeers) return cudaErrorInvalidValue;
+  const int grid = S < 1 ? 1 : (S < 148 * 8 ? S : 148 * 8);
+  return launch_pdl(k_ep_send_peer, dim3(grid), dim3(256), 0, stream, x, sel_idx, perm, offsets, meta, K,
+                    experts_per_rank, S, L, par, seq, slot_pos, arrive);
+}
+
+cudaError_t launch_ep_return_peer(const float *rows_out, const EpPeerLayout &L, int par, uint64_t seq, int32_t *arrive,
+                                  cudaStream_t stream) {
+  if (L.hidden % 4 != 0 || L.world < 1 || L.world > kEpMaxPeers) return cudaErrorInvalidValue;
+  const int64_t n = (int64_t)L.world * L.cap;
+  const int grid = (int)(n < 1 ? 1 : (n < 148 * 8 ? n : 148 * 8));
+  return launch_pdl(k_ep_return_peer, dim3(grid), dim3(256), 0, stream, rows_out, L, par, seq, arrive);
+}
+
+cudaError_t launch_ep_wait(const EpPeerLayout &L, int64_t flag_off, uint64_t seq, int shift, int32_t *err, int code,
+                           cudaStream_t stream) {
+  if (L.world < 1 || L.world > kEpMaxPeers) return cudaErrorInvalidValue;
+  return launch_pdl(k_ep_wait, dim3(1), dim3(32), 0, stream, L, flag_off, seq, shift, err, code);
+}
+
+cudaError_t launch_ep_recv_weights_peer(const EpPeerLayout &L, int par, float *w, cudaStream_t stream) {
+  const int64_t n = (int64_t)L.cap * L.world;
+  if (n <= 0) return cudaSuccess;
+  const int64_t g = (n + 255) / 256;
+  return launch_pdl(k_ep_recv_weights_peer, dim3((unsigned)(g < 148 * 8 ? g : 148 * 8)), dim3(256), 0, stream, L,
+                    par, w);
 }
 
 cudaError_t launch_fill(float *p, int64_t n, float v, cudaStream_t stream) {

@@ -5,8 +5,9 @@ Each of two processes owns one GPU, half of the 128 experts
 tokens; spt_forward_moe_batch_ep exchanges rows over NCCL.  Every rank's
 output must equal the single-GPU block (a full arena on the same GPU) for
 its tokens: bit for bit on the exact path, within the tensor-core path's
-tolerance (max|err| / max|ref| <= 1e-3) on the MMA path.  Skipped on hosts
-with fewer than two GPUs.
+tolerance (max|err| / max|ref| <= 1e-3) on the MMA path, for the counts-first
+exchange and for the fixed-capacity exchange through the NVLink peer windows
+and through NCCL.  Skipped on hosts with fewer than two GPUs.
 """
 import importlib
 import os
@@ -53,9 +54,11 @@ def _rank_main(rank, world, uid_q, results):
         _log(rank, "arenas ready")
         ep = spt.ExpertParallel(ctx, uid, rank, world)
         _log(rank, "group ready")
-        # counts exchanged per call, then the fixed-capacity exchange
-        for mode, capacity in (("counts", 0), ("capacity", 300)):
+        # counts exchanged per call, then the fixed-capacity exchange through
+        # the NVLink peer windows and through NCCL
+        for mode, capacity in (("counts", 0), ("capacity", 300), ("capacity-nccl", 300)):
           ep.set_capacity(capacity)
+          ep.set_exchange(spt.EP_EXCHANGE_NCCL if mode == "capacity-nccl" else spt.EP_EXCHANGE_PEER)
           for call, T in enumerate(TOKENS[rank]):
             x = spt.synth_normal_host(50 + rank, call, T * 2880)
             for path, name in ((spt.PATH_EXACT, "exact"), (spt.PATH_MMA, "mma")):
@@ -105,4 +108,4 @@ def test_expert_parallel_matches_single_gpu():
         assert err is None, (rank, err)
         for key, (ok, e) in res.items():
             assert ok, (rank, key, e)
-        assert len(res) == 2 * 2 * len(TOKENS[rank])
+        assert len(res) == 3 * 2 * len(TOKENS[rank])
