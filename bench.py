@@ -775,12 +775,172 @@ def run_q80(args):
     ctx.close()
 
 
+Q40_LAYERS, Q40_QKV, Q40_QD = 36, 5120, 4096  # GPT-OSS-120B: 36 layers, Q/K/V = 4096 + 512 + 512 rows, O input 4096
+
+
+def _q40_bytes(rows, input_, seed):
+    rng = np.random.default_rng(seed)
+    nb = input_ // 32
+    data = rng.integers(0, 256, size=(rows, nb, 18), dtype=np.uint8)
+    data[:, :, :2] = (rng.standard_normal((rows, nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(rows, nb, 2)
+    return data.reshape(-1)
+
+
+def run_q40(args):
+    """--config q40 / q40b: the Q4_0 attention projections of GPT-OSS-120B
+    (MulQ40Into / MulQ40BatchInto, forward/q40.go:35-101): per layer the
+    Q, K and V rows fused in one 5,120 x 2,880 matrix (the three tensors
+    share their input; rows are independent, so the fused product equals the
+    three) and O, 2,880 x 4,096; 36 layers resident in HBM (537 MB, larger
+    than L2).  q40: one decode token per step (batch 1, the one-input
+    order); q40b: 128 tokens per step (the batched order).  Synthetic bytes
+    (uniform nibbles, float16 scales N(0, 0.01)), N(0, 1) inputs.  The step's
+    72 launches are captured once into a CUDA graph and replayed."""
+    import torch
+    rank, world, local = dist_info()
+    torch.cuda.set_device(local)
+    spt = importlib.import_module("stream-pt_b200")
+    batch = 1 if args.config == "q40" else 128
+    ctx = spt.Context(local)
+    mats = []
+    host = {}
+    for l in range(Q40_LAYERS):
+        for kind, rows, inp in (("qkv", Q40_QKV, H), ("o", H, Q40_QD)):
+            data = _q40_bytes(rows, inp, 4000 + 2 * l + (kind == "o"))
+            if l == 0:
+                host[kind] = data
+            r, t = spt.q40_tensor(data, inp, rows, name=f"blk.{l}.attn_{kind}.weight")
+            mats.append((ctx.q40_matrix(r, t), inp, rows))
+    x_h = spt.synth_normal_host(40, 1, batch * H)
+    a_h = spt.synth_normal_host(41, 1, batch * Q40_QD)
+    dev = f"cuda:{local}"
+    x_d, a_d = torch.from_numpy(x_h).to(dev), torch.from_numpy(a_h).to(dev)
+    y_qkv = torch.empty(batch * Q40_QKV, dtype=torch.float32, device=dev)
+    y_o = torch.empty(batch * H, dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+
+    def step():
+        for m, inp, rows in mats:
+            if inp == H:
+                m.mul_device(x_d.data_ptr(), y_qkv.data_ptr(), batch)
+            else:
+                m.mul_device(a_d.data_ptr(), y_o.data_ptr(), batch)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    launch = "CUDA graph of the step's 72 launches"
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+            step()
+        torch.cuda.synchronize()
+    except Exception as exc:  # capture refused: time the direct launches
+        graph, launch = None, f"direct launches (graph capture failed: {type(exc).__name__})"
+        torch.cuda.synchronize()
+    run = graph.replay if graph is not None else step
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                starts[i].record(stream)
+                run()
+                ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+    # parity of the timed step's first layer against the oracle (outside the timed region)
+    from oracle import oracle
+    workers = os.cpu_count() or 1
+    got_q = torch.empty_like(y_qkv)
+    got_o = torch.empty_like(y_o)
+    mats[0][0].mul_device(x_d.data_ptr(), got_q.data_ptr(), batch)
+    mats[1][0].mul_device(a_d.data_ptr(), got_o.data_ptr(), batch)
+    ctx.sync()
+    items = min(batch, 8)
+    want_q = oracle.mul_q40(host["qkv"], H, Q40_QKV, x_h[:items * H] if batch > 1 else x_h, items if batch > 1 else 1,
+                            workers)
+    want_o = oracle.mul_q40(host["o"], Q40_QD, H, a_h[:items * Q40_QD] if batch > 1 else a_h,
+                            items if batch > 1 else 1, workers)
+    gq = got_q.cpu().numpy().reshape(batch, Q40_QKV)[:items]
+    go = got_o.cpu().numpy().reshape(batch, H)[:items]
+    bit_exact = bool(np.array_equal(gq.view(np.uint32), want_q.view(np.uint32)) and
+                     np.array_equal(go.view(np.uint32), want_o.view(np.uint32)))
+    # e2e: the public host call per matrix (host x -> device -> product -> host y)
+    e_ms = []
+    xq_host, xo_host = x_h, a_h
+    yq_host = np.empty(batch * Q40_QKV, np.float32)
+    yo_host = np.empty(batch * H, np.float32)
+    for i in range(args.warmup + max(2, args.steps // 4)):
+        t0 = time.perf_counter()
+        for m, inp, rows in mats:
+            if inp == H:
+                m.mul(xq_host, batch, yq_host)
+            else:
+                m.mul(xo_host, batch, yo_host)
+        if i >= args.warmup:
+            e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e_ms = sum(e_ms) / len(e_ms)
+    peak, _, peak_src = load_peaks()
+    nbytes = Q40_LAYERS * (Q40_QKV * (H // 32) * 18 + H * (Q40_QD // 32) * 18)
+    fmas = Q40_LAYERS * (Q40_QKV * H + H * Q40_QD) * batch
+    line = {"metric": "attn_proj_tokens_per_s", "value": batch * 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_0 weights x f32 -> f32 (CUDA cores, bit-exact)", "data": "synthetic",
+            "config": {"workload": f"{args.config}: Q4_0 attention projections (fused QKV 5120x2880 + O 2880x4096) "
+                                   f"of 36 layers, batch {batch} (north_star q40.go)",
+                       "batch": batch, "layers": Q40_LAYERS, "launch": launch,
+                       "l2": "537 MB of matrices per step > L2"},
+            "parity": {"bit_exact": bit_exact, "items_checked": items, "matrices_checked": 2},
+            "e2e": {"value": batch * 1e3 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": Q40_LAYERS * batch * (H + Q40_QD) * 4,
+                    "d2h_bytes_per_step": Q40_LAYERS * batch * (Q40_QKV + H) * 4 + Q40_LAYERS * 2 * 4,
+                    "clock": "host (perf_counter) around the 72 synchronous host calls"},
+            "gpu_launches": args.steps * 2 * Q40_LAYERS, "clocks": clocks.summary()}
+    if batch == 1:
+        line["roofline"] = {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                            "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "kernel": "k_q40_gemv",
+                            "algorithmic_bytes": nbytes, "avg_ms": ms, "peak_source": peak_src}
+    else:
+        nominal = 148 * 128 * 2 * 1.965e9 / 1e12  # fp32 FMA on CUDA cores at the max SM clock
+        tf = 2 * fmas / (ms / 1e3) / 1e12
+        line["roofline"] = {"bound": "fp32-fma", "achieved": tf, "peak": nominal, "unit": "TFLOP/s",
+                            "frac": tf / nominal, "traffic": None, "kernel": "k_q40_batch",
+                            "algorithmic_flops": 2 * fmas, "algorithmic_bytes": nbytes, "avg_ms": ms,
+                            "peak_source": "nominal fp32 CUDA-core rate (148 SMs x 128 FMA/clk x 1965 MHz); "
+                                           "no measured fp32 figure"}
+    if not args.no_cpu_baseline:
+        xs_ = x_h[:H * min(batch, 8)] if batch > 1 else x_h
+        nb_ = min(batch, 8) if batch > 1 else 1
+        oracle.mul_q40(host["qkv"], H, Q40_QKV, xs_, nb_, workers)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 and reps < 200:
+            oracle.mul_q40(host["qkv"], H, Q40_QKV, xs_, nb_, workers)
+            reps += 1
+        el = time.perf_counter() - t0
+        per_tok = el / reps / nb_ * (Q40_QKV * H + H * Q40_QD) / (Q40_QKV * H) * Q40_LAYERS
+        line["cpu_baseline"] = {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": workers, "kind": "port",
+                                "sample": f"{reps} products of one fused QKV matrix x {nb_} token(s) ({el:.1f} s), "
+                                          "scaled by FMA count to the 72 matrices of a step"}
+    print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    for m, _, _ in mats:
+        m.close()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["q80"])
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS) + ["q80", "q40", "q40b"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--path", default="auto", choices=["auto", "mma", "gemv16", "exact"],
                     help="expert products: the library's choice (auto), tcgen05 (mma), the decode GEMV "
@@ -796,6 +956,12 @@ def main():
                               "its cpu_baseline (the oracle port) in the same line"}), flush=True)
         else:
             run_q80(args)
+    elif args.config in ("q40", "q40b"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the q40 modes time the oracle port only "
+                              "through the cpu_baseline of the same line"}), flush=True)
+        else:
+            run_q40(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -14,6 +14,8 @@
  *   spt_combine_moe_batch        combine loop      forward/moe_batch.go:163-192
  *   spt_rmsnorm                  normBatch         forward/layer_batch.go:139-195
  *   spt_mul_q80                  MulQ80Into/Argmax forward/q80.go:22-148
+ *   spt_mul_q40                  MulQ40Into        forward/q40.go:35-40
+ *   spt_mul_q40_batch            MulQ40BatchInto   forward/q40.go:46-101
  *   spt_arena_create             ggufmap.WithExpertRanges + readExpertBias
  *                                (ggufmap/mmap_linux.go:391-555, forward/moe.go:72-92):
  *                                the streamed mmap window becomes an HBM arena
@@ -62,7 +64,7 @@ typedef enum spt_status {
  * absent optional tensor (an unnamed bias, forward/moe_batch.go:196-201). */
 typedef struct spt_tensor {
   const char *name;
-  uint32_t type;      /* 0 F32, 1 F16, 8 Q8_0, 30 BF16, 39 MXFP4 */
+  uint32_t type;      /* 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 30 BF16, 39 MXFP4 */
   uint32_t n_dims;    /* entries of shape[] in use (0..4) */
   uint64_t shape[4];
   uint64_t start, end;
@@ -370,6 +372,37 @@ spt_status spt_mul_q80_matrix(spt_context *ctx, spt_q80_matrix *m, const float *
  * float) may each be NULL. */
 spt_status spt_mul_q80_matrix_device(spt_context *ctx, spt_q80_matrix *m, const float *x, float *y,
                                      int64_t *argmax, float *best_logit);
+
+/* ---- Q4_0 products -----------------------------------------------------------
+ * MulQ40Into / MulQ40BatchInto (forward/q40.go:35-101): y[item*output + r] =
+ * row r of the Q4_0 tensor (`tensor` in `reader`, GGML type 2, shape
+ * [input, output], output rows of input/32 18-byte blocks) dotted with
+ * x[item*input ...].  Batch 1 follows the reference's one-input order
+ * (quantQ40AVX2, forward/quant_amd64.go:75-90), larger batches its batched
+ * order (quantDotQ40Batch, :118-148); both bit for bit.  Checks as q40Shape
+ * and MulQ40BatchInto (q40.go:58-71,105-130): SPT_ERR_DIMENSIONS for the
+ * type, rank, shape, batch (< 1 or overflowing) and x_len/y_len != batch *
+ * input/output; SPT_ERR_FILE_RANGE for the byte range; SPT_ERR_OVERLAP when x
+ * and y overlap; SPT_ERR_CANCELED when *cancel is set on entry (the one
+ * launch is not interrupted).  This build needs input <= ~4,600
+ * (SPT_ERR_UNSUPPORTED above; GPT-OSS uses 2,880 and 4,096).  The matrix is
+ * uploaded for the call; spt_q40_matrix keeps it resident. */
+spt_status spt_mul_q40(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor, const float *x,
+                       int64_t x_len, float *y, int64_t y_len, const volatile int32_t *cancel);
+spt_status spt_mul_q40_batch(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor, const float *x,
+                             int64_t x_len, float *y, int64_t y_len, int64_t batch,
+                             const volatile int32_t *cancel);
+typedef struct spt_q40_matrix spt_q40_matrix;
+spt_status spt_q40_matrix_create(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor,
+                                 spt_q40_matrix **out);
+void spt_q40_matrix_destroy(spt_q40_matrix *m);
+spt_status spt_q40_matrix_shape(const spt_q40_matrix *m, int64_t *input, int64_t *output);
+/* Host x [batch*input] / y [batch*output], synchronous. */
+spt_status spt_mul_q40_matrix(spt_context *ctx, spt_q40_matrix *m, const float *x, int64_t x_len, float *y,
+                              int64_t y_len, int64_t batch, const volatile int32_t *cancel);
+/* Device pointers; enqueue only (one kernel launch, no allocation). */
+spt_status spt_mul_q40_matrix_device(spt_context *ctx, spt_q40_matrix *m, const float *x, float *y,
+                                     int64_t batch);
 
 /* ---- GGUF model files -------------------------------------------------------
  * ggufindex.Open (ggufindex/index.go:55-575): headers, metadata and tensor

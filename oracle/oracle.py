@@ -87,6 +87,8 @@ def lib():
         L.spo_add.argtypes = [vp, vp, i64]; L.spo_add.restype = None
         L.spo_dot_q80.argtypes = [vp, vp, i64]; L.spo_dot_q80.restype = f32
         L.spo_mul_q80.argtypes = [vp, i64, i64, vp, vp, vp, i32]; L.spo_mul_q80.restype = i64
+        L.spo_dot_q40.argtypes = [vp, vp, i64]; L.spo_dot_q40.restype = f32
+        L.spo_mul_q40.argtypes = [vp, i64, i64, vp, i64, vp, i32]; L.spo_mul_q40.restype = None
         L.spo_has_avx2.restype = i32
         L.spo_synth_layer.argtypes = [ctypes.POINTER(SynthParams), i64, i64, i64, i64, vp, vp, vp, vp, vp, vp,
                                       vp, vp, i32]
@@ -230,6 +232,22 @@ def mul_q80(data, input_, output, x, workers=1):
     best = ctypes.c_float()
     idx = lib().spo_mul_q80(_p(data), input_, output, _p(x), _p(y), ctypes.byref(best), workers)
     return y, int(idx), np.float32(best.value)
+
+
+def dot_q40(row, x) -> np.float32:
+    row = np.ascontiguousarray(row, dtype=np.uint8)
+    x = _f32(x)
+    return np.float32(lib().spo_dot_q40(_p(row), _p(x), x.size))
+
+
+def mul_q40(data, input_, output, x, batch=1, workers=1):
+    """MulQ40BatchInto: y [batch, output] for x [batch, input]."""
+    data = np.ascontiguousarray(data, dtype=np.uint8)
+    x = _f32(x)
+    assert x.size == batch * input_ and data.size == output * (input_ // 32) * 18
+    y = np.empty(batch * output, np.float32)
+    lib().spo_mul_q40(_p(data), input_, output, _p(x), batch, _p(y), workers)
+    return y.reshape(batch, output)
 
 
 def fmaf(a, b, c) -> np.ndarray:

@@ -583,6 +583,70 @@ int64_t spo_mul_q80(const uint8_t *data, int64_t input, int64_t output, const fl
   return best;
 }
 
+/* ---- Q4_0: forward/quant_amd64.go:65-90 (one input), :118-148 (a batch),
+ * forward/q40.go:35-101 ------------------------------------------------- */
+/* quantQ40WeightsAVX2 (forward/quant_amd64.go:65-73): element c of a block is
+ * the low nibble of byte c (c < 16) or the high nibble of byte c - 16, and
+ * its weight is (nibble - 8) * scale, exact in fp32. */
+static void q40_decode(const uint8_t *enc, float w[32]) {
+  uint16_t hb; memcpy(&hb, enc, 2);
+  const float scale = spo_f16(hb);
+  for (int i = 0; i < 16; i++) {
+    w[i] = (float)((int)(enc[2 + i] & 15) - 8) * scale;
+    w[16 + i] = (float)((int)(enc[2 + i] >> 4) - 8) * scale;
+  }
+}
+
+/* quantQ40AVX2 (forward/quant_amd64.go:75-90): chain c takes element c of
+ * every block; a0+a1+a2+a3, then quantSumAVX2. */
+float spo_dot_q40(const uint8_t *row, const float *x, int64_t input) {
+  float a[32], w[32];
+  for (int c = 0; c < 32; c++) a[c] = 0.0f;
+  for (int64_t b = 0; b < input / 32; b++) {
+    q40_decode(row + 18 * b, w);
+    for (int c = 0; c < 32; c++) a[c] = fmaf(w[c], x[32 * b + c], a[c]);
+  }
+  return reduce32_scalar(a);
+}
+
+/* quantDotQ40Batch (forward/quant_amd64.go:118-148): one 8-lane accumulator
+ * per item; lane l takes elements l, 8+l, 16+l, 24+l of each block in that
+ * order, then quantSumAVX2.  Writes y[item * output + row_index]. */
+void spo_dot_q40_batch(const uint8_t *row, const float *x, float *y, int64_t input, int64_t output,
+                       int64_t row_index, int64_t batch) {
+  float w[32];
+  for (int64_t item = 0; item < batch; item++) {
+    const float *v = x + item * input;
+    float acc[8];
+    for (int l = 0; l < 8; l++) acc[l] = 0.0f;
+    for (int64_t b = 0; b < input / 32; b++) {
+      q40_decode(row + 18 * b, w);
+      for (int l = 0; l < 8; l++)
+        for (int j = 0; j < 4; j++) acc[l] = fmaf(w[8 * j + l], v[32 * b + 8 * j + l], acc[l]);
+    }
+    y[item * output + row_index] = qsum8_scalar(acc);
+  }
+}
+
+typedef struct { const uint8_t *data; int64_t input, output, batch; const float *x; float *y; } q40_ctx;
+static void q40_range(void *p, int64_t begin, int64_t end) {
+  q40_ctx *c = (q40_ctx *)p;
+  const int64_t row_bytes = c->input / 32 * 18;
+  for (int64_t r = begin; r < end; r++) {
+    const uint8_t *row = c->data + r * row_bytes;
+    if (c->batch == 1)
+      c->y[r] = spo_dot_q40(row, c->x, c->input);
+    else
+      spo_dot_q40_batch(row, c->x, c->y, c->input, c->output, r, c->batch);
+  }
+}
+
+void spo_mul_q40(const uint8_t *data, int64_t input, int64_t output, const float *x, int64_t batch, float *y,
+                 int workers) {
+  q40_ctx c = {data, input, output, batch, x, y};
+  spo_parallel(output, workers < 1 ? 1 : workers, q40_range, &c);
+}
+
 void spo_fmaf_vec(const float *a, const float *b, const float *c, float *out, int64_t n) {
   for (int64_t i = 0; i < n; i++) out[i] = fmaf(a[i], b[i], c[i]);
 }

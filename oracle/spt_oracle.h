@@ -136,6 +136,16 @@ float spo_dot_q80(const uint8_t *row, const float *x, int64_t input);
 int64_t spo_mul_q80(const uint8_t *data, int64_t input, int64_t output, const float *x,
                     float *y, float *best_logit, int workers);
 
+/* Q4_0 row dot, one input (forward/quant_amd64.go:75-90 order). */
+float spo_dot_q40(const uint8_t *row, const float *x, int64_t input);
+/* The batched order (forward/quant_amd64.go:118-148): y[item*output + row_index]. */
+void spo_dot_q40_batch(const uint8_t *row, const float *x, float *y, int64_t input, int64_t output,
+                       int64_t row_index, int64_t batch);
+/* MulQ40BatchInto (forward/q40.go:46-101): batch 1 takes the one-input order,
+ * larger batches the batched one; y is [batch][output]. */
+void spo_mul_q40(const uint8_t *data, int64_t input, int64_t output, const float *x, int64_t batch, float *y,
+                 int workers);
+
 /* out[i] = fmaf(a[i], b[i], c[i]) (single rounding), for test references. */
 void spo_fmaf_vec(const float *a, const float *b, const float *c, float *out, int64_t n);
 

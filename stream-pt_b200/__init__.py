@@ -229,6 +229,13 @@ def lib():
         "spt_forward_stack_device": ([vp, vp, vp, i64, i64, vp, i64, f32], st),
         "spt_forward_stack": ([vp, vp, vp, i64, i64, vp, i64, i64, f32, vp], st),
         "spt_synth_norm_host": ([P(_SynthParams), i64, i64, vp], st),
+        "spt_mul_q40": ([vp, vp, vp, vp, i64, vp, i64, vp], st),
+        "spt_mul_q40_batch": ([vp, vp, vp, vp, i64, vp, i64, i64, vp], st),
+        "spt_q40_matrix_create": ([vp, vp, vp, P(vp)], st),
+        "spt_q40_matrix_destroy": ([vp], None),
+        "spt_q40_matrix_shape": ([vp, P(i64), P(i64)], st),
+        "spt_mul_q40_matrix": ([vp, vp, vp, i64, vp, i64, i64, vp], st),
+        "spt_mul_q40_matrix_device": ([vp, vp, vp, vp, i64], st),
         "spt_q80_matrix_create": ([vp, vp, ctypes.c_uint64, i64, i64, P(vp)], st),
         "spt_q80_matrix_destroy": ([vp], None),
         "spt_mul_q80_matrix": ([vp, vp, vp, vp, P(i64), P(f32)], st),
@@ -589,6 +596,33 @@ class Context:
                                      ctypes.byref(am), ctypes.byref(best)))
         return y, am.value, np.float32(best.value)
 
+    def mul_q40_batch(self, reader: "Reader", tensor: "Tensor", x: np.ndarray, batch: int,
+                      y: Optional[np.ndarray] = None, cancel: Optional[np.ndarray] = None) -> np.ndarray:
+        """MulQ40BatchInto (forward/q40.go:46-101): y [batch, output]."""
+        x = _f32(x)
+        out = int(tensor.shape[1]) if len(tensor.shape) > 1 else 0
+        if y is None:
+            y = np.empty(max(batch, 0) * out, np.float32)
+        r, t = reader._c(), tensor._c()
+        self.check(lib().spt_mul_q40_batch(self._h, ctypes.byref(r), ctypes.byref(t), _p(x), x.size, _p(y), y.size,
+                                           batch, _p(cancel)))
+        return y.reshape(batch, -1) if batch > 0 else y
+
+    def mul_q40(self, reader: "Reader", tensor: "Tensor", x: np.ndarray, y: Optional[np.ndarray] = None,
+                cancel: Optional[np.ndarray] = None) -> np.ndarray:
+        """MulQ40Into (forward/q40.go:35-40): y [output]."""
+        x = _f32(x)
+        if y is None:
+            y = np.empty(int(tensor.shape[1]) if len(tensor.shape) > 1 else 0, np.float32)
+        r, t = reader._c(), tensor._c()
+        self.check(lib().spt_mul_q40(self._h, ctypes.byref(r), ctypes.byref(t), _p(x), x.size, _p(y), y.size,
+                                     _p(cancel)))
+        return y
+
+    def q40_matrix(self, reader: "Reader", tensor: "Tensor") -> "Q40Matrix":
+        """Upload a Q4_0 tensor once (spt_q40_matrix_create)."""
+        return Q40Matrix(self, reader, tensor)
+
     def q80_matrix(self, data: np.ndarray, input_: int, output: int) -> "Q80Matrix":
         """Upload a Q8_0 matrix once (spt_q80_matrix_create)."""
         return Q80Matrix(self, data, input_, output)
@@ -640,6 +674,50 @@ class Gguf:
     def close(self):
         if self._h:
             lib().spt_gguf_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def q40_tensor(data: np.ndarray, input_: int, output: int, name: str = "q40.weight", prefix: int = 0):
+    """A Reader holding Q4_0 bytes (after `prefix` bytes) and its Tensor [input, output]."""
+    data = np.ascontiguousarray(data, dtype=np.uint8).reshape(-1)
+    buf = np.zeros(prefix + data.size, np.uint8)
+    buf[prefix:] = data
+    return Reader(buf), Tensor(name, 2, (input_, output), prefix, prefix + data.size)
+
+
+class Q40Matrix:
+    """HBM-resident Q4_0 matrix: y = W x for a batch of inputs."""
+
+    def __init__(self, ctx: "Context", reader: "Reader", tensor: "Tensor"):
+        self.ctx = ctx
+        self._h = ctypes.c_void_p()
+        r, t = reader._c(), tensor._c()
+        ctx.check(lib().spt_q40_matrix_create(ctx._h, ctypes.byref(r), ctypes.byref(t), ctypes.byref(self._h)))
+        i, o = ctypes.c_int64(), ctypes.c_int64()
+        lib().spt_q40_matrix_shape(self._h, ctypes.byref(i), ctypes.byref(o))
+        self.input, self.output = i.value, o.value
+
+    def mul(self, x: np.ndarray, batch: int = 1, y: Optional[np.ndarray] = None, cancel=None) -> np.ndarray:
+        x = _f32(x)
+        if y is None:
+            y = np.empty(batch * self.output, np.float32)
+        self.ctx.check(lib().spt_mul_q40_matrix(self.ctx._h, self._h, _p(x), x.size, _p(y), y.size, batch,
+                                                _p(cancel)))
+        return y.reshape(batch, self.output)
+
+    def mul_device(self, x_ptr: int, y_ptr: int, batch: int = 1):
+        self.ctx.check(lib().spt_mul_q40_matrix_device(self.ctx._h, self._h, ctypes.c_void_p(x_ptr),
+                                                       ctypes.c_void_p(y_ptr), batch))
+
+    def close(self):
+        if self._h:
+            lib().spt_q40_matrix_destroy(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):

@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libspt_moe.so")
 BUILD = os.path.join(HERE, "_build")
 
-SOURCES = ["spt_kernels.cu", "spt_mma.cu", "spt_gemv16.cu", "spt_q80.cu", "spt_gguf.cpp", "spt_api.cu"]
+SOURCES = ["spt_kernels.cu", "spt_mma.cu", "spt_gemv16.cu", "spt_q80.cu", "spt_q40.cu", "spt_gguf.cpp", "spt_api.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -124,6 +124,14 @@ struct spt_q80_matrix {
   DevBuf xdev, ydev;   // host-path staging
 };
 
+struct spt_q40_matrix {
+  spt_context *ctx = nullptr;
+  int64_t input = 0, output = 0;
+  DevBuf w;            // rows x input/32 x 18 bytes, + padding
+  DevBuf err;          // bounded-wait flag of the one-input kernel
+  DevBuf xdev, ydev;   // host-path staging
+};
+
 struct spt_arena {
   uint64_t id = 0;           // unique per arena in the process (keys the context's call graphs)
   int device = -1;
@@ -2065,6 +2073,163 @@ spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len,
   st = spt_mul_q80_matrix(ctx, m, x, y, argmax, best_logit);
   spt_q80_matrix_destroy(m);
   return st;
+}
+
+
+// ---- Q4_0 (forward/q40.go:35-130) -------------------------------------------
+
+namespace {
+
+// q40Shape (forward/q40.go:105-130): type 2, two dimensions, input a nonzero
+// multiple of 32, output nonzero, byte range = output rows of input/32
+// 18-byte blocks; then the reader's range check.
+spt_status q40_shape(spt_context *ctx, const spt_reader *reader, const spt_tensor *t, int64_t *input,
+                     int64_t *output) {
+  if (!reader || !reader->base) return fail(ctx, SPT_ERR_NULL_ARG, "nil GGUF reader");
+  if (!t) return fail(ctx, SPT_ERR_NULL_ARG, "nil tensor");
+  if (t->type != 2)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "\"%s\": GGML type %u instead of Q4_0 (2)", tname(*t), t->type);
+  if (t->n_dims != 2) return fail(ctx, SPT_ERR_DIMENSIONS, "\"%s\": expected a two-dimensional matrix", tname(*t));
+  const uint64_t in = t->shape[0], out = t->shape[1];
+  if (in == 0 || out == 0 || in % 32 != 0)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "\"%s\": invalid Q4_0 matrix shape [%llu %llu]", tname(*t),
+                (unsigned long long)in, (unsigned long long)out);
+  const uint64_t max_int = (uint64_t)INT64_MAX;
+  if (in > max_int || out > max_int || in / 32 > max_int / 18)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "\"%s\": matrix dimensions exceed platform limits", tname(*t));
+  const uint64_t bytes = in / 32 * 18;
+  if (out > UINT64_MAX / bytes || t->end <= t->start || t->end - t->start != out * bytes)
+    return fail(ctx, SPT_ERR_FILE_RANGE, "\"%s\": invalid tensor byte range for shape [%llu %llu]", tname(*t),
+                (unsigned long long)in, (unsigned long long)out);
+  spt_status st = validate_file_range(ctx, reader, *t);
+  if (st) return st;
+  // this build: the one-input kernel's shared-memory ring and 32-bit grids
+  if (!q40_supported((int)std::min<uint64_t>(in, 1u << 30)) || out > 0x7fffffffull)
+    return fail(ctx, SPT_ERR_UNSUPPORTED, "\"%s\": Q4_0 matrix [%llu %llu] exceeds this build's limits", tname(*t),
+                (unsigned long long)in, (unsigned long long)out);
+  *input = (int64_t)in;
+  *output = (int64_t)out;
+  return SPT_OK;
+}
+
+// MulQ40BatchInto's argument checks (forward/q40.go:58-71).
+spt_status q40_args(spt_context *ctx, int64_t input, int64_t output, const float *x, int64_t x_len,
+                    const float *y, int64_t y_len, int64_t batch, bool lengths) {
+  if (batch < 1 || batch > INT64_MAX / input || batch > INT64_MAX / output)
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid or oversized batch: %lld", (long long)batch);
+  if (batch > INT64_MAX / 4 / std::max(input, output))
+    return fail(ctx, SPT_ERR_DIMENSIONS, "invalid or oversized batch: %lld", (long long)batch);
+  if (lengths && (x_len != batch * input || y_len != batch * output))
+    return fail(ctx, SPT_ERR_DIMENSIONS, "expected %lld input and %lld output elements, got %lld and %lld",
+                (long long)(batch * input), (long long)(batch * output), (long long)x_len, (long long)y_len);
+  if (!x || !y) return fail(ctx, SPT_ERR_NULL_ARG, "nil input or output");
+  const uintptr_t a = (uintptr_t)x, b = (uintptr_t)y;
+  const uintptr_t na = (uintptr_t)(batch * input) * 4, nb = (uintptr_t)(batch * output) * 4;
+  if (a < b + nb && b < a + na) return fail(ctx, SPT_ERR_OVERLAP, "input and output must not overlap");
+  return SPT_OK;
+}
+
+}  // namespace
+
+spt_status spt_q40_matrix_create(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor,
+                                 spt_q40_matrix **out) {
+  if (!ctx || !out) return fail(ctx, SPT_ERR_NULL_ARG, "nil context or output");
+  *out = nullptr;
+  int64_t input = 0, output = 0;
+  spt_status st = q40_shape(ctx, reader, tensor, &input, &output);
+  if (st) return st;
+  if ((st = require_device(ctx))) return st;
+  const uint64_t len = tensor->end - tensor->start;
+  spt_q40_matrix *m = new spt_q40_matrix();
+  m->ctx = ctx;
+  m->input = input;
+  m->output = output;
+  cudaError_t e = m->w.ensure(len + 64);  // the last chunk's copy rounds up to 16 bytes
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->w.p, 0, len + 64, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->w.p, reader->base + tensor->start, len, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = m->err.ensure(sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->err.p, 0, sizeof(int32_t), ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    spt_q40_matrix_destroy(m);
+    return cuda_fail(ctx, e, "Q4_0 matrix upload");
+  }
+  *out = m;
+  return SPT_OK;
+}
+
+void spt_q40_matrix_destroy(spt_q40_matrix *m) {
+  if (!m) return;
+  if (m->ctx && m->ctx->has_device) {
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+  }
+  for (DevBuf *b : {&m->w, &m->err, &m->xdev, &m->ydev}) b->release();
+  delete m;
+}
+
+spt_status spt_q40_matrix_shape(const spt_q40_matrix *m, int64_t *input, int64_t *output) {
+  if (!m) return SPT_ERR_NULL_ARG;
+  if (input) *input = m->input;
+  if (output) *output = m->output;
+  return SPT_OK;
+}
+
+spt_status spt_mul_q40_matrix_device(spt_context *ctx, spt_q40_matrix *m, const float *x, float *y, int64_t batch) {
+  if (!ctx || !m) return fail(ctx, SPT_ERR_NULL_ARG, "nil context or matrix");
+  if (m->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "Q4_0 matrix belongs to another context");
+  spt_status st = q40_args(ctx, m->input, m->output, x, 0, y, 0, batch, false);
+  if (st) return st;
+  if ((st = require_device(ctx))) return st;
+  SPT_CUDA(ctx, launch_q40(m->w.as<uint8_t>(), m->output, (int)m->input, x, batch, y, m->err.as<int32_t>(),
+                           ctx->sm_count, ctx->stream));
+  ctx->kernels_last = 1;
+  return SPT_OK;
+}
+
+spt_status spt_mul_q40_matrix(spt_context *ctx, spt_q40_matrix *m, const float *x, int64_t x_len, float *y,
+                              int64_t y_len, int64_t batch, const volatile int32_t *cancel) {
+  if (!ctx || !m) return fail(ctx, SPT_ERR_NULL_ARG, "nil context or matrix");
+  if (m->ctx != ctx) return fail(ctx, SPT_ERR_DIMENSIONS, "Q4_0 matrix belongs to another context");
+  spt_status st = q40_args(ctx, m->input, m->output, x, x_len, y, y_len, batch, true);
+  if (st) return st;
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  if ((st = require_device(ctx))) return st;
+  cudaStream_t s = ctx->stream;
+  const size_t xb = sizeof(float) * (size_t)(batch * m->input), yb = sizeof(float) * (size_t)(batch * m->output);
+  SPT_CUDA(ctx, m->xdev.ensure(xb));
+  SPT_CUDA(ctx, m->ydev.ensure(yb));
+  SPT_CUDA(ctx, cudaMemcpyAsync(m->xdev.p, x, xb, cudaMemcpyHostToDevice, s));
+  if ((st = spt_mul_q40_matrix_device(ctx, m, m->xdev.as<float>(), m->ydev.as<float>(), batch))) return st;
+  SPT_CUDA(ctx, cudaMemcpyAsync(y, m->ydev.p, yb, cudaMemcpyDeviceToHost, s));
+  int32_t err = 0;
+  SPT_CUDA(ctx, cudaMemcpyAsync(&err, m->err.p, sizeof err, cudaMemcpyDeviceToHost, s));
+  SPT_CUDA(ctx, cudaStreamSynchronize(s));
+  if (err) {
+    SPT_CUDA(ctx, cudaMemset(m->err.p, 0, sizeof err));
+    return fail(ctx, SPT_ERR_TIMEOUT, "Q4_0 GEMV: bounded wait gave up");
+  }
+  return SPT_OK;
+}
+
+spt_status spt_mul_q40_batch(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor, const float *x,
+                             int64_t x_len, float *y, int64_t y_len, int64_t batch, const volatile int32_t *cancel) {
+  if (!ctx) return fail(ctx, SPT_ERR_NULL_ARG, "nil context");
+  if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
+  int64_t input = 0, output = 0;
+  spt_status st = q40_shape(ctx, reader, tensor, &input, &output);
+  if (st) return st;
+  if ((st = q40_args(ctx, input, output, x, x_len, y, y_len, batch, true))) return st;
+  spt_q40_matrix *m = nullptr;
+  if ((st = spt_q40_matrix_create(ctx, reader, tensor, &m))) return st;
+  st = spt_mul_q40_matrix(ctx, m, x, x_len, y, y_len, batch, cancel);
+  spt_q40_matrix_destroy(m);
+  return st;
+}
+
+spt_status spt_mul_q40(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor, const float *x,
+                       int64_t x_len, float *y, int64_t y_len, const volatile int32_t *cancel) {
+  return spt_mul_q40_batch(ctx, reader, tensor, x, x_len, y, y_len, 1, cancel);
 }
 
 }  // extern "C"

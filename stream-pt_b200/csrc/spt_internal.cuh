@@ -254,4 +254,12 @@ cudaError_t launch_q80(const uint8_t *w, int64_t rows, int input, const float *x
                        cudaStream_t stream);
 int q80_rows_per_chunk(int input);
 
+// Q4_0 products (spt_q40.cu): y[item][r] = dot(row r, x[item]) for `rows`
+// rows of input/32 18-byte blocks (w padded by >= 16 bytes), batch 1 in the
+// reference's one-input order, larger batches in its batched order.
+cudaError_t launch_q40(const uint8_t *w, int64_t rows, int input, const float *x, int64_t batch, float *y,
+                       int32_t *err, int sm_count, cudaStream_t stream);
+bool q40_supported(int input);
+size_t q40_smem_bytes(int input);
+
 }  // namespace spt

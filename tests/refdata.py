@@ -212,3 +212,40 @@ def q80_reference_dot(row, x):
         for i in range(32):
             s = np.float32(s + np.float32(np.float32(scale * q[i]) * x[block * 32 + i]))
     return s
+
+
+_Q40_STREAM_SCALES = (0x3C00, 0xB800, 0x3400, 0x0001)
+
+
+def q40_fixture(input_, output, kind="stream"):
+    """Q4_0 bytes of q40Fixture (tests/testdata/forward/q40_stream_test.go:20-29,
+    kind "stream") or quantOptimizationFixture(2, ...) (quant_optimization_test.go:25-38,
+    kind "opt"): block b gets the scale table's entry b % len and bytes
+    (b*13 + i*7) & 0xFF for i = 2..17."""
+    scales = _Q40_STREAM_SCALES if kind == "stream" else _Q80_SCALES
+    nb = input_ // 32 * output
+    blocks = np.arange(nb, dtype=np.int64)[:, None]
+    data = ((blocks * 13 + np.arange(18, dtype=np.int64)[None, :] * 7) & 0xFF).astype(np.uint8)
+    sc = np.array([scales[b % len(scales)] for b in range(nb)], np.uint16)
+    data[:, 0:2] = sc.view(np.uint8).reshape(nb, 2)
+    return data.reshape(-1)
+
+
+def q40_stream_x(batch, input_):
+    """x[i] = (i%23 - 11)/32 over the whole batch (q40_stream_test.go:79-81)."""
+    i = np.arange(batch * input_)
+    return ((i % 23 - 11) / 32).astype(np.float32)
+
+
+def q40_reference_dot(row, x):
+    """referenceQ40Dot (tests/testdata/forward/q40_model_test.go:112-129):
+    sequential float32 sum, low then high nibble of each byte."""
+    s = np.float32(0)
+    for block in range(len(row) // 18):
+        b = row[block * 18:(block + 1) * 18]
+        scale = np.frombuffer(bytes(b[0:2]), np.float16)[0].astype(np.float32)
+        for i in range(16):
+            low, high = np.float32(int(b[2 + i] & 15) - 8), np.float32(int(b[2 + i] >> 4) - 8)
+            s = np.float32(s + np.float32(np.float32(scale * low) * x[block * 32 + i]))
+            s = np.float32(s + np.float32(np.float32(scale * high) * x[block * 32 + i + 16]))
+    return s
