@@ -40,27 +40,6 @@ namespace spt {
 
 namespace {
 
-// ---- packed fp32 pairs (sm_100a f32x2): two independent IEEE
-// round-to-nearest operations, results equal to the scalar ones ----------
-__device__ __forceinline__ void add2(float &a0, float &a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-      "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(b0), "f"(b1));
-}
-__device__ __forceinline__ void mul2(float &a0, float &a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-      "mul.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(b0), "f"(b1));
-}
-__device__ __forceinline__ void fma2(float &c0, float &c1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mov.b64 rc, {%0, %1};\n\tfma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
-      : "+f"(c0), "+f"(c1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
 // =========================================================================
 // One input
 // =========================================================================
@@ -180,7 +159,8 @@ __global__ void __launch_bounds__(kQ40Threads, 1) k_q40_gemv(const __grid_consta
       }
       __syncwarp();
       const uint8_t *q = row_at(g) + 2 + 2 * j;
-      float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;  // chains 2j, 2j+1, 16+2j, 17+2j
+      float2 clo = make_float2(0.0f, 0.0f), chi = make_float2(0.0f, 0.0f);  // chains 2j, 2j+1 | 16+2j, 17+2j
+      const float2 sub_lo = make_float2(-8388616.0f, -32776.0f), sub_hi = make_float2(-524296.0f, -2056.0f);
 #pragma unroll 6
       for (int b = 0; b < nb; ++b) {
         const float4 xv = xs[b * 8 + j];
@@ -188,17 +168,17 @@ __global__ void __launch_bounds__(kQ40Threads, 1) k_q40_gemv(const __grid_consta
         const uint32_t v = *reinterpret_cast<const uint16_t *>(q + b * 18);
         // nibble n at bits 0/8 (low nibbles of bytes 2j, 2j+1) and 4/12 (high
         // nibbles): (2^e + n) - (2^e + 8) = n - 8, exact
-        float l0 = __uint_as_float((v & 0x000Fu) | 0x4B000000u);  // 2^23 + n
-        float l1 = __uint_as_float((v & 0x0F00u) | 0x47000000u);  // 2^15 + n
-        float h0 = __uint_as_float((v & 0x00F0u) | 0x49000000u);  // 2^19 + n
-        float h1 = __uint_as_float((v & 0xF000u) | 0x45000000u);  // 2^11 + n
-        add2(l0, l1, -8388616.0f, -32776.0f);
-        add2(h0, h1, -524296.0f, -2056.0f);
-        mul2(l0, l1, s, s);  // weight = (n - 8) * scale (exact)
-        mul2(h0, h1, s, s);
-        fma2(c0, c1, l0, l1, xv.x, xv.y);
-        fma2(c2, c3, h0, h1, xv.z, xv.w);
+        float2 wl = make_float2(__uint_as_float((v & 0x000Fu) | 0x4B000000u),   // 2^23 + n
+                                __uint_as_float((v & 0x0F00u) | 0x47000000u));  // 2^15 + n
+        float2 wh = make_float2(__uint_as_float((v & 0x00F0u) | 0x49000000u),   // 2^19 + n
+                                __uint_as_float((v & 0xF000u) | 0x45000000u));  // 2^11 + n
+        const float2 ss = make_float2(s, s);
+        wl = __fmul2_rn(__fadd2_rn(wl, sub_lo), ss);  // weight = (n - 8) * scale (exact); packed f32x2:
+        wh = __fmul2_rn(__fadd2_rn(wh, sub_hi), ss);  // two independent IEEE operations
+        clo = __ffma2_rn(wl, make_float2(xv.x, xv.y), clo);
+        chi = __ffma2_rn(wh, make_float2(xv.z, xv.w), chi);
       }
+      const float c0 = clo.x, c1 = clo.y, c2 = chi.x, c3 = chi.y;
       // a0+a1+a2+a3 then quantSumAVX2 over the sub-group's 8 lanes:
       // s_m = ((a_m + a_{8+m}) + a_{16+m}) + a_{24+m}; lane j < 4 holds
       // a_{2j+e} and a_{16+2j+e}, lane j+4 holds a_{8+2j+e} and a_{24+2j+e}
@@ -252,7 +232,7 @@ __device__ __forceinline__ void lds_vec(float *v, const float *p) {
 // CTA tile: BM = 8*TM rows x BN = 4*TN items; lane = (pm = lane & 7,
 // pn = lane >> 3) owns rows pm*TM.. and items pn*TN.. of chain `warp`.
 template <int TM, int TN>
-__global__ void __launch_bounds__(kQ40BatchThreads, 2)
+__global__ void __launch_bounds__(kQ40BatchThreads, TM * TN <= 16 ? 3 : 2)
     k_q40_batch(const uint8_t *__restrict__ w, int64_t rows, int input, const float *__restrict__ x,
                 int64_t batch, float *__restrict__ y) {
   constexpr int BM = 8 * TM, BN = 4 * TN;
@@ -271,8 +251,11 @@ __global__ void __launch_bounds__(kQ40BatchThreads, 2)
   const int64_t row0 = (int64_t)blockIdx.x * BM, item0 = (int64_t)blockIdx.y * BN;
 
   // decode role: tile row drow, stage elements [dk, dk + EPT) = one nibble
-  // plane (low: elements 0..15, high: 16..31) of one block
-  const int drow = tid % BM, dk = (tid / BM) * EPT;
+  // plane (low: elements 0..15, high: 16..31) of one block.  With TM = 8 the
+  // 32 rows a warp decodes are those whose shared-memory positions fill one
+  // 128-byte half (dpos = half*32 + lane), so its stores are conflict-free.
+  const int dloc = tid % BM, dk = (tid / BM) * EPT;
+  const int drow = TM == 8 ? ((dloc & 31) >> 2) * 8 + (dloc >> 5) * 4 + (dloc & 3) : dloc;
   const int dblk = dk >> 5, dhalf = (dk & 31) >> 4, dbyte = dk & 15;
   const int dpos = q40_wpos<TM>(drow);
   // staging role for x: item xitem, stage elements [xk, xk + XPT)
@@ -305,10 +288,12 @@ __global__ void __launch_bounds__(kQ40BatchThreads, 2)
     const float s = __half2float(__ushort_as_half((unsigned short)wsc));
 #pragma unroll
     for (int i = 0; i < EPT / 2; ++i) {
-      const uint32_t b0 = wraw[i] & 0xFFu, b1 = (wraw[i] >> 8) & 0xFFu;
-      const int n0 = (int)(dhalf ? (b0 >> 4) : (b0 & 15u)), n1 = (int)(dhalf ? (b1 >> 4) : (b1 & 15u));
-      ws[buf][dk + 2 * i][dpos] = __fmul_rn(__int2float_rn(n0 - 8), s);  // exact
-      ws[buf][dk + 2 * i + 1][dpos] = __fmul_rn(__int2float_rn(n1 - 8), s);
+      // nibble of byte dbyte+2i (bits 0-7) and dbyte+2i+1 (bits 8-15) as
+      // 2^23 + n, then - (2^23 + 8) and * scale: exact (no int->float convert)
+      const uint32_t v = dhalf ? (wraw[i] >> 4) : wraw[i];
+      const float n0 = __uint_as_float(0x4B000000u | (v & 15u)), n1 = __uint_as_float(0x4B000000u | ((v >> 8) & 15u));
+      ws[buf][dk + 2 * i][dpos] = __fmul_rn(__fsub_rn(n0, 8388616.0f), s);
+      ws[buf][dk + 2 * i + 1][dpos] = __fmul_rn(__fsub_rn(n1, 8388616.0f), s);
     }
 #pragma unroll
     for (int i = 0; i < XPT; ++i) xs[buf][xk + i][xitem] = xr[i];
@@ -316,11 +301,13 @@ __global__ void __launch_bounds__(kQ40BatchThreads, 2)
 
   pdl_wait();
   pdl_trigger();
-  float acc[TM][TN];
+  // accumulators in row pairs: accp[i][jj] = (row 2i, row 2i+1) of item jj,
+  // updated by one packed f32x2 fma (two independent IEEE fmas)
+  float2 accp[TM / 2][TN];
 #pragma unroll
-  for (int i = 0; i < TM; ++i)
+  for (int i = 0; i < TM / 2; ++i)
 #pragma unroll
-    for (int jj = 0; jj < TN; ++jj) acc[i][jj] = 0.0f;
+    for (int jj = 0; jj < TN; ++jj) accp[i][jj] = make_float2(0.0f, 0.0f);
   const int nst = (nb + 1) / 2;
   fetch(0);
   stage_in(0);
@@ -341,9 +328,11 @@ __global__ void __launch_bounds__(kQ40BatchThreads, 2)
       }
       lds_vec<TN>(xv, &xs[buf][kk][pn * TN]);
 #pragma unroll
-      for (int i = 0; i < TM; ++i)
+      for (int jj = 0; jj < TN; ++jj) {
+        const float2 xx = make_float2(xv[jj], xv[jj]);
 #pragma unroll
-        for (int jj = 0; jj < TN; ++jj) acc[i][jj] = __fmaf_rn(wv[i], xv[jj], acc[i][jj]);
+        for (int i = 0; i < TM / 2; ++i) accp[i][jj] = __ffma2_rn(make_float2(wv[2 * i], wv[2 * i + 1]), xx, accp[i][jj]);
+      }
     }
     if (st + 1 < nst) stage_in(buf ^ 1);
     __syncthreads();
@@ -353,6 +342,11 @@ __global__ void __launch_bounds__(kQ40BatchThreads, 2)
   // (p_0 + p_1) + (p_2 + p_3); chains meet through shared memory
   float *red = &ws[0][0][0];  // [slot][TM*TN][32 lanes]
   constexpr int A = TM * TN;
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM / 2; ++i)
+#pragma unroll
+    for (int jj = 0; jj < TN; ++jj) acc[2 * i][jj] = accp[i][jj].x, acc[2 * i + 1][jj] = accp[i][jj].y;
   auto put = [&](int slot) {
 #pragma unroll
     for (int i = 0; i < TM; ++i)
@@ -390,6 +384,19 @@ __global__ void __launch_bounds__(kQ40BatchThreads, 2)
   }
 }
 
+// Relative time of one tile shape: the busiest SM's tiles x tile work / the
+// share of issue slots its inner loop gives to FMAs (TM*TN FMAs per TM/4 +
+// ceil(TN/4) shared loads and ~2 loop instructions), 1.5x when an SM would
+// hold a single tile (too few warps to hide latency).
+template <int TM, int TN>
+double batch_tile_cost(int64_t rows, int64_t batch, int sm_count) {
+  constexpr int BM = 8 * TM, BN = 4 * TN;
+  const int64_t tiles = ((rows + BM - 1) / BM) * ((batch + BN - 1) / BN);
+  const int64_t per_sm = (tiles + sm_count - 1) / sm_count;
+  const double eff = (double)(TM * TN) / (TM * TN + TM / 4 + (TN + 3) / 4 + 2);
+  return (double)per_sm * BM * BN / eff * (per_sm < 2 ? 1.5 : 1.0);
+}
+
 template <int TM, int TN>
 cudaError_t launch_batch_tile(const uint8_t *w, int64_t rows, int input, const float *x, int64_t batch, float *y,
                               cudaStream_t stream) {
@@ -416,10 +423,19 @@ cudaError_t launch_q40(const uint8_t *w, int64_t rows, int input, const float *x
                        int32_t *err, int sm_count, cudaStream_t stream) {
   if (!q40_supported(input) || rows <= 0 || batch <= 0) return cudaErrorInvalidValue;
   if (batch > 1) {
-    if (batch <= 4) return launch_batch_tile<4, 1>(w, rows, input, x, batch, y, stream);
-    if (batch <= 8) return launch_batch_tile<4, 2>(w, rows, input, x, batch, y, stream);
-    if (batch <= 16) return launch_batch_tile<4, 4>(w, rows, input, x, batch, y, stream);
-    return launch_batch_tile<8, 8>(w, rows, input, x, batch, y, stream);
+    const double c[5] = {batch_tile_cost<4, 1>(rows, batch, sm_count), batch_tile_cost<4, 2>(rows, batch, sm_count),
+                         batch_tile_cost<4, 4>(rows, batch, sm_count), batch_tile_cost<8, 4>(rows, batch, sm_count),
+                         batch_tile_cost<8, 8>(rows, batch, sm_count)};
+    int best = 0;
+    for (int i = 1; i < 5; ++i)
+      if (c[i] < c[best]) best = i;
+    switch (best) {
+      case 0: return launch_batch_tile<4, 1>(w, rows, input, x, batch, y, stream);
+      case 1: return launch_batch_tile<4, 2>(w, rows, input, x, batch, y, stream);
+      case 2: return launch_batch_tile<4, 4>(w, rows, input, x, batch, y, stream);
+      case 3: return launch_batch_tile<8, 4>(w, rows, input, x, batch, y, stream);
+      default: return launch_batch_tile<8, 8>(w, rows, input, x, batch, y, stream);
+    }
   }
   const size_t smem = q40_smem_bytes(input);
   cudaError_t e = opt_in_smem(k_q40_gemv, (int)smem);

@@ -62,6 +62,13 @@ def main():
         "config_fields": struct_fields(config, "Config"),
         "forward_types": sorted(set(re.findall(r"^type (\w+)", q40, re.M))),
         "forward_moe_batch_params": " ".join(sig.split()),
+        "forward_funcs": sorted(set(re.findall(r"^func ([A-Za-z]\w*)\(", q40, re.M))),
+        "forward_consts": sorted(set(re.findall(r"^(?:const |\t)([A-Za-z]\w*)\s*(?:[\w.]+\s*)?=", q40, re.M))),
+        "mul_q40_params": " ".join(re.search(r"func MulQ40Into\((.*?)\) error \{", q40, re.S).group(1).split()),
+        "mul_q40_batch_params": " ".join(
+            re.search(r"func MulQ40BatchInto\((.*?)\) error \{", q40, re.S).group(1).split()),
+        "q40_shape_results": " ".join(
+            re.search(r"func q40Shape\(tensor ggufindex\.Tensor\) \((.*?)\) \{", q40, re.S).group(1).split()),
     }
     with open(os.path.join(HERE, "go_api.json"), "w") as f:
         json.dump(api, f, indent=1, sort_keys=True)

@@ -12,17 +12,24 @@ import os
 import re
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-SHIM = open(os.path.join(ROOT, "stream-pt_b200", "go", "moe_cuda.go")).read()
+GO_DIR = os.path.join(ROOT, "stream-pt_b200", "go")
+SHIMS = {f: open(os.path.join(GO_DIR, f)).read() for f in sorted(os.listdir(GO_DIR)) if f.endswith(".go")}
+SHIM = SHIMS["moe_cuda.go"]
 API = json.load(open(os.path.join(ROOT, "tests", "golden", "go_api.json")))
 HEADER = open(os.path.join(ROOT, "include", "spt_moe.h")).read()
-CODE = re.sub(r"//[^\n]*", "", SHIM)  # comments out
+# every shim file, comments out (they form one package)
+CODE = "\n".join(re.sub(r"//[^\n]*", "", src) for src in SHIMS.values())
+Q40 = re.sub(r"//[^\n]*", "", SHIMS["q40_cuda.go"])
 
 
 def test_imports_name_the_reference_packages():
-    imports = dict((alias or path.split("/")[-1], path) for alias, path in
-                   re.findall(r'^\s*(\w+)?\s*"([^"]+)"$', CODE.split("import (", 1)[1].split(")", 1)[0], re.M))
-    assert imports["ggufindex"] == API["module"] + "/ggufindex"
-    assert imports[API["packages"]["ggufmap"]] == API["module"] + "/ggufmap"
+    for src in SHIMS.values():
+        code = re.sub(r"//[^\n]*", "", src)
+        imports = dict((alias or path.split("/")[-1], path) for alias, path in
+                       re.findall(r'^\s*(\w+)?\s*"([^"]+)"$', code.split("import (", 1)[1].split(")", 1)[0], re.M))
+        assert imports["ggufindex"] == API["module"] + "/ggufindex"
+        assert imports[API["packages"]["ggufmap"]] == API["module"] + "/ggufmap"
+        assert src.startswith("//go:build goexperiment.simd && sptcuda")
 
 
 def test_reader_methods_exist():
@@ -72,3 +79,27 @@ def test_c_symbols_and_fields_are_declared():
             block = CODE[m.end():i - 1]
             named = set(re.findall(r"\b([a-z_]\w*):", block))
             assert named <= fields, (typ, named - fields)
+
+
+def test_q40_signatures_unchanged():
+    """MulQ40Into / MulQ40BatchInto keep the reference's parameter lists
+    (forward/q40.go:35-101); the helpers the shim keeps from q40.go exist."""
+    one = re.search(r"func MulQ40Into\((.*?)\) error \{", Q40, re.S).group(1)
+    many = re.search(r"func MulQ40BatchInto\((.*?)\) error \{", Q40, re.S).group(1)
+    assert " ".join(one.split()) == API["mul_q40_params"]
+    assert " ".join(many.split()) == API["mul_q40_batch_params"]
+    assert API["q40_shape_results"] == "input, output, rowBytes int, err error"
+    assert re.search(r"input, output, rowBytes, err := q40Shape\(tensor\)", Q40)
+    for fn in ("q40Shape", "float32Overlap"):
+        assert fn in API["forward_funcs"]
+    assert "DefaultQ40WindowBytes" in API["forward_consts"]
+    # the shim defines only the two replaced exported functions and its helpers
+    defined = set(re.findall(r"^func (\w+)\(", Q40, re.M))
+    assert defined == {"q40Matrix", "MulQ40Into", "MulQ40BatchInto"}
+
+
+def test_q40_error_texts_follow_the_reference():
+    for text in ("nil context", "nil GGUF reader", "invalid or oversized batch: %d",
+                 "%q: expected %d input and %d output elements, got %d and %d",
+                 "input and output must not overlap", "window of %d bytes cannot accommodate a %d-byte row"):
+        assert '"%s"' % text in Q40, text
