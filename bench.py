@@ -786,6 +786,11 @@ def _q40_bytes(rows, input_, seed):
     return data.reshape(-1)
 
 
+def _q40_traffic(prefix):
+    qkv, o = load_traffic(prefix + ":qkv_dram_bytes"), load_traffic(prefix + ":o_dram_bytes")
+    return None if qkv is None or o is None else Q40_LAYERS * (qkv + o)
+
+
 def run_q40(args):
     """--config q40 / q40b: the Q4_0 attention projections of GPT-OSS-120B
     (MulQ40Into / MulQ40BatchInto, forward/q40.go:35-101): per layer the
@@ -904,13 +909,17 @@ def run_q40(args):
             "gpu_launches": args.steps * 2 * Q40_LAYERS, "clocks": clocks.summary()}
     if batch == 1:
         line["roofline"] = {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
-                            "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "kernel": "k_q40_gemv",
+                            "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": _q40_traffic("q40:gemv"),
+                            "traffic_scope": "per step: 36 x the fused-QKV and O launches ncu captured",
+                            "kernel": "k_q40_gemv",
                             "algorithmic_bytes": nbytes, "avg_ms": ms, "peak_source": peak_src}
     else:
         nominal = 148 * 128 * 2 * 1.965e9 / 1e12  # fp32 FMA on CUDA cores at the max SM clock
         tf = 2 * fmas / (ms / 1e3) / 1e12
         line["roofline"] = {"bound": "fp32-fma", "achieved": tf, "peak": nominal, "unit": "TFLOP/s",
-                            "frac": tf / nominal, "traffic": None, "kernel": "k_q40_batch",
+                            "frac": tf / nominal, "traffic": _q40_traffic("q40b:batch"),
+                            "traffic_scope": "per step: 36 x the fused-QKV and O launches ncu captured",
+                            "kernel": "k_q40_batch",
                             "algorithmic_flops": 2 * fmas, "algorithmic_bytes": nbytes, "avg_ms": ms,
                             "peak_source": "nominal fp32 CUDA-core rate (148 SMs x 128 FMA/clk x 1965 MHz); "
                                            "no measured fp32 figure"}

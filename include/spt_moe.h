@@ -384,7 +384,7 @@ spt_status spt_mul_q80_matrix_device(spt_context *ctx, spt_q80_matrix *m, const 
  * type, rank, shape, batch (< 1 or overflowing) and x_len/y_len != batch *
  * input/output; SPT_ERR_FILE_RANGE for the byte range; SPT_ERR_OVERLAP when x
  * and y overlap; SPT_ERR_CANCELED when *cancel is set on entry (the one
- * launch is not interrupted).  This build needs input <= ~4,600
+ * launch is not interrupted).  This build needs input <= 4,768
  * (SPT_ERR_UNSUPPORTED above; GPT-OSS uses 2,880 and 4,096).  The matrix is
  * uploaded for the call; spt_q40_matrix keeps it resident. */
 spt_status spt_mul_q40(spt_context *ctx, const spt_reader *reader, const spt_tensor *tensor, const float *x,
