@@ -914,12 +914,13 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // select = false leaves the selection to the fused dispatch kernel.
 spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
                         int64_t T, int32_t *sel_idx, float *sel_w, bool select = true,
-                        const RouterSplit *split = nullptr, bool *split_done = nullptr) {
+                        const RouterSplit *split = nullptr, bool *split_done = nullptr,
+                        const RouterNorm *norm = nullptr, int *router_launches = nullptr) {
   const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
   SPT_MARK(0);
   SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s, split,
-                              split_done));
+                              split_done, norm, router_launches));
   SPT_MARK(1);
   if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
@@ -935,9 +936,10 @@ spt_status check_layer_limits(spt_context *ctx, const spt_moe_config &c) {
 
 // The whole block on device pointers (enqueue only).
 // With resid, out = resid + block(x) (the layer stack's residual add; out
-// may be resid).
+// may be resid).  With norm, the block's input is normBatch(x) (written to
+// norm->out, by the router's prologue when it can), and x is only read.
 spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, const float *x,
-                          float *out, int64_t T, const float *resid = nullptr) {
+                          float *out, int64_t T, const float *resid = nullptr, const RouterNorm *norm = nullptr) {
   const spt_moe_config &c = arena->cfg;
   spt_status st = check_layer_limits(ctx, c);
   if (st) return st;
@@ -960,12 +962,14 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     rs.kp = L.gu_mma.kp;
   }
   bool split_done = false;
+  int router_launches = 1;
   if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse,
-                         path == kPathGemv16 ? &rs : nullptr, &split_done)))
+                         path == kPathGemv16 ? &rs : nullptr, &split_done, norm, &router_launches)))
     return st;
-  if ((st = experts_combine(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), out, 0,
-                            fuse ? ctx->logits.as<float>() : nullptr, split_done, resid)))
+  if ((st = experts_combine(ctx, L, c, norm ? norm->out : x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(),
+                            out, 0, fuse ? ctx->logits.as<float>() : nullptr, split_done, resid)))
     return st;
+  ctx->kernels_last += router_launches - 1;
   ctx->last_T = T;
   ctx->last_E = c.num_experts;
   ctx->last_K = c.num_experts_used;
@@ -3163,17 +3167,22 @@ spt_status forward_stack_device(spt_context *ctx, spt_ep *ep, spt_arena *arena, 
   int kernels = 0;
   for (int64_t l = first; l < first + n; ++l) {
     const LayerDev &L = arena->layers[(size_t)l];
-    SPT_CUDA(ctx, launch_rmsnorm(x, L.norm, (int)T, (int)H, eps, normed, 8, ctx->stream));
     if (ep) {
+      SPT_CUDA(ctx, launch_rmsnorm(x, L.norm, (int)T, (int)H, eps, normed, 8, ctx->stream));
       spt_status st = forward_ep_device(ctx, ep, arena, l, normed, ffn, T);
       if (st) return st;
       SPT_CUDA(ctx, launch_add(x, ffn, T * H, ctx->stream));
       kernels += 2 + ctx->kernels_last;
     } else {
-      // the residual add happens in the block's combine: x = x + block(normed)
-      spt_status st = forward_device(ctx, arena, l, normed, x, T, x);
+      // normBatch happens in the router's prologue (the block's input goes to
+      // `normed`), the residual add in the block's combine: x = x + block(norm(x))
+      RouterNorm rn;
+      rn.w = L.norm;
+      rn.eps = eps;
+      rn.out = normed;
+      spt_status st = forward_device(ctx, arena, l, x, x, T, x, &rn);
       if (st) return st;
-      kernels += 1 + ctx->kernels_last;
+      kernels += ctx->kernels_last;
     }
   }
   ctx->kernels_last = kernels;

@@ -95,9 +95,21 @@ struct RouterSplit {
   int32_t *xe = nullptr;
   int kp = 0;
 };
+// normBatch (8 lanes) applied to the router's input first: out = rows of
+// (x * w) * f, f = 1/float32(sqrt(float64(sum(x^2)/dim + eps))).  Folded into
+// the router's prologue when it stages its rows in shared memory (and then
+// written out by the router's CTAs for the expert kernels), else a separate
+// k_rmsnorm launch before the router; either way the router reads the
+// normalised rows and `out` holds them afterwards.
+struct RouterNorm {
+  const float *w = nullptr;
+  float eps = 0.0f;
+  float *out = nullptr;
+};
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream,
-                          const RouterSplit *split = nullptr, bool *split_done = nullptr);
+                          const RouterSplit *split = nullptr, bool *split_done = nullptr,
+                          const RouterNorm *norm = nullptr, int *launches = nullptr);
 cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
                           float *sel_w, cudaStream_t stream);
 // Tensor-core tile layout computed by the dispatch kernel (bn = 0: none).

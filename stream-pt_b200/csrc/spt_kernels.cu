@@ -202,7 +202,9 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
                                                      const float *__restrict__ bias, int T, int H,
                                                      int E, int EG, int TG,
                                                      float *__restrict__ logits, __half *__restrict__ xq,
-                                                     int32_t *__restrict__ xe, int KP) {
+                                                     int32_t *__restrict__ xe, int KP,
+                                                     const float *__restrict__ norm_w, float eps,
+                                                     float *__restrict__ normed) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 router_smem[];
@@ -220,6 +222,33 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (norm_w) {
+    // normBatch (forward/layer_batch.go:139-195) on the staged token rows, in
+    // k_rmsnorm's order: 8 lanes of sequential squares, summed lane by lane;
+    // then the rows are replaced by (x * w) * f, and this CTA's share of them
+    // (every gridDim.x-th element) goes to `normed` for the expert kernels
+    __shared__ float s_f[8];
+    for (int j = warp; j < nt; j += blockDim.x >> 5) {
+      const float *xr = xs + (size_t)j * H;
+      float acc = 0.0f;
+      if (lane < 8)
+        for (int o = 0; o < H; o += 8) {
+          const float v = (o + lane < H) ? xr[o + lane] : 0.0f;
+          acc = fmaf(v, v, acc);
+        }
+      float sum = 0.0f;
+      for (int l = 0; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(kFull, acc, l));
+      if (lane == 0) s_f[j] = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(__fdiv_rn(sum, (float)H), eps)));
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nt * H; i += blockDim.x) {
+      const int j = i / H, k = i - j * H;
+      xs[i] = __fmul_rn(__fmul_rn(xs[i], __ldg(norm_w + k)), s_f[j]);
+    }
+    __syncthreads();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nt * H; i += gridDim.x * blockDim.x)
+      normed[(size_t)t0 * H + i] = xs[i];
+  }
   if (xq) {
     // The decode GEMV's split operand of these tokens (spt_gemv16.cuh), made
     // here from the staged rows: CTA bx writes K tiles bx, bx + gridDim.x, ...
@@ -973,10 +1002,22 @@ cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
 
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream, const RouterSplit *split,
-                          bool *split_done) {
+                          bool *split_done, const RouterNorm *norm, int *launches) {
   if (split_done) *split_done = false;
+  if (launches) *launches = 1;
   if (T <= 0) return cudaSuccess;
+  // the normalisation is folded into k_router_smem's prologue when that kernel
+  // runs; otherwise it is its own launch and the router reads its output
+  auto separate_norm = [&]() -> cudaError_t {
+    if (!norm) return cudaSuccess;
+    if (launches) *launches = 2;
+    cudaError_t e = launch_rmsnorm(x, norm->w, T, H, norm->eps, norm->out, 8, stream);
+    x = norm->out;
+    return e;
+  };
   if (H % 32 != 0) {
+    cudaError_t e = separate_norm();
+    if (e != cudaSuccess) return e;
     return launch_pdl(k_router_portable, dim3(E, T), dim3(32), 0, stream, W, x, bias, T, H, E, portable_lanes,
                       logits);
     return cudaGetLastError();
@@ -999,8 +1040,12 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
     if (split_done) *split_done = do_split;
     return launch_pdl(k_router_smem, dim3((E + EG - 1) / EG, (T + TG - 1) / TG), dim3(256), (size_t)bytes(EG, TG),
                       stream, W, x, bias, T, H, E, EG, TG, logits, do_split ? split->xq : (__half *)nullptr,
-                      do_split ? split->xe : (int32_t *)nullptr, do_split ? split->kp : 0);
+                      do_split ? split->xe : (int32_t *)nullptr, do_split ? split->kp : 0,
+                      norm ? norm->w : (const float *)nullptr, norm ? norm->eps : 0.0f,
+                      norm ? norm->out : (float *)nullptr);
   } else {
+    cudaError_t e = separate_norm();
+    if (e != cudaSuccess) return e;
     return launch_pdl(k_router<8, 4, 1>, dim3((E + 3) / 4, (T + 7) / 8), dim3(32), 0, stream, W, x, bias, T, H, E,
                       logits);
   }

@@ -33,8 +33,11 @@ def oracle_stack(spt, cfg, params, x, T, layers):
     return x.reshape(-1)
 
 
-@pytest.mark.parametrize("T", [1, 5])
+@pytest.mark.parametrize("T", [1, 5, 9, 70])
 def test_stack_small_exact(ctx, spt, T):
+    """Up to 64 tokens normBatch runs in the router's prologue (k_router_smem),
+    beyond that as its own launch before the register-blocked router; both
+    bit-identical to the oracle's composition."""
     cfg = spt.Config(256, 128, 16, 4)
     params = spt.SynthParams(seed=41)
     arena = ctx.synthetic_arena(cfg, params, n_layers=3, flags=spt.ARENA_GEMV)
@@ -48,6 +51,12 @@ def test_stack_small_exact(ctx, spt, T):
         mid = ctx.forward_stack(arena, x, T, first_layer=0, n_layers=1, eps=EPS)
         rest = ctx.forward_stack(arena, mid, T, first_layer=1, n_layers=2, eps=EPS)
         assert np.array_equal(rest.view(np.uint32), want.view(np.uint32))
+        # launches per layer: the block's own, plus the separate normalisation
+        # only when the router does not stage its rows (T > 64)
+        ctx.forward_stack(arena, x, T, first_layer=0, n_layers=1, eps=EPS)
+        per_layer = ctx.kernels_per_forward()
+        ctx.forward_moe_batch(arena, x, T)
+        assert per_layer == ctx.kernels_per_forward() + (1 if T > 64 else 0)
     finally:
         arena.close()
 
@@ -67,7 +76,15 @@ def test_stack_gpt_oss_two_layers(ctx, spt):
         got = ctx.forward_stack(arena, x, T, eps=EPS)
         err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
         assert np.isfinite(got).all() and err <= 1e-3, err
+        # decode rows on the decode GEMV: its split f16 operand is made from the
+        # rows the router normalised in its prologue
+        ctx.set_path(spt.PATH_AUTO)
+        got4 = ctx.forward_stack(arena, x[:4 * 2880], 4, eps=EPS)
+        want4 = oracle_stack(spt, cfg, params, x[:4 * 2880], 4, 2)
+        err = float(np.max(np.abs(got4 - want4)) / np.max(np.abs(want4)))
+        assert np.isfinite(got4).all() and err <= 1e-3, err
     finally:
+        ctx.set_path(spt.PATH_AUTO)
         arena.close()
 
 
