@@ -212,9 +212,12 @@ spt_status spt_context_set_path(spt_context *ctx, int path);
  * context is created, from the environment variable named beside each.
  *   SPT_OPT_TILE_TOKENS   tcgen05 token-tile width 8, 16 or 128; 0 picks it
  *                         from the batch (SPT_MMA_BN)
- *   SPT_OPT_FUSED_SELECT  1: top-k selection runs inside the dispatch kernel
- *                         for batches of up to 8 tokens; 0: its own launch
- *                         (SPT_FUSED_SELECT)
+ *   SPT_OPT_FUSED_SELECT  batches of up to 8 tokens on one device: 1 (default)
+ *                         top-k selection and dispatch run in the router's
+ *                         last CTA when the router stages its rows in shared
+ *                         memory, else selection inside the dispatch kernel;
+ *                         2: selection inside the dispatch kernel; 0: each
+ *                         its own launch (SPT_FUSED_SELECT); same results
  *   SPT_OPT_L2_PREFETCH   tcgen05 weight tiles prefetched into L2 ahead of
  *                         the ring, 0 off (SPT_MMA_PREFETCH)
  *   SPT_OPT_GEMV16_SLOTS  SPT_PATH_AUTO runs the decode GEMV while

@@ -75,6 +75,7 @@ struct spt_context {
   DevBuf dev_err, pad_off, tile_gu, tile_dn, pos_expert, qx, sfx, qa, sfa;
   DevBuf stack_norm, stack_ffn;  // layer stack: normed rows and block output [T][H]
   DevBuf g16_count;  // decode GEMV: arrivals per down row group of the fused combine (zero between launches)
+  DevBuf route_count;  // router CTAs finished, for the selection + dispatch in its last CTA (zero between launches)
   DevBuf xq, xe, actq, act_off;  // decode GEMV: split x rows, their exponents, split SwiGLU rows,
                                  // first dispatch position of each active expert
   int32_t *err_host = nullptr;  // pinned copy of dev_err, read after the host path's single sync
@@ -82,7 +83,8 @@ struct spt_context {
   size_t hx_bytes = 0, hout_bytes = 0;
   // tuning options (spt_context_set_option), seeded from the environment once
   int opt_tile_tokens = 0;      // tcgen05 token-tile width (0: from the batch)
-  int opt_fused_select = 1;     // top-k inside the dispatch kernel for T <= kSelectDispatchMaxTokens
+  int opt_fused_select = 1;     // T <= kSelectDispatchMaxTokens: 1 top-k + dispatch in the router's last CTA
+                                // (else in the dispatch kernel), 2 in the dispatch kernel, 0 separate
   int opt_prefetch = 0;         // tcgen05 weight tiles prefetched into L2 ahead
   int opt_gemv16_slots = 16;    // SPT_PATH_AUTO: decode GEMV while batch x top-k <= this
   int opt_wait_shift = 31;      // bounded device waits give up after 2^shift clock cycles
@@ -756,10 +758,30 @@ spt_status reserve_experts(spt_context *ctx, const LayerDev &L, const spt_moe_co
 // launch (one launch fewer; the last CTA of each row group does the sums).
 constexpr int64_t kFusedCombineSlots = 64;
 
+// The tensor-core tile layout (and the decode GEMV's position table) the
+// dispatch lays out for this batch on `path`.
+DispatchPlan dispatch_plan(spt_context *ctx, const LayerDev &L, int64_t T, int K, int E, ExpertPath path,
+                           int bn_hint) {
+  DispatchPlan plan;
+  if (path == kPathGemv16) plan.act_off = ctx->act_off.as<int32_t>();
+  if (path == kPathTcgen05) {
+    plan.bn = bn_hint ? bn_hint : pick_bn(ctx, T, K, E);
+    plan.mt_gu = mma_row_units(plan.bn, L.gu_mma.mtiles);
+    plan.mt_dn = mma_row_units(plan.bn, L.dn_mma.mtiles);
+    plan.pad_off = ctx->pad_off.as<int32_t>();
+    plan.tile_gu = ctx->tile_gu.as<int32_t>();
+    plan.tile_dn = ctx->tile_dn.as<int32_t>();
+    plan.pos_expert = ctx->pos_expert.as<int32_t>();
+  }
+  return plan;
+}
+
+// dispatched: the router's last CTA already selected and dispatched (no
+// dispatch launch here).
 spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
                            int64_t T, const int32_t *sel_idx, const float *sel_w, float *out, int bn_hint = 0,
                            const float *logits = nullptr, bool x_split_done = false,
-                           const float *resid = nullptr) {
+                           const float *resid = nullptr, bool dispatched = false) {
   const int H = (int)c.hidden_dim, D = (int)c.expert_hidden_dim, E = (int)c.num_experts,
             K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
@@ -772,19 +794,12 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
   const bool use_mma = path == kPathTcgen05;
   ctx->last_path = path == kPathGemv16 ? SPT_PATH_GEMV16 : use_mma ? SPT_PATH_MMA : SPT_PATH_EXACT;
   ctx->last_bn = 0;
-  DispatchPlan plan;  // tensor-core tile layout, made by the dispatch kernel
-  if (path == kPathGemv16) plan.act_off = ctx->act_off.as<int32_t>();
-  if (use_mma) {
-    plan.bn = bn_hint ? bn_hint : pick_bn(ctx, T, K, E);
-    ctx->last_bn = plan.bn;
-    plan.mt_gu = mma_row_units(plan.bn, L.gu_mma.mtiles);
-    plan.mt_dn = mma_row_units(plan.bn, L.dn_mma.mtiles);
-    plan.pad_off = ctx->pad_off.as<int32_t>();
-    plan.tile_gu = ctx->tile_gu.as<int32_t>();
-    plan.tile_dn = ctx->tile_dn.as<int32_t>();
-    plan.pos_expert = ctx->pos_expert.as<int32_t>();
-  }
-  if (logits) {
+  // tensor-core tile layout, made by the dispatch kernel
+  const DispatchPlan plan = dispatch_plan(ctx, L, T, K, E, path, bn_hint);
+  if (use_mma) ctx->last_bn = plan.bn;
+  if (dispatched) {
+    // made by the router's last CTA
+  } else if (logits) {
     SPT_CUDA(ctx, launch_select_dispatch(logits, (int)T, E, K, const_cast<int32_t *>(sel_idx),
                                          const_cast<float *>(sel_w), ctx->offsets.as<int32_t>(),
                                          ctx->perm.as<int32_t>(), ctx->slot_pos.as<int32_t>(),
@@ -906,7 +921,8 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
     SPT_CUDA(ctx, launch_combine(ctx->res.as<float>(), sel_w, ctx->slot_pos.as<int32_t>(), (int)T, K, H, out, s,
                                  resid));
   SPT_MARK(8);
-  if (logits) ctx->kernels_last -= 1;  // no separate selection launch
+  if (logits || dispatched) ctx->kernels_last -= 1;  // no separate selection launch
+  if (dispatched) ctx->kernels_last -= 1;            // nor a dispatch launch
   return SPT_OK;
 }
 
@@ -915,12 +931,13 @@ spt_status experts_combine(spt_context *ctx, const LayerDev &L, const spt_moe_co
 spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_config &c, const float *x,
                         int64_t T, int32_t *sel_idx, float *sel_w, bool select = true,
                         const RouterSplit *split = nullptr, bool *split_done = nullptr,
-                        const RouterNorm *norm = nullptr, int *router_launches = nullptr) {
+                        const RouterNorm *norm = nullptr, int *router_launches = nullptr,
+                        const RouterDispatch *dispatch = nullptr, bool *dispatch_done = nullptr) {
   const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
   SPT_MARK(0);
   SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s, split,
-                              split_done, norm, router_launches));
+                              split_done, norm, router_launches, dispatch, dispatch_done));
   SPT_MARK(1);
   if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
@@ -961,13 +978,36 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
     rs.xe = ctx->xe.as<int32_t>();
     rs.kp = L.gu_mma.kp;
   }
-  bool split_done = false;
+  bool split_done = false, dispatched = false;
   int router_launches = 1;
+  // decode batches: selection and dispatch in the router's last CTA when it
+  // stages its rows (SPT_OPT_FUSED_SELECT 1), else inside the dispatch kernel
+  RouterDispatch rd;
+  const bool router_dispatch = fuse && ctx->opt_fused_select == 1;
+  if (router_dispatch) {
+    if (ctx->route_count.bytes < sizeof(unsigned)) {
+      SPT_CUDA(ctx, ctx->route_count.ensure(sizeof(unsigned)));
+      SPT_CUDA(ctx, cudaMemsetAsync(ctx->route_count.p, 0, ctx->route_count.bytes, ctx->stream));
+    }
+    rd.sel_idx = ctx->sel_idx.as<int32_t>();
+    rd.sel_w = ctx->sel_w.as<float>();
+    rd.offsets = ctx->offsets.as<int32_t>();
+    rd.perm = ctx->perm.as<int32_t>();
+    rd.slot_pos = ctx->slot_pos.as<int32_t>();
+    rd.act_list = ctx->act_list.as<int32_t>();
+    rd.meta = ctx->meta.as<int32_t>();
+    rd.plan = path != kPathExact ? dispatch_plan(ctx, L, T, (int)c.num_experts_used, (int)c.num_experts, path, 0)
+                                 : DispatchPlan{};
+    rd.topk = (int)c.num_experts_used;
+    rd.count = ctx->route_count.as<unsigned>();
+  }
   if ((st = route_select(ctx, L, c, x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(), !fuse,
-                         path == kPathGemv16 ? &rs : nullptr, &split_done, norm, &router_launches)))
+                         path == kPathGemv16 ? &rs : nullptr, &split_done, norm, &router_launches,
+                         router_dispatch ? &rd : nullptr, &dispatched)))
     return st;
   if ((st = experts_combine(ctx, L, c, norm ? norm->out : x, T, ctx->sel_idx.as<int32_t>(), ctx->sel_w.as<float>(),
-                            out, 0, fuse ? ctx->logits.as<float>() : nullptr, split_done, resid)))
+                            out, 0, fuse && !dispatched ? ctx->logits.as<float>() : nullptr, split_done, resid,
+                            dispatched)))
     return st;
   ctx->kernels_last += router_launches - 1;
   ctx->last_T = T;
@@ -998,7 +1038,8 @@ std::vector<const void *> call_buffers(const spt_context *ctx) {
   for (const DevBuf *b : {&ctx->logits, &ctx->sel_idx, &ctx->sel_w, &ctx->offsets, &ctx->perm, &ctx->slot_pos,
                           &ctx->act_list, &ctx->meta, &ctx->act, &ctx->res, &ctx->xdev, &ctx->outdev, &ctx->dev_err,
                           &ctx->pad_off, &ctx->tile_gu, &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx,
-                          &ctx->qa, &ctx->sfa, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off, &ctx->g16_count})
+                          &ctx->qa, &ctx->sfa, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off, &ctx->g16_count,
+                          &ctx->route_count})
     v.push_back(b->p);
   return v;
 }
@@ -1143,7 +1184,7 @@ void seed_options(spt_context *ctx) {
   };
   env("SPT_MMA_BN", &ctx->opt_tile_tokens, 0, 128);
   if (ctx->opt_tile_tokens != 8 && ctx->opt_tile_tokens != 16 && ctx->opt_tile_tokens != 128) ctx->opt_tile_tokens = 0;
-  env("SPT_FUSED_SELECT", &ctx->opt_fused_select, 0, 1);
+  env("SPT_FUSED_SELECT", &ctx->opt_fused_select, 0, 2);
   env("SPT_MMA_PREFETCH", &ctx->opt_prefetch, 0, 64);
   env("SPT_GEMV16_SLOTS", &ctx->opt_gemv16_slots, 0, 1 << 20);
   env("SPT_HOST_GRAPHS", &ctx->opt_host_graphs, 0, 1);
@@ -1239,7 +1280,7 @@ void spt_context_destroy(spt_context *ctx) {
                       &ctx->xdev, &ctx->outdev, &ctx->dev_err, &ctx->pad_off, &ctx->tile_gu,
                       &ctx->tile_dn, &ctx->pos_expert, &ctx->qx, &ctx->sfx, &ctx->qa, &ctx->sfa,
                       &ctx->stack_norm, &ctx->stack_ffn, &ctx->xq, &ctx->xe, &ctx->actq, &ctx->act_off,
-                      &ctx->g16_count})
+                      &ctx->g16_count, &ctx->route_count})
       b->release();
     for (cudaEvent_t &e : ctx->ev)
       if (e) cudaEventDestroy(e);
@@ -1313,7 +1354,7 @@ spt_status spt_context_set_option(spt_context *ctx, int option, int64_t v) {
       ctx->opt_tile_tokens = (int)v;
       return SPT_OK;
     case SPT_OPT_FUSED_SELECT:
-      if (v != 0 && v != 1) break;
+      if (v < 0 || v > 2) break;
       ctx->opt_fused_select = (int)v;
       return SPT_OK;
     case SPT_OPT_L2_PREFETCH:

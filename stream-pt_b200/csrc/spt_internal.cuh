@@ -106,10 +106,6 @@ struct RouterNorm {
   float eps = 0.0f;
   float *out = nullptr;
 };
-cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
-                          float *logits, int portable_lanes, cudaStream_t stream,
-                          const RouterSplit *split = nullptr, bool *split_done = nullptr,
-                          const RouterNorm *norm = nullptr, int *launches = nullptr);
 cudaError_t launch_select(const float *logits, int T, int E, int K, int32_t *sel_idx,
                           float *sel_w, cudaStream_t stream);
 // Tensor-core tile layout computed by the dispatch kernel (bn = 0: none).
@@ -139,6 +135,26 @@ constexpr int kSelectDispatchMaxTokens = 8;
 cudaError_t launch_select_dispatch(const float *logits, int T, int E, int K, int32_t *sel_idx, float *sel_w,
                                    int32_t *offsets, int32_t *perm, int32_t *slot_pos, int32_t *act_list,
                                    int32_t *meta, cudaStream_t stream, const DispatchPlan *plan = nullptr);
+// Top-k selection and dispatch run by the shared-memory router's last CTA
+// (decode batches, T <= kSelectDispatchMaxTokens, one device): every CTA
+// counts itself in *count after writing its logits, and the one that brings
+// it to the grid size resets it to 0 and does what launch_select_dispatch
+// does, reading the logits through L2.  One launch fewer again.
+struct RouterDispatch {
+  int32_t *sel_idx = nullptr;
+  float *sel_w = nullptr;
+  int32_t *offsets = nullptr, *perm = nullptr, *slot_pos = nullptr, *act_list = nullptr, *meta = nullptr;
+  DispatchPlan plan;
+  int topk = 0;
+  unsigned *count = nullptr;  // zero between launches
+};
+// *dispatch_done (optional) tells whether the launch also selected and
+// dispatched (only the shared-memory router can).
+cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
+                          float *logits, int portable_lanes, cudaStream_t stream,
+                          const RouterSplit *split = nullptr, bool *split_done = nullptr,
+                          const RouterNorm *norm = nullptr, int *launches = nullptr,
+                          const RouterDispatch *dispatch = nullptr, bool *dispatch_done = nullptr);
 // Expert-parallel helpers: gather the send rows (token of slot perm[p], local
 // expert id sel_idx % experts_per_rank) for the meta[1] dispatched slots;
 // per-rank row counts from the rank offsets; fill a float array.

@@ -197,6 +197,16 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
                : "memory");
 }
 
+constexpr int kRouterSmemDispatchMax = 180 * 1024;  // leaves room for dispatch_cta's static tables
+
+template <bool kCG>
+__device__ __forceinline__ void dispatch_cta(int32_t *sel_idx, float *sel_w, int S, int E,
+                                             int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
+                                             int32_t *__restrict__ slot_pos, int32_t *__restrict__ act_list,
+                                             int32_t *__restrict__ meta, const DispatchPlan &plan, int key_div,
+                                             const float *__restrict__ logits, int T, int topk);
+
+template <bool DISPATCH>
 __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W,
                                                      const float *__restrict__ x,
                                                      const float *__restrict__ bias, int T, int H,
@@ -204,7 +214,7 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
                                                      float *__restrict__ logits, __half *__restrict__ xq,
                                                      int32_t *__restrict__ xe, int KP,
                                                      const float *__restrict__ norm_w, float eps,
-                                                     float *__restrict__ normed) {
+                                                     float *__restrict__ normed, RouterDispatch rd) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 router_smem[];
@@ -319,6 +329,23 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
       if (lane == 0 && mb + m < ne) logits[(size_t)(t0 + j) * E + e0 + mb + m] = r + (bias ? bias[e0 + mb + m] : 0.0f);
     }
   }
+  if constexpr (DISPATCH) {
+    // the last CTA to finish selects and dispatches: this CTA's logits are
+    // made visible device-wide before it counts itself
+    __shared__ bool s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(rd.count, 1u);
+      s_last = prev == gridDim.x * gridDim.y - 1;
+      if (s_last) atomicExch(rd.count, 0u);  // every other CTA has counted itself
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    dispatch_cta<true>(rd.sel_idx, rd.sel_w, T * rd.topk, E, rd.offsets, rd.perm, rd.slot_pos, rd.act_list,
+                       rd.meta, rd.plan, 1, logits, T, rd.topk);
+  }
 }
 
 // Router for hidden % 32 != 0: the portable simd.Float32s order with `lanes`
@@ -376,16 +403,15 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
   return v;
 }
 
-__global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_w, int S, int E,
-                                                   int32_t *__restrict__ offsets,
-                                                   int32_t *__restrict__ perm,
-                                                   int32_t *__restrict__ slot_pos,
-                                                   int32_t *__restrict__ act_list,
-                                                   int32_t *__restrict__ meta, DispatchPlan plan,
-                                                   int key_div, const float *__restrict__ logits, int T,
-                                                   int topk) {
-  pdl_wait();
-  pdl_trigger();
+// The whole dispatch, run by one CTA of any size up to 1024 threads (the
+// dispatch kernel's, or the router's last CTA).  kCG: the logits were written
+// by other CTAs of the running kernel and are read through L2 only.
+template <bool kCG>
+__device__ __forceinline__ void dispatch_cta(int32_t *sel_idx, float *sel_w, int S, int E,
+                                             int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
+                                             int32_t *__restrict__ slot_pos, int32_t *__restrict__ act_list,
+                                             int32_t *__restrict__ meta, const DispatchPlan &plan, int key_div,
+                                             const float *__restrict__ logits, int T, int topk) {
   constexpr int kScanWarps = kDispatchMaxExperts / 32;
   constexpr int kVals = 5;  // tokens, active flag, slot rows, gate/up tiles, down tiles
   __shared__ int s_cnt[kDispatchMaxExperts];
@@ -400,7 +426,7 @@ __global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_
     // the later kernels, and __syncthreads makes them visible to this block.
     // sel_idx / sel_w are plain pointers here: no read-only cache path.
     for (int t = warp; t < T; t += (int)(blockDim.x >> 5))
-      select_token(logits, t, E, topk, lane, sel_idx, sel_w);
+      select_token<kCG>(logits, t, E, topk, lane, sel_idx, sel_w);
     __syncthreads();
   }
   for (int e = tid; e < E; e += blockDim.x) {
@@ -505,6 +531,19 @@ __global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_
     }
     __syncthreads();
   }
+}
+
+__global__ void __launch_bounds__(1024) k_dispatch(int32_t *sel_idx, float *sel_w, int S, int E,
+                                                   int32_t *__restrict__ offsets,
+                                                   int32_t *__restrict__ perm,
+                                                   int32_t *__restrict__ slot_pos,
+                                                   int32_t *__restrict__ act_list,
+                                                   int32_t *__restrict__ meta, DispatchPlan plan,
+                                                   int key_div, const float *__restrict__ logits, int T,
+                                                   int topk) {
+  pdl_wait();
+  pdl_trigger();
+  dispatch_cta<false>(sel_idx, sel_w, S, E, offsets, perm, slot_pos, act_list, meta, plan, key_div, logits, T, topk);
 }
 
 // ---------------------------------------------------------------------------
@@ -1002,8 +1041,10 @@ cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
 
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream, const RouterSplit *split,
-                          bool *split_done, const RouterNorm *norm, int *launches) {
+                          bool *split_done, const RouterNorm *norm, int *launches, const RouterDispatch *dispatch,
+                          bool *dispatch_done) {
   if (split_done) *split_done = false;
+  if (dispatch_done) *dispatch_done = false;
   if (launches) *launches = 1;
   if (T <= 0) return cudaSuccess;
   // the normalisation is folded into k_router_smem's prologue when that kernel
@@ -1028,21 +1069,36 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
   int EG = 1;
   while (EG < 8 && (int64_t)(E / (EG * 2)) * n_tg >= 120) EG *= 2;
   auto bytes = [&](int eg, int tg) { return (int64_t)(eg + tg) * H * (int64_t)sizeof(float); };
-  while (EG > 1 && bytes(EG, TG) > kRouterSmemMax) EG /= 2;
-  while (TG > 1 && bytes(EG, TG) > kRouterSmemMax) TG /= 2;
+  const bool with_dispatch = dispatch && dispatch->count && T <= kSelectDispatchMaxTokens &&
+                             E <= kDispatchMaxExperts && dispatch->topk >= 1 && dispatch->topk <= E &&
+                             dispatch->topk <= kSelectMaxK;
+  const int64_t cap = with_dispatch ? kRouterSmemDispatchMax : kRouterSmemMax;
+  while (EG > 1 && bytes(EG, TG) > cap) EG /= 2;
+  while (TG > 1 && bytes(EG, TG) > cap) TG /= 2;
   // Beyond 64 tokens every CTA would restage the same rows many times over;
   // the register-blocked kernel reads them through L1/L2 instead.
   const bool aligned = ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(x)) & 15) == 0;
-  if (T <= 64 && aligned && bytes(EG, TG) <= kRouterSmemMax) {
-    cudaError_t e = opt_in_smem(k_router_smem, kRouterSmemMax);
-    if (e != cudaSuccess) return e;
+  if (T <= 64 && aligned && bytes(EG, TG) <= cap) {
     const bool do_split = split && split->xq && (E + EG - 1) / EG > 0;
     if (split_done) *split_done = do_split;
-    return launch_pdl(k_router_smem, dim3((E + EG - 1) / EG, (T + TG - 1) / TG), dim3(256), (size_t)bytes(EG, TG),
-                      stream, W, x, bias, T, H, E, EG, TG, logits, do_split ? split->xq : (__half *)nullptr,
-                      do_split ? split->xe : (int32_t *)nullptr, do_split ? split->kp : 0,
-                      norm ? norm->w : (const float *)nullptr, norm ? norm->eps : 0.0f,
-                      norm ? norm->out : (float *)nullptr);
+    const dim3 grid((E + EG - 1) / EG, (T + TG - 1) / TG);
+    __half *sx = do_split ? split->xq : (__half *)nullptr;
+    int32_t *se = do_split ? split->xe : (int32_t *)nullptr;
+    const int skp = do_split ? split->kp : 0;
+    const float *nw = norm ? norm->w : (const float *)nullptr;
+    float *nout = norm ? norm->out : (float *)nullptr;
+    const float neps = norm ? norm->eps : 0.0f;
+    if (with_dispatch) {
+      cudaError_t e = opt_in_smem(k_router_smem<true>, kRouterSmemDispatchMax);
+      if (e != cudaSuccess) return e;
+      if (dispatch_done) *dispatch_done = true;
+      return launch_pdl(k_router_smem<true>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E,
+                        EG, TG, logits, sx, se, skp, nw, neps, nout, *dispatch);
+    }
+    cudaError_t e = opt_in_smem(k_router_smem<false>, kRouterSmemMax);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_router_smem<false>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E, EG,
+                      TG, logits, sx, se, skp, nw, neps, nout, RouterDispatch{});
   } else {
     cudaError_t e = separate_norm();
     if (e != cudaSuccess) return e;

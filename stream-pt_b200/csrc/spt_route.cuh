@@ -45,6 +45,9 @@ __device__ __forceinline__ float router_dot(const float *w, const float *x, int 
 // logit among experts not yet chosen (lowest index wins ties, NaN and -Inf
 // never win); no candidate gives (index = pass, value 0), and that index
 // counts as chosen for the later passes.
+// kCG: read the logits through L2 only (ld.global.cg), for logits written by
+// other CTAs of the same kernel (the router's last CTA selects).
+template <bool kCG = false>
 __device__ __forceinline__ void select_token(const float *__restrict__ logits, int t, int E, int K, int lane,
                                              int32_t *__restrict__ sel_idx, float *__restrict__ sel_w) {
   constexpr int kPer = kDispatchMaxExperts / 32;
@@ -52,7 +55,8 @@ __device__ __forceinline__ void select_token(const float *__restrict__ logits, i
   const bool in_regs = E <= 32 * kPer;  // else every pass reads the logits again
   float lv[kPer];
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) lv[i] = (in_regs && lane + 32 * i < E) ? lg[lane + 32 * i] : 0.0f;
+  for (int i = 0; i < kPer; ++i)
+    lv[i] = (in_regs && lane + 32 * i < E) ? (kCG ? __ldcg(lg + lane + 32 * i) : lg[lane + 32 * i]) : 0.0f;
   uint32_t taken = 0;  // bit i: expert lane + 32i already chosen
   int chosen[kSelectMaxK];
   float val[kSelectMaxK];
@@ -72,7 +76,7 @@ __device__ __forceinline__ void select_token(const float *__restrict__ logits, i
       for (int e = lane; e < E; e += 32) {
         bool already = false;
         for (int p = 0; p < r; ++p) already |= (chosen[p] == e);
-        const float l = lg[e];
+        const float l = kCG ? __ldcg(lg + e) : lg[e];
         if (!already && l > v) {
           v = l;
           best = e;

@@ -61,10 +61,10 @@ def test_gemv16_block_matches_oracle(ctx, layer, T):
         r = ctx.last_routing(T, 128, 4)
     finally:
         ctx.set_path(spt.PATH_AUTO)
-    # router (with the f16 split of x), [select], dispatch, gate/up, down
-    # [+ combine]: up to 8 tokens select inside dispatch, up to 64 slots
-    # combine inside the down launch
-    assert kernels == 6 - (T <= 8) - (T * 4 <= 64)
+    # router (with the f16 split of x), [select], [dispatch], gate/up, down
+    # [+ combine]: up to 8 tokens the router's last CTA selects and
+    # dispatches, up to 64 slots combine inside the down launch
+    assert kernels == 6 - 2 * (T <= 8) - (T * 4 <= 64)
     want = oracle.forward_moe_batch(dense, x, T, workers=8, want_internals=True)
     assert np.array_equal(r["sel_idx"], want["sel_idx"])
     assert refdata.bits_equal(r["sel_w"], want["sel_w"]).all()
@@ -80,11 +80,11 @@ def test_gemv16_is_the_auto_decode_path(ctx, layer):
     ctx.set_path(spt.PATH_AUTO)
     x = spt.synth_normal_host(3, 2100, 4 * 2880)
     got = ctx.forward_moe_batch(arena, x, 4)
-    assert ctx.kernels_per_forward() == 4  # router, dispatch, gate/up, down (+ combine)
+    assert ctx.kernels_per_forward() == 3  # router (+ select, dispatch), gate/up, down (+ combine)
     ctx.set_option(spt.OPT_GEMV16_SLOTS, 0)
     try:
         mma = ctx.forward_moe_batch(arena, x, 4)
-        assert ctx.kernels_per_forward() == 7
+        assert ctx.kernels_per_forward() == 6
     finally:
         ctx.set_option(spt.OPT_GEMV16_SLOTS, 16)
     want = oracle.forward_moe_batch(dense, x, 4, workers=8)
@@ -152,7 +152,7 @@ def test_gemv16_refuses_scales_outside_f16(ctx):
             ctx.forward_moe_batch(arena, x, 2)
         ctx.set_path(spt.PATH_AUTO)
         ctx.forward_moe_batch(arena, x, 2)
-        assert ctx.kernels_per_forward() == 7
+        assert ctx.kernels_per_forward() == 6
     finally:
         ctx.set_path(spt.PATH_AUTO)
         arena.close()

@@ -51,8 +51,8 @@ def test_mma_block_matches_oracle(ctx, mma_layer, T):
     ctx.set_path(spt.PATH_MMA)
     got = ctx.forward_moe_batch(arena, x, T)
     # router, select, dispatch, 2x quantize, 2x GEMM, combine; up to 8 tokens
-    # the selection runs inside the dispatch kernel
-    assert ctx.kernels_per_forward() == (7 if T <= 8 else 8)
+    # the router's last CTA selects and dispatches
+    assert ctx.kernels_per_forward() == (6 if T <= 8 else 8)
     r = ctx.last_routing(T, 128, 4)
     sample = list(range(min(T, 8)))
     want = oracle.forward_moe_batch(dense, x[: len(sample) * 2880], len(sample), workers=8,

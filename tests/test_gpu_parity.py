@@ -58,28 +58,32 @@ def test_block_bit_exact_sweep(ctx, experts, bias_type):
 
 
 def test_fused_selection_matches_separate(ctx):
-    """Up to 8 tokens the top-k selection runs inside the dispatch kernel;
-    the context option SPT_OPT_FUSED_SELECT = 0 keeps the separate selection
-    launch.  Both give the
-    same output bits and routing, over every router mode of the sweep."""
+    """Up to 8 tokens the top-k selection and the dispatch run in the
+    router's last CTA (SPT_OPT_FUSED_SELECT = 1, the default: two launches
+    fewer), or the selection inside the dispatch kernel (= 2: one fewer);
+    = 0 keeps three launches.  All give the same output bits and routing,
+    over every router mode of the sweep."""
     for experts, top_k in ((7, 2), (33, 4), (128, 32)):
         for mode in refdata.ROUTER_MODES:
             fx = refdata.moe_batch_fixture(96, 64, experts, top_k, 1, mode)
             for batch in (1, 5, 8):
                 x = refdata.moe_batch_x(batch, 96, mode)
                 got = {}
-                for fused in ("1", "0"):
-                    ctx.set_option(spt.OPT_FUSED_SELECT, int(fused))
+                for fused in (1, 2, 0):
+                    ctx.set_option(spt.OPT_FUSED_SELECT, fused)
                     out, r, _ = _run_block(ctx, fx, x, batch)
                     got[fused] = (out, r, ctx.kernels_per_forward())
                 ctx.set_option(spt.OPT_FUSED_SELECT, 1)
                 tag = (experts, top_k, mode, batch)
-                (a, ra, ka), (b, rb, kb) = got["1"], got["0"]
-                assert bits_equal(a, b).all(), tag
-                assert np.array_equal(ra["sel_idx"], rb["sel_idx"]), tag
-                assert bits_equal(ra["sel_w"], rb["sel_w"]).all(), tag
-                assert np.array_equal(ra["perm"], rb["perm"]), tag
-                assert ka == kb - 1, tag
+                b, rb, kb = got[0]
+                for fused in (1, 2):
+                    a, ra, ka = got[fused]
+                    assert bits_equal(a, b).all(), tag
+                    assert np.array_equal(ra["sel_idx"], rb["sel_idx"]), tag
+                    assert bits_equal(ra["sel_w"], rb["sel_w"]).all(), tag
+                    assert np.array_equal(ra["perm"], rb["perm"]), tag
+                    assert np.array_equal(ra["counts"], rb["counts"]), tag
+                    assert ka == kb - (3 - fused), (tag, fused, ka, kb)
 
 
 @pytest.mark.parametrize("mode", ["ties", "normal", "underflow"])
