@@ -120,8 +120,11 @@ def test_cancel_flag(ctx):
 # ---- stages -----------------------------------------------------------------
 
 @pytest.mark.parametrize("hidden", [3, 31, 32, 96, 2880])
-@pytest.mark.parametrize("batch", [1, 2, 17])
+@pytest.mark.parametrize("batch", [1, 2, 17, 100])
 def test_router_stage(ctx, hidden, batch):
+    """Up to 64 rows the router stages whole rows in shared memory
+    (k_router_smem), beyond that it runs register-blocked from L2
+    (k_router); the 64-chain order is the same."""
     experts = 5
     bias = np.array([.125, -.25, .5, -1, 2], np.float32)
     n = experts * hidden
