@@ -83,6 +83,7 @@ struct spt_context {
   size_t hx_bytes = 0, hout_bytes = 0;
   // tuning options (spt_context_set_option), seeded from the environment once
   int opt_tile_tokens = 0;      // tcgen05 token-tile width (0: from the batch)
+  int opt_router_bulk = 1;      // the shared-memory router stages rows with bulk copies (SPT_ROUTER_BULK)
   int opt_fused_select = 1;     // T <= kSelectDispatchMaxTokens: 1 top-k + dispatch in the router's last CTA
                                 // (else in the dispatch kernel), 2 in the dispatch kernel, 0 separate
   int opt_prefetch = 0;         // tcgen05 weight tiles prefetched into L2 ahead
@@ -664,7 +665,7 @@ spt_status check_device_error(spt_context *ctx) {
   if (e != 0) {
     cudaMemset(ctx->dev_err.p, 0, sizeof e);
     return fail(ctx, SPT_ERR_TIMEOUT, "%s: bounded wait %d gave up",
-                e >= 20 ? "expert-parallel peer exchange" : "tensor-core GEMM", e);
+                e >= 20 ? "expert-parallel peer exchange" : e == 9 ? "router" : "tensor-core GEMM", e);
   }
   return SPT_OK;
 }
@@ -936,8 +937,13 @@ spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_confi
   const int H = (int)c.hidden_dim, E = (int)c.num_experts, K = (int)c.num_experts_used;
   cudaStream_t s = ctx->stream;
   SPT_MARK(0);
+  if (!ctx->dev_err.p) {  // the router's bounded wait reports here
+    SPT_CUDA(ctx, ctx->dev_err.ensure(sizeof(int32_t)));
+    SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
+  }
   SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s, split,
-                              split_done, norm, router_launches, dispatch, dispatch_done));
+                              split_done, norm, router_launches, dispatch, dispatch_done,
+                              ctx->opt_router_bulk ? ctx->dev_err.as<int32_t>() : nullptr));
   SPT_MARK(1);
   if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
@@ -1046,7 +1052,8 @@ std::vector<const void *> call_buffers(const spt_context *ctx) {
 
 std::vector<int64_t> call_options(const spt_context *ctx) {
   return {ctx->path, ctx->opt_tile_tokens, ctx->opt_fused_select, ctx->opt_prefetch, ctx->opt_gemv16_slots,
-          ctx->opt_wait_shift, ctx->opt_fault_stage, ctx->opt_prefill_fp8, (int64_t)(uintptr_t)ctx->stream};
+          ctx->opt_wait_shift, ctx->opt_fault_stage, ctx->opt_prefill_fp8, ctx->opt_router_bulk,
+          (int64_t)(uintptr_t)ctx->stream};
 }
 
 // Capture the block on the context's device buffers into a graph (after a
@@ -1185,6 +1192,7 @@ void seed_options(spt_context *ctx) {
   env("SPT_MMA_BN", &ctx->opt_tile_tokens, 0, 128);
   if (ctx->opt_tile_tokens != 8 && ctx->opt_tile_tokens != 16 && ctx->opt_tile_tokens != 128) ctx->opt_tile_tokens = 0;
   env("SPT_FUSED_SELECT", &ctx->opt_fused_select, 0, 2);
+  env("SPT_ROUTER_BULK", &ctx->opt_router_bulk, 0, 1);
   env("SPT_MMA_PREFETCH", &ctx->opt_prefetch, 0, 64);
   env("SPT_GEMV16_SLOTS", &ctx->opt_gemv16_slots, 0, 1 << 20);
   env("SPT_HOST_GRAPHS", &ctx->opt_host_graphs, 0, 1);

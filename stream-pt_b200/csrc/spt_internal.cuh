@@ -149,12 +149,16 @@ struct RouterDispatch {
   unsigned *count = nullptr;  // zero between launches
 };
 // *dispatch_done (optional) tells whether the launch also selected and
-// dispatched (only the shared-memory router can).
+// dispatched (only the shared-memory router can).  With err (the context's
+// device error flag) the shared-memory router stages its rows with bulk
+// copies on an mbarrier whose bounded wait records code 9 there; without it,
+// with cp.async.
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream,
                           const RouterSplit *split = nullptr, bool *split_done = nullptr,
                           const RouterNorm *norm = nullptr, int *launches = nullptr,
-                          const RouterDispatch *dispatch = nullptr, bool *dispatch_done = nullptr);
+                          const RouterDispatch *dispatch = nullptr, bool *dispatch_done = nullptr,
+                          int32_t *err = nullptr);
 // Expert-parallel helpers: gather the send rows (token of slot perm[p], local
 // expert id sel_idx % experts_per_rank) for the meta[1] dispatched slots;
 // per-rank row counts from the rank offsets; fill a float array.

@@ -22,6 +22,7 @@
 #include "spt_device.cuh"
 #include "spt_internal.cuh"
 #include "spt_philox.h"
+#include "spt_ptx.cuh"
 #include "spt_route.cuh"
 
 namespace spt {
@@ -190,12 +191,6 @@ __global__ void __launch_bounds__(32) k_router(const float *__restrict__ W,
 // the same shuffle tree reduces them (vector_amd64.go:28-56).
 constexpr int kRouterSmemMax = 200 * 1024;
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-               "l"(gmem)
-               : "memory");
-}
 
 constexpr int kRouterSmemDispatchMax = 180 * 1024;  // leaves room for dispatch_cta's static tables
 
@@ -214,23 +209,52 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
                                                      float *__restrict__ logits, __half *__restrict__ xq,
                                                      int32_t *__restrict__ xe, int KP,
                                                      const float *__restrict__ norm_w, float eps,
-                                                     float *__restrict__ normed, RouterDispatch rd) {
-  pdl_wait();
-  pdl_trigger();
+                                                     float *__restrict__ normed, RouterDispatch rd,
+                                                     int32_t *err) {
   extern __shared__ float4 router_smem[];
   float *ws = reinterpret_cast<float *>(router_smem);  // [EG][H]
   float *xs = ws + (size_t)EG * H;                     // [TG][H]
+  __shared__ uint64_t s_rows_full;
   const int e0 = blockIdx.x * EG, t0 = blockIdx.y * TG;
   const int ne = min(EG, E - e0), nt = min(TG, T - t0);
-  const int q = H / 4;  // 16-byte pieces per row
-  for (int i = threadIdx.x; i < (ne + nt) * q; i += blockDim.x) {
-    const int r = i / q, c = i - r * q;
-    const float *src = r < ne ? W + (size_t)(e0 + r) * H : x + (size_t)(t0 + r - ne) * H;
-    float *dst = r < ne ? ws + (size_t)r * H : xs + (size_t)(r - ne) * H;
-    cp_async16(dst + 4 * c, src + 4 * c);
+  if (err) {
+    // every row is one bulk copy on an mbarrier (rows are 16-byte multiples):
+    // the expert rows do not depend on earlier kernels and go out before the
+    // wait for the predecessor grid, the token rows after it
+    if (threadIdx.x == 0) {
+      mbar_init(&s_rows_full, 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      mbar_expect_tx(&s_rows_full, (uint32_t)((ne + nt) * H * (int)sizeof(float)));
+      for (int r = 0; r < ne; ++r)
+        bulk_load(ws + (size_t)r * H, W + (size_t)(e0 + r) * H, (uint32_t)(H * sizeof(float)), &s_rows_full);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0)
+      for (int r = 0; r < nt; ++r)
+        bulk_load(xs + (size_t)r * H, x + (size_t)(t0 + r) * H, (uint32_t)(H * sizeof(float)), &s_rows_full);
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+    // on a timeout (here or recorded by another kernel) the whole CTA leaves
+    // -- the host reports SPT_ERR_TIMEOUT -- once thread 0's copies have
+    // landed or a second bound has passed
+    const bool ok = mbar_wait(&s_rows_full, 0, err, 9);
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) mbar_wait_own(&s_rows_full, 0);
+      return;
+    }
+  } else {
+    pdl_wait();
+    pdl_trigger();
+    const int q = H / 4;  // 16-byte pieces per row
+    for (int i = threadIdx.x; i < (ne + nt) * q; i += blockDim.x) {
+      const int r = i / q, c = i - r * q;
+      const float *src = r < ne ? W + (size_t)(e0 + r) * H : x + (size_t)(t0 + r - ne) * H;
+      float *dst = r < ne ? ws + (size_t)r * H : xs + (size_t)(r - ne) * H;
+      cp_async16(dst + 4 * c, src + 4 * c);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (norm_w) {
     // normBatch (forward/layer_batch.go:139-195) on the staged token rows, in
@@ -241,11 +265,10 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
     for (int j = warp; j < nt; j += blockDim.x >> 5) {
       const float *xr = xs + (size_t)j * H;
       float acc = 0.0f;
-      if (lane < 8)
-        for (int o = 0; o < H; o += 8) {
-          const float v = (o + lane < H) ? xr[o + lane] : 0.0f;
-          acc = fmaf(v, v, acc);
-        }
+      if (lane < 8) {  // H % 32 == 0 here: no zero-padded tail
+#pragma unroll 8
+        for (int o = lane; o < H; o += 8) acc = fmaf(xr[o], xr[o], acc);
+      }
       float sum = 0.0f;
       for (int l = 0; l < 8; ++l) sum = __fadd_rn(sum, __shfl_sync(kFull, acc, l));
       if (lane == 0) s_f[j] = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(__fdiv_rn(sum, (float)H), eps)));
@@ -1042,7 +1065,7 @@ cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream, const RouterSplit *split,
                           bool *split_done, const RouterNorm *norm, int *launches, const RouterDispatch *dispatch,
-                          bool *dispatch_done) {
+                          bool *dispatch_done, int32_t *err) {
   if (split_done) *split_done = false;
   if (dispatch_done) *dispatch_done = false;
   if (launches) *launches = 1;
@@ -1093,12 +1116,12 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
       if (e != cudaSuccess) return e;
       if (dispatch_done) *dispatch_done = true;
       return launch_pdl(k_router_smem<true>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E,
-                        EG, TG, logits, sx, se, skp, nw, neps, nout, *dispatch);
+                        EG, TG, logits, sx, se, skp, nw, neps, nout, *dispatch, err);
     }
     cudaError_t e = opt_in_smem(k_router_smem<false>, kRouterSmemMax);
     if (e != cudaSuccess) return e;
     return launch_pdl(k_router_smem<false>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E, EG,
-                      TG, logits, sx, se, skp, nw, neps, nout, RouterDispatch{});
+                      TG, logits, sx, se, skp, nw, neps, nout, RouterDispatch{}, err);
   } else {
     cudaError_t e = separate_norm();
     if (e != cudaSuccess) return e;
