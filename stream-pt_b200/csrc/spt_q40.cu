@@ -28,6 +28,8 @@
 // micro-tile), weights decoded once per CTA into shared memory and reused
 // by every item of the tile, and the 8 chains of an output meet in shared
 // memory for the quantSumAVX2 tree.
+#include <algorithm>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -385,15 +387,18 @@ __global__ void __launch_bounds__(kQ40BatchThreads, TM * TN <= 16 ? 3 : 2)
 }
 
 // Relative time of one tile shape: the busiest SM's tiles x tile work / the
-// share of issue slots its inner loop gives to FMAs (TM*TN FMAs per TM/4 +
-// ceil(TN/4) shared loads and ~2 loop instructions), 1.5x when an SM would
-// hold a single tile (too few warps to hide latency).
+// share of the FMA pipe the tile can keep busy.  A lane's k step is TM*TN
+// FMAs (TM*TN/4 cycles of the SM's FMA pipe per warp) against TM + TN
+// shared-memory wavefronts (128-bit loads are served a quarter-warp at a
+// time, so the w and x vectors cost TM and TN wavefronts), and the SM serves
+// one wavefront per cycle; 1.5x when an SM would hold a single tile (too few
+// warps to hide latency).
 template <int TM, int TN>
 double batch_tile_cost(int64_t rows, int64_t batch, int sm_count) {
   constexpr int BM = 8 * TM, BN = 4 * TN;
   const int64_t tiles = ((rows + BM - 1) / BM) * ((batch + BN - 1) / BN);
   const int64_t per_sm = (tiles + sm_count - 1) / sm_count;
-  const double eff = (double)(TM * TN) / (TM * TN + TM / 4 + (TN + 3) / 4 + 2);
+  const double eff = std::min(1.0, (double)(TM * TN) / (4.0 * (TM + TN)));
   return (double)per_sm * BM * BN / eff * (per_sm < 2 ? 1.5 : 1.0);
 }
 
