@@ -228,7 +228,9 @@ spt_status spt_context_set_path(spt_context *ctx, int path);
  *                         second) and the call returns SPT_ERR_TIMEOUT
  *   SPT_OPT_FAULT_STAGE   test hook, -1 off: the tcgen05 producer of CTA 0
  *                         skips this pipeline stage, so the MMA issuer's wait
- *                         for it runs out (the failure path without a fault)
+ *                         for it runs out (the failure path without a fault);
+ *                         1000: the shared-memory router's CTA 0 leaves out
+ *                         one row's copy, so its wait runs out
  *   SPT_OPT_HOST_GRAPHS   1 (default): spt_forward_moe_batch / spt_forward_moe
  *                         capture the block's kernels into a CUDA graph on the
  *                         second call with the same arena, layer, batch and

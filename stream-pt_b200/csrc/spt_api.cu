@@ -658,6 +658,11 @@ spt_status forward_mma(spt_context *ctx, const LayerDev &L, const spt_moe_config
   return SPT_OK;
 }
 
+// What gave up, from the code a bounded device wait recorded.
+const char *device_wait_name(int32_t code) {
+  return code >= 20 ? "expert-parallel peer exchange" : code == 9 ? "router" : "tensor-core GEMM";
+}
+
 spt_status check_device_error(spt_context *ctx) {
   if (!ctx->dev_err.p) return SPT_OK;
   int32_t e = 0;
@@ -665,7 +670,7 @@ spt_status check_device_error(spt_context *ctx) {
   if (e != 0) {
     cudaMemset(ctx->dev_err.p, 0, sizeof e);
     return fail(ctx, SPT_ERR_TIMEOUT, "%s: bounded wait %d gave up",
-                e >= 20 ? "expert-parallel peer exchange" : e == 9 ? "router" : "tensor-core GEMM", e);
+                device_wait_name(e), e);
   }
   return SPT_OK;
 }
@@ -943,7 +948,8 @@ spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_confi
   }
   SPT_CUDA(ctx, launch_router(L.router, x, L.router_bias, (int)T, H, E, ctx->logits.as<float>(), 8, s, split,
                               split_done, norm, router_launches, dispatch, dispatch_done,
-                              ctx->opt_router_bulk ? ctx->dev_err.as<int32_t>() : nullptr));
+                              ctx->opt_router_bulk ? ctx->dev_err.as<int32_t>() : nullptr, ctx->opt_wait_shift,
+                              ctx->opt_fault_stage));
   SPT_MARK(1);
   if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
@@ -1174,7 +1180,7 @@ spt_status forward_host(spt_context *ctx, spt_arena *arena, int64_t layer, const
     SPT_CUDA(ctx, cudaMemsetAsync(ctx->dev_err.p, 0, sizeof(int32_t), ctx->stream));
     SPT_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
     return fail(ctx, SPT_ERR_TIMEOUT, "%s: bounded wait %d gave up",
-                e >= 20 ? "expert-parallel peer exchange" : "tensor-core GEMM", e);
+                device_wait_name(e), e);
   }
   if (canceled(cancel)) return fail(ctx, SPT_ERR_CANCELED, "context canceled");
   return SPT_OK;

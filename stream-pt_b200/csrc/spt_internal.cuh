@@ -158,7 +158,10 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
                           const RouterSplit *split = nullptr, bool *split_done = nullptr,
                           const RouterNorm *norm = nullptr, int *launches = nullptr,
                           const RouterDispatch *dispatch = nullptr, bool *dispatch_done = nullptr,
-                          int32_t *err = nullptr);
+                          int32_t *err = nullptr, int wait_shift = 31, int fault_stage = -1);
+// SPT_OPT_FAULT_STAGE value that makes the shared-memory router's bounded
+// wait run out (test hook; the tcgen05 stages are small numbers).
+constexpr int kRouterFault = 1000;
 // Expert-parallel helpers: gather the send rows (token of slot perm[p], local
 // expert id sel_idx % experts_per_rank) for the meta[1] dispatched slots;
 // per-rank row counts from the rank offsets; fill a float array.

@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
                                                      int32_t *__restrict__ xe, int KP,
                                                      const float *__restrict__ norm_w, float eps,
                                                      float *__restrict__ normed, RouterDispatch rd,
-                                                     int32_t *err) {
+                                                     int32_t *err, int wait_shift, int fault) {
   extern __shared__ float4 router_smem[];
   float *ws = reinterpret_cast<float *>(router_smem);  // [EG][H]
   float *xs = ws + (size_t)EG * H;                     // [TG][H]
@@ -225,7 +225,10 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
       mbar_init(&s_rows_full, 1);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
       mbar_expect_tx(&s_rows_full, (uint32_t)((ne + nt) * H * (int)sizeof(float)));
-      for (int r = 0; r < ne; ++r)
+      // test hook (kRouterFault): CTA 0 leaves out its first row's copy, so
+      // the wait below runs out -- the failure path without a fault
+      const int r_first = (fault && blockIdx.x == 0 && blockIdx.y == 0) ? 1 : 0;
+      for (int r = r_first; r < ne; ++r)
         bulk_load(ws + (size_t)r * H, W + (size_t)(e0 + r) * H, (uint32_t)(H * sizeof(float)), &s_rows_full);
     }
     pdl_wait();
@@ -237,9 +240,14 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
     // on a timeout (here or recorded by another kernel) the whole CTA leaves
     // -- the host reports SPT_ERR_TIMEOUT -- once thread 0's copies have
     // landed or a second bound has passed
-    const bool ok = mbar_wait(&s_rows_full, 0, err, 9);
+    const bool ok = mbar_wait(&s_rows_full, 0, err, 9, wait_shift);
     if (__syncthreads_or(!ok)) {
-      if (threadIdx.x == 0) mbar_wait_own(&s_rows_full, 0);
+      if (threadIdx.x == 0) {
+        mbar_wait_own(&s_rows_full, 0, wait_shift);
+        if constexpr (DISPATCH) {  // still counted, so the counter is 0 again for the next launch
+          if (atomicAdd(rd.count, 1u) == gridDim.x * gridDim.y - 1) atomicExch(rd.count, 0u);
+        }
+      }
       return;
     }
   } else {
@@ -1065,7 +1073,8 @@ cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream, const RouterSplit *split,
                           bool *split_done, const RouterNorm *norm, int *launches, const RouterDispatch *dispatch,
-                          bool *dispatch_done, int32_t *err) {
+                          bool *dispatch_done, int32_t *err, int wait_shift, int fault_stage) {
+  const int fault = fault_stage == kRouterFault ? 1 : 0;
   if (split_done) *split_done = false;
   if (dispatch_done) *dispatch_done = false;
   if (launches) *launches = 1;
@@ -1116,12 +1125,12 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
       if (e != cudaSuccess) return e;
       if (dispatch_done) *dispatch_done = true;
       return launch_pdl(k_router_smem<true>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E,
-                        EG, TG, logits, sx, se, skp, nw, neps, nout, *dispatch, err);
+                        EG, TG, logits, sx, se, skp, nw, neps, nout, *dispatch, err, wait_shift, fault);
     }
     cudaError_t e = opt_in_smem(k_router_smem<false>, kRouterSmemMax);
     if (e != cudaSuccess) return e;
     return launch_pdl(k_router_smem<false>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E, EG,
-                      TG, logits, sx, se, skp, nw, neps, nout, RouterDispatch{}, err);
+                      TG, logits, sx, se, skp, nw, neps, nout, RouterDispatch{}, err, wait_shift, fault);
   } else {
     cudaError_t e = separate_norm();
     if (e != cudaSuccess) return e;

@@ -11,6 +11,10 @@ an error status instead of a hang.  These tests make such a wait run out:
   that stage gives up, the CTA waits for its own copies in flight, frees its
   tensor memory and returns, and the call reports SPT_ERR_TIMEOUT; the next
   normal call on the same context is correct;
+* a router CTA that leaves out one row's copy (SPT_OPT_FAULT_STAGE = 1000):
+  the router's wait for its rows gives up, the CTA waits for the copies it
+  did issue and leaves (still counting itself for the last-CTA selection),
+  and the call reports SPT_ERR_TIMEOUT; the next normal call is correct;
 * an expert-parallel group whose second rank never joins: the set-up wait
   gives up after SPT_EP_TIMEOUT_MS and the group is aborted (no exchange
   kernel was launched); the context keeps working.
@@ -68,6 +72,29 @@ def test_gemm_wait_gives_up_and_context_recovers(ctx, small, stage):
     ctx.set_option(spt.OPT_WAIT_LIMIT, 31)
     got = ctx.forward_moe_batch(arena, x, T)
     assert _close(got, want)
+
+
+@pytest.mark.parametrize("T", [4, 24])
+def test_router_wait_gives_up_and_context_recovers(ctx, small, T):
+    """T = 4: the router with the selection and dispatch in its last CTA;
+    T = 24: the plain shared-memory router."""
+    cfg, arena, dense = small
+    x = spt.synth_normal_host(22, 5, T * HID)
+    want = oracle.forward_moe_batch(dense, x, T)
+    ctx.set_path(spt.PATH_MMA)
+    ctx.set_option(spt.OPT_WAIT_LIMIT, 20)
+    ctx.set_option(spt.OPT_FAULT_STAGE, 1000)
+    t0 = time.perf_counter()
+    with pytest.raises(spt.SptError) as e:
+        ctx.forward_moe_batch(arena, x, T)
+    assert e.value.status == spt.ERR_TIMEOUT, e.value
+    assert "router" in str(e.value)
+    assert time.perf_counter() - t0 < 30
+    ctx.set_option(spt.OPT_FAULT_STAGE, -1)
+    ctx.set_option(spt.OPT_WAIT_LIMIT, 31)
+    for _ in range(2):  # the counter of the last-CTA selection is back at 0
+        got = ctx.forward_moe_batch(arena, x, T)
+        assert _close(got, want)
 
 
 @pytest.mark.timeout(180)
