@@ -122,6 +122,10 @@ __global__ void __launch_bounds__(kQ40Threads, 1) k_q40_gemv(const __grid_consta
           bulk_load(dst + (size_t)(p / L.cr) * L.cs, a.w + (r0 + p) * rb, bytes, &full[s]);
         }
       }
+      // if a wait gave up, copies may still be in flight: they land before
+      // the CTA leaves (bounded wait for the last phase issued on each stage)
+      for (int s = 0; s < kQ40Stages && s < it; ++s)
+        mbar_wait_own(&full[s], (uint32_t)((it - 1 - s) / kQ40Stages) & 1u);
     }
     return;
   }

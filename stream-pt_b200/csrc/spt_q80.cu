@@ -137,6 +137,10 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
           bulk_load(dst + (size_t)p * rb, a.w + (r0 + p) * rb, bytes, &full[s]);
         }
       }
+      // if a wait gave up, copies may still be in flight: they land before
+      // the CTA leaves (bounded wait for the last phase issued on each stage)
+      for (int s = 0; s < kQ80Stages && s < it; ++s)
+        mbar_wait_own(&full[s], (uint32_t)((it - 1 - s) / kQ80Stages) & 1u);
     }
   } else {
     // ---- consumers: group g takes stages it = g, g + 4, ...; each warp
