@@ -84,8 +84,9 @@ struct spt_context {
   // tuning options (spt_context_set_option), seeded from the environment once
   int opt_tile_tokens = 0;      // tcgen05 token-tile width (0: from the batch)
   int opt_router_bulk = 1;      // the shared-memory router stages rows with bulk copies (SPT_ROUTER_BULK)
-  int opt_fused_select = 1;     // T <= kSelectDispatchMaxTokens: 1 top-k + dispatch in the router's last CTA
-                                // (else in the dispatch kernel), 2 in the dispatch kernel, 0 separate
+  int opt_fused_select = 1;     // 1: top-k + dispatch in the router's last CTA (T <= kRouterDispatchMaxTokens),
+                                // else for T <= kSelectDispatchMaxTokens top-k in the dispatch kernel;
+                                // 2: top-k in the dispatch kernel (T <= 8); 0: separate launches
   int opt_prefetch = 0;         // tcgen05 weight tiles prefetched into L2 ahead
   int opt_gemv16_slots = 16;    // SPT_PATH_AUTO: decode GEMV while batch x top-k <= this
   int opt_wait_shift = 31;      // bounded device waits give up after 2^shift clock cycles
@@ -951,7 +952,8 @@ spt_status route_select(spt_context *ctx, const LayerDev &L, const spt_moe_confi
                               ctx->opt_router_bulk ? ctx->dev_err.as<int32_t>() : nullptr, ctx->opt_wait_shift,
                               ctx->opt_fault_stage));
   SPT_MARK(1);
-  if (select) SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
+  if (select && !(dispatch_done && *dispatch_done))  // else the router's last CTA selected
+    SPT_CUDA(ctx, launch_select(ctx->logits.as<float>(), (int)T, E, K, sel_idx, sel_w, s));
   SPT_MARK(2);
   return SPT_OK;
 }
@@ -995,7 +997,7 @@ spt_status forward_device(spt_context *ctx, spt_arena *arena, int64_t layer, con
   // decode batches: selection and dispatch in the router's last CTA when it
   // stages its rows (SPT_OPT_FUSED_SELECT 1), else inside the dispatch kernel
   RouterDispatch rd;
-  const bool router_dispatch = fuse && ctx->opt_fused_select == 1;
+  const bool router_dispatch = T <= kRouterDispatchMaxTokens && ctx->opt_fused_select == 1;
   if (router_dispatch) {
     if (ctx->route_count.bytes < sizeof(unsigned)) {
       SPT_CUDA(ctx, ctx->route_count.ensure(sizeof(unsigned)));

@@ -1101,7 +1101,7 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
   int EG = 1;
   while (EG < 8 && (int64_t)(E / (EG * 2)) * n_tg >= 120) EG *= 2;
   auto bytes = [&](int eg, int tg) { return (int64_t)(eg + tg) * H * (int64_t)sizeof(float); };
-  const bool with_dispatch = dispatch && dispatch->count && T <= kSelectDispatchMaxTokens &&
+  const bool with_dispatch = dispatch && dispatch->count && T <= kRouterDispatchMaxTokens &&
                              E <= kDispatchMaxExperts && dispatch->topk >= 1 && dispatch->topk <= E &&
                              dispatch->topk <= kSelectMaxK;
   const int64_t cap = with_dispatch ? kRouterSmemDispatchMax : kRouterSmemMax;

@@ -62,8 +62,8 @@ def test_gemv16_block_matches_oracle(ctx, layer, T):
     finally:
         ctx.set_path(spt.PATH_AUTO)
     # router (with the f16 split of x), [select], [dispatch], gate/up, down
-    # [+ combine]: up to 8 tokens the router's last CTA selects and
-    # dispatches, up to 64 slots combine inside the down launch
+    # [+ combine]: the router's last CTA selects and
+    # dispatches (up to 8 tokens), up to 64 slots combine inside the down launch
     assert kernels == 6 - 2 * (T <= 8) - (T * 4 <= 64)
     want = oracle.forward_moe_batch(dense, x, T, workers=8, want_internals=True)
     assert np.array_equal(r["sel_idx"], want["sel_idx"])

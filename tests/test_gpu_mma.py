@@ -50,8 +50,8 @@ def test_mma_block_matches_oracle(ctx, mma_layer, T):
     x = spt.synth_normal_host(T, 2000, T * 2880)
     ctx.set_path(spt.PATH_MMA)
     got = ctx.forward_moe_batch(arena, x, T)
-    # router, select, dispatch, 2x quantize, 2x GEMM, combine; up to 8 tokens
-    # the router's last CTA selects and dispatches
+    # router, select, dispatch, 2x quantize, 2x GEMM, combine; up to 8
+    # tokens the router's last CTA selects and dispatches
     assert ctx.kernels_per_forward() == (6 if T <= 8 else 8)
     r = ctx.last_routing(T, 128, 4)
     sample = list(range(min(T, 8)))

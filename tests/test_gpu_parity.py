@@ -62,11 +62,12 @@ def test_fused_selection_matches_separate(ctx):
     router's last CTA (SPT_OPT_FUSED_SELECT = 1, the default: two launches
     fewer), or the selection inside the dispatch kernel (= 2: one fewer);
     = 0 keeps three launches.  All give the same output bits and routing,
-    over every router mode of the sweep."""
+    over every router mode of the sweep (20 tokens: separate launches in
+    every mode)."""
     for experts, top_k in ((7, 2), (33, 4), (128, 32)):
         for mode in refdata.ROUTER_MODES:
             fx = refdata.moe_batch_fixture(96, 64, experts, top_k, 1, mode)
-            for batch in (1, 5, 8):
+            for batch in (1, 5, 8, 20):
                 x = refdata.moe_batch_x(batch, 96, mode)
                 got = {}
                 for fused in (1, 2, 0):
@@ -83,6 +84,7 @@ def test_fused_selection_matches_separate(ctx):
                     assert bits_equal(ra["sel_w"], rb["sel_w"]).all(), tag
                     assert np.array_equal(ra["perm"], rb["perm"]), tag
                     assert np.array_equal(ra["counts"], rb["counts"]), tag
+                    # the counts are those of the last call, a one-token forward
                     assert ka == kb - (3 - fused), (tag, fused, ka, kb)
 
 
