@@ -1,10 +1,11 @@
 """Writes tests/golden/go_api.json: the identifiers of the Stream-PT Go
 sources that the cgo shim (stream-pt_b200/go/moe_cuda.go) relies on, read
-from a checkout of the reference (default /root/reference, or argv[1]).
+from a checkout of the reference (argv[1], else the STREAM_PT_SOURCE
+environment variable).
 tests/test_go_shim.py checks the shim against this file, so the check runs
 where the reference is absent.
 
-    python tests/golden/make_go_api.py [path-to-Stream-PT]
+    python tests/golden/make_go_api.py path-to-Stream-PT
 """
 import json
 import os
@@ -37,7 +38,9 @@ def struct_fields(src, name):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("STREAM_PT_SOURCE", "")
+    if not root:
+        sys.exit("usage: make_go_api.py path-to-Stream-PT (or set STREAM_PT_SOURCE)")
     gomod = read(root, "go.mod")
     module = re.search(r"^module\s+(\S+)", gomod, re.M).group(1)
     mm = read(root, "ggufmap/mmap_linux.go")
