@@ -202,7 +202,7 @@ __device__ __forceinline__ void dispatch_cta(int32_t *sel_idx, float *sel_w, int
                                              const float *__restrict__ logits, int T, int topk);
 
 template <bool DISPATCH>
-__global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W,
+__global__ void __launch_bounds__(512) k_router_smem(const float *__restrict__ W,
                                                      const float *__restrict__ x,
                                                      const float *__restrict__ bias, int T, int H,
                                                      int E, int EG, int TG,
@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(256) k_router_smem(const float *__restrict__ W
   if (xq) {
     // The decode GEMV's split operand of these tokens (spt_gemv16.cuh), made
     // here from the staged rows: CTA bx writes K tiles bx, bx + gridDim.x, ...
-    __shared__ float s_red[8];
+    __shared__ float s_red[16];  // one per warp (256 or 512 threads)
     for (int j = 0; j < nt; ++j) {
       const float *xr = xs + (size_t)j * H;
       float m = 0.0f;
@@ -1070,6 +1070,14 @@ cudaError_t opt_in_smem_raw(const void *kernel, int bytes) {
   return e;
 }
 
+bool router_wide() {
+  static const bool on = [] {
+    const char *v = getenv("SPT_ROUTER_WIDE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 cudaError_t launch_router(const float *W, const float *x, const float *bias, int T, int H, int E,
                           float *logits, int portable_lanes, cudaStream_t stream, const RouterSplit *split,
                           bool *split_done, const RouterNorm *norm, int *launches, const RouterDispatch *dispatch,
@@ -1114,6 +1122,9 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
     const bool do_split = split && split->xq && (E + EG - 1) / EG > 0;
     if (split_done) *split_done = do_split;
     const dim3 grid((E + EG - 1) / EG, (T + TG - 1) / TG);
+    // above decode sizes a CTA has 8 tokens x EG experts of dots: 16 warps
+    // take one token x 4 experts each (SPT_ROUTER_WIDE=0: 8 warps, two each)
+    const int threads = (T > kRouterDispatchMaxTokens && router_wide()) ? 512 : 256;
     __half *sx = do_split ? split->xq : (__half *)nullptr;
     int32_t *se = do_split ? split->xe : (int32_t *)nullptr;
     const int skp = do_split ? split->kp : 0;
@@ -1124,12 +1135,12 @@ cudaError_t launch_router(const float *W, const float *x, const float *bias, int
       cudaError_t e = opt_in_smem(k_router_smem<true>, kRouterSmemDispatchMax);
       if (e != cudaSuccess) return e;
       if (dispatch_done) *dispatch_done = true;
-      return launch_pdl(k_router_smem<true>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E,
+      return launch_pdl(k_router_smem<true>, grid, dim3(threads), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E,
                         EG, TG, logits, sx, se, skp, nw, neps, nout, *dispatch, err, wait_shift, fault);
     }
     cudaError_t e = opt_in_smem(k_router_smem<false>, kRouterSmemMax);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_router_smem<false>, grid, dim3(256), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E, EG,
+    return launch_pdl(k_router_smem<false>, grid, dim3(threads), (size_t)bytes(EG, TG), stream, W, x, bias, T, H, E, EG,
                       TG, logits, sx, se, skp, nw, neps, nout, RouterDispatch{}, err, wait_shift, fault);
   } else {
     cudaError_t e = separate_norm();
