@@ -45,27 +45,6 @@ __device__ __forceinline__ float reduce_chains(float v, int lane) {
   return __fadd_rn(q, __shfl_sync(0xffffffffu, q, (lane + 2) & 31));          // lane 0
 }
 
-// Packed fp32 pairs (sm_100a f32x2): two independent IEEE round-to-nearest
-// operations per instruction, so results equal the scalar ones.
-__device__ __forceinline__ void add2(float &a0, float &a1, float b) {
-  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %2};\n\t"
-      "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(b));
-}
-__device__ __forceinline__ void mul2(float &a0, float &a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-      "mul.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(b0), "f"(b1));
-}
-__device__ __forceinline__ void fma2(float &c0, float &c1, float a0, float a1, float b) {
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
-      "mov.b64 rc, {%0, %1};\n\tfma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
-      : "+f"(c0), "+f"(c1)
-      : "f"(a0), "f"(a1), "f"(b));
-}
-
 __device__ __forceinline__ unsigned long long argmax_key(float logit, int64_t row) {
   uint32_t bits = __float_as_uint(logit == 0.0f ? 0.0f : logit);  // -0 ties with +0
   bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);      // order-preserving
@@ -173,25 +152,28 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
         __syncwarp();
         const uint8_t *q0 = row[0] + 2 + lane, *q1 = row[1] + 2 + lane, *q2 = row[2] + 2 + lane,
                       *q3 = row[3] + 2 + lane;
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        // packed fp32 pairs (sm_100a f32x2, the compiler's own float2
+        // operations): two independent IEEE round-to-nearest results each,
+        // equal to the scalar ones
+        float2 a01 = make_float2(0.0f, 0.0f), a23 = make_float2(0.0f, 0.0f);
+        const float2 off = make_float2(-8388736.0f, -8388736.0f);
 #pragma unroll 5
         for (int b = 0; b < nb; ++b) {
           const float xv = xs[b * 32 + lane];
           const float4 sv = sc[b];
           // int8 -> float: (0x4B000000 | (byte ^ 0x80)) - 8388736, exact
-          float w0 = __uint_as_float(0x4B000000u | ((uint32_t)q0[b * 34] ^ 0x80u));
-          float w1 = __uint_as_float(0x4B000000u | ((uint32_t)q1[b * 34] ^ 0x80u));
-          float w2 = __uint_as_float(0x4B000000u | ((uint32_t)q2[b * 34] ^ 0x80u));
-          float w3 = __uint_as_float(0x4B000000u | ((uint32_t)q3[b * 34] ^ 0x80u));
-          add2(w0, w1, -8388736.0f);
-          add2(w2, w3, -8388736.0f);
-          mul2(w0, w1, sv.x, sv.y);  // weight = int8 * scale (exact)
-          mul2(w2, w3, sv.z, sv.w);
-          fma2(a0, a1, w0, w1, xv);
-          fma2(a2, a3, w2, w3, xv);
+          float2 w01 = make_float2(__uint_as_float(0x4B000000u | ((uint32_t)q0[b * 34] ^ 0x80u)),
+                                   __uint_as_float(0x4B000000u | ((uint32_t)q1[b * 34] ^ 0x80u)));
+          float2 w23 = make_float2(__uint_as_float(0x4B000000u | ((uint32_t)q2[b * 34] ^ 0x80u)),
+                                   __uint_as_float(0x4B000000u | ((uint32_t)q3[b * 34] ^ 0x80u)));
+          w01 = __fmul2_rn(__fadd2_rn(w01, off), make_float2(sv.x, sv.y));  // weight = int8 * scale (exact)
+          w23 = __fmul2_rn(__fadd2_rn(w23, off), make_float2(sv.z, sv.w));
+          const float2 xx = make_float2(xv, xv);
+          a01 = __ffma2_rn(w01, xx, a01);
+          a23 = __ffma2_rn(w23, xx, a23);
         }
-        const float y[4] = {reduce_chains(a0, lane), reduce_chains(a1, lane), reduce_chains(a2, lane),
-                            reduce_chains(a3, lane)};
+        const float y[4] = {reduce_chains(a01.x, lane), reduce_chains(a01.y, lane), reduce_chains(a23.x, lane),
+                            reduce_chains(a23.y, lane)};
         if (lane == 0) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
