@@ -754,7 +754,8 @@ def run_q80(args):
             "config": {"workload": "q80: Q8_0 LM head argmax, 201088 x 2880 (north_star q80.go)",
                        "rows": Q80_ROWS, "input": Q80_IN, "l2": "615 MB matrix > L2"},
             "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
-                         "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "kernel": "k_q80_gemv",
+                         "frac": nbytes / (ms / 1e3) / 1e9 / peak,
+                         "traffic": load_traffic("q80:gemv:dram_bytes"), "kernel": "k_q80_gemv",
                          "algorithmic_bytes": nbytes, "avg_ms": ms, "peak_source": peak_src},
             "e2e": {"value": 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": Q80_IN * 4,
                     "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms},

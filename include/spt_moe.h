@@ -365,7 +365,9 @@ spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len,
                        int64_t output, const float *x, float *y, int64_t *argmax,
                        float *best_logit);
 /* The same with the matrix resident in HBM: uploaded once (the reference
- * streams it from the mmap window for every token, q80.go:86-104). */
+ * streams it from the mmap window for every token, q80.go:86-104) and
+ * repacked on the device into four-row groups; the caller's bytes are not
+ * kept. */
 typedef struct spt_q80_matrix spt_q80_matrix;
 spt_status spt_q80_matrix_create(spt_context *ctx, const uint8_t *data, uint64_t data_len,
                                  int64_t input, int64_t output, spt_q80_matrix **out);

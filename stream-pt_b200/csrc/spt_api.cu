@@ -2058,9 +2058,14 @@ spt_status spt_q80_matrix_create(spt_context *ctx, const uint8_t *data, uint64_t
   m->ctx = ctx;
   m->input = input;
   m->output = output;
-  cudaError_t e = m->w.ensure(data_len + 64);  // the last chunk's copy rounds up to 16 bytes
-  if (e == cudaSuccess) e = cudaMemsetAsync(m->w.p, 0, data_len + 64, ctx->stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(m->w.p, data, data_len, cudaMemcpyHostToDevice, ctx->stream);
+  // the file's rows go up once and are repacked into four-row groups in HBM
+  const uint64_t packed = q80_packed_bytes(output, (int)input);
+  Tmp raw;
+  cudaError_t e = m->w.ensure(packed);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->w.p, 0, packed, ctx->stream);
+  if (e == cudaSuccess) e = raw.alloc(data_len);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(raw.p, data, data_len, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = launch_q80_repack(raw.as<uint8_t>(), output, (int)input, m->w.as<uint8_t>(), ctx->stream);
   if (e == cudaSuccess) e = m->best.ensure(sizeof(unsigned long long));
   if (e == cudaSuccess) e = m->err.ensure(sizeof(int32_t));
   if (e == cudaSuccess) e = cudaMemsetAsync(m->err.p, 0, sizeof(int32_t), ctx->stream);

@@ -286,11 +286,14 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 // Q8_0 GEMV + argmax (spt_q80.cu): y[r] = dot(row r, x) for `rows` rows of
-// input/32 34-byte blocks (w padded by >= 16 bytes); best = packed argmax
-// key, decoded into argmax/logit (either may be null).
+// input/32 34-byte blocks, w in the packed four-row-group layout that
+// launch_q80_repack writes (q80_packed_bytes long, zeroed before the repack);
+// best = packed argmax key, decoded into argmax/logit (either may be null).
 cudaError_t launch_q80(const uint8_t *w, int64_t rows, int input, const float *x, float *y,
                        unsigned long long *best, int64_t *argmax, float *logit, int32_t *err, int sm_count,
                        cudaStream_t stream);
+cudaError_t launch_q80_repack(const uint8_t *raw, int64_t rows, int input, uint8_t *packed, cudaStream_t stream);
+uint64_t q80_packed_bytes(int64_t rows, int input);
 int q80_rows_per_chunk(int input);
 
 // Q4_0 products (spt_q40.cu): y[item][r] = dot(row r, x[item]) for `rows`

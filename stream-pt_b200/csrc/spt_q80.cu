@@ -8,15 +8,19 @@
 // ((a0+a1)+a2)+a3 over its four 8-lane accumulators and reduces the 8 lanes
 // with quantSumAVX2.  Here one lane runs one chain.
 //
-// The matrix (615 MB for GPT-OSS's 201,088 x 2,880 output head) streams
-// through a four-stage shared-memory ring of 16-row stages, filled by a
-// producer warp with 8-row bulk copies (up to eight in flight) and released
-// per stage through mbarriers; four groups of four consumer warps take the
-// stages in turn, each warp decoding its rows' block scales (float16 ->
-// float32, exact like the reference's decode) and running four rows at a time on
-// packed fp32 pairs (one x load per four rows).  int8 -> float uses the exact
-// magic-number form (0x4B000000 | (b ^ 0x80)) - 8388736 instead of the
-// quarter-rate convert.
+// The matrix (615 MB for GPT-OSS's 201,088 x 2,880 output head) is repacked
+// once at upload into groups of four rows, the same bytes in another order:
+// per group, the blocks' float16 scales [nb][4 rows], then the quants
+// [nb][32 elements][4 rows] with the sign bit flipped (byte ^ 0x80), so one
+// 32-bit shared load gives a lane its element of all four rows.  The packed
+// matrix streams through a four-stage shared-memory ring of 16-row stages,
+// filled by a producer warp with 8-row bulk copies (up to eight in flight) and
+// released per stage through mbarriers; four groups of four consumer warps
+// take the stages in turn, each warp decoding its row group's block scales
+// (float16 -> float32, exact like the reference's decode) and running the four
+// rows at once on packed fp32 pairs (one x load per four rows).  int8 -> float
+// is the exact magic-number form: a byte permute builds 0x4B000000 | (b ^ 0x80),
+// from which 8388736 is subtracted, instead of the quarter-rate convert.
 // The argmax packs (order-preserving logit bits, ~row) into 64 bits and
 // keeps the maximum with atomicMax: largest logit, lowest row on ties, NaN
 // never chosen, -0 equal to +0, and row 0 when nothing beats -Inf.
@@ -52,7 +56,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float logit, int64_t ro
 }
 
 struct Q80Launch {
-  const uint8_t *w;          // rows x row_bytes (+ at least 16 bytes of padding)
+  const uint8_t *w;          // packed row groups (q80_packed_bytes)
   int64_t rows;
   int input, row_bytes, blocks, rows_per_stage;
   const float *x;            // [input]
@@ -104,7 +108,8 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
         const int s = it % kQ80Stages, use = it / kQ80Stages;
         if (use > 0 && !mbar_wait(&empty[s], (uint32_t)(use - 1) & 1u, a.err, 2)) break;
         const int64_t r0 = chunk * rps;
-        const int nr = (int)(a.rows - r0 < rps ? a.rows - r0 : rps);
+        // whole four-row groups: the last group's missing rows are zero padding
+        const int nr = (int)(((a.rows - r0 < rps ? a.rows - r0 : rps) + 3) & ~3);
         uint32_t tx = 0;
         for (int p = 0; p < nr; p += kQ80RowsPerCopy)
           tx += (uint32_t)((int64_t)(min(kQ80RowsPerCopy, nr - p) * rb + 15) & ~15ll);
@@ -135,23 +140,19 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
       const int64_t r0 = chunk * rps;
       const int nr = (int)(a.rows - r0 < rps ? a.rows - r0 : rps);
       for (int r = 4 * wi; r < nr; r += 4 * kQ80Group) {
-        const int live = min(4, nr - r);  // rows past the end repeat the last live row
-        const uint8_t *row[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) row[k] = cb + (size_t)(r + min(k, live - 1)) * rb;
+        const int live = min(4, nr - r);  // rows past the end are padding, not written
+        const uint8_t *gb = cb + (size_t)r * rb;  // this warp's row group
         for (int b = lane; b < nb; b += 32) {
           // float16 -> float32 is exact for every finite value and infinity
           // (quantFloat16Bits); a NaN scale gives a NaN either way
-          float4 v;
-          v.x = __half2float(*reinterpret_cast<const __half *>(row[0] + b * 34));
-          v.y = __half2float(*reinterpret_cast<const __half *>(row[1] + b * 34));
-          v.z = __half2float(*reinterpret_cast<const __half *>(row[2] + b * 34));
-          v.w = __half2float(*reinterpret_cast<const __half *>(row[3] + b * 34));
-          sc[b] = v;
+          const uint2 h = *reinterpret_cast<const uint2 *>(gb + 8 * b);
+          sc[b] = make_float4(__half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu))),
+                              __half2float(__ushort_as_half((unsigned short)(h.x >> 16))),
+                              __half2float(__ushort_as_half((unsigned short)(h.y & 0xffffu))),
+                              __half2float(__ushort_as_half((unsigned short)(h.y >> 16))));
         }
         __syncwarp();
-        const uint8_t *q0 = row[0] + 2 + lane, *q1 = row[1] + 2 + lane, *q2 = row[2] + 2 + lane,
-                      *q3 = row[3] + 2 + lane;
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(gb + 8 * nb) + lane;  // [nb][32] words
         // packed fp32 pairs (sm_100a f32x2, the compiler's own float2
         // operations): two independent IEEE round-to-nearest results each,
         // equal to the scalar ones
@@ -161,11 +162,13 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
         for (int b = 0; b < nb; ++b) {
           const float xv = xs[b * 32 + lane];
           const float4 sv = sc[b];
-          // int8 -> float: (0x4B000000 | (byte ^ 0x80)) - 8388736, exact
-          float2 w01 = make_float2(__uint_as_float(0x4B000000u | ((uint32_t)q0[b * 34] ^ 0x80u)),
-                                   __uint_as_float(0x4B000000u | ((uint32_t)q1[b * 34] ^ 0x80u)));
-          float2 w23 = make_float2(__uint_as_float(0x4B000000u | ((uint32_t)q2[b * 34] ^ 0x80u)),
-                                   __uint_as_float(0x4B000000u | ((uint32_t)q3[b * 34] ^ 0x80u)));
+          // int8 -> float: (0x4B000000 | (byte ^ 0x80)) - 8388736, exact; byte k
+          // of the word is row k's (sign-flipped) quant
+          const uint32_t q = qw[b * 32];
+          float2 w01 = make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7650)),
+                                   __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7651)));
+          float2 w23 = make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7652)),
+                                   __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7653)));
           w01 = __fmul2_rn(__fadd2_rn(w01, off), make_float2(sv.x, sv.y));  // weight = int8 * scale (exact)
           w23 = __fmul2_rn(__fadd2_rn(w23, off), make_float2(sv.z, sv.w));
           const float2 xx = make_float2(xv, xv);
@@ -196,6 +199,39 @@ __global__ void __launch_bounds__(kQ80Threads, 1) k_q80_gemv(const __grid_consta
   }
 }
 
+// Upload-time repack, one thread per (row group, block): the group's four
+// 34-byte blocks become 8 scale bytes at [block] and 32 words at [block][element]
+// whose byte k is row k's quant ^ 0x80; rows past the end are zero.
+__global__ void k_q80_repack(const uint8_t *__restrict__ raw, int64_t rows, int nb, uint8_t *__restrict__ out) {
+  const int64_t groups = (rows + 3) / 4;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= groups * nb) return;
+  const int64_t g = t / nb;
+  const int b = (int)(t % nb);
+  const int64_t rb = (int64_t)nb * 34;
+  const uint8_t *src[4];
+  bool has[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    has[k] = 4 * g + k < rows;
+    src[k] = raw + (has[k] ? (4 * g + k) * rb + (int64_t)b * 34 : 0);
+  }
+  uint8_t *dst = out + g * 4 * rb;
+  uint32_t sw[2] = {0u, 0u};
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    if (has[k]) sw[k >> 1] |= ((uint32_t)src[k][0] | ((uint32_t)src[k][1] << 8)) << (16 * (k & 1));
+  reinterpret_cast<uint2 *>(dst)[b] = make_uint2(sw[0], sw[1]);
+  uint32_t *qw = reinterpret_cast<uint32_t *>(dst + 8 * nb) + (int64_t)b * 32;
+  for (int c = 0; c < 32; ++c) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (has[k]) w |= (uint32_t)(src[k][2 + c] ^ 0x80u) << (8 * k);
+    qw[c] = w;
+  }
+}
+
 __global__ void k_q80_init(unsigned long long *best) {
   pdl_wait();
   pdl_trigger();
@@ -213,6 +249,19 @@ __global__ void k_q80_finalize(const unsigned long long *best, int64_t *argmax, 
 }
 
 }  // namespace
+
+uint64_t q80_packed_bytes(int64_t rows, int input) {
+  // whole four-row groups, + 64 bytes: the last copy rounds up to 16 bytes
+  return (uint64_t)((rows + 3) / 4 * 4) * (uint64_t)(input / 32 * 34) + 64;
+}
+
+cudaError_t launch_q80_repack(const uint8_t *raw, int64_t rows, int input, uint8_t *packed, cudaStream_t stream) {
+  const int nb = input / 32;
+  const int64_t n = (rows + 3) / 4 * nb;
+  if (n <= 0) return cudaSuccess;
+  k_q80_repack<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(raw, rows, nb, packed);
+  return cudaGetLastError();
+}
 
 size_t q80_smem_bytes(int input, int rps) {
   const int64_t rb = (int64_t)input / 32 * 34;
