@@ -1,5 +1,5 @@
 """Writes tests/golden/go_api.json: the identifiers of the Stream-PT Go
-sources that the cgo shim (stream-pt_b200/go/moe_cuda.go) relies on, read
+sources that the cgo shims (stream-pt_b200/go/*.go) rely on, read
 from a checkout of the reference (argv[1], else the STREAM_PT_SOURCE
 environment variable).
 tests/test_go_shim.py checks the shim against this file, so the check runs
@@ -72,6 +72,13 @@ def main():
             re.search(r"func MulQ40BatchInto\((.*?)\) error \{", q40, re.S).group(1).split()),
         "q40_shape_results": " ".join(
             re.search(r"func q40Shape\(tensor ggufindex\.Tensor\) \((.*?)\) \{", q40, re.S).group(1).split()),
+        "mul_q80_argmax_params": " ".join(
+            re.search(r"func MulQ80Argmax\((.*?)\) \(", q40, re.S).group(1).split()),
+        "mul_q80_argmax_results": " ".join(
+            re.search(r"func MulQ80Argmax\(.*?\) \((.*?)\) \{", q40, re.S).group(1).split()),
+        "mul_q80_into_params": " ".join(re.search(r"func MulQ80Into\((.*?)\) error \{", q40, re.S).group(1).split()),
+        "q80_shape_results": " ".join(
+            re.search(r"func q80Shape\(tensor ggufindex\.Tensor\) \((.*?)\) \{", q40, re.S).group(1).split()),
     }
     with open(os.path.join(HERE, "go_api.json"), "w") as f:
         json.dump(api, f, indent=1, sort_keys=True)

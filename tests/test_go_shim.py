@@ -1,5 +1,6 @@
-"""The cgo shim (stream-pt_b200/go/moe_cuda.go) against the reference's Go
-API and the C ABI, without a Go toolchain (none is installed here).
+"""The cgo shims (stream-pt_b200/go/*.go: the MoE block, the Q4_0 products and
+the Q8_0 head) against the reference's Go API and the C ABI, without a Go
+toolchain (none is installed here).
 
 Every identifier the shim takes from package forward, ggufindex or ggufmap
 must exist in the reference (tests/golden/go_api.json, written from the
@@ -20,6 +21,7 @@ HEADER = open(os.path.join(ROOT, "include", "spt_moe.h")).read()
 # every shim file, comments out (they form one package)
 CODE = "\n".join(re.sub(r"//[^\n]*", "", src) for src in SHIMS.values())
 Q40 = re.sub(r"//[^\n]*", "", SHIMS["q40_cuda.go"])
+Q80 = re.sub(r"//[^\n]*", "", SHIMS["q80_cuda.go"])
 
 
 def test_imports_name_the_reference_packages():
@@ -103,3 +105,32 @@ def test_q40_error_texts_follow_the_reference():
                  "%q: expected %d input and %d output elements, got %d and %d",
                  "input and output must not overlap", "window of %d bytes cannot accommodate a %d-byte row"):
         assert '"%s"' % text in Q40, text
+
+
+def test_q80_signatures_unchanged():
+    """MulQ80Argmax / MulQ80Into keep the reference's parameter and result
+    lists (forward/q80.go:20-148); the helpers the shim keeps from q80.go
+    exist."""
+    argmax = re.search(r"func MulQ80Argmax\((.*?)\) \((.*?)\) \{", Q80, re.S)
+    into = re.search(r"func MulQ80Into\((.*?)\) error \{", Q80, re.S).group(1)
+    assert " ".join(argmax.group(1).split()) == API["mul_q80_argmax_params"]
+    assert " ".join(argmax.group(2).split()) == API["mul_q80_argmax_results"]
+    assert " ".join(into.split()) == API["mul_q80_into_params"]
+    assert API["q80_shape_results"] == "input, output, rowBytes int, err error"
+    assert len(re.findall(r"input, output, rowBytes, err := q80Shape\(tensor\)", Q80)) == 2
+    assert "q80Shape" in API["forward_funcs"] and "DefaultQ40WindowBytes" in API["forward_consts"]
+    defined = set(re.findall(r"^func (\w+)\(", Q80, re.M))
+    assert defined == {"q80Matrix", "q80Window", "mulQ80", "MulQ80Argmax", "MulQ80Into"}
+    # no helper of the same name elsewhere in the shims (one package)
+    others = "\n".join(re.sub(r"//[^\n]*", "", v) for k, v in SHIMS.items() if k != "q80_cuda.go")
+    for fn in defined:
+        assert not re.search(r"^func %s\(" % fn, others, re.M), fn
+
+
+def test_q80_error_texts_follow_the_reference():
+    for text in ("nil context", "nil reader", "nil context or reader",
+                 "%q: expected %d input elements, got %d",
+                 "%q: expected input/output lengths %d/%d, got %d/%d",
+                 "window of %d bytes cannot accommodate a %d-byte row"):
+        assert '"%s"' % text in Q80, text
+
