@@ -745,6 +745,17 @@ def run_q80(args):
         if i >= args.warmup:
             e_ms.append(st.elapsed_time(en))
     e2e_ms = sum(e_ms) / len(e_ms)
+    # parity of the whole head against the oracle (outside the timed regions):
+    # every logit bit for bit, the argmax row and its logit
+    from oracle import oracle
+    y_got, idx_got, logit_got = m.mul(x_host, want_y=True)
+    y_want, idx_want, logit_want = oracle.mul_q80(data, Q80_IN, Q80_ROWS, x_host, os.cpu_count() or 1)
+    logits_exact = bool(np.array_equal(y_got.view(np.uint32), y_want.view(np.uint32)))
+    parity = {"rows_checked": Q80_ROWS, "logits_bit_exact": logits_exact,
+              "argmax_equal": int(idx_got) == int(idx_want) == int(idx),
+              "logit_bit_exact": np.float32(logit_got).view(np.uint32) == np.float32(logit_want).view(np.uint32)}
+    parity["logit_bit_exact"] = bool(parity["logit_bit_exact"])
+    parity["ok"] = bool(logits_exact and parity["argmax_equal"] and parity["logit_bit_exact"])
     peak, _, peak_src = load_peaks()
     nbytes = Q80_ROWS * nb * 34
     line = {"metric": "lm_head_tokens_per_s", "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
@@ -759,7 +770,7 @@ def run_q80(args):
                          "algorithmic_bytes": nbytes, "avg_ms": ms, "peak_source": peak_src},
             "e2e": {"value": 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": Q80_IN * 4,
                     "d2h_bytes_per_step": 16, "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * 3, "argmax": int(idx), "clocks": clocks.summary()}
+            "parity": parity, "gpu_launches": args.steps * 3, "argmax": int(idx), "clocks": clocks.summary()}
     if not args.no_cpu_baseline:
         from oracle import oracle
         workers = os.cpu_count() or 1
