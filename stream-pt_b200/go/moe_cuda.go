@@ -56,8 +56,9 @@ var (
 	sptErr    error
 	sptArenaM sync.Mutex
 	sptArena  = map[arenaKey]*C.spt_arena{}
-	// sptCallM serialises forward calls: they share the context's stream and
-	// device buffers (the reference gives each caller its own scratch).
+	// sptCallM serialises every call into the context (uploads and
+	// products): they share its stream, device buffers and error text (the
+	// reference gives each caller its own scratch).
 	sptCallM sync.Mutex
 )
 
@@ -158,6 +159,8 @@ func arenaFor(ctx *C.spt_context, reader *ggufmmap.Reader, cfg *Config, lw *Laye
 			ffn_down_exps: first(v[6]), ffn_down_exps_bias: first(v[7]),
 			post_attention_norm: first(v[8]),
 		}
+		sptCallM.Lock() // the upload uses the context's stream and error text
+		defer sptCallM.Unlock()
 		return sptError(ctx, C.spt_arena_create_views(ctx, &c, &w, &d, 1, C.SPT_ARENA_GEMV|C.SPT_ARENA_MMA, 0, 0,
 			&arena))
 	})
@@ -209,9 +212,10 @@ func forwardMoEBatch(ctx context.Context, reader *ggufmmap.Reader, x []float32, 
 		(*C.float)(unsafe.Pointer(&x[0])), C.int64_t(len(x)),
 		(*C.float)(unsafe.Pointer(&out[0])), C.int64_t(len(out)),
 		C.int64_t(batch), cancel)
+	err = sptError(sctx, st) // the context's error text, read before another call replaces it
 	sptCallM.Unlock()
 	close(stop)
 	<-exited // the goroutine no longer touches the flag
 	C.free(unsafe.Pointer(cancel))
-	return sptError(sctx, st)
+	return err
 }

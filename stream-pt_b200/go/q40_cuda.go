@@ -65,6 +65,8 @@ func q40Matrix(ctx *C.spt_context, reader *ggufmmap.Reader, tensor ggufindex.Ten
 	err := reader.WithTensor(tensor, func(data []byte) error {
 		r := C.spt_reader{base: first(data), size: C.uint64_t(len(data))}
 		ct.start, ct.end = 0, C.uint64_t(len(data))
+		sptCallM.Lock()
+		defer sptCallM.Unlock()
 		return sptError(ctx, C.spt_q40_matrix_create(ctx, &r, &ct, &m))
 	})
 	if err != nil {
@@ -136,6 +138,7 @@ func MulQ40BatchInto(ctx context.Context, reader *ggufmmap.Reader, tensor ggufin
 	sptCallM.Lock()
 	st := C.spt_mul_q40_matrix(sctx, m, (*C.float)(unsafe.Pointer(&x[0])), C.int64_t(len(x)),
 		(*C.float)(unsafe.Pointer(&y[0])), C.int64_t(len(y)), C.int64_t(batch), cancel)
+	err = sptError(sctx, st)
 	sptCallM.Unlock()
 	close(stop)
 	<-exited
@@ -143,5 +146,5 @@ func MulQ40BatchInto(ctx context.Context, reader *ggufmmap.Reader, tensor ggufin
 	if st == C.SPT_ERR_CANCELED {
 		return ctx.Err()
 	}
-	return sptError(sctx, st)
+	return err
 }

@@ -57,6 +57,8 @@ func q80Matrix(ctx *C.spt_context, reader *ggufmmap.Reader, tensor ggufindex.Ten
 	}
 	var m *C.spt_q80_matrix
 	err := reader.WithTensor(tensor, func(data []byte) error {
+		sptCallM.Lock()
+		defer sptCallM.Unlock()
 		return sptError(ctx, C.spt_q80_matrix_create(ctx, first(data), C.uint64_t(len(data)),
 			C.int64_t(input), C.int64_t(output), &m))
 	})
@@ -99,8 +101,9 @@ func mulQ80(reader *ggufmmap.Reader, tensor ggufindex.Tensor, input, output int,
 	var logit C.float
 	sptCallM.Lock()
 	st := C.spt_mul_q80_matrix(sctx, m, (*C.float)(unsafe.Pointer(&x[0])), yp, &token, &logit)
+	err = sptError(sctx, st)
 	sptCallM.Unlock()
-	if err := sptError(sctx, st); err != nil {
+	if err != nil {
 		return 0, 0, err
 	}
 	return int(token), float32(logit), nil

@@ -134,3 +134,27 @@ def test_q80_error_texts_follow_the_reference():
                  "window of %d bytes cannot accommodate a %d-byte row"):
         assert '"%s"' % text in Q80, text
 
+
+def test_library_calls_hold_the_call_lock():
+    """Every call into the shared context (uploads and products) and every
+    read of its error text runs between sptCallM.Lock() and its Unlock: the
+    calls share one stream, its device buffers and its last-error text.  A
+    "defer sptCallM.Unlock()" holds the lock to the end of its block."""
+    exempt = {"spt_context_create", "spt_last_error"}  # under sync.Once / inside sptError
+    for name, src in SHIMS.items():
+        locked, defer_indent = False, None
+        for n, line in enumerate(src.splitlines(), 1):
+            code = line.split("//")[0]
+            indent = len(line) - len(line.lstrip("\t"))
+            if defer_indent is not None and code.strip() and indent < defer_indent:
+                locked, defer_indent = False, None
+            if "sptCallM.Lock()" in code:
+                locked = True
+            if "defer sptCallM.Unlock()" in code:
+                defer_indent = indent
+            elif "sptCallM.Unlock()" in code:
+                locked = False
+            calls = set(re.findall(r"\bC\.(spt_[a-z_0-9]+)\(", code)) - exempt
+            if calls or (re.search(r"\bsptError\(", code) and not code.startswith("func ")):
+                assert locked, f"{name}:{n}: {line.strip()}"
+
