@@ -6,6 +6,7 @@ the process (the oracle generates its inputs and is what it times).  The
 modes with no reference arm print their ``unavailable`` line and exit 0."""
 import json
 import os
+import socket
 import subprocess
 import sys
 
@@ -15,9 +16,9 @@ sys.path.insert(0, ROOT)
 import bench  # noqa: E402  (imports no GPU code at module level)
 
 
-def run_bench(*args, timeout=240):
+def run_bench(*args, timeout=240, launcher=()):
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
-    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], cwd=ROOT, env=env,
+    out = subprocess.run([sys.executable, *launcher, os.path.join(ROOT, "bench.py"), *args], cwd=ROOT, env=env,
                          capture_output=True, text=True, timeout=timeout)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
@@ -50,3 +51,18 @@ def test_modes_without_a_reference_arm():
     for config in ("q80", "q40", "q40b"):
         line = run_bench("--config", config, "--impl", "reference", "--steps", "1", "--warmup", "3", timeout=60)
         assert line["impl"] == "reference" and line["unavailable"], line
+
+
+def test_reference_arm_under_torchrun():
+    """Two ranks as the scaling runs launch them: rank 0 alone prints one line
+    (the N-rank workload's config), the other rank exits 0 without work."""
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    launcher = ("-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+                "127.0.0.1", "--master-port", str(port))
+    line = run_bench("--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "3", launcher=launcher)
+    assert line["impl"] == "reference" and line["n_gpus"] == 2
+    assert line["config"] == bench.workload_config("c1", 2, bench.ep_mode("c1"))
+    assert not any("libspt_moe" in p for p in line["native_so_loaded"])
+
