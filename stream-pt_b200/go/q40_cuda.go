@@ -11,8 +11,8 @@
 //
 // Each tensor is uploaded once into HBM (keyed by the reader and the
 // tensor's byte range) and stays resident, replacing the streamed mmap
-// window: options.Workers and options.WindowBytes are validated as before
-// but no longer shape the work.
+// window: options.WindowBytes is checked as before, and neither it nor
+// options.Workers (which the reference only clamps) shapes the work.
 package forward
 
 /*

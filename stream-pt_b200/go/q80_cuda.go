@@ -12,9 +12,10 @@
 //
 // Each tensor is uploaded once into HBM (keyed by the reader and the tensor's
 // byte range), repacked there and kept resident, replacing the streamed mmap
-// window: options.Workers and options.WindowBytes are validated as before but
-// no longer shape the work.  One call is a single device pass of about
-// 0.12 ms for GPT-OSS's head, so ctx is checked before and after it.
+// window: options.WindowBytes is checked as before, and neither it nor
+// options.Workers (which the reference only clamps) shapes the work.  One
+// call is a single device pass of about 0.12 ms for GPT-OSS's head, so ctx is
+// checked before and after it.
 package forward
 
 /*

@@ -63,6 +63,7 @@ def main():
         "range_fields": struct_fields(idx, "Range"),
         "layer_weights_fields": struct_fields(layer, "LayerWeights"),
         "config_fields": struct_fields(config, "Config"),
+        "q40_options_fields": struct_fields(q40, "Q40Options"),
         "forward_types": sorted(set(re.findall(r"^type (\w+)", q40, re.M))),
         "forward_moe_batch_params": " ".join(sig.split()),
         "forward_funcs": sorted(set(re.findall(r"^func ([A-Za-z]\w*)\(", q40, re.M))),

@@ -46,6 +46,7 @@ def test_reader_methods_exist():
 def test_fields_exist():
     checks = [(r"\blw\.(\w+)", "layer_weights_fields"), (r"\bcfg\.(\w+)", "config_fields"),
               (r"\bt\.(\w+)", "tensor_fields"), (r"\bts\[\d+\]\.(\w+)", "tensor_fields"),
+              (r"\btensor\.(\w+)", "tensor_fields"), (r"\boptions\.(\w+)", "q40_options_fields"),
               (r"\.Range\.(\w+)", "range_fields")]
     for pat, key in checks:
         used = set(re.findall(pat, CODE))
