@@ -38,6 +38,22 @@ def test_q80_fixture_bit_exact(ctx, input_):
     assert i == want_i and same(l, want_l)
 
 
+@pytest.mark.parametrize("input_", [2912, 4096])
+def test_q80_long_rows_bit_exact(ctx, input_):
+    """Rows too long for 16-row stages run in 8-row stages (odd and even block
+    counts); 45 rows end in a partial four-row group."""
+    rng = np.random.default_rng(input_)
+    nb = input_ // 32
+    data = rng.integers(0, 256, size=(45, nb, 34), dtype=np.uint8)
+    data[:, :, :2] = (rng.standard_normal((45, nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(45, nb, 2)
+    data = data.reshape(-1)
+    x = rng.standard_normal(input_).astype(np.float32)
+    want_y, want_i, want_l = oracle.mul_q80(data, input_, 45, x)
+    y, i, l = ctx.mul_q80(data, input_, 45, x)
+    assert same(y, want_y)
+    assert i == want_i and same(l, want_l)
+
+
 def test_q80_every_scale(ctx):
     rows = np.ones((65536, 34), np.uint8)
     rows[:, :2] = np.arange(65536, dtype=np.uint16).view(np.uint8).reshape(-1, 2)
