@@ -549,7 +549,14 @@ void spo_add(float *dst, const float *src, int64_t n) {
 }
 
 /* ---- Q8_0: forward/quant_amd64.go:92-110, forward/q80.go:22-148 -------- */
-float spo_dot_q80(const uint8_t *row, const float *x, int64_t input) {
+/* The Q8_0 and Q4_0 dots are built twice (x86-64-v3 and baseline, chosen at
+ * load time): with FMA in the instruction set each fmaf is one instruction
+ * instead of a library call.  The arithmetic is the same either way (fmaf
+ * is exact-rounded, and -ffp-contract=off keeps every other operation as
+ * written), so only the speed of the CPU baseline changes. */
+#define SPO_CLONES __attribute__((target_clones("arch=x86-64-v3", "default")))
+
+SPO_CLONES float spo_dot_q80(const uint8_t *row, const float *x, int64_t input) {
   float a[32];
   for (int c = 0; c < 32; c++) a[c] = 0.0f;
   for (int64_t b = 0; b < input / 32; b++) {
@@ -599,7 +606,7 @@ static void q40_decode(const uint8_t *enc, float w[32]) {
 
 /* quantQ40AVX2 (forward/quant_amd64.go:75-90): chain c takes element c of
  * every block; a0+a1+a2+a3, then quantSumAVX2. */
-float spo_dot_q40(const uint8_t *row, const float *x, int64_t input) {
+SPO_CLONES float spo_dot_q40(const uint8_t *row, const float *x, int64_t input) {
   float a[32], w[32];
   for (int c = 0; c < 32; c++) a[c] = 0.0f;
   for (int64_t b = 0; b < input / 32; b++) {
@@ -612,7 +619,7 @@ float spo_dot_q40(const uint8_t *row, const float *x, int64_t input) {
 /* quantDotQ40Batch (forward/quant_amd64.go:118-148): one 8-lane accumulator
  * per item; lane l takes elements l, 8+l, 16+l, 24+l of each block in that
  * order, then quantSumAVX2.  Writes y[item * output + row_index]. */
-void spo_dot_q40_batch(const uint8_t *row, const float *x, float *y, int64_t input, int64_t output,
+SPO_CLONES void spo_dot_q40_batch(const uint8_t *row, const float *x, float *y, int64_t input, int64_t output,
                        int64_t row_index, int64_t batch) {
   float w[32];
   for (int64_t item = 0; item < batch; item++) {
