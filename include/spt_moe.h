@@ -367,7 +367,9 @@ spt_status spt_mul_q80(spt_context *ctx, const uint8_t *data, uint64_t data_len,
 /* The same with the matrix resident in HBM: uploaded once (the reference
  * streams it from the mmap window for every token, q80.go:86-104) and
  * repacked on the device into four-row groups; the caller's bytes are not
- * kept. */
+ * kept.  Creation needs the packed matrix (the file's size rounded up to
+ * whole four-row groups, + 64 bytes) plus a transient device copy of the
+ * file's bytes, freed before it returns. */
 typedef struct spt_q80_matrix spt_q80_matrix;
 spt_status spt_q80_matrix_create(spt_context *ctx, const uint8_t *data, uint64_t data_len,
                                  int64_t input, int64_t output, spt_q80_matrix **out);
